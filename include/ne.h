@@ -1,0 +1,171 @@
+/* ne.h -- C ABI of libne.so, the B200 (sm_100a) implementation of the
+ * per-layer transformer step of the reference's training_dynamic pipeline
+ * (ane-training/training/training_dynamic/) and of its numpy token loop
+ * (tools/generate.py).
+ *
+ * Conventions
+ *   - Every entry point returns ne_status; nothing aborts.  ne_last_error()
+ *     gives a human-readable reason for the last failure on a context.
+ *   - Sizes are in elements.  Pointers named h_* are caller-owned HOST
+ *     buffers; pointers named d_* are DEVICE buffers on the context's GPU.
+ *   - A context owns one GPU, one CUDA stream and all device memory it uses;
+ *     it is single-threaded (one host thread per context).  Calls that return
+ *     data to host memory synchronise the stream; the *_device variants only
+ *     enqueue work.
+ *   - Weights are row-major [out, in] fp32 on the host, exactly the tensors
+ *     of the v4 checkpoint (config.h:26-33, train.m:110-130); the device keeps
+ *     bf16 compute copies.
+ *   - Activations are token-major [tokens, features].  The KV cache is fp16,
+ *     [layer][sequence][kv_head][position][head_dim].
+ */
+#ifndef NE_H_
+#define NE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NE_API __attribute__((visibility("default")))
+#else
+#define NE_API
+#endif
+
+typedef enum ne_status {
+  NE_OK = 0,
+  NE_ERR_INVALID = 1,     /* bad argument or shape */
+  NE_ERR_CUDA = 2,        /* CUDA runtime / launch error */
+  NE_ERR_OOM = 3,         /* device allocation failed */
+  NE_ERR_IO = 4,          /* file open / read / write failed */
+  NE_ERR_FORMAT = 5,      /* checkpoint magic / version / size mismatch */
+  NE_ERR_TIMEOUT = 6,     /* a kernel's bounded wait expired (status word set on device) */
+  NE_ERR_UNSUPPORTED = 7, /* shape or option the kernels are not built for */
+  NE_ERR_STATE = 8,       /* call out of order (e.g. decode before ne_kv_alloc) */
+  NE_ERR_BOUNDS = 9       /* a kernel saw an out-of-range token id or position */
+} ne_status;
+
+/* Model description.  The reference fixes the model at compile time
+ * (models/qwen3_06b.h:6-16, models/stories110m.h:6-16) and hard-codes
+ * eps 1e-5, RoPE theta 10000, no QK-norm and residual alpha 1/sqrt(2L) in
+ * training (train.m:181) but 1 in generate.py; here they are run-time fields. */
+typedef struct ne_model_cfg {
+  int n_layers;
+  int dim;
+  int hidden;
+  int n_heads;
+  int kv_heads;
+  int head_dim;      /* 64 or 128 */
+  int vocab;
+  float rms_eps;     /* RMSNorm eps (generate.py:81) */
+  float rope_theta;  /* RoPE base (generate.py:103) */
+  int qk_norm;       /* 1: per-head RMSNorm of q and k before RoPE (Qwen3) */
+  float qk_eps;
+  float res_alpha;   /* residual branch scale x += alpha * f(x) */
+} ne_model_cfg;
+
+/* Subset of the v4 checkpoint header (config.h:83-91) returned by the loader. */
+typedef struct ne_ckpt_info {
+  int step, total_steps, seq_len, adam_t;
+  float lr, loss;
+  double cum_compile, cum_train, cum_wall;
+  int cum_steps, cum_batches;
+  int has_qk_norm;   /* the trailing QKN1 extension block was present */
+} ne_ckpt_info;
+
+typedef struct ne_ctx ne_ctx;
+
+/* ---- context -------------------------------------------------------------
+ * Replaces the reference's ane_init + compile_dynamic_kernels
+ * (config.h:99-107, train.m:25-94): there is nothing to compile at run time. */
+NE_API ne_status ne_init(ne_ctx** out, const ne_model_cfg* cfg, int device);
+NE_API void ne_free(ne_ctx* ctx);
+NE_API const char* ne_last_error(const ne_ctx* ctx);
+NE_API const char* ne_status_str(ne_status s);
+NE_API ne_status ne_sync(ne_ctx* ctx);
+NE_API ne_status ne_get_cfg(const ne_ctx* ctx, ne_model_cfg* out);
+/* Version string of the library build. */
+NE_API const char* ne_version(void);
+
+/* ---- weights -------------------------------------------------------------
+ * Replaces the weight staging into per-layer IOSurfaces
+ * (io.h:263-409 stage_*_weights; train.m:331-339).  Host fp32 tensors in the
+ * v4 layout; q_norm / k_norm [head_dim] may be NULL (gains of 1). */
+NE_API ne_status ne_set_layer_weights(ne_ctx* ctx, int layer, const float* h_wq, const float* h_wk,
+                                      const float* h_wv, const float* h_wo, const float* h_w1,
+                                      const float* h_w2, const float* h_w3, const float* h_rms_att,
+                                      const float* h_rms_ffn, const float* h_q_norm,
+                                      const float* h_k_norm);
+/* rms_final [dim]; embed [vocab, dim] (tied: also the LM head, generate.py:195). */
+NE_API ne_status ne_set_global_weights(ne_ctx* ctx, const float* h_rms_final, const float* h_embed);
+
+/* v4 checkpoint (train.m:97-165 save/load_checkpoint; config.h:83-91).  The
+ * header's model fields must match the context's configuration. */
+NE_API ne_status ne_load_ckpt_v4(ne_ctx* ctx, const char* path, ne_ckpt_info* info);
+
+/* ---- token loop (tools/generate.py:113-228) ------------------------------
+ * Allocates the fp16 KV cache and the decode / prefill workspaces for up to
+ * max_batch sequences of up to max_seq positions. */
+NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq);
+
+/* Process the prompt h_tokens [B, S] (positions pos0 .. pos0+S-1 of every
+ * sequence) in one causal pass, filling the KV cache.  Writes the next token
+ * (argmax, generate.py:200) into h_next [B] and, if non-NULL, the last
+ * position's logits into h_logits [B, vocab]. */
+NE_API ne_status ne_prefill(ne_ctx* ctx, const int32_t* h_tokens, int B, int S, int pos0,
+                            int32_t* h_next, float* h_logits);
+
+/* One KV-cached step: token h_tok [B] at position pos of every sequence
+ * (generate.py:134-217 loop body).  h_next [B] receives the argmax token;
+ * h_logits [B, vocab] (optional) the logits. */
+NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int pos, int32_t* h_next,
+                                float* h_logits);
+
+/* Greedy generation (temperature 0): prefill h_prompt [B, P], then n_new-1
+ * decode steps; h_out [B, n_new] receives the generated tokens. */
+NE_API ne_status ne_generate(ne_ctx* ctx, const int32_t* h_prompt, int B, int P, int n_new,
+                             int32_t* h_out);
+
+/* Device-resident variants (no host copies; enqueue only). */
+NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, int pos0,
+                                   int32_t* d_next);
+/* n_steps greedy steps starting from d_tok [B] at position pos0; token i of
+ * sequence b is written to d_out[i * B + b].  Each step is one CUDA-graph
+ * replay. */
+NE_API ne_status ne_decode_loop_device(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0,
+                                       int n_steps, int32_t* d_out);
+
+/* ---- dense contraction ---------------------------------------------------
+ * out = op(A[M,K] . B[N,K]^T) on the context's stream, bf16 operands (both
+ * K-major, row-major with leading dims lda / ldb), fp32 accumulation on the
+ * tcgen05 tensor cores.  Library counterpart of the reference's cblas_sgemm
+ * call sites (train.m:500-501 classifier, :514-523 classifier bwd / dEmbed,
+ * :555-597 dW2/dW1/dW3, :629-655 dWo, :733-738 dWq/dWk/dWv).
+ *   epi 0: fp32 out[n*ld + m]  (transposed)     epi 1: fp32 out[m*ld + n]
+ *   epi 2: bf16 out[m*ld + n]                   epi 3: fp32 out[m*ld + n] += alpha*acc
+ *   epi 4: bf16 SwiGLU of a W1/W3 16-row-interleaved B operand, out[m*ld + n/2]
+ * K must be a multiple of 64; pointers 16-byte aligned. */
+NE_API ne_status ne_gemm_device(ne_ctx* ctx, const void* d_A, long long lda, int M, const void* d_B,
+                                long long ldb, int N, int K, int epi, void* d_out, long long ld,
+                                float alpha);
+
+/* As ne_gemm_device with explicit tiling: bn = N tile (16, 32, 64, 128 or 256;
+ * 0 = automatic); splits = split-K factor (epi 0/1 only; 0 = automatic, 1 =
+ * none).  With splits > 1 the output holds `splits` partial slabs, slab s at
+ * d_out + s * split_stride elements; their sum is the product. *h_splits
+ * (optional) receives the factor used. */
+NE_API ne_status ne_gemm_device_ex(ne_ctx* ctx, const void* d_A, long long lda, int M,
+                                   const void* d_B, long long ldb, int N, int K, int epi,
+                                   void* d_out, long long ld, float alpha, int bn, int splits,
+                                   long long split_stride, int* h_splits);
+
+/* Kernel launches enqueued by the last ne_decode_loop_device step graph
+ * (per step), for launch accounting. */
+NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NE_H_ */

@@ -1,0 +1,181 @@
+// gemm.cu -- host side of the tcgen05 GEMM: TMA descriptors, tiling, dispatch.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "ne_internal.h"
+
+namespace ne {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major operand [rows, K] (leading dim ld elements), 128B-swizzled box
+// of 64 x box_rows.
+bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int K, long long ld, int box_rows,
+               int fp16) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)GEMM_BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, class Epi, int FMT>
+cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh,
+                     const typename Epi::Params& p, int grid, cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  gemm_tc_kernel<BN, Epi, FMT><<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, sh, p);
+  return cudaGetLastError();
+}
+
+template <int BN, int FMT>
+cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const GemmShape& sh, int grid, cudaStream_t st) {
+  switch (c.epi) {
+    case EPI_F32T: {
+      EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
+      return launch_t<BN, EpiF32T, FMT>(ta, tb, sh, p, grid, st);
+    }
+    case EPI_F32: {
+      EpiF32::Params p{(float*)c.out, c.ld, c.split_stride};
+      return launch_t<BN, EpiF32, FMT>(ta, tb, sh, p, grid, st);
+    }
+    case EPI_BF16: {
+      EpiBF16::Params p{(__nv_bfloat16*)c.out, c.ld};
+      return launch_t<BN, EpiBF16, FMT>(ta, tb, sh, p, grid, st);
+    }
+    case EPI_RESID: {
+      EpiResid::Params p{(float*)c.out, c.ld, c.alpha};
+      return launch_t<BN, EpiResid, FMT>(ta, tb, sh, p, grid, st);
+    }
+    case EPI_SWIGLU: {
+      if constexpr (GemmCfg<BN>::CH == 32) {
+        EpiSwiGLU::Params p{(__nv_bfloat16*)c.out, c.ld, (__nv_bfloat16*)c.aux1,
+                            (__nv_bfloat16*)c.aux2};
+        return launch_t<BN, EpiSwiGLU, FMT>(ta, tb, sh, p, grid, st);
+      } else {
+        return cudaErrorInvalidValue;
+      }
+    }
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+int pick_bn(const GemmCall& c) {
+  if (c.bn) return c.bn;
+  if (c.N <= 16) return c.epi == EPI_SWIGLU ? 32 : 16;
+  if (c.N <= 32) return 32;
+  if (c.N <= 64) return 64;
+  if (c.N <= 128) return 128;
+  return 256;
+}
+
+}  // namespace
+
+int device_num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int gemm_pick_splits(const GemmCall& c, int num_sms) {
+  if (c.splits > 0) return c.splits;
+  if (c.epi != EPI_F32T && c.epi != EPI_F32) return 1;
+  const int bn = pick_bn(c);
+  const int tiles = ((c.M + GEMM_BM - 1) / GEMM_BM) * ((c.N + bn - 1) / bn);
+  const int kb = c.K / GEMM_BK;
+  int best = 1;
+  for (int d = 1; d <= kb; ++d) {
+    if (kb % d) continue;
+    if (kb / d < 2) break;
+    if (tiles * d > num_sms) break;
+    best = d;
+  }
+  return best;
+}
+
+cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
+  if (c.M <= 0 || c.N <= 0 || c.K <= 0 || c.K % GEMM_BK != 0) return cudaErrorInvalidValue;
+  if ((c.lda * 2) % 16 != 0 || (c.ldb * 2) % 16 != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(c.A) & 15) || (reinterpret_cast<uintptr_t>(c.B) & 15))
+    return cudaErrorInvalidValue;
+  const int num_sms = device_num_sms();
+  const int bn = pick_bn(c);
+  const int splits = gemm_pick_splits(c, num_sms);
+  const int kb = c.K / GEMM_BK;
+  if (kb % splits != 0) return cudaErrorInvalidValue;
+  if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32) return cudaErrorInvalidValue;
+
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, c.A, c.M, c.K, c.lda, GEMM_BM, c.ab_fp16)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tb, c.B, c.N, c.K, c.ldb, bn, c.ab_fp16)) return cudaErrorInvalidValue;
+
+  GemmShape sh;
+  sh.M = c.M;
+  sh.N = c.N;
+  sh.K = c.K;
+  sh.m_tiles = (c.M + GEMM_BM - 1) / GEMM_BM;
+  sh.n_tiles = (c.N + bn - 1) / bn;
+  sh.splits = splits;
+  sh.kb_per_split = kb / splits;
+  sh.status = status;
+  const long long units = (long long)sh.m_tiles * sh.n_tiles * splits;
+  const int cap = c.max_ctas > 0 ? c.max_ctas : num_sms;
+  const int grid = (int)(units < cap ? units : cap);
+
+#define NE_BN(BN_)                                                       \
+  case BN_:                                                              \
+    return c.ab_fp16 ? launch_epi<BN_, 0>(c, ta, tb, sh, grid, st)       \
+                     : launch_epi<BN_, 1>(c, ta, tb, sh, grid, st);
+  switch (bn) {
+    NE_BN(16)
+    NE_BN(32)
+    NE_BN(64)
+    NE_BN(128)
+    NE_BN(256)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef NE_BN
+}
+
+}  // namespace ne

@@ -1,0 +1,403 @@
+// gemm_tc.cuh -- persistent tcgen05/TMEM GEMM for sm_100a.
+//
+//   acc[m, n] = sum_k A[m, k] * B[n, k]          (both operands K-major, bf16)
+//
+// A is tiled 128 rows at a time along TMEM lanes, B is tiled BN rows at a time
+// along TMEM columns, K in blocks of 64 (one 128-byte swizzle atom).  The
+// same kernel serves both orientations the hot path needs:
+//   * token-major ("normal"):  A = activations [tokens, K], B = weight [out, K]
+//     (prefill / training: many tokens, epilogue owns one token row);
+//   * weight-major ("swap-AB"): A = weight [out, K], B = activations [batch, K]
+//     (decode: batch <= 256 fits one N tile; output written transposed).
+//
+// Warp roles (192 threads, one CTA per SM, persistent over work units):
+//   warp 0      TMA producer: one lane streams A/B boxes into a STAGES-deep
+//               shared-memory ring (mbarrier full/empty handshake).
+//   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma
+//               (128 x BN x 16 per instruction) into one of two accumulators,
+//               commits stage release and accumulator-ready barriers.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4) .. +31), apply the fused epilogue functor, store.
+// The two TMEM accumulators let the epilogue of work unit i overlap the MMAs
+// of unit i+1.  Split-K: a work unit is (m_tile, n_tile, split); the epilogue
+// receives the split index and writes a partial slab that the consumer
+// kernel reduces in a fixed order (deterministic, no atomics).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "ne_device.cuh"
+
+namespace ne {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+struct GemmShape {
+  int M, N, K;          // logical sizes (A rows, B rows, reduction)
+  int m_tiles, n_tiles; // ceil(M/128), ceil(N/BN)
+  int splits;           // split-K factor
+  int kb_per_split;     // k-blocks (of 64) per split
+  int* status;          // device status word (timeouts)
+};
+
+template <int BN>
+struct GemmCfg {
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                   : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int CH = (BN % 32 == 0) ? 32 : 16;   // epilogue column chunk
+  // ring + 1 KB of barriers / bookkeeping + 1 KB alignment slack
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2048;
+};
+
+// ------------------------------------------------------------------ epilogues
+// Each functor: apply(p, m, n0, v[CH], split, M, N).  m is the A-side row,
+// n0 the first B-side column of the chunk; only (m < M, n < N) is stored.
+
+// fp32 store, transposed (swap-AB):  out[split*split_stride + n*ld + m]
+struct EpiF32T {
+  struct Params { float* out; long long ld; long long split_stride; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int split,
+                               int M, int N) {
+    if (m >= M) return;
+    float* base = p.out + (long long)split * p.split_stride + m;
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (n0 + j < N) base[(long long)(n0 + j) * p.ld] = v[j];
+  }
+};
+
+// fp32 store, row-major:  out[split*split_stride + m*ld + n]
+struct EpiF32 {
+  struct Params { float* out; long long ld; long long split_stride; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int split,
+                               int M, int N) {
+    if (m >= M) return;
+    float* row = p.out + (long long)split * p.split_stride + (long long)m * p.ld + n0;
+    if (n0 + CH <= N) {
+#pragma unroll
+      for (int j = 0; j < CH; j += 4)
+        *reinterpret_cast<float4*>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) row[j] = v[j];
+    }
+  }
+};
+
+// bf16 store, row-major:  out[m*ld + n]
+struct EpiBF16 {
+  struct Params { __nv_bfloat16* out; long long ld; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    if (m >= M) return;
+    __nv_bfloat16* row = p.out + (long long)m * p.ld + n0;
+    if (n0 + CH <= N) {
+#pragma unroll
+      for (int j = 0; j < CH; j += 8) {
+        uint4 pk;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+        h[0] = __floats2bfloat162_rn(v[j], v[j + 1]);
+        h[1] = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+        h[2] = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+        h[3] = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(row + j) = pk;
+      }
+    } else {
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) row[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+};
+
+// fp32 residual update, row-major:  x[m*ld + n] += alpha * acc
+struct EpiResid {
+  struct Params { float* x; long long ld; float alpha; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    if (m >= M) return;
+    float* row = p.x + (long long)m * p.ld + n0;
+    if (n0 + CH <= N) {
+#pragma unroll
+      for (int j = 0; j < CH; j += 4) {
+        float4 r = *reinterpret_cast<float4*>(row + j);
+        if (p.alpha == 1.0f) {
+          r.x += v[j]; r.y += v[j + 1]; r.z += v[j + 2]; r.w += v[j + 3];
+        } else {
+          r.x += p.alpha * v[j]; r.y += p.alpha * v[j + 1];
+          r.z += p.alpha * v[j + 2]; r.w += p.alpha * v[j + 3];
+        }
+        *reinterpret_cast<float4*>(row + j) = r;
+      }
+    } else {
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) row[j] += (p.alpha == 1.0f) ? v[j] : p.alpha * v[j];
+    }
+  }
+};
+
+// SwiGLU on a W1/W3 row-interleaved weight (16-row blocks: columns
+// [32c, 32c+16) hold h1 of features [16c, 16c+16), [32c+16, 32c+32) hold h3).
+//   gate[m*ld + 16c + j] = bf16( silu(h1_j) * h3_j )
+// Optionally also stores h1 and h3 (bf16, [m, F]) for the backward pass.
+struct EpiSwiGLU {
+  struct Params { __nv_bfloat16* gate; long long ld; __nv_bfloat16* h1; __nv_bfloat16* h3; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    static_assert(CH == 32, "SwiGLU epilogue needs 32-column chunks");
+    if (m >= M || n0 >= N) return;
+    const long long f0 = n0 >> 1;
+    __nv_bfloat16* g = p.gate + (long long)m * p.ld + f0;
+    float out[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float h1 = v[j], h3 = v[16 + j];
+      out[j] = h1 * (1.0f / (1.0f + __expf(-h1))) * h3;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j += 8) {
+      uint4 pk;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(out[j + 2 * t], out[j + 2 * t + 1]);
+      *reinterpret_cast<uint4*>(g + j) = pk;
+    }
+    if (p.h1 != nullptr) {
+      __nv_bfloat16* a = p.h1 + (long long)m * p.ld + f0;
+      __nv_bfloat16* b = p.h3 + (long long)m * p.ld + f0;
+#pragma unroll
+      for (int j = 0; j < 16; j += 8) {
+        uint4 pa, pb;
+        __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&pa);
+        __nv_bfloat162* hb = reinterpret_cast<__nv_bfloat162*>(&pb);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          ha[t] = __floats2bfloat162_rn(v[j + 2 * t], v[j + 2 * t + 1]);
+          hb[t] = __floats2bfloat162_rn(v[16 + j + 2 * t], v[16 + j + 2 * t + 1]);
+        }
+        *reinterpret_cast<uint4*>(a + j) = pa;
+        *reinterpret_cast<uint4*>(b + j) = pb;
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------------ kernel
+template <int BN, class Epi, int AB_FMT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const GemmShape sh, const typename Epi::Params ep) {
+  using C = GemmCfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int CH = C::CH;
+  constexpr uint32_t IDESC = umma_idesc_f16(GEMM_BM, BN, AB_FMT);
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled tiles
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t tiles = base;                                   // STAGES x (A | B)
+  const uint32_t bars = base + STAGES * C::STAGE_BYTES;          // barriers
+  const uint32_t full_bar = bars;                                // [STAGES]
+  const uint32_t empty_bar = bars + 8 * STAGES;                  // [STAGES]
+  const uint32_t tfull_bar = bars + 16 * STAGES;                 // [2]
+  const uint32_t tempty_bar = bars + 16 * STAGES + 16;           // [2]
+  const uint32_t drain_bar = bars + 16 * STAGES + 32;            // [1]
+  uint8_t* const gbars = gbase + STAGES * C::STAGE_BYTES;
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 16 * STAGES + 40);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 16 * STAGES + 44);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int units = sh.m_tiles * sh.n_tiles * sh.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar + 8 * a, 1);
+      mbar_init(tempty_bar + 8 * a, 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_first();
+      const uint64_t pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int mt = u % sh.m_tiles;
+        const int rest = u / sh.m_tiles;
+        const int nt = rest % sh.n_tiles;
+        const int sp = rest / sh.n_tiles;
+        const int kb0 = sp * sh.kb_per_split;
+        for (int kb = 0; kb < sh.kb_per_split; ++kb) {
+          if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, sh.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar + 8 * stage, C::STAGE_BYTES);
+          const uint32_t sa = tiles + stage * C::STAGE_BYTES;
+          tma_load_2d(sa, &tmA, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM, pol_a);
+          tma_load_2d(sa + C::A_BYTES, &tmB, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN,
+                      pol_b);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: wait (bounded) until the most recent load issued into every
+      // stage has landed, so no TMA write is in flight when the CTA exits.
+      // Stages below `stage` were last filled in the current lap (parity
+      // `phase`), the others in the previous lap (or never: parity 1 on a
+      // fresh barrier reads as complete).
+      for (int s = 0; s < STAGES; ++s) {
+        const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(full_bar + 8 * s, par)) {
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        if (!mbar_wait(tempty_bar + 8 * acc, acc_phase ^ 1u, sh.status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < sh.kb_per_split; ++kb) {
+          if (!mbar_wait(full_bar + 8 * stage, phase, sh.status, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = tiles + stage * C::STAGE_BYTES;
+          const uint64_t adesc = smem_desc_k_sw128(sa);
+          const uint64_t bdesc = smem_desc_k_sw128(sa + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            // advance 16 elements (32 bytes) inside the swizzle atom: +2 in addr>>4
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
+          }
+          umma_commit(empty_bar + 8 * stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar + 8 * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      // Wait (bounded) for every MMA this thread issued before TMEM is freed.
+      umma_commit(drain_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int mt = u % sh.m_tiles;
+      const int rest = u / sh.m_tiles;
+      const int nt = rest % sh.n_tiles;
+      const int sp = rest / sh.n_tiles;
+      if (!mbar_wait(tfull_bar + 8 * acc, acc_phase, sh.status, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int m = mt * GEMM_BM + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += CH) {
+        float v[CH];
+        if constexpr (CH == 32) {
+          uint32_t r[32];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+                "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                "=r"(r[30]), "=r"(r[31])
+              : "r"(t_row + c));
+          asm volatile(
+              "tcgen05.wait::ld.sync.aligned;"
+              : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                "+r"(r[30]), "+r"(r[31])
+              :
+              : "memory");
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        } else {
+          uint32_t r[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+              : "r"(t_row + c));
+          asm volatile(
+              "tcgen05.wait::ld.sync.aligned;"
+              : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+              :
+              : "memory");
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+        }
+        Epi::template apply<CH>(ep, m, nt * BN + c, v, sp, sh.M, sh.N);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar + 8 * acc);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace ne

@@ -1,0 +1,494 @@
+// kernels_elem.cu -- HBM-bound kernels of the token loop and forward pass.
+//
+// Row layout everywhere is token-major: activations are [rows, features]
+// with the feature axis contiguous (the reference keeps channel-first
+// [DIM, SEQ] IOSurfaces, ane-training/training/training_dynamic/io.h:6-62;
+// token-major is the natural layout for TMA-fed GEMMs and coalesced rows).
+//
+//   embed_rmsnorm     x = E[tok] (fp32), xn = bf16(rmsnorm(x) * g)
+//                     (cpu_ops.h:433-439 embed_lookup + cpu_ops.h:20-60)
+//   resid_rmsnorm     x += alpha * sum_s P[s]  (split-K partials, fixed order),
+//                     xn = bf16(rmsnorm(x) * g)   (io.h:25-37 residual + rmsnorm)
+//   qkv_post          sum split partials of the fused QKV projection, optional
+//                     per-head QK RMSNorm, interleaved-pair RoPE
+//                     (tools/generate.py:97-110), write q and append K/V (fp16)
+//                     to the cache (generate.py:159-162)
+//   swiglu_split      gate = silu(h1) * h3 from split partials of the W1/W3
+//                     row-interleaved projection (generate.py:188-190)
+//   argmax_rows       greedy next token, first index of the maximum
+//                     (generate.py:200, numpy argmax tie rule)
+//   decode_attention  split-KV GQA attention of one new query per sequence
+//                     over the fp16 cache (generate.py:164-181), + combine
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "ne_device.cuh"
+#include "ne_internal.h"
+
+namespace ne {
+
+// ---------------------------------------------------------------- helpers
+__device__ __forceinline__ float block_sum(float v, float* red /*[32]*/) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+// rmsnorm of one row held as fp32 in shared memory `xs` (length D), written as
+// bf16 to `out`.  rms = sqrt(mean(x^2) + eps); y = (x / rms) * g  (generate.py:81-84)
+__device__ __forceinline__ void rmsnorm_row_store(const float* xs, const float* g, int D,
+                                                  float eps, __nv_bfloat16* out, float* red) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xs[i] * xs[i];
+  ss = block_sum(ss, red);
+  const float rms = sqrtf(ss / (float)D + eps);
+  for (int i = threadIdx.x * 2; i < D; i += blockDim.x * 2) {
+    const float a = (xs[i] / rms) * g[i];
+    const float b = (xs[i + 1] / rms) * g[i + 1];
+    *reinterpret_cast<__nv_bfloat162*>(out + i) = __floats2bfloat162_rn(a, b);
+  }
+}
+
+// ---------------------------------------------------------------- embed + norm
+// One block per row.  tok: [rows]; table bf16 [V, D] (or fp32 if table_f32).
+__global__ void embed_rmsnorm_kernel(const int32_t* __restrict__ tok, const void* __restrict__ table,
+                                     int table_f32, int V, int D, const float* __restrict__ g,
+                                     float eps, float* __restrict__ x, __nv_bfloat16* __restrict__ xn,
+                                     int* status) {
+  extern __shared__ float sm[];
+  float* xs = sm;
+  float* red = sm + D;
+  const int r = blockIdx.x;
+  int t = tok[r];
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) atomicExch(status, DEV_ERR_BOUNDS);
+    t = 0;
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v;
+    if (table_f32) v = reinterpret_cast<const float*>(table)[(size_t)t * D + i];
+    else v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(table)[(size_t)t * D + i]);
+    xs[i] = v;
+    x[(size_t)r * D + i] = v;
+  }
+  __syncthreads();
+  rmsnorm_row_store(xs, g, D, eps, xn + (size_t)r * D, red);
+}
+
+// ---------------------------------------------------------------- residual + norm
+// x[r] += alpha * sum_{s<nsplit} P[s][r] (nsplit may be 0), then xn = rmsnorm.
+__global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ P,
+                                     int nsplit, long long split_stride, float alpha, int D,
+                                     const float* __restrict__ g, float eps,
+                                     __nv_bfloat16* __restrict__ xn) {
+  extern __shared__ float sm[];
+  float* xs = sm;
+  float* red = sm + D;
+  const int r = blockIdx.x;
+  float* xr = x + (size_t)r * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v = xr[i];
+    if (nsplit > 0) {
+      float acc = 0.f;
+      for (int s = 0; s < nsplit; ++s) acc += P[(size_t)s * split_stride + (size_t)r * D + i];
+      v += (alpha == 1.0f) ? acc : alpha * acc;
+      xr[i] = v;
+    }
+    xs[i] = v;
+  }
+  __syncthreads();
+  rmsnorm_row_store(xs, g, D, eps, xn + (size_t)r * D, red);
+}
+
+// ---------------------------------------------------------------- QKV post
+// One warp per (row, head-vector).  Head vectors per row: Hq + 2*Hkv (q, k, v).
+// qkv row layout (the fused projection's output): [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].
+// Row r belongs to sequence b = r / S_rows at position pos0 + r % S_rows.
+template <int HD, typename QT>
+__global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long long split_stride,
+                                int rows, int S_rows, const int* __restrict__ d_pos, int pos0,
+                                int Hq, int Hkv, const float* __restrict__ qn,
+                                const float* __restrict__ kn, float qk_eps,
+                                const float2* __restrict__ rope_cs, QT* __restrict__ q_out,
+                                __half* __restrict__ kc, __half* __restrict__ vc, int Tmax,
+                                int* status) {
+  constexpr int PER = HD / 32;  // elements per lane (2 or 4), consecutive
+  const int warps_per_block = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int nh = Hq + 2 * Hkv;
+  if (gw >= rows * nh) return;
+  const int r = gw / nh, h = gw % nh;
+  const int lane = threadIdx.x & 31;
+  const int b = r / S_rows;
+  const int pos = (d_pos ? *d_pos : pos0) + r % S_rows;
+  if (pos < 0 || pos >= Tmax) {
+    if (lane == 0) atomicExch(status, DEV_ERR_BOUNDS);
+    return;
+  }
+  const int qkv_dim = (Hq + 2 * Hkv) * HD;
+  const float* src = qkv + (size_t)r * qkv_dim + h * HD + lane * PER;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) v[i] = 0.f;
+  for (int s = 0; s < (nsplit > 0 ? nsplit : 1); ++s) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] += src[(size_t)s * split_stride + i];
+  }
+  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
+  if ((is_q || is_k) && qn != nullptr) {
+    const float* gain = is_q ? qn : kn;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
+    ss = warp_sum(ss);
+    const float rms = sqrtf(ss / (float)HD + qk_eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = (v[i] / rms) * gain[lane * PER + i];
+  }
+  if (is_q || is_k) {
+    // interleaved pairs (2i, 2i+1); this lane holds PER/2 pairs
+    const float2* cs = rope_cs + (size_t)pos * (HD / 2) + lane * (PER / 2);
+#pragma unroll
+    for (int i = 0; i < PER / 2; ++i) {
+      const float2 c = cs[i];  // (cos, sin)
+      const float v0 = v[2 * i], v1 = v[2 * i + 1];
+      v[2 * i] = v0 * c.x - v1 * c.y;
+      v[2 * i + 1] = v0 * c.y + v1 * c.x;
+    }
+  }
+  if (is_q) {
+    QT* dst = q_out + ((size_t)r * Hq + h) * HD + lane * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      if constexpr (sizeof(QT) == 4) dst[i] = v[i];
+      else dst[i] = __float2half_rn(v[i]);
+    }
+  } else {
+    const int kvh = is_k ? (h - Hq) : (h - Hq - Hkv);
+    __half* cache = is_k ? kc : vc;
+    __half* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) dst[i] = __float2half_rn(v[i]);
+  }
+}
+
+// ---------------------------------------------------------------- SwiGLU (split partials)
+// P: [nsplit][rows][2F] fp32 with W1/W3 interleaved in 16-row blocks.
+__global__ void swiglu_split_kernel(const float* __restrict__ P, int nsplit, long long split_stride,
+                                    int rows, int F, __nv_bfloat16* __restrict__ gate) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)rows * F) return;
+  const int r = (int)(idx / F), j = (int)(idx % F);
+  const long long c1 = (long long)r * 2 * F + (j >> 4) * 32 + (j & 15);
+  float h1 = 0.f, h3 = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    h1 += P[(size_t)s * split_stride + c1];
+    h3 += P[(size_t)s * split_stride + c1 + 16];
+  }
+  // generate.py:93-94,190:  silu(h1) * h3,  silu(x) = x * (1 / (1 + exp(-x)))
+  gate[idx] = __float2bfloat16_rn(h1 * (1.0f / (1.0f + expf(-h1))) * h3);
+}
+
+// ---------------------------------------------------------------- argmax
+// One block per row; first index of the maximum (numpy argmax).  Writes the
+// token into next_tok[r] and, when out_tokens is given, into
+// out_tokens[(d_state[1]) * rows + r] (d_state = [pos, step]).
+__global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int32_t* next_tok,
+                                   int32_t* out_tokens, const int* d_state) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * V;
+  float best = -FLT_MAX;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = row[i];
+    if (v > best) { best = v; bi = i; }   // per-thread indices increase: strict > keeps first
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { sv[w] = best; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = (l < nw) ? sv[l] : -FLT_MAX;
+    bi = (l < nw) ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (l == 0) {
+      if (bi == 0x7fffffff) bi = 0;   // all NaN row: deterministic fallback
+      next_tok[r] = bi;
+      if (out_tokens) out_tokens[(size_t)d_state[1] * gridDim.x + r] = bi;
+    }
+  }
+}
+
+// Advance the on-device decode state [pos, step] by one token.
+__global__ void advance_state_kernel(int* d_state) {
+  d_state[0] += 1;
+  d_state[1] += 1;
+}
+
+// ---------------------------------------------------------------- decode attention
+// Grid (n_splits, Hkv, B), 128 threads.  q: fp32 [B][Hq][HD] (already
+// normalised / rotated).  Cache (this layer): fp16 [B][Hkv][Tmax][HD].
+// Attends positions 0 .. *d_pos (inclusive).  Scores are kept in the log2
+// domain: q is pre-multiplied by (1/sqrt(hd)) * log2(e), so exp2 of the
+// shifted score equals exp of the natural-log softmax argument
+// (generate.py:166-176).
+template <int HD, int GROUP>
+__global__ void __launch_bounds__(128)
+decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                   const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos,
+                   int n_splits, float qscale, float* __restrict__ part_o,
+                   float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int Hq) {
+  constexpr int LPP = HD / 8;            // lanes per position (16 B each)
+  constexpr int PPW = 32 / LPP;          // positions per warp step
+  constexpr int SLOTS = 4 * PPW;         // position streams per CTA
+  constexpr int U = 4;                   // positions per stream in flight
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int Hkv = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane % LPP, pidx = lane / LPP;
+  const int slot = warp * PPW + pidx;
+
+  const int T = *d_pos + 1;
+  int chunk = (T + n_splits - 1) / n_splits;
+  chunk = (chunk + 7) & ~7;
+  const int t_begin = split * chunk;
+  const int t_end = min(T, t_begin + chunk);
+
+  float qf[GROUP][8];
+#pragma unroll
+  for (int g = 0; g < GROUP; ++g) {
+    const float* qp = q + ((size_t)b * Hq + kvh * GROUP + g) * HD + sub * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qf[g][i] = qp[i] * qscale;
+  }
+  float m[GROUP], l[GROUP], acc[GROUP][8];
+#pragma unroll
+  for (int g = 0; g < GROUP; ++g) {
+    m[g] = -1e30f;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
+  }
+  const size_t head_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
+  const uint4* kbase = reinterpret_cast<const uint4*>(kc + head_base) + sub;
+  const uint4* vbase = reinterpret_cast<const uint4*>(vc + head_base) + sub;
+
+  // The trip count depends only on the warp (tb is warp-uniform), so every
+  // lane reaches the shuffles below; out-of-range positions are masked.
+  for (int tb = t_begin + warp * PPW; tb < t_end; tb += SLOTS * U) {
+    const int t0 = tb + pidx;
+    uint4 kr[U], vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + u * SLOTS;
+      if (t < t_end) {
+        kr[u] = __ldg(kbase + (size_t)t * LPP);
+        vr[u] = __ldg(vbase + (size_t)t * LPP);
+      } else {
+        kr[u] = make_uint4(0, 0, 0, 0);
+        vr[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + u * SLOTS;
+      float kf[8], vf[8];
+      const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
+      const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __half22float2(kh[i]);
+        const float2 c = __half22float2(vh[i]);
+        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
+        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
+      }
+#pragma unroll
+      for (int g = 0; g < GROUP; ++g) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s += qf[g][i] * kf[i];
+#pragma unroll
+        for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (t < t_end) {
+          const float mn = fmaxf(m[g], s);
+          const float corr = exp2f(m[g] - mn);
+          const float p = exp2f(s - mn);
+          l[g] = l[g] * corr + p;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[g][i] = acc[g][i] * corr + p * vf[i];
+          m[g] = mn;
+        }
+      }
+    }
+  }
+
+  // combine the SLOTS streams of this CTA through shared memory
+  __shared__ float s_m[GROUP][SLOTS], s_l[GROUP][SLOTS];
+  __shared__ float s_acc[GROUP][SLOTS][HD];
+#pragma unroll
+  for (int g = 0; g < GROUP; ++g) {
+    if (sub == 0) { s_m[g][slot] = m[g]; s_l[g][slot] = l[g]; }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s_acc[g][slot][sub * 8 + i] = acc[g][i];
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < GROUP * HD; o += blockDim.x) {
+    const int g = o / HD, d = o % HD;
+    float M = -1e30f;
+#pragma unroll
+    for (int s = 0; s < SLOTS; ++s) M = fmaxf(M, s_m[g][s]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int s = 0; s < SLOTS; ++s) {
+      const float w = exp2f(s_m[g][s] - M);
+      L += s_l[g][s] * w;
+      O += s_acc[g][s][d] * w;
+    }
+    const int h = kvh * GROUP + g;
+    if (n_splits == 1) {
+      out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / L);
+    } else {
+      const size_t pi = ((size_t)b * Hq + h) * n_splits + split;
+      part_o[pi * HD + d] = O;
+      if (d == 0) { part_ml[2 * pi] = M; part_ml[2 * pi + 1] = L; }
+    }
+  }
+}
+
+// Grid (Hq, B), HD threads: merge the split partials of one head.
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                    int n_splits, __nv_bfloat16* __restrict__ out, int Hq) {
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const size_t base = ((size_t)b * Hq + h) * n_splits;
+  float M = -1e30f;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[2 * (base + s)]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float w = exp2f(part_ml[2 * (base + s)] - M);
+    L += part_ml[2 * (base + s) + 1] * w;
+    O += part_o[(base + s) * HD + d] * w;
+  }
+  out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / L);
+}
+
+// ================================================================ launchers
+cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int table_f32, int V, int D,
+                                 const float* g, float eps, float* x, __nv_bfloat16* xn, int rows,
+                                 int* status, cudaStream_t st) {
+  const int threads = D >= 1024 ? 256 : 128;
+  const size_t smem = (size_t)(D + 32) * sizeof(float);
+  embed_rmsnorm_kernel<<<rows, threads, smem, st>>>(tok, table, table_f32, V, D, g, eps, x, xn,
+                                                    status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
+                                 float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
+                                 int rows, cudaStream_t st) {
+  const int threads = D >= 1024 ? 256 : 128;
+  const size_t smem = (size_t)(D + 32) * sizeof(float);
+  resid_rmsnorm_kernel<<<rows, threads, smem, st>>>(x, P, nsplit, split_stride, alpha, D, g, eps,
+                                                    xn);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
+                            int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
+                            const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
+                            void* q_out, int q_fp16, __half* kc, __half* vc, int Tmax, int* status,
+                            cudaStream_t st) {
+  const int warps = rows * (Hq + 2 * Hkv);
+  const int threads = 256;
+  const int blocks = (warps + 7) / 8;
+#define NE_QKV(HD_, QT_)                                                                      \
+  qkv_post_kernel<HD_, QT_><<<blocks, threads, 0, st>>>(                                       \
+      qkv, nsplit, split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs, \
+      reinterpret_cast<QT_*>(q_out), kc, vc, Tmax, status)
+  if (hd == 128) {
+    if (q_fp16) NE_QKV(128, __half); else NE_QKV(128, float);
+  } else if (hd == 64) {
+    if (q_fp16) NE_QKV(64, __half); else NE_QKV(64, float);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+#undef NE_QKV
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
+                                __nv_bfloat16* gate, cudaStream_t st) {
+  const long long n = (long long)rows * F;
+  swiglu_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(P, nsplit, split_stride, rows, F,
+                                                                   gate);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
+                          int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st) {
+  argmax_rows_kernel<<<rows, 1024, 0, st>>>(logits, V, next_tok, out_tokens, d_state);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && adv_state) {
+    advance_state_kernel<<<1, 1, 0, st>>>(d_state);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms) {
+  const int pairs = B * Hkv;
+  int s = (4 * num_sms + pairs - 1) / pairs;
+  const int max_s = (Tmax + 63) / 64;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  return s;
+}
+
+cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
+                               int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
+                               float* part_o, float* part_ml, __nv_bfloat16* out, cudaStream_t st) {
+  const float qscale = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  const dim3 grid(n_splits, Hkv, B);
+  const int group = Hq / Hkv;
+#define NE_ATT(HD_, G_)                                                                          \
+  decode_attn_kernel<HD_, G_><<<grid, 128, 0, st>>>(q, kc, vc, Tmax, d_pos, n_splits, qscale, \
+                                                    part_o, part_ml, out, Hq)
+  if (hd == 128 && group == 2) NE_ATT(128, 2);
+  else if (hd == 128 && group == 1) NE_ATT(128, 1);
+  else if (hd == 64 && group == 1) NE_ATT(64, 1);
+  else if (hd == 64 && group == 2) NE_ATT(64, 2);
+  else return cudaErrorInvalidValue;
+#undef NE_ATT
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n_splits == 1) return e;
+  const dim3 g2(Hq, B);
+  if (hd == 128) attn_combine_kernel<128><<<g2, 128, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
+  else attn_combine_kernel<64><<<g2, 64, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
+  return cudaGetLastError();
+}
+
+}  // namespace ne

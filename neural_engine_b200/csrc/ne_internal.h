@@ -1,0 +1,73 @@
+// ne_internal.h -- declarations shared by the library's translation units.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ne {
+
+// ------------------------------------------------------------------ GEMM
+enum GemmEpi : int {
+  EPI_F32T = 0,    // fp32, transposed store  out[split][n][m]   (swap-AB decode)
+  EPI_F32 = 1,     // fp32, row-major        out[split][m][n]
+  EPI_BF16 = 2,    // bf16, row-major        out[m][n]
+  EPI_RESID = 3,   // fp32 residual          x[m][n] += alpha * acc
+  EPI_SWIGLU = 4,  // bf16 silu(h1)*h3 from a W1/W3 16-row-interleaved operand
+};
+
+struct GemmCall {
+  const void* A = nullptr;  // [M, K] row-major (K contiguous), leading dim lda (elements)
+  long long lda = 0;
+  int M = 0;
+  const void* B = nullptr;  // [N, K] row-major, leading dim ldb
+  long long ldb = 0;
+  int N = 0;
+  int K = 0;
+  int epi = EPI_F32;
+  void* out = nullptr;
+  long long ld = 0;             // output leading dim (elements)
+  long long split_stride = 0;   // elements between split slabs (split-capable epilogues)
+  float alpha = 1.0f;
+  void* aux1 = nullptr;         // SwiGLU: h1 store (optional)
+  void* aux2 = nullptr;         // SwiGLU: h3 store (optional)
+  int splits = 1;               // split-K factor (0 = choose)
+  int bn = 0;                   // N tile (0 = choose)
+  int ab_fp16 = 0;              // 1: fp16 operands, 0: bf16
+  int max_ctas = 0;             // 0 = number of SMs
+};
+
+// Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).
+int gemm_pick_splits(const GemmCall& c, int num_sms);
+cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st);
+int device_num_sms();
+
+// ------------------------------------------------------------------ elementwise
+cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int table_f32, int V, int D,
+                                 const float* g, float eps, float* x, __nv_bfloat16* xn, int rows,
+                                 int* status, cudaStream_t st);
+cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
+                                 float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
+                                 int rows, cudaStream_t st);
+cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
+                            int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
+                            const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
+                            void* q_out, int q_fp16, __half* kc, __half* vc, int Tmax, int* status,
+                            cudaStream_t st);
+cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
+                                __nv_bfloat16* gate, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
+                          int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st);
+int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms);
+cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
+                               int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
+                               float* part_o, float* part_ml, __nv_bfloat16* out, cudaStream_t st);
+
+// ------------------------------------------------------------------ prefill attention
+// q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16
+// [B][Hkv][Tmax][hd] holding positions 0 .. pos0+S-1; out bf16 [B*S][Hq*hd].
+cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half* vc, int B, int S,
+                                int pos0, int Hq, int Hkv, int hd, int Tmax, __nv_bfloat16* out,
+                                cudaStream_t st);
+
+}  // namespace ne

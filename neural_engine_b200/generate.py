@@ -1,0 +1,132 @@
+"""Drop-in for the reference's numpy token loop, running on libne.so.
+
+Mirrors ane-training/training/training_dynamic/tools/generate.py:
+  * ``read_checkpoint(path)`` -> (info, layers, rms_final, embed) like
+    generate.py:18-78, but reading the GQA fields from their real header
+    slots (config.h:89; generate.py:28 reads cum_steps/cum_batches/adam_t);
+  * ``generate(info, layers, rms_final, embed, tokenizer, prompt_tokens,
+    max_tokens, temperature, top_p)`` with the same arguments and return value
+    as generate.py:113-228.  The forward pass runs in the CUDA kernels;
+    greedy decoding (temperature < 1e-6) stays entirely on the device, and
+    sampling pulls the step's logits to the host and applies generate.py's
+    temperature / top-p rule (generate.py:201-215) with numpy's global RNG.
+Extra ``info`` keys select the Qwen3 numerics the reference cannot express:
+``eps``, ``theta``, ``qk_norm`` (with ``q_norm`` / ``k_norm`` gains lists),
+``qk_eps``, ``res_alpha``.
+"""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+
+from .runtime import Engine, ModelConfig
+
+_HDR = "<iiiiiiiiiiffdddiiiiii"
+
+
+def read_checkpoint(path: str):
+    with open(path, "rb") as f:
+        h = struct.unpack(_HDR, f.read(struct.calcsize(_HDR)))
+        magic, version, step = h[0], h[1], h[2]
+        n_layers, vocab, dim, hidden, heads, seq = h[4:10]
+        loss = h[11]
+        kv_heads, hd, q_dim = h[18:21]
+        if magic != 0x424C5A54:
+            raise ValueError(f"Bad magic: {magic:#x}")
+        if version != 4:
+            raise ValueError(f"Unsupported version: {version}")
+        kv_dim = kv_heads * hd
+        info = {"step": step, "loss": loss, "dim": dim, "hidden": hidden, "heads": heads,
+                "kv_heads": kv_heads, "hd": hd, "q_dim": q_dim, "kv_dim": kv_dim,
+                "gqa_ratio": heads // kv_heads, "n_layers": n_layers, "vocab": vocab}
+        shapes = [("Wq", (q_dim, dim)), ("Wk", (kv_dim, dim)), ("Wv", (kv_dim, dim)),
+                  ("Wo", (dim, q_dim)), ("W1", (hidden, dim)), ("W2", (dim, hidden)),
+                  ("W3", (hidden, dim)), ("rms_att", (dim,)), ("rms_ffn", (dim,))]
+        layers = []
+        for _ in range(n_layers):
+            lw = {}
+            for name, shp in shapes:
+                n = int(np.prod(shp))
+                lw[name] = np.frombuffer(f.read(4 * n), np.float32).reshape(shp).copy()
+            for _, shp in shapes:                       # Adam m, v
+                f.seek(8 * int(np.prod(shp)), 1)
+            layers.append(lw)
+        rms_final = np.frombuffer(f.read(4 * dim), np.float32).copy()
+        f.seek(8 * dim, 1)
+        embed = np.frombuffer(f.read(4 * vocab * dim), np.float32).reshape(vocab, dim).copy()
+        f.seek(8 * vocab * dim, 1)
+        tail = f.read(4)
+        if tail == b"QKN1":
+            nl, hd2 = struct.unpack("<ii", f.read(8))
+            qn, kn = [], []
+            for _ in range(nl):
+                qn.append(np.frombuffer(f.read(4 * hd2), np.float32).copy())
+                kn.append(np.frombuffer(f.read(4 * hd2), np.float32).copy())
+                f.seek(16 * hd2, 1)
+            info["qk_norm"] = True
+            info["q_norm"], info["k_norm"] = qn, kn
+    return info, layers, rms_final, embed
+
+
+def config_from_info(info: dict) -> ModelConfig:
+    return ModelConfig(n_layers=info["n_layers"], dim=info["dim"], hidden=info["hidden"],
+                       heads=info["heads"], kv_heads=info["kv_heads"], head_dim=info["hd"],
+                       vocab=info["vocab"], eps=info.get("eps", 1e-5),
+                       theta=info.get("theta", 10000.0), qk_norm=bool(info.get("qk_norm", False)),
+                       qk_eps=info.get("qk_eps", 1e-6), res_alpha=info.get("res_alpha", 1.0))
+
+
+def _softmax(x):
+    x = x - np.max(x)
+    e = np.exp(x)
+    return e / np.sum(e)
+
+
+def generate(info, layers, rms_final, embed, tokenizer, prompt_tokens, max_tokens, temperature,
+             top_p, engine: Engine | None = None):
+    """Autoregressive generation with KV cache (generate.py:113-228)."""
+    cfg = config_from_info(info)
+    prompt = np.asarray(list(prompt_tokens), np.int32)
+    if engine is None:
+        engine = Engine(cfg)
+        qk = None
+        if cfg.qk_norm:
+            qk = list(zip(info["q_norm"], info["k_norm"]))
+        engine.set_weights(layers, rms_final, embed, qk)
+    max_seq = len(prompt) + max_tokens
+    if engine.max_batch < 1 or engine.max_seq < max_seq:
+        engine.kv_alloc(1, max_seq)
+    generated = []
+    greedy = temperature < 1e-6
+    if greedy:
+        nxt, logits = engine.prefill(prompt[None], 0), None
+    else:
+        nxt, logits = engine.prefill(prompt[None], 0, return_logits=True)
+    pos = len(prompt)
+    for i in range(max_tokens):
+        if greedy:
+            tok = int(nxt[0])                                         # generate.py:200
+        else:
+            lg = logits[0] / temperature                              # :202
+            probs = _softmax(lg)
+            if top_p < 1.0:                                           # :206-213
+                sorted_idx = np.argsort(-probs)
+                cum = np.cumsum(probs[sorted_idx])
+                cutoff = np.searchsorted(cum, top_p) + 1
+                mask = np.zeros(cfg.vocab, dtype=np.float32)
+                mask[sorted_idx[:cutoff]] = probs[sorted_idx[:cutoff]]
+                mask /= mask.sum()
+                probs = mask
+            tok = int(np.random.choice(cfg.vocab, p=probs))           # :215
+        generated.append(tok)
+        print(tokenizer.decode([tok]), end="", flush=True)            # :220-221
+        if tok == tokenizer.eos_token_id or i == max_tokens - 1:      # :224
+            break
+        if greedy:
+            nxt = engine.decode_step(np.array([tok], np.int32), pos)
+        else:
+            nxt, logits = engine.decode_step(np.array([tok], np.int32), pos, return_logits=True)
+        pos += 1
+    print()
+    return generated

@@ -1,0 +1,245 @@
+"""ctypes binding of libne.so (the C ABI declared in include/ne.h).
+
+The library is the product: every computation below happens in its sm_100a
+kernels.  There is no CPU fallback -- if libne.so is missing or cannot be
+loaded, importing the runtime raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libne.so")
+
+# ne_status values (include/ne.h)
+NE_OK = 0
+STATUS_NAMES = {0: "NE_OK", 1: "NE_ERR_INVALID", 2: "NE_ERR_CUDA", 3: "NE_ERR_OOM",
+                4: "NE_ERR_IO", 5: "NE_ERR_FORMAT", 6: "NE_ERR_TIMEOUT",
+                7: "NE_ERR_UNSUPPORTED", 8: "NE_ERR_STATE", 9: "NE_ERR_BOUNDS"}
+
+# every entry point include/ne.h declares
+EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "ne_get_cfg",
+            "ne_version", "ne_set_layer_weights", "ne_set_global_weights", "ne_load_ckpt_v4",
+            "ne_kv_alloc", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
+            "ne_decode_loop_device", "ne_gemm_device", "ne_gemm_device_ex",
+            "ne_decode_kernels_per_step")
+
+
+class NeError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+class ModelCfgC(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("dim", C.c_int), ("hidden", C.c_int),
+                ("n_heads", C.c_int), ("kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("vocab", C.c_int), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+                ("qk_norm", C.c_int), ("qk_eps", C.c_float), ("res_alpha", C.c_float)]
+
+
+class CkptInfoC(C.Structure):
+    _fields_ = [("step", C.c_int), ("total_steps", C.c_int), ("seq_len", C.c_int),
+                ("adam_t", C.c_int), ("lr", C.c_float), ("loss", C.c_float),
+                ("cum_compile", C.c_double), ("cum_train", C.c_double),
+                ("cum_wall", C.c_double), ("cum_steps", C.c_int), ("cum_batches", C.c_int),
+                ("has_qk_norm", C.c_int)]
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Run-time model description (the reference fixes it at compile time in
+    ane-training/training/training_dynamic/models/*.h)."""
+    n_layers: int
+    dim: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    vocab: int
+    eps: float = 1e-5
+    theta: float = 10000.0
+    qk_norm: bool = False
+    qk_eps: float = 1e-6
+    res_alpha: float = 1.0
+
+    @property
+    def q_dim(self):
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self):
+        return self.kv_heads * self.head_dim
+
+    def to_c(self) -> ModelCfgC:
+        return ModelCfgC(self.n_layers, self.dim, self.hidden, self.heads, self.kv_heads,
+                         self.head_dim, self.vocab, self.eps, self.theta, int(self.qk_norm),
+                         self.qk_eps, self.res_alpha)
+
+    @classmethod
+    def from_any(cls, c) -> "ModelConfig":
+        names = ("n_layers", "dim", "hidden", "heads", "kv_heads", "head_dim", "vocab", "eps",
+                 "theta", "qk_norm", "qk_eps", "res_alpha")
+        return cls(**{n: getattr(c, n) for n in names})
+
+
+STORIES110M = ModelConfig(12, 768, 2048, 12, 12, 64, 32000)
+QWEN3_06B = ModelConfig(28, 1024, 3072, 16, 8, 128, 151936, eps=1e-6, theta=1e6, qk_norm=True)
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> C.CDLL:
+    """Load libne.so; raises if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} not built; run `python -m neural_engine_b200.build`")
+    lib = C.CDLL(path)
+    P, I, LL, F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
+    lib.ne_init.argtypes = [C.POINTER(P), C.POINTER(ModelCfgC), I]
+    lib.ne_free.argtypes = [P]
+    lib.ne_free.restype = None
+    lib.ne_last_error.argtypes = [P]
+    lib.ne_last_error.restype = C.c_char_p
+    lib.ne_status_str.argtypes = [I]
+    lib.ne_status_str.restype = C.c_char_p
+    lib.ne_version.restype = C.c_char_p
+    lib.ne_sync.argtypes = [P]
+    lib.ne_get_cfg.argtypes = [P, C.POINTER(ModelCfgC)]
+    lib.ne_set_layer_weights.argtypes = [P, I] + [P] * 11
+    lib.ne_set_global_weights.argtypes = [P, P, P]
+    lib.ne_load_ckpt_v4.argtypes = [P, C.c_char_p, C.POINTER(CkptInfoC)]
+    lib.ne_kv_alloc.argtypes = [P, I, I]
+    lib.ne_prefill.argtypes = [P, P, I, I, I, P, P]
+    lib.ne_decode_step.argtypes = [P, P, I, I, P, P]
+    lib.ne_generate.argtypes = [P, P, I, I, I, P]
+    lib.ne_prefill_device.argtypes = [P, P, I, I, I, P]
+    lib.ne_decode_loop_device.argtypes = [P, P, I, I, I, P]
+    lib.ne_gemm_device.argtypes = [P, P, LL, I, P, LL, I, I, I, P, LL, F]
+    lib.ne_gemm_device_ex.argtypes = [P, P, LL, I, P, LL, I, I, I, P, LL, F, I, I, LL,
+                                      C.POINTER(C.c_int)]
+    lib.ne_decode_kernels_per_step.argtypes = [P, I]
+    _lib = lib
+    return lib
+
+
+def _ptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Engine:
+    """One GPU context of libne.so (one model, its weights and KV cache)."""
+
+    def __init__(self, cfg, device: int = 0):
+        self.lib = load_library()
+        self.cfg = ModelConfig.from_any(cfg)
+        self._ctx = C.c_void_p()
+        c = self.cfg.to_c()
+        st = self.lib.ne_init(C.byref(self._ctx), C.byref(c), int(device))
+        if st != NE_OK:
+            raise NeError(st, f"ne_init failed ({self.lib.ne_status_str(st).decode()})")
+        self.max_batch = 0
+        self.max_seq = 0
+
+    # -- plumbing
+    def _check(self, st: int):
+        if st != NE_OK:
+            raise NeError(st, self.lib.ne_last_error(self._ctx).decode())
+
+    def close(self):
+        if self._ctx:
+            self.lib.ne_free(self._ctx)
+            self._ctx = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._ctx
+
+    def sync(self):
+        self._check(self.lib.ne_sync(self._ctx))
+
+    # -- weights
+    def set_weights(self, layers, rms_final, embed, qk=None):
+        f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+        for l, lw in enumerate(layers):
+            t = [f32(lw[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3", "rms_att", "rms_ffn")]
+            qn = kn = None
+            if qk is not None:
+                qn, kn = f32(qk[l][0]), f32(qk[l][1])
+            self._check(self.lib.ne_set_layer_weights(self._ctx, l, *[_ptr(a) for a in t],
+                                                      _ptr(qn), _ptr(kn)))
+        self._check(self.lib.ne_set_global_weights(self._ctx, _ptr(f32(rms_final)), _ptr(f32(embed))))
+
+    def load_checkpoint(self, path: str) -> dict:
+        info = CkptInfoC()
+        self._check(self.lib.ne_load_ckpt_v4(self._ctx, path.encode(), C.byref(info)))
+        return {f: getattr(info, f) for f, _ in CkptInfoC._fields_}
+
+    # -- token loop
+    def kv_alloc(self, max_batch: int, max_seq: int):
+        self._check(self.lib.ne_kv_alloc(self._ctx, int(max_batch), int(max_seq)))
+        self.max_batch, self.max_seq = int(max_batch), int(max_seq)
+
+    def prefill(self, tokens: np.ndarray, pos0: int = 0, return_logits: bool = False):
+        tokens = np.ascontiguousarray(np.atleast_2d(tokens), dtype=np.int32)
+        B, S = tokens.shape
+        nxt = np.zeros(B, np.int32)
+        lg = np.zeros((B, self.cfg.vocab), np.float32) if return_logits else None
+        self._check(self.lib.ne_prefill(self._ctx, _ptr(tokens), B, S, int(pos0), _ptr(nxt), _ptr(lg)))
+        return (nxt, lg) if return_logits else nxt
+
+    def decode_step(self, tok: np.ndarray, pos: int, return_logits: bool = False):
+        tok = np.ascontiguousarray(np.atleast_1d(tok), dtype=np.int32)
+        B = tok.shape[0]
+        nxt = np.zeros(B, np.int32)
+        lg = np.zeros((B, self.cfg.vocab), np.float32) if return_logits else None
+        self._check(self.lib.ne_decode_step(self._ctx, _ptr(tok), B, int(pos), _ptr(nxt), _ptr(lg)))
+        return (nxt, lg) if return_logits else nxt
+
+    def generate_greedy(self, prompt: np.ndarray, n_new: int) -> np.ndarray:
+        prompt = np.ascontiguousarray(np.atleast_2d(prompt), dtype=np.int32)
+        B, P = prompt.shape
+        out = np.zeros((B, n_new), np.int32)
+        self._check(self.lib.ne_generate(self._ctx, _ptr(prompt), B, P, int(n_new), _ptr(out)))
+        return out
+
+    # -- device-resident (pointers are device addresses, e.g. torch .data_ptr())
+    def prefill_device(self, d_tokens: int, B: int, S: int, pos0: int, d_next: int):
+        self._check(self.lib.ne_prefill_device(self._ctx, C.c_void_p(d_tokens), B, S, pos0,
+                                               C.c_void_p(d_next)))
+
+    def decode_loop_device(self, d_tok: int, B: int, pos0: int, n_steps: int, d_out: int | None):
+        self._check(self.lib.ne_decode_loop_device(self._ctx, C.c_void_p(d_tok), B, pos0, n_steps,
+                                                   C.c_void_p(d_out) if d_out else None))
+
+    def gemm_device_ex(self, d_a: int, lda: int, M: int, d_b: int, ldb: int, N: int, K: int,
+                       epi: int, d_out: int, ld: int, alpha: float = 1.0, bn: int = 0,
+                       splits: int = 1, split_stride: int = 0) -> int:
+        used = C.c_int(0)
+        self._check(self.lib.ne_gemm_device_ex(self._ctx, C.c_void_p(d_a), lda, M, C.c_void_p(d_b),
+                                               ldb, N, K, epi, C.c_void_p(d_out), ld, alpha, bn,
+                                               splits, split_stride, C.byref(used)))
+        return used.value
+
+    def kernels_per_step(self, B: int) -> int:
+        return int(self.lib.ne_decode_kernels_per_step(self._ctx, B))
+
+    def gemm_device(self, d_a: int, lda: int, M: int, d_b: int, ldb: int, N: int, K: int,
+                    epi: int, d_out: int, ld: int, alpha: float = 1.0):
+        self._check(self.lib.ne_gemm_device(self._ctx, C.c_void_p(d_a), lda, M, C.c_void_p(d_b), ldb,
+                                            N, K, epi, C.c_void_p(d_out), ld, alpha))

@@ -1,0 +1,22 @@
+"""pytest configuration: the ``gpu`` marker and shared fixtures.
+
+Tests marked ``gpu`` need a B200 (sm_100a) and the built libne.so; everything
+else runs on the CPU (``pytest -m "not gpu"``).
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 GPU and the built libne.so")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return os.path.join(ROOT, "tests", "golden")
