@@ -161,6 +161,18 @@ NE_API ne_status ne_gemm_device_ex(ne_ctx* ctx, const void* d_A, long long lda, 
                                    void* d_out, long long ld, float alpha, int bn, int splits,
                                    long long split_stride, int* h_splits);
 
+/* The context's CUDA stream (a cudaStream_t), for events and interop. */
+NE_API void* ne_get_stream(const ne_ctx* ctx);
+
+/* Instrumented decode step: runs one step for B sequences at position pos
+ * WITHOUT the graph, with CUDA events around every kernel group, and adds the
+ * device time (ms) of each group to h_ms[NE_PROF_GROUPS]:
+ *   0 QKV GEMM   1 qkv_post   2 decode attention (+combine)   3 Wo GEMM
+ *   4 residual+RMSNorm   5 W1/W3 GEMM   6 SwiGLU   7 W2 GEMM   8 LM-head GEMM
+ *   9 embed + argmax + state */
+#define NE_PROF_GROUPS 10
+NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms);
+
 /* Kernel launches enqueued by the last ne_decode_loop_device step graph
  * (per step), for launch accounting. */
 NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B);

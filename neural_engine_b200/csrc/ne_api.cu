@@ -107,6 +107,12 @@ struct ne_ctx {
 
   std::map<int, DecodeGraph> graphs;
 
+  // instrumented-step profiling (ne_profile_decode_step)
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<int> prof_groups;
+  int prof_n = 0;
+
   int qkv_dim() const { return (cfg.n_heads + 2 * cfg.kv_heads) * cfg.head_dim; }
   int q_dim() const { return cfg.n_heads * cfg.head_dim; }
   int kv_dim() const { return cfg.kv_heads * cfg.head_dim; }
@@ -205,6 +211,14 @@ ne_status check_status(ne_ctx* ctx) {
   return NE_OK;
 }
 
+// Record an event closing a kernel group when profiling is on.
+void prof_mark(ne_ctx* ctx, int group) {
+  if (!ctx->prof_on || ctx->prof_n >= (int)ctx->prof_events.size()) return;
+  cudaEventRecord(ctx->prof_events[ctx->prof_n], ctx->st);
+  ctx->prof_groups[ctx->prof_n] = group;
+  ctx->prof_n++;
+}
+
 bool ready(ne_ctx* ctx) { return ctx->global_set && ctx->layer_set_count == (unsigned)ctx->cfg.n_layers; }
 
 // ------------------------------------------------------------------ decode step
@@ -214,38 +228,51 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
   const int D = m.dim, F = m.hidden, Hq = m.n_heads, Hkv = m.kv_heads, hd = m.head_dim;
   const int qkv_dim = ctx->qkv_dim(), q_dim = ctx->q_dim();
   ne_status s;
+  prof_mark(ctx, 9);
   NE_LAUNCH(launch_embed_rmsnorm(ctx->tok, ctx->embed, 0, m.vocab, D, ctx->L[0].rms_att, m.rms_eps,
                                  ctx->x, ctx->xn, B, ctx->d_status, ctx->st));
+  prof_mark(ctx, 9);
   const size_t kv_layer = ctx->layer_kv_elems();
   for (int l = 0; l < m.n_layers; ++l) {
     const LayerW& w = ctx->L[l];
     int sp = 1;
     if ((s = gemm_decode(ctx, w.wqkv, qkv_dim, D, ctx->xn, D, B, ctx->part, 0, &sp)) != NE_OK)
       return s;
+    prof_mark(ctx, 0);
     __half* kc = ctx->kcache + kv_layer * l;
     __half* vc = ctx->vcache + kv_layer * l;
     NE_LAUNCH(launch_qkv_post(ctx->part, sp, (long long)B * qkv_dim, B, 1, ctx->state, 0, Hq, Hkv,
                               hd, m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                               m.qk_eps, ctx->rope_cs, ctx->q, 0, kc, vc, ctx->max_seq,
                               ctx->d_status, ctx->st));
+    prof_mark(ctx, 1);
     NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
                                  ctx->attn_splits, ctx->attn_po, ctx->attn_ml, ctx->attn, ctx->st));
     if (ctx->attn_splits > 1) ctx->launches++;  // combine kernel
+    prof_mark(ctx, 2);
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->part, 0, &sp)) != NE_OK)
       return s;
+    prof_mark(ctx, 3);
     NE_LAUNCH(launch_resid_rmsnorm(ctx->x, ctx->part, sp, (long long)B * D, m.res_alpha, D,
                                    w.rms_ffn, m.rms_eps, ctx->xn, B, ctx->st));
+    prof_mark(ctx, 4);
     if ((s = gemm_decode(ctx, w.w13, 2 * F, D, ctx->xn, D, B, ctx->part, 0, &sp)) != NE_OK) return s;
+    prof_mark(ctx, 5);
     NE_LAUNCH(launch_swiglu_split(ctx->part, sp, (long long)B * 2 * F, B, F, ctx->gate, ctx->st));
+    prof_mark(ctx, 6);
     if ((s = gemm_decode(ctx, w.w2, D, F, ctx->gate, F, B, ctx->part, 0, &sp)) != NE_OK) return s;
+    prof_mark(ctx, 7);
     const float* next_g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
     NE_LAUNCH(launch_resid_rmsnorm(ctx->x, ctx->part, sp, (long long)B * D, m.res_alpha, D, next_g,
                                    m.rms_eps, ctx->xn, B, ctx->st));
+    prof_mark(ctx, 4);
   }
   if ((s = gemm_decode(ctx, ctx->embed, m.vocab, D, ctx->xn, D, B, ctx->logits, 1, nullptr)) != NE_OK)
     return s;
+  prof_mark(ctx, 8);
   NE_LAUNCH(launch_argmax(ctx->logits, B, m.vocab, ctx->tok, d_out_tokens, ctx->state, 1, ctx->st));
   ctx->launches++;  // state advance kernel
+  prof_mark(ctx, 9);
   return NE_OK;
 }
 
@@ -341,6 +368,8 @@ ne_status free_workspace(ne_ctx* ctx) {
     if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
   }
   ctx->graphs.clear();
+  for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
+  ctx->prof_events.clear();
   void* ptrs[] = {ctx->kcache, ctx->vcache, ctx->rope_cs, ctx->x, ctx->xn, ctx->part, ctx->q,
                   ctx->attn, ctx->attn_po, ctx->attn_ml, ctx->gate, ctx->logits, ctx->tok,
                   ctx->state, ctx->out_tokens, ctx->pf_x, ctx->pf_xn, ctx->pf_qkv, ctx->pf_q,
@@ -702,6 +731,40 @@ NE_API ne_status ne_gemm_device_ex(ne_ctx* ctx, const void* d_A, long long lda, 
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
   return NE_OK;
+}
+
+NE_API void* ne_get_stream(const ne_ctx* ctx) { return ctx ? (void*)ctx->st : nullptr; }
+
+NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms) {
+  if (!ctx || !h_ms || B <= 0) return NE_ERR_INVALID;
+  if (!ready(ctx)) return fail(ctx, NE_ERR_STATE, "weights not set");
+  if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
+  if (B > ctx->max_batch || pos < 0 || pos >= ctx->max_seq)
+    return fail(ctx, NE_ERR_INVALID, "batch or position exceeds the allocated KV cache");
+  NE_CUDA(cudaSetDevice(ctx->device));
+  const int need = 4 + 9 * ctx->cfg.n_layers + 8;
+  while ((int)ctx->prof_events.size() < need) {
+    cudaEvent_t e;
+    NE_CUDA(cudaEventCreate(&e));
+    ctx->prof_events.push_back(e);
+  }
+  ctx->prof_groups.assign(ctx->prof_events.size(), 0);
+  const int st0[2] = {pos, 0};
+  NE_CUDA(cudaMemcpyAsync(ctx->state, st0, sizeof(st0), cudaMemcpyHostToDevice, ctx->st));
+  ctx->prof_on = true;
+  ctx->prof_n = 0;
+  ctx->launches = 0;
+  ne_status s = enqueue_decode_step(ctx, B, nullptr);
+  ctx->prof_on = false;
+  if (s != NE_OK) return s;
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  for (int i = 1; i < ctx->prof_n; ++i) {
+    float ms = 0.f;
+    NE_CUDA(cudaEventElapsedTime(&ms, ctx->prof_events[i - 1], ctx->prof_events[i]));
+    const int g = ctx->prof_groups[i];
+    if (g >= 0 && g < NE_PROF_GROUPS) h_ms[g] += ms;
+  }
+  return check_status(ctx);
 }
 
 NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B) {

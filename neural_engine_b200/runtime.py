@@ -26,7 +26,10 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_version", "ne_set_layer_weights", "ne_set_global_weights", "ne_load_ckpt_v4",
             "ne_kv_alloc", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
             "ne_decode_loop_device", "ne_gemm_device", "ne_gemm_device_ex",
-            "ne_decode_kernels_per_step")
+            "ne_decode_kernels_per_step", "ne_get_stream", "ne_profile_decode_step")
+
+PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
+               "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
 
 
 class NeError(RuntimeError):
@@ -125,6 +128,9 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_gemm_device_ex.argtypes = [P, P, LL, I, P, LL, I, I, I, P, LL, F, I, I, LL,
                                       C.POINTER(C.c_int)]
     lib.ne_decode_kernels_per_step.argtypes = [P, I]
+    lib.ne_get_stream.argtypes = [P]
+    lib.ne_get_stream.restype = P
+    lib.ne_profile_decode_step.argtypes = [P, I, I, C.POINTER(C.c_float)]
     _lib = lib
     return lib
 
@@ -235,6 +241,17 @@ class Engine:
                                                ldb, N, K, epi, C.c_void_p(d_out), ld, alpha, bn,
                                                splits, split_stride, C.byref(used)))
         return used.value
+
+    @property
+    def stream_ptr(self) -> int:
+        """cudaStream_t of the context (wrap with torch.cuda.ExternalStream)."""
+        return int(self.lib.ne_get_stream(self._ctx) or 0)
+
+    def profile_decode_step(self, B: int, pos: int) -> dict:
+        """Device ms per kernel group of one un-graphed decode step."""
+        arr = (C.c_float * len(PROF_GROUPS))()
+        self._check(self.lib.ne_profile_decode_step(self._ctx, B, pos, arr))
+        return {g: float(arr[i]) for i, g in enumerate(PROF_GROUPS)}
 
     def kernels_per_step(self, B: int) -> int:
         return int(self.lib.ne_decode_kernels_per_step(self._ctx, B))

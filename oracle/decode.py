@@ -72,6 +72,12 @@ def rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, hd: int) -> np.ndarray
     return out.astype(F32).reshape(shp)
 
 
+def _lin(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """x[..., in] @ w[out, in]^T as one 2-D BLAS call (a batched 3-D matmul
+    would re-read w once per leading index)."""
+    return (x.reshape(-1, x.shape[-1]) @ w.T).reshape(x.shape[:-1] + (w.shape[0],))
+
+
 class Decoder:
     """KV-cached batched forward (generate.py:113-195)."""
 
@@ -107,9 +113,9 @@ class Decoder:
         x = self.embed[tokens].astype(F32)                         # generate.py:142  [B,S,D]
         for L, lw in enumerate(self.layers):
             xn = rmsnorm(x, lw["rms_att"], cfg.eps)                  # :149
-            q = xn @ lw["Wq"].T                                      # :151
-            k = xn @ lw["Wk"].T                                      # :152
-            v = xn @ lw["Wv"].T                                      # :153
+            q = _lin(xn, lw["Wq"])                                     # :151
+            k = _lin(xn, lw["Wk"])                                     # :152
+            v = _lin(xn, lw["Wv"])                                     # :153
             if cfg.qk_norm:
                 qn, kn = self.qk[L]
                 q = rmsnorm(q.reshape(B, S, H, hd), qn, cfg.qk_eps).reshape(B, S, H * hd)
@@ -129,22 +135,22 @@ class Decoder:
             p = softmax(sc)
             o = p @ vc[:, :, None]                                            # [B,Hkv,grp,S,hd]
             attn = o.transpose(0, 3, 1, 2, 4).reshape(B, S, H * hd).astype(F32)
-            o_proj = attn @ lw["Wo"].T
+            o_proj = _lin(attn, lw["Wo"])
             if cfg.res_alpha != 1.0:                                          # train.m:441
                 o_proj = o_proj * F32(cfg.res_alpha)
             x = x + o_proj                                                    # :184
             xn = rmsnorm(x, lw["rms_ffn"], cfg.eps)                           # :187
-            h1 = xn @ lw["W1"].T                                              # :188
-            h3 = xn @ lw["W3"].T                                              # :189
+            h1 = _lin(xn, lw["W1"])                                             # :188
+            h3 = _lin(xn, lw["W3"])                                             # :189
             h1 = silu(h1) * h3                                                # :190
-            f_proj = h1 @ lw["W2"].T
+            f_proj = _lin(h1, lw["W2"])
             if cfg.res_alpha != 1.0:                                          # mil_dynamic.h:294-298
                 f_proj = f_proj * F32(cfg.res_alpha)
             x = x + f_proj                                                    # :191
         if last_only:
             x = x[:, -1]
         x = rmsnorm(x, self.rms_final, cfg.eps)                               # :194
-        return (x @ self.embed.T).astype(F32)                                 # :195 tied
+        return _lin(x, self.embed).astype(F32)                                # :195 tied
 
 
 def greedy_generate(cfg: ModelCfg, layers, rms_final, embed, prompt: np.ndarray,
