@@ -177,6 +177,31 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
  * (per step), for launch accounting. */
 NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B);
 
+/* ---- allocation-free split-K product --------------------------------------
+ * No counterpart in the reference: an addition for callers that must not
+ * allocate device memory -- code running inside an allocator hook or a memory
+ * pool callback, plug-ins whose host process owns every device allocation,
+ * start-up code that runs before the caller's allocator exists.  It needs no
+ * ne_ctx (creating one allocates).
+ *
+ * d_out[m*ld + n] = sum_k A[m,k] * B[n,k] in fp32 (the same product as
+ * ne_gemm_device with epi 1), bf16 operands as there, computed with `splits`
+ * split-K slices whose partial slabs live in a static device array of
+ * NE_NOALLOC_SCRATCH_FLOATS floats (8 MiB) that every GPU loading the library
+ * holds until exit.  Nothing is allocated: no cudaMalloc / cudaFree / pools.
+ *   - Returns NE_ERR_INVALID if splits * M * N > NE_NOALLOC_SCRATCH_FLOATS,
+ *     if K is not a multiple of 64 or K/64 is not a multiple of `splits`.
+ *   - Runs on `stream` (a cudaStream_t; NULL = default stream) of the current
+ *     device and synchronises it before returning (NE_ERR_TIMEOUT reports a
+ *     kernel wait that expired).
+ *   - The first call on a device looks up the array's device address; make it
+ *     before any stream capture.
+ *   - All calls share the one array: calls whose GPU work overlaps race. */
+#define NE_NOALLOC_SCRATCH_FLOATS ((size_t)2 * 1024 * 1024)
+NE_API ne_status ne_gemm_splitk_noalloc(const void* d_A, long long lda, int M, const void* d_B,
+                                        long long ldb, int N, int K, int splits, float* d_out,
+                                        long long ld, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,7 +26,8 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_version", "ne_set_layer_weights", "ne_set_global_weights", "ne_load_ckpt_v4",
             "ne_kv_alloc", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
             "ne_decode_loop_device", "ne_gemm_device", "ne_gemm_device_ex",
-            "ne_decode_kernels_per_step", "ne_get_stream", "ne_profile_decode_step")
+            "ne_decode_kernels_per_step", "ne_get_stream", "ne_profile_decode_step",
+            "ne_gemm_splitk_noalloc")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
