@@ -335,7 +335,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int rest = u / sh.m_tiles;
       const int nt = rest % sh.n_tiles;
       const int sp = rest / sh.n_tiles;
-      if (!mbar_wait(tfull_bar + 8 * acc, acc_phase, sh.status, abort_flag)) break;
+      // warp-uniform outcome: tcgen05.ld below is a warp-collective instruction
+      const bool ready = mbar_wait(tfull_bar + 8 * acc, acc_phase, sh.status, abort_flag);
+      if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int m = mt * GEMM_BM + row_in_tile;

@@ -17,8 +17,6 @@
 //                     row-interleaved projection (generate.py:188-190)
 //   argmax_rows       greedy next token, first index of the maximum
 //                     (generate.py:200, numpy argmax tie rule)
-//   decode_attention  split-KV GQA attention of one new query per sequence
-//                     over the fp16 cache (generate.py:164-181), + combine
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -249,153 +247,6 @@ __global__ void advance_state_kernel(int* d_state) {
   d_state[1] += 1;
 }
 
-// ---------------------------------------------------------------- decode attention
-// Grid (n_splits, Hkv, B), 128 threads.  q: fp32 [B][Hq][HD] (already
-// normalised / rotated).  Cache (this layer): fp16 [B][Hkv][Tmax][HD].
-// Attends positions 0 .. *d_pos (inclusive).  Scores are kept in the log2
-// domain: q is pre-multiplied by (1/sqrt(hd)) * log2(e), so exp2 of the
-// shifted score equals exp of the natural-log softmax argument
-// (generate.py:166-176).
-template <int HD, int GROUP>
-__global__ void __launch_bounds__(128)
-decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                   const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos,
-                   int n_splits, float qscale, float* __restrict__ part_o,
-                   float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int Hq) {
-  constexpr int LPP = HD / 8;            // lanes per position (16 B each)
-  constexpr int PPW = 32 / LPP;          // positions per warp step
-  constexpr int SLOTS = 4 * PPW;         // position streams per CTA
-  constexpr int U = 4;                   // positions per stream in flight
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int Hkv = gridDim.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane % LPP, pidx = lane / LPP;
-  const int slot = warp * PPW + pidx;
-
-  const int T = *d_pos + 1;
-  int chunk = (T + n_splits - 1) / n_splits;
-  chunk = (chunk + 7) & ~7;
-  const int t_begin = split * chunk;
-  const int t_end = min(T, t_begin + chunk);
-
-  float qf[GROUP][8];
-#pragma unroll
-  for (int g = 0; g < GROUP; ++g) {
-    const float* qp = q + ((size_t)b * Hq + kvh * GROUP + g) * HD + sub * 8;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qf[g][i] = qp[i] * qscale;
-  }
-  float m[GROUP], l[GROUP], acc[GROUP][8];
-#pragma unroll
-  for (int g = 0; g < GROUP; ++g) {
-    m[g] = -1e30f;
-    l[g] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
-  }
-  const size_t head_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
-  const uint4* kbase = reinterpret_cast<const uint4*>(kc + head_base) + sub;
-  const uint4* vbase = reinterpret_cast<const uint4*>(vc + head_base) + sub;
-
-  // The trip count depends only on the warp (tb is warp-uniform), so every
-  // lane reaches the shuffles below; out-of-range positions are masked.
-  for (int tb = t_begin + warp * PPW; tb < t_end; tb += SLOTS * U) {
-    const int t0 = tb + pidx;
-    uint4 kr[U], vr[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = t0 + u * SLOTS;
-      if (t < t_end) {
-        kr[u] = __ldg(kbase + (size_t)t * LPP);
-        vr[u] = __ldg(vbase + (size_t)t * LPP);
-      } else {
-        kr[u] = make_uint4(0, 0, 0, 0);
-        vr[u] = make_uint4(0, 0, 0, 0);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = t0 + u * SLOTS;
-      float kf[8], vf[8];
-      const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
-      const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __half22float2(kh[i]);
-        const float2 c = __half22float2(vh[i]);
-        kf[2 * i] = a.x; kf[2 * i + 1] = a.y;
-        vf[2 * i] = c.x; vf[2 * i + 1] = c.y;
-      }
-#pragma unroll
-      for (int g = 0; g < GROUP; ++g) {
-        float s = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s += qf[g][i] * kf[i];
-#pragma unroll
-        for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (t < t_end) {
-          const float mn = fmaxf(m[g], s);
-          const float corr = exp2f(m[g] - mn);
-          const float p = exp2f(s - mn);
-          l[g] = l[g] * corr + p;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[g][i] = acc[g][i] * corr + p * vf[i];
-          m[g] = mn;
-        }
-      }
-    }
-  }
-
-  // combine the SLOTS streams of this CTA through shared memory
-  __shared__ float s_m[GROUP][SLOTS], s_l[GROUP][SLOTS];
-  __shared__ float s_acc[GROUP][SLOTS][HD];
-#pragma unroll
-  for (int g = 0; g < GROUP; ++g) {
-    if (sub == 0) { s_m[g][slot] = m[g]; s_l[g][slot] = l[g]; }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s_acc[g][slot][sub * 8 + i] = acc[g][i];
-  }
-  __syncthreads();
-  for (int o = threadIdx.x; o < GROUP * HD; o += blockDim.x) {
-    const int g = o / HD, d = o % HD;
-    float M = -1e30f;
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s) M = fmaxf(M, s_m[g][s]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      const float w = exp2f(s_m[g][s] - M);
-      L += s_l[g][s] * w;
-      O += s_acc[g][s][d] * w;
-    }
-    const int h = kvh * GROUP + g;
-    if (n_splits == 1) {
-      out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / L);
-    } else {
-      const size_t pi = ((size_t)b * Hq + h) * n_splits + split;
-      part_o[pi * HD + d] = O;
-      if (d == 0) { part_ml[2 * pi] = M; part_ml[2 * pi + 1] = L; }
-    }
-  }
-}
-
-// Grid (Hq, B), HD threads: merge the split partials of one head.
-template <int HD>
-__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                    int n_splits, __nv_bfloat16* __restrict__ out, int Hq) {
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const size_t base = ((size_t)b * Hq + h) * n_splits;
-  float M = -1e30f;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[2 * (base + s)]);
-  float L = 0.f, O = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float w = exp2f(part_ml[2 * (base + s)] - M);
-    L += part_ml[2 * (base + s) + 1] * w;
-    O += part_o[(base + s) * HD + d] * w;
-  }
-  out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / L);
-}
-
 // ================================================================ launchers
 cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int table_f32, int V, int D,
                                  const float* g, float eps, float* x, __nv_bfloat16* xn, int rows,
@@ -457,38 +308,6 @@ cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_to
     e = cudaGetLastError();
   }
   return e;
-}
-
-int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms) {
-  const int pairs = B * Hkv;
-  int s = (4 * num_sms + pairs - 1) / pairs;
-  const int max_s = (Tmax + 63) / 64;
-  if (s > max_s) s = max_s;
-  if (s < 1) s = 1;
-  return s;
-}
-
-cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
-                               int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
-                               float* part_o, float* part_ml, __nv_bfloat16* out, cudaStream_t st) {
-  const float qscale = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  const dim3 grid(n_splits, Hkv, B);
-  const int group = Hq / Hkv;
-#define NE_ATT(HD_, G_)                                                                          \
-  decode_attn_kernel<HD_, G_><<<grid, 128, 0, st>>>(q, kc, vc, Tmax, d_pos, n_splits, qscale, \
-                                                    part_o, part_ml, out, Hq)
-  if (hd == 128 && group == 2) NE_ATT(128, 2);
-  else if (hd == 128 && group == 1) NE_ATT(128, 1);
-  else if (hd == 64 && group == 1) NE_ATT(64, 1);
-  else if (hd == 64 && group == 2) NE_ATT(64, 2);
-  else return cudaErrorInvalidValue;
-#undef NE_ATT
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess || n_splits == 1) return e;
-  const dim3 g2(Hq, B);
-  if (hd == 128) attn_combine_kernel<128><<<g2, 128, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
-  else attn_combine_kernel<64><<<g2, 64, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
-  return cudaGetLastError();
 }
 
 }  // namespace ne

@@ -247,7 +247,8 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
                               ctx->d_status, ctx->st));
     prof_mark(ctx, 1);
     NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
-                                 ctx->attn_splits, ctx->attn_po, ctx->attn_ml, ctx->attn, ctx->st));
+                                 ctx->attn_splits, ctx->attn_po, ctx->attn_ml, ctx->attn,
+                                 ctx->d_status, ctx->st));
     if (ctx->attn_splits > 1) ctx->launches++;  // combine kernel
     prof_mark(ctx, 2);
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->part, 0, &sp)) != NE_OK)

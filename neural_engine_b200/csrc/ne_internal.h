@@ -61,7 +61,8 @@ cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_to
 int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms);
 cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
                                int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
-                               float* part_o, float* part_ml, __nv_bfloat16* out, cudaStream_t st);
+                               float* part_o, float* part_ml, __nv_bfloat16* out, int* status,
+                               cudaStream_t st);
 
 // ------------------------------------------------------------------ prefill attention
 // q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16
