@@ -4,26 +4,27 @@
 // every q-head, scores = q . K[t] / sqrt(hd) over the cached positions
 // t <= pos, softmax, weighted sum of V[t]; q-head h reads kv-head h / group.
 // The fp16 KV cache is [sequence][kv_head][position][head_dim], so the K (and
-// V) rows one (sequence, kv-head) needs are one contiguous stream.
+// V) rows one (sequence, kv-head) pair needs are one contiguous stream.
 //
 // Organisation (the kernel is HBM-bound: one pass over the cache):
-//   * A work item is (sequence, kv-head, split): a contiguous position range
-//     serving the group's q-heads together (both Qwen3 q-heads of a kv-head
-//     share every K/V byte read).
-//   * Each warp owns a private 3-stage shared-memory ring and streams its
-//     items' K and V rows into it with 1-D TMA bulk copies
-//     (cp.async.bulk ... mbarrier::complete_tx), issued by lane 0 ahead of the
-//     consumer, so the bytes in flight do not depend on registers.
+//   * Even partition.  The P = B * Hkv pairs, each with T = pos + 1 cached
+//     positions, are laid end to end (P * T positions) and cut into W equal
+//     ranges, one per warp (W = warps of the persistent grid), rounded to
+//     whole chunks.  A range covers the tail of one pair, whole pairs and the
+//     head of another; each piece is a segment with its own online softmax,
+//     and every warp streams the same number of bytes.
+//   * Each warp owns a private shared-memory ring and streams K and V rows
+//     into it with 1-D TMA bulk copies (cp.async.bulk ...
+//     mbarrier::complete_tx) issued by lane 0 ahead of the consumer, so the
+//     bytes in flight do not depend on registers.
 //   * Chunk = 32/group positions.  Lane l owns head dims [l*hd/32, +hd/32);
 //     each lane forms 32 partial dot products (positions x heads) and a
 //     31-shuffle butterfly reduce-scatter leaves lane l with the full score of
 //     (position l/group, head l%group).  Online softmax per head in the log2
 //     domain (q is pre-scaled by log2(e)/sqrt(hd)); the chunk's weights go
-//     through shared memory to the P.V accumulation, where each lane again
-//     owns its head dims.
-//   * Persistent grid (one CTA of 8 warps per SM); warp w takes items
-//     w, w + W, ...; split partials (m, l, unnormalised O) are merged by
-//     attn_combine_kernel.
+//     through shared memory to the P.V accumulation.
+//   * Every segment writes (m, l, unnormalised O) per q-head; the combine
+//     kernel merges the segments of each pair (log-sum-exp rescaling).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -64,40 +65,27 @@ struct DaCfg {
   static constexpr int SMEM = WARPS * WARP_BYTES + WARPS * 32 * 4 + WARPS * STAGES * 8 + 16;
 };
 
-struct ItemGeo {
-  int b, kvh, split, t0, n;
-};
-
-__device__ __forceinline__ ItemGeo item_geo(int item, int n_splits, int Hkv, int T, int chunk_len) {
-  ItemGeo g;
-  const int pair = item / n_splits;
-  g.split = item % n_splits;
-  g.b = pair / Hkv;
-  g.kvh = pair % Hkv;
-  g.t0 = g.split * chunk_len;
-  const int t1 = min(T, g.t0 + chunk_len);
-  g.n = t1 > g.t0 ? t1 - g.t0 : 0;
-  return g;
+// Range length per warp: ceil(P*T / W) rounded up to whole chunks.
+__device__ __forceinline__ long long range_len(long long total, int W, int chp) {
+  long long L = (total + W - 1) / W;
+  return (L + chp - 1) / chp * chp;
 }
 
 template <int HD, int GROUP>
 __global__ void __launch_bounds__(DaCfg<HD, GROUP>::WARPS * 32, 1)
-decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                        const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos,
-                        int B, int Hq, int Hkv, int n_splits, float qscale,
-                        float* __restrict__ part_o, float* __restrict__ part_ml,
-                        __nv_bfloat16* __restrict__ out, int* status) {
+decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                   const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos, int P,
+                   int Hq, int Hkv, float qscale, float* __restrict__ part_o,
+                   float* __restrict__ part_ml, int* status) {
   using C = DaCfg<HD, GROUP>;
-  constexpr int CHP = C::CHP, DPL = C::DPL, STAGES = C::STAGES, DA_WARPS = C::WARPS;
+  constexpr int CHP = C::CHP, DPL = C::DPL, STAGES = C::STAGES, NW = C::WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = smem + warp * C::WARP_BYTES;
-  float* sE = reinterpret_cast<float*>(smem + DA_WARPS * C::WARP_BYTES) + warp * 32;
-  const uint32_t bars =
-      smem_u32(smem + DA_WARPS * C::WARP_BYTES + DA_WARPS * 32 * 4) + warp * STAGES * 8;
-  volatile int* abort_flag =
-      reinterpret_cast<volatile int*>(smem + DA_WARPS * C::WARP_BYTES + DA_WARPS * 32 * 4 +
-                                      DA_WARPS * STAGES * 8);
+  float* sE = reinterpret_cast<float*>(smem + NW * C::WARP_BYTES) + warp * 32;
+  const uint32_t bars = smem_u32(smem + NW * C::WARP_BYTES + NW * 32 * 4) + warp * STAGES * 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(
+      smem + NW * C::WARP_BYTES + NW * 32 * 4 + NW * STAGES * 8);
   if (threadIdx.x == 0) *abort_flag = 0;
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8 * s, 1);
@@ -106,29 +94,25 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
   __syncthreads();
 
   const int T = *d_pos + 1;
-  int chunk_len = (T + n_splits - 1) / n_splits;
-  chunk_len = (chunk_len + CHP - 1) / CHP * CHP;
-  const int items = B * Hkv * n_splits;
-  const int W = gridDim.x * DA_WARPS;
-  const int wg = blockIdx.x * DA_WARPS + warp;
+  const int W = gridDim.x * NW;
+  const int w = blockIdx.x * NW + warp;
+  const long long total = (long long)P * T;
+  const long long L = range_len(total, W, CHP);
+  const long long w_begin = (long long)w * L;
+  const long long w_end = w_begin + L < total ? w_begin + L : total;
+  const int seg_per_warp = (int)((L + T - 1) / T) + 1;
+  const int first_pair = (int)(w_begin / T);
 
-  // ---- producer cursor (lane 0 issues; all lanes track it identically)
-  int p_item = wg, p_chunk = 0;
-  auto skip_empty = [&]() {
-    while (p_item < items) {
-      const ItemGeo g = item_geo(p_item, n_splits, Hkv, T, chunk_len);
-      if (p_chunk * CHP < g.n) return;
-      p_item += W;
-      p_chunk = 0;
-    }
-  };
+  // ---- producer (lane 0 issues; all lanes track the cursor identically)
+  long long p_pos = w_begin;
   auto issue = [&](int slot) {
-    // issue the chunk under the producer cursor into ring slot `slot`, advance
-    const ItemGeo g = item_geo(p_item, n_splits, Hkv, T, chunk_len);
-    const int tt = g.t0 + p_chunk * CHP;
-    const int rows = min(CHP, g.n - p_chunk * CHP);
+    const int pair = (int)(p_pos / T);
+    const int tin = (int)(p_pos % T);
+    long long rows = CHP;
+    if (w_end - p_pos < rows) rows = w_end - p_pos;
+    if (T - tin < rows) rows = T - tin;
     if (lane == 0) {
-      const size_t off = (((size_t)g.b * Hkv + g.kvh) * Tmax + tt) * HD;
+      const size_t off = ((size_t)pair * Tmax + tin) * HD;   // pair = b*Hkv + kvh
       const uint32_t bytes = (uint32_t)rows * C::ROW;
       const uint32_t dst = smem_u32(ring + slot * 2 * C::CHUNK);
       fence_proxy_async_smem();
@@ -136,24 +120,25 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
       bulk_g2s(dst, kc + off, bytes, bars + 8 * slot);
       bulk_g2s(dst + C::CHUNK, vc + off, bytes, bars + 8 * slot);
     }
-    ++p_chunk;
-    skip_empty();
+    p_pos += rows;
   };
-  skip_empty();
   int issued = 0;
-  for (int s = 0; s < STAGES && p_item < items; ++s) {
+  for (int s = 0; s < STAGES && p_pos < w_end; ++s) {
     issue(s);
     ++issued;
   }
 
   int gc = 0;  // chunks consumed by this warp
   bool ok = true;
-  for (int it = wg; it < items && ok; it += W) {
-    const ItemGeo g = item_geo(it, n_splits, Hkv, T, chunk_len);
+  long long c_pos = w_begin;
+  while (c_pos < w_end && ok) {
+    const int pair = (int)(c_pos / T);
+    const long long seg_end = ((long long)(pair + 1) * T < w_end) ? (long long)(pair + 1) * T : w_end;
+    const int b = pair / Hkv, kvh = pair % Hkv;
     float qf[GROUP][DPL];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
-      const float* qp = q + ((size_t)g.b * Hq + g.kvh * GROUP + h) * HD + lane * DPL;
+      const float* qp = q + ((size_t)b * Hq + kvh * GROUP + h) * HD + lane * DPL;
 #pragma unroll
       for (int d = 0; d < DPL; ++d) qf[h][d] = qp[d] * qscale;
     }
@@ -165,17 +150,17 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
 #pragma unroll
       for (int d = 0; d < DPL; ++d) acc[h][d] = 0.f;
     }
-    const int nch = (g.n + CHP - 1) / CHP;
-    for (int c = 0; c < nch; ++c) {
+    while (c_pos < seg_end) {
       const int slot = gc % STAGES;
       // every lane waits (each needs the barrier's acquire); the outcome is
       // made warp-uniform so no lane reaches a shuffle the others skip
-      const bool landed = mbar_wait(bars + 8 * slot, (uint32_t)((gc / STAGES) & 1), status, abort_flag);
+      const bool landed =
+          mbar_wait(bars + 8 * slot, (uint32_t)((gc / STAGES) & 1), status, abort_flag);
       if (!__all_sync(0xffffffffu, landed)) {
         ok = false;
         break;
       }
-      const int nvalid = min(CHP, g.n - c * CHP);
+      const int nvalid = (int)((seg_end - c_pos) < CHP ? (seg_end - c_pos) : CHP);
       const uint8_t* sK = ring + slot * 2 * C::CHUNK + lane * DPL * 2;
       const uint8_t* sV = sK + C::CHUNK;
       // partial dot products over this lane's dims: index p*GROUP + h
@@ -213,7 +198,7 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
         }
       }
       const int myh = lane % GROUP;
-      const bool valid = (lane / GROUP) < nvalid;
+      const bool valid = (lane / GROUP) < nvalid;   // rows past nvalid are stale smem
       const float s = valid ? v[0] : -1e30f;
       float mc = s;
 #pragma unroll
@@ -256,39 +241,30 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
         }
 #pragma unroll
         for (int h = 0; h < GROUP; ++h) {
-          const float w = sE[p * GROUP + h];
+          const float wgt = sE[p * GROUP + h];
 #pragma unroll
-          for (int d = 0; d < DPL; ++d) acc[h][d] += w * vf[d];
+          for (int d = 0; d < DPL; ++d) acc[h][d] += wgt * vf[d];
         }
       }
       __syncwarp();
+      c_pos += nvalid;
       ++gc;
-      if (p_item < items) {
+      if (p_pos < w_end) {
         issue(slot);
         ++issued;
       }
     }
     if (!ok) break;
-    // ---- item result
+    // ---- segment partial: slot (w, pair - first_pair)
+    const size_t si = (size_t)w * seg_per_warp + (pair - first_pair);
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
-      const int qh = g.kvh * GROUP + h;
-      if (n_splits == 1) {
-        const float inv = 1.f / l[h];
-        __nv_bfloat16* dst = out + ((size_t)g.b * Hq + qh) * HD + lane * DPL;
+      float* dst = part_o + (si * GROUP + h) * HD + lane * DPL;
 #pragma unroll
-        for (int d = 0; d < DPL; d += 2)
-          *reinterpret_cast<__nv_bfloat162*>(dst + d) =
-              __floats2bfloat162_rn(acc[h][d] * inv, acc[h][d + 1] * inv);
-      } else {
-        const size_t pi = ((size_t)g.b * Hq + qh) * n_splits + g.split;
-        float* dst = part_o + pi * HD + lane * DPL;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) dst[d] = acc[h][d];
-        if (lane == 0) {
-          part_ml[2 * pi] = m[h];
-          part_ml[2 * pi + 1] = l[h];
-        }
+      for (int d = 0; d < DPL; ++d) dst[d] = acc[h][d];
+      if (lane == 0) {
+        part_ml[(si * GROUP + h) * 2] = m[h];
+        part_ml[(si * GROUP + h) * 2 + 1] = l[h];
       }
     }
   }
@@ -302,79 +278,82 @@ decode_attn_bulk_kernel(const float* __restrict__ q, const __half* __restrict__ 
   }
 }
 
-// Grid (Hq, B), HD threads: merge the split partials of one head.
-template <int HD>
+// Grid (Hq, B), HD threads: merge the segments of one (sequence, q-head).
+template <int HD, int GROUP>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o,
-                                    const float* __restrict__ part_ml, int n_splits,
-                                    __nv_bfloat16* __restrict__ out, int Hq) {
+                                    const float* __restrict__ part_ml, const int* __restrict__ d_pos,
+                                    int W, int Hq, int Hkv, __nv_bfloat16* __restrict__ out) {
+  constexpr int CHP = 32 / GROUP;
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const size_t base = ((size_t)b * Hq + h) * n_splits;
+  const int pair = b * Hkv + h / GROUP, g = h % GROUP;
+  const int T = *d_pos + 1;
+  const long long total = (long long)(gridDim.y * Hkv) * T;
+  const long long L = range_len(total, W, CHP);
+  const int seg_per_warp = (int)((L + T - 1) / T) + 1;
+  const int w0 = (int)(((long long)pair * T) / L);
+  const int w1 = (int)(((long long)(pair + 1) * T - 1) / L);
   float M = -1e30f;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[2 * (base + s)]);
-  float L = 0.f, O = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float w = exp2f(part_ml[2 * (base + s)] - M);
-    L += part_ml[2 * (base + s) + 1] * w;
-    O += part_o[(base + s) * HD + d] * w;
+  for (int w = w0; w <= w1; ++w) {
+    const size_t si = (size_t)w * seg_per_warp + (pair - (int)(((long long)w * L) / T));
+    M = fmaxf(M, part_ml[(si * GROUP + g) * 2]);
   }
-  out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / L);
+  float Lsum = 0.f, O = 0.f;
+  for (int w = w0; w <= w1; ++w) {
+    const size_t si = (size_t)w * seg_per_warp + (pair - (int)(((long long)w * L) / T));
+    const float wt = exp2f(part_ml[(si * GROUP + g) * 2] - M);
+    Lsum += part_ml[(si * GROUP + g) * 2 + 1] * wt;
+    O += part_o[(si * GROUP + g) * HD + d] * wt;
+  }
+  out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / Lsum);
 }
 
 template <int HD, int G>
-cudaError_t launch_bulk(const float* q, const __half* kc, const __half* vc, int B, int Hq, int Hkv,
-                        int Tmax, const int* d_pos, int n_splits, float qscale, float* part_o,
-                        float* part_ml, __nv_bfloat16* out, int* status, cudaStream_t st) {
+cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, int Hq, int Hkv,
+                     int Tmax, const int* d_pos, float qscale, float* part_o, float* part_ml,
+                     __nv_bfloat16* out, int* status, cudaStream_t st) {
   using C = DaCfg<HD, G>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_bulk_kernel<HD, G>,
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD, G>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int items = B * Hkv * n_splits;
-  int grid = (items + C::WARPS - 1) / C::WARPS;
-  const int sms = device_num_sms();
-  if (grid > sms) grid = sms;
-  decode_attn_bulk_kernel<HD, G><<<grid, C::WARPS * 32, C::SMEM, st>>>(
-      q, kc, vc, Tmax, d_pos, B, Hq, Hkv, n_splits, qscale, part_o, part_ml, out, status);
+  const int grid = device_num_sms();
+  const int P = B * Hkv;
+  decode_attn_kernel<HD, G><<<grid, C::WARPS * 32, C::SMEM, st>>>(
+      q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale, part_o, part_ml, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_combine_kernel<HD, G><<<dim3(Hq, B), HD, 0, st>>>(part_o, part_ml, d_pos,
+                                                         grid * C::WARPS, Hq, Hkv, out);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms) {
-  const int pairs = B * Hkv;
-  const int target = 8 * DA_MAX_WARPS * num_sms;   // about 8 items per warp
-  int s = (target + pairs - 1) / pairs;
-  const int max_s = (Tmax + 63) / 64;
-  if (s > max_s) s = max_s;
-  if (s < 1) s = 1;
-  return s;
+// Segment slots the partial buffers must hold.  Warp w writes at most
+// ceil(L/T) + 1 segments with L <= P*T/W + CHP, so all warps together write
+// at most P + 3W of them (W = SMs x 8 warps bounds every configuration).
+size_t decode_attn_partial_slots(int B, int Hkv, int num_sms) {
+  const size_t W = (size_t)num_sms * DA_MAX_WARPS;
+  return (size_t)B * Hkv + 3 * W + 64;
 }
 
 cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
-                               int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
-                               float* part_o, float* part_ml, __nv_bfloat16* out, int* status,
-                               cudaStream_t st) {
+                               int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
+                               float* part_ml, __nv_bfloat16* out, int* status, cudaStream_t st) {
   const float qscale = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   const int group = Hq / Hkv;
-  cudaError_t e;
   if (hd == 128 && group == 2)
-    e = launch_bulk<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, n_splits, qscale, part_o, part_ml, out, status, st);
-  else if (hd == 128 && group == 1)
-    e = launch_bulk<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, n_splits, qscale, part_o, part_ml, out, status, st);
-  else if (hd == 64 && group == 1)
-    e = launch_bulk<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, n_splits, qscale, part_o, part_ml, out, status, st);
-  else if (hd == 64 && group == 2)
-    e = launch_bulk<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, n_splits, qscale, part_o, part_ml, out, status, st);
-  else
-    return cudaErrorInvalidValue;
-  if (e != cudaSuccess || n_splits == 1) return e;
-  const dim3 g2(Hq, B);
-  if (hd == 128) attn_combine_kernel<128><<<g2, 128, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
-  else attn_combine_kernel<64><<<g2, 64, 0, st>>>(part_o, part_ml, n_splits, out, Hq);
-  return cudaGetLastError();
+    return launch_t<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+  if (hd == 128 && group == 1)
+    return launch_t<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+  if (hd == 64 && group == 1)
+    return launch_t<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+  if (hd == 64 && group == 2)
+    return launch_t<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace ne

@@ -87,9 +87,8 @@ struct ne_ctx {
   size_t part_elems = 0;
   float* q = nullptr;            // [maxB, Hq, hd]
   __nv_bfloat16* attn = nullptr; // [maxB, q_dim]
-  float* attn_po = nullptr;      // [maxB, Hq, splits, hd]
-  float* attn_ml = nullptr;      // [maxB, Hq, splits, 2]
-  int attn_splits = 1;
+  float* attn_po = nullptr;      // [segment slots][group][hd]  (decode attention partials)
+  float* attn_ml = nullptr;      // [segment slots][group][2]
   __nv_bfloat16* gate = nullptr; // [maxB, F]
   float* logits = nullptr;       // [maxB, V]
   int32_t* tok = nullptr;        // [maxB]
@@ -247,9 +246,9 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
                               ctx->d_status, ctx->st));
     prof_mark(ctx, 1);
     NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
-                                 ctx->attn_splits, ctx->attn_po, ctx->attn_ml, ctx->attn,
+                                 ctx->attn_po, ctx->attn_ml, ctx->attn,
                                  ctx->d_status, ctx->st));
-    if (ctx->attn_splits > 1) ctx->launches++;  // combine kernel
+    ctx->launches++;  // segment combine kernel
     prof_mark(ctx, 2);
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->part, 0, &sp)) != NE_OK)
       return s;
@@ -607,15 +606,16 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
     }
   }
   ctx->part_elems = part;
-  ctx->attn_splits = decode_attn_splits(max_batch, m.kv_heads, max_seq, ctx->num_sms);
-  // the split count is fixed per context so captured graphs stay valid for
-  // every batch size up to max_batch
+  const size_t attn_slots = decode_attn_partial_slots(max_batch, m.kv_heads, ctx->num_sms);
+  const size_t group = (size_t)(Hq / m.kv_heads);
+  // the attention partial buffers are sized for max_batch, so captured
+  // graphs stay valid for every batch size up to it
   const size_t B = max_batch;
   if ((s = dalloc(ctx, &ctx->x, B * D)) || (s = dalloc(ctx, &ctx->xn, B * D)) ||
       (s = dalloc(ctx, &ctx->part, part)) || (s = dalloc(ctx, &ctx->q, B * Hq * hd)) ||
       (s = dalloc(ctx, &ctx->attn, B * q_dim)) ||
-      (s = dalloc(ctx, &ctx->attn_po, B * Hq * ctx->attn_splits * hd)) ||
-      (s = dalloc(ctx, &ctx->attn_ml, B * Hq * ctx->attn_splits * 2)) ||
+      (s = dalloc(ctx, &ctx->attn_po, attn_slots * group * hd)) ||
+      (s = dalloc(ctx, &ctx->attn_ml, attn_slots * group * 2)) ||
       (s = dalloc(ctx, &ctx->gate, B * F)) || (s = dalloc(ctx, &ctx->logits, B * m.vocab)) ||
       (s = dalloc(ctx, &ctx->tok, B)) || (s = dalloc(ctx, &ctx->state, 2)) ||
       (s = dalloc(ctx, &ctx->out_tokens, (size_t)max_seq * B)))

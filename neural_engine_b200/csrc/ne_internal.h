@@ -58,11 +58,12 @@ cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stri
                                 __nv_bfloat16* gate, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
                           int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st);
-int decode_attn_splits(int B, int Hkv, int Tmax, int num_sms);
+// Segment slots (each GROUP x (hd + 2) floats) the decode-attention partial
+// buffers must hold for batch B.
+size_t decode_attn_partial_slots(int B, int Hkv, int num_sms);
 cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
-                               int Hkv, int hd, int Tmax, const int* d_pos, int n_splits,
-                               float* part_o, float* part_ml, __nv_bfloat16* out, int* status,
-                               cudaStream_t st);
+                               int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
+                               float* part_ml, __nv_bfloat16* out, int* status, cudaStream_t st);
 
 // ------------------------------------------------------------------ prefill attention
 // q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16
