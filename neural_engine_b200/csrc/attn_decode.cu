@@ -32,6 +32,7 @@
 
 #include "ne_device.cuh"
 #include "ne_internal.h"
+#include "ne_launch.cuh"
 
 namespace ne {
 namespace {
@@ -91,7 +92,9 @@ decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
     for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8 * s, 1);
     fence_barrier_init();
   }
+  pdl_trigger();
   __syncthreads();
+  pdl_wait();   // q and the new K/V row come from the preceding kernel
 
   const int T = *d_pos + 1;
   const int W = gridDim.x * NW;
@@ -284,6 +287,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o,
                                     const float* __restrict__ part_ml, const int* __restrict__ d_pos,
                                     int W, int Hq, int Hkv, __nv_bfloat16* __restrict__ out) {
   constexpr int CHP = 32 / GROUP;
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int pair = b * Hkv + h / GROUP, g = h % GROUP;
   const int T = *d_pos + 1;
@@ -321,13 +326,13 @@ cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, 
   }
   const int grid = device_num_sms();
   const int P = B * Hkv;
-  decode_attn_kernel<HD, G><<<grid, C::WARPS * 32, C::SMEM, st>>>(
-      q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale, part_o, part_ml, status);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(decode_attn_kernel<HD, G>, dim3(grid), dim3(C::WARPS * 32),
+                           (size_t)C::SMEM, st, q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale,
+                           part_o, part_ml, status);
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<HD, G><<<dim3(Hq, B), HD, 0, st>>>(part_o, part_ml, d_pos,
-                                                         grid * C::WARPS, Hq, Hkv, out);
-  return cudaGetLastError();
+  return launch_k(attn_combine_kernel<HD, G>, dim3(Hq, B), dim3(HD), 0, st,
+                  (const float*)part_o, (const float*)part_ml, d_pos, grid * C::WARPS, Hq, Hkv,
+                  out);
 }
 
 }  // namespace

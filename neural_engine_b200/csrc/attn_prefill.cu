@@ -15,7 +15,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "ne_device.cuh"
 #include "ne_internal.h"
+#include "ne_launch.cuh"
 
 namespace ne {
 namespace {
@@ -78,6 +80,8 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
   __half* sK = sQ + FA_BQ * LD;           // [2][FA_BK][LD]
   __half* sV = sK + 2 * FA_BK * LD;       // [2][FA_BK][LD]
 
+  pdl_trigger();
+  pdl_wait();
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (Hq / Hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -255,11 +259,13 @@ cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half*
                            (int)smem);
       done = true;
     }
-    prefill_attn_kernel<128><<<grid, 128, smem, st>>>(q, kc, vc, S, pos0, Hq, Hkv, Tmax, qs, out);
+    return launch_k(prefill_attn_kernel<128>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
+                    Hkv, Tmax, qs, out);
   } else if (hd == 64) {
     constexpr int LD = 64 + 8;
     const size_t smem = (size_t)(FA_BQ + 4 * FA_BK) * LD * sizeof(__half);
-    prefill_attn_kernel<64><<<grid, 128, smem, st>>>(q, kc, vc, S, pos0, Hq, Hkv, Tmax, qs, out);
+    return launch_k(prefill_attn_kernel<64>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
+                    Hkv, Tmax, qs, out);
   } else {
     return cudaErrorInvalidValue;
   }

@@ -5,6 +5,7 @@
 
 #include "gemm_tc.cuh"
 #include "ne_internal.h"
+#include "ne_launch.cuh"
 
 namespace ne {
 
@@ -57,8 +58,8 @@ cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmSha
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  gemm_tc_kernel<BN, Epi, FMT><<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, sh, p);
-  return cudaGetLastError();
+  return launch_k(gemm_tc_kernel<BN, Epi, FMT>, dim3(grid), dim3(GEMM_THREADS),
+                  (size_t)C::SMEM_BYTES, st, ta, tb, sh, p);
 }
 
 template <int BN, int FMT>
@@ -123,11 +124,16 @@ int gemm_pick_splits(const GemmCall& c, int num_sms) {
   const int bn = pick_bn(c);
   const int tiles = ((c.M + GEMM_BM - 1) / GEMM_BM) * ((c.N + bn - 1) / bn);
   const int kb = c.K / GEMM_BK;
+  // Split until the work units fill the SMs, but for wide N (large decode
+  // batches) stop at half the SMs: each extra split adds a partial slab of
+  // N x M fp32 that the consumer reads back (fitted to measured decode
+  // shapes: N <= 128 favours ~148 units, N = 256 ~64-96).
+  const int cap = c.N <= 128 ? num_sms : num_sms / 2;
   int best = 1;
   for (int d = 1; d <= kb; ++d) {
     if (kb % d) continue;
-    if (kb / d < 2) break;
-    if (tiles * d > num_sms) break;
+    if (kb / d < 1) break;
+    if (tiles * d > cap) break;
     best = d;
   }
   return best;
@@ -158,6 +164,7 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   sh.splits = splits;
   sh.kb_per_split = kb / splits;
   sh.status = status;
+  sh.prefetch_a = c.prefetch_a;
   const long long units = (long long)sh.m_tiles * sh.n_tiles * splits;
   const int cap = c.max_ctas > 0 ? c.max_ctas : num_sms;
   const int grid = (int)(units < cap ? units : cap);

@@ -40,6 +40,8 @@ struct GemmShape {
   int splits;           // split-K factor
   int kb_per_split;     // k-blocks (of 64) per split
   int* status;          // device status word (timeouts)
+  int prefetch_a;       // A does not depend on the preceding kernel: its first
+                        // tiles may be loaded before the PDL dependency wait
 };
 
 template <int BN>
@@ -242,6 +244,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -252,9 +255,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       const uint64_t pol_a = policy_evict_first();
       const uint64_t pol_b = policy_evict_last();
+      // Prologue overlap: the first stages' A tiles of this CTA's first unit
+      // (weights that no preceding kernel writes) are requested before the
+      // programmatic-dependency wait; their B tiles follow after it.
+      int pre = 0;
+      if (sh.prefetch_a && (int)blockIdx.x < units) {
+        const int u = blockIdx.x;
+        const int mt = u % sh.m_tiles;
+        const int kb0 = (u / sh.m_tiles / sh.n_tiles) * sh.kb_per_split;
+        pre = sh.kb_per_split < STAGES ? sh.kb_per_split : STAGES;
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(full_bar + 8 * kb, C::STAGE_BYTES);
+          tma_load_2d(tiles + kb * C::STAGE_BYTES, &tmA, full_bar + 8 * kb, (kb0 + kb) * GEMM_BK,
+                      mt * GEMM_BM, pol_a);
+        }
+      }
+      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool first = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int mt = u % sh.m_tiles;
         const int rest = u / sh.m_tiles;
@@ -262,17 +282,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int sp = rest / sh.n_tiles;
         const int kb0 = sp * sh.kb_per_split;
         for (int kb = 0; kb < sh.kb_per_split; ++kb) {
-          if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, sh.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(full_bar + 8 * stage, C::STAGE_BYTES);
           const uint32_t sa = tiles + stage * C::STAGE_BYTES;
-          tma_load_2d(sa, &tmA, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM, pol_a);
+          if (!(first && kb < pre)) {
+            if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, sh.status, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full_bar + 8 * stage, C::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM, pol_a);
+          }
           tma_load_2d(sa + C::A_BYTES, &tmB, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN,
                       pol_b);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
+        first = false;
       }
       // Drain: wait (bounded) until the most recent load issued into every
       // stage has landed, so no TMA write is in flight when the CTA exits.
@@ -326,6 +349,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------ epilogue (warps 2..5)
+    pdl_wait();   // outputs may still be read by the preceding kernel until it completes
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;

@@ -25,6 +25,7 @@
 
 #include "ne_device.cuh"
 #include "ne_internal.h"
+#include "ne_launch.cuh"
 
 namespace ne {
 
@@ -64,6 +65,8 @@ __global__ void embed_rmsnorm_kernel(const int32_t* __restrict__ tok, const void
                                      int table_f32, int V, int D, const float* __restrict__ g,
                                      float eps, float* __restrict__ x, __nv_bfloat16* __restrict__ xn,
                                      int* status) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];
   float* xs = sm;
   float* red = sm + D;
@@ -90,6 +93,8 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
                                      int nsplit, long long split_stride, float alpha, int D,
                                      const float* __restrict__ g, float eps,
                                      __nv_bfloat16* __restrict__ xn) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];
   float* xs = sm;
   float* red = sm + D;
@@ -121,6 +126,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
                                 const float2* __restrict__ rope_cs, QT* __restrict__ q_out,
                                 __half* __restrict__ kc, __half* __restrict__ vc, int Tmax,
                                 int* status) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PER = HD / 32;  // elements per lane (2 or 4), consecutive
   const int warps_per_block = blockDim.x >> 5;
   const int gw = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
@@ -185,6 +192,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
 // P: [nsplit][rows][2F] fp32 with W1/W3 interleaved in 16-row blocks.
 __global__ void swiglu_split_kernel(const float* __restrict__ P, int nsplit, long long split_stride,
                                     int rows, int F, __nv_bfloat16* __restrict__ gate) {
+  pdl_trigger();
+  pdl_wait();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)rows * F) return;
   const int r = (int)(idx / F), j = (int)(idx % F);
@@ -204,6 +213,8 @@ __global__ void swiglu_split_kernel(const float* __restrict__ P, int nsplit, lon
 // out_tokens[(d_state[1]) * rows + r] (d_state = [pos, step]).
 __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int32_t* next_tok,
                                    int32_t* out_tokens, const int* d_state) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int r = blockIdx.x;
@@ -243,6 +254,8 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int3
 
 // Advance the on-device decode state [pos, step] by one token.
 __global__ void advance_state_kernel(int* d_state) {
+  pdl_trigger();
+  pdl_wait();
   d_state[0] += 1;
   d_state[1] += 1;
 }
@@ -253,9 +266,8 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
                                  int* status, cudaStream_t st) {
   const int threads = D >= 1024 ? 256 : 128;
   const size_t smem = (size_t)(D + 32) * sizeof(float);
-  embed_rmsnorm_kernel<<<rows, threads, smem, st>>>(tok, table, table_f32, V, D, g, eps, x, xn,
-                                                    status);
-  return cudaGetLastError();
+  return launch_k(embed_rmsnorm_kernel, dim3(rows), dim3(threads), smem, st, tok, table,
+                  table_f32, V, D, g, eps, x, xn, status);
 }
 
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
@@ -263,9 +275,8 @@ cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long
                                  int rows, cudaStream_t st) {
   const int threads = D >= 1024 ? 256 : 128;
   const size_t smem = (size_t)(D + 32) * sizeof(float);
-  resid_rmsnorm_kernel<<<rows, threads, smem, st>>>(x, P, nsplit, split_stride, alpha, D, g, eps,
-                                                    xn);
-  return cudaGetLastError();
+  return launch_k(resid_rmsnorm_kernel, dim3(rows), dim3(threads), smem, st, x, P, nsplit,
+                  split_stride, alpha, D, g, eps, xn);
 }
 
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
@@ -276,10 +287,11 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
   const int warps = rows * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = (warps + 7) / 8;
+  cudaError_t e;
 #define NE_QKV(HD_, QT_)                                                                      \
-  qkv_post_kernel<HD_, QT_><<<blocks, threads, 0, st>>>(                                       \
-      qkv, nsplit, split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs, \
-      reinterpret_cast<QT_*>(q_out), kc, vc, Tmax, status)
+  e = launch_k(qkv_post_kernel<HD_, QT_>, dim3(blocks), dim3(threads), 0, st, qkv, nsplit,   \
+               split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs,     \
+               reinterpret_cast<QT_*>(q_out), kc, vc, Tmax, status)
   if (hd == 128) {
     if (q_fp16) NE_QKV(128, __half); else NE_QKV(128, float);
   } else if (hd == 64) {
@@ -288,25 +300,21 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
     return cudaErrorInvalidValue;
   }
 #undef NE_QKV
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
                                 __nv_bfloat16* gate, cudaStream_t st) {
   const long long n = (long long)rows * F;
-  swiglu_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(P, nsplit, split_stride, rows, F,
-                                                                   gate);
-  return cudaGetLastError();
+  return launch_k(swiglu_split_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, P,
+                  nsplit, split_stride, rows, F, gate);
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
                           int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st) {
-  argmax_rows_kernel<<<rows, 1024, 0, st>>>(logits, V, next_tok, out_tokens, d_state);
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && adv_state) {
-    advance_state_kernel<<<1, 1, 0, st>>>(d_state);
-    e = cudaGetLastError();
-  }
+  cudaError_t e = launch_k(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, logits, V, next_tok,
+                           out_tokens, (const int*)d_state);
+  if (e == cudaSuccess && adv_state) e = launch_k(advance_state_kernel, dim3(1), dim3(1), 0, st, d_state);
   return e;
 }
 

@@ -176,6 +176,7 @@ ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
   c.epi = EPI_F32T;
   c.out = out; c.ld = n_out; c.split_stride = (long long)rows * n_out;
   c.splits = splits;
+  c.prefetch_a = 1;   // A = weights: loaded while the producer of `act` finishes
   const int s = gemm_pick_splits(c, ctx->num_sms);
   c.splits = s;
   if ((size_t)s * rows * n_out > ctx->part_elems && out == ctx->part)

@@ -198,3 +198,16 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 }  // namespace ne
+
+namespace ne {
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialisation attribute may start while its predecessor still runs.
+// pdl_trigger() lets the successor be scheduled; pdl_wait() blocks until the
+// predecessor grid has completed and its memory is visible.  Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+}  // namespace ne

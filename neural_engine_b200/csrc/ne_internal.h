@@ -35,6 +35,7 @@ struct GemmCall {
   int bn = 0;                   // N tile (0 = choose)
   int ab_fp16 = 0;              // 1: fp16 operands, 0: bf16
   int max_ctas = 0;             // 0 = number of SMs
+  int prefetch_a = 0;           // A is not written by the preceding kernel (PDL overlap)
 };
 
 // Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).
