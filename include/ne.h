@@ -173,9 +173,76 @@ NE_API void* ne_get_stream(const ne_ctx* ctx);
 #define NE_PROF_GROUPS 10
 NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms);
 
+/* General form.  a_mn / b_mn: the operand is stored MN-major, i.e. A as
+ * [K, M] (lda >= M) and B as [K, N] (ldb >= N) -- the transposed reads of the
+ * reference's cblas_sgemm(CblasTrans, ...) calls (train.m:555-738) without a
+ * transposed copy.  epi 5: fp32 out = in + alpha*acc (aux0 = in, same ld);
+ * epi 6: SwiGLU backward (aux0 = h1, aux1 = h3 [M, aux_ld] bf16; out = dh13
+ * [M, 2*aux_ld] bf16 in the W1/W3 16-row-interleaved order). */
+typedef struct ne_gemm_desc {
+  const void* a; long long lda; int a_mn;
+  const void* b; long long ldb; int b_mn;
+  int M, N, K;
+  int epi;
+  void* out; long long ld;
+  float alpha;
+  const void* aux0; const void* aux1; long long aux_ld;
+  int bn;            /* 0 = automatic */
+  int half_out;      /* epi 2: write fp16 instead of bf16 */
+} ne_gemm_desc;
+NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d);
+
 /* Kernel launches enqueued by the last ne_decode_loop_device step graph
  * (per step), for launch accounting. */
 NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B);
+
+/* ---- training step (train.m:391-917) --------------------------------------
+ * Typical loop (the reference's step loop with accum micro-steps):
+ *   ne_train_alloc(ctx, B, S);                      once, after the weights are set
+ *   for step: ne_train_fwd_bwd(ctx, tokens[B][S+1], &loss);   (accumulates grads)
+ *             every accum steps: ne_adamw_step(ctx, &cfg, ++t, &norm);
+ * Tokens: inputs tokens[:, :S], targets tokens[:, 1:] (train.m:395-401).
+ * Loss = mean cross-entropy over the B*S targets (cpu_ops.h:348-382). */
+typedef struct ne_adam_cfg {
+  float lr;            /* this step's learning rate (see ne_lr_schedule) */
+  float beta1, beta2;  /* 0.9, 0.95 in train.m:174 */
+  float eps;           /* 1e-8, added after the sqrt (cpu_ops.h:295) */
+  float weight_decay;  /* 0.1; applied to matrices and the embedding, not the gains */
+  float grad_clip;     /* global-norm clip (train.m:833-849); <= 0 disables */
+  float grad_scale;    /* multiplies the accumulated gradients first (1/accum) */
+} ne_adam_cfg;
+
+/* Allocate fp32 masters (initialised from the current weights), gradients,
+ * Adam m/v and the saved activations for batches of B sequences of S tokens
+ * (B*S a multiple of 64). */
+NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S);
+/* Load exact fp32 masters for one layer (v4 tensors); layer -1 loads the
+ * embedding from h_wq.  Call ne_train_sync_weights afterwards. */
+NE_API ne_status ne_train_set_masters(ne_ctx* ctx, int layer, const float* h_wq, const float* h_wk,
+                                      const float* h_wv, const float* h_wo, const float* h_w1,
+                                      const float* h_w2, const float* h_w3);
+/* Refresh the bf16 compute copies from the fp32 masters. */
+NE_API ne_status ne_train_sync_weights(ne_ctx* ctx);
+NE_API ne_status ne_train_zero_grads(ne_ctx* ctx);
+/* Forward + backward of one batch; gradients accumulate.  d_loss / h_loss
+ * (optional) receive the batch's mean loss. */
+NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss);
+NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss);
+/* Global L2 norm of the accumulated gradients times grad_scale. */
+NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm);
+/* Unscale, clip, AdamW (bias correction at step t >= 1), refresh bf16 copies,
+ * zero the gradients (train.m:782-904; cpu_ops.h:266-303). */
+NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t, float* h_grad_norm);
+/* Warmup + cosine learning rate of train.m:851-858. */
+NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_steps,
+                            float min_lr_frac);
+/* Copy a layer's gradients (which 0) or fp32 masters (which 1) to host in the
+ * v4 layout; layer -1 gives rms_final in h_rms_att and the embedding in h_wq.
+ * NULL pointers are skipped. */
+NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_wq, float* h_wk,
+                                    float* h_wv, float* h_wo, float* h_w1, float* h_w2,
+                                    float* h_w3, float* h_rms_att, float* h_rms_ffn,
+                                    float* h_q_norm, float* h_k_norm);
 
 /* ---- allocation-free split-K product --------------------------------------
  * No counterpart in the reference: an addition for callers that must not

@@ -1,0 +1,384 @@
+// attn_bwd.cu -- causal GQA attention backward (training step).
+//
+// Gradients of O = softmax(Q K^T / sqrt(hd) + causal mask) V, the reference's
+// sdpaBwd1 / sdpaBwd2 kernels (ane-training/training/training_dynamic/
+// mil_dynamic.h:583-707: recompute P, dV = P^T dO, dP = dO V^T,
+// dS = P (dP - rowsum(P dP)), dQ = dS K / sqrt(hd), dK = dS^T Q / sqrt(hd))
+// followed by the GQA head-group reduction of dK / dV (cpu_ops.h:585
+// gqa_reduce_kv_f16), evaluated flash-style without materialising P:
+//   delta_kernel   D[b,h,s] = sum_d dO * O      (= rowsum(P * dP))
+//   dkdv_kernel    one CTA per (64-key tile, kv-head, sequence); each warp owns
+//                  16 keys and walks the query tiles at or after its keys,
+//                  for every q-head of the group, so dK/dV of the group are
+//                  summed in registers (no atomics, deterministic)
+//   dq_kernel      one CTA per (64-query tile, q-head, sequence); each warp
+//                  owns 16 queries and walks the key tiles up to the diagonal
+// P is recomputed from the forward's log2-domain row log-sum-exp.  Operands
+// are bf16 (fp16 would underflow dS), fp32 accumulation, m16n8k16 MMAs.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ne_device.cuh"
+#include "ne_internal.h"
+#include "ne_launch.cuh"
+#include "ne_mma.cuh"
+
+namespace ne {
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int KT_KEYS = 64;   // dkdv: keys per CTA
+constexpr int KT_Q = 32;      // dkdv: queries per iteration
+constexpr int QT_Q = 64;      // dq: queries per CTA
+constexpr int QT_KEYS = 32;   // dq: keys per iteration
+
+// ---------------------------------------------------------------- delta
+// One warp per (row, head): D = sum_d dO[row, h, d] * O[row, h, d].
+template <int HD>
+__global__ void delta_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, int rows,
+                             int S, int Hq, float* __restrict__ D) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int PER = HD / 32;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * Hq) return;
+  const int r = gw / Hq, h = gw % Hq;
+  const size_t base = ((size_t)r * Hq + h) * HD + lane * PER;
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc += __bfloat162float(O[base + i]) * __bfloat162float(dO[base + i]);
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const int b = r / S, s = r % S;
+    D[((size_t)b * Hq + h) * S + s] = acc;
+  }
+}
+
+// Fill `rows` x HD of a padded smem tile from global rows (zero beyond `valid`).
+template <int HD>
+__device__ __forceinline__ void load_rows(bf16* dst, const bf16* src, size_t row_stride, int rows,
+                                          int valid) {
+  constexpr int LD = HD + 8, CPR = HD / 8;
+  for (int i = threadIdx.x; i < rows * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i % CPR;
+    const bool ok = r < valid;
+    cp_async16(smem_u32_local(dst + r * LD + c * 8), src + (size_t)(ok ? r : 0) * row_stride + c * 8,
+               ok);
+  }
+}
+
+// ---------------------------------------------------------------- dK, dV
+template <int HD>
+__global__ void __launch_bounds__(128)
+dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V,
+            const bf16* __restrict__ dO, const float* __restrict__ LSE,
+            const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+            float scale, float* __restrict__ dK, float* __restrict__ dV) {
+  constexpr int LD = HD + 8, KS = HD / 16, DT = HD / 8;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* sK = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
+  bf16* sV = sK + KT_KEYS * LD;                    // [64][LD]
+  bf16* sQ = sV + KT_KEYS * LD;                    // [32][LD]
+  bf16* sdO = sQ + KT_Q * LD;                      // [32][LD]
+  float* sL = reinterpret_cast<float*>(sdO + KT_Q * LD);   // [32]
+  float* sD = sL + KT_Q;                                   // [32]
+  pdl_trigger();
+  pdl_wait();
+  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int k0 = kt * KT_KEYS;
+  const size_t kv_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
+  load_rows<HD>(sK, K + kv_base + (size_t)k0 * HD, HD, KT_KEYS, S - k0);
+  load_rows<HD>(sV, V + kv_base + (size_t)k0 * HD, HD, KT_KEYS, S - k0);
+  cp_async_commit();
+
+  float dk[DT][4], dv[DT][4];
+#pragma unroll
+  for (int j = 0; j < DT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk[j][e] = dv[j][e] = 0.f;
+  const int kw = warp * 16;                 // this warp's keys within the tile
+  const int key0 = k0 + kw + g, key1 = key0 + 8;
+
+  for (int gh = 0; gh < G; ++gh) {
+    const int h = kvh * G + gh;
+    for (int q0 = (k0 / KT_Q) * KT_Q; q0 < S; q0 += KT_Q) {
+      __syncthreads();   // previous tile's readers are done
+      const size_t qrow = ((size_t)b * S + q0) * Hq + h;
+      load_rows<HD>(sQ, Q + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
+      load_rows<HD>(sdO, dO + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
+      if (threadIdx.x < KT_Q) {
+        const int qq = q0 + threadIdx.x;
+        sL[threadIdx.x] = qq < S ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
+        sD[threadIdx.x] = qq < S ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+
+      // S^T = K_w Q^T   [16 keys x 32 queries] : 4 n-tiles of 8 queries
+      float st[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st[j][0] = st[j][1] = st[j][2] = st[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(smem_u32_local(sK + (kw + (lane & 15)) * LD + ks * 16 + (lane >> 4) * 8), a[0], a[1],
+                a[2], a[3]);
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          uint32_t b0, b1, b2, b3;
+          const int qr = jp * 16 + (lane >> 4) * 8 + (lane & 7);
+          ldsm_x4(smem_u32_local(sQ + qr * LD + ks * 16 + ((lane >> 3) & 1) * 8), b0, b1, b2, b3);
+          mma16816_bf16(st[2 * jp], a, b0, b1);
+          mma16816_bf16(st[2 * jp + 1], a, b2, b3);
+        }
+      }
+      // P^T (causal: key <= query)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int ql = j * 8 + 2 * tq + (e & 1);
+          const int qq = q0 + ql;
+          const int key = (e < 2) ? key0 : key1;
+          st[j][e] = (key <= qq && qq < S && key < S) ? exp2f(st[j][e] * scale_log2 - sL[ql]) : 0.f;
+        }
+      // dV += P^T dO
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack_bf162(st[2 * kk][0], st[2 * kk][1]);
+        pa[1] = pack_bf162(st[2 * kk][2], st[2 * kk][3]);
+        pa[2] = pack_bf162(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+        pa[3] = pack_bf162(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+#pragma unroll
+        for (int dp = 0; dp < DT / 2; ++dp) {
+          uint32_t b0, b1, b2, b3;
+          const int qr = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+          ldsm_x4_t(smem_u32_local(sdO + qr * LD + dp * 16 + (lane >> 4) * 8), b0, b1, b2, b3);
+          mma16816_bf16(dv[2 * dp], pa, b0, b1);
+          mma16816_bf16(dv[2 * dp + 1], pa, b2, b3);
+        }
+      }
+      // dP^T = V_w dO^T
+      float dpt[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dpt[j][0] = dpt[j][1] = dpt[j][2] = dpt[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(smem_u32_local(sV + (kw + (lane & 15)) * LD + ks * 16 + (lane >> 4) * 8), a[0], a[1],
+                a[2], a[3]);
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          uint32_t b0, b1, b2, b3;
+          const int qr = jp * 16 + (lane >> 4) * 8 + (lane & 7);
+          ldsm_x4(smem_u32_local(sdO + qr * LD + ks * 16 + ((lane >> 3) & 1) * 8), b0, b1, b2, b3);
+          mma16816_bf16(dpt[2 * jp], a, b0, b1);
+          mma16816_bf16(dpt[2 * jp + 1], a, b2, b3);
+        }
+      }
+      // dS^T = P^T (dP^T - D)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int ql = j * 8 + 2 * tq + (e & 1);
+          dpt[j][e] = st[j][e] * (dpt[j][e] - sD[ql]);
+        }
+      // dK += dS^T Q
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack_bf162(dpt[2 * kk][0], dpt[2 * kk][1]);
+        pa[1] = pack_bf162(dpt[2 * kk][2], dpt[2 * kk][3]);
+        pa[2] = pack_bf162(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
+        pa[3] = pack_bf162(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
+#pragma unroll
+        for (int dp = 0; dp < DT / 2; ++dp) {
+          uint32_t b0, b1, b2, b3;
+          const int qr = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+          ldsm_x4_t(smem_u32_local(sQ + qr * LD + dp * 16 + (lane >> 4) * 8), b0, b1, b2, b3);
+          mma16816_bf16(dk[2 * dp], pa, b0, b1);
+          mma16816_bf16(dk[2 * dp + 1], pa, b2, b3);
+        }
+      }
+    }
+  }
+  // store fp32 [B][Hkv][S][HD]
+  const size_t ob = ((size_t)b * Hkv + kvh) * S;
+#pragma unroll
+  for (int j = 0; j < DT; ++j) {
+    const int d = j * 8 + 2 * tq;
+    if (key0 < S) {
+      float* pk = dK + (ob + key0) * HD + d;
+      float* pv = dV + (ob + key0) * HD + d;
+      pk[0] = dk[j][0] * scale; pk[1] = dk[j][1] * scale;
+      pv[0] = dv[j][0]; pv[1] = dv[j][1];
+    }
+    if (key1 < S) {
+      float* pk = dK + (ob + key1) * HD + d;
+      float* pv = dV + (ob + key1) * HD + d;
+      pk[0] = dk[j][2] * scale; pk[1] = dk[j][3] * scale;
+      pv[0] = dv[j][2]; pv[1] = dv[j][3];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- dQ
+template <int HD>
+__global__ void __launch_bounds__(128)
+dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V,
+          const bf16* __restrict__ dO, const float* __restrict__ LSE, const float* __restrict__ Dl,
+          int S, int Hq, int Hkv, int Tmax, float scale_log2, float scale, float* __restrict__ dQ) {
+  constexpr int LD = HD + 8, KS = HD / 16, DT = HD / 8;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* sQ = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
+  bf16* sdO = sQ + QT_Q * LD;                      // [64][LD]
+  bf16* sK = sdO + QT_Q * LD;                      // [32][LD]
+  bf16* sV = sK + QT_KEYS * LD;                    // [32][LD]
+  pdl_trigger();
+  pdl_wait();
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (Hq / Hkv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int q0 = qt * QT_Q;
+  const size_t qrow = ((size_t)b * S + q0) * Hq + h;
+  load_rows<HD>(sQ, Q + qrow * HD, (size_t)Hq * HD, QT_Q, S - q0);
+  load_rows<HD>(sdO, dO + qrow * HD, (size_t)Hq * HD, QT_Q, S - q0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  uint32_t qa[KS][4], oa[KS][4];
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    const int r = warp * 16 + (lane & 15), c = ks * 16 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32_local(sQ + r * LD + c), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    ldsm_x4(smem_u32_local(sdO + r * LD + c), oa[ks][0], oa[ks][1], oa[ks][2], oa[ks][3]);
+  }
+  const int qa0 = q0 + warp * 16 + g, qa1 = qa0 + 8;
+  const float L0 = qa0 < S ? LSE[((size_t)b * Hq + h) * S + qa0] : 0.f;
+  const float L1 = qa1 < S ? LSE[((size_t)b * Hq + h) * S + qa1] : 0.f;
+  const float D0 = qa0 < S ? Dl[((size_t)b * Hq + h) * S + qa0] : 0.f;
+  const float D1 = qa1 < S ? Dl[((size_t)b * Hq + h) * S + qa1] : 0.f;
+  float dq[DT][4];
+#pragma unroll
+  for (int j = 0; j < DT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
+  const size_t kv_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
+  const int kend = min(S, q0 + QT_Q);
+  for (int k0 = 0; k0 < kend; k0 += QT_KEYS) {
+    __syncthreads();
+    load_rows<HD>(sK, K + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
+    load_rows<HD>(sV, V + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    float s[4][4], dp[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[j][e] = dp[j][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int jp = 0; jp < 2; ++jp) {
+        uint32_t b0, b1, b2, b3;
+        const int kr = jp * 16 + (lane >> 4) * 8 + (lane & 7);
+        const int col = ks * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(smem_u32_local(sK + kr * LD + col), b0, b1, b2, b3);
+        mma16816_bf16(s[2 * jp], qa[ks], b0, b1);
+        mma16816_bf16(s[2 * jp + 1], qa[ks], b2, b3);
+        ldsm_x4(smem_u32_local(sV + kr * LD + col), b0, b1, b2, b3);
+        mma16816_bf16(dp[2 * jp], oa[ks], b0, b1);
+        mma16816_bf16(dp[2 * jp + 1], oa[ks], b2, b3);
+      }
+    }
+    // dS = P (dP - D)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + j * 8 + 2 * tq + (e & 1);
+        const int qq = (e < 2) ? qa0 : qa1;
+        const float L = (e < 2) ? L0 : L1, Dd = (e < 2) ? D0 : D1;
+        const float p = (key <= qq && key < S && qq < S) ? exp2f(s[j][e] * scale_log2 - L) : 0.f;
+        s[j][e] = p * (dp[j][e] - Dd);
+      }
+    // dQ += dS K
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf162(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf162(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf162(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf162(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dpi = 0; dpi < DT / 2; ++dpi) {
+        uint32_t b0, b1, b2, b3;
+        const int kr = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        ldsm_x4_t(smem_u32_local(sK + kr * LD + dpi * 16 + (lane >> 4) * 8), b0, b1, b2, b3);
+        mma16816_bf16(dq[2 * dpi], pa, b0, b1);
+        mma16816_bf16(dq[2 * dpi + 1], pa, b2, b3);
+      }
+    }
+  }
+  // store fp32 [B*S][Hq][HD]
+#pragma unroll
+  for (int j = 0; j < DT; ++j) {
+    const int d = j * 8 + 2 * tq;
+    if (qa0 < S) {
+      float* p = dQ + (((size_t)b * S + qa0) * Hq + h) * HD + d;
+      p[0] = dq[j][0] * scale; p[1] = dq[j][1] * scale;
+    }
+    if (qa1 < S) {
+      float* p = dQ + (((size_t)b * S + qa1) * Hq + h) * HD + d;
+      p[0] = dq[j][2] * scale; p[1] = dq[j][3] * scale;
+    }
+  }
+}
+
+template <int HD>
+cudaError_t launch_bwd_t(const bf16* Q, const bf16* K, const bf16* V, const bf16* O, const bf16* dO,
+                         const float* LSE, float* Dl, int B, int S, int Hq, int Hkv, int Tmax,
+                         float* dQ, float* dK, float* dV, cudaStream_t st) {
+  constexpr int LD = HD + 8;
+  const float scale = 1.0f / sqrtf((float)HD);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int rows = B * S;
+  cudaError_t e = launch_k(delta_kernel<HD>, dim3((rows * Hq + 7) / 8), dim3(256), 0, st, O, dO,
+                           rows, S, Hq, Dl);
+  if (e != cudaSuccess) return e;
+  const size_t smem1 = (size_t)(2 * KT_KEYS + 2 * KT_Q) * LD * sizeof(bf16) + 2 * KT_Q * sizeof(float);
+  const size_t smem2 = (size_t)(2 * QT_Q + 2 * QT_KEYS) * LD * sizeof(bf16);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+    cudaFuncSetAttribute(dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+    attr = true;
+  }
+  e = launch_k(dkdv_kernel<HD>, dim3((S + KT_KEYS - 1) / KT_KEYS, Hkv, B), dim3(128), smem1, st, Q,
+               K, V, dO, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, dK, dV);
+  if (e != cudaSuccess) return e;
+  return launch_k(dq_kernel<HD>, dim3((S + QT_Q - 1) / QT_Q, Hq, B), dim3(128), smem2, st, Q, K, V,
+                  dO, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, dQ);
+}
+
+}  // namespace
+
+cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                            const __nv_bfloat16* V, const __nv_bfloat16* O,
+                            const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                            int Hq, int Hkv, int hd, int Tmax, float* dQ, float* dK, float* dV,
+                            cudaStream_t st) {
+  if (hd == 128)
+    return launch_bwd_t<128>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, dQ, dK, dV, st);
+  if (hd == 64)
+    return launch_bwd_t<64>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, dQ, dK, dV, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ne

@@ -18,6 +18,7 @@
 #include "ne_device.cuh"
 #include "ne_internal.h"
 #include "ne_launch.cuh"
+#include "ne_mma.cuh"
 
 namespace ne {
 namespace {
@@ -25,60 +26,18 @@ namespace {
 constexpr int FA_BQ = 64;
 constexpr int FA_BK = 64;
 
-__device__ __forceinline__ uint32_t smem_u32_local(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-  const int sz = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-template <int HD>
+template <int HD, typename T>
 __global__ void __launch_bounds__(128)
-prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
-                    const __half* __restrict__ vc, int S, int pos0, int Hq, int Hkv, int Tmax,
-                    float qscale_log2, __nv_bfloat16* __restrict__ out) {
+prefill_attn_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int S, int pos0, int Hq, int Hkv, int Tmax,
+                    float qscale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
   constexpr int LD = HD + 8;              // padded smem row (halves): conflict-free ldmatrix
   constexpr int KSTEPS = HD / 16;         // k-steps of Q.K^T
   constexpr int DTILES = HD / 8;          // n-tiles of the output
-  extern __shared__ __align__(16) __half smem[];
-  __half* sQ = smem;                      // [FA_BQ][LD]
-  __half* sK = sQ + FA_BQ * LD;           // [2][FA_BK][LD]
-  __half* sV = sK + 2 * FA_BK * LD;       // [2][FA_BK][LD]
+  extern __shared__ __align__(16) unsigned char smem_raw_fa[];
+  T* smem = reinterpret_cast<T*>(smem_raw_fa);
+  T* sQ = smem;                           // [FA_BQ][LD]
+  T* sK = sQ + FA_BQ * LD;                // [2][FA_BK][LD]
+  T* sV = sK + 2 * FA_BK * LD;            // [2][FA_BK][LD]
 
   pdl_trigger();
   pdl_wait();
@@ -90,20 +49,20 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
   const int n_kt = (n_keys + FA_BK - 1) / FA_BK;
 
   const size_t kv_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
-  const __half* kg = kc + kv_base;
-  const __half* vg = vc + kv_base;
+  const T* kg = kc + kv_base;
+  const T* vg = vc + kv_base;
 
   // ---- load Q tile (rows beyond S are zero-filled)
   constexpr int CPR = HD / 8;             // 16-byte chunks per row
   for (int i = threadIdx.x; i < FA_BQ * CPR; i += 128) {
     const int r = i / CPR, c = i % CPR;
     const bool ok = q0 + r < S;
-    const __half* src = q + (((size_t)b * S + (ok ? q0 + r : 0)) * Hq + h) * HD + c * 8;
+    const T* src = q + (((size_t)b * S + (ok ? q0 + r : 0)) * Hq + h) * HD + c * 8;
     cp_async16(smem_u32_local(sQ + r * LD + c * 8), src, ok);
   }
   auto load_kv = [&](int kt, int buf) {
-    __half* dK = sK + buf * FA_BK * LD;
-    __half* dV = sV + buf * FA_BK * LD;
+    T* dK = sK + buf * FA_BK * LD;
+    T* dV = sV + buf * FA_BK * LD;
     for (int i = threadIdx.x; i < FA_BK * CPR; i += 128) {
       const int r = i / CPR, c = i % CPR;
       const int t = kt * FA_BK + r;
@@ -141,8 +100,8 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
         ldsm_x4(smem_u32_local(sQ + r * LD + c), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
       }
     }
-    const __half* cK = sK + buf * FA_BK * LD;
-    const __half* cV = sV + buf * FA_BK * LD;
+    const T* cK = sK + buf * FA_BK * LD;
+    const T* cV = sV + buf * FA_BK * LD;
 
     // ---- S = Q K^T  (16 x 64 per warp: 8 n-tiles of 8 keys)
     float s[8][4];
@@ -156,8 +115,8 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
         const int key = jp * 16 + (lane >> 4) * 8 + (lane & 7);
         const int col = ks * 16 + ((lane >> 3) & 1) * 8;
         ldsm_x4(smem_u32_local(cK + key * LD + col), b0, b1, b2, b3);
-        mma16816(s[2 * jp], qa[ks], b0, b1);
-        mma16816(s[2 * jp + 1], qa[ks], b2, b3);
+        Mma16<T>::mma(s[2 * jp], qa[ks], b0, b1);
+        Mma16<T>::mma(s[2 * jp + 1], qa[ks], b2, b3);
       }
     }
     // ---- scale, causal mask, online softmax (log2 domain)
@@ -208,18 +167,18 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t pa[4];
-      pa[0] = pack_half2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_half2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      pa[0] = Mma16<T>::pack(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = Mma16<T>::pack(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = Mma16<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = Mma16<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
       for (int dp = 0; dp < DTILES / 2; ++dp) {
         uint32_t b0, b1, b2, b3;
         const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
         const int col = dp * 16 + (lane >> 4) * 8;
         ldsm_x4_t(smem_u32_local(cV + key * LD + col), b0, b1, b2, b3);
-        mma16816(o[2 * dp], pa, b0, b1);
-        mma16816(o[2 * dp + 1], pa, b2, b3);
+        Mma16<T>::mma(o[2 * dp], pa, b0, b1);
+        Mma16<T>::mma(o[2 * dp + 1], pa, b2, b3);
       }
     }
     __syncthreads();
@@ -228,6 +187,12 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
   // ---- normalise and store bf16 [row][Hq*HD]
   const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
   const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
+  // log2-domain log-sum-exp of each row's scaled scores, for the backward pass:
+  // P = exp2(s * scale * log2(e) - lse); layout [b][h][row]
+  if (lse != nullptr && tq == 0) {
+    if (r0 < S) lse[((size_t)b * Hq + h) * S + r0] = mrow[0] + log2f(lrow[0]);
+    if (r1 < S) lse[((size_t)b * Hq + h) * S + r1] = mrow[1] + log2f(lrow[1]);
+  }
 #pragma unroll
   for (int j = 0; j < DTILES; ++j) {
     const int d = j * 8 + 2 * tq;
@@ -242,34 +207,45 @@ prefill_attn_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
   }
 }
 
-}  // namespace
-
-cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half* vc, int B, int S,
-                                int pos0, int Hq, int Hkv, int hd, int Tmax, __nv_bfloat16* out,
-                                cudaStream_t st) {
+template <typename T>
+cudaError_t launch_fa(const T* q, const T* kc, const T* vc, int B, int S, int pos0, int Hq, int Hkv,
+                      int hd, int Tmax, __nv_bfloat16* out, cudaStream_t st, float* lse) {
   if (pos0 + S > Tmax || Hq % Hkv) return cudaErrorInvalidValue;
   const float qs = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   const dim3 grid((S + FA_BQ - 1) / FA_BQ, Hq, B);
   if (hd == 128) {
     constexpr int LD = 128 + 8;
-    const size_t smem = (size_t)(FA_BQ + 4 * FA_BK) * LD * sizeof(__half);
+    const size_t smem = (size_t)(FA_BQ + 4 * FA_BK) * LD * sizeof(T);
     static bool done = false;
     if (!done) {
-      cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(prefill_attn_kernel<128, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
       done = true;
     }
-    return launch_k(prefill_attn_kernel<128>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
-                    Hkv, Tmax, qs, out);
+    return launch_k(prefill_attn_kernel<128, T>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
+                    Hkv, Tmax, qs, out, lse);
   } else if (hd == 64) {
     constexpr int LD = 64 + 8;
-    const size_t smem = (size_t)(FA_BQ + 4 * FA_BK) * LD * sizeof(__half);
-    return launch_k(prefill_attn_kernel<64>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
-                    Hkv, Tmax, qs, out);
-  } else {
-    return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(FA_BQ + 4 * FA_BK) * LD * sizeof(T);
+    return launch_k(prefill_attn_kernel<64, T>, grid, dim3(128), smem, st, q, kc, vc, S, pos0, Hq,
+                    Hkv, Tmax, qs, out, lse);
   }
-  return cudaGetLastError();
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half* vc, int B, int S,
+                                int pos0, int Hq, int Hkv, int hd, int Tmax, __nv_bfloat16* out,
+                                cudaStream_t st, float* lse) {
+  return launch_fa<__half>(q, kc, vc, B, S, pos0, Hq, Hkv, hd, Tmax, out, st, lse);
+}
+
+cudaError_t launch_prefill_attn_bf16(const __nv_bfloat16* q, const __nv_bfloat16* kc,
+                                     const __nv_bfloat16* vc, int B, int S, int pos0, int Hq,
+                                     int Hkv, int hd, int Tmax, __nv_bfloat16* out, cudaStream_t st,
+                                     float* lse) {
+  return launch_fa<__nv_bfloat16>(q, kc, vc, B, S, pos0, Hq, Hkv, hd, Tmax, out, st, lse);
 }
 
 }  // namespace ne

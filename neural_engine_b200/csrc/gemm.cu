@@ -47,53 +47,89 @@ bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int K, long long ld, 
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, class Epi, int FMT>
+// 2-D MN-major operand: global [K rows, MN] (MN contiguous, leading dim ld),
+// boxes of 64 (MN) x 64 (K rows), 128B-swizzled.
+bool make_tmap_mn(CUtensorMap* tm, const void* ptr, int mn, int K, long long ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)mn, (cuuint64_t)K};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)GEMM_BK};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, class Epi, int FMT, int AMN, int BMN>
 cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh,
                      const typename Epi::Params& p, int grid, cudaStream_t st) {
   using C = GemmCfg<BN>;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  return launch_k(gemm_tc_kernel<BN, Epi, FMT>, dim3(grid), dim3(GEMM_THREADS),
+  return launch_k(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>, dim3(grid), dim3(GEMM_THREADS),
                   (size_t)C::SMEM_BYTES, st, ta, tb, sh, p);
 }
 
-template <int BN, int FMT>
+// Epilogue dispatch.  K-major x K-major serves every epilogue; the MN-major
+// variants (training backward) instantiate only the epilogues they use.
+template <int BN, int FMT, int AMN, int BMN>
 cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorMap& tb,
                        const GemmShape& sh, int grid, cudaStream_t st) {
+  constexpr bool kk = (AMN == 0 && BMN == 0);
+  constexpr bool kmn = (AMN == 0 && BMN == 1);
+  constexpr bool ch32 = GemmCfg<BN>::CH == 32;
   switch (c.epi) {
-    case EPI_F32T: {
-      EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
-      return launch_t<BN, EpiF32T, FMT>(ta, tb, sh, p, grid, st);
-    }
+    case EPI_F32T:
+      if constexpr (kk) {
+        EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
+        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      }
+      break;
     case EPI_F32: {
       EpiF32::Params p{(float*)c.out, c.ld, c.split_stride};
-      return launch_t<BN, EpiF32, FMT>(ta, tb, sh, p, grid, st);
+      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
     }
-    case EPI_BF16: {
-      EpiBF16::Params p{(__nv_bfloat16*)c.out, c.ld};
-      return launch_t<BN, EpiBF16, FMT>(ta, tb, sh, p, grid, st);
-    }
+    case EPI_BF16:
+      if constexpr (kk || kmn) {
+        EpiBF16::Params p{c.out, c.ld, c.alpha, c.half_out};
+        return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      }
+      break;
     case EPI_RESID: {
       EpiResid::Params p{(float*)c.out, c.ld, c.alpha};
-      return launch_t<BN, EpiResid, FMT>(ta, tb, sh, p, grid, st);
+      return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
     }
-    case EPI_SWIGLU: {
-      if constexpr (GemmCfg<BN>::CH == 32) {
+    case EPI_SWIGLU:
+      if constexpr (kk && ch32) {
         EpiSwiGLU::Params p{(__nv_bfloat16*)c.out, c.ld, (__nv_bfloat16*)c.aux1,
                             (__nv_bfloat16*)c.aux2};
-        return launch_t<BN, EpiSwiGLU, FMT>(ta, tb, sh, p, grid, st);
-      } else {
-        return cudaErrorInvalidValue;
+        return launch_t<BN, EpiSwiGLU, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
       }
-    }
+      break;
+    case EPI_ADD:
+      if constexpr (kk) {
+        EpiAdd::Params p{(float*)c.out, (const float*)c.aux3, c.ld, c.alpha};
+        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      }
+      break;
+    case EPI_SWIGLU_BWD:
+      if constexpr ((kk || kmn) && ch32) {
+        EpiSwiGLUBwd::Params p{(__nv_bfloat16*)c.out, (const __nv_bfloat16*)c.aux3,
+                               (const __nv_bfloat16*)c.aux1, c.aux_ld, c.alpha};
+        return launch_t<BN, EpiSwiGLUBwd, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      }
+      break;
     default:
-      return cudaErrorInvalidValue;
+      break;
   }
+  return cudaErrorInvalidValue;
 }
 
 int pick_bn(const GemmCall& c) {
@@ -144,16 +180,22 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   if ((c.lda * 2) % 16 != 0 || (c.ldb * 2) % 16 != 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(c.A) & 15) || (reinterpret_cast<uintptr_t>(c.B) & 15))
     return cudaErrorInvalidValue;
+  if (c.ab_fp16) return cudaErrorInvalidValue;   // bf16 operands only in this build
+  if (c.a_mn && !c.b_mn) return cudaErrorInvalidValue;
   const int num_sms = device_num_sms();
-  const int bn = pick_bn(c);
+  int bn = pick_bn(c);
+  if (c.b_mn && bn < 64) bn = 64;
   const int splits = gemm_pick_splits(c, num_sms);
   const int kb = c.K / GEMM_BK;
   if (kb % splits != 0) return cudaErrorInvalidValue;
   if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32) return cudaErrorInvalidValue;
 
   CUtensorMap ta, tb;
-  if (!make_tmap(&ta, c.A, c.M, c.K, c.lda, GEMM_BM, c.ab_fp16)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tb, c.B, c.N, c.K, c.ldb, bn, c.ab_fp16)) return cudaErrorInvalidValue;
+  const bool ok_a = c.a_mn ? make_tmap_mn(&ta, c.A, c.M, c.K, c.lda)
+                           : make_tmap(&ta, c.A, c.M, c.K, c.lda, GEMM_BM, 0);
+  const bool ok_b = c.b_mn ? make_tmap_mn(&tb, c.B, c.N, c.K, c.ldb)
+                           : make_tmap(&tb, c.B, c.N, c.K, c.ldb, bn, 0);
+  if (!ok_a || !ok_b) return cudaErrorInvalidValue;
 
   GemmShape sh;
   sh.M = c.M;
@@ -169,20 +211,30 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   const int cap = c.max_ctas > 0 ? c.max_ctas : num_sms;
   const int grid = (int)(units < cap ? units : cap);
 
-#define NE_BN(BN_)                                                       \
-  case BN_:                                                              \
-    return c.ab_fp16 ? launch_epi<BN_, 0>(c, ta, tb, sh, grid, st)       \
-                     : launch_epi<BN_, 1>(c, ta, tb, sh, grid, st);
-  switch (bn) {
-    NE_BN(16)
-    NE_BN(32)
-    NE_BN(64)
-    NE_BN(128)
-    NE_BN(256)
-    default:
-      return cudaErrorInvalidValue;
+  if (!c.a_mn && !c.b_mn) {
+    switch (bn) {
+      case 16: return launch_epi<16, 1, 0, 0>(c, ta, tb, sh, grid, st);
+      case 32: return launch_epi<32, 1, 0, 0>(c, ta, tb, sh, grid, st);
+      case 64: return launch_epi<64, 1, 0, 0>(c, ta, tb, sh, grid, st);
+      case 128: return launch_epi<128, 1, 0, 0>(c, ta, tb, sh, grid, st);
+      case 256: return launch_epi<256, 1, 0, 0>(c, ta, tb, sh, grid, st);
+      default: return cudaErrorInvalidValue;
+    }
   }
-#undef NE_BN
+  if (!c.a_mn) {
+    switch (bn) {
+      case 64: return launch_epi<64, 1, 0, 1>(c, ta, tb, sh, grid, st);
+      case 128: return launch_epi<128, 1, 0, 1>(c, ta, tb, sh, grid, st);
+      case 256: return launch_epi<256, 1, 0, 1>(c, ta, tb, sh, grid, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (bn) {
+    case 64: return launch_epi<64, 1, 1, 1>(c, ta, tb, sh, grid, st);
+    case 128: return launch_epi<128, 1, 1, 1>(c, ta, tb, sh, grid, st);
+    case 256: return launch_epi<256, 1, 1, 1>(c, ta, tb, sh, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace ne

@@ -95,28 +95,129 @@ struct EpiF32 {
   }
 };
 
-// bf16 store, row-major:  out[m*ld + n]
+// 16-bit store, row-major:  out[m*ld + n] = alpha * acc  (bf16, or fp16 if half_out)
 struct EpiBF16 {
-  struct Params { __nv_bfloat16* out; long long ld; };
+  struct Params { void* out; long long ld; float alpha; int half_out; };
   template <int CH>
   __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
                                int M, int N) {
     if (m >= M) return;
-    __nv_bfloat16* row = p.out + (long long)m * p.ld + n0;
+    const long long base = (long long)m * p.ld + n0;
+    float w[CH];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) w[j] = p.alpha * v[j];
+    if (p.half_out) {
+      __half* row = reinterpret_cast<__half*>(p.out) + base;
+      if (n0 + CH <= N) {
+#pragma unroll
+        for (int j = 0; j < CH; j += 8) {
+          uint4 pk;
+          __half2* h = reinterpret_cast<__half2*>(&pk);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(w[j + 2 * t], w[j + 2 * t + 1]);
+          *reinterpret_cast<uint4*>(row + j) = pk;
+        }
+      } else {
+        for (int j = 0; j < CH; ++j)
+          if (n0 + j < N) row[j] = __float2half_rn(w[j]);
+      }
+      return;
+    }
+    __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(p.out) + base;
     if (n0 + CH <= N) {
 #pragma unroll
       for (int j = 0; j < CH; j += 8) {
         uint4 pk;
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
-        h[0] = __floats2bfloat162_rn(v[j], v[j + 1]);
-        h[1] = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-        h[2] = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-        h[3] = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(w[j + 2 * t], w[j + 2 * t + 1]);
         *reinterpret_cast<uint4*>(row + j) = pk;
       }
     } else {
       for (int j = 0; j < CH; ++j)
-        if (n0 + j < N) row[j] = __float2bfloat16_rn(v[j]);
+        if (n0 + j < N) row[j] = __float2bfloat16_rn(w[j]);
+    }
+  }
+};
+
+// fp32 add, row-major:  out[m*ld + n] = in[m*ld + n] + alpha * acc
+struct EpiAdd {
+  struct Params { float* out; const float* in; long long ld; float alpha; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    if (m >= M) return;
+    float* orow = p.out + (long long)m * p.ld + n0;
+    const float* irow = p.in + (long long)m * p.ld + n0;
+    if (n0 + CH <= N) {
+#pragma unroll
+      for (int j = 0; j < CH; j += 4) {
+        float4 r = *reinterpret_cast<const float4*>(irow + j);
+        r.x += p.alpha * v[j]; r.y += p.alpha * v[j + 1];
+        r.z += p.alpha * v[j + 2]; r.w += p.alpha * v[j + 3];
+        *reinterpret_cast<float4*>(orow + j) = r;
+      }
+    } else {
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) orow[j] = irow[j] + p.alpha * v[j];
+    }
+  }
+};
+
+// SwiGLU backward (ffnBwdFull, mil_dynamic.h:320-409): acc = d_gate[m, f] for
+// 32 consecutive features f; with the saved h1, h3 [m, F] (bf16):
+//   dh1 = alpha*dg * h3 * s * (1 + h1 * (1 - s)),  s = sigmoid(h1)
+//   dh3 = alpha*dg * h1 * s
+// written bf16 into dh13 [m, 2F] in the W1/W3 16-row-interleaved order.
+struct EpiSwiGLUBwd {
+  struct Params {
+    __nv_bfloat16* dh13; const __nv_bfloat16* h1; const __nv_bfloat16* h3; long long F; float alpha;
+  };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
+    if (m >= M || n0 >= N) return;
+    const __nv_bfloat16* a = p.h1 + (long long)m * p.F + n0;
+    const __nv_bfloat16* b = p.h3 + (long long)m * p.F + n0;
+    __nv_bfloat16* out = p.dh13 + (long long)m * 2 * p.F;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int f0 = n0 + 16 * half;            // 16 features of block c = f0 / 16
+      float d1[16], d3[16];
+#pragma unroll
+      for (int j = 0; j < 16; j += 8) {
+        const uint4 ra = *reinterpret_cast<const uint4*>(a + 16 * half + j);
+        const uint4 rb = *reinterpret_cast<const uint4*>(b + 16 * half + j);
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra);
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 x1 = __bfloat1622float2(ha[t]);
+          const float2 x3 = __bfloat1622float2(hb[t]);
+          const float g0 = p.alpha * v[16 * half + j + 2 * t];
+          const float g1 = p.alpha * v[16 * half + j + 2 * t + 1];
+          const float s0 = 1.0f / (1.0f + __expf(-x1.x)), s1 = 1.0f / (1.0f + __expf(-x1.y));
+          d1[j + 2 * t] = g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0));
+          d1[j + 2 * t + 1] = g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1));
+          d3[j + 2 * t] = g0 * x1.x * s0;
+          d3[j + 2 * t + 1] = g1 * x1.y * s1;
+        }
+      }
+      __nv_bfloat16* o1 = out + (long long)(f0 / 16) * 32;
+#pragma unroll
+      for (int j = 0; j < 16; j += 8) {
+        uint4 p1, p3;
+        __nv_bfloat162* h1 = reinterpret_cast<__nv_bfloat162*>(&p1);
+        __nv_bfloat162* h3 = reinterpret_cast<__nv_bfloat162*>(&p3);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          h1[t] = __floats2bfloat162_rn(d1[j + 2 * t], d1[j + 2 * t + 1]);
+          h3[t] = __floats2bfloat162_rn(d3[j + 2 * t], d3[j + 2 * t + 1]);
+        }
+        *reinterpret_cast<uint4*>(o1 + j) = p1;
+        *reinterpret_cast<uint4*>(o1 + 16 + j) = p3;
+      }
     }
   }
 };
@@ -196,14 +297,19 @@ struct EpiSwiGLU {
 };
 
 // ------------------------------------------------------------------ kernel
-template <int BN, class Epi, int AB_FMT>
+// A_MN / B_MN: the operand is stored MN-major in global memory ([K rows][MN
+// contiguous]); its tile is then loaded as 64-wide MN boxes of 64 K-rows (8 KB
+// each, placed 8 KB apart) and described to the MMA as MN-major.
+template <int BN, class Epi, int AB_FMT, int A_MN = 0, int B_MN = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const GemmShape sh, const typename Epi::Params ep) {
   using C = GemmCfg<BN>;
+  static_assert(!B_MN || BN % 64 == 0, "MN-major B needs whole 64-wide boxes");
+  constexpr uint32_t MN_BOX = 64 * GEMM_BK * 2;   // one 64 (MN) x 64 (K) box
   constexpr int STAGES = C::STAGES;
   constexpr int CH = C::CH;
-  constexpr uint32_t IDESC = umma_idesc_f16(GEMM_BM, BN, AB_FMT);
+  constexpr uint32_t IDESC = umma_idesc_f16(GEMM_BM, BN, AB_FMT, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled tiles
@@ -255,6 +361,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       const uint64_t pol_a = policy_evict_first();
       const uint64_t pol_b = policy_evict_last();
+      auto load_a = [&](uint32_t dst, uint32_t bar, int k0, int m0) {
+        if constexpr (A_MN) {
+#pragma unroll
+          for (int j = 0; j < GEMM_BM / 64; ++j)
+            tma_load_2d(dst + j * MN_BOX, &tmA, bar, m0 + 64 * j, k0, pol_a);
+        } else {
+          tma_load_2d(dst, &tmA, bar, k0, m0, pol_a);
+        }
+      };
+      auto load_b = [&](uint32_t dst, uint32_t bar, int k0, int n0) {
+        if constexpr (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(dst + j * MN_BOX, &tmB, bar, n0 + 64 * j, k0, pol_b);
+        } else {
+          tma_load_2d(dst, &tmB, bar, k0, n0, pol_b);
+        }
+      };
       // Prologue overlap: the first stages' A tiles of this CTA's first unit
       // (weights that no preceding kernel writes) are requested before the
       // programmatic-dependency wait; their B tiles follow after it.
@@ -266,8 +390,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         pre = sh.kb_per_split < STAGES ? sh.kb_per_split : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
           mbar_arrive_expect_tx(full_bar + 8 * kb, C::STAGE_BYTES);
-          tma_load_2d(tiles + kb * C::STAGE_BYTES, &tmA, full_bar + 8 * kb, (kb0 + kb) * GEMM_BK,
-                      mt * GEMM_BM, pol_a);
+          load_a(tiles + kb * C::STAGE_BYTES, full_bar + 8 * kb, (kb0 + kb) * GEMM_BK, mt * GEMM_BM);
         }
       }
       pdl_wait();
@@ -289,10 +412,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               break;
             }
             mbar_arrive_expect_tx(full_bar + 8 * stage, C::STAGE_BYTES);
-            tma_load_2d(sa, &tmA, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM, pol_a);
+            load_a(sa, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM);
           }
-          tma_load_2d(sa + C::A_BYTES, &tmB, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN,
-                      pol_b);
+          load_b(sa + C::A_BYTES, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         first = false;
@@ -326,13 +448,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!mbar_wait(full_bar + 8 * stage, phase, sh.status, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = tiles + stage * C::STAGE_BYTES;
-          const uint64_t adesc = smem_desc_k_sw128(sa);
-          const uint64_t bdesc = smem_desc_k_sw128(sa + C::A_BYTES);
+          // K-major: advance 16 elements (32 B) inside the swizzle atom (+2 in
+          // addr>>4); MN-major: advance 16 K-rows (2 x 1 KB groups, +128).
+          const uint64_t adesc = A_MN ? smem_desc_mn_sw128(sa, MN_BOX) : smem_desc_k_sw128(sa);
+          const uint64_t bdesc = B_MN ? smem_desc_mn_sw128(sa + C::A_BYTES, MN_BOX)
+                                      : smem_desc_k_sw128(sa + C::A_BYTES);
+          constexpr uint64_t A_STEP = A_MN ? 128 : 2;
+          constexpr uint64_t B_STEP = B_MN ? 128 : 2;
 #pragma unroll
-          for (int k = 0; k < GEMM_BK / 16; ++k) {
-            // advance 16 elements (32 bytes) inside the swizzle atom: +2 in addr>>4
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
-          }
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_f16(d_tmem, adesc + A_STEP * k, bdesc + B_STEP * k, IDESC, (kb | k) != 0);
           umma_commit(empty_bar + 8 * stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }

@@ -118,13 +118,24 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
 // One warp per (row, head-vector).  Head vectors per row: Hq + 2*Hkv (q, k, v).
 // qkv row layout (the fused projection's output): [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].
 // Row r belongs to sequence b = r / S_rows at position pos0 + r % S_rows.
-template <int HD, typename QT>
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <int HD, typename QT, typename KT>
 __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long long split_stride,
                                 int rows, int S_rows, const int* __restrict__ d_pos, int pos0,
                                 int Hq, int Hkv, const float* __restrict__ qn,
                                 const float* __restrict__ kn, float qk_eps,
                                 const float2* __restrict__ rope_cs, QT* __restrict__ q_out,
-                                __half* __restrict__ kc, __half* __restrict__ vc, int Tmax,
+                                KT* __restrict__ kc, KT* __restrict__ vc, int Tmax,
                                 int* status) {
   pdl_trigger();
   pdl_wait();
@@ -175,16 +186,13 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
   if (is_q) {
     QT* dst = q_out + ((size_t)r * Hq + h) * HD + lane * PER;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      if constexpr (sizeof(QT) == 4) dst[i] = v[i];
-      else dst[i] = __float2half_rn(v[i]);
-    }
+    for (int i = 0; i < PER; ++i) dst[i] = from_f32<QT>(v[i]);
   } else {
     const int kvh = is_k ? (h - Hq) : (h - Hq - Hkv);
-    __half* cache = is_k ? kc : vc;
-    __half* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
+    KT* cache = is_k ? kc : vc;
+    KT* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) dst[i] = __float2half_rn(v[i]);
+    for (int i = 0; i < PER; ++i) dst[i] = from_f32<KT>(v[i]);
   }
 }
 
@@ -282,25 +290,27 @@ cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
                             int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
-                            void* q_out, int q_fp16, __half* kc, __half* vc, int Tmax, int* status,
-                            cudaStream_t st) {
+                            void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
+                            cudaStream_t st, int kv_bf16) {
   const int warps = rows * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = (warps + 7) / 8;
-  cudaError_t e;
-#define NE_QKV(HD_, QT_)                                                                      \
-  e = launch_k(qkv_post_kernel<HD_, QT_>, dim3(blocks), dim3(threads), 0, st, qkv, nsplit,   \
-               split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs,     \
-               reinterpret_cast<QT_*>(q_out), kc, vc, Tmax, status)
+#define NE_QKV(HD_, QT_, KT_)                                                                    \
+  return launch_k(qkv_post_kernel<HD_, QT_, KT_>, dim3(blocks), dim3(threads), 0, st, qkv, nsplit, \
+                  split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs,     \
+                  reinterpret_cast<QT_*>(q_out), reinterpret_cast<KT_*>(kc),                     \
+                  reinterpret_cast<KT_*>(vc), Tmax, status)
   if (hd == 128) {
-    if (q_fp16) NE_QKV(128, __half); else NE_QKV(128, float);
+    if (kv_bf16) NE_QKV(128, __nv_bfloat16, __nv_bfloat16);
+    if (q_type == 1) NE_QKV(128, __half, __half);
+    NE_QKV(128, float, __half);
   } else if (hd == 64) {
-    if (q_fp16) NE_QKV(64, __half); else NE_QKV(64, float);
-  } else {
-    return cudaErrorInvalidValue;
+    if (kv_bf16) NE_QKV(64, __nv_bfloat16, __nv_bfloat16);
+    if (q_type == 1) NE_QKV(64, __half, __half);
+    NE_QKV(64, float, __half);
   }
 #undef NE_QKV
-  return e;
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,

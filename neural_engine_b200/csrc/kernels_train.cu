@@ -1,0 +1,372 @@
+// kernels_train.cu -- elementwise / reduction kernels of the training step.
+//
+//   rmsnorm_bwd       dx = rrms * (w*dy - x * rrms^2 * sum(dy*w*x) / D) (+ residual),
+//                     dw += dy * x * rrms.  The reference's CPU routine
+//                     (ane-training/training/training_dynamic/cpu_ops.h:108-261)
+//                     multiplies its whole result by w (exact only for unit
+//                     gains); this kernel is the exact derivative of
+//                     rmsnorm (generate.py:81-84), the oracle's definition.
+//   ce_rows           per token: loss = -log(softmax(logits)[target] + 1e-10),
+//                     dlogits = (softmax - onehot) * scale  (cpu_ops.h:348-382)
+//   qk_rope_bwd       inverse RoPE rotation (cpu_ops.h:479-506) then per-head
+//                     QK-RMSNorm backward; writes d(qkv) bf16 and gain grads
+//   embed_bwd         dE[tok] += dx  (cpu_ops.h:441-447)
+//   adamw             decoupled AdamW with bias correction (cpu_ops.h:266-303)
+//                     on fp32 masters, writing the bf16 compute copy
+//   sumsq             sum of squares for the global gradient norm (train.m:805-826)
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "ne_device.cuh"
+#include "ne_internal.h"
+#include "ne_launch.cuh"
+
+namespace ne {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float block_sum256(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+// ------------------------------------------------------------ RMSNorm backward
+// Block of 256 threads handles R consecutive rows; D <= 256 * 4.
+constexpr int RB_ROWS = 8;
+__global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                   const float* __restrict__ w, float eps, int M, int D,
+                                   const float* __restrict__ residual, float* __restrict__ dx,
+                                   bf16* __restrict__ dx16, float* __restrict__ dw) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  constexpr int PER = 4;
+  float dwp[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) dwp[k] = 0.f;
+  const int r0 = blockIdx.x * RB_ROWS;
+  for (int rr = 0; rr < RB_ROWS; ++rr) {
+    const int r = r0 + rr;
+    if (r >= M) break;
+    const float* xr = x + (size_t)r * D;
+    const float* gr = dy + (size_t)r * D;
+    float xv[PER], gv[PER], wv[PER];
+    float ss = 0.f, dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = threadIdx.x + k * 256;
+      xv[k] = i < D ? xr[i] : 0.f;
+      gv[k] = i < D ? gr[i] : 0.f;
+      wv[k] = i < D ? w[i] : 0.f;
+      ss += xv[k] * xv[k];
+      dot += gv[k] * wv[k] * xv[k];
+    }
+    ss = block_sum256(ss, red);
+    dot = block_sum256(dot, red);
+    const float rrms = 1.0f / sqrtf(ss / (float)D + eps);
+    const float c = rrms * rrms * dot / (float)D;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (i >= D) continue;
+      float v = rrms * (wv[k] * gv[k] - xv[k] * c);
+      if (residual) v += residual[(size_t)r * D + i];
+      dx[(size_t)r * D + i] = v;
+      if (dx16) dx16[(size_t)r * D + i] = __float2bfloat16_rn(v);
+      dwp[k] += gv[k] * xv[k] * rrms;
+    }
+  }
+  if (dw) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (i < D) atomicAdd(dw + i, dwp[k]);
+    }
+  }
+}
+
+// ------------------------------------------------------------ cross-entropy
+// One block (1024 threads) per row of logits [rows, V] (fp32).  Writes the
+// row's loss and dlogits (bf16) = (softmax - onehot(target)) * scale.
+__global__ void ce_rows_kernel(const float* __restrict__ logits, const int32_t* __restrict__ tgt,
+                               int V, float scale, float* __restrict__ loss,
+                               bf16* __restrict__ dlogits, int* status) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red_m[32], red_s[32];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * V;
+  float m = -FLT_MAX, s = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = row[i];
+    if (v > m) {
+      s = s * __expf(m - v) + 1.f;
+      m = v;
+    } else {
+      s += __expf(v - m);
+    }
+  }
+  // combine (m, s) across the block
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = s * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { red_m[w] = m; red_s[w] = s; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    m = l < nw ? red_m[l] : -FLT_MAX;
+    s = l < nw ? red_s[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const float os = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, om);
+      s = s * __expf(m - nm) + os * __expf(om - nm);
+      m = nm;
+    }
+    if (l == 0) { red_m[0] = m; red_s[0] = s; }
+  }
+  __syncthreads();
+  m = red_m[0];
+  s = red_s[0];
+  int t = tgt[r];
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) atomicExch(status, DEV_ERR_BOUNDS);
+    t = 0;
+  }
+  const float inv = 1.0f / s;
+  if (threadIdx.x == 0) {
+    const float pt = expf(row[t] - m) * inv;
+    loss[r] = -logf(pt + 1e-10f);
+  }
+  bf16* drow = dlogits + (size_t)r * V;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float p = expf(row[i] - m) * inv;
+    if (i == t) p -= 1.0f;
+    drow[i] = __float2bfloat16_rn(p * scale);
+  }
+}
+
+// ------------------------------------------------------------ RoPE + QK-norm backward
+// Grid (ceil(M / QRB), Hq + 2*Hkv); 8 warps, each walks QRB/8 rows of one
+// head-vector h.  Row r = b*S + s is at position pos0 + s.
+constexpr int QRB = 64;
+template <int HD>
+__global__ void qk_rope_bwd_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
+                                   const float* __restrict__ dV, const float* __restrict__ qkv_raw,
+                                   const float* __restrict__ qn, const float* __restrict__ kn,
+                                   float qk_eps, const float2* __restrict__ rope_cs, int M, int S,
+                                   int pos0, int Hq, int Hkv, bf16* __restrict__ dqkv,
+                                   float* __restrict__ dqn, float* __restrict__ dkn) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int PER = HD / 32;
+  __shared__ float red[8][HD];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
+  const int qkv_dim = (Hq + 2 * Hkv) * HD;
+  const float* gain = is_q ? qn : (is_k ? kn : nullptr);
+  float dg[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) dg[i] = 0.f;
+  for (int r = blockIdx.x * QRB + warp; r < min(M, (blockIdx.x + 1) * QRB); r += 8) {
+    const int b = r / S, s = r % S;
+    float d[PER];
+    if (is_q) {
+      const float* src = dQ + ((size_t)r * Hq + h) * HD + lane * PER;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) d[i] = src[i];
+    } else {
+      const int kvh = is_k ? h - Hq : h - Hq - Hkv;
+      const float* src = (is_k ? dK : dV) + (((size_t)b * Hkv + kvh) * S + s) * HD + lane * PER;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) d[i] = src[i];
+    }
+    if (is_q || is_k) {
+      // inverse rotation of the interleaved pairs
+      const float2* cs = rope_cs + (size_t)(pos0 + s) * (HD / 2) + lane * (PER / 2);
+#pragma unroll
+      for (int i = 0; i < PER / 2; ++i) {
+        const float2 c = cs[i];
+        const float d0 = d[2 * i], d1 = d[2 * i + 1];
+        d[2 * i] = d0 * c.x + d1 * c.y;
+        d[2 * i + 1] = d1 * c.x - d0 * c.y;
+      }
+      if (gain != nullptr) {
+        const float* xr = qkv_raw + (size_t)r * qkv_dim + h * HD + lane * PER;
+        float xv[PER], ss = 0.f, dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          xv[i] = xr[i];
+          ss += xv[i] * xv[i];
+          dot += d[i] * gain[lane * PER + i] * xv[i];
+        }
+        ss = warp_sum(ss);
+        dot = warp_sum(dot);
+        const float rrms = 1.0f / sqrtf(ss / (float)HD + qk_eps);
+        const float c = rrms * rrms * dot / (float)HD;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          dg[i] += d[i] * xv[i] * rrms;
+          d[i] = rrms * (gain[lane * PER + i] * d[i] - xv[i] * c);
+        }
+      }
+    }
+    bf16* dst = dqkv + (size_t)r * qkv_dim + h * HD + lane * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) dst[i] = __float2bfloat16_rn(d[i]);
+  }
+  if (gain != nullptr) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) red[warp][lane * PER + i] = dg[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += red[w][i];
+      atomicAdd((is_q ? dqn : dkn) + i, t);
+    }
+  }
+}
+
+// ------------------------------------------------------------ embedding backward
+__global__ void embed_bwd_kernel(const int32_t* __restrict__ tok, const float* __restrict__ dx,
+                                 int V, int D, float* __restrict__ dE) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int t = tok[r];
+  if (t < 0 || t >= V) return;
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    atomicAdd(dE + (size_t)t * D + i, dx[(size_t)r * D + i]);
+}
+
+// ------------------------------------------------------------ AdamW
+// cpu_ops.h:266-303, element by element in the same order:
+//   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g
+//   upd = (m / bc1) / (sqrt(v / bc2) + eps) + wd * w;  w -= lr * upd
+// g is the accumulated gradient times gscale (unscale and clip factors).
+__global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v, bf16* __restrict__ w16,
+                             long long n, float lr, float b1, float b2, float eps, float wd,
+                             float inv_bc1, float inv_bc2, float gscale) {
+  pdl_trigger();
+  pdl_wait();
+  const float ob1 = 1.0f - b1, ob2 = 1.0f - b2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float gi = g[i] * gscale;
+    float mi = m[i] * b1;
+    mi = gi * ob1 + mi;
+    float vi = v[i] * b2;
+    vi = (gi * gi) * ob2 + vi;
+    const float mh = mi * inv_bc1;
+    const float vh = sqrtf(vi * inv_bc2) + eps;
+    float upd = mh / vh;
+    upd = w[i] * wd + upd;
+    const float wi = upd * (-lr) + w[i];
+    w[i] = wi;
+    m[i] = mi;
+    v[i] = vi;
+    if (w16) w16[i] = __float2bfloat16_rn(wi);
+  }
+}
+
+// ------------------------------------------------------------ sum of squares
+__global__ void sumsq_kernel(const float* __restrict__ g, long long n, double* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    acc += g[i] * g[i];
+  acc = block_sum256(acc, red);
+  if (threadIdx.x == 0) atomicAdd(out, (double)acc);
+}
+
+// fp32 -> bf16 elementwise copy
+__global__ void f32_to_bf16_kernel(const float* __restrict__ a, bf16* __restrict__ b, long long n) {
+  pdl_trigger();
+  pdl_wait();
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    b[i] = __float2bfloat16_rn(a[i]);
+}
+
+int grid_for(long long n, int threads) {
+  long long g = (n + threads - 1) / threads;
+  const long long cap = (long long)device_num_sms() * 8;
+  return (int)(g < cap ? (g < 1 ? 1 : g) : cap);
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
+                               int D, const float* residual, float* dx, __nv_bfloat16* dx16,
+                               float* dw, cudaStream_t st) {
+  if (D > 1024) return cudaErrorInvalidValue;
+  return launch_k(rmsnorm_bwd_kernel, dim3((M + RB_ROWS - 1) / RB_ROWS), dim3(256), 0, st, dy, x,
+                  w, eps, M, D, residual, dx, dx16, dw);
+}
+
+cudaError_t launch_ce_rows(const float* logits, const int32_t* tgt, int rows, int V, float scale,
+                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st) {
+  return launch_k(ce_rows_kernel, dim3(rows), dim3(1024), 0, st, logits, tgt, V, scale, loss,
+                  dlogits, status);
+}
+
+cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
+                               const float* qkv_raw, const float* qn, const float* kn,
+                               float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
+                               int Hkv, int hd, __nv_bfloat16* dqkv, float* dqn, float* dkn,
+                               cudaStream_t st) {
+  const dim3 grid((M + QRB - 1) / QRB, Hq + 2 * Hkv);
+  if (hd == 128)
+    return launch_k(qk_rope_bwd_kernel<128>, grid, dim3(256), 0, st, dQ, dK, dV, qkv_raw, qn, kn,
+                    qk_eps, rope_cs, M, S, pos0, Hq, Hkv, dqkv, dqn, dkn);
+  if (hd == 64)
+    return launch_k(qk_rope_bwd_kernel<64>, grid, dim3(256), 0, st, dQ, dK, dV, qkv_raw, qn, kn,
+                    qk_eps, rope_cs, M, S, pos0, Hq, Hkv, dqkv, dqn, dkn);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, int D, float* dE,
+                             cudaStream_t st) {
+  return launch_k(embed_bwd_kernel, dim3(M), dim3(256), 0, st, tok, dx, V, D, dE);
+}
+
+cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bfloat16* w16,
+                         long long n, float lr, float b1, float b2, float eps, float wd,
+                         float inv_bc1, float inv_bc2, float gscale, cudaStream_t st) {
+  return launch_k(adamw_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, w, g, m, v, w16, n, lr,
+                  b1, b2, eps, wd, inv_bc1, inv_bc2, gscale);
+}
+
+cudaError_t launch_sumsq(const float* g, long long n, double* out, cudaStream_t st) {
+  return launch_k(sumsq_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, g, n, out);
+}
+
+cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st) {
+  return launch_k(f32_to_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a, b, n);
+}
+
+}  // namespace ne

@@ -175,12 +175,29 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16 with fp32 accumulation, both operands
-// K-major.  ab_fmt: 0 = fp16, 1 = bf16.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int ab_fmt) {
+// Shared-memory matrix descriptor for an MN-major operand tile stored with
+// the 128-byte swizzle: atoms of 64 MN-elements (128 B) x 8 K-rows (1 KB),
+// K-groups of 8 rows 1024 B apart (stride byte offset), 64-element MN chunks
+// `mn_chunk_bytes` apart (leading byte offset).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t mn_chunk_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((mn_chunk_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16 with fp32 accumulation.  ab_fmt: 0 =
+// fp16, 1 = bf16; a_mn / b_mn: operand stored MN-major (bits 15 / 16).
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int ab_fmt, int a_mn = 0,
+                                                      int b_mn = 0) {
   return (1u << 4)                       // D format f32
          | ((uint32_t)ab_fmt << 7)       // A format
          | ((uint32_t)ab_fmt << 10)      // B format
+         | ((uint32_t)a_mn << 15)        // A major (0 = K, 1 = MN)
+         | ((uint32_t)b_mn << 16)        // B major
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }

@@ -14,6 +14,8 @@ enum GemmEpi : int {
   EPI_BF16 = 2,    // bf16, row-major        out[m][n]
   EPI_RESID = 3,   // fp32 residual          x[m][n] += alpha * acc
   EPI_SWIGLU = 4,  // bf16 silu(h1)*h3 from a W1/W3 16-row-interleaved operand
+  EPI_ADD = 5,     // fp32 out[m][n] = in[m][n] + alpha * acc
+  EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and saved h1, h3
 };
 
 struct GemmCall {
@@ -36,6 +38,11 @@ struct GemmCall {
   int ab_fp16 = 0;              // 1: fp16 operands, 0: bf16
   int max_ctas = 0;             // 0 = number of SMs
   int prefetch_a = 0;           // A is not written by the preceding kernel (PDL overlap)
+  int a_mn = 0;                 // A stored MN-major: [K, M] row-major, lda >= M
+  int b_mn = 0;                 // B stored MN-major: [K, N] row-major, ldb >= N
+  int half_out = 0;             // EPI_BF16: write fp16 instead of bf16
+  const void* aux3 = nullptr;   // EPI_ADD: input; EPI_SWIGLU_BWD: h1 (aux1 = h3)
+  long long aux_ld = 0;         // EPI_SWIGLU_BWD: F
 };
 
 // Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).
@@ -50,11 +57,13 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
                                  int rows, cudaStream_t st);
+// q_type: 0 = fp32 q, 1 = fp16 q (with fp16 K/V); kv_bf16: q, K and V all bf16
+// (training path).
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
                             int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
-                            void* q_out, int q_fp16, __half* kc, __half* vc, int Tmax, int* status,
-                            cudaStream_t st);
+                            void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
+                            cudaStream_t st, int kv_bf16 = 0);
 cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
                                 __nv_bfloat16* gate, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
@@ -69,8 +78,37 @@ cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* v
 // ------------------------------------------------------------------ prefill attention
 // q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16
 // [B][Hkv][Tmax][hd] holding positions 0 .. pos0+S-1; out bf16 [B*S][Hq*hd].
+cudaError_t launch_prefill_attn_bf16(const __nv_bfloat16* q, const __nv_bfloat16* kc,
+                                     const __nv_bfloat16* vc, int B, int S, int pos0, int Hq,
+                                     int Hkv, int hd, int Tmax, __nv_bfloat16* out, cudaStream_t st,
+                                     float* lse);
+// lse (optional): log2-domain log-sum-exp per (b, head, row) [B][Hq][S].
 cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half* vc, int B, int S,
                                 int pos0, int Hq, int Hkv, int hd, int Tmax, __nv_bfloat16* out,
-                                cudaStream_t st);
+                                cudaStream_t st, float* lse = nullptr);
+
+// ------------------------------------------------------------------ training
+cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                            const __nv_bfloat16* V, const __nv_bfloat16* O,
+                            const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                            int Hq, int Hkv, int hd, int Tmax, float* dQ, float* dK, float* dV,
+                            cudaStream_t st);
+cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
+                               int D, const float* residual, float* dx, __nv_bfloat16* dx16,
+                               float* dw, cudaStream_t st);
+cudaError_t launch_ce_rows(const float* logits, const int32_t* tgt, int rows, int V, float scale,
+                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st);
+cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
+                               const float* qkv_raw, const float* qn, const float* kn,
+                               float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
+                               int Hkv, int hd, __nv_bfloat16* dqkv, float* dqn, float* dkn,
+                               cudaStream_t st);
+cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, int D, float* dE,
+                             cudaStream_t st);
+cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bfloat16* w16,
+                         long long n, float lr, float b1, float b2, float eps, float wd,
+                         float inv_bc1, float inv_bc2, float gscale, cudaStream_t st);
+cudaError_t launch_sumsq(const float* g, long long n, double* out, cudaStream_t st);
+cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st);
 
 }  // namespace ne

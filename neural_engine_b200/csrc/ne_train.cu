@@ -1,0 +1,582 @@
+// ne_train.cu -- the training step behind the C ABI (forward, backward, AdamW).
+//
+// Device counterpart of the reference's step loop (ane-training/training/
+// training_dynamic/train.m:391-917): per-layer forward with saved activations
+// (train.m:413-488), classifier + cross-entropy (:493-506), backward in
+// reverse layer order (:508-757), then gradient unscale / global-norm clip /
+// AdamW (:782-897).  Every dense contraction runs on the tcgen05 GEMM; the
+// backward's transposed operands are read MN-major straight from the saved
+// token-major activations, so nothing is transposed in memory.
+//
+// Buffers (M = B*S tokens): fp32 masters, gradients, Adam m and v for every
+// trainable tensor in the device layout (Wqkv rows Wq|Wk|Wv, W13 rows
+// interleaved in 16-row blocks); per-layer saved activations
+//   X[l] fp32 [M,D] (layer input), XN[l] bf16, QKVR[l] fp32 [M,qkv],
+//   Q/K/V[l] bf16 (post QK-norm + RoPE), O[l] bf16, LSE[l] fp32 [B,Hq,S],
+//   X2[l] fp32, X2N[l] bf16, H1/H3/GATE[l] bf16 [M,F]
+// and backward scratch.  The tied embedding's gradient collects the LM-head
+// part (dense GEMM) and the gather's scatter-add.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <vector>
+
+#include "../../include/ne.h"
+#include "ne_ctx.h"
+#include "ne_internal.h"
+
+namespace ne {
+
+// One trainable tensor: fp32 master w (device), its gradient / Adam state,
+// optional bf16 compute copy, element count and weight decay.
+struct Seg {
+  float* w;
+  float* g;
+  float* m;
+  float* v;
+  __nv_bfloat16* w16;
+  long long n;
+  float wd;
+};
+
+struct TrainLayerP {
+  float *wqkv, *wo, *w13, *w2;   // fp32 masters (device layout)
+  float *gqkv, *go, *g13, *g2;   // gradients
+  float *g_att, *g_ffn, *g_qn, *g_kn;
+};
+
+struct TrainActs {
+  float *X, *QKVR, *LSE, *X2;
+  __nv_bfloat16 *XN, *Q, *K, *V, *O, *X2N, *H1, *H3, *GATE;
+};
+
+struct TrainState {
+  int B = 0, S = 0, M = 0, Mc = 0;
+  float* pool = nullptr;                 // masters + grads + m + v (fp32)
+  size_t pool_floats = 0;
+  void* act_pool = nullptr;              // saved activations + scratch
+  std::vector<Seg> segs;
+  std::vector<TrainLayerP> P;
+  float *embed_w = nullptr, *embed_g = nullptr, *rmsf_g = nullptr;
+  std::vector<TrainActs> A;
+  float* XL = nullptr;                   // final residual [M, D]
+  __nv_bfloat16* XNF = nullptr;          // final normed [M, D]
+  // backward scratch
+  float *dY = nullptr, *dXF = nullptr, *dX2 = nullptr, *dQ = nullptr, *dK = nullptr,
+        *dV = nullptr, *Dl = nullptr, *logits = nullptr, *loss_rows = nullptr;
+  __nv_bfloat16 *dY16 = nullptr, *dX216 = nullptr, *DH13 = nullptr, *dO = nullptr,
+                *DQKV = nullptr, *dlogits = nullptr;
+  int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
+  double* red = nullptr;                 // [2] sum of squares / loss sum
+  int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
+};
+
+void free_train(ne_ctx* ctx) {
+  if (!ctx || !ctx->train) return;
+  TrainState* t = ctx->train;
+  if (t->pool) cudaFree(t->pool);
+  if (t->act_pool) cudaFree(t->act_pool);
+  delete t;
+  ctx->train = nullptr;
+}
+
+}  // namespace ne
+
+using namespace ne;
+
+namespace {
+
+__global__ void split_tokens_kernel(const int32_t* __restrict__ tok, int B, int S,
+                                    int32_t* __restrict__ ids, int32_t* __restrict__ tgt) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= B * S) return;
+  const int b = r / S, s = r % S;
+  ids[r] = tok[(size_t)b * (S + 1) + s];
+  tgt[r] = tok[(size_t)b * (S + 1) + s + 1];
+}
+
+__global__ void sum_rows_kernel(const float* __restrict__ x, int n, double* __restrict__ out) {
+  double acc = 0.0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    acc += (double)x[i];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(out, acc);
+}
+
+__global__ void mean_from_sum_kernel(const double* s, int n, float* out) { *out = (float)(*s / n); }
+
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ a, float* __restrict__ b,
+                                   long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    b[i] = __bfloat162float(a[i]);
+}
+
+// dst[r, :] = interleave of (W1 row r, W3 row r) blocks: the W13 device layout.
+size_t w13_row(size_t f, bool is_w3) { return (f / 16) * 32 + (is_w3 ? 16 : 0) + f % 16; }
+
+ne_status gemm(ne_ctx* ctx, GemmCall c) {
+  c.splits = 1;
+  cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
+  if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
+  ctx->launches++;
+  return NE_OK;
+}
+
+// C = op(A . B^T) with A [M,K] / B [N,K] K-major (or MN-major when flagged).
+GemmCall gc(const void* A, long long lda, int M, int a_mn, const void* B, long long ldb, int N,
+            int b_mn, int K, int epi, void* out, long long ld, float alpha = 1.f) {
+  GemmCall c;
+  c.A = A; c.lda = lda; c.M = M; c.a_mn = a_mn;
+  c.B = B; c.ldb = ldb; c.N = N; c.b_mn = b_mn;
+  c.K = K; c.epi = epi; c.out = out; c.ld = ld; c.alpha = alpha;
+  c.bn = 256;
+  return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
+  if (!ctx || B <= 0 || S <= 0) return NE_ERR_INVALID;
+  const ne_model_cfg& m = ctx->cfg;
+  const long long M = (long long)B * S;
+  if (M % 64 != 0) return fail(ctx, NE_ERR_UNSUPPORTED, "B*S must be a multiple of 64");
+  if (m.vocab % 64 != 0) return fail(ctx, NE_ERR_UNSUPPORTED, "vocab must be a multiple of 64");
+  if (ctx->layer_set_count != (unsigned)m.n_layers || !ctx->global_set)
+    return fail(ctx, NE_ERR_STATE, "set the weights before ne_train_alloc");
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  if (!ctx->rope_cs || ctx->max_seq < S) {
+    // RoPE table (and decode workspace) sized for S
+    ne_status s = ne_kv_alloc(ctx, 1, std::max(S, ctx->max_seq));
+    if (s != NE_OK) return s;
+  }
+  free_train(ctx);
+  TrainState* t = new TrainState();
+  ctx->train = t;
+  t->B = B;
+  t->S = S;
+  t->M = (int)M;
+  t->Mc = (int)std::min<long long>(M, 2048);
+  const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
+               kvd = (size_t)m.kv_heads * m.head_dim, qkv = qd + 2 * kvd, V = m.vocab,
+               hd = m.head_dim, L = m.n_layers;
+  auto rnd = [](size_t n) { return (n + 63) & ~(size_t)63; };
+  // ---- parameter pool: masters for matrices + embed, grads / m / v for all
+  const size_t mat = qkv * D + D * qd + 2 * F * D + D * F;
+  const size_t gains = 2 * D + (m.qk_norm ? 2 * hd : 0);
+  const size_t per_layer_w = rnd(qkv * D) + rnd(D * qd) + rnd(2 * F * D) + rnd(D * F);
+  const size_t per_layer_all = per_layer_w + 2 * rnd(D) + 2 * rnd(hd);
+  const size_t total_w = L * per_layer_w + rnd(V * D);                     // masters
+  const size_t total_all = L * per_layer_all + rnd(D) + rnd(V * D);        // grads/m/v
+  (void)mat;
+  (void)gains;
+  t->pool_floats = total_w + 3 * total_all;
+  ne_status s;
+  if ((s = dalloc(ctx, &t->pool, t->pool_floats)) != NE_OK) return s;
+  NE_CUDA(cudaMemsetAsync(t->pool, 0, t->pool_floats * 4, ctx->st));
+  float* pw = t->pool;
+  float* pg = t->pool + total_w;
+  float* pm = pg + total_all;
+  float* pv = pm + total_all;
+  size_t ow = 0, oa = 0;
+  auto seg = [&](float* master, __nv_bfloat16* w16, size_t n, float wd) -> Seg {
+    Seg sg;
+    if (master == nullptr) {
+      sg.w = pw + ow;
+      ow += rnd(n);
+    } else {
+      sg.w = master;
+    }
+    sg.g = pg + oa;
+    sg.m = pm + oa;
+    sg.v = pv + oa;
+    oa += rnd(n);
+    sg.w16 = w16;
+    sg.n = (long long)n;
+    sg.wd = wd;
+    return sg;
+  };
+  // weight decay: matrices and the embedding, not the gains (train.m:863-871, 896-897)
+  const float WD = -1.0f;   // placeholder: the configured decay is applied at step time
+  t->P.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    LayerW& w = ctx->L[l];
+    TrainLayerP& p = t->P[l];
+    Seg a = seg(nullptr, w.wqkv, qkv * D, WD);
+    Seg b = seg(nullptr, w.wo, D * qd, WD);
+    Seg c = seg(nullptr, w.w13, 2 * F * D, WD);
+    Seg d = seg(nullptr, w.w2, D * F, WD);
+    Seg e = seg(w.rms_att, nullptr, D, 0.f);
+    Seg f = seg(w.rms_ffn, nullptr, D, 0.f);
+    p.wqkv = a.w; p.gqkv = a.g; p.wo = b.w; p.go = b.g; p.w13 = c.w; p.g13 = c.g;
+    p.w2 = d.w; p.g2 = d.g; p.g_att = e.g; p.g_ffn = f.g;
+    t->segs.insert(t->segs.end(), {a, b, c, d, e, f});
+    if (m.qk_norm) {
+      Seg q = seg(w.q_norm, nullptr, hd, 0.f);
+      Seg k = seg(w.k_norm, nullptr, hd, 0.f);
+      p.g_qn = q.g;
+      p.g_kn = k.g;
+      t->segs.insert(t->segs.end(), {q, k});
+    } else {
+      oa += 2 * rnd(hd);
+      p.g_qn = p.g_kn = nullptr;
+    }
+  }
+  Seg rf = seg(ctx->rms_final, nullptr, D, 0.f);
+  Seg em = seg(nullptr, ctx->embed, V * D, WD);
+  t->rmsf_g = rf.g;
+  t->embed_w = em.w;
+  t->embed_g = em.g;
+  t->segs.push_back(rf);
+  t->segs.push_back(em);
+  // The fp32 masters start as the bf16 compute copies widened (exact when the
+  // host weights were bf16-valued); ne_train_set_masters() loads full fp32
+  // values instead.  Gains are their own masters.
+  for (const Seg& sg : t->segs) {
+    if (sg.w16 == nullptr) continue;
+    const long long n = sg.n;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 8);
+    bf16_to_f32_kernel<<<blocks, 256, 0, ctx->st>>>(sg.w16, sg.w, n);
+    NE_CUDA(cudaGetLastError());
+  }
+  // ---- activations
+  const size_t Mx = (size_t)M;
+  size_t bytes = 0;
+  auto take = [&](size_t nbytes) {
+    const size_t o = bytes;
+    bytes += (nbytes + 255) & ~(size_t)255;
+    return o;
+  };
+  struct Off {
+    size_t X, QKVR, LSE, X2, XN, Q, K, V, O, X2N, H1, H3, GATE;
+  };
+  std::vector<Off> off(L);
+  for (size_t l = 0; l < L; ++l) {
+    Off& o = off[l];
+    o.X = take(Mx * D * 4); o.QKVR = take(Mx * qkv * 4); o.LSE = take(Mx * m.n_heads * 4);
+    o.X2 = take(Mx * D * 4); o.XN = take(Mx * D * 2); o.Q = take(Mx * qd * 2);
+    o.K = take(Mx * kvd * 2); o.V = take(Mx * kvd * 2); o.O = take(Mx * qd * 2);
+    o.X2N = take(Mx * D * 2); o.H1 = take(Mx * F * 2); o.H3 = take(Mx * F * 2);
+    o.GATE = take(Mx * F * 2);
+  }
+  const size_t oXL = take(Mx * D * 4), oXNF = take(Mx * D * 2);
+  const size_t odY = take(Mx * D * 4), odXF = take(Mx * D * 4), odX2 = take(Mx * D * 4);
+  const size_t odQ = take(Mx * qd * 4), odK = take(Mx * kvd * 4), odV = take(Mx * kvd * 4);
+  const size_t oDl = take(Mx * m.n_heads * 4), ologits = take((size_t)t->Mc * V * 4);
+  const size_t oloss = take(Mx * 4), odY16 = take(Mx * D * 2), odX216 = take(Mx * D * 2);
+  const size_t oDH13 = take(Mx * 2 * F * 2), odO = take(Mx * qd * 2), oDQKV = take(Mx * qkv * 2);
+  const size_t odl = take((size_t)t->Mc * V * 2), oids = take(Mx * 4), otgt = take(Mx * 4);
+  const size_t otok = take((size_t)B * (S + 1) * 4), ored = take(64);
+  uint8_t* base = nullptr;
+  if ((s = dalloc(ctx, &base, bytes)) != NE_OK) return s;
+  t->act_pool = base;
+  t->A.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    TrainActs& a = t->A[l];
+    const Off& o = off[l];
+    a.X = (float*)(base + o.X); a.QKVR = (float*)(base + o.QKVR); a.LSE = (float*)(base + o.LSE);
+    a.X2 = (float*)(base + o.X2); a.XN = (__nv_bfloat16*)(base + o.XN);
+    a.Q = (__nv_bfloat16*)(base + o.Q); a.K = (__nv_bfloat16*)(base + o.K);
+    a.V = (__nv_bfloat16*)(base + o.V); a.O = (__nv_bfloat16*)(base + o.O);
+    a.X2N = (__nv_bfloat16*)(base + o.X2N); a.H1 = (__nv_bfloat16*)(base + o.H1);
+    a.H3 = (__nv_bfloat16*)(base + o.H3); a.GATE = (__nv_bfloat16*)(base + o.GATE);
+  }
+  t->XL = (float*)(base + oXL); t->XNF = (__nv_bfloat16*)(base + oXNF);
+  t->dY = (float*)(base + odY); t->dXF = (float*)(base + odXF); t->dX2 = (float*)(base + odX2);
+  t->dQ = (float*)(base + odQ); t->dK = (float*)(base + odK); t->dV = (float*)(base + odV);
+  t->Dl = (float*)(base + oDl); t->logits = (float*)(base + ologits);
+  t->loss_rows = (float*)(base + oloss); t->dY16 = (__nv_bfloat16*)(base + odY16);
+  t->dX216 = (__nv_bfloat16*)(base + odX216); t->DH13 = (__nv_bfloat16*)(base + oDH13);
+  t->dO = (__nv_bfloat16*)(base + odO); t->DQKV = (__nv_bfloat16*)(base + oDQKV);
+  t->dlogits = (__nv_bfloat16*)(base + odl); t->ids = (int32_t*)(base + oids);
+  t->tgt = (int32_t*)(base + otgt); t->tok = (int32_t*)(base + otok);
+  t->red = (double*)(base + ored);
+  return ne_sync(ctx);
+}
+
+// Overwrite the fp32 masters from host fp32 tensors (v4 layout), e.g. a
+// checkpoint's exact values; also refreshes the bf16 compute copies.
+NE_API ne_status ne_train_set_masters(ne_ctx* ctx, int layer, const float* h_wq, const float* h_wk,
+                                      const float* h_wv, const float* h_wo, const float* h_w1,
+                                      const float* h_w2, const float* h_w3) {
+  if (!ctx || !ctx->train) return NE_ERR_STATE;
+  const ne_model_cfg& m = ctx->cfg;
+  TrainState* t = ctx->train;
+  if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
+               kvd = (size_t)m.kv_heads * m.head_dim;
+  if (layer == -1) {   // h_wq = embedding [V, D]
+    NE_CUDA(cudaMemcpy(t->embed_w, h_wq, (size_t)m.vocab * D * 4, cudaMemcpyHostToDevice));
+    NE_CUDA(cudaStreamSynchronize(ctx->st));
+    return NE_OK;
+  }
+  TrainLayerP& p = t->P[layer];
+  NE_CUDA(cudaMemcpy(p.wqkv, h_wq, qd * D * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(p.wqkv + qd * D, h_wk, kvd * D * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(p.wqkv + (qd + kvd) * D, h_wv, kvd * D * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(p.wo, h_wo, D * qd * 4, cudaMemcpyHostToDevice));
+  std::vector<float> w13(2 * F * D);
+  for (size_t f = 0; f < F; ++f) {
+    std::memcpy(&w13[w13_row(f, false) * D], h_w1 + f * D, D * 4);
+    std::memcpy(&w13[w13_row(f, true) * D], h_w3 + f * D, D * 4);
+  }
+  NE_CUDA(cudaMemcpy(p.w13, w13.data(), 2 * F * D * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(p.w2, h_w2, D * F * 4, cudaMemcpyHostToDevice));
+  return NE_OK;
+}
+
+// Refresh every bf16 compute copy from the fp32 masters.
+NE_API ne_status ne_train_sync_weights(ne_ctx* ctx) {
+  if (!ctx || !ctx->train) return NE_ERR_STATE;
+  for (const Seg& sg : ctx->train->segs)
+    if (sg.w16) NE_LAUNCH(launch_f32_to_bf16(sg.w, sg.w16, sg.n, ctx->st));
+  return ne_sync(ctx);
+}
+
+NE_API ne_status ne_train_zero_grads(ne_ctx* ctx) {
+  if (!ctx || !ctx->train) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  for (const Seg& s : t->segs) NE_CUDA(cudaMemsetAsync(s.g, 0, s.n * 4, ctx->st));
+  t->micro_steps = 0;
+  return NE_OK;
+}
+
+// Forward + backward of one batch d_tokens [B, S+1] (inputs tokens[:, :S],
+// targets tokens[:, 1:]); gradients ACCUMULATE into the gradient buffers
+// (mean cross-entropy over the B*S targets of this batch).  *d_loss (device,
+// optional) receives the batch's mean loss.
+NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
+  if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  const ne_model_cfg& m = ctx->cfg;
+  const int B = t->B, S = t->S, M = t->M, D = m.dim, F = m.hidden, Hq = m.n_heads,
+            Hkv = m.kv_heads, hd = m.head_dim, V = m.vocab;
+  const int qd = Hq * hd, kvd = Hkv * hd, qkv = qd + 2 * kvd;
+  const float alpha = m.res_alpha;
+  cudaStream_t st = ctx->st;
+  ne_status s;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  split_tokens_kernel<<<(M + 255) / 256, 256, 0, st>>>(d_tokens, B, S, t->ids, t->tgt);
+  NE_CUDA(cudaGetLastError());
+
+  // ------------------------------------------------ forward
+  NE_LAUNCH(launch_embed_rmsnorm(t->ids, t->embed_w, 1, V, D, ctx->L[0].rms_att, m.rms_eps,
+                                 t->A[0].X, t->A[0].XN, M, ctx->d_status, st));
+  for (int l = 0; l < m.n_layers; ++l) {
+    const LayerW& w = ctx->L[l];
+    TrainActs& a = t->A[l];
+    if ((s = gemm(ctx, gc(a.XN, D, M, 0, w.wqkv, D, qkv, 0, D, EPI_F32, a.QKVR, qkv))) != NE_OK)
+      return s;
+    NE_LAUNCH(launch_qkv_post(a.QKVR, 1, 0, M, S, nullptr, 0, Hq, Hkv, hd,
+                              m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
+                              m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
+    NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
+    GemmCall c = gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_ADD, a.X2, D, alpha);
+    c.aux3 = a.X;
+    if ((s = gemm(ctx, c)) != NE_OK) return s;
+    NE_LAUNCH(launch_resid_rmsnorm(a.X2, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, a.X2N, M, st));
+    c = gc(a.X2N, D, M, 0, w.w13, D, 2 * F, 0, D, EPI_SWIGLU, a.GATE, F);
+    c.aux1 = a.H1;
+    c.aux2 = a.H3;
+    if ((s = gemm(ctx, c)) != NE_OK) return s;
+    float* xnext = (l + 1 < m.n_layers) ? t->A[l + 1].X : t->XL;
+    c = gc(a.GATE, F, M, 0, w.w2, F, D, 0, F, EPI_ADD, xnext, D, alpha);
+    c.aux3 = a.X2;
+    if ((s = gemm(ctx, c)) != NE_OK) return s;
+    const float* g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
+    __nv_bfloat16* xn = (l + 1 < m.n_layers) ? t->A[l + 1].XN : t->XNF;
+    NE_LAUNCH(launch_resid_rmsnorm(xnext, nullptr, 0, 0, 1.f, D, g, m.rms_eps, xn, M, st));
+  }
+  // ------------------------------------------------ classifier + cross-entropy
+  const float ce_scale = 1.0f / (float)M;
+  for (int r0 = 0; r0 < M; r0 += t->Mc) {
+    const int rows = std::min(t->Mc, M - r0);
+    const __nv_bfloat16* xnf = t->XNF + (size_t)r0 * D;
+    if ((s = gemm(ctx, gc(xnf, D, rows, 0, ctx->embed, D, V, 0, D, EPI_F32, t->logits, V))) !=
+        NE_OK)
+      return s;
+    NE_LAUNCH(launch_ce_rows(t->logits, t->tgt + r0, rows, V, ce_scale, t->loss_rows + r0,
+                             t->dlogits, ctx->d_status, st));
+    // dXNF = dlogits . E   (E read MN-major as [V (K), D (N)])
+    if ((s = gemm(ctx, gc(t->dlogits, V, rows, 0, ctx->embed, D, D, 1, V, EPI_F32,
+                          t->dXF + (size_t)r0 * D, D))) != NE_OK)
+      return s;
+    // dE += dlogits^T . XNF   (both MN-major)
+    if ((s = gemm(ctx, gc(t->dlogits, V, V, 1, xnf, D, D, 1, rows, EPI_RESID, t->embed_g, D))) !=
+        NE_OK)
+      return s;
+  }
+  // ------------------------------------------------ backward
+  NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, t->XL, ctx->rms_final, m.rms_eps, M, D, nullptr, t->dY,
+                               t->dY16, t->rmsf_g, st));
+  for (int l = m.n_layers - 1; l >= 0; --l) {
+    const LayerW& w = ctx->L[l];
+    const TrainActs& a = t->A[l];
+    const TrainLayerP& p = t->P[l];
+    // FFN: d_gate -> (dh1, dh3) via the SwiGLU-backward epilogue
+    GemmCall c = gc(t->dY16, D, M, 0, w.w2, F, F, 1, D, EPI_SWIGLU_BWD, t->DH13, 2 * F, alpha);
+    c.aux3 = a.H1;
+    c.aux1 = a.H3;
+    c.aux_ld = F;
+    if ((s = gemm(ctx, c)) != NE_OK) return s;
+    if ((s = gemm(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F, alpha))) != NE_OK)
+      return s;
+    if ((s = gemm(ctx, gc(t->DH13, 2 * F, 2 * F, 1, a.X2N, D, D, 1, M, EPI_RESID, p.g13, D))) !=
+        NE_OK)
+      return s;
+    if ((s = gemm(ctx, gc(t->DH13, 2 * F, M, 0, w.w13, D, D, 1, 2 * F, EPI_F32, t->dXF, D))) !=
+        NE_OK)
+      return s;
+    NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X2, w.rms_ffn, m.rms_eps, M, D, t->dY, t->dX2,
+                                 t->dX216, p.g_ffn, st));
+    // attention
+    c = gc(t->dX216, D, M, 0, w.wo, qd, qd, 1, D, EPI_BF16, t->dO, qd, alpha);
+    if ((s = gemm(ctx, c)) != NE_OK) return s;
+    if ((s = gemm(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd, alpha))) !=
+        NE_OK)
+      return s;
+    NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, t->dQ,
+                              t->dK, t->dV, st));
+    ctx->launches += 2;
+    NE_LAUNCH(launch_qk_rope_bwd(t->dQ, t->dK, t->dV, a.QKVR, m.qk_norm ? w.q_norm : nullptr,
+                                 m.qk_norm ? w.k_norm : nullptr, m.qk_eps, ctx->rope_cs, M, S, 0,
+                                 Hq, Hkv, hd, t->DQKV, p.g_qn, p.g_kn, st));
+    if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
+      return s;
+    if ((s = gemm(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D))) != NE_OK)
+      return s;
+    NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X, w.rms_att, m.rms_eps, M, D, t->dX2, t->dY, t->dY16,
+                                 p.g_att, st));
+  }
+  NE_LAUNCH(launch_embed_bwd(t->ids, t->dY, M, V, D, t->embed_g, st));
+  if (d_loss) {
+    NE_CUDA(cudaMemsetAsync(t->red + 1, 0, sizeof(double), st));
+    sum_rows_kernel<<<64, 256, 0, st>>>(t->loss_rows, M, t->red + 1);
+    NE_CUDA(cudaGetLastError());
+    // d_loss = sum / M  (a 1-thread kernel keeps it on the device)
+    mean_from_sum_kernel<<<1, 1, 0, st>>>(t->red + 1, M, d_loss);
+    NE_CUDA(cudaGetLastError());
+  }
+  t->micro_steps++;
+  return NE_OK;
+}
+
+NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss) {
+  if (!ctx || !ctx->train || !h_tokens) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaMemcpyAsync(t->tok, h_tokens, (size_t)t->B * (t->S + 1) * 4, cudaMemcpyHostToDevice,
+                          ctx->st));
+  float* d_loss = reinterpret_cast<float*>(t->red + 2);
+  ne_status s = ne_train_fwd_bwd_device(ctx, t->tok, h_loss ? d_loss : nullptr);
+  if (s != NE_OK) return s;
+  if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
+  return ne_sync(ctx);
+}
+
+// Global L2 norm of the accumulated gradients times grad_scale (train.m:805-826).
+NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm) {
+  if (!ctx || !ctx->train || !h_norm) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaMemsetAsync(t->red, 0, sizeof(double), ctx->st));
+  for (const Seg& sg : t->segs) NE_LAUNCH(launch_sumsq(sg.g, sg.n, t->red, ctx->st));
+  double ss = 0;
+  NE_CUDA(cudaMemcpyAsync(&ss, t->red, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+  ne_status s = ne_sync(ctx);
+  if (s != NE_OK) return s;
+  *h_norm = (float)(std::sqrt(ss) * grad_scale);
+  return NE_OK;
+}
+
+// AdamW over every trainable tensor (train.m:782-897, cpu_ops.h:266-303):
+// gradients are multiplied by cfg->grad_scale (1/accum in the reference), the
+// global norm of the result is clipped to cfg->grad_clip (when > 0), then
+// decoupled AdamW with bias correction at step t (1-based); weight decay on
+// matrices and the embedding, none on the gains.  Gradients are zeroed
+// afterwards.  *h_grad_norm (optional) receives the pre-clip norm.
+NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, float* h_grad_norm) {
+  if (!ctx || !ctx->train || !cfg || t_step <= 0) return NE_ERR_INVALID;
+  TrainState* t = ctx->train;
+  float norm = 0.f;
+  ne_status s = ne_train_grad_norm(ctx, cfg->grad_scale, &norm);
+  if (s != NE_OK) return s;
+  if (h_grad_norm) *h_grad_norm = norm;
+  float gscale = cfg->grad_scale;
+  if (cfg->grad_clip > 0.f && norm > cfg->grad_clip) gscale *= cfg->grad_clip / norm;
+  const float bc1 = 1.0f - std::pow(cfg->beta1, (float)t_step);
+  const float bc2 = 1.0f - std::pow(cfg->beta2, (float)t_step);
+  for (const Seg& sg : t->segs) {
+    const float wd = sg.wd < 0.f ? cfg->weight_decay : 0.f;
+    NE_LAUNCH(launch_adamw(sg.w, sg.g, sg.m, sg.v, sg.w16, sg.n, cfg->lr, cfg->beta1, cfg->beta2,
+                           cfg->eps, wd, 1.0f / bc1, 1.0f / bc2, gscale, ctx->st));
+  }
+  return ne_train_zero_grads(ctx);
+}
+
+// Learning-rate schedule of train.m:851-858: linear warmup, then cosine decay
+// to min_lr_frac * max_lr.
+NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_steps,
+                            float min_lr_frac) {
+  if (step < warmup_steps) return max_lr * ((float)(step + 1)) / warmup_steps;
+  const float decay_ratio = (float)(step - warmup_steps) / (float)(total_steps - warmup_steps);
+  const float min_lr = max_lr * min_lr_frac;
+  return min_lr + 0.5f * (1.0f + cosf(3.14159265358979323846f * decay_ratio)) * (max_lr - min_lr);
+}
+
+// Copy one layer's gradients (which = 0) or fp32 master weights (which = 1)
+// to host buffers in the v4 layout; layer -1 = (rms_final, embed) into
+// (h_rms_att, h_wq).  Any pointer may be NULL.
+NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_wq, float* h_wk,
+                                    float* h_wv, float* h_wo, float* h_w1, float* h_w2,
+                                    float* h_w3, float* h_rms_att, float* h_rms_ffn,
+                                    float* h_q_norm, float* h_k_norm) {
+  if (!ctx || !ctx->train || which < 0 || which > 1) return NE_ERR_INVALID;
+  TrainState* t = ctx->train;
+  const ne_model_cfg& m = ctx->cfg;
+  if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
+               kvd = (size_t)m.kv_heads * m.head_dim, hd = m.head_dim;
+  auto get = [&](float* dst, const float* src, size_t n) -> ne_status {
+    if (dst) NE_CUDA(cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost));
+    return NE_OK;
+  };
+  ne_status s;
+  if (layer == -1) {
+    if ((s = get(h_rms_att, which ? ctx->rms_final : t->rmsf_g, D))) return s;
+    return get(h_wq, which ? t->embed_w : t->embed_g, (size_t)m.vocab * D);
+  }
+  const TrainLayerP& p = t->P[layer];
+  const LayerW& w = ctx->L[layer];
+  const float* qkv = which ? p.wqkv : p.gqkv;
+  if ((s = get(h_wq, qkv, qd * D)) || (s = get(h_wk, qkv + qd * D, kvd * D)) ||
+      (s = get(h_wv, qkv + (qd + kvd) * D, kvd * D)) || (s = get(h_wo, which ? p.wo : p.go, D * qd)) ||
+      (s = get(h_w2, which ? p.w2 : p.g2, D * F)) ||
+      (s = get(h_rms_att, which ? w.rms_att : p.g_att, D)) ||
+      (s = get(h_rms_ffn, which ? w.rms_ffn : p.g_ffn, D)))
+    return s;
+  if (m.qk_norm) {
+    if ((s = get(h_q_norm, which ? w.q_norm : p.g_qn, hd)) ||
+        (s = get(h_k_norm, which ? w.k_norm : p.g_kn, hd)))
+      return s;
+  }
+  if (h_w1 || h_w3) {
+    std::vector<float> w13(2 * F * D);
+    NE_CUDA(cudaMemcpy(w13.data(), which ? p.w13 : p.g13, 2 * F * D * 4, cudaMemcpyDeviceToHost));
+    for (size_t f = 0; f < F; ++f) {
+      if (h_w1) std::memcpy(h_w1 + f * D, &w13[w13_row(f, false) * D], D * 4);
+      if (h_w3) std::memcpy(h_w3 + f * D, &w13[w13_row(f, true) * D], D * 4);
+    }
+  }
+  return NE_OK;
+}
+
+}  // extern "C"

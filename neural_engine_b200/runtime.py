@@ -27,7 +27,10 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_kv_alloc", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
             "ne_decode_loop_device", "ne_gemm_device", "ne_gemm_device_ex",
             "ne_decode_kernels_per_step", "ne_get_stream", "ne_profile_decode_step",
-            "ne_gemm_splitk_noalloc")
+            "ne_gemm_splitk_noalloc", "ne_train_alloc", "ne_train_set_masters",
+            "ne_train_sync_weights", "ne_train_zero_grads", "ne_train_fwd_bwd_device",
+            "ne_train_fwd_bwd", "ne_train_grad_norm", "ne_adamw_step", "ne_lr_schedule",
+            "ne_train_get_layer", "ne_gemm")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -52,6 +55,20 @@ class CkptInfoC(C.Structure):
                 ("cum_compile", C.c_double), ("cum_train", C.c_double),
                 ("cum_wall", C.c_double), ("cum_steps", C.c_int), ("cum_batches", C.c_int),
                 ("has_qk_norm", C.c_int)]
+
+
+class GemmDescC(C.Structure):
+    _fields_ = [("a", C.c_void_p), ("lda", C.c_longlong), ("a_mn", C.c_int),
+                ("b", C.c_void_p), ("ldb", C.c_longlong), ("b_mn", C.c_int),
+                ("M", C.c_int), ("N", C.c_int), ("K", C.c_int), ("epi", C.c_int),
+                ("out", C.c_void_p), ("ld", C.c_longlong), ("alpha", C.c_float),
+                ("aux0", C.c_void_p), ("aux1", C.c_void_p), ("aux_ld", C.c_longlong),
+                ("bn", C.c_int), ("half_out", C.c_int)]
+
+
+class AdamCfgC(C.Structure):
+    _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
+                ("weight_decay", C.c_float), ("grad_clip", C.c_float), ("grad_scale", C.c_float)]
 
 
 @dataclass(frozen=True)
@@ -132,6 +149,18 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_get_stream.argtypes = [P]
     lib.ne_get_stream.restype = P
     lib.ne_profile_decode_step.argtypes = [P, I, I, C.POINTER(C.c_float)]
+    lib.ne_gemm.argtypes = [P, C.POINTER(GemmDescC)]
+    lib.ne_train_alloc.argtypes = [P, I, I]
+    lib.ne_train_set_masters.argtypes = [P, I] + [P] * 7
+    lib.ne_train_sync_weights.argtypes = [P]
+    lib.ne_train_zero_grads.argtypes = [P]
+    lib.ne_train_fwd_bwd_device.argtypes = [P, P, P]
+    lib.ne_train_fwd_bwd.argtypes = [P, P, C.POINTER(C.c_float)]
+    lib.ne_train_grad_norm.argtypes = [P, F, C.POINTER(C.c_float)]
+    lib.ne_adamw_step.argtypes = [P, C.POINTER(AdamCfgC), I, C.POINTER(C.c_float)]
+    lib.ne_lr_schedule.argtypes = [I, F, I, I, F]
+    lib.ne_lr_schedule.restype = F
+    lib.ne_train_get_layer.argtypes = [P, I, I] + [P] * 11
     _lib = lib
     return lib
 
@@ -242,6 +271,86 @@ class Engine:
                                                ldb, N, K, epi, C.c_void_p(d_out), ld, alpha, bn,
                                                splits, split_stride, C.byref(used)))
         return used.value
+
+    def gemm(self, a: int, lda: int, M: int, b: int, ldb: int, N: int, K: int, epi: int, out: int,
+             ld: int, alpha: float = 1.0, a_mn: int = 0, b_mn: int = 0, aux0: int = 0,
+             aux1: int = 0, aux_ld: int = 0, bn: int = 0, half_out: int = 0):
+        d = GemmDescC(a, lda, a_mn, b, ldb, b_mn, M, N, K, epi, out, ld, alpha, aux0 or None,
+                      aux1 or None, aux_ld, bn, half_out)
+        self._check(self.lib.ne_gemm(self._ctx, C.byref(d)))
+
+    # -- training (train.m step loop)
+    def train_alloc(self, B: int, S: int):
+        self._check(self.lib.ne_train_alloc(self._ctx, int(B), int(S)))
+        self.train_B, self.train_S = int(B), int(S)
+
+    def train_set_masters(self, layers, embed):
+        """Exact fp32 masters (the weights set earlier were stored as bf16)."""
+        f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+        for l, lw in enumerate(layers):
+            t = [f32(lw[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")]
+            self._check(self.lib.ne_train_set_masters(self._ctx, l, *[_ptr(a) for a in t]))
+        e = f32(embed)
+        self._check(self.lib.ne_train_set_masters(self._ctx, -1, _ptr(e), *([None] * 6)))
+        self._check(self.lib.ne_train_sync_weights(self._ctx))
+
+    def train_fwd_bwd(self, tokens: np.ndarray) -> float:
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        assert tokens.shape == (self.train_B, self.train_S + 1), tokens.shape
+        loss = C.c_float(0)
+        self._check(self.lib.ne_train_fwd_bwd(self._ctx, _ptr(tokens), C.byref(loss)))
+        return float(loss.value)
+
+    def train_fwd_bwd_device(self, d_tokens: int, d_loss: int | None = None):
+        self._check(self.lib.ne_train_fwd_bwd_device(self._ctx, C.c_void_p(d_tokens),
+                                                     C.c_void_p(d_loss) if d_loss else None))
+
+    def zero_grads(self):
+        self._check(self.lib.ne_train_zero_grads(self._ctx))
+
+    def grad_norm(self, grad_scale: float = 1.0) -> float:
+        out = C.c_float(0)
+        self._check(self.lib.ne_train_grad_norm(self._ctx, grad_scale, C.byref(out)))
+        return float(out.value)
+
+    def adamw_step(self, t: int, lr: float, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                   grad_clip=1.0, grad_scale=1.0) -> float:
+        cfg = AdamCfgC(lr, beta1, beta2, eps, weight_decay, grad_clip, grad_scale)
+        norm = C.c_float(0)
+        self._check(self.lib.ne_adamw_step(self._ctx, C.byref(cfg), int(t), C.byref(norm)))
+        return float(norm.value)
+
+    def lr_schedule(self, step, max_lr, warmup, total, min_frac=0.1) -> float:
+        return float(self.lib.ne_lr_schedule(step, max_lr, warmup, total, min_frac))
+
+    def _train_tensors(self, which: int):
+        c = self.cfg
+        D, F, qd, kvd = c.dim, c.hidden, c.q_dim, c.kv_dim
+        layers, qk = [], []
+        for l in range(c.n_layers):
+            t = {"Wq": np.zeros((qd, D), np.float32), "Wk": np.zeros((kvd, D), np.float32),
+                 "Wv": np.zeros((kvd, D), np.float32), "Wo": np.zeros((D, qd), np.float32),
+                 "W1": np.zeros((F, D), np.float32), "W2": np.zeros((D, F), np.float32),
+                 "W3": np.zeros((F, D), np.float32), "rms_att": np.zeros(D, np.float32),
+                 "rms_ffn": np.zeros(D, np.float32)}
+            qn, kn = np.zeros(c.head_dim, np.float32), np.zeros(c.head_dim, np.float32)
+            order = ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3", "rms_att", "rms_ffn")
+            self._check(self.lib.ne_train_get_layer(self._ctx, l, which, *[_ptr(t[k]) for k in order],
+                                                    _ptr(qn), _ptr(kn)))
+            layers.append(t)
+            qk.append((qn, kn))
+        rf = np.zeros(D, np.float32)
+        emb = np.zeros((c.vocab, D), np.float32)
+        self._check(self.lib.ne_train_get_layer(self._ctx, -1, which, _ptr(emb), None, None, None,
+                                                None, None, None, _ptr(rf), None, None, None))
+        return {"layers": layers, "rms_final": rf, "embed": emb,
+                "qk": qk if c.qk_norm else None}
+
+    def get_grads(self) -> dict:
+        return self._train_tensors(0)
+
+    def get_masters(self) -> dict:
+        return self._train_tensors(1)
 
     @property
     def stream_ptr(self) -> int:

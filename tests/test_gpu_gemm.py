@@ -149,3 +149,59 @@ def test_gemm_split_k_slabs(eng, splits):
     o = out.sum(0).cpu().double().T
     err = (o - _ref(a, b)).abs().max().item()
     assert err <= _tol(a, b, K), err
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("M,N,K", [(256, 384, 256), (320, 200, 128), (1024, 64, 512)])
+def test_gemm_mn_major_b(eng, bn, M, N, K):
+    """dX-style product: B read MN-major from a [K, N] row-major matrix."""
+    a, bt = _bf16((M, K), 21), _bf16((K, N), 22, 0.1)      # bt = B^T stored [K, N]
+    da, db = a.cuda(), bt.cuda()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    eng.gemm(da.data_ptr(), K, M, db.data_ptr(), N, N, K, 1, out.data_ptr(), N, b_mn=1, bn=bn)
+    eng.sync()
+    ref = a.double() @ bt.double()
+    err = (out.cpu().double() - ref).abs().max().item()
+    assert err <= _tol(a, bt, K), err
+
+
+@pytest.mark.parametrize("bn", [64, 256])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 192, 320), (1024, 128, 2048)])
+def test_gemm_mn_major_both(eng, bn, M, N, K):
+    """dW-style product: A [K, M] and B [K, N] both read MN-major (token-major
+    activations), accumulated into fp32 (epi 3)."""
+    at, bt = _bf16((K, M), 23, 0.1), _bf16((K, N), 24, 0.1)
+    da, db = at.cuda(), bt.cuda()
+    x0 = torch.randn(M, N)
+    out = x0.clone().cuda()
+    eng.gemm(da.data_ptr(), M, M, db.data_ptr(), N, N, K, 3, out.data_ptr(), N, alpha=0.5,
+             a_mn=1, b_mn=1, bn=bn)
+    eng.sync()
+    ref = x0.double() + 0.5 * (at.double().T @ bt.double())
+    err = (out.cpu().double() - ref).abs().max().item()
+    assert err <= _tol(at, bt, K), err
+
+
+def test_gemm_swiglu_backward_epilogue(eng):
+    """d_gate = dY . W2 (W2 read MN-major) with the SwiGLU-backward epilogue."""
+    M, F, D = 192, 256, 128
+    dy = _bf16((M, D), 25)
+    w2 = _bf16((D, F), 26, 0.1)          # W2 [D, F]: MN-major B for d_gate = dY W2
+    h1, h3 = _bf16((M, F), 27), _bf16((M, F), 28)
+    ddy, dw2, dh1, dh3 = dy.cuda(), w2.cuda(), h1.cuda(), h3.cuda()
+    out = torch.zeros((M, 2 * F), dtype=torch.bfloat16, device="cuda")
+    eng.gemm(ddy.data_ptr(), D, M, dw2.data_ptr(), F, F, D, 6, out.data_ptr(), 2 * F, alpha=0.7,
+             b_mn=1, aux0=dh1.data_ptr(), aux1=dh3.data_ptr(), aux_ld=F)
+    eng.sync()
+    dg = 0.7 * (dy.double() @ w2.double())
+    x1, x3 = h1.double(), h3.double()
+    s = torch.sigmoid(x1)
+    r1 = dg * x3 * s * (1 + x1 * (1 - s))
+    r3 = dg * x1 * s
+    o = out.cpu().double()
+    idx = torch.arange(F)
+    c1 = (idx // 16) * 32 + idx % 16
+    got1, got3 = o[:, c1], o[:, c1 + 16]
+    tol = 2 ** -7 * max(r1.abs().max().item(), r3.abs().max().item()) + 1e-3
+    assert (got1 - r1).abs().max().item() <= tol
+    assert (got3 - r3).abs().max().item() <= tol
