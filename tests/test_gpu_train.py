@@ -76,7 +76,8 @@ def test_loss_and_grads_match_float64(kw, B, S):
     loss = e.train_fwd_bwd(tok)
     ref_loss, g_ref = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok)
     assert abs(loss - ref_loss) <= LOSS_REL * ref_loss, (loss, ref_loss)
-    _compare_grads(cfg, e.get_grads(), g_ref)
+    worst = _compare_grads(cfg, e.get_grads(), g_ref)
+    print(f"loss {loss:.6f} ref {ref_loss:.6f}; worst grad rel-L2 {worst[1]:.3e} ({worst[0]})")
     e.close()
 
 
@@ -113,7 +114,8 @@ def test_adamw_step_matches_reference_update(clip):
     grads = e.get_grads()
     before = e.get_masters()
     lr = e.lr_schedule(3, 3e-4, 10, 100)
-    assert abs(lr - ot.lr_schedule(3, 3e-4, 10, 100)) < 1e-12
+    # the schedule is evaluated in float32, as train.m:851-858 does
+    assert abs(lr - ot.lr_schedule(3, 3e-4, 10, 100)) <= 1e-6 * lr
     norm = e.adamw_step(1, lr, grad_clip=clip, grad_scale=0.5)
     after = e.get_masters()
     state = ot.init_state(before)
@@ -160,5 +162,6 @@ def test_full_width_two_layers(name):
     loss = e.train_fwd_bwd(tok)
     ref_loss, g_ref = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok)
     assert abs(loss - ref_loss) <= LOSS_REL * ref_loss, (loss, ref_loss)
-    _compare_grads(cfg, e.get_grads(), g_ref)
+    worst = _compare_grads(cfg, e.get_grads(), g_ref)
+    print(f"{name}: loss {loss:.6f} ref {ref_loss:.6f}; worst grad rel-L2 {worst[1]:.3e} ({worst[0]})")
     e.close()
