@@ -37,6 +37,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "Qwen3-0.6B decode tokens/sec (greedy, 512-token prompt, 256 new tokens)"
+TRAIN_METRIC = "Qwen3-0.6B training tokens/sec (fwd + bwd + AdamW, seq 256, batch 16 per GPU)"
 UNIT = "tokens/s"
 
 # Qwen3-0.6B sizes used by the byte model (SURVEY-style algorithmic counts)
@@ -55,6 +56,9 @@ def parse():
     ap.add_argument("--gen", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
+    ap.add_argument("--train-seq", type=int, default=256)
     return ap.parse_args()
 
 
@@ -71,6 +75,22 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Sustained dense bf16 TFLOP/s (a kernel timed inside a long step)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
+def train_flops_per_token(S: int) -> float:
+    """3 x forward: 2 x 596.0 M params + causal attention 2*L*Hq*hd*(S+1)."""
+    return 3.0 * (2.0 * PARAMS + 2.0 * L * HQ * HD * (S + 1))
 
 
 # ----------------------------------------------------------------- clocks
@@ -224,6 +244,110 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- training
+def cpu_train_sample(layers, rf, emb, qk, S=64):
+    """torch-CPU float32 fwd + bwd of one sequence of S tokens (the oracle's
+    restatement of the training forward), all host cores.  Returns tokens/s."""
+    import torch
+    from oracle import model as om
+    from oracle import train as ot
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = om.QWEN3_06B
+    tok = np.random.default_rng(7).integers(0, cfg.vocab, size=(1, S + 1))
+    t0 = time.perf_counter()
+    ot.loss_and_grads(cfg, layers, rf, emb, qk, tok, dtype="float32")
+    dt = time.perf_counter() - t0
+    return S / dt, dt
+
+
+def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
+    """Data-parallel training steps of BASELINE config 4 (S 256, B 16 per GPU)."""
+    import torch
+    import torch.distributed as dist
+    import neural_engine_b200 as ne
+    cfg = ne.QWEN3_06B
+    B, S = args.train_batch, args.train_seq
+    eng = ne.Engine(cfg, device=local)
+    eng.set_weights(layers, rf, emb, qk)
+    eng.train_alloc(B, S)
+    stream = torch.cuda.ExternalStream(eng.stream_ptr)
+    gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    tok = torch.randint(0, cfg.vocab, (B, S + 1), generator=gen, device="cuda", dtype=torch.int32)
+    grads = eng.grad_pool_tensor() if world > 1 else None
+    tstep = [0]
+
+    def step():
+        eng.train_fwd_bwd_device(tok.data_ptr())
+        if world > 1:
+            with torch.cuda.stream(stream):        # NCCL ordered after the backward kernels
+                dist.all_reduce(grads, op=dist.ReduceOp.SUM)
+        tstep[0] += 1
+        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world)
+
+    for _ in range(args.warmup):
+        step()
+    eng.sync()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    t_ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([t_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    ms_step = t_ms / args.steps
+    value = world * B * S * args.steps / (t_ms / 1000.0)
+    peak, kind = tensor_peak()
+    ach = train_flops_per_token(S) * B * S / (ms_step / 1000.0) / 1e12
+    # e2e through the host-buffer call: tokens H2D, fwd+bwd, loss D2H, AdamW
+    h_tok = tok.cpu().numpy()
+    barrier()
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        eng.train_fwd_bwd(h_tok)
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(grads, op=dist.ReduceOp.SUM)
+        tstep[0] += 1
+        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world)
+    te = (time.perf_counter() - t0) / reps
+    if world > 1:
+        tt = torch.tensor([te], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+    eng.close()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt = cpu_train_sample(layers, rf, emb, qk)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+               "sample": f"torch-CPU float32 fwd+bwd of the oracle's Qwen3-0.6B forward, 1 x 64 "
+                         f"tokens ({dt:.1f} s)"}
+    return {"metric": TRAIN_METRIC, "value": round(value, 1), "unit": UNIT,
+            "ms_per_step": round(ms_step, 3), "steps": args.steps, "warmup": args.warmup,
+            "scaling": "weak", "dtype": "bf16",
+            "config": {"workload": "qwen3_06b_train", "batch_per_gpu": B, "seq_len": S,
+                       "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
+                       "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
+                       "parallelism": f"dp{world} (NCCL all-reduce of the gradient pool)"},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_kind": kind,
+                         "flops_per_token": train_flops_per_token(S), "scope": "whole step"},
+            "clocks": clk,
+            "e2e": {"value": round(world * B * S / te, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": B * (S + 1) * 4, "d2h_bytes_per_step": 8},
+            "cpu_baseline": cpu}
+
+
 # ----------------------------------------------------------------- our arm
 def main():
     args = parse()
@@ -341,6 +465,10 @@ def main():
                           f"steps ({dt:.1f} s)")}
 
     kps = eng.kernels_per_step(B)
+    eng.close()
+    train = None
+    if not args.no_train:
+        train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
@@ -356,9 +484,9 @@ def main():
                 "roofline": roof, "roofline_whole_step": whole,
                 "kernel_groups_ms_per_step": {k: round(v, 4) for k, v in groups.items()},
                 "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
-                "gpu_launches": kps * G * args.steps, "kernels_per_decode_step": kps}
+                "gpu_launches": kps * G * args.steps, "kernels_per_decode_step": kps,
+                "train": train}
         print(json.dumps(line), flush=True)
-    eng.close()
     if world > 1:
         dist.destroy_process_group()
 

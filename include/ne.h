@@ -244,6 +244,11 @@ NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_
                                     float* h_w3, float* h_rms_att, float* h_rms_ffn,
                                     float* h_q_norm, float* h_k_norm);
 
+/* The contiguous fp32 gradient pool (every trainable tensor's gradient), for
+ * data-parallel reduction by the caller (e.g. an NCCL all-reduce on the
+ * context's stream between ne_train_fwd_bwd and ne_adamw_step). */
+NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floats);
+
 /* ---- allocation-free split-K product --------------------------------------
  * No counterpart in the reference: an addition for callers that must not
  * allocate device memory -- code running inside an allocator hook or a memory

@@ -59,6 +59,8 @@ struct TrainState {
   size_t pool_floats = 0;
   void* act_pool = nullptr;              // saved activations + scratch
   std::vector<Seg> segs;
+  float* grad_pool = nullptr;            // start of the gradients inside `pool`
+  size_t grad_floats = 0;
   std::vector<TrainLayerP> P;
   float *embed_w = nullptr, *embed_g = nullptr, *rmsf_g = nullptr;
   std::vector<TrainActs> A;
@@ -168,20 +170,18 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
                hd = m.head_dim, L = m.n_layers;
   auto rnd = [](size_t n) { return (n + 63) & ~(size_t)63; };
   // ---- parameter pool: masters for matrices + embed, grads / m / v for all
-  const size_t mat = qkv * D + D * qd + 2 * F * D + D * F;
-  const size_t gains = 2 * D + (m.qk_norm ? 2 * hd : 0);
   const size_t per_layer_w = rnd(qkv * D) + rnd(D * qd) + rnd(2 * F * D) + rnd(D * F);
   const size_t per_layer_all = per_layer_w + 2 * rnd(D) + 2 * rnd(hd);
   const size_t total_w = L * per_layer_w + rnd(V * D);                     // masters
   const size_t total_all = L * per_layer_all + rnd(D) + rnd(V * D);        // grads/m/v
-  (void)mat;
-  (void)gains;
   t->pool_floats = total_w + 3 * total_all;
   ne_status s;
   if ((s = dalloc(ctx, &t->pool, t->pool_floats)) != NE_OK) return s;
   NE_CUDA(cudaMemsetAsync(t->pool, 0, t->pool_floats * 4, ctx->st));
   float* pw = t->pool;
   float* pg = t->pool + total_w;
+  t->grad_pool = pg;
+  t->grad_floats = total_all;
   float* pm = pg + total_all;
   float* pv = pm + total_all;
   size_t ow = 0, oa = 0;
@@ -479,6 +479,13 @@ NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h
   if (s != NE_OK) return s;
   if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
   return ne_sync(ctx);
+}
+
+NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floats) {
+  if (!ctx || !ctx->train || !d_grads || !n_floats) return NE_ERR_STATE;
+  *d_grads = ctx->train->grad_pool;
+  *n_floats = ctx->train->grad_floats;
+  return NE_OK;
 }
 
 // Global L2 norm of the accumulated gradients times grad_scale (train.m:805-826).

@@ -30,7 +30,7 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_gemm_splitk_noalloc", "ne_train_alloc", "ne_train_set_masters",
             "ne_train_sync_weights", "ne_train_zero_grads", "ne_train_fwd_bwd_device",
             "ne_train_fwd_bwd", "ne_train_grad_norm", "ne_adamw_step", "ne_lr_schedule",
-            "ne_train_get_layer", "ne_gemm")
+            "ne_train_get_layer", "ne_gemm", "ne_train_grad_pool")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -150,6 +150,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_get_stream.restype = P
     lib.ne_profile_decode_step.argtypes = [P, I, I, C.POINTER(C.c_float)]
     lib.ne_gemm.argtypes = [P, C.POINTER(GemmDescC)]
+    lib.ne_train_grad_pool.argtypes = [P, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]
     lib.ne_train_alloc.argtypes = [P, I, I]
     lib.ne_train_set_masters.argtypes = [P, I] + [P] * 7
     lib.ne_train_sync_weights.argtypes = [P]
@@ -345,6 +346,22 @@ class Engine:
                                                 None, None, None, _ptr(rf), None, None, None))
         return {"layers": layers, "rms_final": rf, "embed": emb,
                 "qk": qk if c.qk_norm else None}
+
+    def grad_pool(self):
+        """(device pointer, float count) of the contiguous fp32 gradient pool."""
+        p, n = C.c_void_p(), C.c_size_t()
+        self._check(self.lib.ne_train_grad_pool(self._ctx, C.byref(p), C.byref(n)))
+        return int(p.value), int(n.value)
+
+    def grad_pool_tensor(self):
+        """The gradient pool as a torch CUDA tensor view (no copy)."""
+        import torch
+        ptr, n = self.grad_pool()
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                        "version": 3, "strides": None}
+        return torch.as_tensor(_View(), device=f"cuda:{torch.cuda.current_device()}")
 
     def get_grads(self) -> dict:
         return self._train_tensors(0)

@@ -42,10 +42,11 @@ def forward_loss(cfg: ModelCfg, params: dict, tokens: np.ndarray):
     def rms(x, w, eps):
         return x / torch.sqrt((x * x).mean(-1, keepdim=True) + eps) * w
 
+    dt = params["embed"].dtype
     freqs = torch.tensor([1.0 / (cfg.theta ** (2.0 * i / hd)) for i in range(hd // 2)],
                          dtype=torch.float64)
     ang = torch.arange(S, dtype=torch.float64)[:, None] * freqs[None, :]
-    cos, sin = torch.cos(ang), torch.sin(ang)
+    cos, sin = torch.cos(ang).to(dt), torch.sin(ang).to(dt)
 
     def rope(x):  # x [B, S, nh, hd], interleaved pairs
         x0, x1 = x[..., 0::2], x[..., 1::2]
@@ -86,10 +87,11 @@ def forward_loss(cfg: ModelCfg, params: dict, tokens: np.ndarray):
     return nll.mean()
 
 
-def loss_and_grads(cfg: ModelCfg, layers, rms_final, embed, qk, tokens):
-    """Returns (loss, grads) with grads shaped like the inputs (numpy float64)."""
+def loss_and_grads(cfg: ModelCfg, layers, rms_final, embed, qk, tokens, dtype="float64"):
+    """Returns (loss, grads) with grads shaped like the inputs (numpy, `dtype`)."""
     torch = _torch()
-    t = lambda a: torch.tensor(np.asarray(a, np.float64), requires_grad=True)
+    tdt = getattr(torch, dtype)
+    t = lambda a: torch.tensor(np.asarray(a), dtype=tdt, requires_grad=True)
     P = {"layers": [{k: t(v) for k, v in lw.items()} for lw in layers],
          "rms_final": t(rms_final), "embed": t(embed),
          "qk": [(t(a), t(b)) for a, b in qk] if qk is not None else None}
