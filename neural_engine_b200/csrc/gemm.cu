@@ -103,7 +103,7 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
       }
       break;
     case EPI_RESID: {
-      EpiResid::Params p{(float*)c.out, c.ld, c.alpha};
+      EpiResid::Params p{(float*)c.out, c.ld, c.alpha, c.atomic};
       return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
     }
     case EPI_SWIGLU:
@@ -188,7 +188,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   const int splits = gemm_pick_splits(c, num_sms);
   const int kb = c.K / GEMM_BK;
   if (kb % splits != 0) return cudaErrorInvalidValue;
-  if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32) return cudaErrorInvalidValue;
+  if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32 && !(c.epi == EPI_RESID && c.atomic))
+    return cudaErrorInvalidValue;
 
   CUtensorMap ta, tb;
   const bool ok_a = c.a_mn ? make_tmap_mn(&ta, c.A, c.M, c.K, c.lda)

@@ -223,13 +223,20 @@ struct EpiSwiGLUBwd {
 };
 
 // fp32 residual update, row-major:  x[m*ld + n] += alpha * acc
+// (atomic: red.global.add, for split-K accumulation into gradient buffers)
 struct EpiResid {
-  struct Params { float* x; long long ld; float alpha; };
+  struct Params { float* x; long long ld; float alpha; int atomic; };
   template <int CH>
   __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
                                int M, int N) {
     if (m >= M) return;
     float* row = p.x + (long long)m * p.ld + n0;
+    if (p.atomic) {
+#pragma unroll
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) atomicAdd(row + j, p.alpha * v[j]);
+      return;
+    }
     if (n0 + CH <= N) {
 #pragma unroll
       for (int j = 0; j < CH; j += 4) {

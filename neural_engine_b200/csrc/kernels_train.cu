@@ -42,56 +42,95 @@ __device__ __forceinline__ float block_sum256(float v, float* red) {
 }
 
 // ------------------------------------------------------------ RMSNorm backward
-// Block of 256 threads handles R consecutive rows; D <= 256 * 4.
-constexpr int RB_ROWS = 8;
-__global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                                   const float* __restrict__ w, float eps, int M, int D,
-                                   const float* __restrict__ residual, float* __restrict__ dx,
-                                   bf16* __restrict__ dx16, float* __restrict__ dw) {
+// One warp per row (no block barriers in the row reductions); 8 warps per
+// block walk RB_ROWS rows each and reduce their dw partials once per block.
+constexpr int RB_ROWS = 4;
+template <int PER>
+__global__ void __launch_bounds__(256)
+rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                   const float* __restrict__ w, float eps, int M, int D,
+                   const float* __restrict__ residual, float* __restrict__ dx,
+                   bf16* __restrict__ dx16, float* __restrict__ dw) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float red[32];
-  constexpr int PER = 4;
-  float dwp[PER];
+  extern __shared__ float sdw[];   // [8][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float dwp[PER * 4];
 #pragma unroll
-  for (int k = 0; k < PER; ++k) dwp[k] = 0.f;
-  const int r0 = blockIdx.x * RB_ROWS;
+  for (int k = 0; k < PER * 4; ++k) dwp[k] = 0.f;
+  float wv[PER * 4];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = (k * 32 + lane) * 4;
+    if (i < D) {
+      const float4 t = *reinterpret_cast<const float4*>(w + i);
+      wv[4 * k] = t.x; wv[4 * k + 1] = t.y; wv[4 * k + 2] = t.z; wv[4 * k + 3] = t.w;
+    } else {
+      wv[4 * k] = wv[4 * k + 1] = wv[4 * k + 2] = wv[4 * k + 3] = 0.f;
+    }
+  }
+  const int r0 = (blockIdx.x * 8 + warp) * RB_ROWS;
   for (int rr = 0; rr < RB_ROWS; ++rr) {
     const int r = r0 + rr;
     if (r >= M) break;
-    const float* xr = x + (size_t)r * D;
-    const float* gr = dy + (size_t)r * D;
-    float xv[PER], gv[PER], wv[PER];
+    float xv[PER * 4], gv[PER * 4];
     float ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
-      const int i = threadIdx.x + k * 256;
-      xv[k] = i < D ? xr[i] : 0.f;
-      gv[k] = i < D ? gr[i] : 0.f;
-      wv[k] = i < D ? w[i] : 0.f;
-      ss += xv[k] * xv[k];
-      dot += gv[k] * wv[k] * xv[k];
+      const int i = (k * 32 + lane) * 4;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
+      if (i < D) {
+        a = *reinterpret_cast<const float4*>(x + (size_t)r * D + i);
+        g = *reinterpret_cast<const float4*>(dy + (size_t)r * D + i);
+      }
+      xv[4 * k] = a.x; xv[4 * k + 1] = a.y; xv[4 * k + 2] = a.z; xv[4 * k + 3] = a.w;
+      gv[4 * k] = g.x; gv[4 * k + 1] = g.y; gv[4 * k + 2] = g.z; gv[4 * k + 3] = g.w;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ss += xv[4 * k + j] * xv[4 * k + j];
+        dot += gv[4 * k + j] * wv[4 * k + j] * xv[4 * k + j];
+      }
     }
-    ss = block_sum256(ss, red);
-    dot = block_sum256(dot, red);
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
     const float rrms = 1.0f / sqrtf(ss / (float)D + eps);
     const float c = rrms * rrms * dot / (float)D;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
-      const int i = threadIdx.x + k * 256;
+      const int i = (k * 32 + lane) * 4;
       if (i >= D) continue;
-      float v = rrms * (wv[k] * gv[k] - xv[k] * c);
-      if (residual) v += residual[(size_t)r * D + i];
-      dx[(size_t)r * D + i] = v;
-      if (dx16) dx16[(size_t)r * D + i] = __float2bfloat16_rn(v);
-      dwp[k] += gv[k] * xv[k] * rrms;
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = rrms * (wv[4 * k + j] * gv[4 * k + j] - xv[4 * k + j] * c);
+        dwp[4 * k + j] += gv[4 * k + j] * xv[4 * k + j] * rrms;
+      }
+      if (residual) {
+        const float4 rs = *reinterpret_cast<const float4*>(residual + (size_t)r * D + i);
+        o[0] += rs.x; o[1] += rs.y; o[2] += rs.z; o[3] += rs.w;
+      }
+      *reinterpret_cast<float4*>(dx + (size_t)r * D + i) = make_float4(o[0], o[1], o[2], o[3]);
+      if (dx16) {
+        __nv_bfloat162* d16 = reinterpret_cast<__nv_bfloat162*>(dx16 + (size_t)r * D + i);
+        d16[0] = __floats2bfloat162_rn(o[0], o[1]);
+        d16[1] = __floats2bfloat162_rn(o[2], o[3]);
+      }
     }
   }
   if (dw) {
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
-      const int i = threadIdx.x + k * 256;
-      if (i < D) atomicAdd(dw + i, dwp[k]);
+      const int i = (k * 32 + lane) * 4;
+      if (i < D)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sdw[warp * D + i + j] = dwp[4 * k + j];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) t += sdw[w8 * D + i];
+      atomicAdd(dw + i, t);
     }
   }
 }
@@ -290,6 +329,46 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
   }
 }
 
+// ------------------------------------------------------------ multi-tensor forms
+// One launch over every trainable tensor: blockIdx.y selects the tensor.
+__global__ void adamw_multi_kernel(const AdamSeg* __restrict__ segs, float lr, float b1, float b2,
+                                   float eps, float inv_bc1, float inv_bc2, float gscale) {
+  pdl_trigger();
+  pdl_wait();
+  const AdamSeg sg = segs[blockIdx.y];
+  const float ob1 = 1.0f - b1, ob2 = 1.0f - b2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < sg.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float gi = sg.g[i] * gscale;
+    float mi = sg.m[i] * b1;
+    mi = gi * ob1 + mi;
+    float vi = sg.v[i] * b2;
+    vi = (gi * gi) * ob2 + vi;
+    const float mh = mi * inv_bc1;
+    const float vh = sqrtf(vi * inv_bc2) + eps;
+    float upd = mh / vh;
+    upd = sg.w[i] * sg.wd + upd;
+    const float wi = upd * (-lr) + sg.w[i];
+    sg.w[i] = wi;
+    sg.m[i] = mi;
+    sg.v[i] = vi;
+    if (sg.w16) sg.w16[i] = __float2bfloat16_rn(wi);
+  }
+}
+
+__global__ void sumsq_multi_kernel(const AdamSeg* __restrict__ segs, double* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  const AdamSeg sg = segs[blockIdx.y];
+  float acc = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < sg.n;
+       i += (long long)gridDim.x * blockDim.x)
+    acc += sg.g[i] * sg.g[i];
+  acc = block_sum256(acc, red);
+  if (threadIdx.x == 0) atomicAdd(out, (double)acc);
+}
+
 // ------------------------------------------------------------ sum of squares
 __global__ void sumsq_kernel(const float* __restrict__ g, long long n, double* __restrict__ out) {
   pdl_trigger();
@@ -323,9 +402,14 @@ int grid_for(long long n, int threads) {
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
                                int D, const float* residual, float* dx, __nv_bfloat16* dx16,
                                float* dw, cudaStream_t st) {
-  if (D > 1024) return cudaErrorInvalidValue;
-  return launch_k(rmsnorm_bwd_kernel, dim3((M + RB_ROWS - 1) / RB_ROWS), dim3(256), 0, st, dy, x,
-                  w, eps, M, D, residual, dx, dx16, dw);
+  if (D > 1024 || D % 4) return cudaErrorInvalidValue;
+  const dim3 grid((M + 8 * RB_ROWS - 1) / (8 * RB_ROWS));
+  const size_t smem = (size_t)8 * D * sizeof(float);
+  if (D <= 512)
+    return launch_k(rmsnorm_bwd_kernel<4>, grid, dim3(256), smem, st, dy, x, w, eps, M, D, residual,
+                    dx, dx16, dw);
+  return launch_k(rmsnorm_bwd_kernel<8>, grid, dim3(256), smem, st, dy, x, w, eps, M, D, residual,
+                  dx, dx16, dw);
 }
 
 cudaError_t launch_ce_rows(const float* logits, const int32_t* tgt, int rows, int V, float scale,
@@ -359,6 +443,22 @@ cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bflo
                          float inv_bc1, float inv_bc2, float gscale, cudaStream_t st) {
   return launch_k(adamw_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, w, g, m, v, w16, n, lr,
                   b1, b2, eps, wd, inv_bc1, inv_bc2, gscale);
+}
+
+cudaError_t launch_adamw_multi(const AdamSeg* d_segs, int nseg, long long max_n, float lr,
+                               float b1, float b2, float eps, float inv_bc1, float inv_bc2,
+                               float gscale, cudaStream_t st) {
+  const long long per = (max_n + 255) / 256;
+  const int gx = (int)(per < 256 ? (per < 1 ? 1 : per) : 256);
+  return launch_k(adamw_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, lr, b1, b2, eps,
+                  inv_bc1, inv_bc2, gscale);
+}
+
+cudaError_t launch_sumsq_multi(const AdamSeg* d_segs, int nseg, long long max_n, double* out,
+                               cudaStream_t st) {
+  const long long per = (max_n + 255) / 256;
+  const int gx = (int)(per < 256 ? (per < 1 ? 1 : per) : 256);
+  return launch_k(sumsq_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, out);
 }
 
 cudaError_t launch_sumsq(const float* g, long long n, double* out, cudaStream_t st) {

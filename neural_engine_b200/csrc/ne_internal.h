@@ -43,6 +43,7 @@ struct GemmCall {
   int half_out = 0;             // EPI_BF16: write fp16 instead of bf16
   const void* aux3 = nullptr;   // EPI_ADD: input; EPI_SWIGLU_BWD: h1 (aux1 = h3)
   long long aux_ld = 0;         // EPI_SWIGLU_BWD: F
+  int atomic = 0;               // EPI_RESID: accumulate with atomics (allows split-K)
 };
 
 // Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).
@@ -88,6 +89,21 @@ cudaError_t launch_prefill_attn(const __half* q, const __half* kc, const __half*
                                 cudaStream_t st, float* lse = nullptr);
 
 // ------------------------------------------------------------------ training
+// One trainable tensor for the multi-tensor AdamW / norm kernels (device array).
+struct AdamSeg {
+  float* w;
+  const float* g;
+  float* m;
+  float* v;
+  __nv_bfloat16* w16;
+  long long n;
+  float wd;
+};
+cudaError_t launch_adamw_multi(const AdamSeg* d_segs, int nseg, long long max_n, float lr,
+                               float b1, float b2, float eps, float inv_bc1, float inv_bc2,
+                               float gscale, cudaStream_t st);
+cudaError_t launch_sumsq_multi(const AdamSeg* d_segs, int nseg, long long max_n, double* out,
+                               cudaStream_t st);
 cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* V, const __nv_bfloat16* O,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,

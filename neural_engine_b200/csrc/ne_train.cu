@@ -59,6 +59,9 @@ struct TrainState {
   size_t pool_floats = 0;
   void* act_pool = nullptr;              // saved activations + scratch
   std::vector<Seg> segs;
+  AdamSeg* d_segs = nullptr;             // device copy of the segment table
+  float d_segs_wd = -2.f;                // weight decay the device table holds
+  long long max_seg = 0;
   float* grad_pool = nullptr;            // start of the gradients inside `pool`
   size_t grad_floats = 0;
   std::vector<TrainLayerP> P;
@@ -79,6 +82,7 @@ struct TrainState {
 void free_train(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return;
   TrainState* t = ctx->train;
+  if (t->d_segs) cudaFree(t->d_segs);
   if (t->pool) cudaFree(t->pool);
   if (t->act_pool) cudaFree(t->act_pool);
   delete t;
@@ -120,8 +124,34 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ a, float* _
 // dst[r, :] = interleave of (W1 row r, W3 row r) blocks: the W13 device layout.
 size_t w13_row(size_t f, bool is_w3) { return (f / 16) * 32 + (is_w3 ? 16 : 0) + f % 16; }
 
+// Split-K factor for a gradient GEMM (EPI_RESID, atomic accumulation) whose
+// output has few tiles: the factor with the best wave efficiency
+// units / (SMs * ceil(units / SMs)), at most 4 (every split adds one atomic
+// add per output element), taken only when it gains more than 10 points.
+int dw_splits(const GemmCall& c, int sms) {
+  const int bn = c.bn ? c.bn : 256;
+  const int tiles = ((c.M + 127) / 128) * ((c.N + bn - 1) / bn);
+  const int kb = c.K / 64;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int d = 1; d <= 4; ++d) {
+    if (kb % d || kb / d < 4) continue;
+    const long long u = (long long)tiles * d;
+    const double eff = (double)u / ((double)sms * ((u + sms - 1) / sms));
+    if (eff > best_eff + 0.10) {
+      best_eff = eff;
+      best = d;
+    }
+  }
+  return best;
+}
+
 ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
+  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) {
+    c.atomic = 1;
+    c.splits = dw_splits(c, ctx->num_sms);
+  }
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
   ctx->launches++;
@@ -343,7 +373,7 @@ NE_API ne_status ne_train_sync_weights(ne_ctx* ctx) {
 NE_API ne_status ne_train_zero_grads(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
   TrainState* t = ctx->train;
-  for (const Seg& s : t->segs) NE_CUDA(cudaMemsetAsync(s.g, 0, s.n * 4, ctx->st));
+  NE_CUDA(cudaMemsetAsync(t->grad_pool, 0, t->grad_floats * 4, ctx->st));
   t->micro_steps = 0;
   return NE_OK;
 }
@@ -489,11 +519,36 @@ NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floa
 }
 
 // Global L2 norm of the accumulated gradients times grad_scale (train.m:805-826).
+// Upload the segment table (with the weight decay of this step) when it changed.
+static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
+  TrainState* t = ctx->train;
+  if (t->d_segs && t->d_segs_wd == weight_decay) return NE_OK;
+  std::vector<AdamSeg> hs;
+  t->max_seg = 0;
+  for (const Seg& sg : t->segs) {
+    hs.push_back({sg.w, sg.g, sg.m, sg.v, sg.w16, sg.n, sg.wd < 0.f ? weight_decay : 0.f});
+    t->max_seg = std::max(t->max_seg, sg.n);
+  }
+  if (!t->d_segs) {
+    ne_status s = dalloc(ctx, &t->d_segs, hs.size());
+    if (s != NE_OK) return s;
+  }
+  NE_CUDA(cudaMemcpyAsync(t->d_segs, hs.data(), hs.size() * sizeof(AdamSeg), cudaMemcpyHostToDevice,
+                          ctx->st));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  t->d_segs_wd = weight_decay;
+  return NE_OK;
+}
+
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm) {
   if (!ctx || !ctx->train || !h_norm) return NE_ERR_STATE;
   TrainState* t = ctx->train;
+  if (!t->d_segs) {
+    ne_status s0 = upload_segs(ctx, 0.f);
+    if (s0 != NE_OK) return s0;
+  }
   NE_CUDA(cudaMemsetAsync(t->red, 0, sizeof(double), ctx->st));
-  for (const Seg& sg : t->segs) NE_LAUNCH(launch_sumsq(sg.g, sg.n, t->red, ctx->st));
+  NE_LAUNCH(launch_sumsq_multi(t->d_segs, (int)t->segs.size(), t->max_seg, t->red, ctx->st));
   double ss = 0;
   NE_CUDA(cudaMemcpyAsync(&ss, t->red, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
   ne_status s = ne_sync(ctx);
@@ -519,11 +574,9 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
   if (cfg->grad_clip > 0.f && norm > cfg->grad_clip) gscale *= cfg->grad_clip / norm;
   const float bc1 = 1.0f - std::pow(cfg->beta1, (float)t_step);
   const float bc2 = 1.0f - std::pow(cfg->beta2, (float)t_step);
-  for (const Seg& sg : t->segs) {
-    const float wd = sg.wd < 0.f ? cfg->weight_decay : 0.f;
-    NE_LAUNCH(launch_adamw(sg.w, sg.g, sg.m, sg.v, sg.w16, sg.n, cfg->lr, cfg->beta1, cfg->beta2,
-                           cfg->eps, wd, 1.0f / bc1, 1.0f / bc2, gscale, ctx->st));
-  }
+  if ((s = upload_segs(ctx, cfg->weight_decay)) != NE_OK) return s;
+  NE_LAUNCH(launch_adamw_multi(t->d_segs, (int)t->segs.size(), t->max_seg, cfg->lr, cfg->beta1,
+                               cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, gscale, ctx->st));
   return ne_train_zero_grads(ctx);
 }
 
