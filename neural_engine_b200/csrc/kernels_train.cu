@@ -448,16 +448,16 @@ cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bflo
 cudaError_t launch_adamw_multi(const AdamSeg* d_segs, int nseg, long long max_n, float lr,
                                float b1, float b2, float eps, float inv_bc1, float inv_bc2,
                                float gscale, cudaStream_t st) {
-  const long long per = (max_n + 255) / 256;
-  const int gx = (int)(per < 256 ? (per < 1 ? 1 : per) : 256);
+  const long long per = (max_n + 1023) / 1024;   // ~4 elements per thread for the largest
+  const int gx = (int)(per < 2048 ? (per < 1 ? 1 : per) : 2048);
   return launch_k(adamw_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, lr, b1, b2, eps,
                   inv_bc1, inv_bc2, gscale);
 }
 
 cudaError_t launch_sumsq_multi(const AdamSeg* d_segs, int nseg, long long max_n, double* out,
                                cudaStream_t st) {
-  const long long per = (max_n + 255) / 256;
-  const int gx = (int)(per < 256 ? (per < 1 ? 1 : per) : 256);
+  const long long per = (max_n + 1023) / 1024;
+  const int gx = (int)(per < 2048 ? (per < 1 ? 1 : per) : 2048);
   return launch_k(sumsq_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, out);
 }
 

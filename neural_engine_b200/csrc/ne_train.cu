@@ -124,34 +124,24 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ a, float* _
 // dst[r, :] = interleave of (W1 row r, W3 row r) blocks: the W13 device layout.
 size_t w13_row(size_t f, bool is_w3) { return (f / 16) * 32 + (is_w3 ? 16 : 0) + f % 16; }
 
-// Split-K factor for a gradient GEMM (EPI_RESID, atomic accumulation) whose
-// output has few tiles: the factor with the best wave efficiency
-// units / (SMs * ceil(units / SMs)), at most 4 (every split adds one atomic
-// add per output element), taken only when it gains more than 10 points.
-int dw_splits(const GemmCall& c, int sms) {
-  const int bn = c.bn ? c.bn : 256;
-  const int tiles = ((c.M + 127) / 128) * ((c.N + bn - 1) / bn);
-  const int kb = c.K / 64;
-  int best = 1;
-  double best_eff = 0.0;
-  for (int d = 1; d <= 4; ++d) {
-    if (kb % d || kb / d < 4) continue;
-    const long long u = (long long)tiles * d;
-    const double eff = (double)u / ((double)sms * ((u + sms - 1) / sms));
-    if (eff > best_eff + 0.10) {
-      best_eff = eff;
-      best = d;
-    }
-  }
-  return best;
+// Wave efficiency units / (SMs * ceil(units / SMs)) of a tiling.
+double wave_eff(long long units, int sms) {
+  return (double)units / ((double)sms * ((units + sms - 1) / sms));
+}
+
+// N tile for a gradient GEMM (small weight-shaped output, long K): 128 when it
+// fills the SMs noticeably better than 256.  (Split-K with atomic
+// accumulation was measured slower: one atomic add per element per split.)
+int dw_bn(const GemmCall& c, int sms) {
+  const long long mt = (c.M + 127) / 128;
+  const double e256 = wave_eff(mt * ((c.N + 255) / 256), sms);
+  const double e128 = wave_eff(mt * ((c.N + 127) / 128), sms);
+  return e128 > e256 + 0.05 ? 128 : 256;
 }
 
 ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
-  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) {
-    c.atomic = 1;
-    c.splits = dw_splits(c, ctx->num_sms);
-  }
+  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) c.bn = dw_bn(c, ctx->num_sms);
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
   ctx->launches++;
