@@ -1,6 +1,7 @@
 """Build libne.so in-tree for sm_100a with nvcc.
 
-    python -m neural_engine_b200.build          # or: python neural_engine_b200/build.py
+    python neural_engine_b200/build.py   (or __graft_entry__.build(); the package
+    itself cannot be imported before the library exists)
 
 Every .cu under csrc/ is compiled for ``-gencode arch=compute_100a,code=sm_100a``
 with ``-lineinfo`` into _build/, then linked (static cudart) into

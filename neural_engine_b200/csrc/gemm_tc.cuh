@@ -10,14 +10,18 @@
 //   * weight-major ("swap-AB"): A = weight [out, K], B = activations [batch, K]
 //     (decode: batch <= 256 fits one N tile; output written transposed).
 //
-// Warp roles (192 threads, one CTA per SM, persistent over work units):
+// Warp roles (320 threads, one CTA per SM, persistent over work units):
 //   warp 0      TMA producer: one lane streams A/B boxes into a STAGES-deep
 //               shared-memory ring (mbarrier full/empty handshake).
 //   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma
 //               (128 x BN x 16 per instruction) into one of two accumulators,
 //               commits stage release and accumulator-ready barriers.
-//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4) .. +31), apply the fused epilogue functor, store.
+//   warps 2-9   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4) .. +31; warps 2-5 take the even column chunks,
+//               warps 6-9 the odd ones), apply the fused epilogue functor,
+//               store.  Two warps per lane quarter keep enough independent
+//               instructions and stores in flight for the compute-heavy
+//               epilogues (SwiGLU backward) and the fp32 outputs.
 // The two TMEM accumulators let the epilogue of work unit i overlap the MMAs
 // of unit i+1.  Split-K: a work unit is (m_tile, n_tile, split); the epilogue
 // receives the split index and writes a partial slab that the consumer
@@ -32,7 +36,8 @@ namespace ne {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_EPI_WARPS = 8;                     // two per TMEM lane quarter
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
 struct GemmShape {
   int M, N, K;          // logical sizes (A rows, B rows, reduction)
@@ -61,6 +66,20 @@ struct GemmCfg {
 // ------------------------------------------------------------------ epilogues
 // Each functor: apply(p, m, n0, v[CH], split, M, N).  m is the A-side row,
 // n0 the first B-side column of the chunk; only (m < M, n < N) is stored.
+// A functor that reads global memory besides the accumulator may also define
+// prefetch(p, m, n0, ncols, M, N): called one work unit ahead, it hints that
+// row's inputs into L2 so the epilogue's loads hit L2 instead of waiting on
+// HBM latency with few bytes in flight.
+template <class E, class = void>
+struct EpiHasPrefetch { static constexpr bool value = false; };
+template <class E>
+struct EpiHasPrefetch<E, decltype(void(&E::prefetch))> { static constexpr bool value = true; };
+
+// L2 hints for `bytes` contiguous bytes starting at p (128-byte lines).
+__device__ __forceinline__ void prefetch_row_l2(const void* p, int bytes) {
+  const char* c = reinterpret_cast<const char*>(p);
+  for (int o = 0; o < bytes; o += 128) prefetch_l2(c + o);
+}
 
 // fp32 store, transposed (swap-AB):  out[split*split_stride + n*ld + m]
 struct EpiF32T {
@@ -143,6 +162,10 @@ struct EpiBF16 {
 // fp32 add, row-major:  out[m*ld + n] = in[m*ld + n] + alpha * acc
 struct EpiAdd {
   struct Params { float* out; const float* in; long long ld; float alpha; };
+  __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
+    if (m >= M || n0 >= N) return;
+    prefetch_row_l2(p.in + (long long)m * p.ld + n0, 4 * min(ncols, N - n0));
+  }
   template <int CH>
   __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
                                int M, int N) {
@@ -150,12 +173,15 @@ struct EpiAdd {
     float* orow = p.out + (long long)m * p.ld + n0;
     const float* irow = p.in + (long long)m * p.ld + n0;
     if (n0 + CH <= N) {
+      float4 r[CH / 4];   // every load issued before the first store
+#pragma unroll
+      for (int j = 0; j < CH; j += 4) r[j / 4] = *reinterpret_cast<const float4*>(irow + j);
 #pragma unroll
       for (int j = 0; j < CH; j += 4) {
-        float4 r = *reinterpret_cast<const float4*>(irow + j);
-        r.x += p.alpha * v[j]; r.y += p.alpha * v[j + 1];
-        r.z += p.alpha * v[j + 2]; r.w += p.alpha * v[j + 3];
-        *reinterpret_cast<float4*>(orow + j) = r;
+        float4 q = r[j / 4];
+        q.x += p.alpha * v[j]; q.y += p.alpha * v[j + 1];
+        q.z += p.alpha * v[j + 2]; q.w += p.alpha * v[j + 3];
+        *reinterpret_cast<float4*>(orow + j) = q;
       }
     } else {
       for (int j = 0; j < CH; ++j)
@@ -173,6 +199,12 @@ struct EpiSwiGLUBwd {
   struct Params {
     __nv_bfloat16* dh13; const __nv_bfloat16* h1; const __nv_bfloat16* h3; long long F; float alpha;
   };
+  __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
+    if (m >= M || n0 >= N) return;
+    const int bytes = 2 * min(ncols, N - n0);
+    prefetch_row_l2(p.h1 + (long long)m * p.F + n0, bytes);
+    prefetch_row_l2(p.h3 + (long long)m * p.F + n0, bytes);
+  }
   template <int CH>
   __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
                                int M, int N) {
@@ -181,23 +213,30 @@ struct EpiSwiGLUBwd {
     const __nv_bfloat16* a = p.h1 + (long long)m * p.F + n0;
     const __nv_bfloat16* b = p.h3 + (long long)m * p.F + n0;
     __nv_bfloat16* out = p.dh13 + (long long)m * 2 * p.F;
+    // all 32 features of h1 and h3 are loaded before any store is issued, so
+    // the eight 16-byte loads are in flight together
+    uint4 ra[4], rb[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      ra[q] = *reinterpret_cast<const uint4*>(a + 8 * q);
+      rb[q] = *reinterpret_cast<const uint4*>(b + 8 * q);
+    }
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int f0 = n0 + 16 * half;            // 16 features of block c = f0 / 16
       float d1[16], d3[16];
 #pragma unroll
       for (int j = 0; j < 16; j += 8) {
-        const uint4 ra = *reinterpret_cast<const uint4*>(a + 16 * half + j);
-        const uint4 rb = *reinterpret_cast<const uint4*>(b + 16 * half + j);
-        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra);
-        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb);
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra[2 * half + j / 8]);
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb[2 * half + j / 8]);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const float2 x1 = __bfloat1622float2(ha[t]);
           const float2 x3 = __bfloat1622float2(hb[t]);
           const float g0 = p.alpha * v[16 * half + j + 2 * t];
           const float g1 = p.alpha * v[16 * half + j + 2 * t + 1];
-          const float s0 = 1.0f / (1.0f + __expf(-x1.x)), s1 = 1.0f / (1.0f + __expf(-x1.y));
+          const float s0 = __fdividef(1.0f, 1.0f + __expf(-x1.x));
+          const float s1 = __fdividef(1.0f, 1.0f + __expf(-x1.y));
           d1[j + 2 * t] = g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0));
           d1[j + 2 * t + 1] = g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1));
           d3[j + 2 * t] = g0 * x1.x * s0;
@@ -226,6 +265,10 @@ struct EpiSwiGLUBwd {
 // (atomic: red.global.add, for split-K accumulation into gradient buffers)
 struct EpiResid {
   struct Params { float* x; long long ld; float alpha; int atomic; };
+  __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
+    if (p.atomic || m >= M || n0 >= N) return;
+    prefetch_row_l2(p.x + (long long)m * p.ld + n0, 4 * min(ncols, N - n0));
+  }
   template <int CH>
   __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
                                int M, int N) {
@@ -238,9 +281,12 @@ struct EpiResid {
       return;
     }
     if (n0 + CH <= N) {
+      float4 rr[CH / 4];   // every load issued before the first store
+#pragma unroll
+      for (int j = 0; j < CH; j += 4) rr[j / 4] = *reinterpret_cast<const float4*>(row + j);
 #pragma unroll
       for (int j = 0; j < CH; j += 4) {
-        float4 r = *reinterpret_cast<float4*>(row + j);
+        float4 r = rr[j / 4];
         if (p.alpha == 1.0f) {
           r.x += v[j]; r.y += v[j + 1]; r.z += v[j + 2]; r.w += v[j + 3];
         } else {
@@ -273,7 +319,7 @@ struct EpiSwiGLU {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float h1 = v[j], h3 = v[16 + j];
-      out[j] = h1 * (1.0f / (1.0f + __expf(-h1))) * h3;
+      out[j] = __fdividef(h1, 1.0f + __expf(-h1)) * h3;
     }
 #pragma unroll
     for (int j = 0; j < 16; j += 8) {
@@ -345,7 +391,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar + 8 * a, 1);
-      mbar_init(tempty_bar + 8 * a, 128);
+      mbar_init(tempty_bar + 8 * a, 32 * GEMM_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -480,10 +526,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------ epilogue (warps 2..9)
     pdl_wait();   // outputs may still be read by the preceding kernel until it completes
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
+    const int chunk0 = ((warp - 2) >> 2) * CH;  // first column chunk of this warp
+
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -491,6 +539,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int rest = u / sh.m_tiles;
       const int nt = rest % sh.n_tiles;
       const int sp = rest / sh.n_tiles;
+      if constexpr (EpiHasPrefetch<Epi>::value) {
+        // this unit's rows (first unit only: the others were hinted one unit
+        // ahead), then the next unit's, so they are L2-resident by the time
+        // the epilogue (which, when it reads inputs, is usually the slower
+        // side of the pipeline) reaches them
+        if (u == (int)blockIdx.x && chunk0 == 0)
+          Epi::prefetch(ep, mt * GEMM_BM + row_in_tile, nt * BN, BN, sh.M, sh.N);
+        const int un = u + gridDim.x;
+        if (un < units && chunk0 == 0) {
+          const int rn = un / sh.m_tiles;
+          Epi::prefetch(ep, (un % sh.m_tiles) * GEMM_BM + row_in_tile, (rn % sh.n_tiles) * BN, BN,
+                        sh.M, sh.N);
+        }
+      }
       // warp-uniform outcome: tcgen05.ld below is a warp-collective instruction
       const bool ready = mbar_wait(tfull_bar + 8 * acc, acc_phase, sh.status, abort_flag);
       if (!__all_sync(0xffffffffu, ready)) break;
@@ -498,7 +560,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int m = mt * GEMM_BM + row_in_tile;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += CH) {
+      for (int c = chunk0; c < BN; c += 2 * CH) {
         float v[CH];
         if constexpr (CH == 32) {
           uint32_t r[32];

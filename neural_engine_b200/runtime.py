@@ -120,7 +120,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     if _lib is not None:
         return _lib
     if not os.path.exists(path):
-        raise ImportError(f"{path} not built; run `python -m neural_engine_b200.build`")
+        raise ImportError(f"{path} not built; run `python neural_engine_b200/build.py`")
     lib = C.CDLL(path)
     P, I, LL, F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
     lib.ne_init.argtypes = [C.POINTER(P), C.POINTER(ModelCfgC), I]
