@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--train-only", action="store_true",
+                    help="skip the decode headline; print the training object alone "
+                         "(profiling runs)")
     ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
     ap.add_argument("--train-seq", type=int, default=256)
     return ap.parse_args()
@@ -283,7 +286,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
             with torch.cuda.stream(stream):        # NCCL ordered after the backward kernels
                 dist.all_reduce(grads, op=dist.ReduceOp.SUM)
         tstep[0] += 1
-        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world)
+        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world, return_norm=False)
 
     for _ in range(args.warmup):
         step()
@@ -320,7 +323,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
             with torch.cuda.stream(stream):
                 dist.all_reduce(grads, op=dist.ReduceOp.SUM)
         tstep[0] += 1
-        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world)
+        eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world, return_norm=False)
     te = (time.perf_counter() - t0) / reps
     if world > 1:
         tt = torch.tensor([te], device="cuda")
@@ -372,6 +375,14 @@ def main():
     cfg = ne.QWEN3_06B
     B, P, G = args.batch, args.prompt, args.gen
     layers, rf, emb, qk = host_weights(seed=0)
+    if args.train_only:
+        train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
+        if rank == 0:
+            print(json.dumps(dict(train, n_gpus=world, higher_is_better=True, vs_baseline=None,
+                                  data="synthetic")), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     eng = ne.Engine(cfg, device=local)
     eng.set_weights(layers, rf, emb, qk)
     eng.kv_alloc(B, P + G)

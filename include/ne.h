@@ -178,7 +178,10 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
  * reference's cblas_sgemm(CblasTrans, ...) calls (train.m:555-738) without a
  * transposed copy.  epi 5: fp32 out = in + alpha*acc (aux0 = in, same ld);
  * epi 6: SwiGLU backward (aux0 = h1, aux1 = h3 [M, aux_ld] bf16; out = dh13
- * [M, 2*aux_ld] bf16 in the W1/W3 16-row-interleaved order). */
+ * [M, 2*aux_ld] bf16 in the W1/W3 16-row-interleaved order).  epi 7: fp32
+ * out as epi 1, plus for every row m and 32-column chunk c the pair
+ * (max, sum of exp(acc - max)) over the chunk's columns < N, written as two
+ * floats at aux0 + 2*(m*aux_ld + c) (the classifier's softmax statistics). */
 typedef struct ne_gemm_desc {
   const void* a; long long lda; int a_mn;
   const void* b; long long ldb; int b_mn;
@@ -231,7 +234,10 @@ NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h
 /* Global L2 norm of the accumulated gradients times grad_scale. */
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm);
 /* Unscale, clip, AdamW (bias correction at step t >= 1), refresh bf16 copies,
- * zero the gradients (train.m:782-904; cpu_ops.h:266-303). */
+ * zero the gradients (train.m:782-904; cpu_ops.h:266-303).  The norm and the
+ * clip factor are computed on the device.  h_grad_norm (optional) receives the
+ * pre-clip norm and makes the call wait for the step; with NULL it only
+ * enqueues work on the context's stream. */
 NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t, float* h_grad_norm);
 /* Warmup + cosine learning rate of train.m:851-858. */
 NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_steps,

@@ -126,6 +126,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         return launch_t<BN, EpiSwiGLUBwd, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
       }
       break;
+    case EPI_F32_STATS:
+      if constexpr (kk && ch32) {
+        EpiF32Stats::Params p{(float*)c.out, c.ld, (float2*)c.aux1, c.aux_ld};
+        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      }
+      break;
     default:
       break;
   }
@@ -182,6 +188,16 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     return cudaErrorInvalidValue;
   if (c.ab_fp16) return cudaErrorInvalidValue;   // bf16 operands only in this build
   if (c.a_mn && !c.b_mn) return cudaErrorInvalidValue;
+  // the SwiGLU epilogues move 8 bf16 at a time and have no scalar path
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (c.epi == EPI_SWIGLU &&
+      (!a16(c.out) || c.ld % 8 || (c.aux1 && !a16(c.aux1)) || (c.aux2 && !a16(c.aux2))))
+    return cudaErrorInvalidValue;
+  if (c.epi == EPI_SWIGLU_BWD && (!a16(c.out) || !a16(c.aux1) || !a16(c.aux3) || c.aux_ld % 8))
+    return cudaErrorInvalidValue;
+  if (c.epi == EPI_F32_STATS && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u) ||
+                                 c.aux_ld < (c.N + 31) / 32))
+    return cudaErrorInvalidValue;
   const int num_sms = device_num_sms();
   int bn = pick_bn(c);
   if (c.b_mn && bn < 64) bn = 64;

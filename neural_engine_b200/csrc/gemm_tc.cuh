@@ -75,6 +75,12 @@ struct EpiHasPrefetch { static constexpr bool value = false; };
 template <class E>
 struct EpiHasPrefetch<E, decltype(void(&E::prefetch))> { static constexpr bool value = true; };
 
+// Vector (16-byte) accesses are used only where the row pointer allows them;
+// an output whose leading dimension leaves rows unaligned takes the scalar path.
+__device__ __forceinline__ bool al16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 // L2 hints for `bytes` contiguous bytes starting at p (128-byte lines).
 __device__ __forceinline__ void prefetch_row_l2(const void* p, int bytes) {
   const char* c = reinterpret_cast<const char*>(p);
@@ -103,7 +109,7 @@ struct EpiF32 {
                                int M, int N) {
     if (m >= M) return;
     float* row = p.out + (long long)split * p.split_stride + (long long)m * p.ld + n0;
-    if (n0 + CH <= N) {
+    if (n0 + CH <= N && al16(row)) {
 #pragma unroll
       for (int j = 0; j < CH; j += 4)
         *reinterpret_cast<float4*>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -111,6 +117,42 @@ struct EpiF32 {
       for (int j = 0; j < CH; ++j)
         if (n0 + j < N) row[j] = v[j];
     }
+  }
+};
+
+// fp32 store, row-major, plus softmax statistics of the stored chunk (the
+// classifier logits of the training step):
+//   out[m*ld + n] = acc;   stats[m*stats_ld + n0/32] = (max_j acc, sum_j exp(acc - max))
+// over the chunk's columns n0 .. n0+31 that are < N.  The cross-entropy
+// kernel combines a row's chunk statistics into its log-sum-exp, so it reads
+// the logits once instead of twice.
+struct EpiF32Stats {
+  struct Params { float* out; long long ld; float2* stats; long long stats_ld; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
+                               int M, int N) {
+    static_assert(CH == 32, "statistics epilogue needs 32-column chunks");
+    if (m >= M || n0 >= N) return;
+    float* row = p.out + (long long)m * p.ld + n0;
+    float mx = -3.402823466e38f;
+    if (n0 + CH <= N && al16(row)) {
+#pragma unroll
+      for (int j = 0; j < CH; j += 4)
+        *reinterpret_cast<float4*>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) mx = fmaxf(mx, v[j]);
+    } else {
+      for (int j = 0; j < CH; ++j)
+        if (n0 + j < N) {
+          row[j] = v[j];
+          mx = fmaxf(mx, v[j]);
+        }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (n0 + j < N) sum += __expf(v[j] - mx);
+    p.stats[(long long)m * p.stats_ld + n0 / CH] = make_float2(mx, sum);
   }
 };
 
@@ -127,7 +169,7 @@ struct EpiBF16 {
     for (int j = 0; j < CH; ++j) w[j] = p.alpha * v[j];
     if (p.half_out) {
       __half* row = reinterpret_cast<__half*>(p.out) + base;
-      if (n0 + CH <= N) {
+      if (n0 + CH <= N && al16(row)) {
 #pragma unroll
         for (int j = 0; j < CH; j += 8) {
           uint4 pk;
@@ -143,7 +185,7 @@ struct EpiBF16 {
       return;
     }
     __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(p.out) + base;
-    if (n0 + CH <= N) {
+    if (n0 + CH <= N && al16(row)) {
 #pragma unroll
       for (int j = 0; j < CH; j += 8) {
         uint4 pk;
@@ -172,7 +214,7 @@ struct EpiAdd {
     if (m >= M) return;
     float* orow = p.out + (long long)m * p.ld + n0;
     const float* irow = p.in + (long long)m * p.ld + n0;
-    if (n0 + CH <= N) {
+    if (n0 + CH <= N && al16(orow) && al16(irow)) {
       float4 r[CH / 4];   // every load issued before the first store
 #pragma unroll
       for (int j = 0; j < CH; j += 4) r[j / 4] = *reinterpret_cast<const float4*>(irow + j);
@@ -280,7 +322,7 @@ struct EpiResid {
         if (n0 + j < N) atomicAdd(row + j, p.alpha * v[j]);
       return;
     }
-    if (n0 + CH <= N) {
+    if (n0 + CH <= N && al16(row)) {
       float4 rr[CH / 4];   // every load issued before the first store
 #pragma unroll
       for (int j = 0; j < CH; j += 4) rr[j / 4] = *reinterpret_cast<const float4*>(row + j);

@@ -27,6 +27,7 @@ namespace ne {
 namespace {
 
 using bf16 = __nv_bfloat16;
+using bf162 = __nv_bfloat162;
 
 __device__ __forceinline__ float block_sum256(float v, float* red) {
   v = warp_sum(v);
@@ -136,50 +137,47 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
 }
 
 // ------------------------------------------------------------ cross-entropy
-// One block (1024 threads) per row of logits [rows, V] (fp32).  Writes the
-// row's loss and dlogits (bf16) = (softmax - onehot(target)) * scale.
-__global__ void ce_rows_kernel(const float* __restrict__ logits, const int32_t* __restrict__ tgt,
-                               int V, float scale, float* __restrict__ loss,
-                               bf16* __restrict__ dlogits, int* status) {
+// cpu_ops.h:348-382.  One block (512 threads) per row of logits [rows, V]
+// (fp32).  The row's softmax statistics come from the classifier GEMM's
+// epilogue as (max, sum exp) per 32-column chunk; they are combined into the
+// row's (m, s), then the logits are read once to write
+//   dlogits (bf16) = (softmax - onehot(target)) * scale
+// and the row's loss -log(p_target + 1e-10).
+__device__ __forceinline__ void ms_combine(float& m, float& s, float om, float os) {
+  const float nm = fmaxf(m, om);
+  s = (m == -FLT_MAX ? 0.f : s * __expf(m - nm)) + (om == -FLT_MAX ? 0.f : os * __expf(om - nm));
+  m = nm;
+}
+
+constexpr int CE_THREADS = 512;
+__global__ void __launch_bounds__(CE_THREADS)
+ce_rows_kernel(const float* __restrict__ logits, const float2* __restrict__ stats, int stats_ld,
+               const int32_t* __restrict__ tgt, int V, float scale, float* __restrict__ loss,
+               bf16* __restrict__ dlogits, int* status) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red_m[32], red_s[32];
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * V;
+  const float2* st = stats + (size_t)r * stats_ld;
+  const int nck = (V + 31) / 32;
   float m = -FLT_MAX, s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = row[i];
-    if (v > m) {
-      s = s * __expf(m - v) + 1.f;
-      m = v;
-    } else {
-      s += __expf(v - m);
-    }
+  for (int i = threadIdx.x; i < nck; i += CE_THREADS) {
+    const float2 c = st[i];
+    ms_combine(m, s, c.x, c.y);
   }
-  // combine (m, s) across the block
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, m, o);
-    const float os = __shfl_xor_sync(0xffffffffu, s, o);
-    const float nm = fmaxf(m, om);
-    s = s * __expf(m - nm) + os * __expf(om - nm);
-    m = nm;
-  }
+  for (int o = 16; o > 0; o >>= 1)
+    ms_combine(m, s, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0) { red_m[w] = m; red_s[w] = s; }
   __syncthreads();
   if (w == 0) {
-    const int nw = blockDim.x >> 5;
-    m = l < nw ? red_m[l] : -FLT_MAX;
-    s = l < nw ? red_s[l] : 0.f;
+    m = l < CE_THREADS / 32 ? red_m[l] : -FLT_MAX;
+    s = l < CE_THREADS / 32 ? red_s[l] : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, m, o);
-      const float os = __shfl_xor_sync(0xffffffffu, s, o);
-      const float nm = fmaxf(m, om);
-      s = s * __expf(m - nm) + os * __expf(om - nm);
-      m = nm;
-    }
+    for (int o = 16; o > 0; o >>= 1)
+      ms_combine(m, s, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o));
     if (l == 0) { red_m[0] = m; red_s[0] = s; }
   }
   __syncthreads();
@@ -196,10 +194,30 @@ __global__ void ce_rows_kernel(const float* __restrict__ logits, const int32_t* 
     loss[r] = -logf(pt + 1e-10f);
   }
   bf16* drow = dlogits + (size_t)r * V;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float p = expf(row[i] - m) * inv;
-    if (i == t) p -= 1.0f;
-    drow[i] = __float2bfloat16_rn(p * scale);
+  if ((V & 3) == 0) {
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (V >> 2); i += CE_THREADS) {
+      const float4 x = row4[i];
+      float p0 = __expf(x.x - m) * inv, p1 = __expf(x.y - m) * inv;
+      float p2 = __expf(x.z - m) * inv, p3 = __expf(x.w - m) * inv;
+      const int d = t - 4 * i;
+      if (d == 0) p0 -= 1.0f;
+      if (d == 1) p1 -= 1.0f;
+      if (d == 2) p2 -= 1.0f;
+      if (d == 3) p3 -= 1.0f;
+      uint2 pk;
+      bf162* h = reinterpret_cast<bf162*>(&pk);
+      h[0] = __floats2bfloat162_rn(p0 * scale, p1 * scale);
+      h[1] = __floats2bfloat162_rn(p2 * scale, p3 * scale);
+      *reinterpret_cast<uint2*>(drow + 4 * i) = pk;
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += CE_THREADS) {
+      float p = __expf(row[i] - m) * inv;
+      if (i == t) p -= 1.0f;
+      drow[i] = __float2bfloat16_rn(p * scale);
+    }
   }
 }
 
@@ -303,83 +321,148 @@ __global__ void embed_bwd_kernel(const int32_t* __restrict__ tok, const float* _
 //   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g
 //   upd = (m / bc1) / (sqrt(v / bc2) + eps) + wd * w;  w -= lr * upd
 // g is the accumulated gradient times gscale (unscale and clip factors).
-__global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
-                             float* __restrict__ m, float* __restrict__ v, bf16* __restrict__ w16,
-                             long long n, float lr, float b1, float b2, float eps, float wd,
-                             float inv_bc1, float inv_bc2, float gscale) {
-  pdl_trigger();
-  pdl_wait();
-  const float ob1 = 1.0f - b1, ob2 = 1.0f - b2;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float gi = g[i] * gscale;
-    float mi = m[i] * b1;
+struct AdamElt {
+  float lr, b1, b2, ob1, ob2, eps, inv_bc1, inv_bc2, gscale, wd;
+  __device__ __forceinline__ void step(float& w, float g, float& m, float& v) const {
+    const float gi = g * gscale;
+    float mi = m * b1;
     mi = gi * ob1 + mi;
-    float vi = v[i] * b2;
+    float vi = v * b2;
     vi = (gi * gi) * ob2 + vi;
     const float mh = mi * inv_bc1;
     const float vh = sqrtf(vi * inv_bc2) + eps;
     float upd = mh / vh;
-    upd = w[i] * wd + upd;
-    const float wi = upd * (-lr) + w[i];
+    upd = w * wd + upd;
+    w = upd * (-lr) + w;
+    m = mi;
+    v = vi;
+  }
+};
+
+// ------------------------------------------------------------ chunked multi-tensor forms
+// Every trainable tensor is cut into chunks of OPT_CHUNK elements and one
+// 256-thread block owns one chunk, so all blocks stream the same number of
+// bytes whatever the tensor sizes (the gains are 128..1024 elements, the
+// tied embedding 1.5e8).  Chunks whose four pointers are 16-byte aligned use
+// float4 loads and stores.
+__device__ __forceinline__ double block_sum256_d(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  double t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.0;
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  return t;   // valid in thread 0
+}
+
+// Sum of squares of every gradient (train.m:805-826).  Each block writes its
+// chunk's partial sum; the block that finishes last (ticket) adds the partials
+// in chunk order (deterministic), and writes
+//   norm_out[0] = sqrt(sum) * grad_scale              (pre-clip global norm)
+//   norm_out[1] = grad_scale * min(1, clip / norm)    (factor AdamW applies)
+__global__ void __launch_bounds__(256)
+sumsq_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict__ chunks,
+                    int nchunks, float* __restrict__ partial, unsigned* __restrict__ ticket,
+                    float grad_scale, float grad_clip, float* __restrict__ norm_out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ int last;
+  const OptChunk c = chunks[blockIdx.x];
+  const AdamSeg sg = segs[c.seg];
+  const int n = (int)min((long long)OPT_CHUNK, sg.n - c.off);
+  const float* g = sg.g + c.off;
+  float acc = 0.f;
+  if (c.vec) {
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (n >> 2); i += 256) {
+      const float4 x = g4[i];
+      acc += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    }
+    for (int i = (n & ~3) + threadIdx.x; i < n; i += 256) acc += g[i] * g[i];
+  } else {
+    for (int i = threadIdx.x; i < n; i += 256) acc += g[i] * g[i];
+  }
+  acc = block_sum256(acc, red);
+  if (threadIdx.x == 0) {
+    partial[blockIdx.x] = acc;
+    __threadfence();
+    last = (atomicAdd(ticket, 1u) == (unsigned)nchunks - 1u);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  double s = 0.0;
+  for (int i = threadIdx.x; i < nchunks; i += 256) s += (double)__ldcg(partial + i);
+  s = block_sum256_d(s, redd);
+  if (threadIdx.x == 0) {
+    const float norm = (float)(sqrt(s) * (double)grad_scale);
+    float scale = grad_scale;
+    if (grad_clip > 0.f && norm > grad_clip) scale *= grad_clip / norm;
+    norm_out[0] = norm;
+    norm_out[1] = scale;
+  }
+}
+
+// AdamW over every chunk; the gradient factor is norm_out[1] (written by
+// sumsq_chunks_kernel earlier on the same stream).
+__global__ void __launch_bounds__(256)
+adamw_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict__ chunks,
+                    float lr, float b1, float b2, float eps, float inv_bc1, float inv_bc2,
+                    const float* __restrict__ norm_out) {
+  pdl_trigger();
+  pdl_wait();
+  const OptChunk c = chunks[blockIdx.x];
+  const AdamSeg sg = segs[c.seg];
+  const int n = (int)min((long long)OPT_CHUNK, sg.n - c.off);
+  const AdamElt a{lr, b1, b2, 1.0f - b1, 1.0f - b2, eps, inv_bc1, inv_bc2, norm_out[1], sg.wd};
+  float* w = sg.w + c.off;
+  const float* g = sg.g + c.off;
+  float* m = sg.m + c.off;
+  float* v = sg.v + c.off;
+  bf16* w16 = sg.w16 ? sg.w16 + c.off : nullptr;
+  int i0 = 0;
+  if (c.vec) {
+    float4* w4 = reinterpret_cast<float4*>(w);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+#pragma unroll 2
+    for (int i = threadIdx.x; i < (n >> 2); i += 256) {
+      float4 wv = w4[i], mv = m4[i], vv = v4[i];
+      const float4 gv = g4[i];
+      a.step(wv.x, gv.x, mv.x, vv.x);
+      a.step(wv.y, gv.y, mv.y, vv.y);
+      a.step(wv.z, gv.z, mv.z, vv.z);
+      a.step(wv.w, gv.w, mv.w, vv.w);
+      w4[i] = wv;
+      m4[i] = mv;
+      v4[i] = vv;
+      if (w16) {
+        uint2 pk;
+        bf162* h = reinterpret_cast<bf162*>(&pk);
+        h[0] = __floats2bfloat162_rn(wv.x, wv.y);
+        h[1] = __floats2bfloat162_rn(wv.z, wv.w);
+        *reinterpret_cast<uint2*>(w16 + 4 * i) = pk;
+      }
+    }
+    i0 = n & ~3;
+  }
+  for (int i = i0 + threadIdx.x; i < n; i += 256) {
+    float wi = w[i], mi = m[i], vi = v[i];
+    a.step(wi, g[i], mi, vi);
     w[i] = wi;
     m[i] = mi;
     v[i] = vi;
     if (w16) w16[i] = __float2bfloat16_rn(wi);
   }
-}
-
-// ------------------------------------------------------------ multi-tensor forms
-// One launch over every trainable tensor: blockIdx.y selects the tensor.
-__global__ void adamw_multi_kernel(const AdamSeg* __restrict__ segs, float lr, float b1, float b2,
-                                   float eps, float inv_bc1, float inv_bc2, float gscale) {
-  pdl_trigger();
-  pdl_wait();
-  const AdamSeg sg = segs[blockIdx.y];
-  const float ob1 = 1.0f - b1, ob2 = 1.0f - b2;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < sg.n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float gi = sg.g[i] * gscale;
-    float mi = sg.m[i] * b1;
-    mi = gi * ob1 + mi;
-    float vi = sg.v[i] * b2;
-    vi = (gi * gi) * ob2 + vi;
-    const float mh = mi * inv_bc1;
-    const float vh = sqrtf(vi * inv_bc2) + eps;
-    float upd = mh / vh;
-    upd = sg.w[i] * sg.wd + upd;
-    const float wi = upd * (-lr) + sg.w[i];
-    sg.w[i] = wi;
-    sg.m[i] = mi;
-    sg.v[i] = vi;
-    if (sg.w16) sg.w16[i] = __float2bfloat16_rn(wi);
-  }
-}
-
-__global__ void sumsq_multi_kernel(const AdamSeg* __restrict__ segs, double* __restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ float red[32];
-  const AdamSeg sg = segs[blockIdx.y];
-  float acc = 0.f;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < sg.n;
-       i += (long long)gridDim.x * blockDim.x)
-    acc += sg.g[i] * sg.g[i];
-  acc = block_sum256(acc, red);
-  if (threadIdx.x == 0) atomicAdd(out, (double)acc);
-}
-
-// ------------------------------------------------------------ sum of squares
-__global__ void sumsq_kernel(const float* __restrict__ g, long long n, double* __restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ float red[32];
-  float acc = 0.f;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    acc += g[i] * g[i];
-  acc = block_sum256(acc, red);
-  if (threadIdx.x == 0) atomicAdd(out, (double)acc);
 }
 
 // fp32 -> bf16 elementwise copy
@@ -412,10 +495,11 @@ cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, 
                   dx, dx16, dw);
 }
 
-cudaError_t launch_ce_rows(const float* logits, const int32_t* tgt, int rows, int V, float scale,
-                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st) {
-  return launch_k(ce_rows_kernel, dim3(rows), dim3(1024), 0, st, logits, tgt, V, scale, loss,
-                  dlogits, status);
+cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_ld,
+                           const int32_t* tgt, int rows, int V, float scale, float* loss,
+                           __nv_bfloat16* dlogits, int* status, cudaStream_t st) {
+  return launch_k(ce_rows_kernel, dim3(rows), dim3(CE_THREADS), 0, st, logits, stats, stats_ld,
+                  tgt, V, scale, loss, dlogits, status);
 }
 
 cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
@@ -438,31 +522,20 @@ cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, 
   return launch_k(embed_bwd_kernel, dim3(M), dim3(256), 0, st, tok, dx, V, D, dE);
 }
 
-cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bfloat16* w16,
-                         long long n, float lr, float b1, float b2, float eps, float wd,
-                         float inv_bc1, float inv_bc2, float gscale, cudaStream_t st) {
-  return launch_k(adamw_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, w, g, m, v, w16, n, lr,
-                  b1, b2, eps, wd, inv_bc1, inv_bc2, gscale);
+cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
+                                float* partial, unsigned* ticket, float grad_scale,
+                                float grad_clip, float* norm_out, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(unsigned), st);
+  if (e != cudaSuccess) return e;
+  return launch_k(sumsq_chunks_kernel, dim3(nchunks), dim3(256), 0, st, segs, chunks, nchunks,
+                  partial, ticket, grad_scale, grad_clip, norm_out);
 }
 
-cudaError_t launch_adamw_multi(const AdamSeg* d_segs, int nseg, long long max_n, float lr,
-                               float b1, float b2, float eps, float inv_bc1, float inv_bc2,
-                               float gscale, cudaStream_t st) {
-  const long long per = (max_n + 1023) / 1024;   // ~4 elements per thread for the largest
-  const int gx = (int)(per < 2048 ? (per < 1 ? 1 : per) : 2048);
-  return launch_k(adamw_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, lr, b1, b2, eps,
-                  inv_bc1, inv_bc2, gscale);
-}
-
-cudaError_t launch_sumsq_multi(const AdamSeg* d_segs, int nseg, long long max_n, double* out,
-                               cudaStream_t st) {
-  const long long per = (max_n + 1023) / 1024;
-  const int gx = (int)(per < 2048 ? (per < 1 ? 1 : per) : 2048);
-  return launch_k(sumsq_multi_kernel, dim3(gx, nseg), dim3(256), 0, st, d_segs, out);
-}
-
-cudaError_t launch_sumsq(const float* g, long long n, double* out, cudaStream_t st) {
-  return launch_k(sumsq_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, g, n, out);
+cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
+                                float lr, float b1, float b2, float eps, float inv_bc1,
+                                float inv_bc2, const float* norm_out, cudaStream_t st) {
+  return launch_k(adamw_chunks_kernel, dim3(nchunks), dim3(256), 0, st, segs, chunks, lr, b1, b2,
+                  eps, inv_bc1, inv_bc2, norm_out);
 }
 
 cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st) {

@@ -646,7 +646,7 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
 
 NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   if (!ctx || !d || !d->a || !d->b || !d->out || d->M <= 0 || d->N <= 0 || d->K <= 0 ||
-      d->epi < 0 || d->epi > 6)
+      d->epi < 0 || d->epi > 7)
     return NE_ERR_INVALID;
   if (d->K % 64) return fail(ctx, NE_ERR_UNSUPPORTED, "K must be a multiple of 64");
   if (d->a_mn && !d->b_mn) return fail(ctx, NE_ERR_UNSUPPORTED, "MN-major A needs MN-major B");
@@ -658,6 +658,7 @@ NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   c.bn = d->bn; c.half_out = d->half_out; c.splits = 1;
   if (d->epi == EPI_ADD) c.aux3 = d->aux0;
   if (d->epi == EPI_SWIGLU_BWD) { c.aux3 = d->aux0; c.aux1 = const_cast<void*>(d->aux1); c.aux_ld = d->aux_ld; }
+  if (d->epi == EPI_F32_STATS) { c.aux1 = const_cast<void*>(d->aux0); c.aux_ld = d->aux_ld; }
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
   return NE_OK;

@@ -16,6 +16,7 @@ enum GemmEpi : int {
   EPI_SWIGLU = 4,  // bf16 silu(h1)*h3 from a W1/W3 16-row-interleaved operand
   EPI_ADD = 5,     // fp32 out[m][n] = in[m][n] + alpha * acc
   EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and saved h1, h3
+  EPI_F32_STATS = 7,   // fp32 row-major + per-32-column (max, sum exp) into aux1 [m][aux_ld]
 };
 
 struct GemmCall {
@@ -99,11 +100,21 @@ struct AdamSeg {
   long long n;
   float wd;
 };
-cudaError_t launch_adamw_multi(const AdamSeg* d_segs, int nseg, long long max_n, float lr,
-                               float b1, float b2, float eps, float inv_bc1, float inv_bc2,
-                               float gscale, cudaStream_t st);
-cudaError_t launch_sumsq_multi(const AdamSeg* d_segs, int nseg, long long max_n, double* out,
-                               cudaStream_t st);
+// One chunk of at most OPT_CHUNK elements of segment `seg`, starting at `off`;
+// vec = 1 when the segment's four fp32 pointers are 16-byte aligned (and its
+// bf16 copy 8-byte aligned), so the chunk may use vector accesses.
+constexpr int OPT_CHUNK = 16384;
+struct OptChunk {
+  int seg;
+  int vec;
+  long long off;
+};
+cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
+                                float* partial, unsigned* ticket, float grad_scale,
+                                float grad_clip, float* norm_out, cudaStream_t st);
+cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
+                                float lr, float b1, float b2, float eps, float inv_bc1,
+                                float inv_bc2, const float* norm_out, cudaStream_t st);
 cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* V, const __nv_bfloat16* O,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
@@ -112,8 +123,9 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
                                int D, const float* residual, float* dx, __nv_bfloat16* dx16,
                                float* dw, cudaStream_t st);
-cudaError_t launch_ce_rows(const float* logits, const int32_t* tgt, int rows, int V, float scale,
-                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st);
+cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_ld,
+                           const int32_t* tgt, int rows, int V, float scale, float* loss,
+                           __nv_bfloat16* dlogits, int* status, cudaStream_t st);
 cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
                                const float* qkv_raw, const float* qn, const float* kn,
                                float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
@@ -121,10 +133,6 @@ cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV
                                cudaStream_t st);
 cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, int D, float* dE,
                              cudaStream_t st);
-cudaError_t launch_adamw(float* w, const float* g, float* m, float* v, __nv_bfloat16* w16,
-                         long long n, float lr, float b1, float b2, float eps, float wd,
-                         float inv_bc1, float inv_bc2, float gscale, cudaStream_t st);
-cudaError_t launch_sumsq(const float* g, long long n, double* out, cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st);
 
 }  // namespace ne

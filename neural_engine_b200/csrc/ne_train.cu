@@ -61,7 +61,11 @@ struct TrainState {
   std::vector<Seg> segs;
   AdamSeg* d_segs = nullptr;             // device copy of the segment table
   float d_segs_wd = -2.f;                // weight decay the device table holds
-  long long max_seg = 0;
+  OptChunk* d_chunks = nullptr;          // optimizer work list (chunks of OPT_CHUNK elements)
+  int nchunks = 0;
+  float* opt_partial = nullptr;          // [nchunks] per-chunk sums of squares
+  unsigned* opt_ticket = nullptr;        // last-block ticket of the norm kernel
+  float* norm_out = nullptr;             // [2] pre-clip norm, gradient factor
   float* grad_pool = nullptr;            // start of the gradients inside `pool`
   size_t grad_floats = 0;
   std::vector<TrainLayerP> P;
@@ -74,6 +78,7 @@ struct TrainState {
         *dV = nullptr, *Dl = nullptr, *logits = nullptr, *loss_rows = nullptr;
   __nv_bfloat16 *dY16 = nullptr, *dX216 = nullptr, *DH13 = nullptr, *dO = nullptr,
                 *DQKV = nullptr, *dlogits = nullptr;
+  float2* ce_stats = nullptr;            // [Mc, ceil(V/32)] classifier softmax statistics
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
@@ -83,6 +88,10 @@ void free_train(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return;
   TrainState* t = ctx->train;
   if (t->d_segs) cudaFree(t->d_segs);
+  if (t->d_chunks) cudaFree(t->d_chunks);
+  if (t->opt_partial) cudaFree(t->opt_partial);
+  if (t->opt_ticket) cudaFree(t->opt_ticket);
+  if (t->norm_out) cudaFree(t->norm_out);
   if (t->pool) cudaFree(t->pool);
   if (t->act_pool) cudaFree(t->act_pool);
   delete t;
@@ -184,7 +193,14 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   t->B = B;
   t->S = S;
   t->M = (int)M;
-  t->Mc = (int)std::min<long long>(M, 2048);
+  // classifier rows per chunk: fp32 logits + bf16 dlogits + statistics of one
+  // chunk stay within 4 GB (multiples of 128 rows, at least 128)
+  {
+    const long long per_row = (long long)m.vocab * 6 + ((m.vocab + 31) / 32) * 8;
+    long long mc = (4LL << 30) / per_row;
+    mc = std::max<long long>(128, mc / 128 * 128);
+    t->Mc = (int)std::min<long long>(M, mc);
+  }
   const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
                kvd = (size_t)m.kv_heads * m.head_dim, qkv = qd + 2 * kvd, V = m.vocab,
                hd = m.head_dim, L = m.n_layers;
@@ -292,6 +308,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   const size_t oloss = take(Mx * 4), odY16 = take(Mx * D * 2), odX216 = take(Mx * D * 2);
   const size_t oDH13 = take(Mx * 2 * F * 2), odO = take(Mx * qd * 2), oDQKV = take(Mx * qkv * 2);
   const size_t odl = take((size_t)t->Mc * V * 2), oids = take(Mx * 4), otgt = take(Mx * 4);
+  const size_t ostats = take((size_t)t->Mc * ((V + 31) / 32) * 8);
   const size_t otok = take((size_t)B * (S + 1) * 4), ored = take(64);
   uint8_t* base = nullptr;
   if ((s = dalloc(ctx, &base, bytes)) != NE_OK) return s;
@@ -315,6 +332,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   t->dX216 = (__nv_bfloat16*)(base + odX216); t->DH13 = (__nv_bfloat16*)(base + oDH13);
   t->dO = (__nv_bfloat16*)(base + odO); t->DQKV = (__nv_bfloat16*)(base + oDQKV);
   t->dlogits = (__nv_bfloat16*)(base + odl); t->ids = (int32_t*)(base + oids);
+  t->ce_stats = (float2*)(base + ostats);
   t->tgt = (int32_t*)(base + otgt); t->tok = (int32_t*)(base + otok);
   t->red = (double*)(base + ored);
   return ne_sync(ctx);
@@ -419,10 +437,13 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   for (int r0 = 0; r0 < M; r0 += t->Mc) {
     const int rows = std::min(t->Mc, M - r0);
     const __nv_bfloat16* xnf = t->XNF + (size_t)r0 * D;
-    if ((s = gemm(ctx, gc(xnf, D, rows, 0, ctx->embed, D, V, 0, D, EPI_F32, t->logits, V))) !=
-        NE_OK)
-      return s;
-    NE_LAUNCH(launch_ce_rows(t->logits, t->tgt + r0, rows, V, ce_scale, t->loss_rows + r0,
+    const int nck = (V + 31) / 32;
+    GemmCall cl = gc(xnf, D, rows, 0, ctx->embed, D, V, 0, D, EPI_F32_STATS, t->logits, V);
+    cl.aux1 = t->ce_stats;
+    cl.aux_ld = nck;
+    if ((s = gemm(ctx, cl)) != NE_OK) return s;
+    NE_LAUNCH(launch_ce_rows(t->logits, t->ce_stats, nck, t->tgt + r0, rows, V, ce_scale,
+                             t->loss_rows + r0,
                              t->dlogits, ctx->d_status, st));
     // dXNF = dlogits . E   (E read MN-major as [V (K), D (N)])
     if ((s = gemm(ctx, gc(t->dlogits, V, rows, 0, ctx->embed, D, D, 1, V, EPI_F32,
@@ -512,13 +533,28 @@ NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floa
 // Upload the segment table (with the weight decay of this step) when it changed.
 static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
   TrainState* t = ctx->train;
+  if (!t->d_chunks) {
+    std::vector<OptChunk> hc;
+    for (size_t k = 0; k < t->segs.size(); ++k) {
+      const Seg& sg = t->segs[k];
+      auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+      const int vec = a16(sg.w) && a16(sg.g) && a16(sg.m) && a16(sg.v) &&
+                      (reinterpret_cast<uintptr_t>(sg.w16) & 7u) == 0;
+      for (long long off = 0; off < sg.n; off += OPT_CHUNK) hc.push_back({(int)k, vec, off});
+    }
+    t->nchunks = (int)hc.size();
+    ne_status s;
+    if ((s = dalloc(ctx, &t->d_chunks, hc.size())) != NE_OK ||
+        (s = dalloc(ctx, &t->opt_partial, hc.size())) != NE_OK ||
+        (s = dalloc(ctx, &t->opt_ticket, 1)) != NE_OK || (s = dalloc(ctx, &t->norm_out, 2)) != NE_OK)
+      return s;
+    NE_CUDA(cudaMemcpyAsync(t->d_chunks, hc.data(), hc.size() * sizeof(OptChunk),
+                            cudaMemcpyHostToDevice, ctx->st));
+  }
   if (t->d_segs && t->d_segs_wd == weight_decay) return NE_OK;
   std::vector<AdamSeg> hs;
-  t->max_seg = 0;
-  for (const Seg& sg : t->segs) {
+  for (const Seg& sg : t->segs)
     hs.push_back({sg.w, sg.g, sg.m, sg.v, sg.w16, sg.n, sg.wd < 0.f ? weight_decay : 0.f});
-    t->max_seg = std::max(t->max_seg, sg.n);
-  }
   if (!t->d_segs) {
     ne_status s = dalloc(ctx, &t->d_segs, hs.size());
     if (s != NE_OK) return s;
@@ -530,21 +566,16 @@ static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
   return NE_OK;
 }
 
+// Global gradient norm (train.m:805-826), times grad_scale; synchronises.
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm) {
   if (!ctx || !ctx->train || !h_norm) return NE_ERR_STATE;
   TrainState* t = ctx->train;
-  if (!t->d_segs) {
-    ne_status s0 = upload_segs(ctx, 0.f);
-    if (s0 != NE_OK) return s0;
-  }
-  NE_CUDA(cudaMemsetAsync(t->red, 0, sizeof(double), ctx->st));
-  NE_LAUNCH(launch_sumsq_multi(t->d_segs, (int)t->segs.size(), t->max_seg, t->red, ctx->st));
-  double ss = 0;
-  NE_CUDA(cudaMemcpyAsync(&ss, t->red, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
-  ne_status s = ne_sync(ctx);
+  ne_status s = upload_segs(ctx, t->d_segs ? t->d_segs_wd : 0.f);
   if (s != NE_OK) return s;
-  *h_norm = (float)(std::sqrt(ss) * grad_scale);
-  return NE_OK;
+  NE_LAUNCH(launch_sumsq_chunks(t->d_segs, t->d_chunks, t->nchunks, t->opt_partial, t->opt_ticket,
+                                grad_scale, 0.f, t->norm_out, ctx->st));
+  NE_CUDA(cudaMemcpyAsync(h_norm, t->norm_out, sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  return ne_sync(ctx);
 }
 
 // AdamW over every trainable tensor (train.m:782-897, cpu_ops.h:266-303):
@@ -552,22 +583,27 @@ NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm
 // global norm of the result is clipped to cfg->grad_clip (when > 0), then
 // decoupled AdamW with bias correction at step t (1-based); weight decay on
 // matrices and the embedding, none on the gains.  Gradients are zeroed
-// afterwards.  *h_grad_norm (optional) receives the pre-clip norm.
+// afterwards.  The norm and the clip factor stay on the device (no host round
+// trip between them and the update); *h_grad_norm, when not NULL, receives
+// the pre-clip norm, which makes this call wait for the step to finish.
 NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, float* h_grad_norm) {
   if (!ctx || !ctx->train || !cfg || t_step <= 0) return NE_ERR_INVALID;
   TrainState* t = ctx->train;
-  float norm = 0.f;
-  ne_status s = ne_train_grad_norm(ctx, cfg->grad_scale, &norm);
+  ne_status s = upload_segs(ctx, cfg->weight_decay);
   if (s != NE_OK) return s;
-  if (h_grad_norm) *h_grad_norm = norm;
-  float gscale = cfg->grad_scale;
-  if (cfg->grad_clip > 0.f && norm > cfg->grad_clip) gscale *= cfg->grad_clip / norm;
   const float bc1 = 1.0f - std::pow(cfg->beta1, (float)t_step);
   const float bc2 = 1.0f - std::pow(cfg->beta2, (float)t_step);
-  if ((s = upload_segs(ctx, cfg->weight_decay)) != NE_OK) return s;
-  NE_LAUNCH(launch_adamw_multi(t->d_segs, (int)t->segs.size(), t->max_seg, cfg->lr, cfg->beta1,
-                               cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, gscale, ctx->st));
-  return ne_train_zero_grads(ctx);
+  NE_LAUNCH(launch_sumsq_chunks(t->d_segs, t->d_chunks, t->nchunks, t->opt_partial, t->opt_ticket,
+                                cfg->grad_scale, cfg->grad_clip, t->norm_out, ctx->st));
+  NE_LAUNCH(launch_adamw_chunks(t->d_segs, t->d_chunks, t->nchunks, cfg->lr, cfg->beta1,
+                                cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, t->norm_out, ctx->st));
+  if ((s = ne_train_zero_grads(ctx)) != NE_OK) return s;
+  if (h_grad_norm) {
+    NE_CUDA(cudaMemcpyAsync(h_grad_norm, t->norm_out, sizeof(float), cudaMemcpyDeviceToHost,
+                            ctx->st));
+    return ne_sync(ctx);
+  }
+  return NE_OK;
 }
 
 // Learning-rate schedule of train.m:851-858: linear warmup, then cosine decay

@@ -315,8 +315,13 @@ class Engine:
         return float(out.value)
 
     def adamw_step(self, t: int, lr: float, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
-                   grad_clip=1.0, grad_scale=1.0) -> float:
+                   grad_clip=1.0, grad_scale=1.0, return_norm: bool = True):
+        """One optimizer step; returns the pre-clip gradient norm (waits for the
+        step) or, with return_norm=False, None without waiting."""
         cfg = AdamCfgC(lr, beta1, beta2, eps, weight_decay, grad_clip, grad_scale)
+        if not return_norm:
+            self._check(self.lib.ne_adamw_step(self._ctx, C.byref(cfg), int(t), None))
+            return None
         norm = C.c_float(0)
         self._check(self.lib.ne_adamw_step(self._ctx, C.byref(cfg), int(t), C.byref(norm)))
         return float(norm.value)

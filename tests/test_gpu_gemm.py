@@ -205,3 +205,30 @@ def test_gemm_swiglu_backward_epilogue(eng):
     tol = 2 ** -7 * max(r1.abs().max().item(), r3.abs().max().item()) + 1e-3
     assert (got1 - r1).abs().max().item() <= tol
     assert (got3 - r3).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("M,N", [(256, 1024), (200, 1000), (128, 151936 // 64)])
+def test_gemm_softmax_statistics_epilogue(eng, M, N):
+    """epi 7 (classifier logits): fp32 logits plus per-(row, 32-column chunk)
+    (max, sum exp(x - max)) over the columns < N; combining a row's chunks
+    gives its log-sum-exp."""
+    K = 128
+    a, b = _bf16((M, K), 31), _bf16((N, K), 32, 0.3)
+    da, db = a.cuda(), b.cuda()
+    nck = (N + 31) // 32
+    out = torch.full((M, N), float("nan"), device="cuda")
+    stats = torch.full((M, nck, 2), float("nan"), device="cuda")
+    eng.gemm(da.data_ptr(), K, M, db.data_ptr(), K, N, K, 7, out.data_ptr(), N,
+             aux0=stats.data_ptr(), aux_ld=nck)
+    eng.sync()
+    ref = _ref(a, b)
+    assert (out.cpu().double() - ref).abs().max().item() <= _tol(a, b, K)
+    st = stats.cpu().double()
+    pad = torch.full((M, nck * 32 - N), float("-inf"), dtype=torch.float64)
+    chunks = torch.cat([ref, pad], 1).reshape(M, nck, 32)
+    cmax = chunks.max(-1).values
+    csum = torch.exp(chunks - cmax[..., None]).sum(-1)
+    assert (st[..., 0] - cmax).abs().max().item() <= _tol(a, b, K)
+    assert ((st[..., 1] - csum).abs() / csum).max().item() <= 1e-4
+    lse = (st[..., 0] + torch.log(st[..., 1])).logsumexp(-1)
+    assert (lse - torch.logsumexp(ref, -1)).abs().max().item() <= 1e-4
