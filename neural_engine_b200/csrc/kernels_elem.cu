@@ -114,6 +114,43 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
   rmsnorm_row_store(xs, g, D, eps, xn + (size_t)r * D, red);
 }
 
+// Norm only (nsplit == 0), one warp per row: each lane holds V4 float4 of the
+// row (lane-contiguous, so every load instruction is coalesced), the sum of
+// squares is a warp reduction, no block barrier.  Same arithmetic as
+// rmsnorm_row_store.
+template <int V4>
+__global__ void __launch_bounds__(256)
+rmsnorm_rows_kernel(const float* __restrict__ x, int rows, const float* __restrict__ g,
+                    float eps, __nv_bfloat16* __restrict__ xn) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int D = V4 * 128;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * D);
+  float4 v[V4];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < V4; ++k) {
+    v[k] = xr[lane + 32 * k];
+    ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+  }
+  ss = warp_sum(ss);
+  const float rms = sqrtf(ss / (float)D + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  uint2* out = reinterpret_cast<uint2*>(xn + (size_t)r * D);
+#pragma unroll
+  for (int k = 0; k < V4; ++k) {
+    const float4 gg = g4[lane + 32 * k];
+    uint2 pk;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+    h[0] = __floats2bfloat162_rn((v[k].x / rms) * gg.x, (v[k].y / rms) * gg.y);
+    h[1] = __floats2bfloat162_rn((v[k].z / rms) * gg.z, (v[k].w / rms) * gg.w);
+    out[lane + 32 * k] = pk;
+  }
+}
+
 // ---------------------------------------------------------------- QKV post
 // One warp per (row, head-vector).  Head vectors per row: Hq + 2*Hkv (q, k, v).
 // qkv row layout (the fused projection's output): [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].
@@ -281,6 +318,17 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
                                  int rows, cudaStream_t st) {
+  if (nsplit == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(g) & 15) == 0 && (reinterpret_cast<uintptr_t>(xn) & 7) == 0) {
+    const dim3 grid((rows + 7) / 8);
+    switch (D) {
+      case 512: return launch_k(rmsnorm_rows_kernel<4>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
+      case 768: return launch_k(rmsnorm_rows_kernel<6>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
+      case 1024: return launch_k(rmsnorm_rows_kernel<8>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
+      case 2048: return launch_k(rmsnorm_rows_kernel<16>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
+      default: break;
+    }
+  }
   const int threads = D >= 1024 ? 256 : 128;
   const size_t smem = (size_t)(D + 32) * sizeof(float);
   return launch_k(resid_rmsnorm_kernel, dim3(rows), dim3(threads), smem, st, x, P, nsplit,

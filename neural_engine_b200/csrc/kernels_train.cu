@@ -45,7 +45,7 @@ __device__ __forceinline__ float block_sum256(float v, float* red) {
 // ------------------------------------------------------------ RMSNorm backward
 // One warp per row (no block barriers in the row reductions); 8 warps per
 // block walk RB_ROWS rows each and reduce their dw partials once per block.
-constexpr int RB_ROWS = 4;
+constexpr int RB_ROWS = 2;
 template <int PER>
 __global__ void __launch_bounds__(256)
 rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
