@@ -102,8 +102,18 @@ NE_API ne_status ne_set_layer_weights(ne_ctx* ctx, int layer, const float* h_wq,
 NE_API ne_status ne_set_global_weights(ne_ctx* ctx, const float* h_rms_final, const float* h_embed);
 
 /* v4 checkpoint (train.m:97-165 save/load_checkpoint; config.h:83-91).  The
- * header's model fields must match the context's configuration. */
+ * header's model fields must match the context's configuration.  Without
+ * training state the weights are loaded (Adam moments skipped); after
+ * ne_train_alloc the fp32 masters, gains and Adam moments are restored exactly
+ * (resume), and the bf16 compute copies refreshed.  A file without the QKN1
+ * block gives unit QK-norm gains. */
 NE_API ne_status ne_load_ckpt_v4(ne_ctx* ctx, const char* path, ne_ckpt_info* info);
+/* Write the full training state (needs ne_train_alloc) in the reference's v4
+ * layout, byte for byte (train.m:97-131); the header takes step, total_steps,
+ * lr, loss, cum_*, adam_t (and seq_len if > 0) from info.  With QK-norm the
+ * QKN1 block follows (q_norm, k_norm per layer, then m, v of each), which v4
+ * readers ignore. */
+NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info);
 
 /* ---- token loop (tools/generate.py:113-228) ------------------------------
  * Allocates the fp16 KV cache and the decode / prefill workspaces for up to
@@ -242,13 +252,68 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t, float
 /* Warmup + cosine learning rate of train.m:851-858. */
 NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_steps,
                             float min_lr_frac);
-/* Copy a layer's gradients (which 0) or fp32 masters (which 1) to host in the
- * v4 layout; layer -1 gives rms_final in h_rms_att and the embedding in h_wq.
- * NULL pointers are skipped. */
+/* Copy a layer's gradients (which 0), fp32 masters (1), Adam m (2) or Adam v
+ * (3) to host in the v4 layout; layer -1 gives rms_final in h_rms_att and the
+ * embedding in h_wq.  NULL pointers are skipped. */
 NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_wq, float* h_wk,
                                     float* h_wv, float* h_wo, float* h_w1, float* h_w2,
                                     float* h_w3, float* h_rms_att, float* h_rms_ffn,
                                     float* h_q_norm, float* h_k_norm);
+
+/* ---- per-layer entry points (the reference's kernel set) -----------------
+ * The reference drives one compiled ANE kernel per stage from train.m; these
+ * are the same stages on the training workspace of ne_train_alloc, enqueued
+ * on the context stream.  One micro-step is exactly
+ *   ne_embed_fwd(ctx, d_tokens);
+ *   for l = 0 .. L-1:  ne_attn_fwd(ctx, l); ne_ffn_fwd(ctx, l);
+ *   ne_lmhead_ce_fwd_bwd(ctx, d_loss);
+ *   for l = L-1 .. 0:  ne_ffn_bwd(ctx, l); ne_attn_bwd(ctx, l);
+ *   ne_embed_bwd(ctx);
+ * which is what ne_train_fwd_bwd_device runs.  Gradients accumulate. */
+/* embed_lookup (cpu_ops.h:433-439) + the first RMSNorm; d_tokens [B][S+1]. */
+NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens);
+/* sdpaFwd (mil_dynamic.h:57-234): QKV, QK-norm, RoPE, causal GQA SDPA, Wo,
+ * residual (io.h:25-37), FFN RMSNorm. */
+NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int layer);
+/* ffnFused (mil_dynamic.h:238-306): SwiGLU FFN, residual, next RMSNorm. */
+NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int layer);
+/* Classifier (train.m:495-505), cross_entropy_loss (cpu_ops.h:348-382),
+ * classifier backward, dense embedding gradient, final RMSNorm backward.
+ * d_loss (device, optional): the batch's mean loss. */
+NE_API ne_status ne_lmhead_ce_fwd_bwd(ne_ctx* ctx, float* d_loss);
+/* ffnBwdFull (mil_dynamic.h:320-409) + dW1/dW2/dW3 + rmsnorm_bwd_add. */
+NE_API ne_status ne_ffn_bwd(ne_ctx* ctx, int layer);
+/* wotBwd + sdpaBwd1/2 + RoPE/QK-norm backward + qkvBwd (mil_dynamic.h:412-707)
+ * + dWq/dWk/dWv/dWo + rmsnorm_bwd_add. */
+NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int layer);
+/* embed_backward (cpu_ops.h:441-447). */
+NE_API ne_status ne_embed_bwd(ne_ctx* ctx);
+/* Token-major RMSNorm on caller-owned device buffers (rmsnorm, cpu_ops.h:20-60):
+ * d_out [rows, dim] bf16.  And its backward (rmsnorm_bwd(_add),
+ * cpu_ops.h:108-261): d_dx = J^T d_dy (+ d_residual if not NULL); d_dw
+ * (optional) accumulates the gain gradient. */
+NE_API ne_status ne_rmsnorm_fwd(ne_ctx* ctx, const float* d_x, const float* d_w, int rows,
+                                void* d_out_bf16);
+NE_API ne_status ne_rmsnorm_bwd_add(ne_ctx* ctx, const float* d_dy, const float* d_x,
+                                    const float* d_w, int rows, const float* d_residual,
+                                    float* d_dx, float* d_dw);
+
+/* ---- data-parallel gradients (NCCL over NVLink; no reference counterpart:
+ * the reference trains on one device) ---------------------------------------
+ * Rank 0 makes an id with ne_comm_unique_id and shares it out of band; every
+ * rank calls ne_comm_init with it.  Afterwards each ne_train_fwd_bwd(_device)
+ * sums the gradients over ranks in buckets overlapped with its backward (one
+ * bucket per layer, issued as soon as the layer's gradients are final), so
+ * ne_adamw_step with grad_scale = 1/world takes the same step on every rank.
+ * With gradient accumulation, turn reduction off (ne_comm_set_reduce(ctx, 0))
+ * for all but the last micro-step of each optimizer step.  NCCL is loaded at
+ * run time (libnccl.so.2); NE_ERR_UNSUPPORTED if it cannot be. */
+#define NE_COMM_ID_BYTES 128
+NE_API ne_status ne_comm_unique_id(void* id_out);
+NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world);
+NE_API ne_status ne_comm_set_reduce(ne_ctx* ctx, int on);
+/* Sum the whole gradient pool over the ranks now (ordered on the stream). */
+NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx);
 
 /* The contiguous fp32 gradient pool (every trainable tensor's gradient), for
  * data-parallel reduction by the caller (e.g. an NCCL all-reduce on the

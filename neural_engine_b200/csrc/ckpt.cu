@@ -13,18 +13,11 @@
 #include <vector>
 
 #include "../../include/ne.h"
+#include "ne_ckpt.h"
 
 namespace {
 
-struct CkptHdr {
-  int magic, version, step, total_steps;
-  int n_layers, vocab_size, dim, hidden_dim, n_heads, seq_len;
-  float lr, loss;
-  double cum_compile, cum_train, cum_wall;
-  int cum_steps, cum_batches, adam_t;
-  int kv_heads, head_dim, q_dim;
-};
-static_assert(sizeof(CkptHdr) == 96, "v4 header must be 96 bytes");
+using ne::CkptHdr;
 
 struct File {
   FILE* f = nullptr;
@@ -44,6 +37,9 @@ bool skip_f32(FILE* f, size_t n) { return fseeko(f, (off_t)(n * 4), SEEK_CUR) ==
 
 extern "C" NE_API ne_status ne_load_ckpt_v4(ne_ctx* ctx, const char* path, ne_ckpt_info* info) {
   if (!ctx || !path) return NE_ERR_INVALID;
+  bool handled = false;
+  ne_status ts = ne::train_ckpt_load(ctx, path, info, &handled);
+  if (handled) return ts;
   ne_model_cfg m;
   if (ne_get_cfg(ctx, &m) != NE_OK) return NE_ERR_INVALID;
   File fh;

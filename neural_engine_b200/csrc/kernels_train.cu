@@ -10,7 +10,6 @@
 //                     dlogits = (softmax - onehot) * scale  (cpu_ops.h:348-382)
 //   qk_rope_bwd       inverse RoPE rotation (cpu_ops.h:479-506) then per-head
 //                     QK-RMSNorm backward; writes d(qkv) bf16 and gain grads
-//   embed_bwd         dE[tok] += dx  (cpu_ops.h:441-447)
 //   adamw             decoupled AdamW with bias correction (cpu_ops.h:266-303)
 //                     on fp32 masters, writing the bf16 compute copy
 //   sumsq             sum of squares for the global gradient norm (train.m:805-826)
@@ -305,17 +304,6 @@ __global__ void qk_rope_bwd_kernel(const float* __restrict__ dQ, const float* __
 }
 
 // ------------------------------------------------------------ embedding backward
-__global__ void embed_bwd_kernel(const int32_t* __restrict__ tok, const float* __restrict__ dx,
-                                 int V, int D, float* __restrict__ dE) {
-  pdl_trigger();
-  pdl_wait();
-  const int r = blockIdx.x;
-  const int t = tok[r];
-  if (t < 0 || t >= V) return;
-  for (int i = threadIdx.x; i < D; i += blockDim.x)
-    atomicAdd(dE + (size_t)t * D + i, dx[(size_t)r * D + i]);
-}
-
 // ------------------------------------------------------------ AdamW
 // cpu_ops.h:266-303, element by element in the same order:
 //   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g
@@ -517,10 +505,6 @@ cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, int D, float* dE,
-                             cudaStream_t st) {
-  return launch_k(embed_bwd_kernel, dim3(M), dim3(256), 0, st, tok, dx, V, D, dE);
-}
 
 cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float* partial, unsigned* ticket, float grad_scale,

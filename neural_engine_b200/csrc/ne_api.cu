@@ -362,6 +362,7 @@ NE_API void ne_free(ne_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->st);
+  comm_free(ctx);
   free_train(ctx);
   free_workspace(ctx);
   if (ctx->wpool) cudaFree(ctx->wpool);

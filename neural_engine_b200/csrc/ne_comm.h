@@ -1,0 +1,28 @@
+// ne_comm.h -- internal interface of the NCCL gradient exchange (comm.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "../../include/ne.h"
+
+namespace ne {
+
+struct Comm {
+  void* comm = nullptr;            // ncclComm_t
+  int rank = 0, world = 1;
+  cudaStream_t cs = nullptr;       // collective stream (highest priority)
+  std::vector<cudaEvent_t> ev;     // ring of ordering events
+  int next_ev = 0;
+  bool reduce = true;              // the training step reduces its gradients
+  void* gather = nullptr;          // all-gathered (token id, dY row) pairs
+  size_t gather_bytes = 0;
+};
+
+void comm_free(ne_ctx* ctx);
+ne_status comm_fence_in(ne_ctx* ctx);    // comm stream waits for the compute stream
+ne_status comm_fence_out(ne_ctx* ctx);   // compute stream waits for the comm stream
+ne_status comm_allreduce(ne_ctx* ctx, float* buf, size_t n);
+ne_status comm_allgather(ne_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank);
+
+}  // namespace ne

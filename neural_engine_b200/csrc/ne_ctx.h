@@ -18,6 +18,8 @@
 namespace ne {
 struct TrainState;                      // ne_train.cu
 void free_train(ne_ctx* ctx);           // ne_train.cu
+struct Comm;                            // comm.cu
+void comm_free(ne_ctx* ctx);            // comm.cu
 }  // namespace ne
 
 namespace ne {
@@ -50,6 +52,7 @@ struct ne_ctx {
   int* d_status = nullptr;
   int launches = 0;  // kernels enqueued by the current enqueue_* call
   ne::TrainState* train = nullptr;  // training buffers (ne_train_alloc)
+  ne::Comm* comm = nullptr;         // NCCL gradient exchange (ne_comm_init)
 
   // weights
   void* wpool = nullptr;

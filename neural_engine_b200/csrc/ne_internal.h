@@ -131,8 +131,11 @@ cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV
                                float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
                                int Hkv, int hd, __nv_bfloat16* dqkv, float* dqn, float* dkn,
                                cudaStream_t st);
-cudaError_t launch_embed_bwd(const int32_t* tok, const float* dx, int M, int V, int D, float* dE,
-                             cudaStream_t st);
+// Deterministic dE[tok[r]] += dy[r] over n rows (embed_bwd.cu); scratch of at
+// least embed_bwd_scratch_bytes(n) bytes.
+size_t embed_bwd_scratch_bytes(int n);
+cudaError_t launch_embed_bwd(const int32_t* tok, const float* dy, int n, int V, int D, float* dE,
+                             void* scratch, size_t scratch_bytes, int* status, cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st);
 
 }  // namespace ne

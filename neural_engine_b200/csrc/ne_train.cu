@@ -22,9 +22,12 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <vector>
 
 #include "../../include/ne.h"
+#include "ne_ckpt.h"
+#include "ne_comm.h"
 #include "ne_ctx.h"
 #include "ne_internal.h"
 
@@ -43,6 +46,7 @@ struct Seg {
 };
 
 struct TrainLayerP {
+  int seg0;                      // index of this layer's first segment in TrainState::segs
   float *wqkv, *wo, *w13, *w2;   // fp32 masters (device layout)
   float *gqkv, *go, *g13, *g2;   // gradients
   float *g_att, *g_ffn, *g_qn, *g_kn;
@@ -68,6 +72,8 @@ struct TrainState {
   float* norm_out = nullptr;             // [2] pre-clip norm, gradient factor
   float* grad_pool = nullptr;            // start of the gradients inside `pool`
   size_t grad_floats = 0;
+  size_t layer_grad_floats = 0;          // one layer's gradients (contiguous, layer order)
+  size_t tail_grad_off = 0;              // rms_final + embedding gradients follow the layers
   std::vector<TrainLayerP> P;
   float *embed_w = nullptr, *embed_g = nullptr, *rmsf_g = nullptr;
   std::vector<TrainActs> A;
@@ -79,6 +85,8 @@ struct TrainState {
   __nv_bfloat16 *dY16 = nullptr, *dX216 = nullptr, *DH13 = nullptr, *dO = nullptr,
                 *DQKV = nullptr, *dlogits = nullptr;
   float2* ce_stats = nullptr;            // [Mc, ceil(V/32)] classifier softmax statistics
+  void* embed_scratch = nullptr;         // sort buffers of the embedding backward
+  size_t embed_scratch_bytes = 0;
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
@@ -89,6 +97,7 @@ void free_train(ne_ctx* ctx) {
   TrainState* t = ctx->train;
   if (t->d_segs) cudaFree(t->d_segs);
   if (t->d_chunks) cudaFree(t->d_chunks);
+  if (t->embed_scratch) cudaFree(t->embed_scratch);
   if (t->opt_partial) cudaFree(t->opt_partial);
   if (t->opt_ticket) cudaFree(t->opt_ticket);
   if (t->norm_out) cudaFree(t->norm_out);
@@ -218,6 +227,8 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   float* pg = t->pool + total_w;
   t->grad_pool = pg;
   t->grad_floats = total_all;
+  t->layer_grad_floats = per_layer_all;
+  t->tail_grad_off = L * per_layer_all;
   float* pm = pg + total_all;
   float* pv = pm + total_all;
   size_t ow = 0, oa = 0;
@@ -244,6 +255,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   for (size_t l = 0; l < L; ++l) {
     LayerW& w = ctx->L[l];
     TrainLayerP& p = t->P[l];
+    p.seg0 = (int)t->segs.size();
     Seg a = seg(nullptr, w.wqkv, qkv * D, WD);
     Seg b = seg(nullptr, w.wo, D * qd, WD);
     Seg c = seg(nullptr, w.w13, 2 * F * D, WD);
@@ -386,65 +398,182 @@ NE_API ne_status ne_train_zero_grads(ne_ctx* ctx) {
   return NE_OK;
 }
 
-// Forward + backward of one batch d_tokens [B, S+1] (inputs tokens[:, :S],
-// targets tokens[:, 1:]); gradients ACCUMULATE into the gradient buffers
-// (mean cross-entropy over the B*S targets of this batch).  *d_loss (device,
-// optional) receives the batch's mean loss.
-NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
-  if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+// ---------------------------------------------------------------------------
+// Data-parallel hooks (active once ne_comm_init made a communicator of more
+// than one rank and ne_comm_set_reduce left reduction on).  Buckets follow the
+// backward: the tied-embedding + final-norm gradients right after the
+// classifier, then each layer's contiguous gradient slice as soon as its
+// attention backward finished, all on the comm stream while the compute
+// stream carries on with the layers below.
+static bool comm_active(const ne_ctx* ctx) {
+  return ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce;
+}
+
+static ne_status comm_after_lmhead(ne_ctx* ctx) {
+  if (!comm_active(ctx)) return NE_OK;
+  TrainState* t = ctx->train;
+  ne_status s = comm_fence_in(ctx);
+  if (s != NE_OK) return s;
+  return comm_allreduce(ctx, t->grad_pool + t->tail_grad_off, t->grad_floats - t->tail_grad_off);
+}
+
+static ne_status comm_after_layer(ne_ctx* ctx, int l) {
+  if (!comm_active(ctx)) return NE_OK;
+  TrainState* t = ctx->train;
+  ne_status s = comm_fence_in(ctx);
+  if (s != NE_OK) return s;
+  return comm_allreduce(ctx, t->grad_pool + (size_t)l * t->layer_grad_floats,
+                        t->layer_grad_floats);
+}
+
+// Deterministic scatter of n (token id, dY row) pairs into the embedding gradient.
+static ne_status embed_scatter(ne_ctx* ctx, const int32_t* ids, const float* dy, int n) {
+  TrainState* t = ctx->train;
+  const size_t need = embed_bwd_scratch_bytes(n);
+  if (t->embed_scratch_bytes < need) {
+    if (t->embed_scratch) NE_CUDA(cudaFree(t->embed_scratch));
+    t->embed_scratch = nullptr;
+    t->embed_scratch_bytes = 0;
+    uint8_t* p = nullptr;
+    ne_status s = dalloc(ctx, &p, need);
+    if (s != NE_OK) return s;
+    t->embed_scratch = p;
+    t->embed_scratch_bytes = need;
+  }
+  NE_LAUNCH(launch_embed_bwd(ids, dy, n, ctx->cfg.vocab, ctx->cfg.dim, t->embed_g, t->embed_scratch,
+                             t->embed_scratch_bytes, ctx->d_status, ctx->st));
+  return NE_OK;
+}
+
+// Input-embedding gradient.  Reduced: gather every rank's (token id, dY row)
+// pairs, wait for all buckets, then scatter-add all of them on every rank
+// (the dense part of the embedding gradient was already summed).
+static ne_status comm_embed_bwd(ne_ctx* ctx) {
   TrainState* t = ctx->train;
   const ne_model_cfg& m = ctx->cfg;
-  const int B = t->B, S = t->S, M = t->M, D = m.dim, F = m.hidden, Hq = m.n_heads,
-            Hkv = m.kv_heads, hd = m.head_dim, V = m.vocab;
-  const int qd = Hq * hd, kvd = Hkv * hd, qkv = qd + 2 * kvd;
-  const float alpha = m.res_alpha;
-  cudaStream_t st = ctx->st;
+  const int M = t->M, D = m.dim, V = m.vocab;
+  (void)V;
+  if (!comm_active(ctx)) return embed_scatter(ctx, t->ids, t->dY, M);
+  Comm* c = ctx->comm;
+  const size_t ids_bytes = ((size_t)c->world * M * 4 + 255) & ~(size_t)255;
+  const size_t need = ids_bytes + (size_t)c->world * M * D * 4;
+  if (c->gather_bytes < need) {
+    if (c->gather) NE_CUDA(cudaFree(c->gather));
+    c->gather = nullptr;
+    c->gather_bytes = 0;
+    uint8_t* g = nullptr;
+    ne_status s = dalloc(ctx, &g, need);
+    if (s != NE_OK) return s;
+    c->gather = g;
+    c->gather_bytes = need;
+  }
+  int32_t* ids_all = reinterpret_cast<int32_t*>(c->gather);
+  float* dy_all = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->gather) + ids_bytes);
   ne_status s;
-  NE_CUDA(cudaSetDevice(ctx->device));
+  if ((s = comm_fence_in(ctx)) != NE_OK) return s;
+  if ((s = comm_allgather(ctx, t->ids, ids_all, (size_t)M * 4)) != NE_OK) return s;
+  if ((s = comm_allgather(ctx, t->dY, dy_all, (size_t)M * D * 4)) != NE_OK) return s;
+  if ((s = comm_fence_out(ctx)) != NE_OK) return s;
+  return embed_scatter(ctx, ids_all, dy_all, c->world * M);
+}
+
+// ---------------------------------------------------------------------------
+// Per-layer entry points.  Each enqueues on the context stream and works on
+// the training workspace; the composition below (ne_train_fwd_bwd_device) is
+// the whole micro-step.  Activations saved for the backward pass live in
+// t->A[layer]; the running residual gradient is t->dY (fp32) / t->dY16 (bf16).
+
+#define NE_TRAIN_PRELUDE()                                                                   \
+  if (!ctx || !ctx->train) return NE_ERR_STATE;                                              \
+  TrainState* t = ctx->train;                                                                \
+  const ne_model_cfg& m = ctx->cfg;                                                          \
+  const int B = t->B, S = t->S, M = t->M, D = m.dim, F = m.hidden, Hq = m.n_heads,           \
+            Hkv = m.kv_heads, hd = m.head_dim, V = m.vocab;                                  \
+  const int qd = Hq * hd, kvd = Hkv * hd, qkv = qd + 2 * kvd;                                \
+  const float alpha = m.res_alpha;                                                           \
+  cudaStream_t st = ctx->st;                                                                 \
+  ne_status s = NE_OK;                                                                       \
+  (void)B; (void)S; (void)M; (void)D; (void)F; (void)Hq; (void)Hkv; (void)hd; (void)V;       \
+  (void)qd; (void)kvd; (void)qkv; (void)alpha; (void)st; (void)s;                            \
+  NE_CUDA(cudaSetDevice(ctx->device))
+
+#define NE_LAYER_CHECK(layer) \
+  if ((layer) < 0 || (layer) >= m.n_layers) return fail(ctx, NE_ERR_INVALID, "layer out of range")
+
+// Split d_tokens [B, S+1] into inputs / targets, embed, first RMSNorm
+// (embed_lookup, cpu_ops.h:433-439; rmsnorm, cpu_ops.h:20-60).
+NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens) {
+  NE_TRAIN_PRELUDE();
+  if (!d_tokens) return NE_ERR_INVALID;
   split_tokens_kernel<<<(M + 255) / 256, 256, 0, st>>>(d_tokens, B, S, t->ids, t->tgt);
   NE_CUDA(cudaGetLastError());
-
-  // ------------------------------------------------ forward
   NE_LAUNCH(launch_embed_rmsnorm(t->ids, t->embed_w, 1, V, D, ctx->L[0].rms_att, m.rms_eps,
                                  t->A[0].X, t->A[0].XN, M, ctx->d_status, st));
-  for (int l = 0; l < m.n_layers; ++l) {
-    const LayerW& w = ctx->L[l];
-    TrainActs& a = t->A[l];
-    if ((s = gemm(ctx, gc(a.XN, D, M, 0, w.wqkv, D, qkv, 0, D, EPI_F32, a.QKVR, qkv))) != NE_OK)
-      return s;
-    NE_LAUNCH(launch_qkv_post(a.QKVR, 1, 0, M, S, nullptr, 0, Hq, Hkv, hd,
-                              m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
-                              m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
-    NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
-    GemmCall c = gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_ADD, a.X2, D, alpha);
-    c.aux3 = a.X;
-    if ((s = gemm(ctx, c)) != NE_OK) return s;
-    NE_LAUNCH(launch_resid_rmsnorm(a.X2, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, a.X2N, M, st));
-    c = gc(a.X2N, D, M, 0, w.w13, D, 2 * F, 0, D, EPI_SWIGLU, a.GATE, F);
-    c.aux1 = a.H1;
-    c.aux2 = a.H3;
-    if ((s = gemm(ctx, c)) != NE_OK) return s;
-    float* xnext = (l + 1 < m.n_layers) ? t->A[l + 1].X : t->XL;
-    c = gc(a.GATE, F, M, 0, w.w2, F, D, 0, F, EPI_ADD, xnext, D, alpha);
-    c.aux3 = a.X2;
-    if ((s = gemm(ctx, c)) != NE_OK) return s;
-    const float* g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
-    __nv_bfloat16* xn = (l + 1 < m.n_layers) ? t->A[l + 1].XN : t->XNF;
-    NE_LAUNCH(launch_resid_rmsnorm(xnext, nullptr, 0, 0, 1.f, D, g, m.rms_eps, xn, M, st));
-  }
-  // ------------------------------------------------ classifier + cross-entropy
+  return NE_OK;
+}
+
+// Attention half of a layer (sdpaFwd, mil_dynamic.h:57-234): fused QKV
+// projection, per-head QK-norm, RoPE, causal GQA attention, Wo projection and
+// the scaled residual x2 = x + alpha*o (residual_cvt_f16, io.h:25-37), then the
+// FFN's RMSNorm of x2.
+NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
+  NE_TRAIN_PRELUDE();
+  NE_LAYER_CHECK(l);
+  const LayerW& w = ctx->L[l];
+  TrainActs& a = t->A[l];
+  if ((s = gemm(ctx, gc(a.XN, D, M, 0, w.wqkv, D, qkv, 0, D, EPI_F32, a.QKVR, qkv))) != NE_OK)
+    return s;
+  NE_LAUNCH(launch_qkv_post(a.QKVR, 1, 0, M, S, nullptr, 0, Hq, Hkv, hd,
+                            m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
+                            m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
+  NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
+  GemmCall c = gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_ADD, a.X2, D, alpha);
+  c.aux3 = a.X;
+  if ((s = gemm(ctx, c)) != NE_OK) return s;
+  NE_LAUNCH(launch_resid_rmsnorm(a.X2, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, a.X2N, M, st));
+  return NE_OK;
+}
+
+// FFN half of a layer (ffnFused, mil_dynamic.h:238-306): SwiGLU over the
+// interleaved W1/W3 projection, W2, residual x_next = x2 + alpha*ffn, then the
+// RMSNorm the next consumer needs (next layer's attention norm, or the final
+// norm before the classifier).
+NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int l) {
+  NE_TRAIN_PRELUDE();
+  NE_LAYER_CHECK(l);
+  const LayerW& w = ctx->L[l];
+  TrainActs& a = t->A[l];
+  GemmCall c = gc(a.X2N, D, M, 0, w.w13, D, 2 * F, 0, D, EPI_SWIGLU, a.GATE, F);
+  c.aux1 = a.H1;
+  c.aux2 = a.H3;
+  if ((s = gemm(ctx, c)) != NE_OK) return s;
+  float* xnext = (l + 1 < m.n_layers) ? t->A[l + 1].X : t->XL;
+  c = gc(a.GATE, F, M, 0, w.w2, F, D, 0, F, EPI_ADD, xnext, D, alpha);
+  c.aux3 = a.X2;
+  if ((s = gemm(ctx, c)) != NE_OK) return s;
+  const float* g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
+  __nv_bfloat16* xn = (l + 1 < m.n_layers) ? t->A[l + 1].XN : t->XNF;
+  NE_LAUNCH(launch_resid_rmsnorm(xnext, nullptr, 0, 0, 1.f, D, g, m.rms_eps, xn, M, st));
+  return NE_OK;
+}
+
+// Classifier over the tied embedding (train.m:495-505), mean cross-entropy
+// (cpu_ops.h:348-382), the classifier's backward (dX and the dense part of
+// dE), and the final RMSNorm's backward, leaving dY for the last layer.
+// d_loss (device, optional) receives the batch's mean loss.
+NE_API ne_status ne_lmhead_ce_fwd_bwd(ne_ctx* ctx, float* d_loss) {
+  NE_TRAIN_PRELUDE();
   const float ce_scale = 1.0f / (float)M;
+  const int nck = (V + 31) / 32;
   for (int r0 = 0; r0 < M; r0 += t->Mc) {
     const int rows = std::min(t->Mc, M - r0);
     const __nv_bfloat16* xnf = t->XNF + (size_t)r0 * D;
-    const int nck = (V + 31) / 32;
     GemmCall cl = gc(xnf, D, rows, 0, ctx->embed, D, V, 0, D, EPI_F32_STATS, t->logits, V);
     cl.aux1 = t->ce_stats;
     cl.aux_ld = nck;
     if ((s = gemm(ctx, cl)) != NE_OK) return s;
     NE_LAUNCH(launch_ce_rows(t->logits, t->ce_stats, nck, t->tgt + r0, rows, V, ce_scale,
-                             t->loss_rows + r0,
-                             t->dlogits, ctx->d_status, st));
+                             t->loss_rows + r0, t->dlogits, ctx->d_status, st));
     // dXNF = dlogits . E   (E read MN-major as [V (K), D (N)])
     if ((s = gemm(ctx, gc(t->dlogits, V, rows, 0, ctx->embed, D, D, 1, V, EPI_F32,
                           t->dXF + (size_t)r0 * D, D))) != NE_OK)
@@ -454,49 +583,8 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
         NE_OK)
       return s;
   }
-  // ------------------------------------------------ backward
   NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, t->XL, ctx->rms_final, m.rms_eps, M, D, nullptr, t->dY,
                                t->dY16, t->rmsf_g, st));
-  for (int l = m.n_layers - 1; l >= 0; --l) {
-    const LayerW& w = ctx->L[l];
-    const TrainActs& a = t->A[l];
-    const TrainLayerP& p = t->P[l];
-    // FFN: d_gate -> (dh1, dh3) via the SwiGLU-backward epilogue
-    GemmCall c = gc(t->dY16, D, M, 0, w.w2, F, F, 1, D, EPI_SWIGLU_BWD, t->DH13, 2 * F, alpha);
-    c.aux3 = a.H1;
-    c.aux1 = a.H3;
-    c.aux_ld = F;
-    if ((s = gemm(ctx, c)) != NE_OK) return s;
-    if ((s = gemm(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F, alpha))) != NE_OK)
-      return s;
-    if ((s = gemm(ctx, gc(t->DH13, 2 * F, 2 * F, 1, a.X2N, D, D, 1, M, EPI_RESID, p.g13, D))) !=
-        NE_OK)
-      return s;
-    if ((s = gemm(ctx, gc(t->DH13, 2 * F, M, 0, w.w13, D, D, 1, 2 * F, EPI_F32, t->dXF, D))) !=
-        NE_OK)
-      return s;
-    NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X2, w.rms_ffn, m.rms_eps, M, D, t->dY, t->dX2,
-                                 t->dX216, p.g_ffn, st));
-    // attention
-    c = gc(t->dX216, D, M, 0, w.wo, qd, qd, 1, D, EPI_BF16, t->dO, qd, alpha);
-    if ((s = gemm(ctx, c)) != NE_OK) return s;
-    if ((s = gemm(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd, alpha))) !=
-        NE_OK)
-      return s;
-    NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, t->dQ,
-                              t->dK, t->dV, st));
-    ctx->launches += 2;
-    NE_LAUNCH(launch_qk_rope_bwd(t->dQ, t->dK, t->dV, a.QKVR, m.qk_norm ? w.q_norm : nullptr,
-                                 m.qk_norm ? w.k_norm : nullptr, m.qk_eps, ctx->rope_cs, M, S, 0,
-                                 Hq, Hkv, hd, t->DQKV, p.g_qn, p.g_kn, st));
-    if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
-      return s;
-    if ((s = gemm(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D))) != NE_OK)
-      return s;
-    NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X, w.rms_att, m.rms_eps, M, D, t->dX2, t->dY, t->dY16,
-                                 p.g_att, st));
-  }
-  NE_LAUNCH(launch_embed_bwd(t->ids, t->dY, M, V, D, t->embed_g, st));
   if (d_loss) {
     NE_CUDA(cudaMemsetAsync(t->red + 1, 0, sizeof(double), st));
     sum_rows_kernel<<<64, 256, 0, st>>>(t->loss_rows, M, t->red + 1);
@@ -505,7 +593,124 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
     mean_from_sum_kernel<<<1, 1, 0, st>>>(t->red + 1, M, d_loss);
     NE_CUDA(cudaGetLastError());
   }
-  t->micro_steps++;
+  return comm_after_lmhead(ctx);
+}
+
+// FFN backward of a layer (ffnBwdFull, mil_dynamic.h:320-409): d_gate -> dh1,
+// dh3 through the SwiGLU-backward epilogue, dW2, dW1/dW3, dX through W1/W3,
+// and the FFN RMSNorm's backward plus the residual (rmsnorm_bwd_add,
+// cpu_ops.h:108-261), leaving the gradient at x2 in t->dX2 / t->dX216.
+NE_API ne_status ne_ffn_bwd(ne_ctx* ctx, int l) {
+  NE_TRAIN_PRELUDE();
+  NE_LAYER_CHECK(l);
+  const LayerW& w = ctx->L[l];
+  const TrainActs& a = t->A[l];
+  const TrainLayerP& p = t->P[l];
+  GemmCall c = gc(t->dY16, D, M, 0, w.w2, F, F, 1, D, EPI_SWIGLU_BWD, t->DH13, 2 * F, alpha);
+  c.aux3 = a.H1;
+  c.aux1 = a.H3;
+  c.aux_ld = F;
+  if ((s = gemm(ctx, c)) != NE_OK) return s;
+  if ((s = gemm(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F, alpha))) != NE_OK)
+    return s;
+  if ((s = gemm(ctx, gc(t->DH13, 2 * F, 2 * F, 1, a.X2N, D, D, 1, M, EPI_RESID, p.g13, D))) !=
+      NE_OK)
+    return s;
+  if ((s = gemm(ctx, gc(t->DH13, 2 * F, M, 0, w.w13, D, D, 1, 2 * F, EPI_F32, t->dXF, D))) !=
+      NE_OK)
+    return s;
+  NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X2, w.rms_ffn, m.rms_eps, M, D, t->dY, t->dX2,
+                               t->dX216, p.g_ffn, st));
+  return NE_OK;
+}
+
+// Attention backward of a layer: dO = dx2 . Wo (wotBwd, mil_dynamic.h:412),
+// dWo, SDPA backward (sdpaBwd1/2, mil_dynamic.h:583-707, with the GQA group
+// sum of gqa_reduce_kv_f16, cpu_ops.h:585), RoPE and QK-norm backward
+// (rope_backward_inplace_f16, cpu_ops.h:510-537), dX through Wq/Wk/Wv (qkvBwd,
+// mil_dynamic.h:516-576), dWq/dWk/dWv and the attention RMSNorm's backward
+// plus the residual, leaving dY for the layer below.  The layer's gradients
+// are final afterwards (the data-parallel bucket of this layer may start).
+NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int l) {
+  NE_TRAIN_PRELUDE();
+  NE_LAYER_CHECK(l);
+  const LayerW& w = ctx->L[l];
+  const TrainActs& a = t->A[l];
+  const TrainLayerP& p = t->P[l];
+  GemmCall c = gc(t->dX216, D, M, 0, w.wo, qd, qd, 1, D, EPI_BF16, t->dO, qd, alpha);
+  if ((s = gemm(ctx, c)) != NE_OK) return s;
+  if ((s = gemm(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd, alpha))) !=
+      NE_OK)
+    return s;
+  NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, t->dQ,
+                            t->dK, t->dV, st));
+  ctx->launches += 2;
+  NE_LAUNCH(launch_qk_rope_bwd(t->dQ, t->dK, t->dV, a.QKVR, m.qk_norm ? w.q_norm : nullptr,
+                               m.qk_norm ? w.k_norm : nullptr, m.qk_eps, ctx->rope_cs, M, S, 0,
+                               Hq, Hkv, hd, t->DQKV, p.g_qn, p.g_kn, st));
+  if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
+    return s;
+  if ((s = gemm(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D))) != NE_OK)
+    return s;
+  NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X, w.rms_att, m.rms_eps, M, D, t->dX2, t->dY, t->dY16,
+                               p.g_att, st));
+  return comm_after_layer(ctx, l);
+}
+
+// Scatter-add of the input-embedding gradient (embed_backward,
+// cpu_ops.h:441-447).  With data-parallel reduction active, every rank's
+// (token, dY row) pairs are gathered first and added on every rank.
+NE_API ne_status ne_embed_bwd(ne_ctx* ctx) {
+  NE_TRAIN_PRELUDE();
+  return comm_embed_bwd(ctx);
+}
+
+// Forward + backward of one batch d_tokens [B, S+1] (inputs tokens[:, :S],
+// targets tokens[:, 1:]); gradients ACCUMULATE into the gradient buffers
+// (mean cross-entropy over the B*S targets of this batch).  *d_loss (device,
+// optional) receives the batch's mean loss.
+NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
+  if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+  const int L = ctx->cfg.n_layers;
+  ne_status s;
+  if ((s = ne_embed_fwd(ctx, d_tokens)) != NE_OK) return s;
+  for (int l = 0; l < L; ++l) {
+    if ((s = ne_attn_fwd(ctx, l)) != NE_OK) return s;
+    if ((s = ne_ffn_fwd(ctx, l)) != NE_OK) return s;
+  }
+  if ((s = ne_lmhead_ce_fwd_bwd(ctx, d_loss)) != NE_OK) return s;
+  for (int l = L - 1; l >= 0; --l) {
+    if ((s = ne_ffn_bwd(ctx, l)) != NE_OK) return s;
+    if ((s = ne_attn_bwd(ctx, l)) != NE_OK) return s;
+  }
+  if ((s = ne_embed_bwd(ctx)) != NE_OK) return s;
+  ctx->train->micro_steps++;
+  return NE_OK;
+}
+
+// Token-major RMSNorm (rmsnorm, cpu_ops.h:20-60): out [rows, D] (bf16) =
+// x / sqrt(mean(x^2) + eps) * w, for caller-owned device buffers.
+NE_API ne_status ne_rmsnorm_fwd(ne_ctx* ctx, const float* d_x, const float* d_w, int rows,
+                                void* d_out_bf16) {
+  if (!ctx || !d_x || !d_w || !d_out_bf16 || rows <= 0) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_LAUNCH(launch_resid_rmsnorm(const_cast<float*>(d_x), nullptr, 0, 0, 1.f, ctx->cfg.dim, d_w,
+                                 ctx->cfg.rms_eps, reinterpret_cast<__nv_bfloat16*>(d_out_bf16),
+                                 rows, ctx->st));
+  return NE_OK;
+}
+
+// RMSNorm backward with residual (rmsnorm_bwd / rmsnorm_bwd_add,
+// cpu_ops.h:108-261) in token-major layout: d_dx = d(rmsnorm)/dx . d_dy
+// (+ d_residual when not NULL); d_dw (optional) accumulates the gain gradient.
+// The exact derivative of x*w/rms is used for every gain value.
+NE_API ne_status ne_rmsnorm_bwd_add(ne_ctx* ctx, const float* d_dy, const float* d_x,
+                                    const float* d_w, int rows, const float* d_residual,
+                                    float* d_dx, float* d_dw) {
+  if (!ctx || !d_dy || !d_x || !d_w || !d_dx || rows <= 0) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_LAUNCH(launch_rmsnorm_bwd(d_dy, d_x, d_w, ctx->cfg.rms_eps, rows, ctx->cfg.dim, d_residual,
+                               d_dx, nullptr, d_dw, ctx->st));
   return NE_OK;
 }
 
@@ -520,6 +725,19 @@ NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h
   if (s != NE_OK) return s;
   if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
   return ne_sync(ctx);
+}
+
+// Sum the whole gradient pool over the communicator's ranks now (for callers
+// that drive the per-layer entry points with reduction off); enqueued on the
+// comm stream, ordered after and before the compute stream's work.
+NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx) {
+  if (!ctx || !ctx->train || !ctx->comm) return NE_ERR_STATE;
+  if (ctx->comm->world == 1) return NE_OK;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  ne_status s;
+  if ((s = comm_fence_in(ctx)) != NE_OK) return s;
+  if ((s = comm_allreduce(ctx, ctx->train->grad_pool, ctx->train->grad_floats)) != NE_OK) return s;
+  return comm_fence_out(ctx);
 }
 
 NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floats) {
@@ -616,53 +834,293 @@ NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_
   return min_lr + 0.5f * (1.0f + cosf(3.14159265358979323846f * decay_ratio)) * (max_lr - min_lr);
 }
 
-// Copy one layer's gradients (which = 0) or fp32 master weights (which = 1)
-// to host buffers in the v4 layout; layer -1 = (rms_final, embed) into
-// (h_rms_att, h_wq).  Any pointer may be NULL.
-NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_wq, float* h_wk,
-                                    float* h_wv, float* h_wo, float* h_w1, float* h_w2,
-                                    float* h_w3, float* h_rms_att, float* h_rms_ffn,
-                                    float* h_q_norm, float* h_k_norm) {
-  if (!ctx || !ctx->train || which < 0 || which > 1) return NE_ERR_INVALID;
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// v4 checkpoint with the full training state (train.m:97-165): the layout is
+// the reference's byte for byte; the fp32 masters and both Adam moments come
+// from the device pools, W1/W3 (and their moments) are separated from the
+// interleaved device layout.  When the model has QK-norm, the trailing "QKN1"
+// block follows (q_norm, k_norm per layer, then m, v of each), which v4
+// readers ignore.
+namespace {
+
+struct TensorRef {
+  int seg;          // index into TrainState::segs
+  size_t off, n;    // element offset inside the segment, element count
+  int w13;          // 0 plain, 1 = W1 rows, 2 = W3 rows of the interleaved block
+};
+
+// The nine v4 tensors of layer l in file order.
+std::vector<TensorRef> layer_tensors(const ne_ctx* ctx, int l) {
+  const ne_model_cfg& m = ctx->cfg;
+  const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
+               kvd = (size_t)m.kv_heads * m.head_dim;
+  const int s0 = ctx->train->P[l].seg0;
+  return {{s0, 0, qd * D, 0},          {s0, qd * D, kvd * D, 0}, {s0, (qd + kvd) * D, kvd * D, 0},
+          {s0 + 1, 0, D * qd, 0},      {s0 + 2, 0, F * D, 1},    {s0 + 3, 0, D * F, 0},
+          {s0 + 2, 0, F * D, 2},       {s0 + 4, 0, D, 0},        {s0 + 5, 0, D, 0}};
+}
+
+// which: 0 weights (masters / gains), 1 Adam m, 2 Adam v, 3 gradients
+float* seg_array(const Seg& sg, int which) {
+  return which == 0 ? sg.w : which == 1 ? sg.m : which == 2 ? sg.v : sg.g;
+}
+
+// Copy a tensor (which as in seg_array) between the device and host[n].
+ne_status xfer(ne_ctx* ctx, const TensorRef& r, int which, float* host, bool to_host) {
+  const Seg& sg = ctx->train->segs[r.seg];
+  float* dev = seg_array(sg, which);
+  if (!r.w13) {
+    NE_CUDA(cudaMemcpy(to_host ? (void*)host : (void*)(dev + r.off),
+                       to_host ? (const void*)(dev + r.off) : (const void*)host, r.n * 4,
+                       to_host ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice));
+    return NE_OK;
+  }
+  // W1 / W3 rows live in 16-row blocks of the [2F, D] device array
+  const size_t D = ctx->cfg.dim, F = ctx->cfg.hidden;
+  const bool is_w3 = r.w13 == 2;
+  for (size_t f0 = 0; f0 < F; f0 += 16) {
+    const size_t rows = std::min<size_t>(16, F - f0);
+    float* d = dev + w13_row(f0, is_w3) * D;
+    float* h = host + f0 * D;
+    NE_CUDA(cudaMemcpy(to_host ? (void*)h : (void*)d, to_host ? (const void*)d : (const void*)h,
+                       rows * D * 4, to_host ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice));
+  }
+  return NE_OK;
+}
+
+}  // namespace
+
+extern "C" NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info) {
+  if (!ctx || !path) return NE_ERR_INVALID;
+  if (!ctx->train) return fail(ctx, NE_ERR_STATE, "ne_save_ckpt_v4 needs the training state");
+  const ne_model_cfg& m = ctx->cfg;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(ctx, NE_ERR_IO, std::string("cannot open ") + path);
+  struct Closer {
+    FILE* f;
+    ~Closer() {
+      if (f) fclose(f);
+    }
+  } closer{f};
+  CkptHdr h;
+  std::memset(&h, 0, sizeof(h));
+  h.magic = kCkptMagic;
+  h.version = 4;
+  h.n_layers = m.n_layers;
+  h.vocab_size = m.vocab;
+  h.dim = m.dim;
+  h.hidden_dim = m.hidden;
+  h.n_heads = m.n_heads;
+  h.seq_len = t->S;
+  h.kv_heads = m.kv_heads;
+  h.head_dim = m.head_dim;
+  h.q_dim = m.n_heads * m.head_dim;
+  if (info) {
+    h.step = info->step;
+    h.total_steps = info->total_steps;
+    if (info->seq_len > 0) h.seq_len = info->seq_len;
+    h.lr = info->lr;
+    h.loss = info->loss;
+    h.cum_compile = info->cum_compile;
+    h.cum_train = info->cum_train;
+    h.cum_wall = info->cum_wall;
+    h.cum_steps = info->cum_steps;
+    h.cum_batches = info->cum_batches;
+    h.adam_t = info->adam_t;
+  }
+  auto put = [&](const std::vector<float>& v, size_t n) { return fwrite(v.data(), 4, n, f) == n; };
+  if (fwrite(&h, sizeof(h), 1, f) != 1) return fail(ctx, NE_ERR_IO, "write failed");
+  std::vector<float> buf;
+  ne_status s;
+  for (int l = 0; l < m.n_layers; ++l) {
+    const std::vector<TensorRef> tr = layer_tensors(ctx, l);
+    auto emit = [&](const TensorRef& r, int which) -> ne_status {
+      buf.resize(r.n);
+      ne_status e = xfer(ctx, r, which, buf.data(), true);
+      if (e != NE_OK) return e;
+      return put(buf, r.n) ? NE_OK : fail(ctx, NE_ERR_IO, "write failed");
+    };
+    for (const TensorRef& r : tr)          // the nine weights
+      if ((s = emit(r, 0)) != NE_OK) return s;
+    for (const TensorRef& r : tr)          // then (m, v) of each
+      if ((s = emit(r, 1)) != NE_OK || (s = emit(r, 2)) != NE_OK) return s;
+  }
+  for (int k = 0; k < 2; ++k) {   // rms_final, then the embedding: value, m, v
+    const Seg& sg = t->segs[t->segs.size() - 2 + k];
+    for (int which = 0; which < 3; ++which) {
+      buf.resize((size_t)sg.n);
+      NE_CUDA(cudaMemcpy(buf.data(), seg_array(sg, which), (size_t)sg.n * 4, cudaMemcpyDeviceToHost));
+      if (!put(buf, (size_t)sg.n)) return fail(ctx, NE_ERR_IO, "write failed");
+    }
+  }
+  if (m.qk_norm) {
+    const int nl = m.n_layers, hd = m.head_dim;
+    if (fwrite("QKN1", 1, 4, f) != 4 || fwrite(&nl, 4, 1, f) != 1 || fwrite(&hd, 4, 1, f) != 1)
+      return fail(ctx, NE_ERR_IO, "write failed");
+    for (int l = 0; l < nl; ++l) {
+      const int s0 = t->P[l].seg0;
+      const Seg* qk[2] = {&t->segs[s0 + 6], &t->segs[s0 + 7]};
+      buf.resize(hd);
+      auto emit = [&](const Seg& sg, int which) -> ne_status {
+        NE_CUDA(cudaMemcpy(buf.data(), seg_array(sg, which), (size_t)hd * 4,
+                           cudaMemcpyDeviceToHost));
+        return put(buf, hd) ? NE_OK : fail(ctx, NE_ERR_IO, "write failed");
+      };
+      // q_norm, k_norm, then (m, v) of each
+      if ((s = emit(*qk[0], 0)) != NE_OK || (s = emit(*qk[1], 0)) != NE_OK) return s;
+      for (int i = 0; i < 2; ++i)
+        if ((s = emit(*qk[i], 1)) != NE_OK || (s = emit(*qk[i], 2)) != NE_OK) return s;
+    }
+  }
+  if (fflush(f) != 0) return fail(ctx, NE_ERR_IO, "write failed");
+  return NE_OK;
+}
+
+namespace ne {
+
+ne_status train_ckpt_load(ne_ctx* ctx, const char* path, ne_ckpt_info* info, bool* handled) {
+  *handled = false;
+  if (!ctx->train) return NE_OK;
+  *handled = true;
+  const ne_model_cfg& m = ctx->cfg;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  FILE* f = fopen(path, "rb");
+  if (!f) return NE_ERR_IO;
+  struct Closer {
+    FILE* f;
+    ~Closer() {
+      if (f) fclose(f);
+    }
+  } closer{f};
+  CkptHdr h;
+  if (fread(&h, sizeof(h), 1, f) != 1) return NE_ERR_FORMAT;
+  if (h.magic != kCkptMagic || h.version != 4) return NE_ERR_FORMAT;
+  if (h.n_layers != m.n_layers || h.vocab_size != m.vocab || h.dim != m.dim ||
+      h.hidden_dim != m.hidden || h.n_heads != m.n_heads || h.kv_heads != m.kv_heads ||
+      h.head_dim != m.head_dim || h.q_dim != m.n_heads * m.head_dim)
+    return NE_ERR_FORMAT;
+  auto get = [&](std::vector<float>& v, size_t n) {
+    v.resize(n);
+    return fread(v.data(), 4, n, f) == n;
+  };
+  std::vector<float> buf;
+  ne_status s;
+  for (int l = 0; l < m.n_layers; ++l) {
+    const std::vector<TensorRef> tr = layer_tensors(ctx, l);
+    for (const TensorRef& r : tr) {
+      if (!get(buf, r.n)) return NE_ERR_FORMAT;
+      if ((s = xfer(ctx, r, 0, buf.data(), false)) != NE_OK) return s;
+    }
+    for (const TensorRef& r : tr)
+      for (int which = 1; which <= 2; ++which) {
+        if (!get(buf, r.n)) return NE_ERR_FORMAT;
+        if ((s = xfer(ctx, r, which, buf.data(), false)) != NE_OK) return s;
+      }
+  }
+  for (int k = 0; k < 2; ++k) {
+    const Seg& sg = t->segs[t->segs.size() - 2 + k];
+    for (int which = 0; which < 3; ++which) {
+      if (!get(buf, (size_t)sg.n)) return NE_ERR_FORMAT;
+      NE_CUDA(cudaMemcpy(seg_array(sg, which), buf.data(), (size_t)sg.n * 4, cudaMemcpyHostToDevice));
+    }
+  }
+  bool has_qk = false;
+  char magic[4];
+  if (fread(magic, 1, 4, f) == 4 && std::memcmp(magic, "QKN1", 4) == 0) {
+    int nl = 0, hd = 0;
+    if (fread(&nl, 4, 1, f) != 1 || fread(&hd, 4, 1, f) != 1) return NE_ERR_FORMAT;
+    if (nl != m.n_layers || hd != m.head_dim || !m.qk_norm) return NE_ERR_FORMAT;
+    for (int l = 0; l < nl; ++l) {
+      const int s0 = t->P[l].seg0;
+      const Seg* qk[2] = {&t->segs[s0 + 6], &t->segs[s0 + 7]};
+      for (int i = 0; i < 2; ++i) {
+        if (!get(buf, hd)) return NE_ERR_FORMAT;
+        NE_CUDA(cudaMemcpy(qk[i]->w, buf.data(), (size_t)hd * 4, cudaMemcpyHostToDevice));
+      }
+      for (int i = 0; i < 2; ++i)
+        for (int which = 1; which <= 2; ++which) {
+          if (!get(buf, hd)) return NE_ERR_FORMAT;
+          NE_CUDA(cudaMemcpy(seg_array(*qk[i], which), buf.data(), (size_t)hd * 4,
+                             cudaMemcpyHostToDevice));
+        }
+    }
+    has_qk = true;
+  } else if (m.qk_norm) {
+    // a reference checkpoint has no QK-norm block: unit gains, zero moments
+    std::vector<float> ones(m.head_dim, 1.0f), zeros(m.head_dim, 0.0f);
+    for (int l = 0; l < m.n_layers; ++l) {
+      const int s0 = t->P[l].seg0;
+      for (int i = 0; i < 2; ++i) {
+        const Seg& sg = t->segs[s0 + 6 + i];
+        NE_CUDA(cudaMemcpy(sg.w, ones.data(), (size_t)m.head_dim * 4, cudaMemcpyHostToDevice));
+        NE_CUDA(cudaMemcpy(sg.m, zeros.data(), (size_t)m.head_dim * 4, cudaMemcpyHostToDevice));
+        NE_CUDA(cudaMemcpy(sg.v, zeros.data(), (size_t)m.head_dim * 4, cudaMemcpyHostToDevice));
+      }
+    }
+  }
+  if ((s = ne_train_sync_weights(ctx)) != NE_OK) return s;
+  if (info) {
+    info->step = h.step;
+    info->total_steps = h.total_steps;
+    info->seq_len = h.seq_len;
+    info->adam_t = h.adam_t;
+    info->lr = h.lr;
+    info->loss = h.loss;
+    info->cum_compile = h.cum_compile;
+    info->cum_train = h.cum_train;
+    info->cum_wall = h.cum_wall;
+    info->cum_steps = h.cum_steps;
+    info->cum_batches = h.cum_batches;
+    info->has_qk_norm = has_qk ? 1 : 0;
+  }
+  return NE_OK;
+}
+
+}  // namespace ne
+
+// Copy one layer's tensors to host buffers in the v4 layout: which = 0
+// gradients, 1 fp32 master weights, 2 Adam m, 3 Adam v.  Layer -1 =
+// (rms_final, embedding) into (h_rms_att, h_wq).  Any pointer may be NULL.
+extern "C" NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which, float* h_wq,
+                                               float* h_wk, float* h_wv, float* h_wo,
+                                               float* h_w1, float* h_w2, float* h_w3,
+                                               float* h_rms_att, float* h_rms_ffn,
+                                               float* h_q_norm, float* h_k_norm) {
+  if (!ctx || !ctx->train || which < 0 || which > 3) return NE_ERR_INVALID;
   TrainState* t = ctx->train;
   const ne_model_cfg& m = ctx->cfg;
   if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
   NE_CUDA(cudaSetDevice(ctx->device));
   NE_CUDA(cudaStreamSynchronize(ctx->st));
-  const size_t D = m.dim, F = m.hidden, qd = (size_t)m.n_heads * m.head_dim,
-               kvd = (size_t)m.kv_heads * m.head_dim, hd = m.head_dim;
-  auto get = [&](float* dst, const float* src, size_t n) -> ne_status {
-    if (dst) NE_CUDA(cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost));
-    return NE_OK;
-  };
+  const int arr = which == 0 ? 3 : which - 1;   // seg_array selector
   ne_status s;
   if (layer == -1) {
-    if ((s = get(h_rms_att, which ? ctx->rms_final : t->rmsf_g, D))) return s;
-    return get(h_wq, which ? t->embed_w : t->embed_g, (size_t)m.vocab * D);
-  }
-  const TrainLayerP& p = t->P[layer];
-  const LayerW& w = ctx->L[layer];
-  const float* qkv = which ? p.wqkv : p.gqkv;
-  if ((s = get(h_wq, qkv, qd * D)) || (s = get(h_wk, qkv + qd * D, kvd * D)) ||
-      (s = get(h_wv, qkv + (qd + kvd) * D, kvd * D)) || (s = get(h_wo, which ? p.wo : p.go, D * qd)) ||
-      (s = get(h_w2, which ? p.w2 : p.g2, D * F)) ||
-      (s = get(h_rms_att, which ? w.rms_att : p.g_att, D)) ||
-      (s = get(h_rms_ffn, which ? w.rms_ffn : p.g_ffn, D)))
-    return s;
-  if (m.qk_norm) {
-    if ((s = get(h_q_norm, which ? w.q_norm : p.g_qn, hd)) ||
-        (s = get(h_k_norm, which ? w.k_norm : p.g_kn, hd)))
-      return s;
-  }
-  if (h_w1 || h_w3) {
-    std::vector<float> w13(2 * F * D);
-    NE_CUDA(cudaMemcpy(w13.data(), which ? p.w13 : p.g13, 2 * F * D * 4, cudaMemcpyDeviceToHost));
-    for (size_t f = 0; f < F; ++f) {
-      if (h_w1) std::memcpy(h_w1 + f * D, &w13[w13_row(f, false) * D], D * 4);
-      if (h_w3) std::memcpy(h_w3 + f * D, &w13[w13_row(f, true) * D], D * 4);
+    float* dst[2] = {h_rms_att, h_wq};
+    for (int k = 0; k < 2; ++k) {
+      const Seg& sg = t->segs[t->segs.size() - 2 + k];
+      if (dst[k])
+        NE_CUDA(cudaMemcpy(dst[k], seg_array(sg, arr), (size_t)sg.n * 4, cudaMemcpyDeviceToHost));
     }
+    return NE_OK;
+  }
+  const std::vector<TensorRef> tr = layer_tensors(ctx, layer);
+  float* dst[9] = {h_wq, h_wk, h_wv, h_wo, h_w1, h_w2, h_w3, h_rms_att, h_rms_ffn};
+  for (int k = 0; k < 9; ++k)
+    if (dst[k] && (s = xfer(ctx, tr[k], arr, dst[k], true)) != NE_OK) return s;
+  if (m.qk_norm) {
+    const int s0 = t->P[layer].seg0;
+    float* qk[2] = {h_q_norm, h_k_norm};
+    for (int i = 0; i < 2; ++i)
+      if (qk[i])
+        NE_CUDA(cudaMemcpy(qk[i], seg_array(t->segs[s0 + 6 + i], arr), (size_t)m.head_dim * 4,
+                           cudaMemcpyDeviceToHost));
   }
   return NE_OK;
 }
-
-}  // extern "C"

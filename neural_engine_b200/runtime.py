@@ -30,7 +30,10 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_gemm_splitk_noalloc", "ne_train_alloc", "ne_train_set_masters",
             "ne_train_sync_weights", "ne_train_zero_grads", "ne_train_fwd_bwd_device",
             "ne_train_fwd_bwd", "ne_train_grad_norm", "ne_adamw_step", "ne_lr_schedule",
-            "ne_train_get_layer", "ne_gemm", "ne_train_grad_pool")
+            "ne_train_get_layer", "ne_gemm", "ne_train_grad_pool", "ne_save_ckpt_v4",
+            "ne_embed_fwd", "ne_attn_fwd", "ne_ffn_fwd", "ne_lmhead_ce_fwd_bwd", "ne_ffn_bwd",
+            "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
+            "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -136,6 +139,18 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_set_layer_weights.argtypes = [P, I] + [P] * 11
     lib.ne_set_global_weights.argtypes = [P, P, P]
     lib.ne_load_ckpt_v4.argtypes = [P, C.c_char_p, C.POINTER(CkptInfoC)]
+    lib.ne_save_ckpt_v4.argtypes = [P, C.c_char_p, C.POINTER(CkptInfoC)]
+    lib.ne_embed_fwd.argtypes = [P, P]
+    for n in ("ne_attn_fwd", "ne_ffn_fwd", "ne_ffn_bwd", "ne_attn_bwd"):
+        getattr(lib, n).argtypes = [P, I]
+    lib.ne_lmhead_ce_fwd_bwd.argtypes = [P, P]
+    lib.ne_embed_bwd.argtypes = [P]
+    lib.ne_rmsnorm_fwd.argtypes = [P, P, P, I, P]
+    lib.ne_rmsnorm_bwd_add.argtypes = [P, P, P, P, I, P, P, P]
+    lib.ne_comm_unique_id.argtypes = [P]
+    lib.ne_comm_init.argtypes = [P, P, I, I]
+    lib.ne_comm_set_reduce.argtypes = [P, I]
+    lib.ne_grad_allreduce_async.argtypes = [P]
     lib.ne_kv_alloc.argtypes = [P, I, I]
     lib.ne_prefill.argtypes = [P, P, I, I, I, P, P]
     lib.ne_decode_step.argtypes = [P, P, I, I, P, P]
@@ -223,9 +238,59 @@ class Engine:
         self._check(self.lib.ne_set_global_weights(self._ctx, _ptr(f32(rms_final)), _ptr(f32(embed))))
 
     def load_checkpoint(self, path: str) -> dict:
+        """Weights only; after train_alloc the full training state (resume)."""
         info = CkptInfoC()
         self._check(self.lib.ne_load_ckpt_v4(self._ctx, path.encode(), C.byref(info)))
         return {f: getattr(info, f) for f, _ in CkptInfoC._fields_}
+
+    def save_checkpoint(self, path: str, **info):
+        """Full training state in the v4 layout; info: CkptInfoC field values."""
+        ci = CkptInfoC()
+        for k, v in info.items():
+            setattr(ci, k, v)
+        self._check(self.lib.ne_save_ckpt_v4(self._ctx, path.encode(), C.byref(ci)))
+
+    # -- per-layer entry points (one micro-step = embed_fwd, attn/ffn fwd per
+    #    layer, lmhead_ce, ffn/attn bwd per layer in reverse, embed_bwd)
+    def embed_fwd(self, d_tokens: int):
+        self._check(self.lib.ne_embed_fwd(self._ctx, C.c_void_p(d_tokens)))
+
+    def attn_fwd(self, layer: int):
+        self._check(self.lib.ne_attn_fwd(self._ctx, int(layer)))
+
+    def ffn_fwd(self, layer: int):
+        self._check(self.lib.ne_ffn_fwd(self._ctx, int(layer)))
+
+    def lmhead_ce_fwd_bwd(self, d_loss: int | None = None):
+        self._check(self.lib.ne_lmhead_ce_fwd_bwd(self._ctx, C.c_void_p(d_loss) if d_loss else None))
+
+    def ffn_bwd(self, layer: int):
+        self._check(self.lib.ne_ffn_bwd(self._ctx, int(layer)))
+
+    def attn_bwd(self, layer: int):
+        self._check(self.lib.ne_attn_bwd(self._ctx, int(layer)))
+
+    def embed_bwd(self):
+        self._check(self.lib.ne_embed_bwd(self._ctx))
+
+    # -- data-parallel gradient exchange (NCCL)
+    @staticmethod
+    def comm_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        st = load_library().ne_comm_unique_id(buf)
+        if st != NE_OK:
+            raise NeError(st, "ne_comm_unique_id")
+        return buf.raw
+
+    def comm_init(self, uid: bytes, rank: int, world: int):
+        buf = C.create_string_buffer(bytes(uid), 128)
+        self._check(self.lib.ne_comm_init(self._ctx, buf, int(rank), int(world)))
+
+    def comm_set_reduce(self, on: bool):
+        self._check(self.lib.ne_comm_set_reduce(self._ctx, int(bool(on))))
+
+    def grad_allreduce(self):
+        self._check(self.lib.ne_grad_allreduce_async(self._ctx))
 
     # -- token loop
     def kv_alloc(self, max_batch: int, max_seq: int):
@@ -370,6 +435,10 @@ class Engine:
 
     def get_grads(self) -> dict:
         return self._train_tensors(0)
+
+    def get_adam(self, moment: str) -> dict:
+        """Adam first ("m") or second ("v") moments, same structure as get_grads."""
+        return self._train_tensors({"m": 2, "v": 3}[moment])
 
     def get_masters(self) -> dict:
         return self._train_tensors(1)
