@@ -53,6 +53,7 @@ def build(verbose: bool = True, extra: list[str] | None = None) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra), srcs))
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
+        build_host(verbose)
         return LIB
     cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-ldl", "-lpthread", "-lrt"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -60,7 +61,29 @@ def build(verbose: bool = True, extra: list[str] | None = None) -> str:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     if verbose:
         print(f"built {LIB}")
+    build_host(verbose)
     return LIB
+
+
+HOST_SRC = os.path.join(PKG, "host", "ne_train.cpp")
+HOST_BIN = os.path.join(PKG, "ne_train")
+
+
+def build_host(verbose: bool = True) -> str:
+    """The ne_train command-line driver (plain C++ over the C ABI of libne.so)."""
+    if os.path.exists(HOST_BIN) and os.path.getmtime(HOST_BIN) >= max(
+            os.path.getmtime(HOST_SRC), os.path.getmtime(LIB),
+            os.path.getmtime(os.path.join(ROOT, "include", "ne.h"))):
+        return HOST_BIN
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-Wall", "-I",
+           os.path.join(ROOT, "include"), HOST_SRC, "-o", HOST_BIN, "-L", PKG, "-lne",
+           "-Wl,-rpath,$ORIGIN", "-lpthread"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ne_train build failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(f"built {HOST_BIN}")
+    return HOST_BIN
 
 
 if __name__ == "__main__":

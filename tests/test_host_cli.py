@@ -1,0 +1,71 @@
+"""CPU: the ne_train command-line driver's host logic against the restated
+reference driver (oracle/host_driver.py): the drand48 generator (pinned to the
+C library's own), the scratch initialisation written as a v4 checkpoint
+(--dump-init), and the data windows (--print-windows).  None of these touch a
+GPU."""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import ckpt_v4
+from oracle import host_driver as hd
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "neural_engine_b200", "ne_train")
+
+
+def _bin():
+    if not os.path.exists(BIN):
+        from neural_engine_b200 import build
+        build.build(verbose=False)
+    return BIN
+
+
+def test_drand48_restatement_matches_the_c_library():
+    libc = ctypes.CDLL(None)
+    libc.drand48.restype = ctypes.c_double
+    libc.srand48.argtypes = [ctypes.c_long]
+    for seed in (42, 43, 1042, 0):
+        libc.srand48(seed)
+        r = hd.Drand48(seed)
+        for _ in range(1000):
+            assert libc.drand48() == r()
+
+
+SHAPE = ["--model", "custom", "--layers", "2", "--dim", "64", "--hidden", "128", "--heads", "4",
+         "--kv-heads", "2", "--head-dim", "64", "--vocab", "96"]
+
+
+def test_scratch_init_is_the_reference_initialisation(tmp_path):
+    path = str(tmp_path / "init.bin")
+    subprocess.run([_bin(), *SHAPE, "--seq", "32", "--dump-init", path], check=True, timeout=60)
+    ck = ckpt_v4.read_v4(path, with_adam=True)
+    layers, rf, emb = hd.scratch_init(2, 64, 128, 4, 2, 64, 96)
+    assert ck.hdr.n_layers == 2 and ck.hdr.q_dim == 256 and ck.hdr.seq_len == 32
+    for L in range(2):
+        for k in ckpt_v4.LAYER_KEYS:
+            assert np.array_equal(ck.layers[L][k], layers[L][k]), (L, k)
+            assert not ck.adam["layers"][L][k][0].any()
+    assert np.array_equal(ck.rms_final, rf)
+    assert np.array_equal(ck.embed, emb)
+
+
+def test_data_windows_follow_the_reference_sampling(tmp_path):
+    n = 100_000
+    data = (np.arange(n) % 50_000).astype(np.uint16)
+    path = tmp_path / "tok.bin"
+    data.tofile(path)
+    out = subprocess.run([_bin(), *SHAPE, "--seq", "256", "--data", str(path),
+                          "--print-windows", "20"], check=True, capture_output=True, text=True,
+                         timeout=60).stdout.split()
+    assert [int(x) for x in out] == hd.sample_windows(n, 256, 20, seed=42)
+
+
+def test_cli_rejects_unknown_flags():
+    r = subprocess.run([_bin(), "--bogus"], capture_output=True, text=True, timeout=30)
+    assert r.returncode == 2
+    r = subprocess.run([_bin(), "--help"], capture_output=True, text=True, timeout=30)
+    assert r.returncode == 0 and "--scratch" in r.stdout
