@@ -1,6 +1,7 @@
 // gemm.cu -- host side of the tcgen05 GEMM: TMA descriptors, tiling, dispatch.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cstring>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -62,19 +63,45 @@ bool make_tmap_mn(CUtensorMap* tm, const void* ptr, int mn, int K, long long ld)
   return r == CUDA_SUCCESS;
 }
 
+// Output of a staged epilogue: [rows, cols] row-major with leading dim ld
+// elements, boxes of box_cols x 32 rows whose 64- or 128-byte rows use the
+// matching swizzle (the kernel writes the box in that layout).
+bool make_tmap_out(CUtensorMap* tm, void* ptr, int rows, int cols, long long ld,
+                   CUtensorMapDataType dt, int elem_bytes, int box_cols) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const int row_bytes = box_cols * elem_bytes;
+  if (row_bytes != 64 && row_bytes != 128) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * elem_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// A staged epilogue needs a 16-byte aligned output base and row pitch.
+bool stage_ok(const void* out, long long ld, int elem_bytes) {
+  return out && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (ld * elem_bytes) % 16 == 0;
+}
+
 template <int BN, class Epi, int FMT, int AMN, int BMN>
-cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh,
-                     const typename Epi::Params& p, int grid, cudaStream_t st) {
+cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                     const GemmShape& sh, const typename Epi::Params& p, int grid,
+                     cudaStream_t st) {
   using C = GemmCfg<BN>;
+  constexpr int smem = EpiStage<Epi>::value ? C::SMEM_BYTES_STAGED : C::SMEM_BYTES;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
   return launch_k(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>, dim3(grid), dim3(GEMM_THREADS),
-                  (size_t)C::SMEM_BYTES, st, ta, tb, sh, p);
+                  (size_t)smem, st, ta, tb, tc, sh, p);
 }
 
 // Epilogue dispatch.  K-major x K-major serves every epilogue; the MN-major
@@ -85,51 +112,90 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
   constexpr bool kk = (AMN == 0 && BMN == 0);
   constexpr bool kmn = (AMN == 0 && BMN == 1);
   constexpr bool ch32 = GemmCfg<BN>::CH == 32;
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));   // direct-store epilogues ignore it
   switch (c.epi) {
     case EPI_F32T:
       if constexpr (kk) {
         EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
-        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
       }
       break;
     case EPI_F32: {
+      if constexpr (ch32) {
+        if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
+            make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
+          EpiF32S::Params p{0};
+          return launch_t<BN, EpiF32S, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        }
+      }
       EpiF32::Params p{(float*)c.out, c.ld, c.split_stride};
-      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
     }
     case EPI_BF16:
       if constexpr (kk || kmn) {
-        EpiBF16::Params p{c.out, c.ld, c.alpha, c.half_out};
-        return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        if constexpr (ch32) {
+          if (stage_ok(c.out, c.ld, 2) &&
+              make_tmap_out(&tc, c.out, c.M, c.N, c.ld,
+                            c.half_out ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 32)) {
+            EpiBF16S::Params p{c.alpha, c.half_out};
+            return launch_t<BN, EpiBF16S, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+          }
+        }
+        if constexpr (kk) {
+          EpiBF16::Params p{c.out, c.ld, c.alpha, c.half_out};
+          return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        }
       }
       break;
     case EPI_RESID: {
-      EpiResid::Params p{(float*)c.out, c.ld, c.alpha, c.atomic};
-      return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+      if constexpr (ch32) {
+        if (stage_ok(c.out, c.ld, 4) &&
+            make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
+          EpiResidS::Params p{c.alpha};
+          return launch_t<BN, EpiResidS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        }
+      }
+      if constexpr (kk) {
+        EpiResid::Params p{(float*)c.out, c.ld, c.alpha, c.atomic};
+        return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+      }
+      break;
     }
     case EPI_SWIGLU:
       if constexpr (kk && ch32) {
         EpiSwiGLU::Params p{(__nv_bfloat16*)c.out, c.ld, (__nv_bfloat16*)c.aux1,
                             (__nv_bfloat16*)c.aux2};
-        return launch_t<BN, EpiSwiGLU, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        return launch_t<BN, EpiSwiGLU, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
       }
       break;
     case EPI_ADD:
       if constexpr (kk) {
         EpiAdd::Params p{(float*)c.out, (const float*)c.aux3, c.ld, c.alpha};
-        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
       }
       break;
     case EPI_SWIGLU_BWD:
       if constexpr ((kk || kmn) && ch32) {
-        EpiSwiGLUBwd::Params p{(__nv_bfloat16*)c.out, (const __nv_bfloat16*)c.aux3,
-                               (const __nv_bfloat16*)c.aux1, c.aux_ld, c.alpha};
-        return launch_t<BN, EpiSwiGLUBwd, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        // dh13 [M, 2F] bf16: the chunk of 32 features fills 64 columns
+        if (!make_tmap_out(&tc, c.out, c.M, (int)(2 * c.aux_ld), 2 * c.aux_ld,
+                           CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64))
+          return cudaErrorInvalidValue;
+        EpiSwiGLUBwdS::Params p{(const __nv_bfloat16*)c.aux3, (const __nv_bfloat16*)c.aux1,
+                                c.aux_ld, c.alpha};
+        return launch_t<BN, EpiSwiGLUBwdS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
       }
       break;
     case EPI_F32_STATS:
       if constexpr (kk && ch32) {
+        if (stage_ok(c.out, c.ld, 4) &&
+            make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
+          EpiF32StatsS::Params p{(float2*)c.aux1, c.aux_ld};
+          return launch_t<BN, EpiF32StatsS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        }
         EpiF32Stats::Params p{(float*)c.out, c.ld, (float2*)c.aux1, c.aux_ld};
-        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, sh, p, grid, st);
+        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
       }
       break;
     default:

@@ -61,6 +61,9 @@ struct GemmCfg {
   static constexpr int CH = (BN % 32 == 0) ? 32 : 16;   // epilogue column chunk
   // ring + 1 KB of barriers / bookkeeping + 1 KB alignment slack
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2048;
+  // staged epilogues add one box slot per epilogue warp after the barriers
+  static constexpr int SMEM_BYTES_STAGED = SMEM_BYTES + 8 * 4096;
+  static_assert(SMEM_BYTES_STAGED <= 232448, "shared memory per CTA");
 };
 
 // ------------------------------------------------------------------ epilogues
@@ -232,77 +235,6 @@ struct EpiAdd {
   }
 };
 
-// SwiGLU backward (ffnBwdFull, mil_dynamic.h:320-409): acc = d_gate[m, f] for
-// 32 consecutive features f; with the saved h1, h3 [m, F] (bf16):
-//   dh1 = alpha*dg * h3 * s * (1 + h1 * (1 - s)),  s = sigmoid(h1)
-//   dh3 = alpha*dg * h1 * s
-// written bf16 into dh13 [m, 2F] in the W1/W3 16-row-interleaved order.
-struct EpiSwiGLUBwd {
-  struct Params {
-    __nv_bfloat16* dh13; const __nv_bfloat16* h1; const __nv_bfloat16* h3; long long F; float alpha;
-  };
-  __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
-    if (m >= M || n0 >= N) return;
-    const int bytes = 2 * min(ncols, N - n0);
-    prefetch_row_l2(p.h1 + (long long)m * p.F + n0, bytes);
-    prefetch_row_l2(p.h3 + (long long)m * p.F + n0, bytes);
-  }
-  template <int CH>
-  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
-                               int M, int N) {
-    static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
-    if (m >= M || n0 >= N) return;
-    const __nv_bfloat16* a = p.h1 + (long long)m * p.F + n0;
-    const __nv_bfloat16* b = p.h3 + (long long)m * p.F + n0;
-    __nv_bfloat16* out = p.dh13 + (long long)m * 2 * p.F;
-    // all 32 features of h1 and h3 are loaded before any store is issued, so
-    // the eight 16-byte loads are in flight together
-    uint4 ra[4], rb[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      ra[q] = *reinterpret_cast<const uint4*>(a + 8 * q);
-      rb[q] = *reinterpret_cast<const uint4*>(b + 8 * q);
-    }
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int f0 = n0 + 16 * half;            // 16 features of block c = f0 / 16
-      float d1[16], d3[16];
-#pragma unroll
-      for (int j = 0; j < 16; j += 8) {
-        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra[2 * half + j / 8]);
-        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb[2 * half + j / 8]);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 x1 = __bfloat1622float2(ha[t]);
-          const float2 x3 = __bfloat1622float2(hb[t]);
-          const float g0 = p.alpha * v[16 * half + j + 2 * t];
-          const float g1 = p.alpha * v[16 * half + j + 2 * t + 1];
-          const float s0 = __fdividef(1.0f, 1.0f + __expf(-x1.x));
-          const float s1 = __fdividef(1.0f, 1.0f + __expf(-x1.y));
-          d1[j + 2 * t] = g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0));
-          d1[j + 2 * t + 1] = g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1));
-          d3[j + 2 * t] = g0 * x1.x * s0;
-          d3[j + 2 * t + 1] = g1 * x1.y * s1;
-        }
-      }
-      __nv_bfloat16* o1 = out + (long long)(f0 / 16) * 32;
-#pragma unroll
-      for (int j = 0; j < 16; j += 8) {
-        uint4 p1, p3;
-        __nv_bfloat162* h1 = reinterpret_cast<__nv_bfloat162*>(&p1);
-        __nv_bfloat162* h3 = reinterpret_cast<__nv_bfloat162*>(&p3);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          h1[t] = __floats2bfloat162_rn(d1[j + 2 * t], d1[j + 2 * t + 1]);
-          h3[t] = __floats2bfloat162_rn(d3[j + 2 * t], d3[j + 2 * t + 1]);
-        }
-        *reinterpret_cast<uint4*>(o1 + j) = p1;
-        *reinterpret_cast<uint4*>(o1 + 16 + j) = p3;
-      }
-    }
-  }
-};
-
 // fp32 residual update, row-major:  x[m*ld + n] += alpha * acc
 // (atomic: red.global.add, for split-K accumulation into gradient buffers)
 struct EpiResid {
@@ -391,6 +323,153 @@ struct EpiSwiGLU {
   }
 };
 
+// ------------------------------------------------------------------ staged epilogues
+// A staged functor (kStage 1: store, 2: element-wise add into the output)
+// turns one accumulator chunk of its row into kCols output values; the kernel
+// writes the warp's 32 rows into a swizzled shared-memory box and one lane
+// sends the box with a TMA tensor store (or reduce-add), so global memory
+// sees whole 128-byte lines written asynchronously instead of 32 scattered
+// row segments per store instruction.  The output tensor map (tmC) describes
+// the destination; boxes are clipped to its extent by the hardware.
+template <class E, class = void>
+struct EpiStage { static constexpr int value = 0; };
+template <class E>
+struct EpiStage<E, decltype(void(E::kStage))> { static constexpr int value = E::kStage; };
+
+constexpr int GEMM_STAGE_SLOT = 4096;   // shared-memory box per epilogue warp
+
+// fp32 row-major store (tmC: fp32 [M, N]).
+struct EpiF32S {
+  static constexpr int kStage = 1;
+  static constexpr int kCols = 32;
+  using Out = float;
+  struct Params { int unused; };
+  __device__ static int out_col(const Params&, int n0) { return n0; }
+  template <int CH>
+  __device__ static void stage(const Params&, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               int, int) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) o[j] = v[j];
+  }
+};
+
+// 16-bit row-major store of alpha*acc (bf16, or fp16 if half_out).
+struct EpiBF16S {
+  static constexpr int kStage = 1;
+  static constexpr int kCols = 32;
+  using Out = uint16_t;
+  struct Params { float alpha; int half_out; };
+  __device__ static int out_col(const Params&, int n0) { return n0; }
+  template <int CH>
+  __device__ static void stage(const Params& p, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               int, int) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+      const float x = p.alpha * v[j];
+      o[j] = p.half_out ? __half_as_ushort(__float2half_rn(x))
+                        : __bfloat16_as_ushort(__float2bfloat16_rn(x));
+    }
+  }
+};
+
+// fp32 accumulation  out[m][n] += alpha * acc  through the TMA add (atomic per
+// element in L2, so split-K units may add into the same tile).
+struct EpiResidS {
+  static constexpr int kStage = 2;
+  static constexpr int kCols = 32;
+  using Out = float;
+  struct Params { float alpha; };
+  __device__ static int out_col(const Params&, int n0) { return n0; }
+  template <int CH>
+  __device__ static void stage(const Params& p, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               int, int) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) o[j] = p.alpha * v[j];
+  }
+};
+
+// Classifier logits (fp32 store) plus the chunk's softmax statistics, as EpiF32Stats.
+struct EpiF32StatsS {
+  static constexpr int kStage = 1;
+  static constexpr int kCols = 32;
+  using Out = float;
+  struct Params { float2* stats; long long stats_ld; };
+  __device__ static int out_col(const Params&, int n0) { return n0; }
+  template <int CH>
+  __device__ static void stage(const Params& p, int m, int n0, const float (&v)[CH],
+                               Out (&o)[kCols], int M, int N) {
+    float mx = -3.402823466e38f;
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+      o[j] = v[j];
+      if (n0 + j < N) mx = fmaxf(mx, v[j]);
+    }
+    if (m >= M || n0 >= N) return;
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCols; ++j)
+      if (n0 + j < N) sum += __expf(v[j] - mx);
+    p.stats[(long long)m * p.stats_ld + n0 / kCols] = make_float2(mx, sum);
+  }
+};
+
+// SwiGLU backward (ffnBwdFull, mil_dynamic.h:320-409): acc = d_gate[m, f] for
+// 32 consecutive features f0 .. f0+31; with the saved h1, h3 [m, F] (bf16):
+//   dh1 = alpha*dg * h3 * s * (1 + h1 * (1 - s)),  s = sigmoid(h1)
+//   dh3 = alpha*dg * h1 * s
+// written bf16 into dh13 [m, 2F] columns [2*f0, 2*f0 + 64): two 16-feature
+// blocks of (dh1 | dh3), the W1/W3 16-row-interleaved order.
+struct EpiSwiGLUBwdS {
+  static constexpr int kStage = 1;
+  static constexpr int kCols = 64;
+  using Out = uint16_t;
+  struct Params { const __nv_bfloat16* h1; const __nv_bfloat16* h3; long long F; float alpha; };
+  __device__ static int out_col(const Params&, int n0) { return 2 * n0; }
+  __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
+    if (m >= M || n0 >= N) return;
+    const int bytes = 2 * min(ncols, N - n0);
+    prefetch_row_l2(p.h1 + (long long)m * p.F + n0, bytes);
+    prefetch_row_l2(p.h3 + (long long)m * p.F + n0, bytes);
+  }
+  template <int CH>
+  __device__ static void stage(const Params& p, int m, int n0, const float (&v)[CH],
+                               Out (&o)[kCols], int M, int N) {
+    static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
+    uint4 ra[4], rb[4];
+    if (m < M && n0 < N) {
+      const __nv_bfloat16* a = p.h1 + (long long)m * p.F + n0;
+      const __nv_bfloat16* b = p.h3 + (long long)m * p.F + n0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        ra[q] = *reinterpret_cast<const uint4*>(a + 8 * q);
+        rb[q] = *reinterpret_cast<const uint4*>(b + 8 * q);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ra[q] = rb[q] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra[q]);
+      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb[q]);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 x1 = __bfloat1622float2(ha[t]);
+        const float2 x3 = __bfloat1622float2(hb[t]);
+        const int j = 8 * q + 2 * t;                 // feature offset in the chunk
+        const float g0 = p.alpha * v[j], g1 = p.alpha * v[j + 1];
+        const float s0 = __fdividef(1.0f, 1.0f + __expf(-x1.x));
+        const float s1 = __fdividef(1.0f, 1.0f + __expf(-x1.y));
+        const int blk = (j / 16) * 32 + j % 16;      // dh1 slot; dh3 is 16 further
+        o[blk] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0))));
+        o[blk + 1] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1))));
+        o[blk + 16] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x1.x * s0));
+        o[blk + 17] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x1.y * s1));
+      }
+    }
+  }
+};
+
 // ------------------------------------------------------------------ kernel
 // A_MN / B_MN: the operand is stored MN-major in global memory ([K rows][MN
 // contiguous]); its tile is then loaded as 64-wide MN boxes of 64 K-rows (8 KB
@@ -398,8 +477,10 @@ struct EpiSwiGLU {
 template <int BN, class Epi, int AB_FMT, int A_MN = 0, int B_MN = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const GemmShape sh, const typename Epi::Params ep) {
+               const __grid_constant__ CUtensorMap tmC, const GemmShape sh,
+               const typename Epi::Params ep) {
   using C = GemmCfg<BN>;
+  constexpr int STG = EpiStage<Epi>::value;   // 0: direct stores, 1: TMA store, 2: TMA add
   static_assert(!B_MN || BN % 64 == 0, "MN-major B needs whole 64-wide boxes");
   constexpr uint32_t MN_BOX = 64 * GEMM_BK * 2;   // one 64 (MN) x 64 (K) box
   constexpr int STAGES = C::STAGES;
@@ -440,6 +521,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (STG != 0) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -573,6 +655,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const int chunk0 = ((warp - 2) >> 2) * CH;  // first column chunk of this warp
+    // staged epilogues: this warp's shared-memory box (1 KB aligned, after the barriers)
+    const uint32_t sbuf = base + STAGES * C::STAGE_BYTES + 1024 + (warp - 2) * GEMM_STAGE_SLOT;
+    (void)sbuf;
 
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -648,11 +733,56 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
         }
-        Epi::template apply<CH>(ep, m, nt * BN + c, v, sp, sh.M, sh.N);
+        if constexpr (STG == 0) {
+          Epi::template apply<CH>(ep, m, nt * BN + c, v, sp, sh.M, sh.N);
+        } else {
+          // staged: 32 rows x kCols outputs -> swizzled box -> one TMA store / add
+          static_assert(CH == 32, "staged epilogues work on 32-column chunks");
+          using Out = typename Epi::Out;
+          constexpr int KC = Epi::kCols;
+          constexpr int ROWB = KC * (int)sizeof(Out);
+          static_assert(ROWB == 64 || ROWB == 128, "staged box rows are 64 or 128 bytes");
+          static_assert(32 * ROWB <= GEMM_STAGE_SLOT, "staged box exceeds its slot");
+          const int n0 = nt * BN + c;
+          Out o[KC];
+          Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N);
+          if (lane == 0) bulk_wait_read_all();   // the previous box has left the slot
+          __syncwarp();
+          const uint32_t row = sbuf + lane * ROWB;
+#pragma unroll
+          for (int q = 0; q < ROWB / 16; ++q) {
+            // 128B swizzle: 16-byte chunk ^= row % 8; 64B swizzle: chunk ^= (row / 2) % 4
+            const int phys = ROWB == 128 ? (q ^ (lane & 7)) : (q ^ ((lane >> 1) & 3));
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if constexpr (sizeof(Out) == 4) {
+                w[k] = __float_as_uint(o[4 * q + k]);
+              } else {
+                w[k] = (uint32_t)o[8 * q + 2 * k] | ((uint32_t)o[8 * q + 2 * k + 1] << 16);
+              }
+            }
+            st_shared_v4(row + phys * 16, w[0], w[1], w[2], w[3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int y = mt * GEMM_BM + quarter * 32;
+            if (y < sh.M && n0 < sh.N) {
+              const int x = Epi::out_col(ep, n0);
+              if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
+              else tma_reduce_add_2d(&tmC, sbuf, x, y);
+            }
+            bulk_commit_group();
+          }
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty_bar + 8 * acc);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+    if constexpr (STG != 0) {
+      if (lane == 0) bulk_wait_all();   // every box written before the CTA exits
     }
   }
 

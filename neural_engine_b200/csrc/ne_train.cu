@@ -147,19 +147,33 @@ double wave_eff(long long units, int sms) {
   return (double)units / ((double)sms * ((units + sms - 1) / sms));
 }
 
-// N tile for a gradient GEMM (small weight-shaped output, long K): 128 when it
-// fills the SMs noticeably better than 256.  (Split-K with atomic
-// accumulation was measured slower: one atomic add per element per split.)
-int dw_bn(const GemmCall& c, int sms) {
-  const long long mt = (c.M + 127) / 128;
-  const double e256 = wave_eff(mt * ((c.N + 255) / 256), sms);
-  const double e128 = wave_eff(mt * ((c.N + 127) / 128), sms);
-  return e128 > e256 + 0.05 ? 128 : 256;
+// Gradient GEMMs (weight-shaped output, K = tokens) accumulate through the
+// epilogue's TMA add, which is atomic per element in L2, so they may split K
+// freely: take the 256-wide N tile and the split (at most 4, dividing the
+// k-blocks) whose work units fill the SMs best.
+int dw_splits(const GemmCall& c, int sms) {
+  const long long tiles = (long long)((c.M + 127) / 128) * ((c.N + 255) / 256);
+  const int kb = c.K / 64;
+  int best = 1;
+  double best_eff = wave_eff(tiles, sms);
+  for (int s = 2; s <= 4; ++s) {
+    if (kb % s || kb / s < 4) continue;
+    const double e = wave_eff(tiles * s, sms);
+    if (e > best_eff + 0.03) {
+      best = s;
+      best_eff = e;
+    }
+  }
+  return best;
 }
 
 ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
-  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) c.bn = dw_bn(c, ctx->num_sms);
+  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) {
+    c.bn = 256;
+    c.splits = dw_splits(c, ctx->num_sms);
+    c.atomic = 1;
+  }
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));
   ctx->launches++;
