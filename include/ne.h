@@ -186,9 +186,11 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
 /* General form.  a_mn / b_mn: the operand is stored MN-major, i.e. A as
  * [K, M] (lda >= M) and B as [K, N] (ldb >= N) -- the transposed reads of the
  * reference's cblas_sgemm(CblasTrans, ...) calls (train.m:555-738) without a
- * transposed copy.  epi 5: fp32 out = in + alpha*acc (aux0 = in, same ld);
- * epi 6: SwiGLU backward (aux0 = h1, aux1 = h3 [M, aux_ld] bf16; out = dh13
- * [M, 2*aux_ld] bf16 in the W1/W3 16-row-interleaved order).  epi 7: fp32
+ * transposed copy.  epi 4 as above; aux0 (optional) receives the raw
+ * projection h13 [M, N] bf16 (W1/W3 16-row-interleaved columns).  epi 5: fp32
+ * out = in + alpha*acc (aux0 = in, same ld); epi 6: SwiGLU backward of d_gate
+ * = acc (aux0 = the saved h13 [M, 2*aux_ld] bf16; out = dh13 [M, 2*aux_ld]
+ * bf16 in the same interleaved order).  epi 7: fp32
  * out as epi 1, plus for every row m and 32-column chunk c the pair
  * (max, sum of exp(acc - max)) over the chunk's columns < N, written as two
  * floats at aux0 + 2*(m*aux_ld + c) (the classifier's softmax statistics). */

@@ -64,20 +64,22 @@ bool make_tmap_mn(CUtensorMap* tm, const void* ptr, int mn, int K, long long ld)
 }
 
 // Output of a staged epilogue: [rows, cols] row-major with leading dim ld
-// elements, boxes of box_cols x 32 rows whose 64- or 128-byte rows use the
-// matching swizzle (the kernel writes the box in that layout).
+// elements, boxes of box_cols x 32 rows whose 32-, 64- or 128-byte rows use
+// the matching swizzle (the kernel writes the box in that layout).
 bool make_tmap_out(CUtensorMap* tm, void* ptr, int rows, int cols, long long ld,
                    CUtensorMapDataType dt, int elem_bytes, int box_cols) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   const int row_bytes = box_cols * elem_bytes;
-  if (row_bytes != 64 && row_bytes != 128) return false;
+  if (row_bytes != 32 && row_bytes != 64 && row_bytes != 128) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * elem_bytes};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(tm, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                   : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                     : CU_TENSOR_MAP_SWIZZLE_32B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -89,8 +91,8 @@ bool stage_ok(const void* out, long long ld, int elem_bytes) {
 
 template <int BN, class Epi, int FMT, int AMN, int BMN>
 cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                     const GemmShape& sh, const typename Epi::Params& p, int grid,
-                     cudaStream_t st) {
+                     const CUtensorMap& td, const GemmShape& sh, const typename Epi::Params& p,
+                     int grid, cudaStream_t st) {
   using C = GemmCfg<BN>;
   constexpr int smem = EpiStage<Epi>::value ? C::SMEM_BYTES_STAGED : C::SMEM_BYTES;
   static bool attr_done = false;
@@ -101,7 +103,7 @@ cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
     attr_done = true;
   }
   return launch_k(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>, dim3(grid), dim3(GEMM_THREADS),
-                  (size_t)smem, st, ta, tb, tc, sh, p);
+                  (size_t)smem, st, ta, tb, tc, td, sh, p);
 }
 
 // Epilogue dispatch.  K-major x K-major serves every epilogue; the MN-major
@@ -112,13 +114,14 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
   constexpr bool kk = (AMN == 0 && BMN == 0);
   constexpr bool kmn = (AMN == 0 && BMN == 1);
   constexpr bool ch32 = GemmCfg<BN>::CH == 32;
-  CUtensorMap tc;
-  std::memset(&tc, 0, sizeof(tc));   // direct-store epilogues ignore it
+  CUtensorMap tc, td;
+  std::memset(&tc, 0, sizeof(tc));   // direct-store epilogues ignore them
+  std::memset(&td, 0, sizeof(td));
   switch (c.epi) {
     case EPI_F32T:
       if constexpr (kk) {
         EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
-        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_F32: {
@@ -126,11 +129,11 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiF32S::Params p{0};
-          return launch_t<BN, EpiF32S, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+          return launch_t<BN, EpiF32S, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       EpiF32::Params p{(float*)c.out, c.ld, c.split_stride};
-      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
     }
     case EPI_BF16:
       if constexpr (kk || kmn) {
@@ -140,12 +143,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
                             c.half_out ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 32)) {
             EpiBF16S::Params p{c.alpha, c.half_out};
-            return launch_t<BN, EpiBF16S, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+            return launch_t<BN, EpiBF16S, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
           }
         }
         if constexpr (kk) {
           EpiBF16::Params p{c.out, c.ld, c.alpha, c.half_out};
-          return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+          return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       break;
@@ -154,26 +157,31 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiResidS::Params p{c.alpha};
-          return launch_t<BN, EpiResidS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+          return launch_t<BN, EpiResidS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       if constexpr (kk) {
         EpiResid::Params p{(float*)c.out, c.ld, c.alpha, c.atomic};
-        return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     }
     case EPI_SWIGLU:
       if constexpr (kk && ch32) {
-        EpiSwiGLU::Params p{(__nv_bfloat16*)c.out, c.ld, (__nv_bfloat16*)c.aux1,
-                            (__nv_bfloat16*)c.aux2};
-        return launch_t<BN, EpiSwiGLU, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        // gate [M, N/2] bf16; optional h13 [M, N] bf16 (the raw projection)
+        if (!make_tmap_out(&tc, c.out, c.M, c.N / 2, c.ld, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16))
+          return cudaErrorInvalidValue;
+        if (c.aux1 && !make_tmap_out(&td, c.aux1, c.M, c.N, c.N, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                     2, 32))
+          return cudaErrorInvalidValue;
+        EpiSwiGLUS::Params p{c.aux1 != nullptr};
+        return launch_t<BN, EpiSwiGLUS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_ADD:
       if constexpr (kk) {
         EpiAdd::Params p{(float*)c.out, (const float*)c.aux3, c.ld, c.alpha};
-        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_SWIGLU_BWD:
@@ -182,9 +190,8 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (!make_tmap_out(&tc, c.out, c.M, (int)(2 * c.aux_ld), 2 * c.aux_ld,
                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64))
           return cudaErrorInvalidValue;
-        EpiSwiGLUBwdS::Params p{(const __nv_bfloat16*)c.aux3, (const __nv_bfloat16*)c.aux1,
-                                c.aux_ld, c.alpha};
-        return launch_t<BN, EpiSwiGLUBwdS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        EpiSwiGLUBwdS::Params p{(const __nv_bfloat16*)c.aux3, c.aux_ld, c.alpha};
+        return launch_t<BN, EpiSwiGLUBwdS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_F32_STATS:
@@ -192,10 +199,10 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiF32StatsS::Params p{(float2*)c.aux1, c.aux_ld};
-          return launch_t<BN, EpiF32StatsS, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+          return launch_t<BN, EpiF32StatsS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
         }
         EpiF32Stats::Params p{(float*)c.out, c.ld, (float2*)c.aux1, c.aux_ld};
-        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, tc, sh, p, grid, st);
+        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     default:
@@ -254,12 +261,11 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     return cudaErrorInvalidValue;
   if (c.ab_fp16) return cudaErrorInvalidValue;   // bf16 operands only in this build
   if (c.a_mn && !c.b_mn) return cudaErrorInvalidValue;
-  // the SwiGLU epilogues move 8 bf16 at a time and have no scalar path
+  // the SwiGLU epilogues write TMA boxes: 16-byte aligned rows
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (c.epi == EPI_SWIGLU &&
-      (!a16(c.out) || c.ld % 8 || (c.aux1 && !a16(c.aux1)) || (c.aux2 && !a16(c.aux2))))
+  if (c.epi == EPI_SWIGLU && (!a16(c.out) || c.ld % 8 || c.N % 32 || (c.aux1 && !a16(c.aux1))))
     return cudaErrorInvalidValue;
-  if (c.epi == EPI_SWIGLU_BWD && (!a16(c.out) || !a16(c.aux1) || !a16(c.aux3) || c.aux_ld % 8))
+  if (c.epi == EPI_SWIGLU_BWD && (!a16(c.out) || !a16(c.aux3) || c.aux_ld % 8))
     return cudaErrorInvalidValue;
   if (c.epi == EPI_F32_STATS && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u) ||
                                  c.aux_ld < (c.N + 31) / 32))

@@ -276,52 +276,6 @@ struct EpiResid {
   }
 };
 
-// SwiGLU on a W1/W3 row-interleaved weight (16-row blocks: columns
-// [32c, 32c+16) hold h1 of features [16c, 16c+16), [32c+16, 32c+32) hold h3).
-//   gate[m*ld + 16c + j] = bf16( silu(h1_j) * h3_j )
-// Optionally also stores h1 and h3 (bf16, [m, F]) for the backward pass.
-struct EpiSwiGLU {
-  struct Params { __nv_bfloat16* gate; long long ld; __nv_bfloat16* h1; __nv_bfloat16* h3; };
-  template <int CH>
-  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int,
-                               int M, int N) {
-    static_assert(CH == 32, "SwiGLU epilogue needs 32-column chunks");
-    if (m >= M || n0 >= N) return;
-    const long long f0 = n0 >> 1;
-    __nv_bfloat16* g = p.gate + (long long)m * p.ld + f0;
-    float out[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float h1 = v[j], h3 = v[16 + j];
-      out[j] = __fdividef(h1, 1.0f + __expf(-h1)) * h3;
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j += 8) {
-      uint4 pk;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(out[j + 2 * t], out[j + 2 * t + 1]);
-      *reinterpret_cast<uint4*>(g + j) = pk;
-    }
-    if (p.h1 != nullptr) {
-      __nv_bfloat16* a = p.h1 + (long long)m * p.ld + f0;
-      __nv_bfloat16* b = p.h3 + (long long)m * p.ld + f0;
-#pragma unroll
-      for (int j = 0; j < 16; j += 8) {
-        uint4 pa, pb;
-        __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&pa);
-        __nv_bfloat162* hb = reinterpret_cast<__nv_bfloat162*>(&pb);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          ha[t] = __floats2bfloat162_rn(v[j + 2 * t], v[j + 2 * t + 1]);
-          hb[t] = __floats2bfloat162_rn(v[16 + j + 2 * t], v[16 + j + 2 * t + 1]);
-        }
-        *reinterpret_cast<uint4*>(a + j) = pa;
-        *reinterpret_cast<uint4*>(b + j) = pb;
-      }
-    }
-  }
-};
 
 // ------------------------------------------------------------------ staged epilogues
 // A staged functor (kStage 1: store, 2: element-wise add into the output)
@@ -336,7 +290,42 @@ struct EpiStage { static constexpr int value = 0; };
 template <class E>
 struct EpiStage<E, decltype(void(E::kStage))> { static constexpr int value = E::kStage; };
 
-constexpr int GEMM_STAGE_SLOT = 4096;   // shared-memory box per epilogue warp
+constexpr int GEMM_STAGE_SLOT = 4096;   // shared-memory box(es) per epilogue warp
+constexpr int GEMM_STAGE_BOX2 = 2048;   // offset of an optional second box in the slot
+
+// A functor with kCols2 also fills a second box (tmD), e.g. an activation
+// saved for the backward pass.
+template <class E, class = void>
+struct EpiHasBox2 { static constexpr bool value = false; };
+template <class E>
+struct EpiHasBox2<E, decltype(void(E::kCols2))> { static constexpr bool value = true; };
+
+// Write this lane's row (N 16-bit or 32-bit values, 32, 64 or 128 bytes) of a
+// 32-row box at `box`, in the layout of the TMA swizzle that matches the row
+// size (the 16-byte chunk index XORed with address bits 7.. of the row start):
+// conflict-free, 8 lanes cover all banks.
+template <class T, int N>
+__device__ __forceinline__ void stage_row(uint32_t box, int lane, const T (&o)[N]) {
+  constexpr int ROWB = N * (int)sizeof(T);
+  static_assert(ROWB == 32 || ROWB == 64 || ROWB == 128, "box rows of 32, 64 or 128 bytes");
+  const uint32_t row = box + lane * ROWB;
+#pragma unroll
+  for (int q = 0; q < ROWB / 16; ++q) {
+    const int phys = ROWB == 128 ? (q ^ (lane & 7))
+                     : ROWB == 64 ? (q ^ ((lane >> 1) & 3))
+                                  : (q ^ ((lane >> 2) & 1));
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (sizeof(T) == 4) {
+        w[k] = __float_as_uint(o[4 * q + k]);
+      } else {
+        w[k] = (uint32_t)o[8 * q + 2 * k] | ((uint32_t)o[8 * q + 2 * k + 1] << 16);
+      }
+    }
+    st_shared_v4(row + phys * 16, w[0], w[1], w[2], w[3]);
+  }
+}
 
 // fp32 row-major store (tmC: fp32 [M, N]).
 struct EpiF32S {
@@ -413,8 +402,39 @@ struct EpiF32StatsS {
   }
 };
 
+// SwiGLU on the W1/W3 16-row-interleaved projection (ffnFused,
+// mil_dynamic.h:238-306): columns [32c, 32c+16) of the accumulator hold h1 of
+// features [16c, 16c+16), [32c+16, 32c+32) their h3.
+//   gate[m, 16c + j] = bf16( silu(h1_j) * h3_j )          (box 1: 16 columns)
+//   h13[m, 32c .. 32c+32) = bf16(acc)  (optional box 2, saved for the backward)
+struct EpiSwiGLUS {
+  static constexpr int kStage = 1;
+  static constexpr int kCols = 16;
+  using Out = uint16_t;
+  static constexpr int kCols2 = 32;
+  using Out2 = uint16_t;
+  struct Params { int save_h13; };
+  __device__ static int out_col(const Params&, int n0) { return n0 >> 1; }
+  __device__ static int out_col2(const Params&, int n0) { return n0; }
+  __device__ static bool has_box2(const Params& p) { return p.save_h13 != 0; }
+  template <int CH>
+  __device__ static void stage(const Params& p, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               Out2 (&o2)[kCols2], int, int) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float h1 = v[j], h3 = v[16 + j];
+      o[j] = __bfloat16_as_ushort(__float2bfloat16_rn(__fdividef(h1, 1.0f + __expf(-h1)) * h3));
+    }
+    if (p.save_h13) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o2[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+    }
+  }
+};
+
 // SwiGLU backward (ffnBwdFull, mil_dynamic.h:320-409): acc = d_gate[m, f] for
-// 32 consecutive features f0 .. f0+31; with the saved h1, h3 [m, F] (bf16):
+// 32 consecutive features f0 .. f0+31; with h1, h3 from the saved interleaved
+// projection h13 [m, 2F] (bf16, EpiSwiGLUS's second box):
 //   dh1 = alpha*dg * h3 * s * (1 + h1 * (1 - s)),  s = sigmoid(h1)
 //   dh3 = alpha*dg * h1 * s
 // written bf16 into dh13 [m, 2F] columns [2*f0, 2*f0 + 64): two 16-feature
@@ -423,50 +443,47 @@ struct EpiSwiGLUBwdS {
   static constexpr int kStage = 1;
   static constexpr int kCols = 64;
   using Out = uint16_t;
-  struct Params { const __nv_bfloat16* h1; const __nv_bfloat16* h3; long long F; float alpha; };
+  struct Params { const __nv_bfloat16* h13; long long F; float alpha; };
   __device__ static int out_col(const Params&, int n0) { return 2 * n0; }
   __device__ static void prefetch(const Params& p, int m, int n0, int ncols, int M, int N) {
     if (m >= M || n0 >= N) return;
-    const int bytes = 2 * min(ncols, N - n0);
-    prefetch_row_l2(p.h1 + (long long)m * p.F + n0, bytes);
-    prefetch_row_l2(p.h3 + (long long)m * p.F + n0, bytes);
+    prefetch_row_l2(p.h13 + (long long)m * 2 * p.F + 2 * n0, 4 * min(ncols, N - n0));
   }
   template <int CH>
   __device__ static void stage(const Params& p, int m, int n0, const float (&v)[CH],
                                Out (&o)[kCols], int M, int N) {
     static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
-    uint4 ra[4], rb[4];
+    // 128 contiguous bytes: (h1 x16 | h3 x16) for each of the chunk's two 16-feature blocks
+    uint4 r[8];
     if (m < M && n0 < N) {
-      const __nv_bfloat16* a = p.h1 + (long long)m * p.F + n0;
-      const __nv_bfloat16* b = p.h3 + (long long)m * p.F + n0;
+      const uint4* src = reinterpret_cast<const uint4*>(p.h13 + (long long)m * 2 * p.F + 2 * n0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        ra[q] = *reinterpret_cast<const uint4*>(a + 8 * q);
-        rb[q] = *reinterpret_cast<const uint4*>(b + 8 * q);
-      }
+      for (int q = 0; q < 8; ++q) r[q] = src[q];
     } else {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) ra[q] = rb[q] = make_uint4(0, 0, 0, 0);
+      for (int q = 0; q < 8; ++q) r[q] = make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ra[q]);
-      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&rb[q]);
+    for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 x1 = __bfloat1622float2(ha[t]);
-        const float2 x3 = __bfloat1622float2(hb[t]);
-        const int j = 8 * q + 2 * t;                 // feature offset in the chunk
-        const float g0 = p.alpha * v[j], g1 = p.alpha * v[j + 1];
-        const float s0 = __fdividef(1.0f, 1.0f + __expf(-x1.x));
-        const float s1 = __fdividef(1.0f, 1.0f + __expf(-x1.y));
-        const int blk = (j / 16) * 32 + j % 16;      // dh1 slot; dh3 is 16 further
-        o[blk] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0))));
-        o[blk + 1] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1))));
-        o[blk + 16] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x1.x * s0));
-        o[blk + 17] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x1.y * s1));
+      for (int q = 0; q < 2; ++q) {
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&r[4 * b + q]);
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&r[4 * b + 2 + q]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 x1 = __bfloat1622float2(ha[t]);
+          const float2 x3 = __bfloat1622float2(hb[t]);
+          const int f = 16 * b + 8 * q + 2 * t;      // feature offset in the chunk
+          const float g0 = p.alpha * v[f], g1 = p.alpha * v[f + 1];
+          const float s0 = __fdividef(1.0f, 1.0f + __expf(-x1.x));
+          const float s1 = __fdividef(1.0f, 1.0f + __expf(-x1.y));
+          const int slot = 32 * b + 8 * q + 2 * t;   // dh1 slot; dh3 is 16 further
+          o[slot] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x3.x * s0 * (1.0f + x1.x * (1.0f - s0))));
+          o[slot + 1] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x3.y * s1 * (1.0f + x1.y * (1.0f - s1))));
+          o[slot + 16] = __bfloat16_as_ushort(__float2bfloat16_rn(g0 * x1.x * s0));
+          o[slot + 17] = __bfloat16_as_ushort(__float2bfloat16_rn(g1 * x1.y * s1));
+        }
       }
-    }
   }
 };
 
@@ -477,8 +494,8 @@ struct EpiSwiGLUBwdS {
 template <int BN, class Epi, int AB_FMT, int A_MN = 0, int B_MN = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, const GemmShape sh,
-               const typename Epi::Params ep) {
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+               const GemmShape sh, const typename Epi::Params ep) {
   using C = GemmCfg<BN>;
   constexpr int STG = EpiStage<Epi>::value;   // 0: direct stores, 1: TMA store, 2: TMA add
   static_assert(!B_MN || BN % 64 == 0, "MN-major B needs whole 64-wide boxes");
@@ -522,6 +539,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if constexpr (STG != 0) tma_prefetch_desc(&tmC);
+    if constexpr (EpiHasBox2<Epi>::value) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -738,32 +756,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         } else {
           // staged: 32 rows x kCols outputs -> swizzled box -> one TMA store / add
           static_assert(CH == 32, "staged epilogues work on 32-column chunks");
-          using Out = typename Epi::Out;
-          constexpr int KC = Epi::kCols;
-          constexpr int ROWB = KC * (int)sizeof(Out);
-          static_assert(ROWB == 64 || ROWB == 128, "staged box rows are 64 or 128 bytes");
-          static_assert(32 * ROWB <= GEMM_STAGE_SLOT, "staged box exceeds its slot");
+          constexpr bool BOX2 = EpiHasBox2<Epi>::value;
+          static_assert(32 * Epi::kCols * sizeof(typename Epi::Out) <=
+                            (BOX2 ? GEMM_STAGE_BOX2 : GEMM_STAGE_SLOT), "staged box exceeds its slot");
           const int n0 = nt * BN + c;
-          Out o[KC];
-          Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N);
-          if (lane == 0) bulk_wait_read_all();   // the previous box has left the slot
+          typename Epi::Out o[Epi::kCols];
+          if (lane == 0) bulk_wait_read_all();   // the previous boxes have left the slot
           __syncwarp();
-          const uint32_t row = sbuf + lane * ROWB;
-#pragma unroll
-          for (int q = 0; q < ROWB / 16; ++q) {
-            // 128B swizzle: 16-byte chunk ^= row % 8; 64B swizzle: chunk ^= (row / 2) % 4
-            const int phys = ROWB == 128 ? (q ^ (lane & 7)) : (q ^ ((lane >> 1) & 3));
-            uint32_t w[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if constexpr (sizeof(Out) == 4) {
-                w[k] = __float_as_uint(o[4 * q + k]);
-              } else {
-                w[k] = (uint32_t)o[8 * q + 2 * k] | ((uint32_t)o[8 * q + 2 * k + 1] << 16);
-              }
-            }
-            st_shared_v4(row + phys * 16, w[0], w[1], w[2], w[3]);
+          if constexpr (BOX2) {
+            typename Epi::Out2 o2[Epi::kCols2];
+            Epi::template stage<CH>(ep, m, n0, v, o, o2, sh.M, sh.N);
+            stage_row(sbuf + GEMM_STAGE_BOX2, lane, o2);
+          } else {
+            Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N);
           }
+          stage_row(sbuf, lane, o);
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -772,6 +779,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               const int x = Epi::out_col(ep, n0);
               if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
               else tma_reduce_add_2d(&tmC, sbuf, x, y);
+              if constexpr (EpiHasBox2<Epi>::value) {
+                if (Epi::has_box2(ep)) tma_store_2d(&tmD, sbuf + GEMM_STAGE_BOX2, Epi::out_col2(ep, n0), y);
+              }
             }
             bulk_commit_group();
           }

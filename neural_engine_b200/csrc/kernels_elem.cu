@@ -92,7 +92,7 @@ __global__ void embed_rmsnorm_kernel(const int32_t* __restrict__ tok, const void
 __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ P,
                                      int nsplit, long long split_stride, float alpha, int D,
                                      const float* __restrict__ g, float eps,
-                                     __nv_bfloat16* __restrict__ xn) {
+                                     __nv_bfloat16* __restrict__ xn, float* __restrict__ copy) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
@@ -109,6 +109,7 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
       xr[i] = v;
     }
     xs[i] = v;
+    if (copy) copy[(size_t)r * D + i] = v;
   }
   __syncthreads();
   rmsnorm_row_store(xs, g, D, eps, xn + (size_t)r * D, red);
@@ -121,7 +122,7 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
 template <int V4>
 __global__ void __launch_bounds__(256)
 rmsnorm_rows_kernel(const float* __restrict__ x, int rows, const float* __restrict__ g,
-                    float eps, __nv_bfloat16* __restrict__ xn) {
+                    float eps, __nv_bfloat16* __restrict__ xn, float* __restrict__ copy) {
   pdl_trigger();
   pdl_wait();
   constexpr int D = V4 * 128;
@@ -135,6 +136,11 @@ rmsnorm_rows_kernel(const float* __restrict__ x, int rows, const float* __restri
   for (int k = 0; k < V4; ++k) {
     v[k] = xr[lane + 32 * k];
     ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+  }
+  if (copy) {
+    float4* cr = reinterpret_cast<float4*>(copy + (size_t)r * D);
+#pragma unroll
+    for (int k = 0; k < V4; ++k) cr[lane + 32 * k] = v[k];
   }
   ss = warp_sum(ss);
   const float rms = sqrtf(ss / (float)D + eps);
@@ -317,22 +323,27 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
 
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
-                                 int rows, cudaStream_t st) {
+                                 int rows, cudaStream_t st, float* copy) {
   if (nsplit == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(copy) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(g) & 15) == 0 && (reinterpret_cast<uintptr_t>(xn) & 7) == 0) {
     const dim3 grid((rows + 7) / 8);
     switch (D) {
-      case 512: return launch_k(rmsnorm_rows_kernel<4>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
-      case 768: return launch_k(rmsnorm_rows_kernel<6>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
-      case 1024: return launch_k(rmsnorm_rows_kernel<8>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
-      case 2048: return launch_k(rmsnorm_rows_kernel<16>, grid, dim3(256), 0, st, x, rows, g, eps, xn);
+      case 512: return launch_k(rmsnorm_rows_kernel<4>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
+                          copy);
+      case 768: return launch_k(rmsnorm_rows_kernel<6>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
+                          copy);
+      case 1024: return launch_k(rmsnorm_rows_kernel<8>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
+                          copy);
+      case 2048: return launch_k(rmsnorm_rows_kernel<16>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
+                          copy);
       default: break;
     }
   }
   const int threads = D >= 1024 ? 256 : 128;
   const size_t smem = (size_t)(D + 32) * sizeof(float);
   return launch_k(resid_rmsnorm_kernel, dim3(rows), dim3(threads), smem, st, x, P, nsplit,
-                  split_stride, alpha, D, g, eps, xn);
+                  split_stride, alpha, D, g, eps, xn, copy);
 }
 
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,

@@ -658,7 +658,8 @@ NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   c.K = d->K; c.epi = d->epi; c.out = d->out; c.ld = d->ld; c.alpha = d->alpha;
   c.bn = d->bn; c.half_out = d->half_out; c.splits = 1;
   if (d->epi == EPI_ADD) c.aux3 = d->aux0;
-  if (d->epi == EPI_SWIGLU_BWD) { c.aux3 = d->aux0; c.aux1 = const_cast<void*>(d->aux1); c.aux_ld = d->aux_ld; }
+  if (d->epi == EPI_SWIGLU_BWD) { c.aux3 = d->aux0; c.aux_ld = d->aux_ld; }
+  if (d->epi == EPI_SWIGLU) c.aux1 = const_cast<void*>(d->aux0);
   if (d->epi == EPI_F32_STATS) { c.aux1 = const_cast<void*>(d->aux0); c.aux_ld = d->aux_ld; }
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
   if (e != cudaSuccess) return fail(ctx, NE_ERR_CUDA, std::string("gemm: ") + cudaGetErrorString(e));

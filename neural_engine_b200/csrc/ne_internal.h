@@ -13,9 +13,9 @@ enum GemmEpi : int {
   EPI_F32 = 1,     // fp32, row-major        out[split][m][n]
   EPI_BF16 = 2,    // bf16, row-major        out[m][n]
   EPI_RESID = 3,   // fp32 residual          x[m][n] += alpha * acc
-  EPI_SWIGLU = 4,  // bf16 silu(h1)*h3 from a W1/W3 16-row-interleaved operand
+  EPI_SWIGLU = 4,  // bf16 silu(h1)*h3 from a W1/W3 16-row-interleaved operand (aux1: h13 save)
   EPI_ADD = 5,     // fp32 out[m][n] = in[m][n] + alpha * acc
-  EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and saved h1, h3
+  EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and the saved h13 (aux3)
   EPI_F32_STATS = 7,   // fp32 row-major + per-32-column (max, sum exp) into aux1 [m][aux_ld]
 };
 
@@ -32,8 +32,8 @@ struct GemmCall {
   long long ld = 0;             // output leading dim (elements)
   long long split_stride = 0;   // elements between split slabs (split-capable epilogues)
   float alpha = 1.0f;
-  void* aux1 = nullptr;         // SwiGLU: h1 store (optional)
-  void* aux2 = nullptr;         // SwiGLU: h3 store (optional)
+  void* aux1 = nullptr;         // SwiGLU: h13 store [M, N] (optional); stats (epi 7)
+  void* aux2 = nullptr;         // unused
   int splits = 1;               // split-K factor (0 = choose)
   int bn = 0;                   // N tile (0 = choose)
   int ab_fp16 = 0;              // 1: fp16 operands, 0: bf16
@@ -42,7 +42,7 @@ struct GemmCall {
   int a_mn = 0;                 // A stored MN-major: [K, M] row-major, lda >= M
   int b_mn = 0;                 // B stored MN-major: [K, N] row-major, ldb >= N
   int half_out = 0;             // EPI_BF16: write fp16 instead of bf16
-  const void* aux3 = nullptr;   // EPI_ADD: input; EPI_SWIGLU_BWD: h1 (aux1 = h3)
+  const void* aux3 = nullptr;   // EPI_ADD: input; EPI_SWIGLU_BWD: h13 [M, 2F]
   long long aux_ld = 0;         // EPI_SWIGLU_BWD: F
   int atomic = 0;               // EPI_RESID: accumulate with atomics (allows split-K)
 };
@@ -56,9 +56,11 @@ int device_num_sms();
 cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int table_f32, int V, int D,
                                  const float* g, float eps, float* x, __nv_bfloat16* xn, int rows,
                                  int* status, cudaStream_t st);
+// x[r] += alpha * sum of nsplit slabs (nsplit may be 0); xn = rmsnorm(x) (bf16);
+// copy (optional) receives the resulting x, e.g. to seed the next residual sum.
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
-                                 int rows, cudaStream_t st);
+                                 int rows, cudaStream_t st, float* copy = nullptr);
 // q_type: 0 = fp32 q, 1 = fp16 q (with fp16 K/V); kv_bf16: q, K and V all bf16
 // (training path).
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,

@@ -13,7 +13,7 @@
 // interleaved in 16-row blocks); per-layer saved activations
 //   X[l] fp32 [M,D] (layer input), XN[l] bf16, QKVR[l] fp32 [M,qkv],
 //   Q/K/V[l] bf16 (post QK-norm + RoPE), O[l] bf16, LSE[l] fp32 [B,Hq,S],
-//   X2[l] fp32, X2N[l] bf16, H1/H3/GATE[l] bf16 [M,F]
+//   X2[l] fp32, X2N[l] bf16, H13[l] bf16 [M,2F] (raw W1/W3 projection), GATE[l] bf16 [M,F]
 // and backward scratch.  The tied embedding's gradient collects the LM-head
 // part (dense GEMM) and the gather's scatter-add.
 #include <cuda_bf16.h>
@@ -54,7 +54,7 @@ struct TrainLayerP {
 
 struct TrainActs {
   float *X, *QKVR, *LSE, *X2;
-  __nv_bfloat16 *XN, *Q, *K, *V, *O, *X2N, *H1, *H3, *GATE;
+  __nv_bfloat16 *XN, *Q, *K, *V, *O, *X2N, *H13, *GATE;
 };
 
 struct TrainState {
@@ -316,7 +316,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
     return o;
   };
   struct Off {
-    size_t X, QKVR, LSE, X2, XN, Q, K, V, O, X2N, H1, H3, GATE;
+    size_t X, QKVR, LSE, X2, XN, Q, K, V, O, X2N, H13, GATE;
   };
   std::vector<Off> off(L);
   for (size_t l = 0; l < L; ++l) {
@@ -324,7 +324,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
     o.X = take(Mx * D * 4); o.QKVR = take(Mx * qkv * 4); o.LSE = take(Mx * m.n_heads * 4);
     o.X2 = take(Mx * D * 4); o.XN = take(Mx * D * 2); o.Q = take(Mx * qd * 2);
     o.K = take(Mx * kvd * 2); o.V = take(Mx * kvd * 2); o.O = take(Mx * qd * 2);
-    o.X2N = take(Mx * D * 2); o.H1 = take(Mx * F * 2); o.H3 = take(Mx * F * 2);
+    o.X2N = take(Mx * D * 2); o.H13 = take(Mx * 2 * F * 2);
     o.GATE = take(Mx * F * 2);
   }
   const size_t oXL = take(Mx * D * 4), oXNF = take(Mx * D * 2);
@@ -347,8 +347,8 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
     a.X2 = (float*)(base + o.X2); a.XN = (__nv_bfloat16*)(base + o.XN);
     a.Q = (__nv_bfloat16*)(base + o.Q); a.K = (__nv_bfloat16*)(base + o.K);
     a.V = (__nv_bfloat16*)(base + o.V); a.O = (__nv_bfloat16*)(base + o.O);
-    a.X2N = (__nv_bfloat16*)(base + o.X2N); a.H1 = (__nv_bfloat16*)(base + o.H1);
-    a.H3 = (__nv_bfloat16*)(base + o.H3); a.GATE = (__nv_bfloat16*)(base + o.GATE);
+    a.X2N = (__nv_bfloat16*)(base + o.X2N); a.H13 = (__nv_bfloat16*)(base + o.H13);
+    a.GATE = (__nv_bfloat16*)(base + o.GATE);
   }
   t->XL = (float*)(base + oXL); t->XNF = (__nv_bfloat16*)(base + oXNF);
   t->dY = (float*)(base + odY); t->dXF = (float*)(base + odXF); t->dX2 = (float*)(base + odX2);
@@ -523,6 +523,8 @@ NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens) {
   NE_CUDA(cudaGetLastError());
   NE_LAUNCH(launch_embed_rmsnorm(t->ids, t->embed_w, 1, V, D, ctx->L[0].rms_att, m.rms_eps,
                                  t->A[0].X, t->A[0].XN, M, ctx->d_status, st));
+  // the attention residual of layer 0 accumulates onto a copy of x
+  NE_CUDA(cudaMemcpyAsync(t->A[0].X2, t->A[0].X, (size_t)M * D * 4, cudaMemcpyDeviceToDevice, st));
   return NE_OK;
 }
 
@@ -541,10 +543,13 @@ NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
                             m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                             m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
   NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
-  GemmCall c = gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_ADD, a.X2, D, alpha);
-  c.aux3 = a.X;
-  if ((s = gemm(ctx, c)) != NE_OK) return s;
-  NE_LAUNCH(launch_resid_rmsnorm(a.X2, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, a.X2N, M, st));
+  // x2 (seeded with x by the preceding norm) += alpha * o.Wo^T
+  if ((s = gemm(ctx, gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_RESID, a.X2, D, alpha))) != NE_OK)
+    return s;
+  // FFN norm of x2; x2 also seeds the FFN residual sum x_next
+  float* xnext = (l + 1 < m.n_layers) ? t->A[l + 1].X : t->XL;
+  NE_LAUNCH(launch_resid_rmsnorm(a.X2, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, a.X2N, M, st,
+                                 xnext));
   return NE_OK;
 }
 
@@ -558,16 +563,17 @@ NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int l) {
   const LayerW& w = ctx->L[l];
   TrainActs& a = t->A[l];
   GemmCall c = gc(a.X2N, D, M, 0, w.w13, D, 2 * F, 0, D, EPI_SWIGLU, a.GATE, F);
-  c.aux1 = a.H1;
-  c.aux2 = a.H3;
+  c.aux1 = a.H13;
   if ((s = gemm(ctx, c)) != NE_OK) return s;
+  // x_next (seeded with x2 by the FFN norm) += alpha * gate.W2^T
   float* xnext = (l + 1 < m.n_layers) ? t->A[l + 1].X : t->XL;
-  c = gc(a.GATE, F, M, 0, w.w2, F, D, 0, F, EPI_ADD, xnext, D, alpha);
-  c.aux3 = a.X2;
-  if ((s = gemm(ctx, c)) != NE_OK) return s;
-  const float* g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
-  __nv_bfloat16* xn = (l + 1 < m.n_layers) ? t->A[l + 1].XN : t->XNF;
-  NE_LAUNCH(launch_resid_rmsnorm(xnext, nullptr, 0, 0, 1.f, D, g, m.rms_eps, xn, M, st));
+  if ((s = gemm(ctx, gc(a.GATE, F, M, 0, w.w2, F, D, 0, F, EPI_RESID, xnext, D, alpha))) != NE_OK)
+    return s;
+  const bool last = l + 1 == m.n_layers;
+  const float* g = last ? ctx->rms_final : ctx->L[l + 1].rms_att;
+  __nv_bfloat16* xn = last ? t->XNF : t->A[l + 1].XN;
+  NE_LAUNCH(launch_resid_rmsnorm(xnext, nullptr, 0, 0, 1.f, D, g, m.rms_eps, xn, M, st,
+                                 last ? nullptr : t->A[l + 1].X2));
   return NE_OK;
 }
 
@@ -621,8 +627,7 @@ NE_API ne_status ne_ffn_bwd(ne_ctx* ctx, int l) {
   const TrainActs& a = t->A[l];
   const TrainLayerP& p = t->P[l];
   GemmCall c = gc(t->dY16, D, M, 0, w.w2, F, F, 1, D, EPI_SWIGLU_BWD, t->DH13, 2 * F, alpha);
-  c.aux3 = a.H1;
-  c.aux1 = a.H3;
+  c.aux3 = a.H13;
   c.aux_ld = F;
   if ((s = gemm(ctx, c)) != NE_OK) return s;
   if ((s = gemm(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F, alpha))) != NE_OK)

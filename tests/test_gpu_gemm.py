@@ -106,6 +106,15 @@ def test_gemm_swiglu_epilogue(eng):
     ref = h1 * (1.0 / (1.0 + torch.exp(-h1))) * h3
     err = (out.cpu().double() - ref).abs().max().item()
     assert err <= 2 ** -8 * ref.abs().max().item() + 1e-3, err
+    # with a second output the raw projection is saved too (bf16, same interleaved columns)
+    h13 = torch.zeros((M, 2 * F), dtype=torch.bfloat16, device="cuda")
+    out2 = torch.zeros_like(out)
+    eng.gemm(da.data_ptr(), K, M, dw.data_ptr(), K, 2 * F, K, 4, out2.data_ptr(), F,
+             aux0=h13.data_ptr())
+    eng.sync()
+    assert torch.equal(out2, out)
+    raw = _ref(a, w13)
+    assert (h13.cpu().double() - raw).abs().max().item() <= 2 ** -8 * raw.abs().max().item()
 
 
 def test_gemm_rejects_bad_k(eng):
@@ -188,10 +197,12 @@ def test_gemm_swiglu_backward_epilogue(eng):
     dy = _bf16((M, D), 25)
     w2 = _bf16((D, F), 26, 0.1)          # W2 [D, F]: MN-major B for d_gate = dY W2
     h1, h3 = _bf16((M, F), 27), _bf16((M, F), 28)
-    ddy, dw2, dh1, dh3 = dy.cuda(), w2.cuda(), h1.cuda(), h3.cuda()
+    # the forward saves h1 / h3 interleaved in 16-feature blocks: (h1 x16 | h3 x16) ...
+    h13 = torch.stack([h1.reshape(M, F // 16, 16), h3.reshape(M, F // 16, 16)], 2).reshape(M, 2 * F)
+    ddy, dw2, dh13 = dy.cuda(), w2.cuda(), h13.cuda()
     out = torch.zeros((M, 2 * F), dtype=torch.bfloat16, device="cuda")
     eng.gemm(ddy.data_ptr(), D, M, dw2.data_ptr(), F, F, D, 6, out.data_ptr(), 2 * F, alpha=0.7,
-             b_mn=1, aux0=dh1.data_ptr(), aux1=dh3.data_ptr(), aux_ld=F)
+             b_mn=1, aux0=dh13.data_ptr(), aux_ld=F)
     eng.sync()
     dg = 0.7 * (dy.double() @ w2.double())
     x1, x3 = h1.double(), h3.double()
