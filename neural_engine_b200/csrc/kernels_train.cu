@@ -44,6 +44,7 @@ __device__ __forceinline__ float block_sum256(float v, float* red) {
 // ------------------------------------------------------------ RMSNorm backward
 // One warp per row (no block barriers in the row reductions); 8 warps per
 // block walk RB_ROWS rows each and reduce their dw partials once per block.
+// All of a row's loads (x, dy, the residual) are issued before its reductions.
 constexpr int RB_ROWS = 2;
 template <int PER>
 __global__ void __launch_bounds__(256)
@@ -55,41 +56,34 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
   pdl_wait();
   extern __shared__ float sdw[];   // [8][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float dwp[PER * 4];
+  float4 dwp[PER];
 #pragma unroll
-  for (int k = 0; k < PER * 4; ++k) dwp[k] = 0.f;
-  float wv[PER * 4];
+  for (int k = 0; k < PER; ++k) dwp[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 wv[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
     const int i = (k * 32 + lane) * 4;
-    if (i < D) {
-      const float4 t = *reinterpret_cast<const float4*>(w + i);
-      wv[4 * k] = t.x; wv[4 * k + 1] = t.y; wv[4 * k + 2] = t.z; wv[4 * k + 3] = t.w;
-    } else {
-      wv[4 * k] = wv[4 * k + 1] = wv[4 * k + 2] = wv[4 * k + 3] = 0.f;
-    }
+    wv[k] = i < D ? *reinterpret_cast<const float4*>(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const int r0 = (blockIdx.x * 8 + warp) * RB_ROWS;
   for (int rr = 0; rr < RB_ROWS; ++rr) {
     const int r = r0 + rr;
     if (r >= M) break;
-    float xv[PER * 4], gv[PER * 4];
-    float ss = 0.f, dot = 0.f;
+    float4 xv[PER], gv[PER], rv[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int i = (k * 32 + lane) * 4;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
-      if (i < D) {
-        a = *reinterpret_cast<const float4*>(x + (size_t)r * D + i);
-        g = *reinterpret_cast<const float4*>(dy + (size_t)r * D + i);
-      }
-      xv[4 * k] = a.x; xv[4 * k + 1] = a.y; xv[4 * k + 2] = a.z; xv[4 * k + 3] = a.w;
-      gv[4 * k] = g.x; gv[4 * k + 1] = g.y; gv[4 * k + 2] = g.z; gv[4 * k + 3] = g.w;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[k] = i < D ? *reinterpret_cast<const float4*>(x + (size_t)r * D + i) : z;
+      gv[k] = i < D ? *reinterpret_cast<const float4*>(dy + (size_t)r * D + i) : z;
+      rv[k] = (residual && i < D) ? *reinterpret_cast<const float4*>(residual + (size_t)r * D + i) : z;
+    }
+    float ss = 0.f, dot = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ss += xv[4 * k + j] * xv[4 * k + j];
-        dot += gv[4 * k + j] * wv[4 * k + j] * xv[4 * k + j];
-      }
+    for (int k = 0; k < PER; ++k) {
+      ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y + xv[k].z * xv[k].z + xv[k].w * xv[k].w;
+      dot += gv[k].x * wv[k].x * xv[k].x + gv[k].y * wv[k].y * xv[k].y +
+             gv[k].z * wv[k].z * xv[k].z + gv[k].w * wv[k].w * xv[k].w;
     }
     ss = warp_sum(ss);
     dot = warp_sum(dot);
@@ -99,21 +93,22 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
     for (int k = 0; k < PER; ++k) {
       const int i = (k * 32 + lane) * 4;
       if (i >= D) continue;
-      float o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        o[j] = rrms * (wv[4 * k + j] * gv[4 * k + j] - xv[4 * k + j] * c);
-        dwp[4 * k + j] += gv[4 * k + j] * xv[4 * k + j] * rrms;
-      }
-      if (residual) {
-        const float4 rs = *reinterpret_cast<const float4*>(residual + (size_t)r * D + i);
-        o[0] += rs.x; o[1] += rs.y; o[2] += rs.z; o[3] += rs.w;
-      }
-      *reinterpret_cast<float4*>(dx + (size_t)r * D + i) = make_float4(o[0], o[1], o[2], o[3]);
+      float4 o;
+      o.x = rrms * (wv[k].x * gv[k].x - xv[k].x * c) + rv[k].x;
+      o.y = rrms * (wv[k].y * gv[k].y - xv[k].y * c) + rv[k].y;
+      o.z = rrms * (wv[k].z * gv[k].z - xv[k].z * c) + rv[k].z;
+      o.w = rrms * (wv[k].w * gv[k].w - xv[k].w * c) + rv[k].w;
+      dwp[k].x += gv[k].x * xv[k].x * rrms;
+      dwp[k].y += gv[k].y * xv[k].y * rrms;
+      dwp[k].z += gv[k].z * xv[k].z * rrms;
+      dwp[k].w += gv[k].w * xv[k].w * rrms;
+      *reinterpret_cast<float4*>(dx + (size_t)r * D + i) = o;
       if (dx16) {
-        __nv_bfloat162* d16 = reinterpret_cast<__nv_bfloat162*>(dx16 + (size_t)r * D + i);
-        d16[0] = __floats2bfloat162_rn(o[0], o[1]);
-        d16[1] = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 pk;
+        bf162* h = reinterpret_cast<bf162*>(&pk);
+        h[0] = __floats2bfloat162_rn(o.x, o.y);
+        h[1] = __floats2bfloat162_rn(o.z, o.w);
+        *reinterpret_cast<uint2*>(dx16 + (size_t)r * D + i) = pk;
       }
     }
   }
@@ -121,9 +116,7 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int i = (k * 32 + lane) * 4;
-      if (i < D)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sdw[warp * D + i + j] = dwp[4 * k + j];
+      if (i < D) *reinterpret_cast<float4*>(sdw + warp * D + i) = dwp[k];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < D; i += blockDim.x) {

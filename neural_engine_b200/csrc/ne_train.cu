@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -87,6 +88,10 @@ struct TrainState {
   float2* ce_stats = nullptr;            // [Mc, ceil(V/32)] classifier softmax statistics
   void* embed_scratch = nullptr;         // sort buffers of the embedding backward
   size_t embed_scratch_bytes = 0;
+  // the micro-step after the token split, captured once as a CUDA graph
+  cudaGraphExec_t step_graph = nullptr;
+  const void* step_graph_rope = nullptr;  // RoPE table the graph was captured with
+  long long steps_run = 0;                // micro-steps so far (the first runs eagerly)
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
@@ -98,6 +103,7 @@ void free_train(ne_ctx* ctx) {
   if (t->d_segs) cudaFree(t->d_segs);
   if (t->d_chunks) cudaFree(t->d_chunks);
   if (t->embed_scratch) cudaFree(t->embed_scratch);
+  if (t->step_graph) cudaGraphExecDestroy(t->step_graph);
   if (t->opt_partial) cudaFree(t->opt_partial);
   if (t->opt_ticket) cudaFree(t->opt_ticket);
   if (t->norm_out) cudaFree(t->norm_out);
@@ -361,6 +367,14 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   t->ce_stats = (float2*)(base + ostats);
   t->tgt = (int32_t*)(base + otgt); t->tok = (int32_t*)(base + otok);
   t->red = (double*)(base + ored);
+  // sort buffers of the local embedding backward (allocated here so that the
+  // step can be captured in a graph)
+  t->embed_scratch_bytes = embed_bwd_scratch_bytes(t->M);
+  {
+    uint8_t* p = nullptr;
+    if ((s = dalloc(ctx, &p, t->embed_scratch_bytes)) != NE_OK) return s;
+    t->embed_scratch = p;
+  }
   return ne_sync(ctx);
 }
 
@@ -516,16 +530,30 @@ static ne_status comm_embed_bwd(ne_ctx* ctx) {
 
 // Split d_tokens [B, S+1] into inputs / targets, embed, first RMSNorm
 // (embed_lookup, cpu_ops.h:433-439; rmsnorm, cpu_ops.h:20-60).
-NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens) {
-  NE_TRAIN_PRELUDE();
-  if (!d_tokens) return NE_ERR_INVALID;
-  split_tokens_kernel<<<(M + 255) / 256, 256, 0, st>>>(d_tokens, B, S, t->ids, t->tgt);
+static ne_status split_tokens(ne_ctx* ctx, const int32_t* d_tokens) {
+  TrainState* t = ctx->train;
+  split_tokens_kernel<<<(t->M + 255) / 256, 256, 0, ctx->st>>>(d_tokens, t->B, t->S, t->ids,
+                                                               t->tgt);
   NE_CUDA(cudaGetLastError());
+  return NE_OK;
+}
+
+// embed + first norm of the split batch (t->ids)
+static ne_status embed_fwd_ids(ne_ctx* ctx) {
+  NE_TRAIN_PRELUDE();
   NE_LAUNCH(launch_embed_rmsnorm(t->ids, t->embed_w, 1, V, D, ctx->L[0].rms_att, m.rms_eps,
                                  t->A[0].X, t->A[0].XN, M, ctx->d_status, st));
   // the attention residual of layer 0 accumulates onto a copy of x
   NE_CUDA(cudaMemcpyAsync(t->A[0].X2, t->A[0].X, (size_t)M * D * 4, cudaMemcpyDeviceToDevice, st));
   return NE_OK;
+}
+
+NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens) {
+  if (!ctx || !ctx->train) return NE_ERR_STATE;
+  if (!d_tokens) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  ne_status s = split_tokens(ctx, d_tokens);
+  return s != NE_OK ? s : embed_fwd_ids(ctx);
 }
 
 // Attention half of a layer (sdpaFwd, mil_dynamic.h:57-234): fused QKV
@@ -688,11 +716,10 @@ NE_API ne_status ne_embed_bwd(ne_ctx* ctx) {
 // targets tokens[:, 1:]); gradients ACCUMULATE into the gradient buffers
 // (mean cross-entropy over the B*S targets of this batch).  *d_loss (device,
 // optional) receives the batch's mean loss.
-NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
-  if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+static ne_status step_body(ne_ctx* ctx, float* d_loss) {
   const int L = ctx->cfg.n_layers;
   ne_status s;
-  if ((s = ne_embed_fwd(ctx, d_tokens)) != NE_OK) return s;
+  if ((s = embed_fwd_ids(ctx)) != NE_OK) return s;
   for (int l = 0; l < L; ++l) {
     if ((s = ne_attn_fwd(ctx, l)) != NE_OK) return s;
     if ((s = ne_ffn_fwd(ctx, l)) != NE_OK) return s;
@@ -702,8 +729,62 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
     if ((s = ne_ffn_bwd(ctx, l)) != NE_OK) return s;
     if ((s = ne_attn_bwd(ctx, l)) != NE_OK) return s;
   }
-  if ((s = ne_embed_bwd(ctx)) != NE_OK) return s;
-  ctx->train->micro_steps++;
+  return ne_embed_bwd(ctx);
+}
+
+// Whether the micro-step runs as a captured graph: on by default (NE_TRAIN_GRAPH=0
+// turns it off); not while gradients are exchanged over NCCL (the comm
+// stream's buckets are issued directly).
+static bool use_step_graph(const ne_ctx* ctx) {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_TRAIN_GRAPH");
+    return !(e && e[0] == '0');
+  }();
+  return on && !comm_active(ctx);
+}
+
+NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
+  if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  ne_status s = split_tokens(ctx, d_tokens);
+  if (s != NE_OK) return s;
+  // The first micro-step runs eagerly (kernel attributes and modules get
+  // loaded outside any capture); later ones replay the captured graph.
+  if (!use_step_graph(ctx) || t->steps_run == 0) {
+    if ((s = step_body(ctx, d_loss)) != NE_OK) return s;
+  } else {
+    // The graph always writes the loss to its own slot; copied out below.
+    float* g_loss = reinterpret_cast<float*>(t->red + 3);
+    if (t->step_graph && t->step_graph_rope != ctx->rope_cs) {
+      NE_CUDA(cudaGraphExecDestroy(t->step_graph));
+      t->step_graph = nullptr;
+    }
+    if (!t->step_graph) {
+      cudaGraph_t g = nullptr;
+      NE_CUDA(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
+      const ne_status sb = step_body(ctx, g_loss);
+      const cudaError_t ec = cudaStreamEndCapture(ctx->st, &g);
+      if (sb != NE_OK) {
+        if (g) cudaGraphDestroy(g);
+        return sb;
+      }
+      if (ec != cudaSuccess)
+        return fail(ctx, NE_ERR_CUDA, std::string("step capture: ") + cudaGetErrorString(ec));
+      const cudaError_t ei = cudaGraphInstantiate(&t->step_graph, g, 0);
+      cudaGraphDestroy(g);
+      if (ei != cudaSuccess) {
+        t->step_graph = nullptr;
+        return fail(ctx, NE_ERR_CUDA, std::string("step graph: ") + cudaGetErrorString(ei));
+      }
+      t->step_graph_rope = ctx->rope_cs;
+    }
+    NE_CUDA(cudaGraphLaunch(t->step_graph, ctx->st));
+    if (d_loss)
+      NE_CUDA(cudaMemcpyAsync(d_loss, g_loss, sizeof(float), cudaMemcpyDeviceToDevice, ctx->st));
+  }
+  t->micro_steps++;
+  t->steps_run++;
   return NE_OK;
 }
 
