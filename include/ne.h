@@ -193,7 +193,10 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
  * bf16 in the same interleaved order).  epi 7: fp32
  * out as epi 1, plus for every row m and 32-column chunk c the pair
  * (max, sum of exp(acc - max)) over the chunk's columns < N, written as two
- * floats at aux0 + 2*(m*aux_ld + c) (the classifier's softmax statistics). */
+ * floats at aux0 + 2*(m*aux_ld + c) (the classifier's softmax statistics).
+ * epi 8: out[n*ld + m] += alpha*acc (transposed like epi 0, accumulated
+ * through element-wise TMA adds, so K is split across the SMs without
+ * partial slabs; the decode projections). */
 typedef struct ne_gemm_desc {
   const void* a; long long lda; int a_mn;
   const void* b; long long ldb; int b_mn;

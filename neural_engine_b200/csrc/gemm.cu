@@ -124,6 +124,16 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
+    case EPI_F32T_ADD:
+      if constexpr (kk && ch32) {
+        // out [N (batch) rows, M (features) columns], leading dim ld
+        if (!stage_ok(c.out, c.ld, 4) ||
+            !make_tmap_out(&tc, c.out, c.N, c.M, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32))
+          return cudaErrorInvalidValue;
+        EpiF32TS::Params p{c.alpha};
+        return launch_t<BN, EpiF32TS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+      }
+      break;
     case EPI_F32: {
       if constexpr (ch32) {
         if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
@@ -213,7 +223,7 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
 
 int pick_bn(const GemmCall& c) {
   if (c.bn) return c.bn;
-  if (c.N <= 16) return c.epi == EPI_SWIGLU ? 32 : 16;
+  if (c.N <= 16) return (c.epi == EPI_SWIGLU || c.epi == EPI_F32T_ADD) ? 32 : 16;
   if (c.N <= 32) return 32;
   if (c.N <= 64) return 64;
   if (c.N <= 128) return 128;
@@ -235,6 +245,20 @@ int device_num_sms() {
 
 int gemm_pick_splits(const GemmCall& c, int num_sms) {
   if (c.splits > 0) return c.splits;
+  if (c.epi == EPI_F32T_ADD) {
+    // partial sums meet in L2 through the TMA add: split until the work
+    // units fill the SMs, keeping at least two 64-deep k-blocks per unit
+    const int bn = pick_bn(c);
+    const int tiles = ((c.M + GEMM_BM - 1) / GEMM_BM) * ((c.N + bn - 1) / bn);
+    const int kb = c.K / GEMM_BK;
+    int best = 1;
+    for (int d = 1; d <= kb / 2; ++d) {
+      if (kb % d) continue;
+      if (tiles * d > num_sms) break;
+      best = d;
+    }
+    return best;
+  }
   if (c.epi != EPI_F32T && c.epi != EPI_F32) return 1;
   const int bn = pick_bn(c);
   const int tiles = ((c.M + GEMM_BM - 1) / GEMM_BM) * ((c.N + bn - 1) / bn);
@@ -276,7 +300,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   const int splits = gemm_pick_splits(c, num_sms);
   const int kb = c.K / GEMM_BK;
   if (kb % splits != 0) return cudaErrorInvalidValue;
-  if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32 && !(c.epi == EPI_RESID && c.atomic))
+  if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32 && c.epi != EPI_F32T_ADD &&
+      !(c.epi == EPI_RESID && c.atomic))
     return cudaErrorInvalidValue;
 
   CUtensorMap ta, tb;

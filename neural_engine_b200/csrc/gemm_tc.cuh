@@ -293,6 +293,11 @@ struct EpiStage<E, decltype(void(E::kStage))> { static constexpr int value = E::
 constexpr int GEMM_STAGE_SLOT = 4096;   // shared-memory box(es) per epilogue warp
 constexpr int GEMM_STAGE_BOX2 = 2048;   // offset of an optional second box in the slot
 
+template <class E, class = void>
+struct EpiTransposed { static constexpr bool value = false; };
+template <class E>
+struct EpiTransposed<E, decltype(void(E::kTransposed))> { static constexpr bool value = true; };
+
 // A functor with kCols2 also fills a second box (tmD), e.g. an activation
 // saved for the backward pass.
 template <class E, class = void>
@@ -326,6 +331,25 @@ __device__ __forceinline__ void stage_row(uint32_t box, int lane, const T (&o)[N
     st_shared_v4(row + phys * 16, w[0], w[1], w[2], w[3]);
   }
 }
+
+// Weight-major ("swap-AB") GEMMs: the accumulator row is an output feature
+// and its columns are batch rows, so the chunk is written transposed into the
+// box (box row = batch row, box column = feature) and added element-wise into
+// out [N (batch), M (features)] fp32 with alpha: split-K units add into the same
+// output, so no partial slabs are written or re-read.
+struct EpiF32TS {
+  static constexpr int kStage = 2;
+  static constexpr int kCols = 32;
+  static constexpr int kTransposed = 1;
+  using Out = float;
+  struct Params { float alpha; };
+  template <int CH>
+  __device__ static void stage(const Params& p, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               int, int) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) o[j] = p.alpha * v[j];
+  }
+};
 
 // fp32 row-major store (tmC: fp32 [M, N]).
 struct EpiF32S {
@@ -770,17 +794,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           } else {
             Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N);
           }
-          stage_row(sbuf, lane, o);
+          if constexpr (EpiTransposed<Epi>::value) {
+            // box row j = batch row n0 + j, column lane = this thread's feature:
+            // 4-byte stores, one box row per instruction (128B swizzle)
+            static_assert(Epi::kCols == 32 && sizeof(typename Epi::Out) == 4, "32x32 fp32 box");
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t a = sbuf + j * 128 + ((((lane >> 2) ^ (j & 7)) << 4) | ((lane & 3) << 2));
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(__float_as_uint(o[j])) : "memory");
+            }
+          } else {
+            stage_row(sbuf, lane, o);
+          }
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
             const int y = mt * GEMM_BM + quarter * 32;
-            if (y < sh.M && n0 < sh.N) {
-              const int x = Epi::out_col(ep, n0);
-              if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
-              else tma_reduce_add_2d(&tmC, sbuf, x, y);
-              if constexpr (EpiHasBox2<Epi>::value) {
-                if (Epi::has_box2(ep)) tma_store_2d(&tmD, sbuf + GEMM_STAGE_BOX2, Epi::out_col2(ep, n0), y);
+            if constexpr (EpiTransposed<Epi>::value) {
+              // output [N (batch), M (features)]: x = feature, y = batch row
+              if (y < sh.M && n0 < sh.N) tma_reduce_add_2d(&tmC, sbuf, y, n0);
+            } else {
+              if (y < sh.M && n0 < sh.N) {
+                const int x = Epi::out_col(ep, n0);
+                if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
+                else tma_reduce_add_2d(&tmC, sbuf, x, y);
+                if constexpr (EpiHasBox2<Epi>::value) {
+                  if (Epi::has_box2(ep))
+                    tma_store_2d(&tmD, sbuf + GEMM_STAGE_BOX2, Epi::out_col2(ep, n0), y);
+                }
               }
             }
             bulk_commit_group();

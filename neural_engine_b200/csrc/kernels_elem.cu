@@ -179,7 +179,7 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
                                 const float* __restrict__ kn, float qk_eps,
                                 const float2* __restrict__ rope_cs, QT* __restrict__ q_out,
                                 KT* __restrict__ kc, KT* __restrict__ vc, int Tmax,
-                                int* status) {
+                                int* status, int zero_src) {
   pdl_trigger();
   pdl_wait();
   constexpr int PER = HD / 32;  // elements per lane (2 or 4), consecutive
@@ -203,6 +203,12 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
   for (int s = 0; s < (nsplit > 0 ? nsplit : 1); ++s) {
 #pragma unroll
     for (int i = 0; i < PER; ++i) v[i] += src[(size_t)s * split_stride + i];
+  }
+  if (zero_src) {
+    // the source is an accumulator the next projection adds into: leave it zeroed
+    float* z = const_cast<float*>(src);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) z[i] = 0.f;
   }
   const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
   if ((is_q || is_k) && qn != nullptr) {
@@ -241,8 +247,9 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
 
 // ---------------------------------------------------------------- SwiGLU (split partials)
 // P: [nsplit][rows][2F] fp32 with W1/W3 interleaved in 16-row blocks.
-__global__ void swiglu_split_kernel(const float* __restrict__ P, int nsplit, long long split_stride,
-                                    int rows, int F, __nv_bfloat16* __restrict__ gate) {
+__global__ void swiglu_split_kernel(float* __restrict__ P, int nsplit, long long split_stride,
+                                    int rows, int F, __nv_bfloat16* __restrict__ gate,
+                                    int zero_src) {
   pdl_trigger();
   pdl_wait();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -253,6 +260,10 @@ __global__ void swiglu_split_kernel(const float* __restrict__ P, int nsplit, lon
   for (int s = 0; s < nsplit; ++s) {
     h1 += P[(size_t)s * split_stride + c1];
     h3 += P[(size_t)s * split_stride + c1 + 16];
+  }
+  if (zero_src) {   // accumulator of the next W1/W3 projection
+    P[c1] = 0.f;
+    P[c1 + 16] = 0.f;
   }
   // generate.py:93-94,190:  silu(h1) * h3,  silu(x) = x * (1 / (1 + exp(-x)))
   gate[idx] = __float2bfloat16_rn(h1 * (1.0f / (1.0f + expf(-h1))) * h3);
@@ -350,7 +361,7 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
                             int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
                             void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
-                            cudaStream_t st, int kv_bf16) {
+                            cudaStream_t st, int kv_bf16, int zero_src) {
   const int warps = rows * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = (warps + 7) / 8;
@@ -358,7 +369,7 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
   return launch_k(qkv_post_kernel<HD_, QT_, KT_>, dim3(blocks), dim3(threads), 0, st, qkv, nsplit, \
                   split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs,     \
                   reinterpret_cast<QT_*>(q_out), reinterpret_cast<KT_*>(kc),                     \
-                  reinterpret_cast<KT_*>(vc), Tmax, status)
+                  reinterpret_cast<KT_*>(vc), Tmax, status, zero_src)
   if (hd == 128) {
     if (kv_bf16) NE_QKV(128, __nv_bfloat16, __nv_bfloat16);
     if (q_type == 1) NE_QKV(128, __half, __half);
@@ -372,11 +383,11 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
-                                __nv_bfloat16* gate, cudaStream_t st) {
+cudaError_t launch_swiglu_split(float* P, int nsplit, long long split_stride, int rows, int F,
+                                __nv_bfloat16* gate, cudaStream_t st, int zero_src) {
   const long long n = (long long)rows * F;
   return launch_k(swiglu_split_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, P,
-                  nsplit, split_stride, rows, F, gate);
+                  nsplit, split_stride, rows, F, gate, zero_src);
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,

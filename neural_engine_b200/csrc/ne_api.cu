@@ -39,23 +39,38 @@ using namespace ne;
 
 namespace {
 
-// Decode-GEMM helper: out_partials[split][rows][n_out] = W[n_out, K] . act[rows, K]^T
+// Decode-GEMM helper (weight-major, batch <= 256 rows in one N tile):
+//   out[rows][n_out] += alpha * act[rows, K] . W[n_out, K]^T
+// through the TMA add, split-K across the SMs (the partial sums meet in L2).
 ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
-                      const __nv_bfloat16* act, long long ld_act, int rows, float* out, int splits,
-                      int* used_splits) {
+                      const __nv_bfloat16* act, long long ld_act, int rows, float* out,
+                      float alpha) {
   GemmCall c;
   c.A = W; c.lda = K; c.M = n_out;
   c.B = act; c.ldb = ld_act; c.N = rows;
   c.K = K;
-  c.epi = EPI_F32T;
-  c.out = out; c.ld = n_out; c.split_stride = (long long)rows * n_out;
-  c.splits = splits;
+  c.epi = EPI_F32T_ADD;
+  c.out = out; c.ld = n_out;
+  c.alpha = alpha;
+  c.splits = 0;
   c.prefetch_a = 1;   // A = weights: loaded while the producer of `act` finishes
-  const int s = gemm_pick_splits(c, ctx->num_sms);
-  c.splits = s;
-  if ((size_t)s * rows * n_out > ctx->part_elems && out == ctx->part)
-    return fail(ctx, NE_ERR_INVALID, "split-K workspace too small");
-  if (used_splits) *used_splits = s;
+  c.splits = gemm_pick_splits(c, ctx->num_sms);
+  NE_LAUNCH(gemm_run(c, ctx->d_status, ctx->st));
+  return NE_OK;
+}
+
+// The tied LM head: out[rows][V] = act . E^T (plain transposed store; the
+// vocabulary gives enough tiles without splitting K).
+ne_status gemm_lm_head(ne_ctx* ctx, const __nv_bfloat16* act, long long ld_act, int rows,
+                       float* out) {
+  GemmCall c;
+  c.A = ctx->embed; c.lda = ctx->cfg.dim; c.M = ctx->cfg.vocab;
+  c.B = act; c.ldb = ld_act; c.N = rows;
+  c.K = ctx->cfg.dim;
+  c.epi = EPI_F32T;
+  c.out = out; c.ld = ctx->cfg.vocab; c.split_stride = (long long)rows * ctx->cfg.vocab;
+  c.splits = 1;
+  c.prefetch_a = 1;
   NE_LAUNCH(gemm_run(c, ctx->d_status, ctx->st));
   return NE_OK;
 }
@@ -107,43 +122,44 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
                                  ctx->x, ctx->xn, B, ctx->d_status, ctx->st));
   prof_mark(ctx, 9);
   const size_t kv_layer = ctx->layer_kv_elems();
+  // ctx->part holds the QKV and W1/W3 sums (zero between uses: their consumers
+  // clear what they read); the Wo and W2 projections add alpha * acc straight
+  // into the fp32 residual stream x.
   for (int l = 0; l < m.n_layers; ++l) {
     const LayerW& w = ctx->L[l];
-    int sp = 1;
-    if ((s = gemm_decode(ctx, w.wqkv, qkv_dim, D, ctx->xn, D, B, ctx->part, 0, &sp)) != NE_OK)
+    if ((s = gemm_decode(ctx, w.wqkv, qkv_dim, D, ctx->xn, D, B, ctx->part, 1.f)) != NE_OK)
       return s;
     prof_mark(ctx, 0);
     __half* kc = ctx->kcache + kv_layer * l;
     __half* vc = ctx->vcache + kv_layer * l;
-    NE_LAUNCH(launch_qkv_post(ctx->part, sp, (long long)B * qkv_dim, B, 1, ctx->state, 0, Hq, Hkv,
-                              hd, m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
+    NE_LAUNCH(launch_qkv_post(ctx->part, 1, 0, B, 1, ctx->state, 0, Hq, Hkv, hd,
+                              m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                               m.qk_eps, ctx->rope_cs, ctx->q, 0, kc, vc, ctx->max_seq,
-                              ctx->d_status, ctx->st));
+                              ctx->d_status, ctx->st, 0, 1));
     prof_mark(ctx, 1);
     NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
                                  ctx->attn_po, ctx->attn_ml, ctx->attn,
                                  ctx->d_status, ctx->st));
     ctx->launches++;  // segment combine kernel
     prof_mark(ctx, 2);
-    if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->part, 0, &sp)) != NE_OK)
+    if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->x, m.res_alpha)) != NE_OK)
       return s;
     prof_mark(ctx, 3);
-    NE_LAUNCH(launch_resid_rmsnorm(ctx->x, ctx->part, sp, (long long)B * D, m.res_alpha, D,
-                                   w.rms_ffn, m.rms_eps, ctx->xn, B, ctx->st));
+    NE_LAUNCH(launch_resid_rmsnorm(ctx->x, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, ctx->xn, B,
+                                   ctx->st));
     prof_mark(ctx, 4);
-    if ((s = gemm_decode(ctx, w.w13, 2 * F, D, ctx->xn, D, B, ctx->part, 0, &sp)) != NE_OK) return s;
+    if ((s = gemm_decode(ctx, w.w13, 2 * F, D, ctx->xn, D, B, ctx->part, 1.f)) != NE_OK) return s;
     prof_mark(ctx, 5);
-    NE_LAUNCH(launch_swiglu_split(ctx->part, sp, (long long)B * 2 * F, B, F, ctx->gate, ctx->st));
+    NE_LAUNCH(launch_swiglu_split(ctx->part, 1, 0, B, F, ctx->gate, ctx->st, 1));
     prof_mark(ctx, 6);
-    if ((s = gemm_decode(ctx, w.w2, D, F, ctx->gate, F, B, ctx->part, 0, &sp)) != NE_OK) return s;
+    if ((s = gemm_decode(ctx, w.w2, D, F, ctx->gate, F, B, ctx->x, m.res_alpha)) != NE_OK) return s;
     prof_mark(ctx, 7);
     const float* next_g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
-    NE_LAUNCH(launch_resid_rmsnorm(ctx->x, ctx->part, sp, (long long)B * D, m.res_alpha, D, next_g,
-                                   m.rms_eps, ctx->xn, B, ctx->st));
+    NE_LAUNCH(launch_resid_rmsnorm(ctx->x, nullptr, 0, 0, 1.f, D, next_g, m.rms_eps, ctx->xn, B,
+                                   ctx->st));
     prof_mark(ctx, 4);
   }
-  if ((s = gemm_decode(ctx, ctx->embed, m.vocab, D, ctx->xn, D, B, ctx->logits, 1, nullptr)) != NE_OK)
-    return s;
+  if ((s = gemm_lm_head(ctx, ctx->xn, D, B, ctx->logits)) != NE_OK) return s;
   prof_mark(ctx, 8);
   NE_LAUNCH(launch_argmax(ctx->logits, B, m.vocab, ctx->tok, d_out_tokens, ctx->state, 1, ctx->st));
   ctx->launches++;  // state advance kernel
@@ -228,9 +244,8 @@ ne_status enqueue_prefill(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, in
                                      ctx->pf_xn, rows, ctx->st));
     }
     // LM head on the last position of each sequence: rows (S-1), (2S-1), ...
-    if ((s = gemm_decode(ctx, ctx->embed, m.vocab, D, ctx->pf_xn + (size_t)(S - 1) * D,
-                         (long long)S * D, nb, ctx->logits + (size_t)b0 * m.vocab, 1, nullptr)) !=
-        NE_OK)
+    if ((s = gemm_lm_head(ctx, ctx->pf_xn + (size_t)(S - 1) * D, (long long)S * D, nb,
+                          ctx->logits + (size_t)b0 * m.vocab)) != NE_OK)
       return s;
   }
   NE_LAUNCH(launch_argmax(ctx->logits, B, m.vocab, d_next, nullptr, ctx->state, 0, ctx->st));
@@ -470,18 +485,9 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
     if ((s = dalloc(ctx, &ctx->rope_cs, cs.size()))) return s;
     NE_CUDA(cudaMemcpy(ctx->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
   }
-  // split-K partials: the largest splits * rows * n_out over the decode GEMMs
-  size_t part = 0;
+  // decode accumulators of the QKV and W1/W3 projections (zero between uses)
   const int qkv_dim = ctx->qkv_dim(), q_dim = ctx->q_dim();
-  const int shapes[4][2] = {{qkv_dim, D}, {D, q_dim}, {2 * F, D}, {D, F}};
-  for (int rows : {std::min(max_batch, 256), max_batch}) {
-    for (auto& sh : shapes) {
-      GemmCall c;
-      c.M = sh[0]; c.K = sh[1]; c.N = rows; c.epi = EPI_F32T; c.splits = 0;
-      const int sp = gemm_pick_splits(c, ctx->num_sms);
-      part = std::max(part, (size_t)sp * rows * sh[0]);
-    }
-  }
+  const size_t part = (size_t)max_batch * std::max(qkv_dim, 2 * F);
   ctx->part_elems = part;
   const size_t attn_slots = decode_attn_partial_slots(max_batch, m.kv_heads, ctx->num_sms);
   const size_t group = (size_t)(Hq / m.kv_heads);
@@ -508,6 +514,7 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
   NE_CUDA(cudaMemset(ctx->kcache, 0, kv * sizeof(__half)));
   NE_CUDA(cudaMemset(ctx->vcache, 0, kv * sizeof(__half)));
   NE_CUDA(cudaMemset(ctx->state, 0, 2 * sizeof(int)));
+  NE_CUDA(cudaMemset(ctx->part, 0, part * sizeof(float)));
   return NE_OK;
 }
 
@@ -647,7 +654,7 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
 
 NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   if (!ctx || !d || !d->a || !d->b || !d->out || d->M <= 0 || d->N <= 0 || d->K <= 0 ||
-      d->epi < 0 || d->epi > 7)
+      d->epi < 0 || d->epi > 8)
     return NE_ERR_INVALID;
   if (d->K % 64) return fail(ctx, NE_ERR_UNSUPPORTED, "K must be a multiple of 64");
   if (d->a_mn && !d->b_mn) return fail(ctx, NE_ERR_UNSUPPORTED, "MN-major A needs MN-major B");
@@ -657,6 +664,7 @@ NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   c.B = d->b; c.ldb = d->ldb; c.N = d->N; c.b_mn = d->b_mn;
   c.K = d->K; c.epi = d->epi; c.out = d->out; c.ld = d->ld; c.alpha = d->alpha;
   c.bn = d->bn; c.half_out = d->half_out; c.splits = 1;
+  if (d->epi == EPI_F32T_ADD) c.splits = gemm_pick_splits(c, ctx->num_sms);
   if (d->epi == EPI_ADD) c.aux3 = d->aux0;
   if (d->epi == EPI_SWIGLU_BWD) { c.aux3 = d->aux0; c.aux_ld = d->aux_ld; }
   if (d->epi == EPI_SWIGLU) c.aux1 = const_cast<void*>(d->aux0);

@@ -17,6 +17,7 @@ enum GemmEpi : int {
   EPI_ADD = 5,     // fp32 out[m][n] = in[m][n] + alpha * acc
   EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and the saved h13 (aux3)
   EPI_F32_STATS = 7,   // fp32 row-major + per-32-column (max, sum exp) into aux1 [m][aux_ld]
+  EPI_F32T_ADD = 8,    // swap-AB: out[n][m] += alpha * acc through the TMA add (split-K safe)
 };
 
 struct GemmCall {
@@ -67,9 +68,11 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
                             int S_rows, const int* d_pos, int pos0, int Hq, int Hkv, int hd,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
                             void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
-                            cudaStream_t st, int kv_bf16 = 0);
-cudaError_t launch_swiglu_split(const float* P, int nsplit, long long split_stride, int rows, int F,
-                                __nv_bfloat16* gate, cudaStream_t st);
+                            cudaStream_t st, int kv_bf16 = 0, int zero_src = 0);
+// zero_src: clear the consumed sums (the decode accumulators are reused by the
+// next projection's TMA add)
+cudaError_t launch_swiglu_split(float* P, int nsplit, long long split_stride, int rows, int F,
+                                __nv_bfloat16* gate, cudaStream_t st, int zero_src = 0);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
                           int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st);
 // Segment slots (each GROUP x (hd + 2) floats) the decode-attention partial

@@ -243,3 +243,18 @@ def test_gemm_softmax_statistics_epilogue(eng, M, N):
     assert ((st[..., 1] - csum).abs() / csum).max().item() <= 1e-4
     lse = (st[..., 0] + torch.log(st[..., 1])).logsumexp(-1)
     assert (lse - torch.logsumexp(ref, -1)).abs().max().item() <= 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 256, 1024), (1024, 256, 3072), (6144, 5, 1024),
+                                   (1000, 1, 512)])
+def test_gemm_transposed_accumulate(eng, M, N, K):
+    """epi 8 (decode projections): out[n, m] += alpha * (A B^T)[m, n], split-K
+    partials added in L2; the existing contents are kept."""
+    a, b = _bf16((M, K), 41), _bf16((N, K), 42)
+    da, db = a.cuda(), b.cuda()
+    base = torch.randn(N, M, generator=torch.Generator().manual_seed(43))
+    out = base.clone().cuda()
+    eng.gemm(da.data_ptr(), K, M, db.data_ptr(), K, N, K, 8, out.data_ptr(), M, alpha=0.5)
+    eng.sync()
+    ref = base.double() + 0.5 * _ref(a, b).T
+    assert (out.cpu().double() - ref).abs().max().item() <= 0.5 * _tol(a, b, K) + 1e-5
