@@ -23,8 +23,11 @@
 //     (position l/group, head l%group).  Online softmax per head in the log2
 //     domain (q is pre-scaled by log2(e)/sqrt(hd)); the chunk's weights go
 //     through shared memory to the P.V accumulation.
-//   * Every segment writes (m, l, unnormalised O) per q-head; the combine
-//     kernel merges the segments of each pair (log-sum-exp rescaling).
+//   * A pair covered by one segment is normalised and written directly.
+//     Otherwise every segment writes (m, l, unnormalised O) per q-head and
+//     takes a ticket on the pair's counter; the warp that takes the last
+//     ticket merges the pair's segments (log-sum-exp rescaling), writes the
+//     output and resets the counter -- no second kernel, no waiting.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -77,7 +80,8 @@ __global__ void __launch_bounds__(DaCfg<HD, GROUP>::WARPS * 32, 1)
 decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
                    const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos, int P,
                    int Hq, int Hkv, float qscale, float* __restrict__ part_o,
-                   float* __restrict__ part_ml, int* status) {
+                   float* __restrict__ part_ml, int* __restrict__ pair_cnt,
+                   __nv_bfloat16* __restrict__ out, int* status) {
   using C = DaCfg<HD, GROUP>;
   constexpr int CHP = C::CHP, DPL = C::DPL, STAGES = C::STAGES, NW = C::WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -258,6 +262,20 @@ decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
       }
     }
     if (!ok) break;
+    // segments of this pair: warps w0 .. w1 (the same cut as every warp makes)
+    const int w0 = (int)(((long long)pair * T) / L);
+    const int w1 = (int)(((long long)(pair + 1) * T - 1) / L);
+    if (w0 == w1) {
+      // the whole pair is this segment: normalise and write the output
+#pragma unroll
+      for (int h = 0; h < GROUP; ++h) {
+        __nv_bfloat16* o = out + ((size_t)b * Hq + kvh * GROUP + h) * HD + lane * DPL;
+        const float inv = 1.0f / l[h];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[d] = __float2bfloat16_rn(acc[h][d] * inv);
+      }
+      continue;
+    }
     // ---- segment partial: slot (w, pair - first_pair)
     const size_t si = (size_t)w * seg_per_warp + (pair - first_pair);
 #pragma unroll
@@ -270,6 +288,38 @@ decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
         part_ml[(si * GROUP + h) * 2 + 1] = l[h];
       }
     }
+    __threadfence();   // partials visible device-wide before the ticket
+    __syncwarp();
+    int ticket = 0;
+    if (lane == 0) ticket = atomicAdd(pair_cnt + pair, 1);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != w1 - w0) continue;
+    // last segment of the pair to finish: merge all of them
+    __threadfence();
+    if (lane == 0) pair_cnt[pair] = 0;   // ready for the next launch
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+      float M = -1e30f;
+      for (int ww = w0; ww <= w1; ++ww) {
+        const size_t sj = (size_t)ww * seg_per_warp + (pair - (int)(((long long)ww * L) / T));
+        M = fmaxf(M, __ldcg(part_ml + (sj * GROUP + h) * 2));
+      }
+      float Lsum = 0.f, O[DPL];
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) O[d] = 0.f;
+      for (int ww = w0; ww <= w1; ++ww) {
+        const size_t sj = (size_t)ww * seg_per_warp + (pair - (int)(((long long)ww * L) / T));
+        const float wt = exp2f(__ldcg(part_ml + (sj * GROUP + h) * 2) - M);
+        Lsum += __ldcg(part_ml + (sj * GROUP + h) * 2 + 1) * wt;
+        const float* src = part_o + (sj * GROUP + h) * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) O[d] += __ldcg(src + d) * wt;
+      }
+      __nv_bfloat16* o = out + ((size_t)b * Hq + kvh * GROUP + h) * HD + lane * DPL;
+      const float inv = 1.0f / Lsum;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[d] = __float2bfloat16_rn(O[d] * inv);
+    }
   }
   // Drain (bounded): copies issued but not consumed (only after an abort).
   for (int k = gc; k < issued; ++k) {
@@ -281,41 +331,10 @@ decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
   }
 }
 
-// Grid (Hq, B), HD threads: merge the segments of one (sequence, q-head).
-template <int HD, int GROUP>
-__global__ void attn_combine_kernel(const float* __restrict__ part_o,
-                                    const float* __restrict__ part_ml, const int* __restrict__ d_pos,
-                                    int W, int Hq, int Hkv, __nv_bfloat16* __restrict__ out) {
-  constexpr int CHP = 32 / GROUP;
-  pdl_trigger();
-  pdl_wait();
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const int pair = b * Hkv + h / GROUP, g = h % GROUP;
-  const int T = *d_pos + 1;
-  const long long total = (long long)(gridDim.y * Hkv) * T;
-  const long long L = range_len(total, W, CHP);
-  const int seg_per_warp = (int)((L + T - 1) / T) + 1;
-  const int w0 = (int)(((long long)pair * T) / L);
-  const int w1 = (int)(((long long)(pair + 1) * T - 1) / L);
-  float M = -1e30f;
-  for (int w = w0; w <= w1; ++w) {
-    const size_t si = (size_t)w * seg_per_warp + (pair - (int)(((long long)w * L) / T));
-    M = fmaxf(M, part_ml[(si * GROUP + g) * 2]);
-  }
-  float Lsum = 0.f, O = 0.f;
-  for (int w = w0; w <= w1; ++w) {
-    const size_t si = (size_t)w * seg_per_warp + (pair - (int)(((long long)w * L) / T));
-    const float wt = exp2f(part_ml[(si * GROUP + g) * 2] - M);
-    Lsum += part_ml[(si * GROUP + g) * 2 + 1] * wt;
-    O += part_o[(si * GROUP + g) * HD + d] * wt;
-  }
-  out[((size_t)b * Hq + h) * HD + d] = __float2bfloat16_rn(O / Lsum);
-}
-
 template <int HD, int G>
 cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, int Hq, int Hkv,
                      int Tmax, const int* d_pos, float qscale, float* part_o, float* part_ml,
-                     __nv_bfloat16* out, int* status, cudaStream_t st) {
+                     int* pair_cnt, __nv_bfloat16* out, int* status, cudaStream_t st) {
   using C = DaCfg<HD, G>;
   static bool attr = false;
   if (!attr) {
@@ -326,13 +345,9 @@ cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, 
   }
   const int grid = device_num_sms();
   const int P = B * Hkv;
-  cudaError_t e = launch_k(decode_attn_kernel<HD, G>, dim3(grid), dim3(C::WARPS * 32),
-                           (size_t)C::SMEM, st, q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale,
-                           part_o, part_ml, status);
-  if (e != cudaSuccess) return e;
-  return launch_k(attn_combine_kernel<HD, G>, dim3(Hq, B), dim3(HD), 0, st,
-                  (const float*)part_o, (const float*)part_ml, d_pos, grid * C::WARPS, Hq, Hkv,
-                  out);
+  return launch_k(decode_attn_kernel<HD, G>, dim3(grid), dim3(C::WARPS * 32), (size_t)C::SMEM,
+                  st, q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale, part_o, part_ml, pair_cnt, out,
+                  status);
 }
 
 }  // namespace
@@ -347,17 +362,18 @@ size_t decode_attn_partial_slots(int B, int Hkv, int num_sms) {
 
 cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
                                int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
-                               float* part_ml, __nv_bfloat16* out, int* status, cudaStream_t st) {
+                               float* part_ml, int* pair_cnt, __nv_bfloat16* out, int* status,
+                               cudaStream_t st) {
   const float qscale = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   const int group = Hq / Hkv;
   if (hd == 128 && group == 2)
-    return launch_t<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+    return launch_t<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 128 && group == 1)
-    return launch_t<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+    return launch_t<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 64 && group == 1)
-    return launch_t<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+    return launch_t<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 64 && group == 2)
-    return launch_t<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, out, status, st);
+    return launch_t<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   return cudaErrorInvalidValue;
 }
 

@@ -138,9 +138,8 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
                               ctx->d_status, ctx->st, 0, 1));
     prof_mark(ctx, 1);
     NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
-                                 ctx->attn_po, ctx->attn_ml, ctx->attn,
+                                 ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->attn,
                                  ctx->d_status, ctx->st));
-    ctx->launches++;  // segment combine kernel
     prof_mark(ctx, 2);
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->x, m.res_alpha)) != NE_OK)
       return s;
@@ -261,7 +260,8 @@ ne_status free_workspace(ne_ctx* ctx) {
   for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
   ctx->prof_events.clear();
   void* ptrs[] = {ctx->kcache, ctx->vcache, ctx->rope_cs, ctx->x, ctx->xn, ctx->part, ctx->q,
-                  ctx->attn, ctx->attn_po, ctx->attn_ml, ctx->gate, ctx->logits, ctx->tok,
+                  ctx->attn, ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->gate, ctx->logits,
+                  ctx->tok,
                   ctx->state, ctx->out_tokens, ctx->pf_x, ctx->pf_xn, ctx->pf_qkv, ctx->pf_q,
                   ctx->pf_o, ctx->pf_gate, ctx->pf_tok};
   for (void* p : ptrs)
@@ -269,7 +269,8 @@ ne_status free_workspace(ne_ctx* ctx) {
   ctx->kcache = ctx->vcache = nullptr;
   ctx->rope_cs = nullptr;
   ctx->x = nullptr; ctx->xn = nullptr; ctx->part = nullptr; ctx->q = nullptr;
-  ctx->attn = nullptr; ctx->attn_po = nullptr; ctx->attn_ml = nullptr; ctx->gate = nullptr;
+  ctx->attn = nullptr; ctx->attn_po = nullptr; ctx->attn_ml = nullptr; ctx->attn_cnt = nullptr;
+  ctx->gate = nullptr;
   ctx->logits = nullptr; ctx->tok = nullptr; ctx->state = nullptr; ctx->out_tokens = nullptr;
   ctx->pf_x = nullptr; ctx->pf_xn = nullptr; ctx->pf_qkv = nullptr; ctx->pf_q = nullptr;
   ctx->pf_o = nullptr; ctx->pf_gate = nullptr; ctx->pf_tok = nullptr;
@@ -499,6 +500,7 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
       (s = dalloc(ctx, &ctx->attn, B * q_dim)) ||
       (s = dalloc(ctx, &ctx->attn_po, attn_slots * group * hd)) ||
       (s = dalloc(ctx, &ctx->attn_ml, attn_slots * group * 2)) ||
+      (s = dalloc(ctx, &ctx->attn_cnt, B * m.kv_heads)) ||
       (s = dalloc(ctx, &ctx->gate, B * F)) || (s = dalloc(ctx, &ctx->logits, B * m.vocab)) ||
       (s = dalloc(ctx, &ctx->tok, B)) || (s = dalloc(ctx, &ctx->state, 2)) ||
       (s = dalloc(ctx, &ctx->out_tokens, (size_t)max_seq * B)))
@@ -515,6 +517,7 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
   NE_CUDA(cudaMemset(ctx->vcache, 0, kv * sizeof(__half)));
   NE_CUDA(cudaMemset(ctx->state, 0, 2 * sizeof(int)));
   NE_CUDA(cudaMemset(ctx->part, 0, part * sizeof(float)));
+  NE_CUDA(cudaMemset(ctx->attn_cnt, 0, B * m.kv_heads * sizeof(int)));
   return NE_OK;
 }
 

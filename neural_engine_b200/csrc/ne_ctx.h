@@ -71,12 +71,13 @@ struct ne_ctx {
   // decode workspace
   float* x = nullptr;            // [maxB, D]
   __nv_bfloat16* xn = nullptr;   // [maxB, D]
-  float* part = nullptr;         // split-K partial slabs
+  float* part = nullptr;         // decode QKV / W1-W3 accumulators (zero between uses)
   size_t part_elems = 0;
   float* q = nullptr;            // [maxB, Hq, hd]
   __nv_bfloat16* attn = nullptr; // [maxB, q_dim]
   float* attn_po = nullptr;      // [segment slots][group][hd]  (decode attention partials)
   float* attn_ml = nullptr;      // [segment slots][group][2]
+  int* attn_cnt = nullptr;       // [maxB * Hkv] segment tickets per (sequence, kv-head)
   __nv_bfloat16* gate = nullptr; // [maxB, F]
   float* logits = nullptr;       // [maxB, V]
   int32_t* tok = nullptr;        // [maxB]

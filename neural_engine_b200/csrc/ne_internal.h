@@ -80,7 +80,8 @@ cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_to
 size_t decode_attn_partial_slots(int B, int Hkv, int num_sms);
 cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
                                int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
-                               float* part_ml, __nv_bfloat16* out, int* status, cudaStream_t st);
+                               float* part_ml, int* pair_cnt, __nv_bfloat16* out, int* status,
+                               cudaStream_t st);
 
 // ------------------------------------------------------------------ prefill attention
 // q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16
