@@ -6,15 +6,20 @@
 // dS = P (dP - rowsum(P dP)), dQ = dS K / sqrt(hd), dK = dS^T Q / sqrt(hd))
 // followed by the GQA head-group reduction of dK / dV (cpu_ops.h:585
 // gqa_reduce_kv_f16), evaluated flash-style without materialising P:
-//   delta_kernel   D[b,h,s] = sum_d dO * O      (= rowsum(P * dP))
+//   dq_kernel      one CTA per (64-query tile, q-head, sequence); each warp
+//                  owns 16 queries and walks the key tiles up to the diagonal.
+//                  It first forms D[b,h,s] = sum_d dO * O (= rowsum(P * dP))
+//                  for its queries and publishes it for dkdv_kernel.
 //   dkdv_kernel    one CTA per (64-key tile, kv-head, sequence); each warp owns
 //                  16 keys and walks the query tiles at or after its keys,
 //                  for every q-head of the group, so dK/dV of the group are
 //                  summed in registers (no atomics, deterministic)
-//   dq_kernel      one CTA per (64-query tile, q-head, sequence); each warp
-//                  owns 16 queries and walks the key tiles up to the diagonal
 // P is recomputed from the forward's log2-domain row log-sum-exp.  Operands
 // are bf16 (fp16 would underflow dS), fp32 accumulation, m16n8k16 MMAs.
+// The dQ and dK results leave through the RoPE and QK-norm backward
+// (rope_backward_inplace_f16, cpu_ops.h:510-537, and the RMSNorm derivative)
+// applied to the accumulator fragments, and are written as bf16 straight into
+// the gradient of the fused QKV projection; dV is written there unchanged.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -33,29 +38,6 @@ constexpr int KT_Q = 32;      // dkdv: queries per iteration
 constexpr int QT_Q = 64;      // dq: queries per CTA
 constexpr int QT_KEYS = 32;   // dq: keys per iteration
 
-// ---------------------------------------------------------------- delta
-// One warp per (row, head): D = sum_d dO[row, h, d] * O[row, h, d].
-template <int HD>
-__global__ void delta_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, int rows,
-                             int S, int Hq, float* __restrict__ D) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int PER = HD / 32;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= rows * Hq) return;
-  const int r = gw / Hq, h = gw % Hq;
-  const size_t base = ((size_t)r * Hq + h) * HD + lane * PER;
-  float acc = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) acc += __bfloat162float(O[base + i]) * __bfloat162float(dO[base + i]);
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const int b = r / S, s = r % S;
-    D[((size_t)b * Hq + h) * S + s] = acc;
-  }
-}
-
 // Fill `rows` x HD of a padded smem tile from global rows (zero beyond `valid`).
 template <int HD>
 __device__ __forceinline__ void load_rows(bf16* dst, const bf16* src, size_t row_stride, int rows,
@@ -69,13 +51,105 @@ __device__ __forceinline__ void load_rows(bf16* dst, const bf16* src, size_t row
   }
 }
 
+// ---------------------------------------------------------------- fragment epilogue
+// Gradient of one head-vector row held as m16n8k16 accumulator fragments: the
+// lane's values are columns 8j + 2tq, 8j + 2tq + 1 (j < HD/8) of a row; the 4
+// lanes with equal g (lane >> 2) share the row.  Applies the inverse RoPE
+// rotation at `pos` and, with a gain, the QK-norm backward of the raw
+// (pre-norm) row, accumulates the gain gradient into dg, and stores bf16.
+struct QkBwd {
+  const float* gain;      // QK-norm gain (nullptr: no QK-norm)
+  float eps;
+  const float2* rope_cs;  // [pos][HD/2] (cos, sin); nullptr: no rotation (V)
+};
+
+template <int HD>
+__device__ __forceinline__ void head_row_grad_store(const float (&acc)[HD / 8][4], int e0,
+                                                    float scale, bool ok, int pos,
+                                                    const float* raw, const QkBwd& qb,
+                                                    bf16* out, float (&dg)[HD / 8][2], int tq) {
+  constexpr int DT = HD / 8;
+  float d[DT][2];
+#pragma unroll
+  for (int j = 0; j < DT; ++j) {
+    d[j][0] = acc[j][e0] * scale;
+    d[j][1] = acc[j][e0 + 1] * scale;
+  }
+  if (qb.rope_cs != nullptr) {
+    const float2* cs = qb.rope_cs + (size_t)(ok ? pos : 0) * (HD / 2) + tq;
+#pragma unroll
+    for (int j = 0; j < DT; ++j) {
+      const float2 c = cs[4 * j];
+      const float d0 = d[j][0], d1 = d[j][1];
+      d[j][0] = d0 * c.x + d1 * c.y;
+      d[j][1] = d1 * c.x - d0 * c.y;
+    }
+    if (qb.gain != nullptr) {
+      float x[DT][2], ss = 0.f, dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        const float2 xv = ok ? *reinterpret_cast<const float2*>(raw + 8 * j + 2 * tq)
+                             : make_float2(0.f, 0.f);
+        const float2 gv = *reinterpret_cast<const float2*>(qb.gain + 8 * j + 2 * tq);
+        x[j][0] = xv.x;
+        x[j][1] = xv.y;
+        ss += xv.x * xv.x + xv.y * xv.y;
+        dot += d[j][0] * gv.x * xv.x + d[j][1] * gv.y * xv.y;
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      const float rrms = 1.0f / sqrtf(ss / (float)HD + qb.eps);
+      const float c = rrms * rrms * dot / (float)HD;
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        const float2 gv = *reinterpret_cast<const float2*>(qb.gain + 8 * j + 2 * tq);
+        if (ok) {
+          dg[j][0] += d[j][0] * x[j][0] * rrms;
+          dg[j][1] += d[j][1] * x[j][1] * rrms;
+        }
+        d[j][0] = rrms * (gv.x * d[j][0] - x[j][0] * c);
+        d[j][1] = rrms * (gv.y * d[j][1] - x[j][1] * c);
+      }
+    }
+  }
+  if (!ok) return;
+#pragma unroll
+  for (int j = 0; j < DT; ++j)
+    *reinterpret_cast<__nv_bfloat162*>(out + 8 * j + 2 * tq) = __floats2bfloat162_rn(d[j][0], d[j][1]);
+}
+
+// Sum the per-lane gain-gradient partials of the CTA (4 warps) and add them
+// to dgain[HD] (one atomic per column per CTA).
+template <int HD>
+__device__ __forceinline__ void gain_grad_flush(float (&dg)[HD / 8][2], float* red,
+                                                float* dgain) {
+  constexpr int DT = HD / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tq = lane & 3;
+#pragma unroll
+  for (int j = 0; j < DT; ++j)
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float v = dg[j][k];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (lane < 4) red[warp * HD + 8 * j + 2 * tq + k] = v;
+    }
+  __syncthreads();
+  for (int c = threadIdx.x; c < HD; c += blockDim.x)
+    atomicAdd(dgain + c, red[c] + red[HD + c] + red[2 * HD + c] + red[3 * HD + c]);
+}
+
 // ---------------------------------------------------------------- dK, dV
 template <int HD>
 __global__ void __launch_bounds__(128)
 dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V,
             const bf16* __restrict__ dO, const float* __restrict__ LSE,
             const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
-            float scale, float* __restrict__ dK, float* __restrict__ dV) {
+            float scale, const float* __restrict__ qkv_raw, QkBwd kq, bf16* __restrict__ dqkv,
+            float* __restrict__ dkn) {
   constexpr int LD = HD + 8, KS = HD / 16, DT = HD / 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   bf16* sK = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
@@ -209,23 +283,26 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
       }
     }
   }
-  // store fp32 [B][Hkv][S][HD]
-  const size_t ob = ((size_t)b * Hkv + kvh) * S;
+  // dK through the RoPE / k-norm backward, dV unchanged, both bf16 into the
+  // K and V columns of the QKV-projection gradient [B*S][qkv_dim]
+  const int qd = Hq * HD, qkv_dim = (Hq + 2 * Hkv) * HD;
+  const size_t t0 = (size_t)b * S + key0, t1 = (size_t)b * S + key1;
+  const size_t kcol = (size_t)qd + kvh * HD, vcol = kcol + (size_t)Hkv * HD;
+  float dg[DT][2];
 #pragma unroll
-  for (int j = 0; j < DT; ++j) {
-    const int d = j * 8 + 2 * tq;
-    if (key0 < S) {
-      float* pk = dK + (ob + key0) * HD + d;
-      float* pv = dV + (ob + key0) * HD + d;
-      pk[0] = dk[j][0] * scale; pk[1] = dk[j][1] * scale;
-      pv[0] = dv[j][0]; pv[1] = dv[j][1];
-    }
-    if (key1 < S) {
-      float* pk = dK + (ob + key1) * HD + d;
-      float* pv = dV + (ob + key1) * HD + d;
-      pk[0] = dk[j][2] * scale; pk[1] = dk[j][3] * scale;
-      pv[0] = dv[j][2]; pv[1] = dv[j][3];
-    }
+  for (int j = 0; j < DT; ++j) dg[j][0] = dg[j][1] = 0.f;
+  head_row_grad_store<HD>(dk, 0, scale, key0 < S, key0, qkv_raw + t0 * qkv_dim + kcol, kq,
+                          dqkv + t0 * qkv_dim + kcol, dg, tq);
+  head_row_grad_store<HD>(dk, 2, scale, key1 < S, key1, qkv_raw + t1 * qkv_dim + kcol, kq,
+                          dqkv + t1 * qkv_dim + kcol, dg, tq);
+  const QkBwd plain{nullptr, 0.f, nullptr};
+  head_row_grad_store<HD>(dv, 0, 1.0f, key0 < S, key0, nullptr, plain, dqkv + t0 * qkv_dim + vcol,
+                          dg, tq);
+  head_row_grad_store<HD>(dv, 2, 1.0f, key1 < S, key1, nullptr, plain, dqkv + t1 * qkv_dim + vcol,
+                          dg, tq);
+  if (kq.gain != nullptr) {
+    __syncthreads();   // the tiles are no longer read: reuse them for the reduction
+    gain_grad_flush<HD>(dg, reinterpret_cast<float*>(smem_raw), dkn);
   }
 }
 
@@ -233,14 +310,18 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
 template <int HD>
 __global__ void __launch_bounds__(128)
 dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V,
-          const bf16* __restrict__ dO, const float* __restrict__ LSE, const float* __restrict__ Dl,
-          int S, int Hq, int Hkv, int Tmax, float scale_log2, float scale, float* __restrict__ dQ) {
+          const bf16* __restrict__ O, const bf16* __restrict__ dO, const float* __restrict__ LSE,
+          float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2, float scale,
+          const float* __restrict__ qkv_raw, QkBwd qq_, bf16* __restrict__ dqkv,
+          float* __restrict__ dqn) {
   constexpr int LD = HD + 8, KS = HD / 16, DT = HD / 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
   bf16* sdO = sQ + QT_Q * LD;                      // [64][LD]
   bf16* sK = sdO + QT_Q * LD;                      // [32][LD]
   bf16* sV = sK + QT_KEYS * LD;                    // [32][LD]
+  bf16* sO = sV + QT_KEYS * LD;                    // [64][LD]
+  float* sDv = reinterpret_cast<float*>(sO + QT_Q * LD);   // [64]
   pdl_trigger();
   pdl_wait();
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -250,8 +331,26 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
   const size_t qrow = ((size_t)b * S + q0) * Hq + h;
   load_rows<HD>(sQ, Q + qrow * HD, (size_t)Hq * HD, QT_Q, S - q0);
   load_rows<HD>(sdO, dO + qrow * HD, (size_t)Hq * HD, QT_Q, S - q0);
+  load_rows<HD>(sO, O + qrow * HD, (size_t)Hq * HD, QT_Q, S - q0);
   cp_async_commit();
   cp_async_wait<0>();
+  __syncthreads();
+  // D = rowsum(dO * O) of this tile's queries: two threads per row
+  {
+    const int r = threadIdx.x >> 1, hf = threadIdx.x & 1;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int c = hf * (HD / 2); c < (hf + 1) * (HD / 2); c += 2) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sdO + r * LD + c));
+      const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sO + r * LD + c));
+      acc += a.x * o.x + a.y * o.y;
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (hf == 0) {
+      sDv[r] = acc;
+      if (q0 + r < S) Dl[((size_t)b * Hq + h) * S + q0 + r] = acc;
+    }
+  }
   __syncthreads();
   uint32_t qa[KS][4], oa[KS][4];
 #pragma unroll
@@ -263,8 +362,8 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
   const int qa0 = q0 + warp * 16 + g, qa1 = qa0 + 8;
   const float L0 = qa0 < S ? LSE[((size_t)b * Hq + h) * S + qa0] : 0.f;
   const float L1 = qa1 < S ? LSE[((size_t)b * Hq + h) * S + qa1] : 0.f;
-  const float D0 = qa0 < S ? Dl[((size_t)b * Hq + h) * S + qa0] : 0.f;
-  const float D1 = qa1 < S ? Dl[((size_t)b * Hq + h) * S + qa1] : 0.f;
+  const float D0 = sDv[warp * 16 + g];
+  const float D1 = sDv[warp * 16 + g + 8];
   float dq[DT][4];
 #pragma unroll
   for (int j = 0; j < DT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
@@ -326,45 +425,48 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
       }
     }
   }
-  // store fp32 [B*S][Hq][HD]
+  // dQ through the RoPE / q-norm backward, bf16 into the Q columns of the
+  // QKV-projection gradient [B*S][qkv_dim]
+  const int qkv_dim = (Hq + 2 * Hkv) * HD;
+  const size_t t0 = (size_t)b * S + qa0, t1 = (size_t)b * S + qa1;
+  float dg[DT][2];
 #pragma unroll
-  for (int j = 0; j < DT; ++j) {
-    const int d = j * 8 + 2 * tq;
-    if (qa0 < S) {
-      float* p = dQ + (((size_t)b * S + qa0) * Hq + h) * HD + d;
-      p[0] = dq[j][0] * scale; p[1] = dq[j][1] * scale;
-    }
-    if (qa1 < S) {
-      float* p = dQ + (((size_t)b * S + qa1) * Hq + h) * HD + d;
-      p[0] = dq[j][2] * scale; p[1] = dq[j][3] * scale;
-    }
+  for (int j = 0; j < DT; ++j) dg[j][0] = dg[j][1] = 0.f;
+  head_row_grad_store<HD>(dq, 0, scale, qa0 < S, qa0, qkv_raw + t0 * qkv_dim + (size_t)h * HD,
+                          qq_, dqkv + t0 * qkv_dim + (size_t)h * HD, dg, tq);
+  head_row_grad_store<HD>(dq, 2, scale, qa1 < S, qa1, qkv_raw + t1 * qkv_dim + (size_t)h * HD,
+                          qq_, dqkv + t1 * qkv_dim + (size_t)h * HD, dg, tq);
+  if (qq_.gain != nullptr) {
+    __syncthreads();
+    gain_grad_flush<HD>(dg, reinterpret_cast<float*>(smem_raw), dqn);
   }
 }
 
 template <int HD>
 cudaError_t launch_bwd_t(const bf16* Q, const bf16* K, const bf16* V, const bf16* O, const bf16* dO,
                          const float* LSE, float* Dl, int B, int S, int Hq, int Hkv, int Tmax,
-                         float* dQ, float* dK, float* dV, cudaStream_t st) {
+                         const float* qkv_raw, const float* qn, const float* kn, float qk_eps,
+                         const float2* rope_cs, bf16* dqkv, float* dqn, float* dkn,
+                         cudaStream_t st) {
   constexpr int LD = HD + 8;
   const float scale = 1.0f / sqrtf((float)HD);
   const float scale_log2 = scale * 1.4426950408889634f;
-  const int rows = B * S;
-  cudaError_t e = launch_k(delta_kernel<HD>, dim3((rows * Hq + 7) / 8), dim3(256), 0, st, O, dO,
-                           rows, S, Hq, Dl);
-  if (e != cudaSuccess) return e;
   const size_t smem1 = (size_t)(2 * KT_KEYS + 2 * KT_Q) * LD * sizeof(bf16) + 2 * KT_Q * sizeof(float);
-  const size_t smem2 = (size_t)(2 * QT_Q + 2 * QT_KEYS) * LD * sizeof(bf16);
+  const size_t smem2 = (size_t)(3 * QT_Q + 2 * QT_KEYS) * LD * sizeof(bf16) + QT_Q * sizeof(float);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
     cudaFuncSetAttribute(dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
     attr = true;
   }
-  e = launch_k(dkdv_kernel<HD>, dim3((S + KT_KEYS - 1) / KT_KEYS, Hkv, B), dim3(128), smem1, st, Q,
-               K, V, dO, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, dK, dV);
+  // dQ first: it also publishes D, which dK / dV read
+  cudaError_t e = launch_k(dq_kernel<HD>, dim3((S + QT_Q - 1) / QT_Q, Hq, B), dim3(128), smem2, st,
+                           Q, K, V, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                           QkBwd{qn, qk_eps, rope_cs}, dqkv, dqn);
   if (e != cudaSuccess) return e;
-  return launch_k(dq_kernel<HD>, dim3((S + QT_Q - 1) / QT_Q, Hq, B), dim3(128), smem2, st, Q, K, V,
-                  dO, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, dQ);
+  return launch_k(dkdv_kernel<HD>, dim3((S + KT_KEYS - 1) / KT_KEYS, Hkv, B), dim3(128), smem1, st,
+                  Q, K, V, dO, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                  QkBwd{kn, qk_eps, rope_cs}, dqkv, dkn);
 }
 
 }  // namespace
@@ -372,12 +474,15 @@ cudaError_t launch_bwd_t(const bf16* Q, const bf16* K, const bf16* V, const bf16
 cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* V, const __nv_bfloat16* O,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
-                            int Hq, int Hkv, int hd, int Tmax, float* dQ, float* dK, float* dV,
-                            cudaStream_t st) {
+                            int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                            const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
+                            __nv_bfloat16* dqkv, float* dqn, float* dkn, cudaStream_t st) {
   if (hd == 128)
-    return launch_bwd_t<128>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, dQ, dK, dV, st);
+    return launch_bwd_t<128>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn, kn, qk_eps,
+                             rope_cs, dqkv, dqn, dkn, st);
   if (hd == 64)
-    return launch_bwd_t<64>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, dQ, dK, dV, st);
+    return launch_bwd_t<64>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn, kn, qk_eps,
+                            rope_cs, dqkv, dqn, dkn, st);
   return cudaErrorInvalidValue;
 }
 

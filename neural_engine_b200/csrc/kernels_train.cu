@@ -8,8 +8,7 @@
 //                     rmsnorm (generate.py:81-84), the oracle's definition.
 //   ce_rows           per token: loss = -log(softmax(logits)[target] + 1e-10),
 //                     dlogits = (softmax - onehot) * scale  (cpu_ops.h:348-382)
-//   qk_rope_bwd       inverse RoPE rotation (cpu_ops.h:479-506) then per-head
-//                     QK-RMSNorm backward; writes d(qkv) bf16 and gain grads
+//   (the RoPE / QK-norm backward runs inside the attention backward, attn_bwd.cu)
 //   adamw             decoupled AdamW with bias correction (cpu_ops.h:266-303)
 //                     on fp32 masters, writing the bf16 compute copy
 //   sumsq             sum of squares for the global gradient norm (train.m:805-826)
@@ -213,90 +212,6 @@ ce_rows_kernel(const float* __restrict__ logits, const float2* __restrict__ stat
   }
 }
 
-// ------------------------------------------------------------ RoPE + QK-norm backward
-// Grid (ceil(M / QRB), Hq + 2*Hkv); 8 warps, each walks QRB/8 rows of one
-// head-vector h.  Row r = b*S + s is at position pos0 + s.
-constexpr int QRB = 64;
-template <int HD>
-__global__ void qk_rope_bwd_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
-                                   const float* __restrict__ dV, const float* __restrict__ qkv_raw,
-                                   const float* __restrict__ qn, const float* __restrict__ kn,
-                                   float qk_eps, const float2* __restrict__ rope_cs, int M, int S,
-                                   int pos0, int Hq, int Hkv, bf16* __restrict__ dqkv,
-                                   float* __restrict__ dqn, float* __restrict__ dkn) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int PER = HD / 32;
-  __shared__ float red[8][HD];
-  const int h = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
-  const int qkv_dim = (Hq + 2 * Hkv) * HD;
-  const float* gain = is_q ? qn : (is_k ? kn : nullptr);
-  float dg[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) dg[i] = 0.f;
-  for (int r = blockIdx.x * QRB + warp; r < min(M, (blockIdx.x + 1) * QRB); r += 8) {
-    const int b = r / S, s = r % S;
-    float d[PER];
-    if (is_q) {
-      const float* src = dQ + ((size_t)r * Hq + h) * HD + lane * PER;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) d[i] = src[i];
-    } else {
-      const int kvh = is_k ? h - Hq : h - Hq - Hkv;
-      const float* src = (is_k ? dK : dV) + (((size_t)b * Hkv + kvh) * S + s) * HD + lane * PER;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) d[i] = src[i];
-    }
-    if (is_q || is_k) {
-      // inverse rotation of the interleaved pairs
-      const float2* cs = rope_cs + (size_t)(pos0 + s) * (HD / 2) + lane * (PER / 2);
-#pragma unroll
-      for (int i = 0; i < PER / 2; ++i) {
-        const float2 c = cs[i];
-        const float d0 = d[2 * i], d1 = d[2 * i + 1];
-        d[2 * i] = d0 * c.x + d1 * c.y;
-        d[2 * i + 1] = d1 * c.x - d0 * c.y;
-      }
-      if (gain != nullptr) {
-        const float* xr = qkv_raw + (size_t)r * qkv_dim + h * HD + lane * PER;
-        float xv[PER], ss = 0.f, dot = 0.f;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          xv[i] = xr[i];
-          ss += xv[i] * xv[i];
-          dot += d[i] * gain[lane * PER + i] * xv[i];
-        }
-        ss = warp_sum(ss);
-        dot = warp_sum(dot);
-        const float rrms = 1.0f / sqrtf(ss / (float)HD + qk_eps);
-        const float c = rrms * rrms * dot / (float)HD;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          dg[i] += d[i] * xv[i] * rrms;
-          d[i] = rrms * (gain[lane * PER + i] * d[i] - xv[i] * c);
-        }
-      }
-    }
-    bf16* dst = dqkv + (size_t)r * qkv_dim + h * HD + lane * PER;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) dst[i] = __float2bfloat16_rn(d[i]);
-  }
-  if (gain != nullptr) {
-#pragma unroll
-    for (int i = 0; i < PER; ++i) red[warp][lane * PER + i] = dg[i];
-    __syncthreads();
-    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) t += red[w][i];
-      atomicAdd((is_q ? dqn : dkn) + i, t);
-    }
-  }
-}
-
-// ------------------------------------------------------------ embedding backward
 // ------------------------------------------------------------ AdamW
 // cpu_ops.h:266-303, element by element in the same order:
 //   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g
@@ -483,20 +398,6 @@ cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_l
                   tgt, V, scale, loss, dlogits, status);
 }
 
-cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
-                               const float* qkv_raw, const float* qn, const float* kn,
-                               float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
-                               int Hkv, int hd, __nv_bfloat16* dqkv, float* dqn, float* dkn,
-                               cudaStream_t st) {
-  const dim3 grid((M + QRB - 1) / QRB, Hq + 2 * Hkv);
-  if (hd == 128)
-    return launch_k(qk_rope_bwd_kernel<128>, grid, dim3(256), 0, st, dQ, dK, dV, qkv_raw, qn, kn,
-                    qk_eps, rope_cs, M, S, pos0, Hq, Hkv, dqkv, dqn, dkn);
-  if (hd == 64)
-    return launch_k(qk_rope_bwd_kernel<64>, grid, dim3(256), 0, st, dQ, dK, dV, qkv_raw, qn, kn,
-                    qk_eps, rope_cs, M, S, pos0, Hq, Hkv, dqkv, dqn, dkn);
-  return cudaErrorInvalidValue;
-}
 
 
 cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,

@@ -121,22 +121,23 @@ cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
                                 float inv_bc2, const float* norm_out, cudaStream_t st);
+// Causal GQA attention backward; dQ and dK leave through the RoPE and QK-norm
+// backward (qn / kn may be NULL: no QK-norm; the raw projection qkv_raw gives
+// the pre-norm rows) and dQ, dK, dV are written bf16 into dqkv [B*S][qkv_dim];
+// the gain gradients add into dqn / dkn.  Dl: [B][Hq][S] scratch.
 cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* V, const __nv_bfloat16* O,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
-                            int Hq, int Hkv, int hd, int Tmax, float* dQ, float* dK, float* dV,
-                            cudaStream_t st);
+                            int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                            const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
+                            __nv_bfloat16* dqkv, float* dqn, float* dkn, cudaStream_t st);
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
                                int D, const float* residual, float* dx, __nv_bfloat16* dx16,
                                float* dw, cudaStream_t st);
 cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_ld,
                            const int32_t* tgt, int rows, int V, float scale, float* loss,
                            __nv_bfloat16* dlogits, int* status, cudaStream_t st);
-cudaError_t launch_qk_rope_bwd(const float* dQ, const float* dK, const float* dV,
-                               const float* qkv_raw, const float* qn, const float* kn,
-                               float qk_eps, const float2* rope_cs, int M, int S, int pos0, int Hq,
-                               int Hkv, int hd, __nv_bfloat16* dqkv, float* dqn, float* dkn,
-                               cudaStream_t st);
+
 // Deterministic dE[tok[r]] += dy[r] over n rows (embed_bwd.cu); scratch of at
 // least embed_bwd_scratch_bytes(n) bytes.
 size_t embed_bwd_scratch_bytes(int n);

@@ -81,8 +81,8 @@ struct TrainState {
   float* XL = nullptr;                   // final residual [M, D]
   __nv_bfloat16* XNF = nullptr;          // final normed [M, D]
   // backward scratch
-  float *dY = nullptr, *dXF = nullptr, *dX2 = nullptr, *dQ = nullptr, *dK = nullptr,
-        *dV = nullptr, *Dl = nullptr, *logits = nullptr, *loss_rows = nullptr;
+  float *dY = nullptr, *dXF = nullptr, *dX2 = nullptr, *Dl = nullptr, *logits = nullptr,
+        *loss_rows = nullptr;
   __nv_bfloat16 *dY16 = nullptr, *dX216 = nullptr, *DH13 = nullptr, *dO = nullptr,
                 *DQKV = nullptr, *dlogits = nullptr;
   float2* ce_stats = nullptr;            // [Mc, ceil(V/32)] classifier softmax statistics
@@ -335,7 +335,6 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   }
   const size_t oXL = take(Mx * D * 4), oXNF = take(Mx * D * 2);
   const size_t odY = take(Mx * D * 4), odXF = take(Mx * D * 4), odX2 = take(Mx * D * 4);
-  const size_t odQ = take(Mx * qd * 4), odK = take(Mx * kvd * 4), odV = take(Mx * kvd * 4);
   const size_t oDl = take(Mx * m.n_heads * 4), ologits = take((size_t)t->Mc * V * 4);
   const size_t oloss = take(Mx * 4), odY16 = take(Mx * D * 2), odX216 = take(Mx * D * 2);
   const size_t oDH13 = take(Mx * 2 * F * 2), odO = take(Mx * qd * 2), oDQKV = take(Mx * qkv * 2);
@@ -358,7 +357,6 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   }
   t->XL = (float*)(base + oXL); t->XNF = (__nv_bfloat16*)(base + oXNF);
   t->dY = (float*)(base + odY); t->dXF = (float*)(base + odXF); t->dX2 = (float*)(base + odX2);
-  t->dQ = (float*)(base + odQ); t->dK = (float*)(base + odK); t->dV = (float*)(base + odV);
   t->Dl = (float*)(base + oDl); t->logits = (float*)(base + ologits);
   t->loss_rows = (float*)(base + oloss); t->dY16 = (__nv_bfloat16*)(base + odY16);
   t->dX216 = (__nv_bfloat16*)(base + odX216); t->DH13 = (__nv_bfloat16*)(base + oDH13);
@@ -689,12 +687,10 @@ NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int l) {
   if ((s = gemm(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd, alpha))) !=
       NE_OK)
     return s;
-  NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, t->dQ,
-                            t->dK, t->dV, st));
-  ctx->launches += 2;
-  NE_LAUNCH(launch_qk_rope_bwd(t->dQ, t->dK, t->dV, a.QKVR, m.qk_norm ? w.q_norm : nullptr,
-                               m.qk_norm ? w.k_norm : nullptr, m.qk_eps, ctx->rope_cs, M, S, 0,
-                               Hq, Hkv, hd, t->DQKV, p.g_qn, p.g_kn, st));
+  NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, a.QKVR,
+                            m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
+                            m.qk_eps, ctx->rope_cs, t->DQKV, p.g_qn, p.g_kn, st));
+  ctx->launches += 1;
   if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
     return s;
   if ((s = gemm(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D))) != NE_OK)
