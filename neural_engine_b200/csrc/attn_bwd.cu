@@ -154,10 +154,10 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
   extern __shared__ __align__(16) unsigned char smem_raw[];
   bf16* sK = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
   bf16* sV = sK + KT_KEYS * LD;                    // [64][LD]
-  bf16* sQ = sV + KT_KEYS * LD;                    // [32][LD]
-  bf16* sdO = sQ + KT_Q * LD;                      // [32][LD]
-  float* sL = reinterpret_cast<float*>(sdO + KT_Q * LD);   // [32]
-  float* sD = sL + KT_Q;                                   // [32]
+  bf16* sQb = sV + KT_KEYS * LD;                   // [2][32][LD]
+  bf16* sdOb = sQb + 2 * KT_Q * LD;                // [2][32][LD]
+  float* sLb = reinterpret_cast<float*>(sdOb + 2 * KT_Q * LD);   // [2][32]
+  float* sDb = sLb + 2 * KT_Q;                                   // [2][32]
   pdl_trigger();
   pdl_wait();
   const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -167,6 +167,24 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
   const size_t kv_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
   load_rows<HD>(sK, K + kv_base + (size_t)k0 * HD, HD, KT_KEYS, S - k0);
   load_rows<HD>(sV, V + kv_base + (size_t)k0 * HD, HD, KT_KEYS, S - k0);
+  // iterations: (q-head of the group, query tile at or after the keys), the
+  // next one's tiles loading while the current one computes
+  const int qstart = (k0 / KT_Q) * KT_Q;
+  const int n_qt = (S - qstart + KT_Q - 1) / KT_Q;
+  const int n_it = G * n_qt;
+  auto load_it = [&](int it, int buf) {
+    const int h = kvh * G + it / n_qt;
+    const int q0 = qstart + (it % n_qt) * KT_Q;
+    const size_t qrow = ((size_t)b * S + q0) * Hq + h;
+    load_rows<HD>(sQb + buf * KT_Q * LD, Q + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
+    load_rows<HD>(sdOb + buf * KT_Q * LD, dO + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
+    if (threadIdx.x < KT_Q) {
+      const int qq = q0 + threadIdx.x;
+      sLb[buf * KT_Q + threadIdx.x] = qq < S ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
+      sDb[buf * KT_Q + threadIdx.x] = qq < S ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
+    }
+  };
+  if (n_it > 0) load_it(0, 0);
   cp_async_commit();
 
   float dk[DT][4], dv[DT][4];
@@ -177,21 +195,18 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
   const int kw = warp * 16;                 // this warp's keys within the tile
   const int key0 = k0 + kw + g, key1 = key0 + 8;
 
-  for (int gh = 0; gh < G; ++gh) {
-    const int h = kvh * G + gh;
-    for (int q0 = (k0 / KT_Q) * KT_Q; q0 < S; q0 += KT_Q) {
-      __syncthreads();   // previous tile's readers are done
-      const size_t qrow = ((size_t)b * S + q0) * Hq + h;
-      load_rows<HD>(sQ, Q + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
-      load_rows<HD>(sdO, dO + qrow * HD, (size_t)Hq * HD, KT_Q, S - q0);
-      if (threadIdx.x < KT_Q) {
-        const int qq = q0 + threadIdx.x;
-        sL[threadIdx.x] = qq < S ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
-        sD[threadIdx.x] = qq < S ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
-      }
+  for (int it = 0; it < n_it; ++it) {
+    {
+      const int buf = it & 1;
+      const int q0 = qstart + (it % n_qt) * KT_Q;
+      if (it + 1 < n_it) load_it(it + 1, buf ^ 1);
       cp_async_commit();
-      cp_async_wait<0>();
+      cp_async_wait<1>();
       __syncthreads();
+      const bf16* sQ = sQb + buf * KT_Q * LD;
+      const bf16* sdO = sdOb + buf * KT_Q * LD;
+      const float* sL = sLb + buf * KT_Q;
+      const float* sD = sDb + buf * KT_Q;
 
       // S^T = K_w Q^T   [16 keys x 32 queries] : 4 n-tiles of 8 queries
       float st[4][4];
@@ -281,6 +296,7 @@ dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* 
           mma16816_bf16(dk[2 * dp + 1], pa, b2, b3);
         }
       }
+      __syncthreads();   // this buffer is refilled by the next iteration's prefetch
     }
   }
   // dK through the RoPE / k-norm backward, dV unchanged, both bf16 into the
@@ -318,9 +334,9 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
   extern __shared__ __align__(16) unsigned char smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);   // [64][LD]
   bf16* sdO = sQ + QT_Q * LD;                      // [64][LD]
-  bf16* sK = sdO + QT_Q * LD;                      // [32][LD]
-  bf16* sV = sK + QT_KEYS * LD;                    // [32][LD]
-  bf16* sO = sV + QT_KEYS * LD;                    // [64][LD]
+  bf16* sKb = sdO + QT_Q * LD;                     // [2][32][LD]
+  bf16* sVb = sKb + 2 * QT_KEYS * LD;              // [2][32][LD]
+  bf16* sO = sVb + 2 * QT_KEYS * LD;               // [64][LD]
   float* sDv = reinterpret_cast<float*>(sO + QT_Q * LD);   // [64]
   pdl_trigger();
   pdl_wait();
@@ -369,13 +385,22 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
   for (int j = 0; j < DT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
   const size_t kv_base = ((size_t)b * Hkv + kvh) * Tmax * HD;
   const int kend = min(S, q0 + QT_Q);
-  for (int k0 = 0; k0 < kend; k0 += QT_KEYS) {
-    __syncthreads();
-    load_rows<HD>(sK, K + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
-    load_rows<HD>(sV, V + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
+  const int n_kt = (kend + QT_KEYS - 1) / QT_KEYS;
+  auto load_kt = [&](int i, int buf) {
+    const int k0 = i * QT_KEYS;
+    load_rows<HD>(sKb + buf * QT_KEYS * LD, K + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
+    load_rows<HD>(sVb + buf * QT_KEYS * LD, V + kv_base + (size_t)k0 * HD, HD, QT_KEYS, S - k0);
+  };
+  if (n_kt > 0) load_kt(0, 0);
+  cp_async_commit();
+  for (int i = 0; i < n_kt; ++i) {
+    const int k0 = i * QT_KEYS, buf = i & 1;
+    if (i + 1 < n_kt) load_kt(i + 1, buf ^ 1);
     cp_async_commit();
-    cp_async_wait<0>();
+    cp_async_wait<1>();
     __syncthreads();
+    const bf16* sK = sKb + buf * QT_KEYS * LD;
+    const bf16* sV = sVb + buf * QT_KEYS * LD;
     float s[4][4], dp[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -424,6 +449,7 @@ dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __
         mma16816_bf16(dq[2 * dpi + 1], pa, b2, b3);
       }
     }
+    __syncthreads();   // this buffer is refilled by the next iteration's prefetch
   }
   // dQ through the RoPE / q-norm backward, bf16 into the Q columns of the
   // QKV-projection gradient [B*S][qkv_dim]
@@ -451,8 +477,8 @@ cudaError_t launch_bwd_t(const bf16* Q, const bf16* K, const bf16* V, const bf16
   constexpr int LD = HD + 8;
   const float scale = 1.0f / sqrtf((float)HD);
   const float scale_log2 = scale * 1.4426950408889634f;
-  const size_t smem1 = (size_t)(2 * KT_KEYS + 2 * KT_Q) * LD * sizeof(bf16) + 2 * KT_Q * sizeof(float);
-  const size_t smem2 = (size_t)(3 * QT_Q + 2 * QT_KEYS) * LD * sizeof(bf16) + QT_Q * sizeof(float);
+  const size_t smem1 = (size_t)(2 * KT_KEYS + 4 * KT_Q) * LD * sizeof(bf16) + 4 * KT_Q * sizeof(float);
+  const size_t smem2 = (size_t)(3 * QT_Q + 4 * QT_KEYS) * LD * sizeof(bf16) + QT_Q * sizeof(float);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
