@@ -303,6 +303,14 @@ NE_API ne_status ne_rmsnorm_bwd_add(ne_ctx* ctx, const float* d_dy, const float*
                                     const float* d_w, int rows, const float* d_residual,
                                     float* d_dx, float* d_dw);
 
+/* Causal GQA scaled-dot-product attention on device buffers (the core of
+ * sdpaFwd, mil_dynamic.h:184-198): d_q [B*S][Hq*hd] bf16 (token major), d_k /
+ * d_v [B][Hkv][S][hd] bf16; d_out [B*S][Hq*hd] bf16; d_lse (optional) [B][Hq][S]
+ * fp32 log-sum-exp of the scaled scores in the log2 domain.  Enqueued on the
+ * context stream. */
+NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, const void* d_k,
+                                    const void* d_v, int B, int S, void* d_out, float* d_lse);
+
 /* ---- data-parallel gradients (NCCL over NVLink; no reference counterpart:
  * the reference trains on one device) ---------------------------------------
  * Rank 0 makes an id with ne_comm_unique_id and shares it out of band; every

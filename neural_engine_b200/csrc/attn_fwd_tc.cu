@@ -1,0 +1,426 @@
+// attn_fwd_tc.cu -- causal GQA attention forward on the tcgen05 tensor cores
+// (training step, head_dim 128, bf16).
+//
+// Math of the reference's sdpaFwd kernel (ane-training/training/
+// training_dynamic/mil_dynamic.h:184-198: softmax(Q K^T / sqrt(hd) + causal
+// mask) V with GQA head sharing) evaluated flash-style: one CTA owns 128
+// query rows of one (sequence, q-head) and walks 128-key tiles up to the
+// diagonal with an online softmax; it also writes the row log-sum-exp (log2
+// domain) that the backward recomputes P from.
+//
+// Roles (320 threads):
+//   warp 0     TMA producer: Q once, then K and V tiles into a 2-deep ring.
+//   warp 1     MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers
+//              (128 x 128 fp32), and O += P_j V_j into the TMEM output
+//              accumulator (128 x 128 fp32); S_{j+1} is issued before waiting
+//              for P_j so the score MMAs overlap the softmax.
+//   warps 2-9  softmax: two warps per TMEM lane quarter, thread = query row,
+//              each warp of the pair owning 64 of the tile's 128 key columns
+//              (and 64 of the 128 output columns); per tile: row max of the
+//              scaled, masked scores (first pass over TMEM, the pair's halves
+//              combined through shared memory), then p = exp2(s - m) written
+//              bf16 into shared memory as the K-major A operand of the P.V
+//              product (128-byte swizzle), row sums, and the running output
+//              rescaled in TMEM by exp2(m_old - m_new).  At the end O / l
+//              leaves as bf16, and m + log2(l) as the LSE.
+// Operand layouts: Q, K and P K-major (64-element 128-byte swizzle atoms), V
+// read MN-major (64 x 64 boxes) so V[keys][hd] needs no transpose.  Every
+// mbarrier wait is bounded (2 s) and records a timeout in the status word.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "ne_device.cuh"
+#include "ne_internal.h"
+#include "ne_launch.cuh"
+
+namespace ne {
+namespace {
+
+constexpr int TA_HD = 128;          // head dim (this kernel)
+constexpr int TA_BQ = 128;          // query rows per CTA (UMMA M)
+constexpr int TA_BK = 128;          // keys per tile (UMMA N of the score product)
+constexpr int TA_THREADS = 320;
+constexpr int TA_SOFTMAX = 256;     // softmax threads (warps 2..9)
+constexpr uint32_t TA_Q_BYTES = TA_BQ * TA_HD * 2;      // 32 KB: 2 atoms of 64 dims
+constexpr uint32_t TA_K_BYTES = TA_BK * TA_HD * 2;      // 32 KB
+constexpr uint32_t TA_V_BYTES = TA_BK * TA_HD * 2;      // 32 KB: 2 key blocks x 2 hd boxes
+constexpr uint32_t TA_P_BYTES = TA_BQ * TA_BK * 2;      // 32 KB: 2 atoms of 64 keys
+constexpr uint32_t TA_ATOM = 128 * 128;                 // 128 rows x 64 bf16
+constexpr uint32_t TA_MN_BOX = 64 * 64 * 2;             // one 64 (hd) x 64 (keys) V box
+// Q | K[2] | V[2] | P | barriers + row-max exchange (2 x 128 floats), plus 1 KB alignment slack
+constexpr int TA_SMEM = TA_Q_BYTES + 2 * TA_K_BYTES + 2 * TA_V_BYTES + TA_P_BYTES + 2048 + 1024;
+static_assert(1280 + 32 <= 2048, "barrier / exchange area");
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(TA_THREADS, 1)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, int S, int Hq, int Hkv, int Tmax,
+                   float qscale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
+                   int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  const uint32_t sK = sQ + TA_Q_BYTES;                    // [2]
+  const uint32_t sV = sK + 2 * TA_K_BYTES;                // [2]
+  const uint32_t sP = sV + 2 * TA_V_BYTES;
+  const uint32_t bars = sP + TA_P_BYTES;
+  const uint32_t q_full = bars;
+  const uint32_t kv_full = bars + 8;      // [2]
+  const uint32_t kv_empty = bars + 24;    // [2]
+  const uint32_t s_full = bars + 40;      // [2]
+  const uint32_t s_free = bars + 56;      // [2]
+  const uint32_t p_full = bars + 72;
+  const uint32_t o_done = bars + 80;
+  const uint32_t drain = bars + 88;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 128);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 132);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (Hq / Hkv);
+  const int q0 = qt * TA_BQ;
+  const int n_keys = min(S, q0 + TA_BQ);                // causal: keys < q0 + 128
+  const int n_kt = (n_keys + TA_BK - 1) / TA_BK;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(TA_BQ, TA_BK, 1, 0, 0);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, TA_HD, 1, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + 8 * i, 1);
+      mbar_init(kv_empty + 8 * i, 1);
+      mbar_init(s_full + 8 * i, 1);
+      mbar_init(s_free + 8 * i, TA_SOFTMAX);
+    }
+    mbar_init(p_full, TA_SOFTMAX);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;          // S0 at +0, S1 at +128, O at +256
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = policy_evict_last();
+      const int qrow = b * S + q0;
+      const int kvrow = (b * Hkv + kvh) * Tmax;
+      mbar_arrive_expect_tx(q_full, TA_Q_BYTES);
+      for (int a = 0; a < 2; ++a)
+        tma_load_2d(sQ + a * TA_ATOM, &tmQ, q_full, h * TA_HD + a * 64, qrow, pol);
+      for (int j = 0; j < n_kt; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(kv_empty + 8 * st, ((j >> 1) - 1) & 1, status, abort_flag)) break;
+        mbar_arrive_expect_tx(kv_full + 8 * st, TA_K_BYTES + TA_V_BYTES);
+        const int k0 = kvrow + j * TA_BK;
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(sK + st * TA_K_BYTES + a * TA_ATOM, &tmK, kv_full + 8 * st, a * 64, k0, pol);
+        for (int kb = 0; kb < 2; ++kb)
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d(sV + st * TA_V_BYTES + kb * 2 * TA_MN_BOX + c * TA_MN_BOX, &tmV,
+                        kv_full + 8 * st, c * 64, k0 + kb * 64, pol);
+      }
+      // drain (bounded): every load issued has landed before the CTA exits
+      {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+      for (int j = (n_kt > 2 ? n_kt - 2 : 0); j < n_kt; ++j) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full + 8 * (j & 1), (j >> 1) & 1))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full + 8 * st, (j >> 1) & 1, status, abort_flag)) return false;
+        if (j >= 2 && !mbar_wait(s_free + 8 * st, ((j >> 1) - 1) & 1, status, abort_flag))
+          return false;
+        tc_fence_after();
+        const uint32_t kbase = sK + st * TA_K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TA_HD / 16; ++kk) {
+          const uint64_t ad = smem_desc_k_sw128(sQ + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          const uint64_t bd = smem_desc_k_sw128(kbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + st * TA_BK, ad, bd, IDESC_S, kk > 0);
+        }
+        umma_commit(s_full + 8 * st);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, status, abort_flag);
+      if (ok && n_kt > 0) ok = issue_s(0);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 1 < n_kt && !(ok = issue_s(j + 1))) break;
+        if (!(ok = mbar_wait(p_full, j & 1, status, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t vbase = sV + (j & 1) * TA_V_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TA_BK / 16; ++kk) {
+          const uint64_t ad = smem_desc_k_sw128(sP + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          const uint64_t bd =
+              smem_desc_mn_sw128(vbase + (kk >> 2) * 2 * TA_MN_BOX, TA_MN_BOX) + 128 * (kk & 3);
+          umma_f16(tmem + 256, ad, bd, IDESC_O, (j | kk) != 0);
+        }
+        umma_commit(o_done);
+        umma_commit(kv_empty + 8 * (j & 1));
+      }
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ softmax / output (warps 2..9)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;             // which 64 columns of S / O
+    const int row = quarter * 32 + lane;          // query row within the tile = TMEM lane
+    const int qpos = q0 + row;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float* const xmax = reinterpret_cast<float*>(gbars + 256);   // [2][128] row-max halves
+    const int c_lo = half * 64;
+    float m = -1e30f, l = 0.f;
+    bool ok = true;
+    int* const xok = reinterpret_cast<int*>(gbars + 1280);         // [2][4] per-warp outcome
+    for (int j = 0; j < n_kt; ++j) {
+      const int st = j & 1;
+      // scores of tile j ready; the previous P.V product done (P is rewritten
+      // and O rescaled below).  Both warps of the pair reach the exchange
+      // barrier whatever the outcome, and leave together.
+      bool ready = true;
+      if (j > 0) ready = mbar_wait(o_done, (j - 1) & 1, status, abort_flag);
+      ready = mbar_wait(s_full + 8 * st, (j >> 1) & 1, status, abort_flag) && ready;
+      ready = __all_sync(0xffffffffu, ready);
+      tc_fence_after();
+      const uint32_t srow = tmem + lane_off + st * TA_BK;
+      const int kbase = j * TA_BK;
+      // pass 1: row max over this warp's 64 columns, then over both halves
+      float mx = m;
+      if (ready) {
+        for (int c = c_lo; c < c_lo + 64; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(srow + c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = kbase + c + i;
+            const float v = (key <= qpos && key < S) ? __uint_as_float(r[i]) * qscale_log2 : -1e30f;
+            mx = fmaxf(mx, v);
+          }
+        }
+      }
+      xmax[half * 128 + row] = mx;
+      if (lane == 0) xok[half * 4 + quarter] = ready ? 1 : 0;
+      // the two warps of this lane quarter (64 threads) exchange their halves
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      mx = fmaxf(mx, xmax[(half ^ 1) * 128 + row]);
+      const bool both = ready && xok[(half ^ 1) * 4 + quarter] != 0;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");   // xmax / xok reusable
+      if (!both) {
+        ok = false;
+        break;
+      }
+      const float corr = exp2f(m - mx);
+      m = mx;
+      // pass 2: p = exp2(s - m) -> P (bf16, swizzled K-major rows), row sum
+      float sum = 0.f;
+      for (int c = c_lo; c < c_lo + 64; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(srow + c, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int key = kbase + c + i;
+          const float p0 = (key <= qpos && key < S)
+                               ? exp2f(__uint_as_float(r[i]) * qscale_log2 - m) : 0.f;
+          const float p1 = (key + 1 <= qpos && key + 1 < S)
+                               ? exp2f(__uint_as_float(r[i + 1]) * qscale_log2 - m) : 0.f;
+          sum += p0 + p1;
+          const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
+          w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+        }
+        // 32 keys = 4 chunks of 8 (16 bytes) in atom c / 64, chunk index (c % 64) / 8 + q
+        const uint32_t atom = sP + (c >> 6) * TA_ATOM + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((c & 63) >> 3) + q;
+          st_shared_v4(atom + ((chunk ^ (row & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2],
+                       w[4 * q + 3]);
+        }
+      }
+      l = l * corr + sum;   // this half's share of the row sum
+      // running output *= corr (the accumulator holds tiles < j); this warp's 64 columns
+      if (j > 0) {
+        const uint32_t orow = tmem + lane_off + 256;
+        for (int c = c_lo; c < c_lo + 64; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(orow + c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+          tmem_st32(orow + c, r);
+        }
+      }
+      fence_async_smem();        // P visible to the tensor cores
+      tc_fence_before();
+      mbar_arrive(s_free + 8 * st);
+      mbar_arrive(p_full);
+    }
+    // ---- output: O / l (bf16) and the row LSE (log2 domain)
+    if (ok && n_kt > 0) {
+      const bool od = mbar_wait(o_done, (n_kt - 1) & 1, status, abort_flag);
+      // full row sum = both halves (same running max)
+      xmax[half * 128 + row] = l;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      const float lrow = l + xmax[(half ^ 1) * 128 + row];
+      if (__all_sync(0xffffffffu, od)) {
+        tc_fence_after();
+        pdl_wait();
+        const uint32_t orow = tmem + lane_off + 256;
+        const float inv = 1.0f / lrow;
+        __nv_bfloat16* dst = out + ((size_t)b * S + qpos) * Hq * TA_HD + (size_t)h * TA_HD;
+        for (int c = c_lo; c < c_lo + 64; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(orow + c, r);
+          if (qpos < S) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 pk;
+              __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                hv[t] = __floats2bfloat162_rn(__uint_as_float(r[i + 2 * t]) * inv,
+                                              __uint_as_float(r[i + 2 * t + 1]) * inv);
+              *reinterpret_cast<uint4*>(dst + c + i) = pk;
+            }
+          }
+        }
+        if (half == 0 && qpos < S && lse) lse[((size_t)b * Hq + h) * S + qpos] = m + log2f(lrow);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 [rows, cols] row-major, 128-byte-swizzled boxes of 64 columns x box_rows.
+bool tmap_bf16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
+                               int Tmax, __nv_bfloat16* out, float* lse, int* status,
+                               cudaStream_t st) {
+  if (hd != TA_HD || Hq % Hkv) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return cudaErrorInvalidValue;
+  CUtensorMap tq, tk, tv;
+  if (!tmap_bf16(&tq, Q, (long long)B * S, (long long)Hq * hd, TA_BQ) ||
+      !tmap_bf16(&tk, K, (long long)B * Hkv * Tmax, hd, TA_BK) ||
+      !tmap_bf16(&tv, V, (long long)B * Hkv * Tmax, hd, 64))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  return launch_k(attn_fwd_tc_kernel, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B), dim3(TA_THREADS),
+                  (size_t)TA_SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax, qscale_log2, out, lse, status);
+}
+
+}  // namespace ne

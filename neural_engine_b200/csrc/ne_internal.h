@@ -121,6 +121,13 @@ cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
                                 float inv_bc2, const float* norm_out, cudaStream_t st);
+// Causal GQA attention forward on the tcgen05 tensor cores (head_dim 128,
+// bf16): Q [B*S][Hq*hd], K / V [B][Hkv][Tmax][hd]; out [B*S][Hq*hd] bf16 and
+// the row log-sum-exp lse [B][Hq][S] (log2 domain).
+cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
+                               int Tmax, __nv_bfloat16* out, float* lse, int* status,
+                               cudaStream_t st);
 // Causal GQA attention backward; dQ and dK leave through the RoPE and QK-norm
 // backward (qn / kn may be NULL: no QK-norm; the raw projection qkv_raw gives
 // the pre-norm rows) and dQ, dK, dV are written bf16 into dqkv [B*S][qkv_dim];

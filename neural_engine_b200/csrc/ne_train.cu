@@ -503,6 +503,16 @@ static ne_status comm_embed_bwd(ne_ctx* ctx) {
   return embed_scatter(ctx, ids_all, dy_all, c->world * M);
 }
 
+// The tcgen05 attention forward serves head_dim 128; NE_ATTN_TC=0 selects the
+// mma.sync kernel instead (both are complete implementations; for comparison).
+static bool attn_tc_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_ATTN_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // ---------------------------------------------------------------------------
 // Per-layer entry points.  Each enqueues on the context stream and works on
 // the training workspace; the composition below (ne_train_fwd_bwd_device) is
@@ -568,7 +578,10 @@ NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
   NE_LAUNCH(launch_qkv_post(a.QKVR, 1, 0, M, S, nullptr, 0, Hq, Hkv, hd,
                             m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                             m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
-  NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
+  if (hd == 128 && attn_tc_enabled())
+    NE_LAUNCH(launch_attn_fwd_tc(a.Q, a.K, a.V, B, S, Hq, Hkv, hd, S, a.O, a.LSE, ctx->d_status, st));
+  else
+    NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
   // x2 (seeded with x by the preceding norm) += alpha * o.Wo^T
   if ((s = gemm(ctx, gc(a.O, qd, M, 0, w.wo, qd, D, 0, qd, EPI_RESID, a.X2, D, alpha))) != NE_OK)
     return s;
@@ -1218,5 +1231,28 @@ extern "C" NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which
         NE_CUDA(cudaMemcpy(qk[i], seg_array(t->segs[s0 + 6 + i], arr), (size_t)m.head_dim * 4,
                            cudaMemcpyDeviceToHost));
   }
+  return NE_OK;
+}
+
+// Causal GQA scaled-dot-product attention on caller-owned device buffers (the
+// reference's sdpaFwd core, mil_dynamic.h:184-198): Q [B*S][Hq*hd] bf16 (token
+// major), K / V [B][Hkv][S][hd] bf16; out [B*S][Hq*hd] bf16; lse (optional)
+// [B][Hq][S] fp32 row log-sum-exp of the scaled scores, log2 domain.
+extern "C" NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, const void* d_k,
+                                               const void* d_v, int B, int S, void* d_out,
+                                               float* d_lse) {
+  if (!ctx || !d_q || !d_k || !d_v || !d_out || B <= 0 || S <= 0) return NE_ERR_INVALID;
+  const ne_model_cfg& m = ctx->cfg;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  const auto* q = static_cast<const __nv_bfloat16*>(d_q);
+  const auto* k = static_cast<const __nv_bfloat16*>(d_k);
+  const auto* v = static_cast<const __nv_bfloat16*>(d_v);
+  auto* o = static_cast<__nv_bfloat16*>(d_out);
+  if (m.head_dim == 128 && attn_tc_enabled())
+    NE_LAUNCH(launch_attn_fwd_tc(q, k, v, B, S, m.n_heads, m.kv_heads, m.head_dim, S, o, d_lse,
+                                 ctx->d_status, ctx->st));
+  else
+    NE_LAUNCH(launch_prefill_attn_bf16(q, k, v, B, S, 0, m.n_heads, m.kv_heads, m.head_dim, S, o,
+                                       ctx->st, d_lse));
   return NE_OK;
 }

@@ -33,7 +33,8 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_train_get_layer", "ne_gemm", "ne_train_grad_pool", "ne_save_ckpt_v4",
             "ne_embed_fwd", "ne_attn_fwd", "ne_ffn_fwd", "ne_lmhead_ce_fwd_bwd", "ne_ffn_bwd",
             "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
-            "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async")
+            "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
+            "ne_sdpa_fwd_device")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -151,6 +152,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_comm_init.argtypes = [P, P, I, I]
     lib.ne_comm_set_reduce.argtypes = [P, I]
     lib.ne_grad_allreduce_async.argtypes = [P]
+    lib.ne_sdpa_fwd_device.argtypes = [P, P, P, P, I, I, P, P]
     lib.ne_kv_alloc.argtypes = [P, I, I]
     lib.ne_prefill.argtypes = [P, P, I, I, I, P, P]
     lib.ne_decode_step.argtypes = [P, P, I, I, P, P]
@@ -272,6 +274,12 @@ class Engine:
 
     def embed_bwd(self):
         self._check(self.lib.ne_embed_bwd(self._ctx))
+
+    def sdpa_fwd_device(self, d_q: int, d_k: int, d_v: int, B: int, S: int, d_out: int,
+                        d_lse: int | None = None):
+        self._check(self.lib.ne_sdpa_fwd_device(self._ctx, C.c_void_p(d_q), C.c_void_p(d_k),
+                                                C.c_void_p(d_v), int(B), int(S), C.c_void_p(d_out),
+                                                C.c_void_p(d_lse) if d_lse else None))
 
     # -- data-parallel gradient exchange (NCCL)
     @staticmethod

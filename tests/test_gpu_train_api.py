@@ -201,3 +201,36 @@ def test_rmsnorm_entry_points_match_float64():
     assert _rel(dx_.cpu(), xd.grad + res.double()) <= 1e-5
     assert _rel(dw.cpu(), wd.grad) <= 1e-5
     e.close()
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv,B,S", [(128, 4, 2, 2, 256), (128, 2, 2, 1, 200),
+                                           (128, 4, 2, 1, 384), (128, 2, 1, 3, 64),
+                                           (64, 4, 2, 2, 160)])
+def test_sdpa_forward_matches_float64(hd, Hq, Hkv, B, S):
+    """Causal GQA attention (tcgen05 kernel at head_dim 128) vs float64 softmax;
+    ragged and multi-tile sequence lengths; the row LSE (log2 domain) too.
+    Tolerance: bf16 output, max-abs <= 2^-7 * max|O| + 1e-3; LSE <= 1e-3."""
+    import neural_engine_b200 as ne
+    cfg = ne.ModelConfig(1, 256, 256, Hq, Hkv, hd, 512)
+    e = ne.Engine(cfg)
+    g = torch.Generator().manual_seed(S + hd)
+    q = torch.randn(B * S, Hq * hd, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, S, hd, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, hd, generator=g).to(torch.bfloat16)
+    dq, dk, dv = q.cuda(), k.cuda(), v.cuda()
+    out = torch.zeros(B * S, Hq * hd, dtype=torch.bfloat16, device="cuda")
+    lse = torch.zeros(B, Hq, S, device="cuda")
+    e.sdpa_fwd_device(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S, out.data_ptr(),
+                      lse.data_ptr())
+    e.sync()
+    qd = q.double().reshape(B, S, Hq, hd).permute(0, 2, 1, 3)
+    kd = k.double().repeat_interleave(Hq // Hkv, 1)
+    vd = v.double().repeat_interleave(Hq // Hkv, 1)
+    sc = qd @ kd.transpose(-1, -2) / hd ** 0.5
+    sc = sc.masked_fill(~torch.ones(S, S, dtype=torch.bool).tril(), float("-inf"))
+    ref = (torch.softmax(sc, -1) @ vd).permute(0, 2, 1, 3).reshape(B * S, Hq * hd)
+    got = out.cpu().double()
+    assert (got - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item() + 1e-3
+    ref_lse = torch.logsumexp(sc, -1) / np.log(2.0)
+    assert (lse.cpu().double() - ref_lse).abs().max().item() <= 1e-3
+    e.close()
