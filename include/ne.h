@@ -246,6 +246,12 @@ NE_API ne_status ne_train_zero_grads(ne_ctx* ctx);
  * (optional) receive the batch's mean loss. */
 NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss);
 NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss);
+/* Vocabulary compaction (cpu_ops.h:385-431, applied by train.m to every run):
+ * the classifier and its softmax use only the CV embedding rows h_c2f[0..CV)
+ * (distinct ids; the reference takes the tokens present in the data, in
+ * increasing order); every target must be one of them.  Their gradient is
+ * added back into the tied embedding's.  CV = 0 / NULL: full vocabulary. */
+NE_API ne_status ne_train_set_vocab_map(ne_ctx* ctx, const int32_t* h_c2f, int CV);
 /* Global L2 norm of the accumulated gradients times grad_scale. */
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm);
 /* Unscale, clip, AdamW (bias correction at step t >= 1), refresh bf16 copies,

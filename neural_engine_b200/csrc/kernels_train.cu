@@ -142,14 +142,15 @@ __device__ __forceinline__ void ms_combine(float& m, float& s, float om, float o
 
 constexpr int CE_THREADS = 512;
 __global__ void __launch_bounds__(CE_THREADS)
-ce_rows_kernel(const float* __restrict__ logits, const float2* __restrict__ stats, int stats_ld,
-               const int32_t* __restrict__ tgt, int V, float scale, float* __restrict__ loss,
-               bf16* __restrict__ dlogits, int* status) {
+ce_rows_kernel(const float* __restrict__ logits, int ld, const float2* __restrict__ stats,
+               int stats_ld, const int32_t* __restrict__ tgt, const int32_t* __restrict__ remap,
+               int V, float scale, float* __restrict__ loss, bf16* __restrict__ dlogits,
+               int* status) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red_m[32], red_s[32];
   const int r = blockIdx.x;
-  const float* row = logits + (size_t)r * V;
+  const float* row = logits + (size_t)r * ld;
   const float2* st = stats + (size_t)r * stats_ld;
   const int nck = (V + 31) / 32;
   float m = -FLT_MAX, s = 0.f;
@@ -175,6 +176,7 @@ ce_rows_kernel(const float* __restrict__ logits, const float2* __restrict__ stat
   m = red_m[0];
   s = red_s[0];
   int t = tgt[r];
+  if (remap) t = (t >= 0) ? remap[t] : -1;   // full vocabulary id -> classifier column
   if (t < 0 || t >= V) {
     if (threadIdx.x == 0) atomicExch(status, DEV_ERR_BOUNDS);
     t = 0;
@@ -184,8 +186,8 @@ ce_rows_kernel(const float* __restrict__ logits, const float2* __restrict__ stat
     const float pt = expf(row[t] - m) * inv;
     loss[r] = -logf(pt + 1e-10f);
   }
-  bf16* drow = dlogits + (size_t)r * V;
-  if ((V & 3) == 0) {
+  bf16* drow = dlogits + (size_t)r * ld;
+  if ((V & 3) == 0 && (ld & 3) == 0) {
     const float4* row4 = reinterpret_cast<const float4*>(row);
 #pragma unroll 4
     for (int i = threadIdx.x; i < (V >> 2); i += CE_THREADS) {
@@ -391,11 +393,51 @@ cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, 
                   dx, dx16, dw);
 }
 
-cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_ld,
-                           const int32_t* tgt, int rows, int V, float scale, float* loss,
-                           __nv_bfloat16* dlogits, int* status, cudaStream_t st) {
-  return launch_k(ce_rows_kernel, dim3(rows), dim3(CE_THREADS), 0, st, logits, stats, stats_ld,
-                  tgt, V, scale, loss, dlogits, status);
+cudaError_t launch_ce_rows(const float* logits, int ld, const float2* stats, int stats_ld,
+                           const int32_t* tgt, const int32_t* remap, int rows, int V, float scale,
+                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st) {
+  return launch_k(ce_rows_kernel, dim3(rows), dim3(CE_THREADS), 0, st, logits, ld, stats,
+                  stats_ld, tgt, remap, V, scale, loss, dlogits, status);
+}
+
+// ------------------------------------------------------------ vocabulary compaction
+// (vocab_compact_embed / vocab_scatter_grads, cpu_ops.h:416-431)
+namespace {
+__global__ void gather_rows_kernel(const bf16* __restrict__ src, const int32_t* __restrict__ idx,
+                                   int n, int D, bf16* __restrict__ dst) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + (size_t)idx[r] * D);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)r * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) d4[i] = s4[i];
+}
+// dst[idx[r]] += src[r]; src[r] = 0 (each destination row appears once)
+__global__ void scatter_add_rows_kernel(float* __restrict__ src, const int32_t* __restrict__ idx,
+                                        int n, int D, float* __restrict__ dst) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  float* s = src + (size_t)r * D;
+  float* d = dst + (size_t)idx[r] * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    d[i] += s[i];
+    s[i] = 0.f;
+  }
+}
+}  // namespace
+
+cudaError_t launch_gather_rows(const __nv_bfloat16* src, const int32_t* idx, int n, int D,
+                               __nv_bfloat16* dst, cudaStream_t st) {
+  if (D % 8) return cudaErrorInvalidValue;
+  return launch_k(gather_rows_kernel, dim3(n), dim3(128), 0, st, src, idx, n, D, dst);
+}
+
+cudaError_t launch_scatter_add_rows(float* src, const int32_t* idx, int n, int D, float* dst,
+                                    cudaStream_t st) {
+  return launch_k(scatter_add_rows_kernel, dim3(n), dim3(256), 0, st, src, idx, n, D, dst);
 }
 
 

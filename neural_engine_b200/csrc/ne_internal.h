@@ -141,9 +141,16 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
                                int D, const float* residual, float* dx, __nv_bfloat16* dx16,
                                float* dw, cudaStream_t st);
-cudaError_t launch_ce_rows(const float* logits, const float2* stats, int stats_ld,
-                           const int32_t* tgt, int rows, int V, float scale, float* loss,
-                           __nv_bfloat16* dlogits, int* status, cudaStream_t st);
+// Cross-entropy rows: logits [rows][ld] (V valid columns) with the GEMM's
+// softmax chunk statistics; remap (optional) maps target ids to columns.
+cudaError_t launch_ce_rows(const float* logits, int ld, const float2* stats, int stats_ld,
+                           const int32_t* tgt, const int32_t* remap, int rows, int V, float scale,
+                           float* loss, __nv_bfloat16* dlogits, int* status, cudaStream_t st);
+// dst[r] = src[idx[r]] (bf16 rows of D) / dst[idx[r]] += src[r], src[r] = 0 (fp32)
+cudaError_t launch_gather_rows(const __nv_bfloat16* src, const int32_t* idx, int n, int D,
+                               __nv_bfloat16* dst, cudaStream_t st);
+cudaError_t launch_scatter_add_rows(float* src, const int32_t* idx, int n, int D, float* dst,
+                                    cudaStream_t st);
 
 // Deterministic dE[tok[r]] += dy[r] over n rows (embed_bwd.cu); scratch of at
 // least embed_bwd_scratch_bytes(n) bytes.

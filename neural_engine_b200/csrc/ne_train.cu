@@ -86,6 +86,13 @@ struct TrainState {
   __nv_bfloat16 *dY16 = nullptr, *dX216 = nullptr, *DH13 = nullptr, *dO = nullptr,
                 *DQKV = nullptr, *dlogits = nullptr;
   float2* ce_stats = nullptr;            // [Mc, ceil(V/32)] classifier softmax statistics
+  // vocabulary compaction (the reference's classifier over the tokens present
+  // in the data): CV classifier rows, padded to CVp (a multiple of 64)
+  int CV = 0, CVp = 0;
+  int32_t* d_c2f = nullptr;              // [CV] compact -> full id
+  int32_t* d_f2c = nullptr;              // [V] full -> compact id (-1: absent)
+  __nv_bfloat16* Ec = nullptr;           // [CVp, D] gathered classifier rows (bf16)
+  float* dEc = nullptr;                  // [CVp, D] their gradient (scattered into embed_g)
   void* embed_scratch = nullptr;         // sort buffers of the embedding backward
   size_t embed_scratch_bytes = 0;
   // the micro-step after the token split, captured once as a CUDA graph
@@ -104,6 +111,8 @@ void free_train(ne_ctx* ctx) {
   if (t->d_chunks) cudaFree(t->d_chunks);
   if (t->embed_scratch) cudaFree(t->embed_scratch);
   if (t->step_graph) cudaGraphExecDestroy(t->step_graph);
+  for (void* p : {(void*)t->d_c2f, (void*)t->d_f2c, (void*)t->Ec, (void*)t->dEc})
+    if (p) cudaFree(p);
   if (t->opt_partial) cudaFree(t->opt_partial);
   if (t->opt_ticket) cudaFree(t->opt_ticket);
   if (t->norm_out) cudaFree(t->norm_out);
@@ -623,25 +632,34 @@ NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int l) {
 NE_API ne_status ne_lmhead_ce_fwd_bwd(ne_ctx* ctx, float* d_loss) {
   NE_TRAIN_PRELUDE();
   const float ce_scale = 1.0f / (float)M;
-  const int nck = (V + 31) / 32;
+  // classifier rows: the whole tied embedding, or its compacted rows
+  const bool cmp = t->CV > 0;
+  const int Vc = cmp ? t->CV : V;           // classes of the softmax
+  const int ldl = cmp ? t->CVp : V;         // logits row stride = classifier rows
+  const __nv_bfloat16* Wcls = cmp ? t->Ec : ctx->embed;
+  float* dWcls = cmp ? t->dEc : t->embed_g;
+  if (cmp) NE_LAUNCH(launch_gather_rows(ctx->embed, t->d_c2f, t->CV, D, t->Ec, st));
+  const int nck = (Vc + 31) / 32;
   for (int r0 = 0; r0 < M; r0 += t->Mc) {
     const int rows = std::min(t->Mc, M - r0);
     const __nv_bfloat16* xnf = t->XNF + (size_t)r0 * D;
-    GemmCall cl = gc(xnf, D, rows, 0, ctx->embed, D, V, 0, D, EPI_F32_STATS, t->logits, V);
+    GemmCall cl = gc(xnf, D, rows, 0, Wcls, D, Vc, 0, D, EPI_F32_STATS, t->logits, ldl);
     cl.aux1 = t->ce_stats;
     cl.aux_ld = nck;
     if ((s = gemm(ctx, cl)) != NE_OK) return s;
-    NE_LAUNCH(launch_ce_rows(t->logits, t->ce_stats, nck, t->tgt + r0, rows, V, ce_scale,
-                             t->loss_rows + r0, t->dlogits, ctx->d_status, st));
-    // dXNF = dlogits . E   (E read MN-major as [V (K), D (N)])
-    if ((s = gemm(ctx, gc(t->dlogits, V, rows, 0, ctx->embed, D, D, 1, V, EPI_F32,
+    NE_LAUNCH(launch_ce_rows(t->logits, ldl, t->ce_stats, nck, t->tgt + r0,
+                             cmp ? t->d_f2c : nullptr, rows, Vc, ce_scale, t->loss_rows + r0,
+                             t->dlogits, ctx->d_status, st));
+    // dXNF = dlogits . Wcls   (Wcls read MN-major as [classes (K), D (N)])
+    if ((s = gemm(ctx, gc(t->dlogits, ldl, rows, 0, Wcls, D, D, 1, ldl, EPI_F32,
                           t->dXF + (size_t)r0 * D, D))) != NE_OK)
       return s;
-    // dE += dlogits^T . XNF   (both MN-major)
-    if ((s = gemm(ctx, gc(t->dlogits, V, V, 1, xnf, D, D, 1, rows, EPI_RESID, t->embed_g, D))) !=
+    // dWcls += dlogits^T . XNF   (both MN-major)
+    if ((s = gemm(ctx, gc(t->dlogits, ldl, ldl, 1, xnf, D, D, 1, rows, EPI_RESID, dWcls, D))) !=
         NE_OK)
       return s;
   }
+  if (cmp) NE_LAUNCH(launch_scatter_add_rows(t->dEc, t->d_c2f, t->CV, D, t->embed_g, st));
   NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, t->XL, ctx->rms_final, m.rms_eps, M, D, nullptr, t->dY,
                                t->dY16, t->rmsf_g, st));
   if (d_loss) {
@@ -1254,5 +1272,53 @@ extern "C" NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, con
   else
     NE_LAUNCH(launch_prefill_attn_bf16(q, k, v, B, S, 0, m.n_heads, m.kv_heads, m.head_dim, S, o,
                                        ctx->st, d_lse));
+  return NE_OK;
+}
+
+// Vocabulary compaction (vocab_map_build / vocab_compact_embed /
+// vocab_scatter_grads, cpu_ops.h:385-431): the classifier and its softmax run
+// over the CV rows h_c2f[0..CV) of the tied embedding (the tokens present in
+// the training data, in increasing id order when built as the reference does);
+// targets must be among them.  Their gradient is added back into the full
+// embedding gradient.  CV = 0 (or NULL) restores the full vocabulary.
+extern "C" NE_API ne_status ne_train_set_vocab_map(ne_ctx* ctx, const int32_t* h_c2f, int CV) {
+  if (!ctx || !ctx->train) return NE_ERR_STATE;
+  TrainState* t = ctx->train;
+  const ne_model_cfg& m = ctx->cfg;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  for (void* p : {(void*)t->d_c2f, (void*)t->d_f2c, (void*)t->Ec, (void*)t->dEc})
+    if (p) NE_CUDA(cudaFree(p));
+  t->d_c2f = t->d_f2c = nullptr;
+  t->Ec = nullptr;
+  t->dEc = nullptr;
+  t->CV = t->CVp = 0;
+  if (t->step_graph) {   // the captured step used the previous classifier
+    NE_CUDA(cudaGraphExecDestroy(t->step_graph));
+    t->step_graph = nullptr;
+  }
+  if (!h_c2f || CV <= 0) return NE_OK;
+  if (CV > m.vocab) return fail(ctx, NE_ERR_INVALID, "vocab map larger than the vocabulary");
+  std::vector<int32_t> f2c(m.vocab, -1);
+  for (int c = 0; c < CV; ++c) {
+    const int32_t v = h_c2f[c];
+    if (v < 0 || v >= m.vocab || f2c[v] >= 0)
+      return fail(ctx, NE_ERR_INVALID, "vocab map entries must be distinct ids < vocab");
+    f2c[v] = c;
+  }
+  const int CVp = (CV + 63) / 64 * 64;
+  const size_t D = m.dim;
+  ne_status s;
+  if ((s = dalloc(ctx, &t->d_c2f, (size_t)CV)) != NE_OK || (s = dalloc(ctx, &t->d_f2c, (size_t)m.vocab)) ||
+      (s = dalloc(ctx, &t->Ec, (size_t)CVp * D)) || (s = dalloc(ctx, &t->dEc, (size_t)CVp * D)))
+    return s;
+  NE_CUDA(cudaMemcpy(t->d_c2f, h_c2f, (size_t)CV * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(t->d_f2c, f2c.data(), (size_t)m.vocab * 4, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemset(t->Ec, 0, (size_t)CVp * D * 2));     // padding rows stay zero
+  NE_CUDA(cudaMemset(t->dEc, 0, (size_t)CVp * D * 4));
+  // padding columns of dlogits are never written by the cross-entropy kernel
+  NE_CUDA(cudaMemset(t->dlogits, 0, (size_t)t->Mc * m.vocab * 2));
+  t->CV = CV;
+  t->CVp = CVp;
   return NE_OK;
 }

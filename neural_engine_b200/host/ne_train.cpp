@@ -12,10 +12,10 @@
 // ("step N loss=...", "[ckpt saved, best_loss=...]").
 //
 // A "step" is one micro-step as in the reference: --batch sequences (1 in the
-// reference) through forward + backward.  Differences from the reference that
-// a user may want: the classifier runs over the full vocabulary (the
-// reference's vocabulary compaction is not applied), and gradients need no
-// loss scaling (fp32 accumulation), so the update scales by 1/accum only.
+// reference) through forward + backward.  As in the reference the classifier
+// runs over the token ids present in the data file (vocabulary compaction,
+// cpu_ops.h:385-431; --no-compact-vocab uses the full vocabulary).  Gradients
+// need no loss scaling (fp32 accumulation), so the update scales by 1/accum.
 //
 // Extensions: --model (qwen3_06b | stories110m | custom shape flags), --seq,
 // --batch, --ckpt, --device, --synthetic (uniform random tokens, no data
@@ -44,7 +44,7 @@
 namespace {
 
 struct Args {
-  bool scratch = false, resume = false, synthetic = false;
+  bool scratch = false, resume = false, synthetic = false, compact_vocab = true, print_vocab = false;
   int steps = 10000, accum = 10, warmup = 100;
   float lr = 3e-4f, clip = 1.0f;
   std::string data = "../tinystories_data00.bin";
@@ -63,9 +63,9 @@ void usage() {
       "usage: ne_train [--scratch | --resume] [--steps N] [--lr X] [--accum N] [--warmup N]\n"
       "                [--clip X] [--data FILE] [--model qwen3_06b|stories110m] [--seq S]\n"
       "                [--batch B] [--ckpt FILE] [--device D] [--synthetic] [--save-every N]\n"
-      "                [--qk-norm 0|1] [--theta X] [--eps X] [--alpha X]\n"
+      "                [--qk-norm 0|1] [--theta X] [--eps X] [--alpha X] [--no-compact-vocab]\n"
       "                [--layers N --dim N --hidden N --heads N --kv-heads N --head-dim N\n"
-      "                 --vocab N] [--dump-init FILE] [--print-windows N]\n");
+      "                 --vocab N] [--dump-init FILE] [--print-windows N] [--print-vocab]\n");
 }
 
 bool parse(int argc, char** argv, Args& a) {
@@ -81,6 +81,8 @@ bool parse(int argc, char** argv, Args& a) {
     if (s == "--resume") a.resume = true;
     else if (s == "--scratch") a.scratch = true;
     else if (s == "--synthetic") a.synthetic = true;
+    else if (s == "--no-compact-vocab") a.compact_vocab = false;
+    else if (s == "--print-vocab") a.print_vocab = true;
     else if (s == "--steps") a.steps = std::atoi(next("--steps"));
     else if (s == "--lr") a.lr = (float)std::atof(next("--lr"));
     else if (s == "--accum") a.accum = std::atoi(next("--accum"));
@@ -283,6 +285,18 @@ void sample(const TokenFile& tf, bool synthetic, int V, int B, int S, std::vecto
   }
 }
 
+// Vocabulary compaction map (vocab_map_build, cpu_ops.h:391-414): the token
+// ids present in the data, in increasing order.
+std::vector<int32_t> vocab_map(const TokenFile& tf, int V) {
+  std::vector<char> used(V, 0);
+  for (size_t i = 0; i < tf.n; ++i)
+    if (tf.tok[i] < V) used[tf.tok[i]] = 1;
+  std::vector<int32_t> c2f;
+  for (int v = 0; v < V; ++v)
+    if (used[v]) c2f.push_back(v);
+  return c2f;
+}
+
 double now_ms() {
   using namespace std::chrono;
   return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
@@ -340,6 +354,13 @@ int main(int argc, char** argv) {
       std::printf("Token file too short\n");
       return 1;
     }
+  }
+  std::vector<int32_t> c2f;
+  if (!a.synthetic && a.compact_vocab) c2f = vocab_map(tf, c.vocab);
+  if (a.print_vocab) {
+    std::printf("%zu\n", c2f.size());
+    for (int32_t v : c2f) std::printf("%d\n", v);
+    return 0;
   }
   if (a.print_windows > 0) {
     srand48(42 + 0 + 1000L * rank);
@@ -416,6 +437,12 @@ int main(int argc, char** argv) {
   }
   if (!a.synthetic && rank == 0)
     std::printf("Token data: %zu tokens (%.1f MB)\n", tf.n, tf.bytes / 1e6);
+  if (!c2f.empty()) {
+    CHECK(ne_train_set_vocab_map(ctx, c2f.data(), (int)c2f.size()));
+    if (rank == 0)
+      std::printf("Vocab compaction: %d \xe2\x86\x92 %zu active tokens (%.1fx reduction)\n", c.vocab,
+                  c2f.size(), (float)c.vocab / (float)c2f.size());
+  }
 
   // ---- data-parallel ranks
   if (world > 1) {

@@ -34,7 +34,7 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_embed_fwd", "ne_attn_fwd", "ne_ffn_fwd", "ne_lmhead_ce_fwd_bwd", "ne_ffn_bwd",
             "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
-            "ne_sdpa_fwd_device")
+            "ne_sdpa_fwd_device", "ne_train_set_vocab_map")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -153,6 +153,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_comm_set_reduce.argtypes = [P, I]
     lib.ne_grad_allreduce_async.argtypes = [P]
     lib.ne_sdpa_fwd_device.argtypes = [P, P, P, P, I, I, P, P]
+    lib.ne_train_set_vocab_map.argtypes = [P, P, I]
     lib.ne_kv_alloc.argtypes = [P, I, I]
     lib.ne_prefill.argtypes = [P, P, I, I, I, P, P]
     lib.ne_decode_step.argtypes = [P, P, I, I, P, P]
@@ -378,6 +379,14 @@ class Engine:
     def train_fwd_bwd_device(self, d_tokens: int, d_loss: int | None = None):
         self._check(self.lib.ne_train_fwd_bwd_device(self._ctx, C.c_void_p(d_tokens),
                                                      C.c_void_p(d_loss) if d_loss else None))
+
+    def train_set_vocab_map(self, compact_to_full=None):
+        """Classifier over the given vocabulary rows only (None: all rows)."""
+        if compact_to_full is None:
+            self._check(self.lib.ne_train_set_vocab_map(self._ctx, None, 0))
+            return
+        a = np.ascontiguousarray(compact_to_full, dtype=np.int32)
+        self._check(self.lib.ne_train_set_vocab_map(self._ctx, _ptr(a), int(a.size)))
 
     def zero_grads(self):
         self._check(self.lib.ne_train_zero_grads(self._ctx))

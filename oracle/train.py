@@ -29,8 +29,11 @@ def _torch():
     return torch
 
 
-def forward_loss(cfg: ModelCfg, params: dict, tokens: np.ndarray):
-    """params: torch float64 tensors {layers: [dict], rms_final, embed, qk: [(qn, kn)] or None}."""
+def forward_loss(cfg: ModelCfg, params: dict, tokens: np.ndarray, compact=None):
+    """params: torch float64 tensors {layers: [dict], rms_final, embed, qk: [(qn, kn)] or None}.
+    compact: optional compact -> full vocabulary ids; the classifier then uses
+    those embedding rows only and targets map to their compact index
+    (vocab_map_build / vocab_compact_embed, cpu_ops.h:385-422)."""
     torch = _torch()
     tok = torch.as_tensor(np.asarray(tokens, np.int64))
     B, S1 = tok.shape
@@ -81,13 +84,22 @@ def forward_loss(cfg: ModelCfg, params: dict, tokens: np.ndarray):
         g = h1 * torch.sigmoid(h1) * h3
         x = x + alpha * (g @ lw["W2"].T)
     x = rms(x, params["rms_final"], cfg.eps)
-    logits = x @ params["embed"].T
+    if compact is not None:
+        c2f = torch.as_tensor(np.asarray(compact, np.int64))
+        f2c = torch.full((params["embed"].shape[0],), -1, dtype=torch.int64)
+        f2c[c2f] = torch.arange(len(c2f))
+        logits = x @ params["embed"][c2f].T
+        tgt = f2c[tgt]
+        assert bool((tgt >= 0).all()), "target outside the compact vocabulary"
+    else:
+        logits = x @ params["embed"].T
     logp = torch.log_softmax(logits, -1)
     nll = -logp.gather(-1, tgt[..., None])[..., 0]
     return nll.mean()
 
 
-def loss_and_grads(cfg: ModelCfg, layers, rms_final, embed, qk, tokens, dtype="float64"):
+def loss_and_grads(cfg: ModelCfg, layers, rms_final, embed, qk, tokens, dtype="float64",
+                   compact=None):
     """Returns (loss, grads) with grads shaped like the inputs (numpy, `dtype`)."""
     torch = _torch()
     tdt = getattr(torch, dtype)
@@ -95,7 +107,7 @@ def loss_and_grads(cfg: ModelCfg, layers, rms_final, embed, qk, tokens, dtype="f
     P = {"layers": [{k: t(v) for k, v in lw.items()} for lw in layers],
          "rms_final": t(rms_final), "embed": t(embed),
          "qk": [(t(a), t(b)) for a, b in qk] if qk is not None else None}
-    loss = forward_loss(cfg, P, tokens)
+    loss = forward_loss(cfg, P, tokens, compact)
     loss.backward()
     g = {"layers": [{k: v.grad.numpy() for k, v in lw.items()} for lw in P["layers"]],
          "rms_final": P["rms_final"].grad.numpy(), "embed": P["embed"].grad.numpy(),

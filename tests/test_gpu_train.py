@@ -165,3 +165,29 @@ def test_full_width_two_layers(name):
     worst = _compare_grads(cfg, e.get_grads(), g_ref)
     print(f"{name}: loss {loss:.6f} ref {ref_loss:.6f}; worst grad rel-L2 {worst[1]:.3e} ({worst[0]})")
     e.close()
+
+
+@pytest.mark.parametrize("CV", [97, 128])
+def test_compact_vocabulary_classifier(CV):
+    """The reference's vocabulary compaction: softmax over the embedding rows of
+    the tokens in use only; gradients (including the tied embedding's, added
+    back into the used rows) vs float64 autograd of the compacted forward."""
+    cfg = _cfg(qk_norm=True, theta=1e6, eps=1e-6)
+    layers, rf, emb, qk = om.init_weights(cfg, seed=101, std=0.08, bf16=True)
+    rng = np.random.default_rng(CV)
+    c2f = np.sort(rng.choice(cfg.vocab, CV, replace=False)).astype(np.int32)
+    B, S = 2, 32
+    tok = c2f[rng.integers(0, CV, (B, S + 1))]
+    e = _engine(cfg, layers, rf, emb, qk, B, S)
+    e.train_set_vocab_map(c2f)
+    loss = e.train_fwd_bwd(tok)
+    ref_loss, g_ref = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok, compact=c2f)
+    assert abs(loss - ref_loss) <= LOSS_REL * ref_loss, (loss, ref_loss)
+    _compare_grads(cfg, e.get_grads(), g_ref)
+    # back to the full vocabulary: the same batch gives the uncompacted loss
+    e.zero_grads()
+    e.train_set_vocab_map(None)
+    full = e.train_fwd_bwd(tok)
+    ref_full, _ = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok)
+    assert abs(full - ref_full) <= LOSS_REL * ref_full
+    e.close()

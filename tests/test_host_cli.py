@@ -69,3 +69,18 @@ def test_cli_rejects_unknown_flags():
     assert r.returncode == 2
     r = subprocess.run([_bin(), "--help"], capture_output=True, text=True, timeout=30)
     assert r.returncode == 0 and "--scratch" in r.stdout
+
+
+def test_vocab_compaction_map_is_the_reference_map(tmp_path):
+    """vocab_map_build (cpu_ops.h:391-414): ids present in the data, ascending."""
+    rs = np.random.default_rng(3)
+    data = rs.choice([5, 17, 3, 90, 41, 95], size=5000).astype(np.uint16)
+    path = tmp_path / "tok.bin"
+    data.tofile(path)
+    out = subprocess.run([_bin(), *SHAPE, "--data", str(path), "--print-vocab"], check=True,
+                         capture_output=True, text=True, timeout=60).stdout.split()
+    assert int(out[0]) == 6 and [int(x) for x in out[1:]] == sorted(set(data.tolist()))
+    out = subprocess.run([_bin(), *SHAPE, "--data", str(path), "--print-vocab",
+                          "--no-compact-vocab"], check=True, capture_output=True, text=True,
+                         timeout=60).stdout.split()
+    assert out == ["0"]
