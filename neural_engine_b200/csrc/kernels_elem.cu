@@ -172,6 +172,23 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// PER consecutive values -> one vector store (PER * sizeof(T) bytes, aligned
+// because rows and heads are multiples of PER elements).
+template <typename T, int PER>
+__device__ __forceinline__ void store_vec(T* dst, const float (&v)[PER]) {
+  if constexpr (PER == 4 && sizeof(T) == 2) {
+    T t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t[i] = from_f32<T>(v[i]);
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(t);
+  } else if constexpr (PER == 4 && sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) dst[i] = from_f32<T>(v[i]);
+  }
+}
+
 template <int HD, typename QT, typename KT>
 __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long long split_stride,
                                 int rows, int S_rows, const int* __restrict__ d_pos, int pos0,
@@ -201,14 +218,23 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
 #pragma unroll
   for (int i = 0; i < PER; ++i) v[i] = 0.f;
   for (int s = 0; s < (nsplit > 0 ? nsplit : 1); ++s) {
+    if constexpr (PER == 4) {   // 16-byte aligned: rows and heads are multiples of 4 floats
+      const float4 t = *reinterpret_cast<const float4*>(src + (size_t)s * split_stride);
+      v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < PER; ++i) v[i] += src[(size_t)s * split_stride + i];
+      for (int i = 0; i < PER; ++i) v[i] += src[(size_t)s * split_stride + i];
+    }
   }
   if (zero_src) {
     // the source is an accumulator the next projection adds into: leave it zeroed
     float* z = const_cast<float*>(src);
+    if constexpr (PER == 4) {
+      *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
 #pragma unroll
-    for (int i = 0; i < PER; ++i) z[i] = 0.f;
+      for (int i = 0; i < PER; ++i) z[i] = 0.f;
+    }
   }
   const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
   if ((is_q || is_k) && qn != nullptr) {
@@ -234,14 +260,12 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
   }
   if (is_q) {
     QT* dst = q_out + ((size_t)r * Hq + h) * HD + lane * PER;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) dst[i] = from_f32<QT>(v[i]);
+    store_vec<QT, PER>(dst, v);
   } else {
     const int kvh = is_k ? (h - Hq) : (h - Hq - Hkv);
     KT* cache = is_k ? kc : vc;
     KT* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) dst[i] = from_f32<KT>(v[i]);
+    store_vec<KT, PER>(dst, v);
   }
 }
 
