@@ -1,6 +1,7 @@
 // gemm.cu -- host side of the tcgen05 GEMM: TMA descriptors, tiling, dispatch.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -248,11 +249,16 @@ int gemm_pick_splits(const GemmCall& c, int num_sms) {
   if (c.epi == EPI_F32T_ADD) {
     // partial sums meet in L2 through the TMA add: split until the work
     // units fill the SMs, keeping at least two 64-deep k-blocks per unit
+    static const int min_kb = [] {
+      const char* e = getenv("NE_SPLITK_MIN_KB");   // tuning: k-blocks per split, at least
+      const int v = e ? atoi(e) : 2;
+      return v < 1 ? 1 : v;
+    }();
     const int bn = pick_bn(c);
     const int tiles = ((c.M + GEMM_BM - 1) / GEMM_BM) * ((c.N + bn - 1) / bn);
     const int kb = c.K / GEMM_BK;
     int best = 1;
-    for (int d = 1; d <= kb / 2; ++d) {
+    for (int d = 1; d <= kb / min_kb; ++d) {
       if (kb % d) continue;
       if (tiles * d > num_sms) break;
       best = d;

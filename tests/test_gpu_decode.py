@@ -90,6 +90,32 @@ def test_prefill_and_decode_teacher_forced(kw, B, S):
     e.close()
 
 
+@pytest.mark.parametrize("B,S", [(3, 130), (160, 5)])
+def test_head_dim_128_group_2(B, S):
+    """head_dim 128 with GQA groups of 2 (the Qwen3 attention shape) takes the
+    tensor-core decode attention.  (3, 130): few long sequences, every one
+    split over many warps and merged; (160, 5): many short ones, most finished
+    inside one warp and written directly."""
+    cfg = _tiny_cfg(head_dim=128, qk_norm=True, theta=1e6, eps=1e-6)
+    layers, rf, emb, qk = om.init_weights(cfg, seed=41, std=0.08, bf16=True)
+    layers, rf, qk = om.random_gains(cfg, layers, rf, qk)
+    prompt = om.prompt_tokens(cfg.vocab, S, 42, batch=B)
+    steps = 8
+    e = _engine(cfg, layers, rf, emb, qk, B, S + steps + 1)
+    dec = od.Decoder(cfg, layers, rf, emb, qk, batch=B, max_seq=S + steps + 1)
+    ref = dec.forward(prompt.astype(np.int64), 0, last_only=True)
+    _, lg = e.prefill(prompt, 0, return_logits=True)
+    _check_logits(lg, ref, "prefill")
+    tok = np.argmax(ref, -1).astype(np.int32)
+    for i in range(steps):
+        ref = dec.forward(tok[:, None].astype(np.int64), S + i, last_only=True)
+        _, lg = e.decode_step(tok, S + i, return_logits=True)
+        err = _check_logits(lg, ref, f"step {i}")
+        _check_argmax(lg, ref, err, f"step {i}")
+        tok = np.argmax(ref, -1).astype(np.int32)
+    e.close()
+
+
 def test_decode_only_matches_prefill_path():
     """Feeding the prompt token by token through decode steps (generate.py:134
     style) gives the same logits as the one-pass prefill."""
