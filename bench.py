@@ -174,6 +174,37 @@ def gemm_bytes(group: str, B: int) -> float:
 
 
 # ----------------------------------------------------------------- CPU baseline
+def read_ceiling(nbytes: int, iters: int = 10) -> float:
+    """Median time (ms) of ne_stream_read over nbytes: the read-only floor of
+    the decode attention's data path for that many bytes in one launch."""
+    import torch
+    from neural_engine_b200 import runtime as rt
+    lib = rt.load_library()
+    nbytes = nbytes // 16 * 16
+    buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    buf.fill_(1)
+    sink = torch.zeros(2, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    ts = []
+    for i in range(iters + 3):
+        flush.fill_(i & 0xFF)   # larger than L2: every timed read comes from HBM
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        st = lib.ne_stream_read(buf.data_ptr(), nbytes, sink.data_ptr(), stream)
+        b.record()
+        if st != 0:
+            raise RuntimeError(f"ne_stream_read failed ({st})")
+        torch.cuda.synchronize()
+        if i >= 3:
+            ts.append(a.elapsed_time(b))
+    if int(sink[1].item()):
+        raise RuntimeError("ne_stream_read: a bounded wait ran out")
+    ts.sort()
+    del buf, flush
+    return ts[len(ts) // 2]
+
+
 def cpu_decode_sample(layers, rms_final, embed, qk, B=8, steps=12, prompt=512, seed=5):
     """Time the oracle's numpy token loop (restated from the reference's
     tools/generate.py) on the host cores: B sequences, KV cache pre-filled with
@@ -323,6 +354,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
         eng.train_fwd_bwd(h_tok)
         tstep[0] += 1
         eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world, return_norm=False)
+    eng.sync()   # the last AdamW is asynchronous: the timed region ends when it has run
     te = (time.perf_counter() - t0) / reps
     if world > 1:
         tt = torch.tensor([te], device="cuda")
@@ -443,6 +475,13 @@ def main():
                 "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
                 "peak_kind": peak_kind, "bytes_per_launch": dom_bytes,
                 "ms_per_launch": round(dom_ms, 4)}
+    if roof is not None and dom == "decode_attention" and rank == 0:
+        # the same bytes through the same data path with no arithmetic
+        rc_ms = read_ceiling(int(dom_bytes))
+        rc_gbs = dom_bytes / (rc_ms / 1000.0) / 1e9
+        roof["read_floor"] = {"kernel": "ne_stream_read", "ms": round(rc_ms, 4),
+                              "gbs": round(rc_gbs, 1), "frac_of_peak": round(rc_gbs / peak, 4)}
+        roof["frac_of_read_floor"] = round(rc_ms / dom_ms, 4)
     step_bytes = sum(decode_step_bytes(B, P + i) for i in range(G)) / G
     whole = {"bytes_per_decode_step": step_bytes,
              "achieved_gbs": round(step_bytes / (ms_step / G / 1000.0) / 1e9, 1),

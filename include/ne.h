@@ -364,6 +364,18 @@ NE_API ne_status ne_gemm_splitk_noalloc(const void* d_A, long long lda, int M, c
                                         long long ldb, int N, int K, int splits, float* d_out,
                                         long long ld, void* stream);
 
+/* ---------------------------------------------------------------- measurement
+ * Read-only streaming floor (no counterpart in the reference; a measuring aid
+ * for the decode attention's roofline).  Reads `bytes` (a multiple of 16) of
+ * device memory at d_src (16-byte aligned) once, through the decode attention's
+ * data path -- 8 warps per SM, equal per-warp ranges, 3-stage rings of 8 KB
+ * bulk copies -- with no arithmetic, XOR-folding one word per chunk into
+ * d_sink[0]; d_sink[1] is set to 1 if a bounded wait ran out.  Enqueued on
+ * `stream` (a cudaStream_t; NULL = default stream) without synchronising, so
+ * a caller can time it with events. */
+NE_API ne_status ne_stream_read(const void* d_src, long long bytes, unsigned int* d_sink,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

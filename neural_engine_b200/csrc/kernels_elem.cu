@@ -189,7 +189,9 @@ __device__ __forceinline__ void store_vec(T* dst, const float (&v)[PER]) {
   }
 }
 
-template <int HD, typename QT, typename KT>
+// One warp per (row, group of HPW heads): the group's loads are all issued
+// before any of them is used, so each warp keeps HPW x 512 bytes in flight.
+template <int HD, typename QT, typename KT, int HPW>
 __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long long split_stride,
                                 int rows, int S_rows, const int* __restrict__ d_pos, int pos0,
                                 int Hq, int Hkv, const float* __restrict__ qn,
@@ -203,8 +205,9 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
   const int warps_per_block = blockDim.x >> 5;
   const int gw = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
   const int nh = Hq + 2 * Hkv;
-  if (gw >= rows * nh) return;
-  const int r = gw / nh, h = gw % nh;
+  const int groups = nh / HPW;
+  if (gw >= rows * groups) return;
+  const int r = gw / groups, h0 = (gw % groups) * HPW;
   const int lane = threadIdx.x & 31;
   const int b = r / S_rows;
   const int pos = (d_pos ? *d_pos : pos0) + r % S_rows;
@@ -212,60 +215,74 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int nsplit, long 
     if (lane == 0) atomicExch(status, DEV_ERR_BOUNDS);
     return;
   }
-  const int qkv_dim = (Hq + 2 * Hkv) * HD;
-  const float* src = qkv + (size_t)r * qkv_dim + h * HD + lane * PER;
-  float v[PER];
+  const int qkv_dim = nh * HD;
+  const float* src = qkv + (size_t)r * qkv_dim + h0 * HD + lane * PER;
+  float v[HPW][PER];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) v[i] = 0.f;
+  for (int j = 0; j < HPW; ++j)
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[j][i] = 0.f;
   for (int s = 0; s < (nsplit > 0 ? nsplit : 1); ++s) {
-    if constexpr (PER == 4) {   // 16-byte aligned: rows and heads are multiples of 4 floats
-      const float4 t = *reinterpret_cast<const float4*>(src + (size_t)s * split_stride);
-      v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
-    } else {
 #pragma unroll
-      for (int i = 0; i < PER; ++i) v[i] += src[(size_t)s * split_stride + i];
+    for (int j = 0; j < HPW; ++j) {
+      const float* p = src + (size_t)s * split_stride + j * HD;
+      if constexpr (PER == 4) {   // 16-byte aligned: rows and heads are multiples of 4 floats
+        const float4 t = __ldcs(reinterpret_cast<const float4*>(p));
+        v[j][0] += t.x; v[j][1] += t.y; v[j][2] += t.z; v[j][3] += t.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) v[j][i] += p[i];
+      }
     }
   }
   if (zero_src) {
     // the source is an accumulator the next projection adds into: leave it zeroed
-    float* z = const_cast<float*>(src);
-    if constexpr (PER == 4) {
-      *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < HPW; ++j) {
+      float* z = const_cast<float*>(src) + j * HD;
+      if constexpr (PER == 4) {
+        *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) z[i] = 0.f;
+      }
+    }
+  }
+  // RoPE table row of this position: interleaved pairs (2i, 2i+1), PER/2 per lane
+  float2 cs[PER / 2];
+#pragma unroll
+  for (int i = 0; i < PER / 2; ++i) cs[i] = rope_cs[(size_t)pos * (HD / 2) + lane * (PER / 2) + i];
+#pragma unroll
+  for (int j = 0; j < HPW; ++j) {
+    const int h = h0 + j;
+    const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
+    if ((is_q || is_k) && qn != nullptr) {
+      const float* gain = is_q ? qn : kn;
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) ss += v[j][i] * v[j][i];
+      ss = warp_sum(ss);
+      const float rms = sqrtf(ss / (float)HD + qk_eps);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) v[j][i] = (v[j][i] / rms) * gain[lane * PER + i];
+    }
+    if (is_q || is_k) {
+#pragma unroll
+      for (int i = 0; i < PER / 2; ++i) {
+        const float v0 = v[j][2 * i], v1 = v[j][2 * i + 1];
+        v[j][2 * i] = v0 * cs[i].x - v1 * cs[i].y;
+        v[j][2 * i + 1] = v0 * cs[i].y + v1 * cs[i].x;
+      }
+    }
+    if (is_q) {
+      QT* dst = q_out + ((size_t)r * Hq + h) * HD + lane * PER;
+      store_vec<QT, PER>(dst, v[j]);
     } else {
-#pragma unroll
-      for (int i = 0; i < PER; ++i) z[i] = 0.f;
+      const int kvh = is_k ? (h - Hq) : (h - Hq - Hkv);
+      KT* cache = is_k ? kc : vc;
+      KT* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
+      store_vec<KT, PER>(dst, v[j]);
     }
-  }
-  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
-  if ((is_q || is_k) && qn != nullptr) {
-    const float* gain = is_q ? qn : kn;
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
-    ss = warp_sum(ss);
-    const float rms = sqrtf(ss / (float)HD + qk_eps);
-#pragma unroll
-    for (int i = 0; i < PER; ++i) v[i] = (v[i] / rms) * gain[lane * PER + i];
-  }
-  if (is_q || is_k) {
-    // interleaved pairs (2i, 2i+1); this lane holds PER/2 pairs
-    const float2* cs = rope_cs + (size_t)pos * (HD / 2) + lane * (PER / 2);
-#pragma unroll
-    for (int i = 0; i < PER / 2; ++i) {
-      const float2 c = cs[i];  // (cos, sin)
-      const float v0 = v[2 * i], v1 = v[2 * i + 1];
-      v[2 * i] = v0 * c.x - v1 * c.y;
-      v[2 * i + 1] = v0 * c.y + v1 * c.x;
-    }
-  }
-  if (is_q) {
-    QT* dst = q_out + ((size_t)r * Hq + h) * HD + lane * PER;
-    store_vec<QT, PER>(dst, v);
-  } else {
-    const int kvh = is_k ? (h - Hq) : (h - Hq - Hkv);
-    KT* cache = is_k ? kc : vc;
-    KT* dst = cache + (((size_t)b * Hkv + kvh) * Tmax + pos) * HD + lane * PER;
-    store_vec<KT, PER>(dst, v);
   }
 }
 
@@ -386,14 +403,22 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
                             void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
                             cudaStream_t st, int kv_bf16, int zero_src) {
-  const int warps = rows * (Hq + 2 * Hkv);
+  const int nh = Hq + 2 * Hkv;
+  const bool by4 = nh % 4 == 0;
+  const int warps = rows * (by4 ? nh / 4 : nh);
   const int threads = 256;
   const int blocks = (warps + 7) / 8;
 #define NE_QKV(HD_, QT_, KT_)                                                                    \
-  return launch_k(qkv_post_kernel<HD_, QT_, KT_>, dim3(blocks), dim3(threads), 0, st, qkv, nsplit, \
-                  split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn, qk_eps, rope_cs,     \
-                  reinterpret_cast<QT_*>(q_out), reinterpret_cast<KT_*>(kc),                     \
-                  reinterpret_cast<KT_*>(vc), Tmax, status, zero_src)
+  return by4 ? launch_k(qkv_post_kernel<HD_, QT_, KT_, 4>, dim3(blocks), dim3(threads), 0, st,   \
+                        qkv, nsplit, split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn,   \
+                        qk_eps, rope_cs, reinterpret_cast<QT_*>(q_out),                          \
+                        reinterpret_cast<KT_*>(kc), reinterpret_cast<KT_*>(vc), Tmax, status,    \
+                        zero_src)                                                                \
+             : launch_k(qkv_post_kernel<HD_, QT_, KT_, 1>, dim3(blocks), dim3(threads), 0, st,   \
+                        qkv, nsplit, split_stride, rows, S_rows, d_pos, pos0, Hq, Hkv, qn, kn,   \
+                        qk_eps, rope_cs, reinterpret_cast<QT_*>(q_out),                          \
+                        reinterpret_cast<KT_*>(kc), reinterpret_cast<KT_*>(vc), Tmax, status,    \
+                        zero_src)
   if (hd == 128) {
     if (kv_bf16) NE_QKV(128, __nv_bfloat16, __nv_bfloat16);
     if (q_type == 1) NE_QKV(128, __half, __half);

@@ -34,7 +34,7 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_embed_fwd", "ne_attn_fwd", "ne_ffn_fwd", "ne_lmhead_ce_fwd_bwd", "ne_ffn_bwd",
             "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
-            "ne_sdpa_fwd_device", "ne_train_set_vocab_map")
+            "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -180,6 +180,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_lr_schedule.argtypes = [I, F, I, I, F]
     lib.ne_lr_schedule.restype = F
     lib.ne_train_get_layer.argtypes = [P, I, I] + [P] * 11
+    lib.ne_stream_read.argtypes = [P, C.c_longlong, P, P]
     _lib = lib
     return lib
 
