@@ -1,0 +1,728 @@
+// attn_bwd_tc.cu -- causal GQA attention backward on the tcgen05 tensor cores
+// (training step, head_dim 128, bf16 operands, fp32 accumulation in TMEM).
+//
+// Same mathematics as attn_bwd.cu (the reference's sdpaBwd1 / sdpaBwd2,
+// ane-training/training/training_dynamic/mil_dynamic.h:583-707, then the GQA
+// group reduction gqa_reduce_kv_f16, cpu_ops.h:585, and the RoPE / QK-norm
+// backward, cpu_ops.h:510-537): P is recomputed from the forward's log2-domain
+// row log-sum-exp, dS = P (dP - D) with D = rowsum(dO * O).
+//
+//   dq_tc_kernel    one CTA per (128-query tile, q-head, sequence).  Per key
+//                   tile up to the diagonal: S = Q K^T and dP = dO V^T into
+//                   TMEM, dS (bf16) written by the softmax warps into shared
+//                   memory as a K-major operand, dQ += dS K in TMEM (K read
+//                   MN-major from the same shared tile).  It also computes D
+//                   for its queries and publishes it for the dK/dV kernel.
+//   dkdv_tc_kernel  one CTA per (128-key tile, kv-head, sequence), thread =
+//                   key.  Per (q-head of the group, query tile at or after the
+//                   keys): S^T = K Q^T and dP^T = V dO^T into TMEM, P^T and
+//                   dS^T (bf16) into shared memory, dV += P^T dO and
+//                   dK += dS^T Q in TMEM, so the group's dK / dV are summed in
+//                   the accumulators (no atomics).
+// Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// warps 2-9 element-wise work, two per TMEM lane quarter, each of the pair
+// owning 64 of the 128 columns.  Epilogues run the inverse RoPE and the
+// QK-norm backward on each thread's row and write bf16 into the gradient of
+// the fused QKV projection; the norm gains' gradients are reduced per CTA in
+// shared memory and added with one atomic per column.  Every mbarrier wait is
+// bounded (2 s) and records a timeout in the status word; the named barriers
+// of the epilogue are reached by every element-wise warp whatever happened
+// before them.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "ne_device.cuh"
+#include "ne_internal.h"
+#include "ne_launch.cuh"
+
+namespace ne {
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int TB_HD = 128;
+constexpr int TB_THREADS = 320;
+constexpr int TB_EW = 256;                        // element-wise threads (warps 2..9)
+constexpr uint32_t TB_ATOM = 128 * 128;           // 128 rows x 64 bf16, 128-byte swizzle
+constexpr uint32_t TB_TILE = 2 * TB_ATOM;         // 128 rows x 128 bf16
+constexpr uint32_t TB_HALF_ROWS = 64 * 128;       // 64 rows of one atom (MN-major K step)
+// gain-gradient staging: 128 rows x 129 floats (padded against bank conflicts)
+constexpr uint32_t TB_RED_BYTES = 128 * 129 * 4;
+// barrier area: 128 bytes of barriers / TMEM slot / abort flag, then the pair
+// exchange [2 quantities][2 halves][128 rows] floats
+constexpr int TB_BAR_AREA = 128 + 2 * 2 * 128 * 4;
+// dq: Q | dO | K | V | dS, then the barrier area (+1 KB alignment slack)
+constexpr int DQ_SMEM = 5 * TB_TILE + TB_BAR_AREA + 1024;
+// dkdv: K | V | Q | dO | P | dS | LSE, D (2 x 128 floats, 1 KB), barrier area
+constexpr int DKV_SMEM = 6 * TB_TILE + 1024 + TB_BAR_AREA + 1024;
+static_assert(TB_RED_BYTES <= 4 * TB_TILE, "staging fits in the operand tiles");
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// 32 bf16 values (16 packed words) of one row into a 128-byte-swizzled K-major
+// atom: columns c0 .. c0+31 (c0 a multiple of 32 within the atom's 64).
+__device__ __forceinline__ void st_row32(uint32_t atom, int row, int c0, const uint32_t (&w)[16]) {
+  const uint32_t rbase = atom + row * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int chunk = (c0 >> 3) + q;
+    st_shared_v4(rbase + ((chunk ^ (row & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2],
+                 w[4 * q + 3]);
+  }
+}
+
+// S-type product: D[128 x 128] = A[128 x 128] . B[128 x 128]^T, both K-major tiles.
+__device__ __forceinline__ void mma_kk(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < TB_HD / 16; ++kk) {
+    const uint64_t ad = smem_desc_k_sw128(a + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+    const uint64_t bd = smem_desc_k_sw128(b + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+    umma_f16(d, ad, bd, idesc, kk > 0);
+  }
+}
+// Accumulating product: D[128 x 128] (+)= A[128 x 128 (K)] . B where B is a
+// K-major tile [K rows][128] read MN-major (the K dimension runs over its rows).
+__device__ __forceinline__ void mma_kmn(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc,
+                                        bool acc) {
+#pragma unroll
+  for (int kk = 0; kk < 128 / 16; ++kk) {
+    const uint64_t ad = smem_desc_k_sw128(a + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+    const uint64_t bd = smem_desc_mn_sw128(b + (kk >> 2) * TB_HALF_ROWS, TB_ATOM) + 128 * (kk & 3);
+    umma_f16(d, ad, bd, idesc, (acc || kk > 0) ? 1u : 0u);
+  }
+}
+
+// Inverse RoPE and QK-norm backward of one head row's gradient, this thread
+// holding 64 consecutive columns c_lo .. c_lo+63 (the pair's other thread the
+// other 64): d (in/out), x = raw pre-norm row (same columns), dg += d x rrms.
+// `xch` is the pair's exchange area [2][128] floats, `bar_id` its barrier.
+// Every thread of the pair calls this (ok or not) so the barriers match.
+struct RowBwd {
+  const float* gain;      // QK-norm gain (nullptr: none)
+  float eps;
+  const float2* rope_cs;  // [pos][64] (cos, sin)
+};
+__device__ __forceinline__ void row_bwd(float (&d)[64], const float* raw, int pos, bool ok,
+                                        int c_lo, const RowBwd& rb, float* xch, int half,
+                                        int row, int bar_id, float (&dg)[64]) {
+  if (ok) {
+    const float2* cs = rb.rope_cs + (size_t)pos * (TB_HD / 2) + c_lo / 2;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float2 c = cs[i];
+      const float d0 = d[2 * i], d1 = d[2 * i + 1];
+      d[2 * i] = d0 * c.x + d1 * c.y;
+      d[2 * i + 1] = d1 * c.x - d0 * c.y;
+    }
+  }
+  if (rb.gain == nullptr) return;
+  float x[64];
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 4) {
+    const float4 xv = ok ? *reinterpret_cast<const float4*>(raw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[i] = xv.x; x[i + 1] = xv.y; x[i + 2] = xv.z; x[i + 3] = xv.w;
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    ss += x[i] * x[i];
+    dot += d[i] * rb.gain[c_lo + i] * x[i];
+  }
+  xch[half * 128 + row] = ss;
+  xch[256 + half * 128 + row] = dot;
+  named_bar(bar_id, 64);
+  ss += xch[(half ^ 1) * 128 + row];
+  dot += xch[256 + (half ^ 1) * 128 + row];
+  named_bar(bar_id, 64);   // the exchange area is reusable
+  const float rrms = 1.0f / sqrtf(ss / (float)TB_HD + rb.eps);
+  const float c = rrms * rrms * dot / (float)TB_HD;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    if (ok) dg[i] += d[i] * x[i] * rrms;
+    d[i] = rrms * (rb.gain[c_lo + i] * d[i] - x[i] * c);
+  }
+}
+
+// Sum the element-wise threads' gain-gradient rows (each thread: 64 columns
+// of one of 128 rows) over the rows and add them to dgain[128].  `red` is
+// free shared memory of TB_RED_BYTES; all 256 element-wise threads call it.
+__device__ __forceinline__ void gain_flush(const float (&dg)[64], float* red, int half, int row,
+                                           int t, float* dgain) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i) red[row * 129 + half * 64 + i] = dg[i];
+  named_bar(5, TB_EW);
+  if (t < TB_HD) {
+    float s = 0.f;
+    for (int r = 0; r < 128; ++r) s += red[r * 129 + t];
+    atomicAdd(dgain + t, s);
+  }
+}
+
+__device__ __forceinline__ void store_row64_bf16(bf16* dst, const float (&d)[64]) {
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    uint4 pk;
+    __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) hv[t] = __floats2bfloat162_rn(d[i + 2 * t], d[i + 2 * t + 1]);
+    *reinterpret_cast<uint4*>(dst + i) = pk;
+  }
+}
+
+// Bounded wait that every lane of the warp performs; warp-uniform outcome.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* status,
+                                          volatile int* abort_flag) {
+  const bool ok = mbar_wait(bar, parity, status, abort_flag);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// ================================================================== dQ
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+             const bf16* __restrict__ O, const bf16* __restrict__ dO,
+             const float* __restrict__ LSE, float* __restrict__ Dl, int S, int Hq, int Hkv,
+             int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
+             RowBwd rb, bf16* __restrict__ dqkv, float* __restrict__ dqn, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base, sdO = sQ + TB_TILE, sK = sdO + TB_TILE, sV = sK + TB_TILE;
+  const uint32_t sdS = sV + TB_TILE;
+  const uint32_t bars = sdS + TB_TILE;
+  const uint32_t q_full = bars, kv_full = bars + 8, kv_empty = bars + 16, s_full = bars + 24;
+  const uint32_t ds_full = bars + 32, dq_done = bars + 40, drain = bars + 48;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 64);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 68);
+  float* const xch = reinterpret_cast<float*>(gbars + 128);   // [2][2][128], indexed by row
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (Hq / Hkv);
+  const int q0 = qt * 128;
+  const int n_keys = min(S, q0 + 128);
+  const int n_kt = (n_keys + 127) / 128;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(128, 128, 1, 0, 0);
+  constexpr uint32_t IDESC_Q = umma_idesc_f16(128, TB_HD, 1, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, TB_EW);
+    mbar_init(dq_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmdO);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S at +0, dP at +128, dQ at +256
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = policy_evict_last();
+      const int qrow = b * S + q0;
+      const int kvrow = (b * Hkv + kvh) * Tmax;
+      mbar_arrive_expect_tx(q_full, 2 * TB_TILE);
+      for (int a = 0; a < 2; ++a) {
+        tma_load_2d(sQ + a * TB_ATOM, &tmQ, q_full, h * TB_HD + a * 64, qrow, pol);
+        tma_load_2d(sdO + a * TB_ATOM, &tmdO, q_full, h * TB_HD + a * 64, qrow, pol);
+      }
+      int j = 0;
+      for (; j < n_kt; ++j) {
+        if (j > 0 && !mbar_wait(kv_empty, (j - 1) & 1, status, abort_flag)) break;
+        mbar_arrive_expect_tx(kv_full, 2 * TB_TILE);
+        for (int a = 0; a < 2; ++a) {
+          tma_load_2d(sK + a * TB_ATOM, &tmK, kv_full, a * 64, kvrow + j * 128, pol);
+          tma_load_2d(sV + a * TB_ATOM, &tmV, kv_full, a * 64, kvrow + j * 128, pol);
+        }
+      }
+      // drain (bounded): the loads issued have landed before the CTA exits
+      {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+      if (j > 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full, (j - 1) & 1))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, status, abort_flag);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (!(ok = mbar_wait(kv_full, j & 1, status, abort_flag))) break;
+        tc_fence_after();
+        mma_kk(tmem, sQ, sK, IDESC_S);           // S = Q K^T
+        mma_kk(tmem + 128, sdO, sV, IDESC_S);    // dP = dO V^T
+        umma_commit(s_full);
+        if (!(ok = mbar_wait(ds_full, j & 1, status, abort_flag))) break;
+        tc_fence_after();
+        mma_kmn(tmem + 256, sdS, sK, IDESC_Q, j > 0);   // dQ += dS K
+        umma_commit(dq_done);
+        umma_commit(kv_empty);
+      }
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ element-wise warps
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const bool qv = q < S;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int c_lo = half * 64;
+    float* const pxch = xch;   // pairs own disjoint rows of the shared exchange area
+    pdl_wait();   // O, dO and LSE come from earlier kernels
+    // D = rowsum(dO * O) over this thread's 64 columns, then the pair's sum
+    float dsum = 0.f;
+    if (qv) {
+      const size_t off = ((size_t)(b * S + q) * Hq + h) * TB_HD + c_lo;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) {
+        const uint4 ov = *reinterpret_cast<const uint4*>(O + off + i);
+        const uint4 gv = *reinterpret_cast<const uint4*>(dO + off + i);
+        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
+          dsum += of.x * gf.x + of.y * gf.y;
+        }
+      }
+    }
+    pxch[half * 128 + row] = dsum;
+    named_bar(1 + quarter, 64);
+    const float Drow = dsum + pxch[(half ^ 1) * 128 + row];
+    named_bar(1 + quarter, 64);
+    if (half == 0 && qv) Dl[((size_t)b * Hq + h) * S + q] = Drow;
+    const float Lrow = qv ? LSE[((size_t)b * Hq + h) * S + q] : 0.f;
+
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      bool ready = true;
+      if (j > 0) ready = warp_wait(dq_done, (j - 1) & 1, status, abort_flag);   // dS free
+      ready = warp_wait(s_full, j & 1, status, abort_flag) && ready;
+      if (!ready) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t srow = tmem + lane_off;
+      const int kbase = j * 128;
+      for (int c = c_lo; c < c_lo + 64; c += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(srow + c, rs);
+        tmem_ld32(srow + 128 + c, rp);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float ds2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = kbase + c + i + e;
+            const float p = (qv && key <= q && key < S)
+                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - Lrow) : 0.f;
+            ds2[e] = p * (__uint_as_float(rp[i + e]) - Drow);
+          }
+          const __nv_bfloat162 pk = __floats2bfloat162_rn(ds2[0], ds2[1]);
+          w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+        }
+        st_row32(sdS + (c >> 6) * TB_ATOM, row, c & 63, w);
+      }
+      fence_async_smem();   // dS visible to the tensor cores
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    // ---- epilogue: dQ * scale through the RoPE / q-norm backward, bf16 out
+    if (ok && n_kt > 0) ok = warp_wait(dq_done, (n_kt - 1) & 1, status, abort_flag);
+    float d[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    if (ok) {
+      tc_fence_after();
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 256 + c_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
+      }
+    }
+    const int qkv_dim = (Hq + 2 * Hkv) * TB_HD;
+    const size_t tok = (size_t)b * S + (qv ? q : 0);
+    const bool rv = ok && qv;
+    float dg[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) dg[i] = 0.f;
+    row_bwd(d, qkv_raw + tok * qkv_dim + (size_t)h * TB_HD + c_lo, q, rv, c_lo, rb,
+            pxch, half, row, 1 + quarter, dg);
+    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + (size_t)h * TB_HD + c_lo, d);
+    if (rb.gain != nullptr) {
+      // every MMA and load of this CTA has completed (dq_done of the last
+      // tile, or nothing was issued): reuse the operand tiles as staging
+      gain_flush(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dqn);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ================================================================== dK, dV
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq,
+               int Hkv, int Tmax, float scale_log2, float scale,
+               const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
+               float* __restrict__ dkn, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t sK = base, sV = sK + TB_TILE, sQ = sV + TB_TILE, sdO = sQ + TB_TILE;
+  const uint32_t sP = sdO + TB_TILE, sdS = sP + TB_TILE;
+  float* const sL = reinterpret_cast<float*>(gbase + 6 * TB_TILE);   // [128]
+  float* const sD = sL + 128;                                        // [128]
+  const uint32_t bars = sdS + TB_TILE + 1024;
+  const uint32_t kv_full = bars, qd_full = bars + 8, qd_empty = bars + 16, s_full = bars + 24;
+  const uint32_t ps_full = bars + 32, mm2_done = bars + 40, drain = bars + 48;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 64);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 68);
+  float* const xch = reinterpret_cast<float*>(gbars + 128);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int k0 = kt * 128;
+  const int n_qt_all = (S + 127) / 128;
+  const int n_qt = n_qt_all - kt;          // query tiles at or after this key tile
+  const int n_it = G * n_qt;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(128, 128, 1, 0, 0);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(128, TB_HD, 1, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qd_full, 32);       // the producer warp's lanes (LSE / D) + the TMA bytes
+    mbar_init(qd_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(ps_full, TB_EW);
+    mbar_init(mm2_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmdO);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S^T +0, dP^T +128, dV +256, dK +384
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer (whole warp)
+    pdl_wait();
+    const uint64_t pol = policy_evict_last();
+    const int kvrow = (b * Hkv + kvh) * Tmax + k0;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * TB_TILE);
+      for (int a = 0; a < 2; ++a) {
+        tma_load_2d(sK + a * TB_ATOM, &tmK, kv_full, a * 64, kvrow, pol);
+        tma_load_2d(sV + a * TB_ATOM, &tmV, kv_full, a * 64, kvrow, pol);
+      }
+    }
+    int it = 0;
+    for (; it < n_it; ++it) {
+      const int h = kvh * G + it / n_qt;
+      const int q0 = (kt + it % n_qt) * 128;
+      if (it > 0 && !warp_wait(qd_empty, (it - 1) & 1, status, abort_flag)) break;
+      for (int r = lane; r < 128; r += 32) {
+        const int qq = q0 + r;
+        const bool v = qq < S;
+        sL[r] = v ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
+        sD[r] = v ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(qd_full, 2 * TB_TILE);
+        const int qrow = b * S + q0;
+        for (int a = 0; a < 2; ++a) {
+          tma_load_2d(sQ + a * TB_ATOM, &tmQ, qd_full, h * TB_HD + a * 64, qrow, pol);
+          tma_load_2d(sdO + a * TB_ATOM, &tmdO, qd_full, h * TB_HD + a * 64, qrow, pol);
+        }
+      } else {
+        mbar_arrive(qd_full);
+      }
+    }
+    if (lane == 0) {   // drain (bounded)
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(kv_full, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+      if (it > 0) {
+        const uint64_t t1 = globaltimer_ns();
+        while (!mbar_try_wait(qd_full, (it - 1) & 1))
+          if (globaltimer_ns() - t1 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, status, abort_flag);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!(ok = mbar_wait(qd_full, it & 1, status, abort_flag))) break;
+        tc_fence_after();
+        mma_kk(tmem, sK, sQ, IDESC_S);           // S^T = K Q^T
+        mma_kk(tmem + 128, sV, sdO, IDESC_S);    // dP^T = V dO^T
+        umma_commit(s_full);
+        if (!(ok = mbar_wait(ps_full, it & 1, status, abort_flag))) break;
+        tc_fence_after();
+        mma_kmn(tmem + 256, sP, sdO, IDESC_O, it > 0);    // dV += P^T dO
+        mma_kmn(tmem + 384, sdS, sQ, IDESC_O, it > 0);    // dK += dS^T Q
+        umma_commit(mm2_done);
+        umma_commit(qd_empty);
+      }
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ element-wise warps
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int key = k0 + row;
+    const bool kv = key < S;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int c_lo = half * 64;
+    float* const pxch = xch;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (kt + it % n_qt) * 128;
+      bool ready = true;
+      if (it > 0) ready = warp_wait(mm2_done, (it - 1) & 1, status, abort_flag);   // P, dS free
+      ready = warp_wait(s_full, it & 1, status, abort_flag) && ready;
+      ready = warp_wait(qd_full, it & 1, status, abort_flag) && ready;   // LSE / D of this tile
+      if (!ready) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t srow = tmem + lane_off;
+      for (int c = c_lo; c < c_lo + 64; c += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(srow + c, rs);
+        tmem_ld32(srow + 128 + c, rp);
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int ql = c + i + e;
+            const int qq = q0 + ql;
+            const float p = (kv && key <= qq && qq < S)
+                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - sL[ql]) : 0.f;
+            p2[e] = p;
+            d2[e] = p * (__uint_as_float(rp[i + e]) - sD[ql]);
+          }
+          const __nv_bfloat162 pp = __floats2bfloat162_rn(p2[0], p2[1]);
+          const __nv_bfloat162 dd = __floats2bfloat162_rn(d2[0], d2[1]);
+          wp[i >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
+          wd[i >> 1] = *reinterpret_cast<const uint32_t*>(&dd);
+        }
+        st_row32(sP + (c >> 6) * TB_ATOM, row, c & 63, wp);
+        st_row32(sdS + (c >> 6) * TB_ATOM, row, c & 63, wd);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(ps_full);
+    }
+    // ---- epilogue: dV unchanged, dK * scale through RoPE / k-norm backward
+    if (ok && n_it > 0) ok = warp_wait(mm2_done, (n_it - 1) & 1, status, abort_flag);
+    const int qd = Hq * TB_HD, qkv_dim = (Hq + 2 * Hkv) * TB_HD;
+    const size_t tok = (size_t)b * S + (kv ? key : 0);
+    const size_t kcol = (size_t)qd + (size_t)kvh * TB_HD, vcol = kcol + (size_t)Hkv * TB_HD;
+    const bool rv = ok && kv;
+    float d[64];
+    if (ok) tc_fence_after();
+    // dV
+#pragma unroll
+    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    if (ok && n_it > 0) {
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 256 + c_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]);
+      }
+    }
+    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + vcol + c_lo, d);
+    // dK
+#pragma unroll
+    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    if (ok && n_it > 0) {
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 384 + c_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
+      }
+    }
+    float dg[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) dg[i] = 0.f;
+    row_bwd(d, qkv_raw + tok * qkv_dim + kcol + c_lo, key, rv, c_lo, rb, pxch, half, row,
+            1 + quarter, dg);
+    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + kcol + c_lo, d);
+    if (rb.gain != nullptr)
+      gain_flush(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dkn);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) ==
+            cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 [rows, cols] row-major, 128-byte-swizzled boxes of 64 columns x 128 rows.
+bool tmap_tile(CUtensorMap* tm, const void* ptr, long long rows, long long cols) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool attn_bwd_tc_supported(int hd) { return hd == TB_HD; }
+
+cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, const __nv_bfloat16* O,
+                               const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                               int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                               const float* qn, const float* kn, float qk_eps,
+                               const float2* rope_cs, __nv_bfloat16* dqkv, float* dqn, float* dkn,
+                               int* status, cudaStream_t st, bool tc_dq) {
+  if (hd != TB_HD || Hq % Hkv || S <= 0 || rope_cs == nullptr) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O) |
+       reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dqkv) |
+       reinterpret_cast<uintptr_t>(qkv_raw)) & 15)
+    return cudaErrorInvalidValue;
+  CUtensorMap tq, tdo, tk, tv;
+  if (!tmap_tile(&tq, Q, (long long)B * S, (long long)Hq * hd) ||
+      !tmap_tile(&tdo, dO, (long long)B * S, (long long)Hq * hd) ||
+      !tmap_tile(&tk, K, (long long)B * Hkv * Tmax, hd) ||
+      !tmap_tile(&tv, V, (long long)B * Hkv * Tmax, hd))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         DQ_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DKV_SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const float scale = 1.0f / sqrtf((float)hd);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int n_t = (S + 127) / 128;
+  // dQ first: it also publishes D, which dK / dV read
+  cudaError_t e =
+      tc_dq ? launch_k(dq_tc_kernel, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)DQ_SMEM, st, tq,
+                       tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                       RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
+            : launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn, qk_eps,
+                                 rope_cs, dqkv, dqn, st);
+  if (e != cudaSuccess) return e;
+  return launch_k(dkdv_tc_kernel, dim3(n_t, Hkv, B), dim3(TB_THREADS), (size_t)DKV_SMEM, st, tq,
+                  tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                  RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn, status);
+}
+
+}  // namespace ne

@@ -137,7 +137,24 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
                             int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
-                            __nv_bfloat16* dqkv, float* dqn, float* dkn, cudaStream_t st);
+                            __nv_bfloat16* dqkv, float* dqn, float* dkn, int* status,
+                            cudaStream_t st);
+// tcgen05 variant (head_dim 128), chosen by launch_attn_bwd; tc_dq = false
+// computes dQ (and D) with the mma.sync kernel and dK / dV with tcgen05.
+cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, const __nv_bfloat16* O,
+                               const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                               int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                               const float* qn, const float* kn, float qk_eps,
+                               const float2* rope_cs, __nv_bfloat16* dqkv, float* dqn, float* dkn,
+                               int* status, cudaStream_t st, bool tc_dq);
+// mma.sync dQ kernel alone (also publishes D); head_dim 128.
+cudaError_t launch_attn_dq_mma(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, const __nv_bfloat16* O,
+                               const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                               int Hq, int Hkv, int Tmax, const float* qkv_raw, const float* qn,
+                               float qk_eps, const float2* rope_cs, __nv_bfloat16* dqkv,
+                               float* dqn, cudaStream_t st);
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,
                                int D, const float* residual, float* dx, __nv_bfloat16* dx16,
                                float* dw, cudaStream_t st);

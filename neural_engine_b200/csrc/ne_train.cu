@@ -720,7 +720,7 @@ NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int l) {
     return s;
   NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, a.QKVR,
                             m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
-                            m.qk_eps, ctx->rope_cs, t->DQKV, p.g_qn, p.g_kn, st));
+                            m.qk_eps, ctx->rope_cs, t->DQKV, p.g_qn, p.g_kn, ctx->d_status, st));
   ctx->launches += 1;
   if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
     return s;

@@ -149,6 +149,29 @@ def test_training_reduces_loss():
     e.close()
 
 
+HD128 = [dict(head_dim=128, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=1e-6),
+         dict(head_dim=128, heads=4, kv_heads=4, qk_norm=False, theta=1e4, eps=1e-5)]
+
+
+@pytest.mark.parametrize("kw", HD128)
+@pytest.mark.parametrize("B,S", [(2, 224), (1, 256), (4, 80), (1, 1088)])
+def test_head_dim_128_attention_backward(kw, B, S):
+    """head_dim 128 takes the tcgen05 attention kernels (forward, dK / dV,
+    and dQ from 1024 positions on): several 128-row query / key tiles, a ragged
+    last tile, GQA groups of 2 and 1, with and without QK-norm."""
+    cfg = _cfg(**kw)
+    layers, rf, emb, qk = om.init_weights(cfg, seed=71, std=0.08, bf16=True)
+    layers, rf, qk = om.random_gains(cfg, layers, rf, qk)
+    tok = om.prompt_tokens(cfg.vocab, S + 1, 72, batch=B)
+    e = _engine(cfg, layers, rf, emb, qk, B, S)
+    loss = e.train_fwd_bwd(tok)
+    ref_loss, g_ref = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok)
+    assert abs(loss - ref_loss) <= LOSS_REL * ref_loss, (loss, ref_loss)
+    worst = _compare_grads(cfg, e.get_grads(), g_ref)
+    print(f"loss {loss:.6f} ref {ref_loss:.6f}; worst grad rel-L2 {worst[1]:.3e} ({worst[0]})")
+    e.close()
+
+
 @pytest.mark.parametrize("name", ["stories110m", "qwen3_06b"])
 def test_full_width_two_layers(name):
     """Full-width Stories110M / Qwen3-0.6B layers (2 of them, full vocabulary,
