@@ -67,10 +67,26 @@ def build(verbose: bool = True, extra: list[str] | None = None) -> str:
 
 HOST_SRC = os.path.join(PKG, "host", "ne_train.cpp")
 HOST_BIN = os.path.join(PKG, "ne_train")
+CONV_SRC = os.path.join(PKG, "host", "ne_convert.cpp")
+CONV_BIN = os.path.join(PKG, "ne_convert")
+
+
+def build_convert(verbose: bool = True) -> str:
+    """ne_convert: HF safetensors <-> v4 checkpoint (plain C++, no CUDA)."""
+    if os.path.exists(CONV_BIN) and os.path.getmtime(CONV_BIN) >= os.path.getmtime(CONV_SRC):
+        return CONV_BIN
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-Wall", CONV_SRC, "-o", CONV_BIN]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ne_convert build failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(f"built {CONV_BIN}")
+    return CONV_BIN
 
 
 def build_host(verbose: bool = True) -> str:
     """The ne_train command-line driver (plain C++ over the C ABI of libne.so)."""
+    build_convert(verbose)
     if os.path.exists(HOST_BIN) and os.path.getmtime(HOST_BIN) >= max(
             os.path.getmtime(HOST_SRC), os.path.getmtime(LIB),
             os.path.getmtime(os.path.join(ROOT, "include", "ne.h"))):

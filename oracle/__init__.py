@@ -15,6 +15,9 @@ Modules
   decode    -- numpy token loop restated from tools/generate.py:81-228,
                parameterised (RoPE theta, eps, QK-norm, residual alpha,
                batched sequences, prompt processed in one causal pass)
+  hf_fixture -- seeded synthetic Hugging Face checkpoints (safetensors I/O)
+               and the HF Qwen3 forward (rotate_half RoPE) in float64, for the
+               converter tests
   train     -- float64 torch autograd of the same forward (teacher-forced,
                full-vocab mean cross-entropy) and the AdamW step restated from
                cpu_ops.h:266-303 with the schedule / clip of train.m:782-858
