@@ -90,29 +90,33 @@ bool stage_ok(const void* out, long long ld, int elem_bytes) {
   return out && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (ld * elem_bytes) % 16 == 0;
 }
 
-template <int BN, class Epi, int FMT, int AMN, int BMN>
+template <int BN, class Epi, int FMT, int AMN, int BMN, int CG = 1>
 cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                      const CUtensorMap& td, const GemmShape& sh, const typename Epi::Params& p,
                      int grid, cudaStream_t st) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
   constexpr int smem = EpiStage<Epi>::value ? C::SMEM_BYTES_STAGED : C::SMEM_BYTES;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN, CG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  return launch_k(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN>, dim3(grid), dim3(GEMM_THREADS),
+  if constexpr (CG == 2)
+    return launch_k_cluster(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN, CG>, dim3(grid),
+                            dim3(GEMM_THREADS), (size_t)smem, st, 2u, ta, tb, tc, td, sh, p);
+  return launch_k(gemm_tc_kernel<BN, Epi, FMT, AMN, BMN, CG>, dim3(grid), dim3(GEMM_THREADS),
                   (size_t)smem, st, ta, tb, tc, td, sh, p);
 }
 
 // Epilogue dispatch.  K-major x K-major serves every epilogue; the MN-major
 // variants (training backward) instantiate only the epilogues they use.
-template <int BN, int FMT, int AMN, int BMN>
+template <int BN, int FMT, int AMN, int BMN, int CG = 1>
 cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorMap& tb,
                        const GemmShape& sh, int grid, cudaStream_t st) {
   constexpr bool kk = (AMN == 0 && BMN == 0);
+  constexpr bool tr_ok = CG == 1;   // transposed (swap-AB) epilogues: single-CTA tiles only
   constexpr bool kmn = (AMN == 0 && BMN == 1);
   constexpr bool ch32 = GemmCfg<BN>::CH == 32;
   CUtensorMap tc, td;
@@ -120,19 +124,19 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
   std::memset(&td, 0, sizeof(td));
   switch (c.epi) {
     case EPI_F32T:
-      if constexpr (kk) {
+      if constexpr (kk && tr_ok) {
         EpiF32T::Params p{(float*)c.out, c.ld, c.split_stride};
-        return launch_t<BN, EpiF32T, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiF32T, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_F32T_ADD:
-      if constexpr (kk && ch32) {
+      if constexpr (kk && ch32 && tr_ok) {
         // out [N (batch) rows, M (features) columns], leading dim ld
         if (!stage_ok(c.out, c.ld, 4) ||
             !make_tmap_out(&tc, c.out, c.N, c.M, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32))
           return cudaErrorInvalidValue;
         EpiF32TS::Params p{c.alpha};
-        return launch_t<BN, EpiF32TS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiF32TS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_F32: {
@@ -140,11 +144,11 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiF32S::Params p{0};
-          return launch_t<BN, EpiF32S, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+          return launch_t<BN, EpiF32S, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       EpiF32::Params p{(float*)c.out, c.ld, c.split_stride};
-      return launch_t<BN, EpiF32, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+      return launch_t<BN, EpiF32, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
     }
     case EPI_BF16:
       if constexpr (kk || kmn) {
@@ -154,12 +158,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
                             c.half_out ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 32)) {
             EpiBF16S::Params p{c.alpha, c.half_out};
-            return launch_t<BN, EpiBF16S, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+            return launch_t<BN, EpiBF16S, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
           }
         }
         if constexpr (kk) {
           EpiBF16::Params p{c.out, c.ld, c.alpha, c.half_out};
-          return launch_t<BN, EpiBF16, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+          return launch_t<BN, EpiBF16, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       break;
@@ -168,12 +172,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiResidS::Params p{c.alpha};
-          return launch_t<BN, EpiResidS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+          return launch_t<BN, EpiResidS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
         }
       }
       if constexpr (kk) {
         EpiResid::Params p{(float*)c.out, c.ld, c.alpha, c.atomic};
-        return launch_t<BN, EpiResid, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiResid, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     }
@@ -186,13 +190,13 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
                                      2, 32))
           return cudaErrorInvalidValue;
         EpiSwiGLUS::Params p{c.aux1 != nullptr};
-        return launch_t<BN, EpiSwiGLUS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiSwiGLUS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_ADD:
       if constexpr (kk) {
         EpiAdd::Params p{(float*)c.out, (const float*)c.aux3, c.ld, c.alpha};
-        return launch_t<BN, EpiAdd, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiAdd, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_SWIGLU_BWD:
@@ -202,7 +206,7 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64))
           return cudaErrorInvalidValue;
         EpiSwiGLUBwdS::Params p{(const __nv_bfloat16*)c.aux3, c.aux_ld, c.alpha};
-        return launch_t<BN, EpiSwiGLUBwdS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiSwiGLUBwdS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     case EPI_F32_STATS:
@@ -210,10 +214,10 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         if (stage_ok(c.out, c.ld, 4) &&
             make_tmap_out(&tc, c.out, c.M, c.N, c.ld, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32)) {
           EpiF32StatsS::Params p{(float2*)c.aux1, c.aux_ld};
-          return launch_t<BN, EpiF32StatsS, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+          return launch_t<BN, EpiF32StatsS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
         }
         EpiF32Stats::Params p{(float*)c.out, c.ld, (float2*)c.aux1, c.aux_ld};
-        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN>(ta, tb, tc, td, sh, p, grid, st);
+        return launch_t<BN, EpiF32Stats, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
     default:
@@ -310,24 +314,42 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
       !(c.epi == EPI_RESID && c.atomic))
     return cudaErrorInvalidValue;
 
+  // CTA pairs (cta_group::2, 256 x 256 tiles over two SMs) for the large
+  // token-major products; NE_GEMM_PAIR=0 keeps single-CTA tiles everywhere.
+  static const bool pair_on = [] {
+    const char* e = getenv("NE_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  const bool pair = pair_on && bn == 256 && c.max_ctas <= 0 && c.M >= 512 &&
+                    c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && num_sms >= 2;
+  const int tile_m = pair ? 2 * GEMM_BM : GEMM_BM;
+
   CUtensorMap ta, tb;
   const bool ok_a = c.a_mn ? make_tmap_mn(&ta, c.A, c.M, c.K, c.lda)
                            : make_tmap(&ta, c.A, c.M, c.K, c.lda, GEMM_BM, 0);
+  // pair mode: each CTA loads half of B's rows per stage
   const bool ok_b = c.b_mn ? make_tmap_mn(&tb, c.B, c.N, c.K, c.ldb)
-                           : make_tmap(&tb, c.B, c.N, c.K, c.ldb, bn, 0);
+                           : make_tmap(&tb, c.B, c.N, c.K, c.ldb, pair ? bn / 2 : bn, 0);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
 
   GemmShape sh;
   sh.M = c.M;
   sh.N = c.N;
   sh.K = c.K;
-  sh.m_tiles = (c.M + GEMM_BM - 1) / GEMM_BM;
+  sh.m_tiles = (c.M + tile_m - 1) / tile_m;
   sh.n_tiles = (c.N + bn - 1) / bn;
   sh.splits = splits;
   sh.kb_per_split = kb / splits;
   sh.status = status;
   sh.prefetch_a = c.prefetch_a;
   const long long units = (long long)sh.m_tiles * sh.n_tiles * splits;
+  if (pair) {
+    const long long clusters = units < num_sms / 2 ? units : num_sms / 2;
+    const int grid2 = (int)(2 * clusters);
+    if (!c.a_mn && !c.b_mn) return launch_epi<256, 1, 0, 0, 2>(c, ta, tb, sh, grid2, st);
+    if (!c.a_mn) return launch_epi<256, 1, 0, 1, 2>(c, ta, tb, sh, grid2, st);
+    return launch_epi<256, 1, 1, 1, 2>(c, ta, tb, sh, grid2, st);
+  }
   const int cap = c.max_ctas > 0 ? c.max_ctas : num_sms;
   const int grid = (int)(units < cap ? units : cap);
 

@@ -49,11 +49,14 @@ struct GemmShape {
                         // tiles may be loaded before the PDL dependency wait
 };
 
-template <int BN>
+// CG = 2: a CTA pair shares each 256 x BN tile (cta_group::2); each CTA
+// stages its 128 rows of A and BN/2 rows of B.
+template <int BN, int CG = 1>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(CG == 1 || (CG == 2 && BN % 32 == 0), "pair tiles split B in halves");
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int B_BYTES = (BN / CG) * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
@@ -515,18 +518,21 @@ struct EpiSwiGLUBwdS {
 // A_MN / B_MN: the operand is stored MN-major in global memory ([K rows][MN
 // contiguous]); its tile is then loaded as 64-wide MN boxes of 64 K-rows (8 KB
 // each, placed 8 KB apart) and described to the MMA as MN-major.
-template <int BN, class Epi, int AB_FMT, int A_MN = 0, int B_MN = 0>
+template <int BN, class Epi, int AB_FMT, int A_MN = 0, int B_MN = 0, int CG = 1>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                const GemmShape sh, const typename Epi::Params ep) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
+  constexpr bool PAIR = CG == 2;
+  constexpr int TILE_M = GEMM_BM * CG;          // rows of A per work unit (both CTAs)
+  static_assert(!PAIR || !EpiTransposed<Epi>::value, "pair tiles: row-major epilogues only");
   constexpr int STG = EpiStage<Epi>::value;   // 0: direct stores, 1: TMA store, 2: TMA add
   static_assert(!B_MN || BN % 64 == 0, "MN-major B needs whole 64-wide boxes");
   constexpr uint32_t MN_BOX = 64 * GEMM_BK * 2;   // one 64 (MN) x 64 (K) box
   constexpr int STAGES = C::STAGES;
   constexpr int CH = C::CH;
-  constexpr uint32_t IDESC = umma_idesc_f16(GEMM_BM, BN, AB_FMT, A_MN, B_MN);
+  constexpr uint32_t IDESC = umma_idesc_f16(TILE_M, BN, AB_FMT, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled tiles
@@ -547,6 +553,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int units = sh.m_tiles * sh.n_tiles * sh.splits;
+  // pair mode: both CTAs of a cluster walk the same units (one per cluster)
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int u_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int u_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -555,7 +565,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar + 8 * a, 1);
-      mbar_init(tempty_bar + 8 * a, 32 * GEMM_EPI_WARPS);
+      // pair mode: one arrival per epilogue warp of both CTAs (on the even CTA's)
+      mbar_init(tempty_bar + 8 * a, PAIR ? 2 * GEMM_EPI_WARPS : 32 * GEMM_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -566,12 +577,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if constexpr (EpiHasBox2<Epi>::value) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   pdl_trigger();
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();   // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -580,36 +597,47 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       const uint64_t pol_a = policy_evict_first();
       const uint64_t pol_b = policy_evict_last();
+      // pair mode: every load of both CTAs completes on the even CTA's full
+      // barrier, which the even CTA arms for the bytes of both
+      auto tma_ld = [&](uint32_t dst, const CUtensorMap* tm, uint32_t bar, int c0, int c1,
+                        uint64_t pol) {
+        if constexpr (PAIR) tma_load_2d_pair(dst, tm, mapa_shared(bar, 0), c0, c1, pol);
+        else tma_load_2d(dst, tm, bar, c0, c1, pol);
+      };
       auto load_a = [&](uint32_t dst, uint32_t bar, int k0, int m0) {
         if constexpr (A_MN) {
 #pragma unroll
           for (int j = 0; j < GEMM_BM / 64; ++j)
-            tma_load_2d(dst + j * MN_BOX, &tmA, bar, m0 + 64 * j, k0, pol_a);
+            tma_ld(dst + j * MN_BOX, &tmA, bar, m0 + 64 * j, k0, pol_a);
         } else {
-          tma_load_2d(dst, &tmA, bar, k0, m0, pol_a);
+          tma_ld(dst, &tmA, bar, k0, m0, pol_a);
         }
       };
       auto load_b = [&](uint32_t dst, uint32_t bar, int k0, int n0) {
         if constexpr (B_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(dst + j * MN_BOX, &tmB, bar, n0 + 64 * j, k0, pol_b);
+          for (int j = 0; j < BN / CG / 64; ++j)
+            tma_ld(dst + j * MN_BOX, &tmB, bar, n0 + 64 * j, k0, pol_b);
         } else {
-          tma_load_2d(dst, &tmB, bar, k0, n0, pol_b);
+          tma_ld(dst, &tmB, bar, k0, n0, pol_b);
         }
       };
+      const bool arms = !PAIR || crank == 0;
+      const int a_row0 = (int)crank * GEMM_BM;          // this CTA's rows of the unit
+      const int b_row0 = (int)crank * (BN / CG);
       // Prologue overlap: the first stages' A tiles of this CTA's first unit
       // (weights that no preceding kernel writes) are requested before the
       // programmatic-dependency wait; their B tiles follow after it.
       int pre = 0;
-      if (sh.prefetch_a && (int)blockIdx.x < units) {
-        const int u = blockIdx.x;
+      if (sh.prefetch_a && u_first < units) {
+        const int u = u_first;
         const int mt = u % sh.m_tiles;
         const int kb0 = (u / sh.m_tiles / sh.n_tiles) * sh.kb_per_split;
         pre = sh.kb_per_split < STAGES ? sh.kb_per_split : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
-          mbar_arrive_expect_tx(full_bar + 8 * kb, C::STAGE_BYTES);
-          load_a(tiles + kb * C::STAGE_BYTES, full_bar + 8 * kb, (kb0 + kb) * GEMM_BK, mt * GEMM_BM);
+          if (arms) mbar_arrive_expect_tx(full_bar + 8 * kb, CG * C::STAGE_BYTES);
+          load_a(tiles + kb * C::STAGE_BYTES, full_bar + 8 * kb, (kb0 + kb) * GEMM_BK,
+                 mt * TILE_M + a_row0);
         }
       }
       pdl_wait();
@@ -617,7 +645,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       bool ok = true;
       bool first = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int u = u_first; u < units && ok; u += u_step) {
         const int mt = u % sh.m_tiles;
         const int rest = u / sh.m_tiles;
         const int nt = rest % sh.n_tiles;
@@ -630,10 +658,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(full_bar + 8 * stage, C::STAGE_BYTES);
-            load_a(sa, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * GEMM_BM);
+            if (arms) mbar_arrive_expect_tx(full_bar + 8 * stage, CG * C::STAGE_BYTES);
+            load_a(sa, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, mt * TILE_M + a_row0);
           }
-          load_b(sa + C::A_BYTES, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN);
+          load_b(sa + C::A_BYTES, full_bar + 8 * stage, (kb0 + kb) * GEMM_BK, nt * BN + b_row0);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         first = false;
@@ -642,23 +670,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // stage has landed, so no TMA write is in flight when the CTA exits.
       // Stages below `stage` were last filled in the current lap (parity
       // `phase`), the others in the previous lap (or never: parity 1 on a
-      // fresh barrier reads as complete).
-      for (int s = 0; s < STAGES; ++s) {
-        const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(full_bar + 8 * s, par)) {
-          if (globaltimer_ns() - t0 > 100000000ull) break;
+      // fresh barrier reads as complete).  In pair mode only the even CTA's
+      // barriers count the loads (of both CTAs); the odd CTA relies on it and
+      // on the closing cluster barrier.
+      if (arms) {
+        for (int s = 0; s < STAGES; ++s) {
+          const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar + 8 * s, par)) {
+            if (globaltimer_ns() - t0 > 100000000ull) break;
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || crank == 0)) {   // pair mode: the even CTA issues for both
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      for (int u = u_first; u < units; u += u_step) {
         if (!mbar_wait(tempty_bar + 8 * acc, acc_phase ^ 1u, sh.status, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -676,16 +708,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           constexpr uint64_t B_STEP = B_MN ? 128 : 2;
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k)
-            umma_f16(d_tmem, adesc + A_STEP * k, bdesc + B_STEP * k, IDESC, (kb | k) != 0);
-          umma_commit(empty_bar + 8 * stage);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, adesc + A_STEP * k, bdesc + B_STEP * k, IDESC, (kb | k) != 0);
+            else
+              umma_f16(d_tmem, adesc + A_STEP * k, bdesc + B_STEP * k, IDESC, (kb | k) != 0);
+          // the stage is free again in both CTAs of a pair
+          if constexpr (PAIR) umma_commit_pair(empty_bar + 8 * stage, 0x3);
+          else umma_commit(empty_bar + 8 * stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit(tfull_bar + 8 * acc);
+        if constexpr (PAIR) umma_commit_pair(tfull_bar + 8 * acc, 0x3);   // both epilogues
+        else umma_commit(tfull_bar + 8 * acc);
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
       // Wait (bounded) for every MMA this thread issued before TMEM is freed.
-      umma_commit(drain_bar);
+      if constexpr (PAIR) umma_commit_pair(drain_bar, 0x1);
+      else umma_commit(drain_bar);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(drain_bar, 0)) {
         if (globaltimer_ns() - t0 > 100000000ull) break;
@@ -703,7 +742,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int row0 = (int)crank * GEMM_BM;   // this CTA's rows within a unit
+    for (int u = u_first; u < units; u += u_step) {
       const int mt = u % sh.m_tiles;
       const int rest = u / sh.m_tiles;
       const int nt = rest % sh.n_tiles;
@@ -713,12 +753,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // ahead), then the next unit's, so they are L2-resident by the time
         // the epilogue (which, when it reads inputs, is usually the slower
         // side of the pipeline) reaches them
-        if (u == (int)blockIdx.x && chunk0 == 0)
-          Epi::prefetch(ep, mt * GEMM_BM + row_in_tile, nt * BN, BN, sh.M, sh.N);
-        const int un = u + gridDim.x;
+        if (u == u_first && chunk0 == 0)
+          Epi::prefetch(ep, mt * TILE_M + row0 + row_in_tile, nt * BN, BN, sh.M, sh.N);
+        const int un = u + u_step;
         if (un < units && chunk0 == 0) {
           const int rn = un / sh.m_tiles;
-          Epi::prefetch(ep, (un % sh.m_tiles) * GEMM_BM + row_in_tile, (rn % sh.n_tiles) * BN, BN,
+          Epi::prefetch(ep, (un % sh.m_tiles) * TILE_M + row0 + row_in_tile, (rn % sh.n_tiles) * BN, BN,
                         sh.M, sh.N);
         }
       }
@@ -727,7 +767,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const int m = mt * GEMM_BM + row_in_tile;
+      const int m = mt * TILE_M + row0 + row_in_tile;
 #pragma unroll 1
       for (int c = chunk0; c < BN; c += 2 * CH) {
         float v[CH];
@@ -809,7 +849,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            const int y = mt * GEMM_BM + quarter * 32;
+            const int y = mt * TILE_M + row0 + quarter * 32;
             if constexpr (EpiTransposed<Epi>::value) {
               // output [N (batch), M (features)]: x = feature, y = batch row
               if (y < sh.M && n0 < sh.N) tma_reduce_add_2d(&tmC, sbuf, y, n0);
@@ -829,7 +869,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       tc_fence_before();
-      mbar_arrive(tempty_bar + 8 * acc);
+      if constexpr (PAIR) {
+        // one arrival per warp, on the even CTA's barrier (the MMA issuer's)
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * acc, 0));
+      } else {
+        mbar_arrive(tempty_bar + 8 * acc);
+      }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
     if constexpr (STG != 0) {
@@ -839,8 +885,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   tc_fence_before();
   __syncthreads();
+  // pair mode: neither CTA leaves (or frees its TMEM) while the other may
+  // still signal its barriers or the pair's MMAs may read its tiles
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
 }
 
 }  // namespace ne

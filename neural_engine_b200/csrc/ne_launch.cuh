@@ -33,4 +33,26 @@ cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// The same with thread-block clusters of `cluster_x` CTAs along x (the grid's x
+// extent must be a multiple of it).
+template <class Kern, class... Args>
+cudaError_t launch_k_cluster(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 }  // namespace ne

@@ -89,6 +89,49 @@ def test_gemm_residual_epilogue(eng):
     assert err <= _tol(a, b, K), err
 
 
+@pytest.mark.parametrize("M,N,K,mn", [(600, 300, 320, 0), (1300, 520, 256, 0), (4096, 1024, 1024, 0),
+                                      (600, 296, 320, 1), (1024, 768, 512, 2)])
+@pytest.mark.parametrize("epi", [1, 2, 3])
+def test_gemm_cta_pair_tiles(eng, M, N, K, mn, epi):
+    """M >= 512 with 256-wide tiles runs on CTA pairs (cta_group::2: one MMA
+    over two SMs, each CTA holding half of A's and half of B's rows): ragged M
+    and N (the odd CTA's rows or B-half past the end), K-major and MN-major
+    operands (mn 1: B MN-major, 2: both), fp32 / bf16 / residual outputs."""
+    if mn == 2:
+        at, bt = _bf16((K, M), 41, 0.1), _bf16((K, N), 42, 0.1)
+        a, b = at.T, bt.T
+        da, db = at.cuda(), bt.cuda()
+        lda, ldb, a_mn, b_mn = M, N, 1, 1
+    elif mn == 1:
+        a, bt = _bf16((M, K), 41), _bf16((K, N), 42, 0.1)
+        b = bt.T
+        da, db = a.cuda(), bt.cuda()
+        lda, ldb, a_mn, b_mn = K, N, 0, 1
+    else:
+        a, b = _bf16((M, K), 41), _bf16((N, K), 42, 0.1)
+        da, db = a.cuda(), b.cuda()
+        lda, ldb, a_mn, b_mn = K, K, 0, 0
+    if mn == 2 and epi != 3:
+        pytest.skip("MN/MN products accumulate (dW)")
+    x0 = torch.randn(M, N)
+    if epi == 2:
+        out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    elif epi == 3:
+        out = x0.clone().cuda()
+    else:
+        out = torch.full((M, N), float("nan"), device="cuda")
+    eng.gemm(da.data_ptr(), lda, M, db.data_ptr(), ldb, N, K, epi, out.data_ptr(), N,
+             alpha=0.5 if epi == 3 else 1.0, a_mn=a_mn, b_mn=b_mn, bn=256)
+    eng.sync()
+    ref = a.double() @ b.double().T
+    if epi == 3:
+        ref = x0.double() + 0.5 * ref
+    got = out.cpu().double()
+    tol = _tol(a, b, K) + (float(ref.abs().max()) * 2 ** -8 if epi == 2 else 0.0)
+    err = (got - ref).abs().max().item()
+    assert err <= tol, (err, tol)
+
+
 def test_gemm_swiglu_epilogue(eng):
     """B = [W1/W3 interleaved in 16-row blocks]; out[m, j] = silu(h1_j) * h3_j."""
     M, F, K = 200, 256, 128
