@@ -152,13 +152,13 @@ class ClockSampler:
 def decode_step_bytes(B: int, T: int) -> float:
     """Algorithmic HBM bytes of one decode step for B sequences at context T:
     bf16 weights once (tied LM head reads the whole embedding) plus per
-    sequence: K and V of T positions x 28 layers x 8 heads x 128 (fp16), the
-    new K/V row written, and the fp32 logits written."""
+    sequence: K and V of T positions x 28 layers x 8 heads x 128 (fp16) and
+    the new K/V row written.  The greedy loop's LM head keeps only each row's
+    best (logit, id), so no logits reach HBM and none are counted."""
     weights = 2.0 * PARAMS
     kv_read = L * 2 * HKV * HD * 2 * T
     kv_write = L * 2 * HKV * HD * 2
-    logits = V * 4
-    return weights + B * (kv_read + kv_write + logits)
+    return weights + B * (kv_read + kv_write)
 
 
 def attention_bytes(B: int, T: int) -> float:

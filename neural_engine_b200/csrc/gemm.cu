@@ -139,6 +139,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         return launch_t<BN, EpiF32TS, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
+    case EPI_ARGMAX_T:
+      if constexpr (kk && tr_ok && ch32) {
+        EpiArgmaxT::Params p{(unsigned long long*)c.aux1};
+        return launch_t<BN, EpiArgmaxT, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
+      }
+      break;
     case EPI_F32: {
       if constexpr (ch32) {
         if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
@@ -228,7 +234,8 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
 
 int pick_bn(const GemmCall& c) {
   if (c.bn) return c.bn;
-  if (c.N <= 16) return (c.epi == EPI_SWIGLU || c.epi == EPI_F32T_ADD) ? 32 : 16;
+  if (c.N <= 16)
+    return (c.epi == EPI_SWIGLU || c.epi == EPI_F32T_ADD || c.epi == EPI_ARGMAX_T) ? 32 : 16;
   if (c.N <= 32) return 32;
   if (c.N <= 64) return 64;
   if (c.N <= 128) return 128;
@@ -301,6 +308,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     return cudaErrorInvalidValue;
   if (c.epi == EPI_SWIGLU_BWD && (!a16(c.out) || !a16(c.aux3) || c.aux_ld % 8))
     return cudaErrorInvalidValue;
+  if (c.epi == EPI_ARGMAX_T && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u)))
+    return cudaErrorInvalidValue;
   if (c.epi == EPI_F32_STATS && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u) ||
                                  c.aux_ld < (c.N + 31) / 32))
     return cudaErrorInvalidValue;
@@ -321,7 +330,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     return !(e && e[0] == '0');
   }();
   const bool pair = pair_on && bn == 256 && c.max_ctas <= 0 && c.M >= 512 &&
-                    c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && num_sms >= 2;
+                    c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T &&
+                    num_sms >= 2;
   const int tile_m = pair ? 2 * GEMM_BM : GEMM_BM;
 
   CUtensorMap ta, tb;

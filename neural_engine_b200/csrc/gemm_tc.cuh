@@ -107,6 +107,43 @@ struct EpiF32T {
   }
 };
 
+// Swap-AB LM head fused with the greedy choice (A = the tied embedding, row m
+// = token id; B = the batch): instead of storing logits[n][m], every
+// (token id, batch row) value becomes a 64-bit key whose order is that of the
+// logit, ties broken towards the smaller id (numpy's first-index argmax), and
+// the key of each batch row's best id is kept with one atomicMax per column
+// per warp.  A warp's 32 rows x 32 columns are first reduced with a
+// transposing butterfly (31 exchanges) so lane j ends with column j's best.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int m) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);   // order-preserving
+  return ((unsigned long long)o << 32) | (uint32_t)~(uint32_t)m;
+}
+struct EpiArgmaxT {
+  struct Params { unsigned long long* keys; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int, int M,
+                               int N) {
+    static_assert(CH == 32, "one column per lane");
+    const int lane = threadIdx.x & 31;
+    unsigned long long k[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) k[j] = m < M ? argmax_key(v[j], m) : 0ull;
+#pragma unroll
+    for (int o = 16, cnt = 32; o >= 1; o >>= 1, cnt >>= 1) {
+      const bool up = (lane & o) != 0;   // keeps the upper half of its columns
+#pragma unroll
+      for (int i = 0; i < cnt / 2; ++i) {
+        const unsigned long long send = up ? k[i] : k[i + cnt / 2];
+        const unsigned long long keep = up ? k[i + cnt / 2] : k[i];
+        const unsigned long long recv = __shfl_xor_sync(0xffffffffu, send, o);
+        k[i] = keep > recv ? keep : recv;
+      }
+    }
+    if (n0 + lane < N && k[0] != 0ull) atomicMax(p.keys + n0 + lane, k[0]);
+  }
+};
+
 // fp32 store, row-major:  out[split*split_stride + m*ld + n]
 struct EpiF32 {
   struct Params { float* out; long long ld; long long split_stride; };

@@ -439,6 +439,30 @@ cudaError_t launch_swiglu_split(float* P, int nsplit, long long split_stride, in
                   nsplit, split_stride, rows, F, gate, zero_src);
 }
 
+__global__ void argmax_keys_kernel(unsigned long long* keys, int rows, int32_t* next_tok,
+                                   int32_t* out_tokens, int* d_state) {
+  pdl_trigger();
+  pdl_wait();
+  const int step = d_state[1];
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const int32_t id = (int32_t)~(uint32_t)(keys[r] & 0xffffffffull);
+    next_tok[r] = id;
+    if (out_tokens) out_tokens[(size_t)step * rows + r] = id;
+    keys[r] = 0ull;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    d_state[0] += 1;
+    d_state[1] += 1;
+  }
+}
+
+cudaError_t launch_argmax_keys(unsigned long long* keys, int rows, int32_t* next_tok,
+                               int32_t* out_tokens, int* d_state, cudaStream_t st) {
+  return launch_k(argmax_keys_kernel, dim3(1), dim3(256), 0, st, keys, rows, next_tok, out_tokens,
+                  d_state);
+}
+
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
                           int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st) {
   cudaError_t e = launch_k(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, logits, V, next_tok,

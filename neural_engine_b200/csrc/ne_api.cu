@@ -59,6 +59,21 @@ ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
   return NE_OK;
 }
 
+// The greedy LM head: act . E^T reduced on the fly to each row's best
+// (logit, id) key in ctx->argmax_keys (launch_argmax_keys finishes the step).
+ne_status gemm_lm_head_argmax(ne_ctx* ctx, const __nv_bfloat16* act, long long ld_act, int rows) {
+  GemmCall c;
+  c.A = ctx->embed; c.lda = ctx->cfg.dim; c.M = ctx->cfg.vocab;
+  c.B = act; c.ldb = ld_act; c.N = rows;
+  c.K = ctx->cfg.dim;
+  c.epi = EPI_ARGMAX_T;
+  c.aux1 = ctx->argmax_keys;
+  c.splits = 1;
+  c.prefetch_a = 1;
+  NE_LAUNCH(gemm_run(c, ctx->d_status, ctx->st));
+  return NE_OK;
+}
+
 // The tied LM head: out[rows][V] = act . E^T (plain transposed store; the
 // vocabulary gives enough tiles without splitting K).
 ne_status gemm_lm_head(ne_ctx* ctx, const __nv_bfloat16* act, long long ld_act, int rows,
@@ -112,7 +127,7 @@ bool ready(ne_ctx* ctx) { return ctx->global_set && ctx->layer_set_count == (uns
 
 // ------------------------------------------------------------------ decode step
 // Enqueue one step for B sequences.  Token input: ctx->tok; position: state[0].
-ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
+ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool keep_logits) {
   const ne_model_cfg& m = ctx->cfg;
   const int D = m.dim, F = m.hidden, Hq = m.n_heads, Hkv = m.kv_heads, hd = m.head_dim;
   const int qkv_dim = ctx->qkv_dim(), q_dim = ctx->q_dim();
@@ -158,16 +173,26 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens) {
                                    ctx->st));
     prof_mark(ctx, 4);
   }
-  if ((s = gemm_lm_head(ctx, ctx->xn, D, B, ctx->logits)) != NE_OK) return s;
-  prof_mark(ctx, 8);
-  NE_LAUNCH(launch_argmax(ctx->logits, B, m.vocab, ctx->tok, d_out_tokens, ctx->state, 1, ctx->st));
-  ctx->launches++;  // state advance kernel
+  if (keep_logits) {
+    if ((s = gemm_lm_head(ctx, ctx->xn, D, B, ctx->logits)) != NE_OK) return s;
+    prof_mark(ctx, 8);
+    NE_LAUNCH(launch_argmax(ctx->logits, B, m.vocab, ctx->tok, d_out_tokens, ctx->state, 1,
+                            ctx->st));
+    ctx->launches++;  // state advance kernel
+  } else {
+    // greedy: the LM head keeps only each row's best (logit, id); no logits in HBM
+    if ((s = gemm_lm_head_argmax(ctx, ctx->xn, D, B)) != NE_OK) return s;
+    prof_mark(ctx, 8);
+    NE_LAUNCH(launch_argmax_keys(ctx->argmax_keys, B, ctx->tok, d_out_tokens, ctx->state,
+                                 ctx->st));
+  }
   prof_mark(ctx, 9);
   return NE_OK;
 }
 
-ne_status get_graph(ne_ctx* ctx, int B, DecodeGraph** out) {
-  auto it = ctx->graphs.find(B);
+ne_status get_graph(ne_ctx* ctx, int B, bool keep_logits, DecodeGraph** out) {
+  const int key = 2 * B + (keep_logits ? 1 : 0);
+  auto it = ctx->graphs.find(key);
   if (it != ctx->graphs.end()) {
     *out = &it->second;
     return NE_OK;
@@ -175,7 +200,7 @@ ne_status get_graph(ne_ctx* ctx, int B, DecodeGraph** out) {
   DecodeGraph g;
   ctx->launches = 0;
   NE_CUDA(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
-  ne_status s = enqueue_decode_step(ctx, B, ctx->out_tokens);
+  ne_status s = enqueue_decode_step(ctx, B, ctx->out_tokens, keep_logits);
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(ctx->st, &graph);
   if (s != NE_OK) {
@@ -191,8 +216,8 @@ ne_status get_graph(ne_ctx* ctx, int B, DecodeGraph** out) {
   }
   g.graph = graph;
   g.kernels = ctx->launches;
-  ctx->graphs[B] = g;
-  *out = &ctx->graphs[B];
+  ctx->graphs[key] = g;
+  *out = &ctx->graphs[key];
   return NE_OK;
 }
 
@@ -261,7 +286,7 @@ ne_status free_workspace(ne_ctx* ctx) {
   ctx->prof_events.clear();
   void* ptrs[] = {ctx->kcache, ctx->vcache, ctx->rope_cs, ctx->x, ctx->xn, ctx->part, ctx->q,
                   ctx->attn, ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->gate, ctx->logits,
-                  ctx->tok,
+                  ctx->argmax_keys, ctx->tok,
                   ctx->state, ctx->out_tokens, ctx->pf_x, ctx->pf_xn, ctx->pf_qkv, ctx->pf_q,
                   ctx->pf_o, ctx->pf_gate, ctx->pf_tok};
   for (void* p : ptrs)
@@ -270,6 +295,7 @@ ne_status free_workspace(ne_ctx* ctx) {
   ctx->rope_cs = nullptr;
   ctx->x = nullptr; ctx->xn = nullptr; ctx->part = nullptr; ctx->q = nullptr;
   ctx->attn = nullptr; ctx->attn_po = nullptr; ctx->attn_ml = nullptr; ctx->attn_cnt = nullptr;
+  ctx->argmax_keys = nullptr;
   ctx->gate = nullptr;
   ctx->logits = nullptr; ctx->tok = nullptr; ctx->state = nullptr; ctx->out_tokens = nullptr;
   ctx->pf_x = nullptr; ctx->pf_xn = nullptr; ctx->pf_qkv = nullptr; ctx->pf_q = nullptr;
@@ -501,6 +527,7 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
       (s = dalloc(ctx, &ctx->attn_po, attn_slots * group * hd)) ||
       (s = dalloc(ctx, &ctx->attn_ml, attn_slots * group * 2)) ||
       (s = dalloc(ctx, &ctx->attn_cnt, B * m.kv_heads)) ||
+      (s = dalloc(ctx, &ctx->argmax_keys, B)) ||
       (s = dalloc(ctx, &ctx->gate, B * F)) || (s = dalloc(ctx, &ctx->logits, B * m.vocab)) ||
       (s = dalloc(ctx, &ctx->tok, B)) || (s = dalloc(ctx, &ctx->state, 2)) ||
       (s = dalloc(ctx, &ctx->out_tokens, (size_t)max_seq * B)))
@@ -518,6 +545,7 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
   NE_CUDA(cudaMemset(ctx->state, 0, 2 * sizeof(int)));
   NE_CUDA(cudaMemset(ctx->part, 0, part * sizeof(float)));
   NE_CUDA(cudaMemset(ctx->attn_cnt, 0, B * m.kv_heads * sizeof(int)));
+  NE_CUDA(cudaMemset(ctx->argmax_keys, 0, B * sizeof(unsigned long long)));
   return NE_OK;
 }
 
@@ -552,15 +580,25 @@ NE_API ne_status ne_prefill(ne_ctx* ctx, const int32_t* h_tokens, int B, int S, 
   return ne_sync(ctx);
 }
 
+// The graph-replayed token loop; keep_logits leaves the last step's logits in
+// ctx->logits (the sampling path), otherwise the greedy LM head runs fused.
+ne_status decode_loop(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0, int n_steps,
+                      int32_t* d_out, bool keep_logits);
+
 NE_API ne_status ne_decode_loop_device(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0,
                                        int n_steps, int32_t* d_out) {
+  return decode_loop(ctx, d_tok, B, pos0, n_steps, d_out, false);
+}
+
+ne_status decode_loop(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0, int n_steps,
+                      int32_t* d_out, bool keep_logits) {
   if (!ctx || !d_tok || B <= 0 || n_steps < 0 || pos0 < 0) return NE_ERR_INVALID;
   if (!ready(ctx)) return fail(ctx, NE_ERR_STATE, "weights not set");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B > ctx->max_batch || pos0 + n_steps > ctx->max_seq)
     return fail(ctx, NE_ERR_INVALID, "batch or positions exceed the allocated KV cache");
   DecodeGraph* g = nullptr;
-  ne_status s = get_graph(ctx, B, &g);
+  ne_status s = get_graph(ctx, B, keep_logits, &g);
   if (s != NE_OK) return s;
   const int st0[2] = {pos0, 0};
   if (d_tok != ctx->tok)
@@ -642,7 +680,7 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
   ctx->prof_on = true;
   ctx->prof_n = 0;
   ctx->launches = 0;
-  ne_status s = enqueue_decode_step(ctx, B, nullptr);
+  ne_status s = enqueue_decode_step(ctx, B, nullptr, false);
   ctx->prof_on = false;
   if (s != NE_OK) return s;
   NE_CUDA(cudaStreamSynchronize(ctx->st));
@@ -679,7 +717,7 @@ NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
 
 NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B) {
   if (!ctx) return 0;
-  auto it = ctx->graphs.find(B);
+  auto it = ctx->graphs.find(2 * B);   // the greedy loop's graph
   return it == ctx->graphs.end() ? 0 : it->second.kernels;
 }
 
@@ -692,7 +730,7 @@ NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int po
   NE_CUDA(cudaSetDevice(ctx->device));
   NE_CUDA(cudaMemcpyAsync(ctx->tok, h_tok, (size_t)B * sizeof(int32_t), cudaMemcpyHostToDevice,
                           ctx->st));
-  ne_status s = ne_decode_loop_device(ctx, ctx->tok, B, pos, 1, nullptr);
+  ne_status s = decode_loop(ctx, ctx->tok, B, pos, 1, nullptr, h_logits != nullptr);
   if (s != NE_OK) return s;
   if (h_next)
     NE_CUDA(cudaMemcpyAsync(h_next, ctx->tok, (size_t)B * sizeof(int32_t), cudaMemcpyDeviceToHost,
@@ -720,7 +758,7 @@ NE_API ne_status ne_generate(ne_ctx* ctx, const int32_t* h_prompt, int B, int P,
                           cudaMemcpyDeviceToDevice, ctx->st));
   if (n_new > 1) {
     DecodeGraph* g = nullptr;
-    if ((s = get_graph(ctx, B, &g)) != NE_OK) return s;
+    if ((s = get_graph(ctx, B, false, &g)) != NE_OK) return s;
     const int st0[2] = {P, 1};
     NE_CUDA(cudaMemcpyAsync(ctx->state, st0, sizeof(st0), cudaMemcpyHostToDevice, ctx->st));
     for (int i = 1; i < n_new; ++i) NE_CUDA(cudaGraphLaunch(g->exec, ctx->st));

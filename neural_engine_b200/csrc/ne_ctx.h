@@ -78,6 +78,7 @@ struct ne_ctx {
   float* attn_po = nullptr;      // [segment slots][group][hd]  (decode attention partials)
   float* attn_ml = nullptr;      // [segment slots][group][2]
   int* attn_cnt = nullptr;       // [maxB * Hkv] segment tickets per (sequence, kv-head)
+  unsigned long long* argmax_keys = nullptr;   // [maxB] greedy LM head: best (logit, id) keys
   __nv_bfloat16* gate = nullptr; // [maxB, F]
   float* logits = nullptr;       // [maxB, V]
   int32_t* tok = nullptr;        // [maxB]
@@ -93,7 +94,7 @@ struct ne_ctx {
   __nv_bfloat16* pf_gate = nullptr;
   int32_t* pf_tok = nullptr;
 
-  std::map<int, ne::DecodeGraph> graphs;
+  std::map<int, ne::DecodeGraph> graphs;   // key: 2 * batch + (logits kept)
 
   // instrumented-step profiling (ne_profile_decode_step)
   bool prof_on = false;

@@ -18,6 +18,7 @@ enum GemmEpi : int {
   EPI_SWIGLU_BWD = 6,  // bf16 dh1/dh3 (interleaved) from d_gate and the saved h13 (aux3)
   EPI_F32_STATS = 7,   // fp32 row-major + per-32-column (max, sum exp) into aux1 [m][aux_ld]
   EPI_F32T_ADD = 8,    // swap-AB: out[n][m] += alpha * acc through the TMA add (split-K safe)
+  EPI_ARGMAX_T = 9,    // swap-AB: atomicMax of (logit, ~m) keys into aux1 [N] (greedy LM head)
 };
 
 struct GemmCall {
@@ -73,6 +74,10 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
 // next projection's TMA add)
 cudaError_t launch_swiglu_split(float* P, int nsplit, long long split_stride, int rows, int F,
                                 __nv_bfloat16* gate, cudaStream_t st, int zero_src = 0);
+// Turns the keys of EPI_ARGMAX_T into next_tok[r] (and out_tokens[step][r]),
+// clears the keys for the next step and advances [pos, step].
+cudaError_t launch_argmax_keys(unsigned long long* keys, int rows, int32_t* next_tok,
+                               int32_t* out_tokens, int* d_state, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_tok,
                           int32_t* out_tokens, int* d_state, int adv_state, cudaStream_t st);
 // Segment slots (each GROUP x (hd + 2) floats) the decode-attention partial

@@ -152,6 +152,29 @@ def test_generate_greedy_free_running():
     e.close()
 
 
+@pytest.mark.parametrize("B,V", [(5, 512), (130, 1000)])
+def test_fused_greedy_head_equals_logits_argmax(B, V):
+    """The greedy decode loop's LM head keeps only each row's best (logit, id)
+    instead of writing logits: its tokens equal numpy's first-index argmax of
+    the logits the logits-keeping step computes for the same tokens (teacher
+    forced), except where the top two logits are within accumulation noise."""
+    cfg = _tiny_cfg(qk_norm=True, theta=1e6, eps=1e-6, vocab=V)
+    layers, rf, emb, qk = om.init_weights(cfg, seed=43, std=0.1, bf16=True)
+    P, n = 12, 10
+    prompt = om.prompt_tokens(cfg.vocab, P, 44, batch=B)
+    e = _engine(cfg, layers, rf, emb, qk, B, P + n)
+    fused = e.generate_greedy(prompt, n)                      # [B, n]
+    tok, _ = e.prefill(prompt, 0, return_logits=True)
+    assert np.array_equal(tok, fused[:, 0])
+    for i in range(1, n):
+        _, lg = e.decode_step(fused[:, i - 1].astype(np.int32), P + i - 1, return_logits=True)
+        want = np.argmax(lg, -1)
+        top2 = np.sort(lg, -1)[:, -2:]
+        close = (top2[:, 1] - top2[:, 0]) <= 1e-4 * np.maximum(1.0, np.abs(top2[:, 1]))
+        assert np.all((want == fused[:, i]) | close), f"step {i}"
+    e.close()
+
+
 def test_python_generate_mirror():
     """neural_engine_b200.generate.generate has generate.py's signature and
     returns the same greedy tokens as the oracle."""
