@@ -403,8 +403,10 @@ int main(int argc, char** argv) {
   const double per_layer = qd * c.dim + 2 * kvd * c.dim + c.dim * qd + 3.0 * c.hidden * c.dim;
   if (!resuming) {
     if (rank == 0) {
-      std::printf("=== B200 Training: %s (%d layers, GQA %d/%d heads) ===\n", mdl.name.c_str(),
-                  c.n_layers, c.n_heads, c.kv_heads);
+      // train.m:222's banner, word for word: the reference's dashboard reads the
+      // model name and layer count from it (dashboard.py RE_MODEL_NAME)
+      std::printf("=== ANE Dynamic Training: %s (%d layers, GQA %d/%d heads) ===\n",
+                  mdl.name.c_str(), c.n_layers, c.n_heads, c.kv_heads);
       std::printf("dim=%d q_dim=%d kv_dim=%d hd=%d hidden=%d seq=%d vocab=%d batch=%d\n", c.dim,
                   (int)qd, (int)kvd, c.head_dim, c.hidden, S, c.vocab, B);
       const double xf = c.n_layers * (per_layer + 2.0 * c.dim) / 1e6;

@@ -70,6 +70,17 @@ def test_cli_training_run_matches_the_binding_driven_loop(tmp_path):
              for m in re.finditer(r"step\s+(\d+)\s+loss=([\d.]+)", r.stdout)]
     assert steps and steps[0][0] == 0
     assert "[ckpt saved, best_loss=" in r.stdout
+    # the lines the reference's dashboard parses (training/dashboard.py:338-357)
+    for pat in (r"ANE Dynamic Training: (.+?) \((\d+) layers",
+                r"dim=(\d+) q_dim=(\d+) kv_dim=(\d+) hd=(\d+) hidden=(\d+) seq=(\d+) vocab=(\d+)",
+                r"Params: ([\d.]+)M \(transformer ([\d.]+)M \+ embed ([\d.]+)M\)",
+                r"Accum (\d+).*LR=([\d.e+-]+)",
+                r"step\s+(\d+)\s+loss=([\d.]+)(?:\s+lr=([\d.e+-]+))?(?:\s+([\d.]+)ms/step)?",
+                r"\[ckpt saved, best_loss=([\d.]+)\]"):
+        assert re.search(pat, r.stdout), pat
+    m = re.search(r"step\s+(\d+)\s+loss=([\d.]+)(?:\s+lr=([\d.e+-]+))?(?:\s+([\d.]+)ms/step)?",
+                  r.stdout)
+    assert m.group(3) is not None and m.group(4) is not None   # lr and ms/step parsed too
     ref, losses = _replay(data, 6, 2, 2e-3, 2)
     assert abs(steps[0][1] - losses[0]) <= 1e-4
     got = ckpt_v4.read_v4(ck)
