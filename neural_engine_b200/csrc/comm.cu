@@ -72,6 +72,7 @@ ne_status nccl_fail(ne_ctx* ctx, ncclResult_t r, const char* what) {
 
 void comm_free(ne_ctx* ctx) {
   if (!ctx || !ctx->comm) return;
+  train_drop_step_graph(ctx);
   Comm* c = ctx->comm;
   if (c->cs) cudaStreamSynchronize(c->cs);
   if (c->comm && nccl().loaded) nccl().CommDestroy(reinterpret_cast<ncclComm_t>(c->comm));
@@ -141,6 +142,7 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) 
   NcclApi& api = nccl();
   if (!api.loaded) return fail(ctx, NE_ERR_UNSUPPORTED, api.error);
   NE_CUDA(cudaSetDevice(ctx->device));
+  train_drop_step_graph(ctx);
   comm_free(ctx);
   Comm* c = new Comm();
   ctx->comm = c;
@@ -162,6 +164,7 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) 
 
 NE_API ne_status ne_comm_set_reduce(ne_ctx* ctx, int on) {
   if (!ctx || !ctx->comm) return NE_ERR_STATE;
+  if (ctx->comm->reduce != (on != 0)) train_drop_step_graph(ctx);   // captured with the other mode
   ctx->comm->reduce = on != 0;
   return NE_OK;
 }

@@ -329,7 +329,7 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     const char* e = getenv("NE_GEMM_PAIR");
     return !(e && e[0] == '0');
   }();
-  const bool pair = pair_on && bn == 256 && c.max_ctas <= 0 && c.M >= 512 &&
+  const bool pair = pair_on && bn == 256 && (c.max_ctas <= 0 || c.max_ctas >= 2) && c.M >= 512 &&
                     c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T &&
                     num_sms >= 2;
   const int tile_m = pair ? 2 * GEMM_BM : GEMM_BM;
@@ -354,7 +354,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   sh.prefetch_a = c.prefetch_a;
   const long long units = (long long)sh.m_tiles * sh.n_tiles * splits;
   if (pair) {
-    const long long clusters = units < num_sms / 2 ? units : num_sms / 2;
+    const int cap2 = (c.max_ctas > 0 ? c.max_ctas : num_sms) / 2;
+    const long long clusters = units < cap2 ? units : cap2;
     const int grid2 = (int)(2 * clusters);
     if (!c.a_mn && !c.b_mn) return launch_epi<256, 1, 0, 0, 2>(c, ta, tb, sh, grid2, st);
     if (!c.a_mn) return launch_epi<256, 1, 0, 1, 2>(c, ta, tb, sh, grid2, st);

@@ -404,8 +404,8 @@ NE_API void ne_free(ne_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->st);
+  free_train(ctx);   // first: a captured training step may hold NCCL calls of the communicator
   comm_free(ctx);
-  free_train(ctx);
   free_workspace(ctx);
   if (ctx->wpool) cudaFree(ctx->wpool);
   if (ctx->d_status) cudaFree(ctx->d_status);

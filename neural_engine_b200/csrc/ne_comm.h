@@ -20,6 +20,7 @@ struct Comm {
 };
 
 void comm_free(ne_ctx* ctx);
+void train_drop_step_graph(ne_ctx* ctx);   // ne_train.cu: before the communicator changes
 ne_status comm_fence_in(ne_ctx* ctx);    // comm stream waits for the compute stream
 ne_status comm_fence_out(ne_ctx* ctx);   // compute stream waits for the comm stream
 ne_status comm_allreduce(ne_ctx* ctx, float* buf, size_t n);

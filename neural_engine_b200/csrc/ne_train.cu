@@ -104,6 +104,15 @@ struct TrainState {
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
 };
 
+// Drops the captured training step (it may hold NCCL calls of a communicator
+// about to change, or the exchange may have been switched on or off).
+void train_drop_step_graph(ne_ctx* ctx) {
+  if (!ctx || !ctx->train || !ctx->train->step_graph) return;
+  cudaStreamSynchronize(ctx->st);
+  cudaGraphExecDestroy(ctx->train->step_graph);
+  ctx->train->step_graph = nullptr;
+}
+
 void free_train(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return;
   TrainState* t = ctx->train;
@@ -182,8 +191,22 @@ int dw_splits(const GemmCall& c, int sms) {
   return best;
 }
 
+// With data-parallel reduction on, the GEMMs leave NE_COMM_SMS SMs (default
+// 0) to the NCCL kernels of the gradient buckets, which otherwise find every
+// SM held by a persistent GEMM and run only between launches.
+int comm_reserved_sms() {
+  static const int r = [] {
+    const char* e = std::getenv("NE_COMM_SMS");
+    const int v = e ? std::atoi(e) : 0;
+    return v < 0 ? 0 : (v > 64 ? 64 : v);
+  }();
+  return r;
+}
+
 ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
+  if (ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce && comm_reserved_sms() > 0)
+    c.max_ctas = ctx->num_sms - comm_reserved_sms();
   if (c.epi == EPI_RESID && c.a_mn && c.b_mn) {
     c.bn = 256;
     c.splits = dw_splits(c, ctx->num_sms);
@@ -760,14 +783,19 @@ static ne_status step_body(ne_ctx* ctx, float* d_loss) {
 }
 
 // Whether the micro-step runs as a captured graph: on by default (NE_TRAIN_GRAPH=0
-// turns it off); not while gradients are exchanged over NCCL (the comm
-// stream's buckets are issued directly).
+// turns it off).  With gradients exchanged over NCCL the comm stream's
+// buckets are captured into the same graph (the first, eager micro-step has
+// allocated the exchange buffers) unless NE_TRAIN_GRAPH_COMM=0.
 static bool use_step_graph(const ne_ctx* ctx) {
   static const bool on = [] {
     const char* e = std::getenv("NE_TRAIN_GRAPH");
     return !(e && e[0] == '0');
   }();
-  return on && !comm_active(ctx);
+  static const bool with_comm = [] {
+    const char* e = std::getenv("NE_TRAIN_GRAPH_COMM");
+    return !(e && e[0] == '0');
+  }();
+  return on && (with_comm || !comm_active(ctx));
 }
 
 NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {

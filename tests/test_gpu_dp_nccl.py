@@ -47,11 +47,16 @@ def _rank(rank, world, uid, tok, q):
         B = tok.shape[0] // world
         e = _setup(rank, B, tok.shape[1] - 1)
         e.comm_init(uid, rank, world)
-        loss = e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])
+        loss = e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])   # eager first micro-step
         g = e.get_grads()
+        e.zero_grads()
+        # the same micro-step again, now replayed as a captured graph that
+        # holds the NCCL buckets too
+        e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])
+        g2 = e.get_grads()
         norm = e.adamw_step(1, 1e-3, grad_scale=1.0 / world)
         w = e.get_masters()
-        q.put((rank, loss, g, norm, w))
+        q.put((rank, loss, (g, g2), norm, w))
         e.close()
     except Exception as ex:   # report instead of hanging the parent
         q.put((rank, repr(ex), None, None, None))
@@ -95,7 +100,13 @@ def test_bucketed_allreduce_equals_global_batch_gradient():
     ref_norm = e.adamw_step(1, 1e-3)
     ref_w = e.get_masters()
     e.close()
-    g0, g1 = res[0][2], res[1][2]
+    (g0, g0b), (g1, g1b) = res[0][2], res[1][2]
+    # the captured replay reproduces the eager exchange on both ranks
+    for L in range(cfg.n_layers):
+        for k in ref["layers"][L]:
+            assert np.array_equal(g0b["layers"][L][k], g1b["layers"][L][k]), (L, k)
+            assert _rel(g0b["layers"][L][k], g0["layers"][L][k]) <= 1e-5, (L, k)
+    assert _rel(g0b["embed"], g0["embed"]) <= 1e-5
     for L in range(cfg.n_layers):
         for k in ref["layers"][L]:
             # every rank holds the summed gradient: sum of per-half means = 2 x global mean
