@@ -62,6 +62,9 @@ def parse():
                          "(profiling runs)")
     ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
     ap.add_argument("--train-seq", type=int, default=256)
+    ap.add_argument("--dp-mode", choices=("zero1", "allreduce"), default="zero1",
+                    help="training with N > 1: ZeRO-1 (reduce-scatter, sharded AdamW, "
+                         "all-gathered bf16 weights) or all-reduce with replicated AdamW")
     return ap.parse_args()
 
 
@@ -314,6 +317,8 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
         uid = [ne.Engine.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         eng.comm_init(uid[0], rank, world)
+        if args.dp_mode == "zero1":
+            eng.comm_set_sharding(True)
     tstep = [0]
 
     def step():
@@ -373,8 +378,12 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
             "config": {"workload": "qwen3_06b_train", "batch_per_gpu": B, "seq_len": S,
                        "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
                        "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
-                       "parallelism": f"dp{world} (per-layer NCCL all-reduce buckets "
-                                      "overlapped with the backward)"},
+                       "parallelism": (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
+                                       "buckets overlapped with the backward, sharded AdamW, "
+                                       "bf16 weight all-gather)"
+                                       if world > 1 and args.dp_mode == "zero1" else
+                                       f"dp{world} (per-layer NCCL all-reduce buckets "
+                                       "overlapped with the backward)")},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_kind": kind,
                          "flops_per_token": train_flops_per_token(S), "scope": "whole step"},

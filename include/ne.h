@@ -333,6 +333,20 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world);
 NE_API ne_status ne_comm_set_reduce(ne_ctx* ctx, int on);
 /* Sum the whole gradient pool over the ranks now (ordered on the stream). */
 NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx);
+/* ZeRO-1 (on = 1; no counterpart in the single-device reference).  Every
+ * matrix and the embedding are owned in world equal parts: the gradient
+ * buckets reduce-scatter (rank r keeps the sum of part r), the norm adds the
+ * ranks' shares, AdamW updates only the owned parts, and the updated bf16
+ * compute copies are all-gathered; gains stay replicated.  The fp32 masters
+ * and Adam moments of the other parts are then stale until
+ * ne_train_gather_state(ctx, 0), which checkpoints and the state getters
+ * require; gradients read back need ne_train_gather_state(ctx, 1).  Call
+ * ne_train_gather_state(ctx, 0) before turning sharding off. */
+NE_API ne_status ne_comm_set_sharding(ne_ctx* ctx, int on);
+/* Collective (every rank, same order): all-gather the owned parts of the fp32
+ * masters and both moments (which = 0) or of the reduced gradients (which =
+ * 1).  A no-op without sharding. */
+NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which);
 
 /* The contiguous fp32 gradient pool (every trainable tensor's gradient), for
  * data-parallel reduction by the caller (e.g. an NCCL all-reduce on the

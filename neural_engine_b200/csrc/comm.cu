@@ -33,6 +33,10 @@ struct NcclApi {
                             cudaStream_t) = nullptr;
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*ReduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                                ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
@@ -53,10 +57,14 @@ NcclApi& nccl() {
   api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
   api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
   api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+  api.ReduceScatter = reinterpret_cast<decltype(api.ReduceScatter)>(sym("ncclReduceScatter"));
+  api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+  api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
   api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
   api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
   if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.AllGather ||
-      !api.CommDestroy || !api.GetErrorString) {
+      !api.ReduceScatter || !api.GroupStart || !api.GroupEnd || !api.CommDestroy ||
+      !api.GetErrorString) {
     api.error = "libnccl.so.2 lacks a required symbol";
     return api;
   }
@@ -112,6 +120,22 @@ ne_status comm_allreduce(ne_ctx* ctx, float* buf, size_t n) {
   return NE_OK;
 }
 
+// In place: rank r keeps the sum over ranks of buf[r * n_per_rank, +n_per_rank).
+ne_status comm_reduce_scatter(ne_ctx* ctx, float* buf, size_t n_per_rank) {
+  Comm* c = ctx->comm;
+  ncclResult_t r = nccl().ReduceScatter(buf, buf + (size_t)c->rank * n_per_rank, n_per_rank,
+                                        ncclFloat32, ncclSum,
+                                        reinterpret_cast<ncclComm_t>(c->comm), c->cs);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclReduceScatter");
+  return NE_OK;
+}
+
+ne_status comm_group(ne_ctx* ctx, bool start) {
+  ncclResult_t r = start ? nccl().GroupStart() : nccl().GroupEnd();
+  if (r != ncclSuccess) return nccl_fail(ctx, r, start ? "ncclGroupStart" : "ncclGroupEnd");
+  return NE_OK;
+}
+
 ne_status comm_allgather(ne_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank) {
   Comm* c = ctx->comm;
   ncclResult_t r = nccl().AllGather(send, recv, bytes_per_rank, ncclUint8,
@@ -164,8 +188,14 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) 
 
 NE_API ne_status ne_comm_set_reduce(ne_ctx* ctx, int on) {
   if (!ctx || !ctx->comm) return NE_ERR_STATE;
-  if (ctx->comm->reduce != (on != 0)) train_drop_step_graph(ctx);   // captured with the other mode
-  ctx->comm->reduce = on != 0;
+  ctx->comm->reduce = on != 0;   // the training step keeps one captured graph per mode
+  return NE_OK;
+}
+
+NE_API ne_status ne_comm_set_sharding(ne_ctx* ctx, int on) {
+  if (!ctx || !ctx->comm) return NE_ERR_STATE;
+  if (ctx->comm->shard != (on != 0)) train_drop_step_graph(ctx);
+  ctx->comm->shard = on != 0;
   return NE_OK;
 }
 

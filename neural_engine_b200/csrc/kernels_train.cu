@@ -266,7 +266,8 @@ __device__ __forceinline__ double block_sum256_d(double v, double* red) {
 __global__ void __launch_bounds__(256)
 sumsq_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict__ chunks,
                     int nchunks, float* __restrict__ partial, unsigned* __restrict__ ticket,
-                    float grad_scale, float grad_clip, float* __restrict__ norm_out) {
+                    float grad_scale, float grad_clip, float* __restrict__ norm_out,
+                    int partial_only) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[32];
@@ -274,7 +275,7 @@ sumsq_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict
   __shared__ int last;
   const OptChunk c = chunks[blockIdx.x];
   const AdamSeg sg = segs[c.seg];
-  const int n = (int)min((long long)OPT_CHUNK, sg.n - c.off);
+  const int n = c.norm ? c.n : 0;   // chunks outside this rank's share add nothing
   const float* g = sg.g + c.off;
   float acc = 0.f;
   if (c.vec) {
@@ -301,12 +302,26 @@ sumsq_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict
   for (int i = threadIdx.x; i < nchunks; i += 256) s += (double)__ldcg(partial + i);
   s = block_sum256_d(s, redd);
   if (threadIdx.x == 0) {
-    const float norm = (float)(sqrt(s) * (double)grad_scale);
-    float scale = grad_scale;
-    if (grad_clip > 0.f && norm > grad_clip) scale *= grad_clip / norm;
-    norm_out[0] = norm;
-    norm_out[1] = scale;
+    norm_out[2] = (float)s;
+    if (!partial_only) {
+      const float norm = (float)(sqrt(s) * (double)grad_scale);
+      float scale = grad_scale;
+      if (grad_clip > 0.f && norm > grad_clip) scale *= grad_clip / norm;
+      norm_out[0] = norm;
+      norm_out[1] = scale;
+    }
   }
+}
+
+// Norm and clip factor from the rank-summed sum of squares in norm_out[2].
+__global__ void norm_finish_kernel(float* norm_out, float grad_scale, float grad_clip) {
+  pdl_trigger();
+  pdl_wait();
+  const float norm = sqrtf(norm_out[2]) * grad_scale;
+  float scale = grad_scale;
+  if (grad_clip > 0.f && norm > grad_clip) scale *= grad_clip / norm;
+  norm_out[0] = norm;
+  norm_out[1] = scale;
 }
 
 // AdamW over every chunk; the gradient factor is norm_out[1] (written by
@@ -319,7 +334,7 @@ adamw_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict
   pdl_wait();
   const OptChunk c = chunks[blockIdx.x];
   const AdamSeg sg = segs[c.seg];
-  const int n = (int)min((long long)OPT_CHUNK, sg.n - c.off);
+  const int n = c.n;
   const AdamElt a{lr, b1, b2, 1.0f - b1, 1.0f - b2, eps, inv_bc1, inv_bc2, norm_out[1], sg.wd};
   float* w = sg.w + c.off;
   const float* g = sg.g + c.off;
@@ -444,11 +459,16 @@ cudaError_t launch_scatter_add_rows(float* src, const int32_t* idx, int n, int D
 
 cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float* partial, unsigned* ticket, float grad_scale,
-                                float grad_clip, float* norm_out, cudaStream_t st) {
+                                float grad_clip, float* norm_out, cudaStream_t st,
+                                int partial_only) {
   cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(unsigned), st);
   if (e != cudaSuccess) return e;
   return launch_k(sumsq_chunks_kernel, dim3(nchunks), dim3(256), 0, st, segs, chunks, nchunks,
-                  partial, ticket, grad_scale, grad_clip, norm_out);
+                  partial, ticket, grad_scale, grad_clip, norm_out, partial_only);
+}
+
+cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_clip, cudaStream_t st) {
+  return launch_k(norm_finish_kernel, dim3(1), dim3(1), 0, st, norm_out, grad_scale, grad_clip);
 }
 
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,

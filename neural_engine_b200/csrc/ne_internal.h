@@ -119,10 +119,17 @@ struct OptChunk {
   int seg;
   int vec;
   long long off;
+  int n;      // elements in this chunk (<= OPT_CHUNK)
+  int norm;   // 1: counts in this rank's share of the global gradient norm
 };
+// norm_out: [0] pre-clip norm, [1] gradient factor, [2] this rank's sum of
+// squares.  partial_only = 1 stops after [2] (sharded optimizer state: the
+// sums are added over ranks first, then launch_norm_finish fills [0], [1]).
 cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float* partial, unsigned* ticket, float grad_scale,
-                                float grad_clip, float* norm_out, cudaStream_t st);
+                                float grad_clip, float* norm_out, cudaStream_t st,
+                                int partial_only = 0);
+cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_clip, cudaStream_t st);
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
                                 float inv_bc2, const float* norm_out, cudaStream_t st);

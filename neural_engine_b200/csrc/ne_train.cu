@@ -70,7 +70,8 @@ struct TrainState {
   int nchunks = 0;
   float* opt_partial = nullptr;          // [nchunks] per-chunk sums of squares
   unsigned* opt_ticket = nullptr;        // last-block ticket of the norm kernel
-  float* norm_out = nullptr;             // [2] pre-clip norm, gradient factor
+  float* norm_out = nullptr;             // [0] pre-clip norm, [1] gradient factor, [2] sum of squares
+  bool state_gathered = true;            // sharded mode: masters / moments whole on every rank
   float* grad_pool = nullptr;            // start of the gradients inside `pool`
   size_t grad_floats = 0;
   size_t layer_grad_floats = 0;          // one layer's gradients (contiguous, layer order)
@@ -96,8 +97,9 @@ struct TrainState {
   void* embed_scratch = nullptr;         // sort buffers of the embedding backward
   size_t embed_scratch_bytes = 0;
   // the micro-step after the token split, captured once as a CUDA graph
-  cudaGraphExec_t step_graph = nullptr;
-  const void* step_graph_rope = nullptr;  // RoPE table the graph was captured with
+  // captured micro-steps: [1] with the gradient exchange, [0] without
+  cudaGraphExec_t step_graphs[2] = {nullptr, nullptr};
+  const void* step_graph_rope[2] = {nullptr, nullptr};   // RoPE table each was captured with
   long long steps_run = 0;                // micro-steps so far (the first runs eagerly)
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
@@ -105,12 +107,20 @@ struct TrainState {
 };
 
 // Drops the captured training step (it may hold NCCL calls of a communicator
-// about to change, or the exchange may have been switched on or off).
+// about to change, or the exchange may have been switched on or off) and the
+// optimizer work list (whose chunks depend on this rank's share).
 void train_drop_step_graph(ne_ctx* ctx) {
-  if (!ctx || !ctx->train || !ctx->train->step_graph) return;
+  if (!ctx || !ctx->train) return;
+  TrainState* t = ctx->train;
   cudaStreamSynchronize(ctx->st);
-  cudaGraphExecDestroy(ctx->train->step_graph);
-  ctx->train->step_graph = nullptr;
+  for (cudaGraphExec_t& g : t->step_graphs) {
+    if (g) cudaGraphExecDestroy(g);
+    g = nullptr;
+  }
+  if (t->d_chunks) cudaFree(t->d_chunks);
+  if (t->opt_partial) cudaFree(t->opt_partial);
+  t->d_chunks = nullptr;
+  t->opt_partial = nullptr;
 }
 
 void free_train(ne_ctx* ctx) {
@@ -119,7 +129,8 @@ void free_train(ne_ctx* ctx) {
   if (t->d_segs) cudaFree(t->d_segs);
   if (t->d_chunks) cudaFree(t->d_chunks);
   if (t->embed_scratch) cudaFree(t->embed_scratch);
-  if (t->step_graph) cudaGraphExecDestroy(t->step_graph);
+  for (cudaGraphExec_t g : t->step_graphs)
+    if (g) cudaGraphExecDestroy(g);
   for (void* p : {(void*)t->d_c2f, (void*)t->d_f2c, (void*)t->Ec, (void*)t->dEc})
     if (p) cudaFree(p);
   if (t->opt_partial) cudaFree(t->opt_partial);
@@ -467,11 +478,72 @@ static bool comm_active(const ne_ctx* ctx) {
   return ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce;
 }
 
+// ZeRO-1 (ne_comm_set_sharding): each matrix segment (and the embedding) whose
+// size splits into world equal parts of a multiple of 4 elements is owned in
+// parts -- rank r reduces, updates and keeps current the r-th part, and the
+// updated bf16 compute copies are all-gathered after the optimizer step; the
+// gains (and any segment that does not split) stay replicated.
+static bool shard_mode(const ne_ctx* ctx) {   // ownership (optimizer), whatever the reduction
+  return ctx->comm && ctx->comm->world > 1 && ctx->comm->shard;
+}
+static bool shard_active(const ne_ctx* ctx) {   // the buckets reduce-scatter
+  return comm_active(ctx) && ctx->comm->shard;
+}
+static bool seg_sharded(const ne_ctx* ctx, const Seg& sg) {
+  if (!shard_mode(ctx) || sg.w16 == nullptr) return false;
+  const long long W = ctx->comm->world;
+  return sg.n % W == 0 && (sg.n / W) % 4 == 0;
+}
+static long long shard_len(const ne_ctx* ctx, const Seg& sg) { return sg.n / ctx->comm->world; }
+static long long shard_off(const ne_ctx* ctx, const Seg& sg) {
+  return shard_len(ctx, sg) * ctx->comm->rank;
+}
+
+// One bucket (segments [s0, s1)): reduce-scatter the owned segments, all-reduce
+// the replicated ones, as one NCCL group on the comm stream.
+static ne_status exchange_segments(ne_ctx* ctx, int s0, int s1) {
+  TrainState* t = ctx->train;
+  ne_status s = comm_group(ctx, true);
+  if (s != NE_OK) return s;
+  for (int k = s0; k < s1 && s == NE_OK; ++k) {
+    const Seg& sg = t->segs[k];
+    s = seg_sharded(ctx, sg) ? comm_reduce_scatter(ctx, sg.g, (size_t)shard_len(ctx, sg))
+                             : comm_allreduce(ctx, sg.g, (size_t)sg.n);
+  }
+  const ne_status e = comm_group(ctx, false);
+  return s != NE_OK ? s : e;
+}
+
+// In place all-gather of the owned parts of one array (seg_array selector:
+// 0 masters, 1 m, 2 v, 3 gradients) of every sharded segment; 4 = the bf16
+// compute copies.  Enqueued on the comm stream between fences.
+static ne_status gather_owned(ne_ctx* ctx, int which) {
+  TrainState* t = ctx->train;
+  ne_status s = comm_fence_in(ctx);
+  if (s != NE_OK) return s;
+  if ((s = comm_group(ctx, true)) != NE_OK) return s;
+  for (const Seg& sg : t->segs) {
+    if (!seg_sharded(ctx, sg) || s != NE_OK) continue;
+    const long long off = shard_off(ctx, sg), len = shard_len(ctx, sg);
+    if (which == 4) {
+      s = comm_allgather(ctx, sg.w16 + off, sg.w16, (size_t)len * 2);
+    } else {
+      float* a = which == 0 ? sg.w : which == 1 ? sg.m : which == 2 ? sg.v : sg.g;
+      s = comm_allgather(ctx, a + off, a, (size_t)len * 4);
+    }
+  }
+  const ne_status e = comm_group(ctx, false);
+  if (s != NE_OK) return s;
+  if (e != NE_OK) return e;
+  return comm_fence_out(ctx);
+}
+
 static ne_status comm_after_lmhead(ne_ctx* ctx) {
   if (!comm_active(ctx)) return NE_OK;
   TrainState* t = ctx->train;
   ne_status s = comm_fence_in(ctx);
   if (s != NE_OK) return s;
+  if (shard_active(ctx)) return exchange_segments(ctx, (int)t->segs.size() - 2, (int)t->segs.size());
   return comm_allreduce(ctx, t->grad_pool + t->tail_grad_off, t->grad_floats - t->tail_grad_off);
 }
 
@@ -480,6 +552,10 @@ static ne_status comm_after_layer(ne_ctx* ctx, int l) {
   TrainState* t = ctx->train;
   ne_status s = comm_fence_in(ctx);
   if (s != NE_OK) return s;
+  if (shard_active(ctx)) {
+    const int s1 = l + 1 < (int)t->P.size() ? t->P[l + 1].seg0 : (int)t->segs.size() - 2;
+    return exchange_segments(ctx, t->P[l].seg0, s1);
+  }
   return comm_allreduce(ctx, t->grad_pool + (size_t)l * t->layer_grad_floats,
                         t->layer_grad_floats);
 }
@@ -811,11 +887,13 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   } else {
     // The graph always writes the loss to its own slot; copied out below.
     float* g_loss = reinterpret_cast<float*>(t->red + 3);
-    if (t->step_graph && t->step_graph_rope != ctx->rope_cs) {
-      NE_CUDA(cudaGraphExecDestroy(t->step_graph));
-      t->step_graph = nullptr;
+    const int gi = comm_active(ctx) ? 1 : 0;
+    cudaGraphExec_t& sgraph = t->step_graphs[gi];
+    if (sgraph && t->step_graph_rope[gi] != ctx->rope_cs) {
+      NE_CUDA(cudaGraphExecDestroy(sgraph));
+      sgraph = nullptr;
     }
-    if (!t->step_graph) {
+    if (!sgraph) {
       cudaGraph_t g = nullptr;
       NE_CUDA(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
       const ne_status sb = step_body(ctx, g_loss);
@@ -826,15 +904,15 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
       }
       if (ec != cudaSuccess)
         return fail(ctx, NE_ERR_CUDA, std::string("step capture: ") + cudaGetErrorString(ec));
-      const cudaError_t ei = cudaGraphInstantiate(&t->step_graph, g, 0);
+      const cudaError_t ei = cudaGraphInstantiate(&sgraph, g, 0);
       cudaGraphDestroy(g);
       if (ei != cudaSuccess) {
-        t->step_graph = nullptr;
+        sgraph = nullptr;
         return fail(ctx, NE_ERR_CUDA, std::string("step graph: ") + cudaGetErrorString(ei));
       }
-      t->step_graph_rope = ctx->rope_cs;
+      t->step_graph_rope[gi] = ctx->rope_cs;
     }
-    NE_CUDA(cudaGraphLaunch(t->step_graph, ctx->st));
+    NE_CUDA(cudaGraphLaunch(sgraph, ctx->st));
     if (d_loss)
       NE_CUDA(cudaMemcpyAsync(d_loss, g_loss, sizeof(float), cudaMemcpyDeviceToDevice, ctx->st));
   }
@@ -907,19 +985,29 @@ NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floa
 static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
   TrainState* t = ctx->train;
   if (!t->d_chunks) {
+    // the rank's work: its part of each sharded segment, every replicated
+    // segment (whose norm share only rank 0 counts)
+    const bool sharded = shard_mode(ctx);
+    const bool count_replicated = !sharded || ctx->comm->rank == 0;
     std::vector<OptChunk> hc;
     for (size_t k = 0; k < t->segs.size(); ++k) {
       const Seg& sg = t->segs[k];
-      auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+      const bool own = seg_sharded(ctx, sg);
+      const long long b0 = own ? shard_off(ctx, sg) : 0;
+      const long long b1 = own ? b0 + shard_len(ctx, sg) : sg.n;
+      auto a16 = [&](const float* p) { return (reinterpret_cast<uintptr_t>(p + b0) & 15u) == 0; };
       const int vec = a16(sg.w) && a16(sg.g) && a16(sg.m) && a16(sg.v) &&
-                      (reinterpret_cast<uintptr_t>(sg.w16) & 7u) == 0;
-      for (long long off = 0; off < sg.n; off += OPT_CHUNK) hc.push_back({(int)k, vec, off});
+                      (sg.w16 == nullptr || (reinterpret_cast<uintptr_t>(sg.w16 + b0) & 7u) == 0);
+      const int norm = (own || count_replicated) ? 1 : 0;
+      for (long long off = b0; off < b1; off += OPT_CHUNK)
+        hc.push_back({(int)k, vec, off, (int)std::min<long long>(OPT_CHUNK, b1 - off), norm});
     }
     t->nchunks = (int)hc.size();
     ne_status s;
     if ((s = dalloc(ctx, &t->d_chunks, hc.size())) != NE_OK ||
         (s = dalloc(ctx, &t->opt_partial, hc.size())) != NE_OK ||
-        (s = dalloc(ctx, &t->opt_ticket, 1)) != NE_OK || (s = dalloc(ctx, &t->norm_out, 2)) != NE_OK)
+        (s = dalloc(ctx, &t->opt_ticket, 1)) != NE_OK ||
+        (!t->norm_out && (s = dalloc(ctx, &t->norm_out, 4)) != NE_OK))
       return s;
     NE_CUDA(cudaMemcpyAsync(t->d_chunks, hc.data(), hc.size() * sizeof(OptChunk),
                             cudaMemcpyHostToDevice, ctx->st));
@@ -940,13 +1028,29 @@ static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
 }
 
 // Global gradient norm (train.m:805-826), times grad_scale; synchronises.
+// The global gradient norm into t->norm_out ([0] norm, [1] factor): in sharded
+// mode each rank's sum of squares (its parts + rank 0's replicated segments)
+// is added over the ranks before the norm and the clip factor are formed.
+static ne_status enqueue_norm(ne_ctx* ctx, float grad_scale, float grad_clip) {
+  TrainState* t = ctx->train;
+  const bool sharded = shard_mode(ctx);
+  NE_LAUNCH(launch_sumsq_chunks(t->d_segs, t->d_chunks, t->nchunks, t->opt_partial, t->opt_ticket,
+                                grad_scale, grad_clip, t->norm_out, ctx->st, sharded ? 1 : 0));
+  if (!sharded) return NE_OK;
+  ne_status s;
+  if ((s = comm_fence_in(ctx)) != NE_OK || (s = comm_allreduce(ctx, t->norm_out + 2, 1)) != NE_OK ||
+      (s = comm_fence_out(ctx)) != NE_OK)
+    return s;
+  NE_LAUNCH(launch_norm_finish(t->norm_out, grad_scale, grad_clip, ctx->st));
+  return NE_OK;
+}
+
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm) {
   if (!ctx || !ctx->train || !h_norm) return NE_ERR_STATE;
   TrainState* t = ctx->train;
   ne_status s = upload_segs(ctx, t->d_segs ? t->d_segs_wd : 0.f);
   if (s != NE_OK) return s;
-  NE_LAUNCH(launch_sumsq_chunks(t->d_segs, t->d_chunks, t->nchunks, t->opt_partial, t->opt_ticket,
-                                grad_scale, 0.f, t->norm_out, ctx->st));
+  if ((s = enqueue_norm(ctx, grad_scale, 0.f)) != NE_OK) return s;
   NE_CUDA(cudaMemcpyAsync(h_norm, t->norm_out, sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
   return ne_sync(ctx);
 }
@@ -966,10 +1070,15 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
   if (s != NE_OK) return s;
   const float bc1 = 1.0f - std::pow(cfg->beta1, (float)t_step);
   const float bc2 = 1.0f - std::pow(cfg->beta2, (float)t_step);
-  NE_LAUNCH(launch_sumsq_chunks(t->d_segs, t->d_chunks, t->nchunks, t->opt_partial, t->opt_ticket,
-                                cfg->grad_scale, cfg->grad_clip, t->norm_out, ctx->st));
+  if ((s = enqueue_norm(ctx, cfg->grad_scale, cfg->grad_clip)) != NE_OK) return s;
   NE_LAUNCH(launch_adamw_chunks(t->d_segs, t->d_chunks, t->nchunks, cfg->lr, cfg->beta1,
                                 cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, t->norm_out, ctx->st));
+  if (shard_mode(ctx)) {
+    // every rank needs the whole updated compute copy; the fp32 masters and
+    // moments stay with their owners until ne_train_gather_state
+    if ((s = gather_owned(ctx, 4)) != NE_OK) return s;
+    t->state_gathered = false;
+  }
   if ((s = ne_train_zero_grads(ctx)) != NE_OK) return s;
   if (h_grad_norm) {
     NE_CUDA(cudaMemcpyAsync(h_grad_norm, t->norm_out, sizeof(float), cudaMemcpyDeviceToHost,
@@ -977,6 +1086,24 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
     return ne_sync(ctx);
   }
   return NE_OK;
+}
+
+// Sharded mode: all-gather the owned parts of the fp32 masters and both Adam
+// moments (which = 0) and of the gradients (which = 1), so checkpoints and the
+// state getters see whole tensors.  Collective: every rank calls it.
+NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which) {
+  if (!ctx || !ctx->train || which < 0 || which > 1) return NE_ERR_INVALID;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  if (!shard_mode(ctx)) return NE_OK;
+  ne_status s;
+  if (which == 1) {
+    if ((s = gather_owned(ctx, 3)) != NE_OK) return s;
+  } else {
+    for (int a = 0; a < 3; ++a)
+      if ((s = gather_owned(ctx, a)) != NE_OK) return s;
+    ctx->train->state_gathered = true;
+  }
+  return ne_sync(ctx);
 }
 
 // Learning-rate schedule of train.m:851-858: linear warmup, then cosine decay
@@ -1050,6 +1177,8 @@ ne_status xfer(ne_ctx* ctx, const TensorRef& r, int which, float* host, bool to_
 extern "C" NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info) {
   if (!ctx || !path) return NE_ERR_INVALID;
   if (!ctx->train) return fail(ctx, NE_ERR_STATE, "ne_save_ckpt_v4 needs the training state");
+  if (!ctx->train->state_gathered)
+    return fail(ctx, NE_ERR_STATE, "sharded optimizer state: ne_train_gather_state on every rank first");
   const ne_model_cfg& m = ctx->cfg;
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
@@ -1235,6 +1364,7 @@ ne_status train_ckpt_load(ne_ctx* ctx, const char* path, ne_ckpt_info* info, boo
     info->cum_batches = h.cum_batches;
     info->has_qk_norm = has_qk ? 1 : 0;
   }
+  t->state_gathered = true;   // every part came from the file
   return NE_OK;
 }
 
@@ -1252,6 +1382,8 @@ extern "C" NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which
   TrainState* t = ctx->train;
   const ne_model_cfg& m = ctx->cfg;
   if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
+  if (which != 0 && !t->state_gathered)   // which 0 = gradients (see ne_train_gather_state)
+    return fail(ctx, NE_ERR_STATE, "sharded optimizer state: ne_train_gather_state on every rank first");
   NE_CUDA(cudaSetDevice(ctx->device));
   NE_CUDA(cudaStreamSynchronize(ctx->st));
   const int arr = which == 0 ? 3 : which - 1;   // seg_array selector
@@ -1321,9 +1453,9 @@ extern "C" NE_API ne_status ne_train_set_vocab_map(ne_ctx* ctx, const int32_t* h
   t->Ec = nullptr;
   t->dEc = nullptr;
   t->CV = t->CVp = 0;
-  if (t->step_graph) {   // the captured step used the previous classifier
-    NE_CUDA(cudaGraphExecDestroy(t->step_graph));
-    t->step_graph = nullptr;
+  for (cudaGraphExec_t& g : t->step_graphs) {   // the captured steps used the previous classifier
+    if (g) NE_CUDA(cudaGraphExecDestroy(g));
+    g = nullptr;
   }
   if (!h_c2f || CV <= 0) return NE_OK;
   if (CV > m.vocab) return fail(ctx, NE_ERR_INVALID, "vocab map larger than the vocabulary");

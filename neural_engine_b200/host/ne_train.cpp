@@ -45,6 +45,7 @@ namespace {
 
 struct Args {
   bool scratch = false, resume = false, synthetic = false, compact_vocab = true, print_vocab = false;
+  bool zero1 = false;   // data parallel: ZeRO-1 (sharded optimizer state)
   int steps = 10000, accum = 10, warmup = 100;
   float lr = 3e-4f, clip = 1.0f;
   std::string data = "../tinystories_data00.bin";
@@ -64,6 +65,7 @@ void usage() {
       "                [--clip X] [--data FILE] [--model qwen3_06b|stories110m] [--seq S]\n"
       "                [--batch B] [--ckpt FILE] [--device D] [--synthetic] [--save-every N]\n"
       "                [--qk-norm 0|1] [--theta X] [--eps X] [--alpha X] [--no-compact-vocab]\n"
+      "                [--zero1]   (with WORLD_SIZE > 1: reduce-scatter + sharded AdamW)\n"
       "                [--layers N --dim N --hidden N --heads N --kv-heads N --head-dim N\n"
       "                 --vocab N] [--dump-init FILE] [--print-windows N] [--print-vocab]\n");
 }
@@ -82,6 +84,7 @@ bool parse(int argc, char** argv, Args& a) {
     else if (s == "--scratch") a.scratch = true;
     else if (s == "--synthetic") a.synthetic = true;
     else if (s == "--no-compact-vocab") a.compact_vocab = false;
+    else if (s == "--zero1") a.zero1 = true;
     else if (s == "--print-vocab") a.print_vocab = true;
     else if (s == "--steps") a.steps = std::atoi(next("--steps"));
     else if (s == "--lr") a.lr = (float)std::atof(next("--lr"));
@@ -476,6 +479,7 @@ int main(int argc, char** argv) {
       }
     }
     CHECK(ne_comm_init(ctx, id, rank, world));
+    if (a.zero1) CHECK(ne_comm_set_sharding(ctx, 1));
   }
 
   // ---- training loop (train.m:389-917)
@@ -518,6 +522,9 @@ int main(int argc, char** argv) {
         if ((step + 1) % 10 == 0) std::printf("  grad_norm=%.4f\n", norm);
         std::printf("  [adam] step %d: %.1fms (update+restage+zero)\n", step, now_ms() - ta);
       }
+      // sharded state: every rank takes part in gathering it at each save point
+      if (a.zero1 && world > 1 && (step + 1) % a.save_every == 0)
+        CHECK(ne_train_gather_state(ctx, 0));
       if (rank == 0 && (step + 1) % a.save_every == 0 && last_loss < best_loss) {
         best_loss = last_loss;
         ne_ckpt_info info{};

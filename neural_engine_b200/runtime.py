@@ -34,7 +34,8 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_embed_fwd", "ne_attn_fwd", "ne_ffn_fwd", "ne_lmhead_ce_fwd_bwd", "ne_ffn_bwd",
             "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
-            "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read")
+            "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
+            "ne_comm_set_sharding", "ne_train_gather_state")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -151,6 +152,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_comm_unique_id.argtypes = [P]
     lib.ne_comm_init.argtypes = [P, P, I, I]
     lib.ne_comm_set_reduce.argtypes = [P, I]
+    lib.ne_comm_set_sharding.argtypes = [P, I]
+    lib.ne_train_gather_state.argtypes = [P, I]
     lib.ne_grad_allreduce_async.argtypes = [P]
     lib.ne_sdpa_fwd_device.argtypes = [P, P, P, P, I, I, P, P]
     lib.ne_train_set_vocab_map.argtypes = [P, P, I]
@@ -298,6 +301,14 @@ class Engine:
 
     def comm_set_reduce(self, on: bool):
         self._check(self.lib.ne_comm_set_reduce(self._ctx, int(bool(on))))
+
+    def comm_set_sharding(self, on: bool):
+        """ZeRO-1: reduce-scatter, sharded AdamW, all-gathered compute copies."""
+        self._check(self.lib.ne_comm_set_sharding(self._ctx, int(bool(on))))
+
+    def gather_state(self, grads: bool = False):
+        """Collective: whole masters and moments (or reduced gradients) on every rank."""
+        self._check(self.lib.ne_train_gather_state(self._ctx, int(bool(grads))))
 
     def grad_allreduce(self):
         self._check(self.lib.ne_grad_allreduce_async(self._ctx))

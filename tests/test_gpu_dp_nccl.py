@@ -38,7 +38,7 @@ def _setup(device, B, S):
     return e
 
 
-def _rank(rank, world, uid, tok, q):
+def _rank(rank, world, uid, tok, q, mode):
     import sys
     import os
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -47,14 +47,23 @@ def _rank(rank, world, uid, tok, q):
         B = tok.shape[0] // world
         e = _setup(rank, B, tok.shape[1] - 1)
         e.comm_init(uid, rank, world)
+        zero1 = mode == "zero1"
+        if zero1:
+            e.comm_set_sharding(True)
         loss = e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])   # eager first micro-step
+        if zero1:
+            e.gather_state(grads=True)   # each rank reduced only its parts
         g = e.get_grads()
         e.zero_grads()
         # the same micro-step again, now replayed as a captured graph that
         # holds the NCCL buckets too
         e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])
+        if zero1:
+            e.gather_state(grads=True)
         g2 = e.get_grads()
         norm = e.adamw_step(1, 1e-3, grad_scale=1.0 / world)
+        if zero1:
+            e.gather_state()             # masters and moments from their owners
         w = e.get_masters()
         q.put((rank, loss, (g, g2), norm, w))
         e.close()
@@ -68,7 +77,11 @@ def _rel(a, b):
     return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
 
 
-def test_bucketed_allreduce_equals_global_batch_gradient():
+@pytest.mark.parametrize("mode", ["allreduce", "zero1"])
+def test_bucketed_allreduce_equals_global_batch_gradient(mode):
+    """allreduce: every rank sums every bucket and takes the whole AdamW step;
+    zero1: buckets reduce-scatter, each rank updates its parts, the bf16
+    copies are all-gathered (ne_comm_set_sharding)."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs two GPUs")
@@ -82,7 +95,7 @@ def test_bucketed_allreduce_equals_global_batch_gradient():
     uid = ne.Engine.comm_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, tok, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, tok, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
