@@ -255,6 +255,17 @@ int device_num_sms() {
   return n;
 }
 
+// CTA pairs (cta_group::2, 256 x 256 tiles over two SMs) for the large
+// token-major products; NE_GEMM_PAIR=0 keeps single-CTA tiles everywhere.
+bool gemm_pair_tiles(const GemmCall& c) {
+  static const bool pair_on = [] {
+    const char* e = getenv("NE_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return pair_on && pick_bn(c) == 256 && (c.max_ctas <= 0 || c.max_ctas >= 2) && c.M >= 512 &&
+         c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T;
+}
+
 int gemm_pick_splits(const GemmCall& c, int num_sms) {
   if (c.splits > 0) return c.splits;
   if (c.epi == EPI_F32T_ADD) {
@@ -323,15 +334,7 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
       !(c.epi == EPI_RESID && c.atomic))
     return cudaErrorInvalidValue;
 
-  // CTA pairs (cta_group::2, 256 x 256 tiles over two SMs) for the large
-  // token-major products; NE_GEMM_PAIR=0 keeps single-CTA tiles everywhere.
-  static const bool pair_on = [] {
-    const char* e = getenv("NE_GEMM_PAIR");
-    return !(e && e[0] == '0');
-  }();
-  const bool pair = pair_on && bn == 256 && (c.max_ctas <= 0 || c.max_ctas >= 2) && c.M >= 512 &&
-                    c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T &&
-                    num_sms >= 2;
+  const bool pair = gemm_pair_tiles(c) && bn == 256 && num_sms >= 2;
   const int tile_m = pair ? 2 * GEMM_BM : GEMM_BM;
 
   CUtensorMap ta, tb;

@@ -50,6 +50,8 @@ struct GemmCall {
 };
 
 // Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).
+// Whether gemm_run takes CTA-pair tiles (256 x 256 over two SMs) for this call.
+bool gemm_pair_tiles(const GemmCall& c);
 int gemm_pick_splits(const GemmCall& c, int num_sms);
 cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st);
 int device_num_sms();

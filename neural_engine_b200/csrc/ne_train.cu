@@ -187,7 +187,11 @@ double wave_eff(long long units, int sms) {
 // freely: take the 256-wide N tile and the split (at most 4, dividing the
 // k-blocks) whose work units fill the SMs best.
 int dw_splits(const GemmCall& c, int sms) {
-  const long long tiles = (long long)((c.M + 127) / 128) * ((c.N + 255) / 256);
+  // products with M >= 512 run as CTA pairs (256-row tiles, one slot per two SMs)
+  const bool pair = gemm_pair_tiles(c);
+  const int bm = pair ? 256 : 128;
+  if (pair) sms /= 2;
+  const long long tiles = (long long)((c.M + bm - 1) / bm) * ((c.N + 255) / 256);
   const int kb = c.K / 64;
   int best = 1;
   double best_eff = wave_eff(tiles, sms);
