@@ -253,16 +253,18 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tc_fence_after();
       const uint32_t srow = tmem + lane_off + st * TA_BK;
       const int kbase = j * TA_BK;
-      // pass 1: row max over this warp's 64 columns, then over both halves
+      // pass 1: this warp's 64 scores (kept in registers for pass 2), their
+      // row max, then the max over both halves
+      uint32_t sr[2][32];
       float mx = m;
       if (ready) {
-        for (int c = c_lo; c < c_lo + 64; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(srow + c, r);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tmem_ld32(srow + c_lo + 32 * h, sr[h]);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int key = kbase + c + i;
-            const float v = (key <= qpos && key < S) ? __uint_as_float(r[i]) * qscale_log2 : -1e30f;
+            const int key = kbase + c_lo + 32 * h + i;
+            const float v = (key <= qpos && key < S) ? __uint_as_float(sr[h][i]) * qscale_log2 : -1e30f;
             mx = fmaxf(mx, v);
           }
         }
@@ -278,21 +280,26 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         ok = false;
         break;
       }
-      const float corr = exp2f(m - mx);
-      m = mx;
+      // Lazy rescaling: the running max m moves (and O, l are rescaled) only
+      // when the tile's max exceeds it by more than 2^8; otherwise p = exp2(s - m)
+      // stays below 256, well inside bf16 and fp32, and the TMEM round trip of
+      // O is skipped.  Both warps of the pair see the same m and mx.
+      const bool move = mx > m + 8.0f;
+      const float corr = move ? exp2f(m - mx) : 1.0f;
+      if (move) m = mx;
       // pass 2: p = exp2(s - m) -> P (bf16, swizzled K-major rows), row sum
       float sum = 0.f;
-      for (int c = c_lo; c < c_lo + 64; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(srow + c, r);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = c_lo + 32 * h;
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int key = kbase + c + i;
           const float p0 = (key <= qpos && key < S)
-                               ? exp2f(__uint_as_float(r[i]) * qscale_log2 - m) : 0.f;
+                               ? exp2f(__uint_as_float(sr[h][i]) * qscale_log2 - m) : 0.f;
           const float p1 = (key + 1 <= qpos && key + 1 < S)
-                               ? exp2f(__uint_as_float(r[i + 1]) * qscale_log2 - m) : 0.f;
+                               ? exp2f(__uint_as_float(sr[h][i + 1]) * qscale_log2 - m) : 0.f;
           sum += p0 + p1;
           const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
           w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
@@ -308,7 +315,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
       l = l * corr + sum;   // this half's share of the row sum
       // running output *= corr (the accumulator holds tiles < j); this warp's 64 columns
-      if (j > 0) {
+      if (j > 0 && move) {
         const uint32_t orow = tmem + lane_off + 256;
         for (int c = c_lo; c < c_lo + 64; c += 32) {
           uint32_t r[32];
