@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the prefill measurement (config 2)")
+    ap.add_argument("--no-stories", action="store_true",
+                    help="skip the Stories110M training measurement (config 3)")
     ap.add_argument("--train-only", action="store_true",
                     help="skip the decode headline; print the training object alone "
                          "(profiling runs)")
@@ -94,9 +98,28 @@ def tensor_peak():
         return 1400.0, "fallback (sustained)"
 
 
-def train_flops_per_token(S: int) -> float:
-    """3 x forward: 2 x 596.0 M params + causal attention 2*L*Hq*hd*(S+1)."""
-    return 3.0 * (2.0 * PARAMS + 2.0 * L * HQ * HD * (S + 1))
+def n_params(cfg) -> int:
+    """Parameters of a model config (matrices, gains, embedding)."""
+    d = cfg.dim
+    per = cfg.q_dim * d + 2 * cfg.kv_dim * d + d * cfg.q_dim + 3 * cfg.hidden * d + 2 * d
+    return cfg.n_layers * per + d + cfg.vocab * d
+
+
+def train_flops_per_token(S: int, cfg=None) -> float:
+    """3 x forward: 2 x params (596.0 M for Qwen3-0.6B, 109.5 M for Stories110M)
+    + causal attention 2*L*Hq*hd*(S+1)."""
+    if cfg is None:
+        return 3.0 * (2.0 * PARAMS + 2.0 * L * HQ * HD * (S + 1))
+    return 3.0 * (2.0 * n_params(cfg) + 2.0 * cfg.n_layers * cfg.q_dim * (S + 1))
+
+
+def prefill_flops(B: int, S: int) -> float:
+    """FLOPs one Qwen3-0.6B prefill of B x S tokens executes: the layer
+    matrices for every token (2 x 440.4 M), causal attention counted once
+    (2*L*Hq*hd*(S+1) per token) and the tied LM head for the last position of
+    each sequence only (the token loop needs no other logits)."""
+    mats = L * ((HQ * HD) * D + 2 * (HKV * HD) * D + D * (HQ * HD) + 3 * F * D)
+    return B * S * (2.0 * mats + 2.0 * L * HQ * HD * (S + 1)) + B * 2.0 * V * D
 
 
 # ----------------------------------------------------------------- clocks
@@ -231,23 +254,28 @@ def cpu_decode_sample(layers, rms_final, embed, qk, B=8, steps=12, prompt=512, s
     return B * steps / dt, dt
 
 
-def host_weights(seed=0):
-    """bf16-valued N(0, 0.02) weights generated on the GPU, returned as host fp32."""
+def host_weights(seed=0, cfg=None):
+    """bf16-valued N(0, 0.02) weights generated on the GPU, returned as host
+    fp32 (Qwen3-0.6B unless another model config is given)."""
     import torch
+    import neural_engine_b200 as ne
+    cfg = cfg or ne.QWEN3_06B
     g = torch.Generator(device="cuda").manual_seed(seed)
+    d, f, qd, kd = cfg.dim, cfg.hidden, cfg.q_dim, cfg.kv_dim
 
     def t(*shape):
         return (torch.randn(*shape, generator=g, device="cuda") * 0.02).to(torch.bfloat16) \
             .float().cpu().numpy()
 
     layers = []
-    for _ in range(L):
-        layers.append({"Wq": t(HQ * HD, D), "Wk": t(HKV * HD, D), "Wv": t(HKV * HD, D),
-                       "Wo": t(D, HQ * HD), "W1": t(F, D), "W2": t(D, F), "W3": t(F, D),
-                       "rms_att": np.ones(D, np.float32), "rms_ffn": np.ones(D, np.float32)})
-    embed = t(V, D)
-    qk = [(np.ones(HD, np.float32), np.ones(HD, np.float32)) for _ in range(L)]
-    return layers, np.ones(D, np.float32), embed, qk
+    for _ in range(cfg.n_layers):
+        layers.append({"Wq": t(qd, d), "Wk": t(kd, d), "Wv": t(kd, d),
+                       "Wo": t(d, qd), "W1": t(f, d), "W2": t(d, f), "W3": t(f, d),
+                       "rms_att": np.ones(d, np.float32), "rms_ffn": np.ones(d, np.float32)})
+    embed = t(cfg.vocab, d)
+    qk = ([(np.ones(cfg.head_dim, np.float32), np.ones(cfg.head_dim, np.float32))
+           for _ in range(cfg.n_layers)] if cfg.qk_norm else None)
+    return layers, np.ones(d, np.float32), embed, qk
 
 
 # ----------------------------------------------------------------- reference arm
@@ -282,14 +310,14 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- training
-def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3):
+def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3, model="qwen3_06b"):
     """torch-CPU float32 fwd + bwd of one sequence of S tokens (the oracle's
     restatement of the training forward), all host cores.  Returns tokens/s."""
     import torch
     from oracle import model as om
     from oracle import train as ot
     torch.set_num_threads(os.cpu_count() or 1)
-    cfg = om.QWEN3_06B
+    cfg = om.PRESETS[model]
     tok = np.random.default_rng(7).integers(0, cfg.vocab, size=(1, S + 1))
     t0 = time.perf_counter()
     for _ in range(reps):
@@ -298,18 +326,23 @@ def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3):
     return reps * S / dt, dt
 
 
-def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
-    """Data-parallel training steps of BASELINE config 4 (S 256, B 16 per GPU)."""
+def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwen3_06b",
+              B=None, S=None):
+    """Data-parallel training steps: BASELINE config 4 (Qwen3-0.6B, S 256, B 16
+    per GPU; token ids from seed 3) or config 3 (Stories110M, S 256, B 32 per
+    GPU; seed 2)."""
     import torch
     import torch.distributed as dist
     import neural_engine_b200 as ne
-    cfg = ne.QWEN3_06B
-    B, S = args.train_batch, args.train_seq
+    stories = model == "stories110m"
+    cfg = ne.STORIES110M if stories else ne.QWEN3_06B
+    B = B or args.train_batch
+    S = S or args.train_seq
     eng = ne.Engine(cfg, device=local)
     eng.set_weights(layers, rf, emb, qk)
     eng.train_alloc(B, S)
     stream = torch.cuda.ExternalStream(eng.stream_ptr)
-    gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    gen = torch.Generator(device="cuda").manual_seed((2000 if stories else 3000) + rank)
     tok = torch.randint(0, cfg.vocab, (B, S + 1), generator=gen, device="cuda", dtype=torch.int32)
     if world > 1:
         # the library's own exchange: one NCCL bucket per layer, issued as the
@@ -349,7 +382,8 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
     ms_step = t_ms / args.steps
     value = world * B * S * args.steps / (t_ms / 1000.0)
     peak, kind = tensor_peak()
-    ach = train_flops_per_token(S) * B * S / (ms_step / 1000.0) / 1e12
+    fpt = train_flops_per_token(S, cfg)
+    ach = fpt * B * S / (ms_step / 1000.0) / 1e12
     # e2e through the host-buffer call: tokens H2D, fwd+bwd, loss D2H, AdamW
     h_tok = tok.cpu().numpy()
     barrier()
@@ -368,14 +402,17 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
     eng.close()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, dt = cpu_train_sample(layers, rf, emb, qk)
+        v, dt = cpu_train_sample(layers, rf, emb, qk, S=S, model=model)
         cpu = {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-               "sample": f"torch-CPU float32 fwd+bwd of the oracle's Qwen3-0.6B forward, 3 x 1 x "
-                         f"256 tokens ({dt:.1f} s)"}
-    return {"metric": TRAIN_METRIC, "value": round(value, 1), "unit": UNIT,
+               "sample": f"torch-CPU float32 fwd+bwd of the oracle's "
+                         f"{'Stories110M' if stories else 'Qwen3-0.6B'} forward, 3 x 1 x "
+                         f"{S} tokens ({dt:.1f} s)"}
+    metric = (f"Stories110M training tokens/sec (fwd + bwd + AdamW, seq {S}, batch {B} per GPU)"
+              if stories else TRAIN_METRIC)
+    return {"metric": metric, "value": round(value, 1), "unit": UNIT,
             "ms_per_step": round(ms_step, 3), "steps": args.steps, "warmup": args.warmup,
             "scaling": "weak", "dtype": "bf16",
-            "config": {"workload": "qwen3_06b_train", "batch_per_gpu": B, "seq_len": S,
+            "config": {"workload": f"{model}_train", "batch_per_gpu": B, "seq_len": S,
                        "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
                        "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
                        "parallelism": (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
@@ -386,11 +423,67 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier):
                                        "overlapped with the backward)")},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_kind": kind,
-                         "flops_per_token": train_flops_per_token(S), "scope": "whole step"},
+                         "flops_per_token": fpt, "scope": "whole step"},
             "clocks": clk,
             "e2e": {"value": round(world * B * S / te, 1), "unit": UNIT,
                     "h2d_bytes_per_step": B * (S + 1) * 4, "d2h_bytes_per_step": 8},
             "cpu_baseline": cpu}
+
+
+# ----------------------------------------------------------------- prefill
+def run_prefill(args, rank, local, world, layers, rf, emb, qk):
+    """Qwen3-0.6B prefill -- the token loop's causal pass
+    over the prompt that fills the fp16 KV cache (ne_prefill_device) -- at B 16
+    per GPU, S 256 and 2048, uniform-random token ids.  Device time of whole
+    calls on the library's stream (CUDA events, max over ranks); the KV cache
+    and activations (>= 470 MB per call) exceed L2."""
+    import torch
+    import torch.distributed as dist
+    import neural_engine_b200 as ne
+    cfg = ne.QWEN3_06B
+    B, seqs, reps = 16, (256, 2048), 5
+    peak, kind = tensor_peak()
+    runs = {}
+    eng = ne.Engine(cfg, device=local)
+    try:
+        eng.set_weights(layers, rf, emb, qk)
+        eng.kv_alloc(B, max(seqs))
+        stream = torch.cuda.ExternalStream(eng.stream_ptr)
+        nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+        for S in seqs:
+            gen = torch.Generator(device="cuda").manual_seed(4000 + 7 * rank + S)
+            tok = torch.randint(0, cfg.vocab, (B, S), generator=gen, device="cuda",
+                                dtype=torch.int32)
+            torch.cuda.synchronize()
+            for _ in range(3):
+                eng.prefill_device(tok.data_ptr(), B, S, 0, nxt.data_ptr())
+            eng.sync()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            for _ in range(reps):
+                eng.prefill_device(tok.data_ptr(), B, S, 0, nxt.data_ptr())
+            ev1.record(stream)
+            ev1.synchronize()
+            ms = ev0.elapsed_time(ev1) / reps
+            if world > 1:
+                tt = torch.tensor([ms], device="cuda")
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                ms = float(tt.item())
+            fl = prefill_flops(B, S)
+            ach = fl / (ms / 1000.0) / 1e12
+            runs[f"seq{S}"] = {"seq_len": S, "ms_per_call": round(ms, 3),
+                               "tokens_per_s": round(world * B * S / (ms / 1000.0), 1),
+                               "flops_per_call": fl, "achieved_tflops": round(ach, 1),
+                               "frac": round(ach / peak, 4)}
+    finally:
+        eng.close()
+    return {"metric": "Qwen3-0.6B prefill tokens/sec (causal pass filling the fp16 KV cache)",
+            "unit": UNIT, "workload": "qwen3_06b_prefill", "batch_per_gpu": B,
+            "global_batch": B * world, "calls_timed": reps,
+            "roofline": {"bound": "tensor", "peak": peak, "unit": "TFLOP/s", "peak_kind": kind,
+                         "flops": "layer matrices for every token + causal attention once + "
+                                  "LM head on the last position"},
+            "runs": runs}
 
 
 # ----------------------------------------------------------------- our arm
@@ -526,9 +619,17 @@ def main():
 
     kps = eng.kernels_per_step(B)
     eng.close()
-    train = None
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(args, rank, local, world, layers, rf, emb, qk)
+    train = train_stories = None
     if not args.no_train:
         train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
+        if not args.no_stories:
+            import neural_engine_b200 as ne_mod
+            s_w = host_weights(seed=0, cfg=ne_mod.STORIES110M)
+            train_stories = run_train(args, rank, local, world, *s_w, barrier,
+                                      model="stories110m", B=32, S=256)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
@@ -545,7 +646,7 @@ def main():
                 "kernel_groups_ms_per_step": {k: round(v, 4) for k, v in groups.items()},
                 "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
                 "gpu_launches": kps * G * args.steps, "kernels_per_decode_step": kps,
-                "train": train}
+                "prefill": prefill, "train": train, "train_stories110m": train_stories}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
