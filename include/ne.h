@@ -196,7 +196,11 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
  * floats at aux0 + 2*(m*aux_ld + c) (the classifier's softmax statistics).
  * epi 8: out[n*ld + m] += alpha*acc (transposed like epi 0, accumulated
  * through element-wise TMA adds, so K is split across the SMs without
- * partial slabs; the decode projections). */
+ * partial slabs; the decode projections).  epi 10: SwiGLU of a W1/W3
+ * 16-row-interleaved A (rows [32c, 32c+16) = W1 rows [16c, 16c+16), the next
+ * 16 the W3 rows), written transposed: bf16 out[n*ld + f] = silu(h1) * h3 for
+ * feature f < M/2 (M a multiple of 32, K not split; the decode step's fused
+ * W1/W3 projection). */
 typedef struct ne_gemm_desc {
   const void* a; long long lda; int a_mn;
   const void* b; long long ldb; int b_mn;

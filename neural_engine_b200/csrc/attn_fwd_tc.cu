@@ -33,6 +33,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "ne_device.cuh"
 #include "ne_internal.h"
@@ -92,6 +93,10 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// T = __nv_bfloat16 (training: Q, K, V and P bf16) or __half (the token
+// loop's prefill over the fp16 KV cache: Q, K, V and P fp16); the output is
+// bf16 either way.
+template <typename T>
 __global__ void __launch_bounds__(TA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int S, int Hq, int Hkv, int Tmax,
@@ -124,8 +129,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const int q0 = qt * TA_BQ;
   const int n_keys = min(S, q0 + TA_BQ);                // causal: keys < q0 + 128
   const int n_kt = (n_keys + TA_BK - 1) / TA_BK;
-  constexpr uint32_t IDESC_S = umma_idesc_f16(TA_BQ, TA_BK, 1, 0, 0);
-  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, TA_HD, 1, 0, 1);
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  constexpr int FMT = kF16 ? 0 : 1;      // instruction-descriptor A/B format: 0 f16, 1 bf16
+  constexpr uint32_t IDESC_S = umma_idesc_f16(TA_BQ, TA_BK, FMT, 0, 0);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, TA_HD, FMT, 0, 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -287,7 +294,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const bool move = mx > m + 8.0f;
       const float corr = move ? exp2f(m - mx) : 1.0f;
       if (move) m = mx;
-      // pass 2: p = exp2(s - m) -> P (bf16, swizzled K-major rows), row sum
+      // pass 2: p = exp2(s - m) -> P (T, swizzled K-major rows), row sum
       float sum = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -301,8 +308,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           const float p1 = (key + 1 <= qpos && key + 1 < S)
                                ? exp2f(__uint_as_float(sr[h][i + 1]) * qscale_log2 - m) : 0.f;
           sum += p0 + p1;
-          const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
-          w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          if constexpr (kF16) {
+            const __half2 pk = __floats2half2_rn(p0, p1);
+            w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          } else {
+            const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
+            w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          }
         }
         // 32 keys = 4 chunks of 8 (16 bytes) in atom c / 64, chunk index (c % 64) / 8 + q
         const uint32_t atom = sP + (c >> 6) * TA_ATOM + row * 128;
@@ -389,18 +401,50 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 [rows, cols] row-major, 128-byte-swizzled boxes of 64 columns x box_rows.
-bool tmap_bf16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, int box_rows) {
+// 16-bit [rows, cols] row-major (bf16 or fp16), 128-byte-swizzled boxes of 64
+// columns x box_rows.
+bool tmap_16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, int box_rows,
+             CUtensorMapDataType dt) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+  return enc(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
+}
+
+}  // namespace
+
+namespace {
+
+template <typename T>
+cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, int Hkv, int hd,
+                      int Tmax, __nv_bfloat16* out, float* lse, int* status, cudaStream_t st) {
+  if (hd != TA_HD || Hq % Hkv) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return cudaErrorInvalidValue;
+  const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq, tk, tv;
+  if (!tmap_16(&tq, Q, (long long)B * S, (long long)Hq * hd, TA_BQ, dt) ||
+      !tmap_16(&tk, K, (long long)B * Hkv * Tmax, hd, TA_BK, dt) ||
+      !tmap_16(&tv, V, (long long)B * Hkv * Tmax, hd, 64, dt))
+    return cudaErrorInvalidValue;
+  static bool attr = false;   // one flag per instantiation
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  return launch_k(attn_fwd_tc_kernel<T>, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B), dim3(TA_THREADS),
+                  (size_t)TA_SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax, qscale_log2, out, lse, status);
 }
 
 }  // namespace
@@ -409,25 +453,13 @@ cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
                                int Tmax, __nv_bfloat16* out, float* lse, int* status,
                                cudaStream_t st) {
-  if (hd != TA_HD || Hq % Hkv) return cudaErrorInvalidValue;
-  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
-       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(out)) & 15)
-    return cudaErrorInvalidValue;
-  CUtensorMap tq, tk, tv;
-  if (!tmap_bf16(&tq, Q, (long long)B * S, (long long)Hq * hd, TA_BQ) ||
-      !tmap_bf16(&tk, K, (long long)B * Hkv * Tmax, hd, TA_BK) ||
-      !tmap_bf16(&tv, V, (long long)B * Hkv * Tmax, hd, 64))
-    return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  return launch_k(attn_fwd_tc_kernel, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B), dim3(TA_THREADS),
-                  (size_t)TA_SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax, qscale_log2, out, lse, status);
+  return launch_tc(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, lse, status, st);
+}
+
+cudaError_t launch_attn_fwd_tc_f16(const __half* Q, const __half* K, const __half* V, int B,
+                                   int S, int Hq, int Hkv, int hd, int Tmax,
+                                   __nv_bfloat16* out, int* status, cudaStream_t st) {
+  return launch_tc(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, nullptr, status, st);
 }
 
 }  // namespace ne

@@ -145,6 +145,12 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
         return launch_t<BN, EpiArgmaxT, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
       }
       break;
+    case EPI_SWIGLU_T:
+      if constexpr (kk && tr_ok && ch32) {
+        EpiSwiGLUT::Params p{(__nv_bfloat16*)c.out, c.ld};
+        return launch_t<BN, EpiSwiGLUT, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
+      }
+      break;
     case EPI_F32: {
       if constexpr (ch32) {
         if (sh.splits == 1 && stage_ok(c.out, c.ld, 4) &&
@@ -235,7 +241,8 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
 int pick_bn(const GemmCall& c) {
   if (c.bn) return c.bn;
   if (c.N <= 16)
-    return (c.epi == EPI_SWIGLU || c.epi == EPI_F32T_ADD || c.epi == EPI_ARGMAX_T) ? 32 : 16;
+    return (c.epi == EPI_SWIGLU || c.epi == EPI_F32T_ADD || c.epi == EPI_ARGMAX_T ||
+            c.epi == EPI_SWIGLU_T) ? 32 : 16;
   if (c.N <= 32) return 32;
   if (c.N <= 64) return 64;
   if (c.N <= 128) return 128;
@@ -263,7 +270,8 @@ bool gemm_pair_tiles(const GemmCall& c) {
     return !(e && e[0] == '0');
   }();
   return pair_on && pick_bn(c) == 256 && (c.max_ctas <= 0 || c.max_ctas >= 2) && c.M >= 512 &&
-         c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T;
+         c.epi != EPI_F32T && c.epi != EPI_F32T_ADD && c.epi != EPI_ARGMAX_T &&
+         c.epi != EPI_SWIGLU_T;
 }
 
 int gemm_pick_splits(const GemmCall& c, int num_sms) {
@@ -321,6 +329,8 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
     return cudaErrorInvalidValue;
   if (c.epi == EPI_ARGMAX_T && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u)))
     return cudaErrorInvalidValue;
+  // the fused SwiGLU pairs rows 32c + i and 32c + 16 + i of one unsplit tile
+  if (c.epi == EPI_SWIGLU_T && (c.M % 32 != 0 || !c.out || c.splits > 1)) return cudaErrorInvalidValue;
   if (c.epi == EPI_F32_STATS && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u) ||
                                  c.aux_ld < (c.N + 31) / 32))
     return cudaErrorInvalidValue;

@@ -144,6 +144,39 @@ struct EpiArgmaxT {
   }
 };
 
+// Swap-AB W1/W3 projection with the SwiGLU fused (decode, K not split): the
+// accumulator rows are the 16-row-interleaved W13 features -- rows
+// [32c, 32c+16) hold h1 of features [16c, 16c+16), rows [32c+16, 32c+32) their
+// h3 -- and its columns are batch rows.  A warp's lanes hold 32 consecutive
+// rows starting at a multiple of 32, so lane i < 16 has h1 and lane i + 16 has
+// h3 of feature 16c + i.  Per pair of columns, lanes < 16 finish the even
+// column and lanes >= 16 the odd one, each taking the value it lacks from its
+// partner (one exchange):
+//   gate[n * ld + f] = bf16( silu(h1) * h3 ),  silu(x) = x * (1 / (1 + exp(-x)))
+// (generate.py:93-94,190; the same expression as swiglu_split_kernel).
+struct EpiSwiGLUT {
+  struct Params { __nv_bfloat16* gate; long long ld; };
+  template <int CH>
+  __device__ static void apply(const Params& p, int m, int n0, const float (&v)[CH], int, int M,
+                               int N) {
+    static_assert(CH % 2 == 0, "column pairs");
+    const int lane = threadIdx.x & 31;
+    const bool hi = lane >= 16;
+    const int f = (m >> 5) * 16 + (lane & 15);
+    __nv_bfloat16* const col = p.gate + f;
+#pragma unroll
+    for (int j = 0; j < CH; j += 2) {
+      const float give = hi ? v[j] : v[j + 1];
+      const float got = __shfl_xor_sync(0xffffffffu, give, 16);
+      const float h1 = hi ? got : v[j];
+      const float h3 = hi ? v[j + 1] : got;
+      const int n = n0 + j + (hi ? 1 : 0);
+      if (m < M && n < N)
+        col[(long long)n * p.ld] = __float2bfloat16_rn(h1 * (1.0f / (1.0f + expf(-h1))) * h3);
+    }
+  }
+};
+
 // fp32 store, row-major:  out[split*split_stride + m*ld + n]
 struct EpiF32 {
   struct Params { float* out; long long ld; long long split_stride; };

@@ -43,9 +43,9 @@ namespace {
 // Decode-GEMM helper (weight-major, batch <= 256 rows in one N tile):
 //   out[rows][n_out] += alpha * act[rows, K] . W[n_out, K]^T
 // through the TMA add, split-K across the SMs (the partial sums meet in L2).
-ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
-                      const __nv_bfloat16* act, long long ld_act, int rows, float* out,
-                      float alpha) {
+GemmCall decode_call(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
+                     const __nv_bfloat16* act, long long ld_act, int rows, float* out,
+                     float alpha) {
   GemmCall c;
   c.A = W; c.lda = K; c.M = n_out;
   c.B = act; c.ldb = ld_act; c.N = rows;
@@ -66,6 +66,41 @@ ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
   }();
   if (rows > bn_cfg) c.bn = bn_cfg;
   c.splits = gemm_pick_splits(c, ctx->num_sms);
+  return c;
+}
+
+ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
+                      const __nv_bfloat16* act, long long ld_act, int rows, float* out,
+                      float alpha) {
+  const GemmCall c = decode_call(ctx, W, n_out, K, act, ld_act, rows, out, alpha);
+  NE_LAUNCH(gemm_run(c, ctx->d_status, ctx->st));
+  return NE_OK;
+}
+
+// The W1/W3 projection of a decode step writes the SwiGLU gate directly
+// (EPI_SWIGLU_T) when its tiles fill the SMs without splitting K (B > 128 on
+// 148 SMs): no fp32 h1/h3 sums in HBM and no separate SwiGLU kernel.
+// NE_DECODE_SWIGLU=0 keeps the split projection + swiglu_split pair.
+bool decode_swiglu_fused(ne_ctx* ctx, int rows) {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_DECODE_SWIGLU");
+    return !(e && e[0] == '0');
+  }();
+  const ne_model_cfg& m = ctx->cfg;
+  if (!on || m.hidden % 16) return false;
+  const GemmCall c =
+      decode_call(ctx, ctx->L[0].w13, 2 * m.hidden, m.dim, ctx->xn, m.dim, rows, ctx->part, 1.f);
+  return c.splits == 1;
+}
+
+ne_status gemm_decode_swiglu(ne_ctx* ctx, const __nv_bfloat16* W13, const __nv_bfloat16* act,
+                             long long ld_act, int rows, __nv_bfloat16* gate) {
+  const ne_model_cfg& m = ctx->cfg;
+  GemmCall c = decode_call(ctx, W13, 2 * m.hidden, m.dim, act, ld_act, rows, nullptr, 1.f);
+  c.epi = EPI_SWIGLU_T;
+  c.out = gate;
+  c.ld = m.hidden;
+  c.splits = 1;
   NE_LAUNCH(gemm_run(c, ctx->d_status, ctx->st));
   return NE_OK;
 }
@@ -148,9 +183,10 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
                                  ctx->x, ctx->xn, B, ctx->d_status, ctx->st));
   prof_mark(ctx, 9);
   const size_t kv_layer = ctx->layer_kv_elems();
-  // ctx->part holds the QKV and W1/W3 sums (zero between uses: their consumers
-  // clear what they read); the Wo and W2 projections add alpha * acc straight
-  // into the fp32 residual stream x.
+  const bool swiglu_fused = decode_swiglu_fused(ctx, B);
+  // ctx->part holds the QKV and (unless fused) W1/W3 sums (zero between uses:
+  // their consumers clear what they read); the Wo and W2 projections add
+  // alpha * acc straight into the fp32 residual stream x.
   for (int l = 0; l < m.n_layers; ++l) {
     const LayerW& w = ctx->L[l];
     if ((s = gemm_decode(ctx, w.wqkv, qkv_dim, D, ctx->xn, D, B, ctx->part, 1.f)) != NE_OK)
@@ -173,10 +209,16 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
     NE_LAUNCH(launch_resid_rmsnorm(ctx->x, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, ctx->xn, B,
                                    ctx->st));
     prof_mark(ctx, 4);
-    if ((s = gemm_decode(ctx, w.w13, 2 * F, D, ctx->xn, D, B, ctx->part, 1.f)) != NE_OK) return s;
-    prof_mark(ctx, 5);
-    NE_LAUNCH(launch_swiglu_split(ctx->part, 1, 0, B, F, ctx->gate, ctx->st, 1));
-    prof_mark(ctx, 6);
+    if (swiglu_fused) {
+      if ((s = gemm_decode_swiglu(ctx, w.w13, ctx->xn, D, B, ctx->gate)) != NE_OK) return s;
+      prof_mark(ctx, 5);
+    } else {
+      if ((s = gemm_decode(ctx, w.w13, 2 * F, D, ctx->xn, D, B, ctx->part, 1.f)) != NE_OK)
+        return s;
+      prof_mark(ctx, 5);
+      NE_LAUNCH(launch_swiglu_split(ctx->part, 1, 0, B, F, ctx->gate, ctx->st, 1));
+      prof_mark(ctx, 6);
+    }
     if ((s = gemm_decode(ctx, w.w2, D, F, ctx->gate, F, B, ctx->x, m.res_alpha)) != NE_OK) return s;
     prof_mark(ctx, 7);
     const float* next_g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
@@ -243,6 +285,15 @@ ne_status enqueue_prefill(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, in
   const size_t kv_layer = ctx->layer_kv_elems();
   const size_t kv_seq = (size_t)Hkv * ctx->max_seq * hd;
   ne_status s;
+  // A prompt that starts at position 0 with head_dim 128 runs its attention on
+  // the tcgen05 kernel (fp16 operands, TMEM accumulators); a continuation
+  // (pos0 > 0, keys before the chunk already cached) and other head sizes on
+  // the mma.sync kernel.  NE_PREFILL_TC=0 keeps the mma.sync kernel throughout.
+  static const bool tc_on = [] {
+    const char* e = getenv("NE_PREFILL_TC");
+    return !(e && e[0] == '0');
+  }();
+  const bool tc_attn = tc_on && pos0 == 0 && hd == 128;
   const int seqs_per_chunk = std::max(1, ctx->pf_rows / S);
   for (int b0 = 0; b0 < B; b0 += seqs_per_chunk) {
     const int nb = std::min(seqs_per_chunk, B - b0);
@@ -261,8 +312,12 @@ ne_status enqueue_prefill(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, in
                                 m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                                 m.qk_eps, ctx->rope_cs, ctx->pf_q, 1, kc, vc, ctx->max_seq,
                                 ctx->d_status, ctx->st));
-      NE_LAUNCH(launch_prefill_attn(ctx->pf_q, kc, vc, nb, S, pos0, Hq, Hkv, hd, ctx->max_seq,
-                                    ctx->pf_o, ctx->st));
+      if (tc_attn)
+        NE_LAUNCH(launch_attn_fwd_tc_f16(ctx->pf_q, kc, vc, nb, S, Hq, Hkv, hd, ctx->max_seq,
+                                         ctx->pf_o, ctx->d_status, ctx->st));
+      else
+        NE_LAUNCH(launch_prefill_attn(ctx->pf_q, kc, vc, nb, S, pos0, Hq, Hkv, hd, ctx->max_seq,
+                                      ctx->pf_o, ctx->st));
       if ((s = gemm_tokens(ctx, ctx->pf_o, q_dim, rows, w.wo, D, q_dim, EPI_RESID, ctx->pf_x, D,
                            m.res_alpha)) != NE_OK)
         return s;
@@ -706,7 +761,7 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
 
 NE_API ne_status ne_gemm(ne_ctx* ctx, const ne_gemm_desc* d) {
   if (!ctx || !d || !d->a || !d->b || !d->out || d->M <= 0 || d->N <= 0 || d->K <= 0 ||
-      d->epi < 0 || d->epi > 8)
+      d->epi < 0 || (d->epi > 8 && d->epi != EPI_SWIGLU_T))
     return NE_ERR_INVALID;
   if (d->K % 64) return fail(ctx, NE_ERR_UNSUPPORTED, "K must be a multiple of 64");
   if (d->a_mn && !d->b_mn) return fail(ctx, NE_ERR_UNSUPPORTED, "MN-major A needs MN-major B");

@@ -19,6 +19,7 @@ enum GemmEpi : int {
   EPI_F32_STATS = 7,   // fp32 row-major + per-32-column (max, sum exp) into aux1 [m][aux_ld]
   EPI_F32T_ADD = 8,    // swap-AB: out[n][m] += alpha * acc through the TMA add (split-K safe)
   EPI_ARGMAX_T = 9,    // swap-AB: atomicMax of (logit, ~m) keys into aux1 [N] (greedy LM head)
+  EPI_SWIGLU_T = 10,   // swap-AB, K not split: bf16 out[n][m/2] = silu(h1)*h3 of a W1/W3 16-row-interleaved A
 };
 
 struct GemmCall {
@@ -142,6 +143,11 @@ cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
                                int Tmax, __nv_bfloat16* out, float* lse, int* status,
                                cudaStream_t st);
+// The same kernel over fp16 operands (the token loop's prompt pass: fp16 Q and
+// the fp16 KV cache, K / V rows [b][kv_head][Tmax][hd]); positions start at 0.
+cudaError_t launch_attn_fwd_tc_f16(const __half* Q, const __half* K, const __half* V, int B,
+                                   int S, int Hq, int Hkv, int hd, int Tmax,
+                                   __nv_bfloat16* out, int* status, cudaStream_t st);
 // Causal GQA attention backward; dQ and dK leave through the RoPE and QK-norm
 // backward (qn / kn may be NULL: no QK-norm; the raw projection qkv_raw gives
 // the pre-norm rows) and dQ, dK, dV are written bf16 into dqkv [B*S][qkv_dim];

@@ -301,3 +301,26 @@ def test_gemm_transposed_accumulate(eng, M, N, K):
     eng.sync()
     ref = base.double() + 0.5 * _ref(a, b).T
     assert (out.cpu().double() - ref).abs().max().item() <= 0.5 * _tol(a, b, K) + 1e-5
+
+
+@pytest.mark.parametrize("F,N,K", [(3072, 256, 1024), (256, 200, 128), (512, 77, 192)])
+def test_gemm_swiglu_transposed_epilogue(eng, F, N, K):
+    """epi 10 (the decode step's fused W1/W3 projection): A = W1/W3 interleaved
+    in 16-row blocks, B = the batch; gate[n, f] = silu(h1) * h3 written
+    transposed (bf16), one unsplit pass."""
+    w1, w3 = _bf16((F, K), 51, 0.1), _bf16((F, K), 52, 0.1)
+    w13 = torch.empty((2 * F, K), dtype=torch.bfloat16)
+    for c in range(F // 16):
+        w13[32 * c:32 * c + 16] = w1[16 * c:16 * c + 16]
+        w13[32 * c + 16:32 * c + 32] = w3[16 * c:16 * c + 16]
+    x = _bf16((N, K), 53)
+    gate = torch.full((N, F), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dw, dx = w13.cuda(), x.cuda()
+    eng.gemm(dw.data_ptr(), K, 2 * F, dx.data_ptr(), K, N, K, 10, gate.data_ptr(), F)
+    eng.sync()
+    h1, h3 = _ref(x, w1), _ref(x, w3)
+    ref = h1 * (1.0 / (1.0 + torch.exp(-h1))) * h3
+    got = gate.cpu().double()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs().max().item()
+    assert err <= 2 ** -8 * ref.abs().max().item() + 1e-3, err
