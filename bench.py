@@ -64,6 +64,12 @@ def parse():
     ap.add_argument("--train-only", action="store_true",
                     help="skip the decode headline; print the training object alone "
                          "(profiling runs)")
+    ap.add_argument("--profile-layers", type=int, default=0,
+                    help="with --train-only: a Qwen3-0.6B-width model of this many layers "
+                         "(per-launch kernel shapes unchanged, a few GB on the device) for "
+                         "ncu captures of the layer kernels; not a bench number")
+    ap.add_argument("--profile-vocab", type=int, default=0,
+                    help="with --profile-layers: vocabulary of the profiling model")
     ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
     ap.add_argument("--train-seq", type=int, default=256)
     ap.add_argument("--dp-mode", choices=("zero1", "allreduce"), default="zero1",
@@ -193,6 +199,14 @@ def attention_bytes(B: int, T: int) -> float:
     return B * (HKV * T * HD * 2 * 2 + HQ * HD * 4 + HQ * HD * 2)
 
 
+# DRAM bytes (read + write) per algorithmic byte of the decode attention: one
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of a launch at
+# B 64, context 514 -- 139,092,736 B against 135,528,448 algorithmic bytes.
+# Both grow in proportion to B x T, so the full launch's traffic is this ratio
+# times its algorithmic bytes (profiles/decode_launches_qwen3_b256.md).
+ATTN_TRAFFIC_RATIO = 139092736 / 135528448
+
+
 def gemm_bytes(group: str, B: int) -> float:
     n_out, k = {"gemm_qkv": ((HQ + 2 * HKV) * HD, D), "gemm_wo": (D, HQ * HD),
                 "gemm_w13": (2 * F, D), "gemm_w2": (D, F), "gemm_lm_head": (V, D)}[group]
@@ -310,6 +324,15 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- training
+def profile_cfg(args):
+    """Qwen3-0.6B layer width with fewer layers / a smaller vocabulary (ncu
+    captures of the per-layer training kernels on a small case)."""
+    import dataclasses
+    import neural_engine_b200 as ne
+    return dataclasses.replace(ne.QWEN3_06B, n_layers=args.profile_layers,
+                               vocab=args.profile_vocab or ne.QWEN3_06B.vocab)
+
+
 def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3, model="qwen3_06b"):
     """torch-CPU float32 fwd + bwd of one sequence of S tokens (the oracle's
     restatement of the training forward), all host cores.  Returns tokens/s."""
@@ -336,6 +359,8 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     import neural_engine_b200 as ne
     stories = model == "stories110m"
     cfg = ne.STORIES110M if stories else ne.QWEN3_06B
+    if not stories and args.profile_layers > 0:
+        cfg = profile_cfg(args)
     B = B or args.train_batch
     S = S or args.train_seq
     eng = ne.Engine(cfg, device=local)
@@ -401,7 +426,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
         te = float(tt.item())
     eng.close()
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.n_layers in (12, 28):
         v, dt = cpu_train_sample(layers, rf, emb, qk, S=S, model=model)
         cpu = {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                "sample": f"torch-CPU float32 fwd+bwd of the oracle's "
@@ -412,7 +437,9 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     return {"metric": metric, "value": round(value, 1), "unit": UNIT,
             "ms_per_step": round(ms_step, 3), "steps": args.steps, "warmup": args.warmup,
             "scaling": "weak", "dtype": "bf16",
-            "config": {"workload": f"{model}_train", "batch_per_gpu": B, "seq_len": S,
+            "config": {"workload": (f"{model}_train" if cfg.n_layers in (12, 28) else
+                                    f"profiling case: {cfg.n_layers} layers, vocab {cfg.vocab}"),
+                       "batch_per_gpu": B, "seq_len": S,
                        "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
                        "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
                        "parallelism": (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
@@ -508,7 +535,10 @@ def main():
     import neural_engine_b200 as ne
     cfg = ne.QWEN3_06B
     B, P, G = args.batch, args.prompt, args.gen
-    layers, rf, emb, qk = host_weights(seed=0)
+    if args.profile_layers > 0 and not args.train_only:
+        raise SystemExit("--profile-layers needs --train-only")
+    layers, rf, emb, qk = host_weights(seed=0, cfg=profile_cfg(args) if args.profile_layers > 0
+                                       else None)
     if args.train_only:
         train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
         if rank == 0:
@@ -577,6 +607,10 @@ def main():
                 "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
                 "peak_kind": peak_kind, "bytes_per_launch": dom_bytes,
                 "ms_per_launch": round(dom_ms, 4)}
+    if roof is not None and dom == "decode_attention":
+        roof["traffic"] = round(ATTN_TRAFFIC_RATIO * dom_bytes)
+        roof["traffic_source"] = ("ncu DRAM read + write bytes of one launch at B 64, context "
+                                  "514, scaled by the algorithmic bytes (B x T)")
     if roof is not None and dom == "decode_attention" and rank == 0:
         # the same bytes through the same data path with no arithmetic
         rc_ms = read_ceiling(int(dom_bytes))
