@@ -378,6 +378,18 @@ struct EpiHasBox2 { static constexpr bool value = false; };
 template <class E>
 struct EpiHasBox2<E, decltype(void(E::kCols2))> { static constexpr bool value = true; };
 
+// A functor with a `Pre` type reads global memory for each chunk: preload()
+// issues the loads of a chunk into registers one chunk ahead of its stage(),
+// so their latency overlaps the current chunk's TMEM read, arithmetic and
+// store instead of stalling every chunk.
+template <class E, class = void>
+struct EpiPre { static constexpr bool value = false; struct type {}; };
+template <class E>
+struct EpiPre<E, decltype(void(sizeof(typename E::Pre)))> {
+  static constexpr bool value = true;
+  using type = typename E::Pre;
+};
+
 // Write this lane's row (N 16-bit or 32-bit values, 32, 64 or 128 bytes) of a
 // 32-row box at `box`, in the layout of the TMA swizzle that matches the row
 // size (the 16-byte chunk index XORed with address bits 7.. of the row start):
@@ -546,20 +558,24 @@ struct EpiSwiGLUBwdS {
     if (m >= M || n0 >= N) return;
     prefetch_row_l2(p.h13 + (long long)m * 2 * p.F + 2 * n0, 4 * min(ncols, N - n0));
   }
-  template <int CH>
-  __device__ static void stage(const Params& p, int m, int n0, const float (&v)[CH],
-                               Out (&o)[kCols], int M, int N) {
-    static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
-    // 128 contiguous bytes: (h1 x16 | h3 x16) for each of the chunk's two 16-feature blocks
-    uint4 r[8];
+  // 128 contiguous bytes of the chunk's row: (h1 x16 | h3 x16) for each of its
+  // two 16-feature blocks, loaded one chunk ahead
+  struct Pre { uint4 r[8]; };
+  __device__ static void preload(const Params& p, int m, int n0, int M, int N, Pre& pr) {
     if (m < M && n0 < N) {
       const uint4* src = reinterpret_cast<const uint4*>(p.h13 + (long long)m * 2 * p.F + 2 * n0);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) r[q] = src[q];
+      for (int q = 0; q < 8; ++q) pr.r[q] = src[q];
     } else {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) r[q] = make_uint4(0, 0, 0, 0);
+      for (int q = 0; q < 8; ++q) pr.r[q] = make_uint4(0, 0, 0, 0);
     }
+  }
+  template <int CH>
+  __device__ static void stage(const Params& p, int m, int n0, const float (&v)[CH],
+                               Out (&o)[kCols], int M, int N, const Pre& pr) {
+    static_assert(CH == 32, "SwiGLU backward epilogue needs 32-column chunks");
+    const uint4 (&r)[8] = pr.r;
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
@@ -838,8 +854,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int m = mt * TILE_M + row0 + row_in_tile;
+      [[maybe_unused]] typename EpiPre<Epi>::type pre_cur, pre_nxt;
+      if constexpr (EpiPre<Epi>::value) Epi::preload(ep, m, nt * BN + chunk0, sh.M, sh.N, pre_cur);
 #pragma unroll 1
       for (int c = chunk0; c < BN; c += 2 * CH) {
+        if constexpr (EpiPre<Epi>::value) {
+          if (c + 2 * CH < BN) Epi::preload(ep, m, nt * BN + c + 2 * CH, sh.M, sh.N, pre_nxt);
+        }
         float v[CH];
         if constexpr (CH == 32) {
           uint32_t r[32];
@@ -901,6 +922,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             typename Epi::Out2 o2[Epi::kCols2];
             Epi::template stage<CH>(ep, m, n0, v, o, o2, sh.M, sh.N);
             stage_row(sbuf + GEMM_STAGE_BOX2, lane, o2);
+          } else if constexpr (EpiPre<Epi>::value) {
+            Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N, pre_cur);
+            pre_cur = pre_nxt;
           } else {
             Epi::template stage<CH>(ep, m, n0, v, o, sh.M, sh.N);
           }
