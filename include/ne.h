@@ -120,6 +120,14 @@ NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_in
  * max_batch sequences of up to max_seq positions. */
 NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq);
 
+/* Start a new set of sequences in the allocated cache: clears the KV cache and
+ * the decode state (position and step counters, accumulators) to what
+ * ne_kv_alloc leaves, without freeing or reallocating anything.  Enqueued on
+ * the context's stream after the work already there.  The reference builds a
+ * fresh cache per generate() call (tools/generate.py:125-128); this is that
+ * step for a long-lived context. */
+NE_API ne_status ne_kv_reset(ne_ctx* ctx);
+
 /* Process the prompt h_tokens [B, S] (positions pos0 .. pos0+S-1 of every
  * sequence) in one causal pass, filling the KV cache.  Writes the next token
  * (argmax, generate.py:200) into h_next [B] and, if non-NULL, the last

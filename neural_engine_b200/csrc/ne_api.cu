@@ -615,6 +615,25 @@ NE_API ne_status ne_kv_alloc(ne_ctx* ctx, int max_batch, int max_seq) {
   return NE_OK;
 }
 
+NE_API ne_status ne_kv_reset(ne_ctx* ctx) {
+  if (!ctx) return NE_ERR_INVALID;
+  if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
+  NE_CUDA(cudaSetDevice(ctx->device));
+  const ne_model_cfg& m = ctx->cfg;
+  const size_t B = ctx->max_batch;
+  const size_t kv = ctx->layer_kv_elems() * m.n_layers;
+  const size_t part = B * std::max(ctx->qkv_dim(), 2 * m.hidden);
+  // the same state ne_kv_alloc leaves, enqueued after the work already on the
+  // context's stream; buffers and captured graphs stay as they are
+  NE_CUDA(cudaMemsetAsync(ctx->kcache, 0, kv * sizeof(__half), ctx->st));
+  NE_CUDA(cudaMemsetAsync(ctx->vcache, 0, kv * sizeof(__half), ctx->st));
+  NE_CUDA(cudaMemsetAsync(ctx->state, 0, 2 * sizeof(int), ctx->st));
+  NE_CUDA(cudaMemsetAsync(ctx->part, 0, part * sizeof(float), ctx->st));
+  NE_CUDA(cudaMemsetAsync(ctx->attn_cnt, 0, B * m.kv_heads * sizeof(int), ctx->st));
+  NE_CUDA(cudaMemsetAsync(ctx->argmax_keys, 0, B * sizeof(unsigned long long), ctx->st));
+  return NE_OK;
+}
+
 NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, int pos0,
                                    int32_t* d_next) {
   if (!ctx || !d_tokens || !d_next || B <= 0 || S <= 0 || pos0 < 0) return NE_ERR_INVALID;

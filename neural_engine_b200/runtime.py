@@ -24,7 +24,7 @@ STATUS_NAMES = {0: "NE_OK", 1: "NE_ERR_INVALID", 2: "NE_ERR_CUDA", 3: "NE_ERR_OO
 # every entry point include/ne.h declares
 EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "ne_get_cfg",
             "ne_version", "ne_set_layer_weights", "ne_set_global_weights", "ne_load_ckpt_v4",
-            "ne_kv_alloc", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
+            "ne_kv_alloc", "ne_kv_reset", "ne_prefill", "ne_decode_step", "ne_generate", "ne_prefill_device",
             "ne_decode_loop_device", "ne_gemm_device", "ne_gemm_device_ex",
             "ne_decode_kernels_per_step", "ne_get_stream", "ne_profile_decode_step",
             "ne_gemm_splitk_noalloc", "ne_train_alloc", "ne_train_set_masters",
@@ -158,6 +158,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_sdpa_fwd_device.argtypes = [P, P, P, P, I, I, P, P]
     lib.ne_train_set_vocab_map.argtypes = [P, P, I]
     lib.ne_kv_alloc.argtypes = [P, I, I]
+    lib.ne_kv_reset.argtypes = [P]
     lib.ne_prefill.argtypes = [P, P, I, I, I, P, P]
     lib.ne_decode_step.argtypes = [P, P, I, I, P, P]
     lib.ne_generate.argtypes = [P, P, I, I, I, P]
@@ -317,6 +318,10 @@ class Engine:
     def kv_alloc(self, max_batch: int, max_seq: int):
         self._check(self.lib.ne_kv_alloc(self._ctx, int(max_batch), int(max_seq)))
         self.max_batch, self.max_seq = int(max_batch), int(max_seq)
+
+    def kv_reset(self):
+        """Clear the KV cache and decode state for a new set of sequences."""
+        self._check(self.lib.ne_kv_reset(self._ctx))
 
     def prefill(self, tokens: np.ndarray, pos0: int = 0, return_logits: bool = False):
         tokens = np.ascontiguousarray(np.atleast_2d(tokens), dtype=np.int32)

@@ -133,6 +133,47 @@ def test_decode_only_matches_prefill_path():
     e.close()
 
 
+def test_kv_reset_starts_new_sequences():
+    """ne_kv_reset on a long-lived context: refused before ne_kv_alloc; after a
+    prefill and three decode steps, a reset and the same prompt and tokens
+    again give the same logits (same kernels on the same inputs: only the
+    order of split-K additions may differ), checked against the oracle too."""
+    import neural_engine_b200 as ne
+    cfg = _tiny_cfg(qk_norm=True, theta=1e6, eps=1e-6)
+    layers, rf, emb, qk = om.init_weights(cfg, seed=35, std=0.08, bf16=True)
+    prompt = om.prompt_tokens(cfg.vocab, 11, 36, batch=2)
+    fresh = ne.Engine(cfg)
+    with pytest.raises(ne.NeError) as err:
+        fresh.kv_reset()
+    assert err.value.status == 8   # NE_ERR_STATE
+    fresh.close()
+    e = _engine(cfg, layers, rf, emb, qk, 2, 16)
+
+    def run():
+        nxt, lg = e.prefill(prompt, 0, return_logits=True)
+        out = [lg]
+        feed = [nxt.copy()]
+        for i in range(3):
+            nxt, lg = e.decode_step(feed[-1], 11 + i, return_logits=True)
+            out.append(lg)
+            feed.append(nxt.copy())
+        return out, feed
+
+    first, toks = run()
+    e.kv_reset()
+    again, _ = run()
+    for i, (a, b) in enumerate(zip(first, again)):
+        rel = np.linalg.norm(a - b) / np.linalg.norm(a)
+        assert rel <= 1e-4, f"step {i}: rel-L2 {rel:.3e} after the reset"
+    dec = od.Decoder(cfg, layers, rf, emb, qk, batch=2, max_seq=16)
+    ref = dec.forward(prompt.astype(np.int64), 0, last_only=True)
+    _check_logits(again[0], ref, "prefill after reset")
+    for i in range(3):
+        ref = dec.forward(toks[i][:, None].astype(np.int64), 11 + i, last_only=True)
+        _check_logits(again[i + 1], ref, f"decode step {i} after reset")
+    e.close()
+
+
 def test_generate_greedy_free_running():
     """ne_generate (prefill + graph-replayed decode) vs the oracle's greedy loop."""
     cfg = _tiny_cfg(qk_norm=True, theta=1e6, eps=1e-6)
