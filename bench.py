@@ -40,7 +40,9 @@ METRIC = "Qwen3-0.6B decode tokens/sec (greedy, 512-token prompt, 256 new tokens
 TRAIN_METRIC = "Qwen3-0.6B training tokens/sec (fwd + bwd + AdamW, seq 256, batch 16 per GPU)"
 UNIT = "tokens/s"
 
-# Qwen3-0.6B sizes used by the byte model (SURVEY-style algorithmic counts)
+# Qwen3-0.6B sizes (models/qwen3_06b.h:6-16 of the reference) for the byte and
+# FLOP models below: algorithmic counts, i.e. what the step must read, write or
+# multiply at least once, independent of how the kernels tile it
 L, D, F, HQ, HKV, HD, V = 28, 1024, 3072, 16, 8, 128, 151936
 PARAMS = L * ((HQ * HD) * D + 2 * (HKV * HD) * D + D * (HQ * HD) + 3 * F * D + 2 * D) + D + V * D
 
@@ -203,7 +205,7 @@ def attention_bytes(B: int, T: int) -> float:
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of a launch at
 # B 64, context 514 -- 139,092,736 B against 135,528,448 algorithmic bytes.
 # Both grow in proportion to B x T, so the full launch's traffic is this ratio
-# times its algorithmic bytes (profiles/decode_launches_qwen3_b256.md).
+# times its algorithmic bytes.
 ATTN_TRAFFIC_RATIO = 139092736 / 135528448
 
 
@@ -245,19 +247,21 @@ def read_ceiling(nbytes: int, iters: int = 10) -> float:
     return ts[len(ts) // 2]
 
 
-def cpu_decode_sample(layers, rms_final, embed, qk, B=8, steps=12, prompt=512, seed=5):
+def cpu_decode_sample(layers, rms_final, embed, qk, B=256, steps=4, prompt=512, seed=5):
     """Time the oracle's numpy token loop (restated from the reference's
-    tools/generate.py) on the host cores: B sequences, KV cache pre-filled with
-    `prompt` positions, `steps` greedy decode steps.  Returns tokens/s."""
+    tools/generate.py) on every host core: B sequences, KV cache pre-filled
+    with `prompt` positions, `steps` greedy decode steps after one untimed
+    step.  Returns (tokens/s, seconds, BLAS threads)."""
     from oracle import decode as od
     from oracle import model as om
+    threads = host_threads()
     cfg = om.QWEN3_06B
     dec = od.Decoder(cfg, layers, rms_final, embed, qk, batch=B, max_seq=prompt + steps + 1)
     rng = np.random.default_rng(seed)
-    dec.k_cache[:, :, :, :prompt] = rng.standard_normal(dec.k_cache[:, :, :, :prompt].shape,
-                                                        dtype=np.float32)
-    dec.v_cache[:, :, :, :prompt] = rng.standard_normal(dec.v_cache[:, :, :, :prompt].shape,
-                                                        dtype=np.float32)
+    for l in range(cfg.n_layers):
+        dec.k_cache[l, :, :, :prompt] = rng.standard_normal(
+            (B, cfg.kv_heads, prompt, cfg.head_dim), dtype=np.float32)
+        dec.v_cache[l, :, :, :prompt] = dec.k_cache[l, :, :, :prompt]
     tok = rng.integers(0, cfg.vocab, size=(B, 1))
     dec.forward(tok, prompt, last_only=True)          # warm caches / BLAS threads
     t0 = time.perf_counter()
@@ -265,7 +269,7 @@ def cpu_decode_sample(layers, rms_final, embed, qk, B=8, steps=12, prompt=512, s
         lg = dec.forward(tok, prompt + 1 + i, last_only=True)
         tok = np.argmax(lg, -1)[:, None]
     dt = time.perf_counter() - t0
-    return B * steps / dt, dt
+    return B * steps / dt, dt, threads
 
 
 def host_weights(seed=0, cfg=None):
@@ -293,31 +297,70 @@ def host_weights(seed=0, cfg=None):
 
 
 # ----------------------------------------------------------------- reference arm
+_THREAD_LIMITS = []
+
+
+def host_threads() -> int:
+    """Give the host's BLAS and torch every core, whatever OMP_NUM_THREADS the
+    launcher set (torchrun sets 1 per process for nproc > 1), and return the
+    BLAS thread count now in effect."""
+    import threadpoolctl
+    n = os.cpu_count() or 1
+    _THREAD_LIMITS.append(threadpoolctl.threadpool_limits(limits=n))
+    try:
+        import torch
+        torch.set_num_threads(n)
+    except Exception:
+        pass
+    info = [i.get("num_threads", 0) for i in threadpoolctl.threadpool_info()
+            if i.get("user_api") == "blas"]
+    return max(info) if info else n
+
+
 def run_reference(args):
+    """The reference's CPU token loop (the oracle's numpy restatement of
+    tools/generate.py:113-228) on the host cores, on this arm's workload: each
+    step is one greedy decode step of all `--batch` sequences over a KV cache
+    pre-filled with `--prompt` positions.  Rank 0 alone runs it."""
     rank, _, world = dist_env()
     if rank != 0:
         return
+    threads = host_threads()
+    from oracle import decode as od
     from oracle import model as om
     cfg = om.QWEN3_06B
     layers, rf, emb, qk = om.init_weights(cfg, seed=0, bf16=True)
-    B, per_step = 16, 4
-    vals = []
+    B, P = args.batch, args.prompt
+    dec = od.Decoder(cfg, layers, rf, emb, qk, batch=B, max_seq=P + 2)
+    rng = np.random.default_rng(5)
+    # the attention's cost does not depend on the cached values: fill by layer
+    for l in range(cfg.n_layers):
+        dec.k_cache[l, :, :, :P] = rng.standard_normal((B, cfg.kv_heads, P, cfg.head_dim),
+                                                       dtype=np.float32)
+        dec.v_cache[l, :, :, :P] = dec.k_cache[l, :, :, :P]
+    tok = rng.integers(0, cfg.vocab, size=(B, 1))
+    ts = []
     for i in range(args.warmup + args.steps):
-        v, _ = cpu_decode_sample(layers, rf, emb, qk, B=B, steps=per_step, prompt=args.prompt,
-                                 seed=100 + i)
+        t0 = time.perf_counter()
+        lg = dec.forward(tok, P, last_only=True)
+        tok = np.argmax(lg, -1)[:, None]
         if i >= args.warmup:
-            vals.append(v)
-    value = statistics.mean(vals)
-    cores = os.cpu_count()
-    sample = (f"oracle numpy port of tools/generate.py, Qwen3-0.6B, {B} sequences, KV cache "
-              f"pre-filled with {args.prompt} positions, {per_step} greedy steps per step")
+            ts.append(time.perf_counter() - t0)
+    sec = statistics.mean(ts)
+    value = B / sec
+    sample = (f"oracle numpy port of tools/generate.py, Qwen3-0.6B, {B} sequences, one greedy "
+              f"decode step per timed step at context {P} ({threads} BLAS threads)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * B * per_step / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sec,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": "qwen3_06b_decode", "model": "Qwen3-0.6B",
-                       "batch_per_gpu": B, "prompt_len": args.prompt, "gen_tokens": per_step},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                       "batch_per_gpu": B, "prompt_len": P, "gen_tokens": args.gen,
+                       "kv_cache": "fp32 (generate.py:128-129)"},
+            "extrapolated_from": (f"B={B} x 1 greedy step per timed step at context {P}; the "
+                                  f"GPU arm decodes {args.gen} steps at contexts {P}-"
+                                  f"{P + args.gen - 1}"),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -339,14 +382,14 @@ def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3, model="qwen3_06b"):
     import torch
     from oracle import model as om
     from oracle import train as ot
-    torch.set_num_threads(os.cpu_count() or 1)
+    threads = host_threads()
     cfg = om.PRESETS[model]
     tok = np.random.default_rng(7).integers(0, cfg.vocab, size=(1, S + 1))
     t0 = time.perf_counter()
     for _ in range(reps):
         ot.loss_and_grads(cfg, layers, rf, emb, qk, tok, dtype="float32")
     dt = time.perf_counter() - t0
-    return reps * S / dt, dt
+    return reps * S / dt, dt, threads
 
 
 def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwen3_06b",
@@ -427,8 +470,8 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     eng.close()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.n_layers in (12, 28):
-        v, dt = cpu_train_sample(layers, rf, emb, qk, S=S, model=model)
-        cpu = {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+        v, dt, thr = cpu_train_sample(layers, rf, emb, qk, S=S, model=model)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": "port",
                "sample": f"torch-CPU float32 fwd+bwd of the oracle's "
                          f"{'Stories110M' if stories else 'Qwen3-0.6B'} forward, 3 x 1 x "
                          f"{S} tokens ({dt:.1f} s)"}
@@ -644,11 +687,11 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        Bc, steps_c = 8, 96
-        v, dt = cpu_decode_sample(layers, rf, emb, qk, B=Bc, steps=steps_c, prompt=P)
-        cpu = {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+        steps_c = 4
+        v, dt, thr = cpu_decode_sample(layers, rf, emb, qk, B=B, steps=steps_c, prompt=P)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": "port",
                "sample": (f"oracle numpy port of tools/generate.py on all host cores, Qwen3-0.6B,"
-                          f" {Bc} sequences, KV pre-filled with {P} positions, {steps_c} greedy "
+                          f" {B} sequences, KV pre-filled with {P} positions, {steps_c} greedy "
                           f"steps ({dt:.1f} s)")}
 
     kps = eng.kernels_per_step(B)

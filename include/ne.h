@@ -258,6 +258,22 @@ NE_API ne_status ne_train_zero_grads(ne_ctx* ctx);
  * (optional) receive the batch's mean loss. */
 NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss);
 NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss);
+/* One micro-step exactly as ne_train_fwd_bwd, run without the captured graph
+ * and timed per stage with CUDA events (the per-phase "timing:" line of
+ * train.m:763-768, which the reference prints every 10 steps).
+ * h_ms[NE_TRAIN_PHASES] receives device milliseconds: 0 embedding forward,
+ * 1 attention forward (all layers), 2 FFN forward, 3 classifier +
+ * cross-entropy + classifier backward, 4 FFN backward, 5 attention backward,
+ * 6 embedding backward (including the wait for the gradient exchange), 7 the
+ * whole micro-step.  Synchronises. */
+#define NE_TRAIN_PHASES 8
+NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss,
+                                        float* h_ms);
+/* Value ranges the reference prints on its step line (train.m:771-776):
+ * h_out[4] = {min, max} of the final residual stream x (before the final
+ * norm) and {min, max} of the gradient at the embedding output, both from the
+ * last micro-step.  Synchronises. */
+NE_API ne_status ne_train_value_ranges(ne_ctx* ctx, float* h_out);
 /* Vocabulary compaction (cpu_ops.h:385-431, applied by train.m to every run):
  * the classifier and its softmax use only the CV embedding rows h_c2f[0..CV)
  * (distinct ids; the reference takes the tokens present in the data, in
@@ -377,8 +393,11 @@ NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floa
  * split-K slices whose partial slabs live in a static device array of
  * NE_NOALLOC_SCRATCH_FLOATS floats (8 MiB) that every GPU loading the library
  * holds until exit.  Nothing is allocated: no cudaMalloc / cudaFree / pools.
- *   - Returns NE_ERR_INVALID if splits * M * N > NE_NOALLOC_SCRATCH_FLOATS,
- *     if K is not a multiple of 64 or K/64 is not a multiple of `splits`.
+ *   - Returns NE_ERR_INVALID, before any GPU work, if splits * M * N >
+ *     NE_NOALLOC_SCRATCH_FLOATS, if K is not a multiple of 64 or K/64 is not
+ *     a multiple of `splits`, if lda or ldb is below K or not a multiple of 8,
+ *     if d_A or d_B is not 16-byte aligned or d_out not 4-byte aligned, or if
+ *     `stream` belongs to another device than the current one.
  *   - Runs on `stream` (a cudaStream_t; NULL = default stream) of the current
  *     device and synchronises it before returning (NE_ERR_TIMEOUT reports a
  *     kernel wait that expired).

@@ -24,6 +24,7 @@
 //     report a kernel wait that timed out.
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "../../include/ne.h"
@@ -90,12 +91,26 @@ extern "C" NE_API ne_status ne_gemm_splitk_noalloc(const void* d_A, long long ld
     return NE_ERR_INVALID;
   if (K % 64 != 0 || (K / 64) % splits != 0) return NE_ERR_INVALID;
   if ((size_t)splits * (size_t)M * (size_t)N > kScratchFloats) return NE_ERR_INVALID;
+  // the operands are read by TMA: rows of at least K elements, row pitches of
+  // whole 16-byte units and 16-byte aligned bases (what the tensor maps need)
+  if (lda < K || ldb < K || lda % 8 != 0 || ldb % 8 != 0) return NE_ERR_INVALID;
+  const uintptr_t a_addr = reinterpret_cast<uintptr_t>(d_A);
+  const uintptr_t b_addr = reinterpret_cast<uintptr_t>(d_B);
+  if ((a_addr & 15u) != 0 || (b_addr & 15u) != 0 || (reinterpret_cast<uintptr_t>(d_out) & 3u) != 0)
+    return NE_ERR_INVALID;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return NE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the scratch address below belongs to the current device; a stream of
+  // another device would run the kernels against that device's memory
+  if (s != nullptr) {
+    int stream_device = -1;
+    if (cudaStreamGetDevice(s, &stream_device) != cudaSuccess || stream_device != device)
+      return NE_ERR_INVALID;
+  }
   DeviceSymbols sym;
   ne_status st = device_symbols(device, &sym);
   if (st != NE_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(sym.status, 0, sizeof(int), s) != cudaSuccess) return NE_ERR_CUDA;
 
   ne::GemmCall c;

@@ -478,6 +478,62 @@ cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int
                   eps, inv_bc1, inv_bc2, norm_out);
 }
 
+// ------------------------------------------------------------ value ranges
+// out[0] = min, out[1] = max of a[0..n) (the step line's x[...] / dy[...]
+// ranges, train.m:771-776); out must hold (+inf, -inf) before the launch.
+namespace {
+__device__ __forceinline__ void atomic_min_f(float* a, float v) {
+  if (v >= 0.f) atomicMin(reinterpret_cast<int*>(a), __float_as_int(v));
+  else atomicMax(reinterpret_cast<unsigned*>(a), __float_as_uint(v));
+}
+__device__ __forceinline__ void atomic_max_f(float* a, float v) {
+  if (v >= 0.f) atomicMax(reinterpret_cast<int*>(a), __float_as_int(v));
+  else atomicMin(reinterpret_cast<unsigned*>(a), __float_as_uint(v));
+}
+__global__ void __launch_bounds__(256) minmax_kernel(const float* __restrict__ a, long long n,
+                                                     float* out) {
+  pdl_trigger();
+  pdl_wait();
+  float lo = INFINITY, hi = -INFINITY;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = a[i];
+    lo = fminf(lo, v);
+    hi = fmaxf(hi, v);
+  }
+  for (int o = 16; o; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  __shared__ float slo[8], shi[8];
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    slo[w] = lo;
+    shi[w] = hi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) {
+      lo = fminf(lo, slo[i]);
+      hi = fmaxf(hi, shi[i]);
+    }
+    atomic_min_f(out, lo);
+    atomic_max_f(out + 1, hi);
+  }
+}
+__global__ void minmax_init_kernel(float* out) {
+  out[0] = INFINITY;
+  out[1] = -INFINITY;
+}
+}  // namespace
+
+cudaError_t launch_minmax(const float* a, long long n, float* out, cudaStream_t st) {
+  minmax_init_kernel<<<1, 1, 0, st>>>(out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_k(minmax_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a, n, out);
+}
+
 cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st) {
   return launch_k(f32_to_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a, b, n);
 }

@@ -195,5 +195,7 @@ size_t embed_bwd_scratch_bytes(int n);
 cudaError_t launch_embed_bwd(const int32_t* tok, const float* dy, int n, int V, int D, float* dE,
                              void* scratch, size_t scratch_bytes, int* status, cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float* a, __nv_bfloat16* b, long long n, cudaStream_t st);
+// out[0] = min, out[1] = max of a[0..n)
+cudaError_t launch_minmax(const float* a, long long n, float* out, cudaStream_t st);
 
 }  // namespace ne

@@ -104,6 +104,8 @@ struct TrainState {
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
+  std::vector<cudaEvent_t> phase_ev;     // ne_train_fwd_bwd_timed: one event per phase boundary
+  float* range_out = nullptr;            // ne_train_value_ranges: [4]
 };
 
 // Drops the captured training step (it may hold NCCL calls of a communicator
@@ -134,6 +136,9 @@ void free_train(ne_ctx* ctx) {
   for (void* p : {(void*)t->d_c2f, (void*)t->d_f2c, (void*)t->Ec, (void*)t->dEc})
     if (p) cudaFree(p);
   if (t->opt_partial) cudaFree(t->opt_partial);
+  for (cudaEvent_t e : t->phase_ev)
+    if (e) cudaEventDestroy(e);
+  if (t->range_out) cudaFree(t->range_out);
   if (t->opt_ticket) cudaFree(t->opt_ticket);
   if (t->norm_out) cudaFree(t->norm_out);
   if (t->pool) cudaFree(t->pool);
@@ -961,6 +966,82 @@ NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h
   ne_status s = ne_train_fwd_bwd_device(ctx, t->tok, h_loss ? d_loss : nullptr);
   if (s != NE_OK) return s;
   if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
+  return ne_sync(ctx);
+}
+
+// One micro-step like ne_train_fwd_bwd, run without the captured graph and
+// with an event between consecutive entry points, so the device time of each
+// stage can be reported (the per-phase timing line of train.m:763-768).
+// h_ms[NE_TRAIN_PHASES] receives, in ms: 0 embedding forward, 1 attention
+// forward (all layers), 2 FFN forward, 3 classifier + cross-entropy + its
+// backward, 4 FFN backward, 5 attention backward, 6 embedding backward (with
+// the wait for the gradient exchange), 7 the whole micro-step.
+NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss,
+                                        float* h_ms) {
+  if (!ctx || !ctx->train || !h_tokens || !h_ms) return NE_ERR_INVALID;
+  TrainState* t = ctx->train;
+  const int L = ctx->cfg.n_layers;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  const size_t nev = 4 * (size_t)L + 4;
+  if (t->phase_ev.size() != nev) {
+    for (cudaEvent_t e : t->phase_ev)
+      if (e) cudaEventDestroy(e);
+    t->phase_ev.assign(nev, nullptr);
+    for (cudaEvent_t& e : t->phase_ev) NE_CUDA(cudaEventCreate(&e));
+  }
+  NE_CUDA(cudaMemcpyAsync(t->tok, h_tokens, (size_t)t->B * (t->S + 1) * 4, cudaMemcpyHostToDevice,
+                          ctx->st));
+  float* d_loss = reinterpret_cast<float*>(t->red + 2);
+  ne_status s = split_tokens(ctx, t->tok);
+  if (s != NE_OK) return s;
+  std::vector<int> phase;   // phase of the interval that ends at event k + 1
+  size_t k = 0;
+  auto mark = [&](int ph) -> ne_status {
+    NE_CUDA(cudaEventRecord(t->phase_ev[k++], ctx->st));
+    if (ph >= 0) phase.push_back(ph);
+    return NE_OK;
+  };
+  if ((s = mark(-1)) != NE_OK) return s;
+  if ((s = embed_fwd_ids(ctx)) != NE_OK || (s = mark(0)) != NE_OK) return s;
+  for (int l = 0; l < L; ++l) {
+    if ((s = ne_attn_fwd(ctx, l)) != NE_OK || (s = mark(1)) != NE_OK) return s;
+    if ((s = ne_ffn_fwd(ctx, l)) != NE_OK || (s = mark(2)) != NE_OK) return s;
+  }
+  if ((s = ne_lmhead_ce_fwd_bwd(ctx, d_loss)) != NE_OK || (s = mark(3)) != NE_OK) return s;
+  for (int l = L - 1; l >= 0; --l) {
+    if ((s = ne_ffn_bwd(ctx, l)) != NE_OK || (s = mark(4)) != NE_OK) return s;
+    if ((s = ne_attn_bwd(ctx, l)) != NE_OK || (s = mark(5)) != NE_OK) return s;
+  }
+  if ((s = ne_embed_bwd(ctx)) != NE_OK || (s = mark(6)) != NE_OK) return s;
+  t->micro_steps++;
+  t->steps_run++;
+  if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
+  if ((s = ne_sync(ctx)) != NE_OK) return s;
+  for (int i = 0; i < NE_TRAIN_PHASES; ++i) h_ms[i] = 0.f;
+  for (size_t i = 0; i < phase.size(); ++i) {
+    float ms = 0.f;
+    NE_CUDA(cudaEventElapsedTime(&ms, t->phase_ev[i], t->phase_ev[i + 1]));
+    h_ms[phase[i]] += ms;
+  }
+  NE_CUDA(cudaEventElapsedTime(&h_ms[7], t->phase_ev[0], t->phase_ev[phase.size()]));
+  return NE_OK;
+}
+
+// Smallest and largest value of the final residual stream x (before the
+// final norm) and of the gradient the last micro-step left at the embedding
+// output: h_out = {x_min, x_max, dy_min, dy_max} (train.m:771-776).
+NE_API ne_status ne_train_value_ranges(ne_ctx* ctx, float* h_out) {
+  if (!ctx || !ctx->train || !h_out) return NE_ERR_INVALID;
+  TrainState* t = ctx->train;
+  NE_CUDA(cudaSetDevice(ctx->device));
+  if (!t->range_out) {
+    ne_status s = dalloc(ctx, &t->range_out, 4);
+    if (s != NE_OK) return s;
+  }
+  const long long n = (long long)t->M * ctx->cfg.dim;
+  NE_LAUNCH(launch_minmax(t->XL, n, t->range_out, ctx->st));
+  NE_LAUNCH(launch_minmax(t->dY, n, t->range_out + 2, ctx->st));
+  NE_CUDA(cudaMemcpyAsync(h_out, t->range_out, 4 * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
   return ne_sync(ctx);
 }
 

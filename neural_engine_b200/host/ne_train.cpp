@@ -46,6 +46,7 @@ namespace {
 struct Args {
   bool scratch = false, resume = false, synthetic = false, compact_vocab = true, print_vocab = false;
   bool zero1 = false;   // data parallel: ZeRO-1 (sharded optimizer state)
+  bool data_u32 = false;   // token file of uint32 ids (vocabularies beyond 65,536)
   int steps = 10000, accum = 10, warmup = 100;
   float lr = 3e-4f, clip = 1.0f;
   std::string data = "../tinystories_data00.bin";
@@ -62,7 +63,8 @@ struct Args {
 void usage() {
   std::printf(
       "usage: ne_train [--scratch | --resume] [--steps N] [--lr X] [--accum N] [--warmup N]\n"
-      "                [--clip X] [--data FILE] [--model qwen3_06b|stories110m] [--seq S]\n"
+      "                [--clip X] [--data FILE] [--data-u32] [--model qwen3_06b|stories110m]\n"
+      "                [--seq S]\n"
       "                [--batch B] [--ckpt FILE] [--device D] [--synthetic] [--save-every N]\n"
       "                [--qk-norm 0|1] [--theta X] [--eps X] [--alpha X] [--no-compact-vocab]\n"
       "                [--zero1]   (with WORLD_SIZE > 1: reduce-scatter + sharded AdamW)\n"
@@ -85,6 +87,7 @@ bool parse(int argc, char** argv, Args& a) {
     else if (s == "--synthetic") a.synthetic = true;
     else if (s == "--no-compact-vocab") a.compact_vocab = false;
     else if (s == "--zero1") a.zero1 = true;
+    else if (s == "--data-u32") a.data_u32 = true;
     else if (s == "--print-vocab") a.print_vocab = true;
     else if (s == "--steps") a.steps = std::atoi(next("--steps"));
     else if (s == "--lr") a.lr = (float)std::atof(next("--lr"));
@@ -248,15 +251,20 @@ bool write_init_ckpt(const std::string& path, const ne_model_cfg& c, const HostW
   return std::fclose(f) == 0 && ok;
 }
 
+// Memory-mapped token file: uint16 ids as the reference writes them
+// (tools/tokenize_data.py, read at train.m:276-284), or uint32 ids with
+// --data-u32 for vocabularies beyond 65,536 (Qwen3's 151,936).
 struct TokenFile {
-  const uint16_t* tok = nullptr;
+  const void* base = nullptr;
   size_t n = 0, bytes = 0;
   int fd = -1;
+  bool u32 = false;
   ~TokenFile() {
-    if (tok) munmap(const_cast<uint16_t*>(tok), bytes);
+    if (base) munmap(const_cast<void*>(base), bytes);
     if (fd >= 0) close(fd);
   }
-  bool open_file(const std::string& path) {
+  bool open_file(const std::string& path, bool wide) {
+    u32 = wide;
     fd = ::open(path.c_str(), O_RDONLY);
     if (fd < 0) return false;
     struct stat st;
@@ -264,9 +272,12 @@ struct TokenFile {
     bytes = (size_t)st.st_size;
     void* p = mmap(nullptr, bytes, PROT_READ, MAP_PRIVATE, fd, 0);
     if (p == MAP_FAILED) return false;
-    tok = static_cast<const uint16_t*>(p);
-    n = bytes / 2;
+    base = p;
+    n = bytes / (u32 ? 4 : 2);
     return true;
+  }
+  uint32_t operator[](size_t i) const {
+    return u32 ? static_cast<const uint32_t*>(base)[i] : static_cast<const uint16_t*>(base)[i];
   }
 };
 
@@ -284,7 +295,7 @@ void sample(const TokenFile& tf, bool synthetic, int V, int B, int S, std::vecto
     const size_t max_pos = tf.n - S - 1;
     const size_t pos = (size_t)(drand48() * max_pos);
     if (positions) positions->push_back(pos);
-    for (int t = 0; t <= S; ++t) out[(size_t)b * (S + 1) + t] = tf.tok[pos + t];
+    for (int t = 0; t <= S; ++t) out[(size_t)b * (S + 1) + t] = (int32_t)tf[pos + t];
   }
 }
 
@@ -293,7 +304,7 @@ void sample(const TokenFile& tf, bool synthetic, int V, int B, int S, std::vecto
 std::vector<int32_t> vocab_map(const TokenFile& tf, int V) {
   std::vector<char> used(V, 0);
   for (size_t i = 0; i < tf.n; ++i)
-    if (tf.tok[i] < V) used[tf.tok[i]] = 1;
+    if (tf[i] < (uint32_t)V) used[tf[i]] = 1;
   std::vector<int32_t> c2f;
   for (int v = 0; v < V; ++v)
     if (used[v]) c2f.push_back(v);
@@ -349,7 +360,7 @@ int main(int argc, char** argv) {
   }
   TokenFile tf;
   if (!a.synthetic) {
-    if (!tf.open_file(a.data)) {
+    if (!tf.open_file(a.data, a.data_u32)) {
       std::printf("Cannot open %s\n", a.data.c_str());
       return 1;
     }
@@ -496,13 +507,37 @@ int main(int argc, char** argv) {
     const bool update = (step + 1) % a.accum == 0 || step == total_steps - 1;
     if (world > 1) CHECK(ne_comm_set_reduce(ctx, update ? 1 : 0));
     float loss = 0.f;
-    CHECK(ne_train_fwd_bwd(ctx, tok.data(), &loss));
+    // every 10th step (train.m:763-777) runs the micro-step with per-stage
+    // device timing; every rank takes the same path
+    const bool log = step % 10 == 0 || step == start_step;
+    float ph[NE_TRAIN_PHASES] = {0};
+    if (log) CHECK(ne_train_fwd_bwd_timed(ctx, tok.data(), &loss, ph));
+    else CHECK(ne_train_fwd_bwd(ctx, tok.data(), &loss));
     last_loss = loss;
     const double step_ms = now_ms() - t0;
     total_train_ms += step_ms;
     steps_done++;
-    if (rank == 0 && (step % 10 == 0 || step == start_step))
-      std::printf("step %-4d loss=%.4f  lr=%.2e  %.1fms/step\n", step, loss, lr, step_ms);
+    if (log) {
+      float rg[4] = {0, 0, 0, 0};
+      CHECK(ne_train_value_ranges(ctx, rg));
+      if (rank == 0) {
+        // train.m:766's fields: the forward / backward kernels take the ANE
+        // stages' places; norms, residuals, RoPE and the GQA sums are fused
+        // into them and there is no IOSurface staging, so those read 0; dwait
+        // is the embedding backward with the wait for the gradient exchange
+        const double fwd = ph[0] + ph[1] + ph[2], bwd = ph[4] + ph[5];
+        const double timed = fwd + bwd + ph[3] + ph[6];
+        std::printf("  timing: ane_fwd=%.1f io_fwd=%.1f rms=%.1f ane_bwd=%.1f io_bwd=%.1f "
+                    "rms_bwd=%.1f cls=%.1f dw=%.1f dwait=%.1f resid=%.1f gqa=%.1f rope=%.1f "
+                    "[gap=%.1f]\n",
+                    fwd, 0.0, 0.0, bwd, 0.0, 0.0, (double)ph[3], 0.0, (double)ph[6], 0.0, 0.0, 0.0,
+                    step_ms - timed > 0 ? step_ms - timed : 0.0);
+        std::printf("  io_bwd: ffn_w=%.1f ffn_r=%.1f wot_w=%.1f s1=%.1f s2=%.1f s2r=%.1f "
+                    "qkv_w=%.1f qkv_r=%.1f\n", 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0);
+        std::printf("step %-4d loss=%.4f  lr=%.2e  %.1fms/step  x[%.2f,%.2f] dy[%.3e,%.3e]\n",
+                    step, loss, lr, step_ms, rg[0], rg[1], rg[2], rg[3]);
+      }
+    }
     if (update) {
       const double ta = now_ms();
       adam_t++;

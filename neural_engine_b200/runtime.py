@@ -35,7 +35,8 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_attn_bwd", "ne_embed_bwd", "ne_rmsnorm_fwd", "ne_rmsnorm_bwd_add",
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
             "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
-            "ne_comm_set_sharding", "ne_train_gather_state")
+            "ne_comm_set_sharding", "ne_train_gather_state", "ne_train_fwd_bwd_timed",
+            "ne_train_value_ranges")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -179,6 +180,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_train_zero_grads.argtypes = [P]
     lib.ne_train_fwd_bwd_device.argtypes = [P, P, P]
     lib.ne_train_fwd_bwd.argtypes = [P, P, C.POINTER(C.c_float)]
+    lib.ne_train_fwd_bwd_timed.argtypes = [P, P, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+    lib.ne_train_value_ranges.argtypes = [P, C.POINTER(C.c_float)]
     lib.ne_train_grad_norm.argtypes = [P, F, C.POINTER(C.c_float)]
     lib.ne_adamw_step.argtypes = [P, C.POINTER(AdamCfgC), I, C.POINTER(C.c_float)]
     lib.ne_lr_schedule.argtypes = [I, F, I, I, F]
@@ -392,6 +395,24 @@ class Engine:
         loss = C.c_float(0)
         self._check(self.lib.ne_train_fwd_bwd(self._ctx, _ptr(tokens), C.byref(loss)))
         return float(loss.value)
+
+    TRAIN_PHASES = ("embed_fwd", "attn_fwd", "ffn_fwd", "classifier", "ffn_bwd", "attn_bwd",
+                    "embed_bwd", "step")
+
+    def train_fwd_bwd_timed(self, tokens: np.ndarray):
+        """One micro-step (as train_fwd_bwd) with per-stage device times in ms;
+        returns (loss, {phase: ms})."""
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        loss = C.c_float(0.0)
+        ms = (C.c_float * 8)()
+        self._check(self.lib.ne_train_fwd_bwd_timed(self._ctx, _ptr(tok), C.byref(loss), ms))
+        return float(loss.value), dict(zip(self.TRAIN_PHASES, [float(v) for v in ms]))
+
+    def value_ranges(self):
+        """(x_min, x_max, dy_min, dy_max) of the last micro-step."""
+        out = (C.c_float * 4)()
+        self._check(self.lib.ne_train_value_ranges(self._ctx, out))
+        return tuple(float(v) for v in out)
 
     def train_fwd_bwd_device(self, d_tokens: int, d_loss: int | None = None):
         self._check(self.lib.ne_train_fwd_bwd_device(self._ctx, C.c_void_p(d_tokens),

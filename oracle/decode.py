@@ -6,7 +6,9 @@ reference at their defaults:
   * ``theta`` (RoPE base; generate.py:103 hard-codes 10000.0),
   * ``eps`` (RMSNorm eps; generate.py:81 default 1e-5),
   * ``qk_norm`` (per-head RMSNorm of q and k after projection, before RoPE,
-    with gains and ``qk_eps``; absent from the reference, F3 of the survey),
+    with gains and ``qk_eps``; generate.py has no such step, while the
+    Qwen3 models the reference converts carry q_norm / k_norm gains,
+    tools/convert_hf.py:84-89 notes and skips them),
   * ``res_alpha`` (residual branch scale; 1.0 in generate.py:184,191, the
     training forward uses 1/sqrt(2L), train.m:181,441),
 and two structural ones that do not change the arithmetic of a position:

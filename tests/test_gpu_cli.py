@@ -76,8 +76,22 @@ def test_cli_training_run_matches_the_binding_driven_loop(tmp_path):
                 r"Params: ([\d.]+)M \(transformer ([\d.]+)M \+ embed ([\d.]+)M\)",
                 r"Accum (\d+).*LR=([\d.e+-]+)",
                 r"step\s+(\d+)\s+loss=([\d.]+)(?:\s+lr=([\d.e+-]+))?(?:\s+([\d.]+)ms/step)?",
-                r"\[ckpt saved, best_loss=([\d.]+)\]"):
+                r"\[ckpt saved, best_loss=([\d.]+)\]",
+                # the web dashboard's step, timing and io_bwd lines
+                # (training/dashboard-web/app.py:40-53), printed as train.m:766-776 does
+                r"step\s+(\d+)\s+loss=([\d.]+)\s+lr=([\d.e+-]+)\s+([\d.]+)ms/step\s+"
+                r"x\[([-\d.]+),([-\d.]+)\]\s+dy\[([-\d.e+-]+),([-\d.e+-]+)\]",
+                r"timing: ane_fwd=([\d.]+) io_fwd=([\d.]+) rms=([\d.]+) "
+                r"ane_bwd=([\d.]+) io_bwd=([\d.]+) rms_bwd=([\d.]+) "
+                r"cls=([\d.]+) dw=([\d.]+) dwait=([\d.]+) resid=([\d.]+) "
+                r"gqa=([\d.]+) rope=([\d.]+) \[gap=([\d.]+)\]",
+                r"io_bwd: ffn_w=([\d.]+) ffn_r=([\d.]+) wot_w=([\d.]+) "
+                r"s1=([\d.]+) s2=([\d.]+) s2r=([\d.]+) qkv_w=([\d.]+) qkv_r=([\d.]+)"):
         assert re.search(pat, r.stdout), pat
+    t = re.search(r"timing: ane_fwd=([\d.]+) .* ane_bwd=([\d.]+) .* cls=([\d.]+)", r.stdout)
+    assert float(t.group(1)) > 0 and float(t.group(2)) > 0 and float(t.group(3)) > 0
+    xr = re.search(r"x\[([-\d.]+),([-\d.]+)\]\s+dy\[([-\d.e+-]+),([-\d.e+-]+)\]", r.stdout)
+    assert float(xr.group(1)) < float(xr.group(2)) and float(xr.group(3)) < float(xr.group(4))
     m = re.search(r"step\s+(\d+)\s+loss=([\d.]+)(?:\s+lr=([\d.e+-]+))?(?:\s+([\d.]+)ms/step)?",
                   r.stdout)
     assert m.group(3) is not None and m.group(4) is not None   # lr and ms/step parsed too

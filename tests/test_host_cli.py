@@ -84,3 +84,20 @@ def test_vocab_compaction_map_is_the_reference_map(tmp_path):
                           "--no-compact-vocab"], check=True, capture_output=True, text=True,
                          timeout=60).stdout.split()
     assert out == ["0"]
+
+
+def test_uint32_token_file_reads_ids_beyond_uint16(tmp_path):
+    """--data-u32: the same windows and compaction map over uint32 ids, so a
+    Qwen3-vocabulary token file (ids up to 151,935) can be fed."""
+    shape = [*SHAPE[:-2], "--vocab", "151936"]
+    ids = [5, 70_000, 151_935, 65_536, 17]
+    data = np.random.default_rng(4).choice(ids, size=6000).astype(np.uint32)
+    path = tmp_path / "tok32.bin"
+    data.tofile(path)
+    out = subprocess.run([_bin(), *shape, "--data", str(path), "--data-u32", "--print-vocab"],
+                         check=True, capture_output=True, text=True, timeout=60).stdout.split()
+    assert int(out[0]) == len(ids) and [int(x) for x in out[1:]] == sorted(ids)
+    out = subprocess.run([_bin(), *shape, "--seq", "256", "--data", str(path), "--data-u32",
+                          "--print-windows", "10"], check=True, capture_output=True, text=True,
+                         timeout=60).stdout.split()
+    assert [int(x) for x in out] == hd.sample_windows(len(data), 256, 10, seed=42)
