@@ -85,6 +85,23 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+def log(msg: str):
+    """Progress on stderr (the JSON line stays the only stdout)."""
+    rank = int(os.environ.get("RANK", 0))
+    print(f"[bench rank {rank} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
+def allmax(x: float, world: int) -> float:
+    """Max over ranks of a host float (the coordination group is gloo, CPU)."""
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -258,10 +275,11 @@ def cpu_decode_sample(layers, rms_final, embed, qk, B=256, steps=4, prompt=512, 
     cfg = om.QWEN3_06B
     dec = od.Decoder(cfg, layers, rms_final, embed, qk, batch=B, max_seq=prompt + steps + 1)
     rng = np.random.default_rng(seed)
-    for l in range(cfg.n_layers):
-        dec.k_cache[l, :, :, :prompt] = rng.standard_normal(
-            (B, cfg.kv_heads, prompt, cfg.head_dim), dtype=np.float32)
-        dec.v_cache[l, :, :, :prompt] = dec.k_cache[l, :, :, :prompt]
+    # the attention's cost does not depend on the cached values: one random
+    # [prompt, head_dim] block broadcast over layers, sequences and heads
+    blk = rng.standard_normal((prompt, cfg.head_dim), dtype=np.float32)
+    dec.k_cache[:, :, :, :prompt] = blk
+    dec.v_cache[:, :, :, :prompt] = blk
     tok = rng.integers(0, cfg.vocab, size=(B, 1))
     dec.forward(tok, prompt, last_only=True)          # warm caches / BLAS threads
     t0 = time.perf_counter()
@@ -333,11 +351,11 @@ def run_reference(args):
     B, P = args.batch, args.prompt
     dec = od.Decoder(cfg, layers, rf, emb, qk, batch=B, max_seq=P + 2)
     rng = np.random.default_rng(5)
-    # the attention's cost does not depend on the cached values: fill by layer
-    for l in range(cfg.n_layers):
-        dec.k_cache[l, :, :, :P] = rng.standard_normal((B, cfg.kv_heads, P, cfg.head_dim),
-                                                       dtype=np.float32)
-        dec.v_cache[l, :, :, :P] = dec.k_cache[l, :, :, :P]
+    # the attention's cost does not depend on the cached values: one random
+    # [P, head_dim] block broadcast over layers, sequences and heads
+    blk = rng.standard_normal((P, cfg.head_dim), dtype=np.float32)
+    dec.k_cache[:, :, :, :P] = blk
+    dec.v_cache[:, :, :, :P] = blk
     tok = rng.integers(0, cfg.vocab, size=(B, 1))
     ts = []
     for i in range(args.warmup + args.steps):
@@ -429,7 +447,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
 
     for _ in range(args.warmup):
         step()
-    eng.sync()
+    eng.sync()        # bounded by the exchange's deadline: a stuck exchange raises
     barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -440,13 +458,10 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     for _ in range(args.steps):
         step()
     ev1.record(stream)
+    eng.sync()
     ev1.synchronize()
     clk = clocks.stop()
-    t_ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        tt = torch.tensor([t_ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_ms = float(tt.item())
+    t_ms = allmax(ev0.elapsed_time(ev1), world)
     ms_step = t_ms / args.steps
     value = world * B * S * args.steps / (t_ms / 1000.0)
     peak, kind = tensor_peak()
@@ -462,21 +477,19 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
         tstep[0] += 1
         eng.adamw_step(tstep[0], 3e-4, grad_scale=1.0 / world, return_norm=False)
     eng.sync()   # the last AdamW is asynchronous: the timed region ends when it has run
-    te = (time.perf_counter() - t0) / reps
-    if world > 1:
-        tt = torch.tensor([te], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        te = float(tt.item())
+    te = allmax((time.perf_counter() - t0) / reps, world)
     eng.close()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.n_layers in (12, 28):
-        v, dt, thr = cpu_train_sample(layers, rf, emb, qk, S=S, model=model)
+        v, dt, thr = cpu_train_sample(layers, rf, emb, qk, S=S, model=model,
+                                      reps=3 if S <= 256 else 1)
         cpu = {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": "port",
                "sample": f"torch-CPU float32 fwd+bwd of the oracle's "
-                         f"{'Stories110M' if stories else 'Qwen3-0.6B'} forward, 3 x 1 x "
-                         f"{S} tokens ({dt:.1f} s)"}
+                         f"{'Stories110M' if stories else 'Qwen3-0.6B'} forward, "
+                         f"{3 if S <= 256 else 1} x 1 x {S} tokens ({dt:.1f} s)"}
     metric = (f"Stories110M training tokens/sec (fwd + bwd + AdamW, seq {S}, batch {B} per GPU)"
-              if stories else TRAIN_METRIC)
+              if stories else
+              f"Qwen3-0.6B training tokens/sec (fwd + bwd + AdamW, seq {S}, batch {B} per GPU)")
     return {"metric": metric, "value": round(value, 1), "unit": UNIT,
             "ms_per_step": round(ms_step, 3), "steps": args.steps, "warmup": args.warmup,
             "scaling": "weak", "dtype": "bf16",
@@ -533,12 +546,9 @@ def run_prefill(args, rank, local, world, layers, rf, emb, qk):
             for _ in range(reps):
                 eng.prefill_device(tok.data_ptr(), B, S, 0, nxt.data_ptr())
             ev1.record(stream)
+            eng.sync()
             ev1.synchronize()
-            ms = ev0.elapsed_time(ev1) / reps
-            if world > 1:
-                tt = torch.tensor([ms], device="cuda")
-                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                ms = float(tt.item())
+            ms = allmax(ev0.elapsed_time(ev1) / reps, world)
             fl = prefill_flops(B, S)
             ach = fl / (ms / 1000.0) / 1e12
             runs[f"seq{S}"] = {"seq_len": S, "ms_per_call": round(ms, 3),
@@ -556,6 +566,53 @@ def run_prefill(args, rank, local, world, layers, rf, emb, qk):
             "runs": runs}
 
 
+# ----------------------------------------------------------------- decode legs
+def run_decode(args, eng, prompt, B, P, G, rank, world, barrier, with_clocks=True):
+    """Timed greedy decode of B sequences (config 1): `--steps` passes of G
+    CUDA-graph decode steps from the prefilled P-position cache, after
+    `--warmup` passes; device time on the library's stream, max over ranks.
+    Returns the measurements and the per-kernel-group times of one step at the
+    mean context length."""
+    import torch
+    first = torch.zeros(B, dtype=torch.int32, device="cuda")
+    out = torch.zeros(G * B, dtype=torch.int32, device="cuda")
+    eng.prefill_device(prompt.data_ptr(), B, P, 0, first.data_ptr())
+    eng.sync()
+    stream = torch.cuda.ExternalStream(eng.stream_ptr)
+    for _ in range(args.warmup):
+        eng.decode_loop_device(first.data_ptr(), B, P, G, out.data_ptr())
+    eng.sync()
+    barrier()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) if with_clocks else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.decode_loop_device(first.data_ptr(), B, P, G, out.data_ptr())
+    ev1.record(stream)
+    eng.sync()
+    ev1.synchronize()
+    clk = clocks.stop() if clocks else None
+    barrier()
+    t_ms = allmax(ev0.elapsed_time(ev1), world)
+    ms_step = t_ms / args.steps
+    value = world * B * G * args.steps / (t_ms / 1000.0)
+    T_mid = P + G // 2
+    groups = {}
+    for _ in range(3):
+        for k, v in eng.profile_decode_step(B, T_mid).items():
+            groups[k] = groups.get(k, 0.0) + v / 3
+    peak, _ = peaks()
+    step_bytes = sum(decode_step_bytes(B, P + i) for i in range(G)) / G
+    whole = {"bytes_per_decode_step": step_bytes,
+             "achieved_gbs": round(step_bytes / (ms_step / G / 1000.0) / 1e9, 1),
+             "frac_of_peak": round(step_bytes / (ms_step / G / 1000.0) / 1e9 / peak, 4)}
+    return {"value": value, "ms_per_step": ms_step, "ms_per_decode_step": ms_step / G,
+            "groups": groups, "whole": whole, "clocks": clk, "first": first, "T_mid": T_mid}
+
+
 # ----------------------------------------------------------------- our arm
 def main():
     args = parse()
@@ -567,9 +624,11 @@ def main():
     rank, local, world = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
+        # coordination only (barriers, max over ranks, the NCCL id): a CPU
+        # group with a timeout, so no collective of this script can hold a GPU;
+        # the gradient exchange is the library's own communicator
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
 
     def barrier():
         if world > 1:
@@ -590,49 +649,18 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
+    log("decode: weights ready")
     eng = ne.Engine(cfg, device=local)
     eng.set_weights(layers, rf, emb, qk)
     eng.kv_alloc(B, P + G)
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
     prompt = torch.randint(0, cfg.vocab, (B, P), generator=gen, device="cuda", dtype=torch.int32)
-    first = torch.zeros(B, dtype=torch.int32, device="cuda")
-    out = torch.zeros(G * B, dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
-    eng.prefill_device(prompt.data_ptr(), B, P, 0, first.data_ptr())
-    eng.sync()
-    stream = torch.cuda.ExternalStream(eng.stream_ptr)
-
-    for _ in range(args.warmup):
-        eng.decode_loop_device(first.data_ptr(), B, P, G, out.data_ptr())
-    eng.sync()
-    barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        eng.decode_loop_device(first.data_ptr(), B, P, G, out.data_ptr())
-    ev1.record(stream)
-    ev1.synchronize()
-    clk = clocks.stop()
-    torch.cuda.synchronize()
-    barrier()
-    t_ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        tt = torch.tensor([t_ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_ms = float(tt.item())
-    ms_step = t_ms / args.steps
-    value = world * B * G * args.steps / (t_ms / 1000.0)
-
-    # live per-kernel-group timing of one decode step at the mean context length
-    T_mid = P + G // 2
-    groups = {}
-    for _ in range(3):
-        for k, v in eng.profile_decode_step(B, T_mid).items():
-            groups[k] = groups.get(k, 0.0) + v / 3
+    d = run_decode(args, eng, prompt, B, P, G, rank, world, barrier)
+    ms_step, value, groups, whole, clk = (d["ms_per_step"], d["value"], d["groups"], d["whole"],
+                                          d["clocks"])
+    log(f"decode B={B}: {value:.0f} tokens/s")
+    T_mid = d["T_mid"]
     dom = max(groups, key=groups.get)
     dom_ms = groups[dom] / (L if dom in ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo",
                                          "gemm_w13", "swiglu", "gemm_w2") else 1)
@@ -661,10 +689,6 @@ def main():
         roof["read_floor"] = {"kernel": "ne_stream_read", "ms": round(rc_ms, 4),
                               "gbs": round(rc_gbs, 1), "frac_of_peak": round(rc_gbs / peak, 4)}
         roof["frac_of_read_floor"] = round(rc_ms / dom_ms, 4)
-    step_bytes = sum(decode_step_bytes(B, P + i) for i in range(G)) / G
-    whole = {"bytes_per_decode_step": step_bytes,
-             "achieved_gbs": round(step_bytes / (ms_step / G / 1000.0) / 1e9, 1),
-             "frac_of_peak": round(step_bytes / (ms_step / G / 1000.0) / 1e9 / peak, 4)}
 
     # end to end through the public API: host prompt -> ne_generate -> host tokens
     e2e = None
@@ -676,14 +700,28 @@ def main():
         t0 = time.perf_counter()
         for _ in range(reps):
             eng.generate_greedy(h_prompt, G)
-        te = (time.perf_counter() - t0) / reps
-        if world > 1:
-            tt = torch.tensor([te], device="cuda")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            te = float(tt.item())
+        te = allmax((time.perf_counter() - t0) / reps, world)
         e2e = {"value": world * B * G / te, "unit": UNIT, "h2d_bytes_per_step": B * P * 4,
                "d2h_bytes_per_step": B * G * 4, "s_per_call": round(te, 4),
                "includes": "H2D prompt, prefill of 512 positions, 255 decode steps, D2H tokens"}
+
+    # the other batch sizes of config 1 (B = 1 runs as one replica per GPU)
+    decode_batches = {}
+    for Bx in (1, 32):
+        if Bx >= B:
+            continue
+        dx = run_decode(args, eng, prompt[:Bx], Bx, P, G, rank, world, barrier,
+                        with_clocks=False)
+        decode_batches[f"b{Bx}"] = {
+            "batch_per_gpu": Bx, "global_batch": Bx * world,
+            "value": round(dx["value"], 1), "unit": UNIT,
+            "ms_per_step": round(dx["ms_per_step"], 3),
+            "ms_per_decode_step": round(dx["ms_per_decode_step"], 4),
+            "roofline_whole_step": dx["whole"],
+            "kernel_groups_ms_per_step": {k: round(v, 4) for k, v in dx["groups"].items()},
+            "parallelism": ("replicas (one sequence per GPU)" if Bx == 1 else
+                            f"sequence-sharded x{world} (no collective)")}
+        log(f"decode B={Bx}: {dx['value']:.1f} tokens/s")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -696,17 +734,41 @@ def main():
 
     kps = eng.kernels_per_step(B)
     eng.close()
+
+    # the other legs: a failure is recorded in the line instead of ending the
+    # run; after one, legs with collectives are skipped (ranks may disagree on
+    # where they stopped)
+    errors = {}
+
+    def leg(name, fn):
+        if errors and world > 1:
+            return {"skipped": "an earlier leg failed on this rank"}
+        log(f"{name}: start")
+        try:
+            r = fn()
+            log(f"{name}: done")
+            return r
+        except Exception as ex:          # noqa: BLE001 -- recorded in the JSON line
+            errors[name] = f"{type(ex).__name__}: {ex}"
+            log(f"{name}: FAILED {errors[name]}")
+            return {"error": errors[name]}
+
     prefill = None
     if not args.no_prefill:
-        prefill = run_prefill(args, rank, local, world, layers, rf, emb, qk)
-    train = train_stories = None
+        prefill = leg("prefill", lambda: run_prefill(args, rank, local, world, layers, rf, emb,
+                                                     qk))
+    train = train_s1024 = train_stories = None
     if not args.no_train:
-        train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
+        train = leg("train", lambda: run_train(args, rank, local, world, layers, rf, emb, qk,
+                                               barrier))
+        train_s1024 = leg("train_s1024", lambda: run_train(args, rank, local, world, layers, rf,
+                                                           emb, qk, barrier, S=1024))
         if not args.no_stories:
             import neural_engine_b200 as ne_mod
             s_w = host_weights(seed=0, cfg=ne_mod.STORIES110M)
-            train_stories = run_train(args, rank, local, world, *s_w, barrier,
-                                      model="stories110m", B=32, S=256)
+            train_stories = leg("train_stories110m",
+                                lambda: run_train(args, rank, local, world, *s_w, barrier,
+                                                  model="stories110m", B=32, S=256))
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
@@ -723,10 +785,17 @@ def main():
                 "kernel_groups_ms_per_step": {k: round(v, 4) for k, v in groups.items()},
                 "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
                 "gpu_launches": kps * G * args.steps, "kernels_per_decode_step": kps,
-                "prefill": prefill, "train": train, "train_stories110m": train_stories}
+                "decode_batches": decode_batches,
+                "prefill": prefill, "train": train, "train_s1024": train_s1024,
+                "train_stories110m": train_stories}
+        if errors:
+            line["errors"] = errors
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        try:
+            dist.destroy_process_group()
+        except Exception:                # noqa: BLE001 -- teardown after a failed leg
+            pass
 
 
 if __name__ == "__main__":

@@ -359,6 +359,14 @@ NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, const void* d_
 NE_API ne_status ne_comm_unique_id(void* id_out);
 NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world);
 NE_API ne_status ne_comm_set_reduce(ne_ctx* ctx, int on);
+/* Deadline, in ms, of every wait on the exchange: ne_comm_init waiting for all
+ * ranks to join, and ne_sync (and the calls that synchronise) waiting for a
+ * step's exchange.  0 restores the default (NE_COMM_TIMEOUT_MS, else 120 s).
+ * When a deadline passes -- a rank that never joined or never entered an
+ * exchange -- the communicator is aborted (its kernels return), the call
+ * returns NE_ERR_TIMEOUT, and later exchanges return NE_ERR_STATE until
+ * ne_comm_init builds a new communicator.  May be called before ne_comm_init. */
+NE_API ne_status ne_comm_set_timeout(ne_ctx* ctx, int timeout_ms);
 /* Sum the whole gradient pool over the ranks now (ordered on the stream). */
 NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx);
 /* ZeRO-1 (on = 1; no counterpart in the single-device reference).  Every

@@ -11,11 +11,22 @@
 // NCCL (e.g. through torch.distributed) the same shared object is reused.
 // Collectives run on a dedicated high-priority stream; ordering against the
 // compute stream is by events only (no host synchronisation).
+//
+// Failure handling: the communicator is created non-blocking, every NCCL call
+// that reports ncclInProgress is polled to completion against a deadline, and
+// ne_sync waits for the streams by polling (cudaStreamQuery plus
+// ncclCommGetAsyncError) instead of blocking.  When a deadline passes -- a rank
+// that never joined, an exchange some rank never entered -- the communicator is
+// aborted (ncclCommAbort makes its kernels return), the streams drain, and the
+// call returns NE_ERR_TIMEOUT instead of holding the GPUs.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 
 #include "ne_comm.h"
 #include "ne_ctx.h"
@@ -39,6 +50,9 @@ struct NcclApi {
   ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
 };
 
 NcclApi& nccl() {
@@ -62,9 +76,15 @@ NcclApi& nccl() {
   api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
   api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
   api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+  api.CommInitRankConfig =
+      reinterpret_cast<decltype(api.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
+  api.CommGetAsyncError =
+      reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+  api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
   if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.AllGather ||
       !api.ReduceScatter || !api.GroupStart || !api.GroupEnd || !api.CommDestroy ||
-      !api.GetErrorString) {
+      !api.GetErrorString || !api.CommInitRankConfig || !api.CommGetAsyncError ||
+      !api.CommAbort) {
     api.error = "libnccl.so.2 lacks a required symbol";
     return api;
   }
@@ -76,14 +96,110 @@ ne_status nccl_fail(ne_ctx* ctx, ncclResult_t r, const char* what) {
   return fail(ctx, NE_ERR_CUDA, std::string(what) + ": " + nccl().GetErrorString(r));
 }
 
+using Clock = std::chrono::steady_clock;
+
+// Default deadline of one wait on the exchange: NE_COMM_TIMEOUT_MS, else 120 s.
+int default_timeout_ms() {
+  static const int ms = [] {
+    const char* e = std::getenv("NE_COMM_TIMEOUT_MS");
+    const int v = e ? std::atoi(e) : 0;
+    return v > 0 ? v : 120000;
+  }();
+  return ms;
+}
+
+// Back-off of the host polling loops: spin briefly, then sleep a little.
+void poll_pause(int iter) {
+  if (iter < 2000) std::this_thread::yield();
+  else std::this_thread::sleep_for(std::chrono::microseconds(50));
+}
+
+// The communicator ran into a deadline or an asynchronous error: abort it (its
+// kernels in flight return), let both streams drain (bounded), drop it.
+ne_status comm_abort(ne_ctx* ctx, ne_status why, const std::string& msg) {
+  Comm* c = ctx->comm;
+  if (c->comm) nccl().CommAbort(reinterpret_cast<ncclComm_t>(c->comm));
+  c->comm = nullptr;
+  c->aborted = true;
+  const auto until = Clock::now() + std::chrono::seconds(30);
+  for (int i = 0; Clock::now() < until; ++i) {
+    const bool idle = cudaStreamQuery(ctx->st) != cudaErrorNotReady &&
+                      (!c->cs || cudaStreamQuery(c->cs) != cudaErrorNotReady);
+    if (idle) break;
+    poll_pause(i);
+  }
+  return fail(ctx, why, msg + "; communicator aborted");
+}
+
+// Poll a non-blocking NCCL call that returned ncclInProgress until its host
+// side finished (or failed, or the deadline passed).
+ne_status comm_settle(ne_ctx* ctx, ncclResult_t r, const char* what) {
+  Comm* c = ctx->comm;
+  if (r == ncclSuccess) return NE_OK;
+  if (r != ncclInProgress) return nccl_fail(ctx, r, what);
+  const auto until = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  for (int i = 0;; ++i) {
+    ncclResult_t st = ncclSuccess;
+    nccl().CommGetAsyncError(reinterpret_cast<ncclComm_t>(c->comm), &st);
+    if (st == ncclSuccess) return NE_OK;
+    if (st != ncclInProgress)
+      return comm_abort(ctx, NE_ERR_CUDA, std::string(what) + ": " + nccl().GetErrorString(st));
+    if (Clock::now() > until)
+      return comm_abort(ctx, NE_ERR_TIMEOUT,
+                        std::string(what) + " did not complete within " +
+                            std::to_string(c->timeout_ms) + " ms");
+    poll_pause(i);
+  }
+}
+
+ne_status comm_usable(ne_ctx* ctx) {
+  if (!ctx->comm || ctx->comm->aborted || !ctx->comm->comm)
+    return fail(ctx, NE_ERR_STATE, "the communicator was aborted after a failed exchange");
+  return NE_OK;
+}
+
 }  // namespace
+
+// Wait for the compute and comm streams with the exchange's deadline, watching
+// the communicator for asynchronous errors (ne_sync with a communicator).
+ne_status comm_sync(ne_ctx* ctx) {
+  Comm* c = ctx->comm;
+  if (c->aborted || !c->comm) {
+    NE_CUDA(cudaStreamSynchronize(ctx->st));
+    return NE_OK;
+  }
+  const auto until = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  for (int i = 0;; ++i) {
+    const cudaError_t a = cudaStreamQuery(ctx->st);
+    const cudaError_t b = cudaStreamQuery(c->cs);
+    if (a != cudaErrorNotReady && b != cudaErrorNotReady) {
+      NE_CUDA(a);
+      NE_CUDA(b);
+      return NE_OK;
+    }
+    ncclResult_t st = ncclSuccess;
+    nccl().CommGetAsyncError(reinterpret_cast<ncclComm_t>(c->comm), &st);
+    if (st != ncclSuccess && st != ncclInProgress)
+      return comm_abort(ctx, NE_ERR_CUDA, std::string("gradient exchange: ") +
+                                              nccl().GetErrorString(st));
+    if (Clock::now() > until)
+      return comm_abort(ctx, NE_ERR_TIMEOUT,
+                        "the gradient exchange did not complete within " +
+                            std::to_string(c->timeout_ms) + " ms (a rank did not take part)");
+    poll_pause(i);
+  }
+}
 
 void comm_free(ne_ctx* ctx) {
   if (!ctx || !ctx->comm) return;
-  train_drop_step_graph(ctx);
   Comm* c = ctx->comm;
+  // bounded: a communicator whose work cannot finish is aborted, not destroyed
+  const bool idle = c->comm && nccl().loaded && comm_sync(ctx) == NE_OK && c->comm;
+  // captured steps hold NCCL work of this communicator: release them first
+  train_drop_step_graph(ctx);
   if (c->cs) cudaStreamSynchronize(c->cs);
-  if (c->comm && nccl().loaded) nccl().CommDestroy(reinterpret_cast<ncclComm_t>(c->comm));
+  if (idle) nccl().CommDestroy(reinterpret_cast<ncclComm_t>(c->comm));
+  c->comm = nullptr;
   for (cudaEvent_t e : c->ev)
     if (e) cudaEventDestroy(e);
   if (c->cs) cudaStreamDestroy(c->cs);
@@ -113,35 +229,39 @@ ne_status comm_fence_out(ne_ctx* ctx) {
 }
 
 ne_status comm_allreduce(ne_ctx* ctx, float* buf, size_t n) {
+  ne_status s = comm_usable(ctx);
+  if (s != NE_OK) return s;
   Comm* c = ctx->comm;
   ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum,
                                     reinterpret_cast<ncclComm_t>(c->comm), c->cs);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce");
-  return NE_OK;
+  return comm_settle(ctx, r, "ncclAllReduce");
 }
 
 // In place: rank r keeps the sum over ranks of buf[r * n_per_rank, +n_per_rank).
 ne_status comm_reduce_scatter(ne_ctx* ctx, float* buf, size_t n_per_rank) {
+  ne_status s = comm_usable(ctx);
+  if (s != NE_OK) return s;
   Comm* c = ctx->comm;
   ncclResult_t r = nccl().ReduceScatter(buf, buf + (size_t)c->rank * n_per_rank, n_per_rank,
                                         ncclFloat32, ncclSum,
                                         reinterpret_cast<ncclComm_t>(c->comm), c->cs);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclReduceScatter");
-  return NE_OK;
+  return comm_settle(ctx, r, "ncclReduceScatter");
 }
 
 ne_status comm_group(ne_ctx* ctx, bool start) {
+  ne_status s = comm_usable(ctx);
+  if (s != NE_OK) return s;
   ncclResult_t r = start ? nccl().GroupStart() : nccl().GroupEnd();
-  if (r != ncclSuccess) return nccl_fail(ctx, r, start ? "ncclGroupStart" : "ncclGroupEnd");
-  return NE_OK;
+  return comm_settle(ctx, r, start ? "ncclGroupStart" : "ncclGroupEnd");
 }
 
 ne_status comm_allgather(ne_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank) {
+  ne_status s = comm_usable(ctx);
+  if (s != NE_OK) return s;
   Comm* c = ctx->comm;
   ncclResult_t r = nccl().AllGather(send, recv, bytes_per_rank, ncclUint8,
                                     reinterpret_cast<ncclComm_t>(c->comm), c->cs);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllGather");
-  return NE_OK;
+  return comm_settle(ctx, r, "ncclAllGather");
 }
 
 }  // namespace ne
@@ -177,12 +297,28 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) 
   NE_CUDA(cudaStreamCreateWithPriority(&c->cs, cudaStreamNonBlocking, hi));
   c->ev.resize(64, nullptr);
   for (cudaEvent_t& e : c->ev) NE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  c->timeout_ms = ctx->comm_timeout_ms > 0 ? ctx->comm_timeout_ms : default_timeout_ms();
   ncclUniqueId uid;
   std::memcpy(&uid, id, sizeof(uid));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;   // every wait is ours, with a deadline
   ncclComm_t comm = nullptr;
-  ncclResult_t r = api.CommInitRank(&comm, world, uid, rank);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclCommInitRank");
+  ncclResult_t r = api.CommInitRankConfig(&comm, world, uid, rank, &cfg);
   c->comm = comm;
+  if (r != ncclSuccess && r != ncclInProgress) {
+    c->comm = nullptr;
+    c->aborted = true;
+    if (comm) api.CommAbort(comm);
+    return nccl_fail(ctx, r, "ncclCommInitRankConfig");
+  }
+  // the init runs in the background until every rank has joined
+  return comm_settle(ctx, r, "ncclCommInitRankConfig (every rank must join)");
+}
+
+NE_API ne_status ne_comm_set_timeout(ne_ctx* ctx, int timeout_ms) {
+  if (!ctx || timeout_ms < 0) return NE_ERR_INVALID;
+  ctx->comm_timeout_ms = timeout_ms;
+  if (ctx->comm) ctx->comm->timeout_ms = timeout_ms > 0 ? timeout_ms : default_timeout_ms();
   return NE_OK;
 }
 

@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "../../include/ne.h"
+#include "ne_comm.h"
 #include "ne_ctx.h"
 #include "ne_device.cuh"
 #include "ne_internal.h"
@@ -481,7 +482,13 @@ NE_API void ne_free(ne_ctx* ctx) {
 
 NE_API ne_status ne_sync(ne_ctx* ctx) {
   if (!ctx) return NE_ERR_INVALID;
-  NE_CUDA(cudaStreamSynchronize(ctx->st));
+  if (ctx->comm && ctx->comm->world > 1) {
+    // bounded: a gradient exchange that cannot finish aborts the communicator
+    ne_status s = comm_sync(ctx);
+    if (s != NE_OK) return s;
+  } else {
+    NE_CUDA(cudaStreamSynchronize(ctx->st));
+  }
   return check_status(ctx);
 }
 

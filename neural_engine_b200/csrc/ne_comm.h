@@ -18,6 +18,8 @@ struct Comm {
   bool shard = false;              // ZeRO-1: reduce-scatter, sharded AdamW, weight all-gather
   void* gather = nullptr;          // all-gathered (token id, dY row) pairs
   size_t gather_bytes = 0;
+  int timeout_ms = 120000;         // deadline of one wait on the exchange
+  bool aborted = false;            // a deadline passed or NCCL failed: no more exchanges
 };
 
 void comm_free(ne_ctx* ctx);
@@ -30,5 +32,8 @@ ne_status comm_allreduce(ne_ctx* ctx, float* buf, size_t n);
 ne_status comm_allgather(ne_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank);
 ne_status comm_reduce_scatter(ne_ctx* ctx, float* buf, size_t n_per_rank);   // in place
 ne_status comm_group(ne_ctx* ctx, bool start);   // ncclGroupStart / ncclGroupEnd
+// Wait for the compute and comm streams within the exchange's deadline; on
+// expiry or an NCCL error the communicator is aborted (NE_ERR_TIMEOUT / CUDA).
+ne_status comm_sync(ne_ctx* ctx);
 
 }  // namespace ne

@@ -53,6 +53,7 @@ struct ne_ctx {
   int launches = 0;  // kernels enqueued by the current enqueue_* call
   ne::TrainState* train = nullptr;  // training buffers (ne_train_alloc)
   ne::Comm* comm = nullptr;         // NCCL gradient exchange (ne_comm_init)
+  int comm_timeout_ms = 0;          // ne_comm_set_timeout (0: NE_COMM_TIMEOUT_MS or 120 s)
 
   // weights
   void* wpool = nullptr;

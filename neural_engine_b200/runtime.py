@@ -36,7 +36,7 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
             "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
             "ne_comm_set_sharding", "ne_train_gather_state", "ne_train_fwd_bwd_timed",
-            "ne_train_value_ranges")
+            "ne_train_value_ranges", "ne_comm_set_timeout")
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -153,6 +153,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_comm_unique_id.argtypes = [P]
     lib.ne_comm_init.argtypes = [P, P, I, I]
     lib.ne_comm_set_reduce.argtypes = [P, I]
+    lib.ne_comm_set_timeout.argtypes = [P, I]
     lib.ne_comm_set_sharding.argtypes = [P, I]
     lib.ne_train_gather_state.argtypes = [P, I]
     lib.ne_grad_allreduce_async.argtypes = [P]
@@ -302,6 +303,10 @@ class Engine:
     def comm_init(self, uid: bytes, rank: int, world: int):
         buf = C.create_string_buffer(bytes(uid), 128)
         self._check(self.lib.ne_comm_init(self._ctx, buf, int(rank), int(world)))
+
+    def comm_set_timeout(self, timeout_ms: int):
+        """Deadline of every wait on the gradient exchange (0 = default)."""
+        self._check(self.lib.ne_comm_set_timeout(self._ctx, int(timeout_ms)))
 
     def comm_set_reduce(self, on: bool):
         self._check(self.lib.ne_comm_set_reduce(self._ctx, int(bool(on))))
