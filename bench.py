@@ -63,6 +63,12 @@ def parse():
                     help="skip the prefill measurement (config 2)")
     ap.add_argument("--no-stories", action="store_true",
                     help="skip the Stories110M training measurement (config 3)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="skip everything but the prefill measurement (profiling runs)")
+    ap.add_argument("--prefill-seqs", default="256,2048",
+                    help="comma-separated prompt lengths of the prefill measurement")
+    ap.add_argument("--prefill-batch", type=int, default=16,
+                    help="sequences per GPU of the prefill measurement")
     ap.add_argument("--train-only", action="store_true",
                     help="skip the decode headline; print the training object alone "
                          "(profiling runs)")
@@ -74,6 +80,8 @@ def parse():
                     help="with --profile-layers: vocabulary of the profiling model")
     ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
     ap.add_argument("--train-seq", type=int, default=256)
+    ap.add_argument("--train-seqs", default="256,1024",
+                    help="Qwen3 training sequence lengths measured after the decode (config 4)")
     ap.add_argument("--dp-mode", choices=("zero1", "allreduce"), default="zero1",
                     help="training with N > 1: ZeRO-1 (reduce-scatter, sharded AdamW, "
                          "all-gathered bf16 weights) or all-reduce with replicated AdamW")
@@ -524,7 +532,8 @@ def run_prefill(args, rank, local, world, layers, rf, emb, qk):
     import torch.distributed as dist
     import neural_engine_b200 as ne
     cfg = ne.QWEN3_06B
-    B, seqs, reps = 16, (256, 2048), 5
+    B, reps = args.prefill_batch, 5
+    seqs = tuple(int(x) for x in args.prefill_seqs.split(","))
     peak, kind = tensor_peak()
     runs = {}
     eng = ne.Engine(cfg, device=local)
@@ -641,6 +650,13 @@ def main():
         raise SystemExit("--profile-layers needs --train-only")
     layers, rf, emb, qk = host_weights(seed=0, cfg=profile_cfg(args) if args.profile_layers > 0
                                        else None)
+    if args.prefill_only:
+        pf = run_prefill(args, rank, local, world, layers, rf, emb, qk)
+        if rank == 0:
+            print(json.dumps(dict(pf, n_gpus=world, data="synthetic")), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.train_only:
         train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
         if rank == 0:
@@ -759,10 +775,13 @@ def main():
                                                      qk))
     train = train_s1024 = train_stories = None
     if not args.no_train:
-        train = leg("train", lambda: run_train(args, rank, local, world, layers, rf, emb, qk,
-                                               barrier))
-        train_s1024 = leg("train_s1024", lambda: run_train(args, rank, local, world, layers, rf,
-                                                           emb, qk, barrier, S=1024))
+        tseqs = [int(x) for x in args.train_seqs.split(",") if x]
+        if 256 in tseqs:
+            train = leg("train", lambda: run_train(args, rank, local, world, layers, rf, emb, qk,
+                                                   barrier))
+        if 1024 in tseqs:
+            train_s1024 = leg("train_s1024", lambda: run_train(args, rank, local, world, layers,
+                                                               rf, emb, qk, barrier, S=1024))
         if not args.no_stories:
             import neural_engine_b200 as ne_mod
             s_w = host_weights(seed=0, cfg=ne_mod.STORIES110M)

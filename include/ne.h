@@ -370,10 +370,18 @@ NE_API ne_status ne_comm_set_timeout(ne_ctx* ctx, int timeout_ms);
 /* Sum the whole gradient pool over the ranks now (ordered on the stream). */
 NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx);
 /* ZeRO-1 (on = 1; no counterpart in the single-device reference).  Every
- * matrix and the embedding are owned in world equal parts: the gradient
+ * trainable tensor is owned in world parts (ne_shard_range): the gradient
  * buckets reduce-scatter (rank r keeps the sum of part r), the norm adds the
- * ranks' shares, AdamW updates only the owned parts, and the updated bf16
- * compute copies are all-gathered; gains stay replicated.  The fp32 masters
+ * ranks' shares, AdamW updates only the owned parts, and the updated compute
+ * copies (bf16 matrices, fp32 gains) are all-gathered.  The exchange runs on
+ * the library's own kernels over NVLink peer memory: the ranks' buffers are
+ * mapped through CUDA IPC at the first reduced micro-step (collective, outside
+ * any capture), and the ranks order their reads by epoch flags whose waits
+ * are bounded by the ne_comm_set_timeout deadline (NE_ERR_TIMEOUT).  At most
+ * 8 ranks, one process per GPU of one node.  NE_COMM_PX=0 runs the same
+ * scheme over NCCL collectives (equal parts of the matrices and the
+ * embedding, replicated gains).  With gradient accumulation, turn reduction
+ * on only for the last micro-step of each optimizer step.  The fp32 masters
  * and Adam moments of the other parts are then stale until
  * ne_train_gather_state(ctx, 0), which checkpoints and the state getters
  * require; gradients read back need ne_train_gather_state(ctx, 1).  Call
@@ -383,6 +391,13 @@ NE_API ne_status ne_comm_set_sharding(ne_ctx* ctx, int on);
  * masters and both moments (which = 0) or of the reduced gradients (which =
  * 1).  A no-op without sharding. */
 NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which);
+
+/* Which part of an n-element tensor rank `rank` of `world` owns under ZeRO-1
+ * over peer memory: [*off, *off + *len).  Part boundaries sit at multiples of
+ * 64 elements (256-byte aligned fp32, 128-byte aligned bf16) and the last
+ * rank takes the remainder, so every element is owned exactly once and every
+ * rank computes the same table.  Host arithmetic only (no GPU). */
+NE_API ne_status ne_shard_range(long long n, int world, int rank, long long* off, long long* len);
 
 /* The contiguous fp32 gradient pool (every trainable tensor's gradient), for
  * data-parallel reduction by the caller (e.g. an NCCL all-reduce on the

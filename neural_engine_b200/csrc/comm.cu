@@ -53,6 +53,8 @@ struct NcclApi {
   ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
+                            cudaStream_t) = nullptr;
 };
 
 NcclApi& nccl() {
@@ -81,10 +83,11 @@ NcclApi& nccl() {
   api.CommGetAsyncError =
       reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
   api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
+  api.Broadcast = reinterpret_cast<decltype(api.Broadcast)>(sym("ncclBroadcast"));
   if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.AllGather ||
       !api.ReduceScatter || !api.GroupStart || !api.GroupEnd || !api.CommDestroy ||
       !api.GetErrorString || !api.CommInitRankConfig || !api.CommGetAsyncError ||
-      !api.CommAbort) {
+      !api.CommAbort || !api.Broadcast) {
     api.error = "libnccl.so.2 lacks a required symbol";
     return api;
   }
@@ -198,6 +201,7 @@ void comm_free(ne_ctx* ctx) {
   // captured steps hold NCCL work of this communicator: release them first
   train_drop_step_graph(ctx);
   if (c->cs) cudaStreamSynchronize(c->cs);
+  px_free(ctx);
   if (idle) nccl().CommDestroy(reinterpret_cast<ncclComm_t>(c->comm));
   c->comm = nullptr;
   for (cudaEvent_t e : c->ev)
@@ -264,6 +268,29 @@ ne_status comm_allgather(ne_ctx* ctx, const void* send, void* recv, size_t bytes
   return comm_settle(ctx, r, "ncclAllGather");
 }
 
+// In place: every rank receives root's `bytes` at buf.
+ne_status comm_broadcast(ne_ctx* ctx, void* buf, size_t bytes, int root) {
+  ne_status s = comm_usable(ctx);
+  if (s != NE_OK) return s;
+  Comm* c = ctx->comm;
+  ncclResult_t r = nccl().Broadcast(buf, buf, bytes, ncclUint8, root,
+                                    reinterpret_cast<ncclComm_t>(c->comm), c->cs);
+  return comm_settle(ctx, r, "ncclBroadcast");
+}
+
+// Unmap the other ranks' buffers and free the exchange's own (no work of it
+// may be in flight).
+void px_free(ne_ctx* ctx) {
+  if (!ctx->comm) return;
+  PxState& x = ctx->comm->pxs;
+  for (void* p : x.mapped)
+    if (p) cudaIpcCloseMemHandle(p);
+  x.mapped.clear();
+  for (void* p : {(void*)x.flags, (void*)x.d_wsrc, (void*)x.d_asrc, (void*)x.d_chunks})
+    if (p) cudaFree(p);
+  x = PxState();
+}
+
 }  // namespace ne
 
 using namespace ne;
@@ -298,6 +325,10 @@ NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) 
   c->ev.resize(64, nullptr);
   for (cudaEvent_t& e : c->ev) NE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   c->timeout_ms = ctx->comm_timeout_ms > 0 ? ctx->comm_timeout_ms : default_timeout_ms();
+  {
+    const char* e = std::getenv("NE_COMM_PX");
+    c->px = !(e && e[0] == '0');
+  }
   ncclUniqueId uid;
   std::memcpy(&uid, id, sizeof(uid));
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;

@@ -1,4 +1,5 @@
 // gemm.cu -- host side of the tcgen05 GEMM: TMA descriptors, tiling, dispatch.
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdlib>
@@ -365,6 +366,21 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   sh.kb_per_split = kb / splits;
   sh.status = status;
   sh.prefetch_a = c.prefetch_a;
+  // Raster groups when A outgrows a share of L2: M-fastest order re-reads all
+  // of A for every wave of n-tiles once A no longer stays resident, so the
+  // units run in groups of m-tiles whose A panels total ~48 MB (the wave's B
+  // panels take the rest of the 126 MB L2).  NE_GEMM_GROUP_MB overrides
+  // (0 disables).
+  {
+    static const long long budget = [] {
+      const char* e = std::getenv("NE_GEMM_GROUP_MB");
+      return (e ? std::atoll(e) : 48LL) << 20;
+    }();
+    const long long a_panel = (long long)tile_m * c.K * 2;
+    sh.group_m = 0;
+    if (budget > 0 && sh.n_tiles > 1 && a_panel * sh.m_tiles > budget)
+      sh.group_m = (int)std::max<long long>(1, budget / a_panel);
+  }
   const long long units = (long long)sh.m_tiles * sh.n_tiles * splits;
   if (pair) {
     const int cap2 = (c.max_ctas > 0 ? c.max_ctas : num_sms) / 2;

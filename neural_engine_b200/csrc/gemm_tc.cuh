@@ -47,7 +47,32 @@ struct GemmShape {
   int* status;          // device status word (timeouts)
   int prefetch_a;       // A does not depend on the preceding kernel: its first
                         // tiles may be loaded before the PDL dependency wait
+  int group_m;          // m-tiles per raster group (0: one group of all m-tiles)
 };
+
+// Work unit u -> (m tile, n tile, split).  Units run M-fastest inside groups
+// of group_m m-tiles: a wave of consecutive units covers a block of about
+// group_m x (CTAs / group_m) tiles, whose A panels and B panels both stay in
+// L2 while the wave reuses them, instead of sweeping all of A once per n-tile.
+__device__ __forceinline__ void unit_coords(const GemmShape& sh, int u, int& mt, int& nt,
+                                            int& sp) {
+  const int mn = sh.m_tiles * sh.n_tiles;
+  sp = u / mn;
+  const int r = u - sp * mn;
+  const int G = sh.group_m;
+  if (G <= 0 || G >= sh.m_tiles) {
+    mt = r % sh.m_tiles;
+    nt = r / sh.m_tiles;
+    return;
+  }
+  const int per_group = G * sh.n_tiles;
+  const int g = r / per_group;
+  const int first = g * G;
+  const int gm = sh.m_tiles - first < G ? sh.m_tiles - first : G;
+  const int w = r - g * per_group;
+  mt = first + w % gm;
+  nt = w / gm;
+}
 
 // CG = 2: a CTA pair shares each 256 x BN tile (cta_group::2); each CTA
 // stages its 128 rows of A and BN/2 rows of B.
@@ -681,7 +706,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = policy_evict_first();
+      // A is streamed (evict first) unless a raster group reuses its panels
+      const uint64_t pol_a = sh.group_m > 0 ? policy_evict_normal() : policy_evict_first();
       const uint64_t pol_b = policy_evict_last();
       // pair mode: every load of both CTAs completes on the even CTA's full
       // barrier, which the even CTA arms for the bytes of both
@@ -716,9 +742,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // programmatic-dependency wait; their B tiles follow after it.
       int pre = 0;
       if (sh.prefetch_a && u_first < units) {
-        const int u = u_first;
-        const int mt = u % sh.m_tiles;
-        const int kb0 = (u / sh.m_tiles / sh.n_tiles) * sh.kb_per_split;
+        int mt, nt_unused, sp0;
+        unit_coords(sh, u_first, mt, nt_unused, sp0);
+        const int kb0 = sp0 * sh.kb_per_split;
         pre = sh.kb_per_split < STAGES ? sh.kb_per_split : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
           if (arms) mbar_arrive_expect_tx(full_bar + 8 * kb, CG * C::STAGE_BYTES);
@@ -732,10 +758,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       bool ok = true;
       bool first = true;
       for (int u = u_first; u < units && ok; u += u_step) {
-        const int mt = u % sh.m_tiles;
-        const int rest = u / sh.m_tiles;
-        const int nt = rest % sh.n_tiles;
-        const int sp = rest / sh.n_tiles;
+        int mt, nt, sp;
+        unit_coords(sh, u, mt, nt, sp);
         const int kb0 = sp * sh.kb_per_split;
         for (int kb = 0; kb < sh.kb_per_split; ++kb) {
           const uint32_t sa = tiles + stage * C::STAGE_BYTES;
@@ -830,10 +854,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t acc_phase = 0;
     const int row0 = (int)crank * GEMM_BM;   // this CTA's rows within a unit
     for (int u = u_first; u < units; u += u_step) {
-      const int mt = u % sh.m_tiles;
-      const int rest = u / sh.m_tiles;
-      const int nt = rest % sh.n_tiles;
-      const int sp = rest / sh.n_tiles;
+      int mt, nt, sp;
+      unit_coords(sh, u, mt, nt, sp);
       if constexpr (EpiHasPrefetch<Epi>::value) {
         // this unit's rows (first unit only: the others were hinted one unit
         // ahead), then the next unit's, so they are L2-resident by the time
@@ -843,9 +865,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           Epi::prefetch(ep, mt * TILE_M + row0 + row_in_tile, nt * BN, BN, sh.M, sh.N);
         const int un = u + u_step;
         if (un < units && chunk0 == 0) {
-          const int rn = un / sh.m_tiles;
-          Epi::prefetch(ep, (un % sh.m_tiles) * TILE_M + row0 + row_in_tile, (rn % sh.n_tiles) * BN, BN,
-                        sh.M, sh.N);
+          int mn, nn, sn;
+          unit_coords(sh, un, mn, nn, sn);
+          Epi::prefetch(ep, mn * TILE_M + row0 + row_in_tile, nn * BN, BN, sh.M, sh.N);
         }
       }
       // warp-uniform outcome: tcgen05.ld below is a warp-collective instruction

@@ -5,8 +5,24 @@
 #include <vector>
 
 #include "../../include/ne.h"
+#include "ne_px.h"
 
 namespace ne {
+
+// Peer-memory ZeRO-1 exchange (px.cu): the other ranks' pools mapped through
+// CUDA IPC, this rank's flag words, and the chunk lists of every exchange.
+struct PxState {
+  bool ready = false;
+  uint32_t* flags = nullptr;           // this rank's flag words (device)
+  std::vector<void*> mapped;           // the other ranks' mapped buffers
+  PxTables T;                          // flag and gradient bases of every rank
+  const char** d_wsrc = nullptr;       // [world] weight pool of each rank (device table)
+  const char** d_asrc = nullptr;       // [world] activation pool of each rank
+  PxChunk* d_chunks = nullptr;         // every chunk list below, one allocation
+  std::vector<int> rs_first, rs_count; // per bucket (0 = tail, 1 + layer)
+  int ag_first = 0, ag_count = 0;      // weight all-gather
+  int em_first = 0, em_count = 0;      // (token id, dY row) gather
+};
 
 struct Comm {
   void* comm = nullptr;            // ncclComm_t
@@ -20,6 +36,8 @@ struct Comm {
   size_t gather_bytes = 0;
   int timeout_ms = 120000;         // deadline of one wait on the exchange
   bool aborted = false;            // a deadline passed or NCCL failed: no more exchanges
+  bool px = true;                  // ZeRO-1 over peer memory (NE_COMM_PX=0: NCCL collectives)
+  PxState pxs;
 };
 
 void comm_free(ne_ctx* ctx);
@@ -35,5 +53,7 @@ ne_status comm_group(ne_ctx* ctx, bool start);   // ncclGroupStart / ncclGroupEn
 // Wait for the compute and comm streams within the exchange's deadline; on
 // expiry or an NCCL error the communicator is aborted (NE_ERR_TIMEOUT / CUDA).
 ne_status comm_sync(ne_ctx* ctx);
+ne_status comm_broadcast(ne_ctx* ctx, void* buf, size_t bytes, int root);   // in place
+void px_free(ne_ctx* ctx);   // unmap the other ranks' buffers (streams idle)
 
 }  // namespace ne

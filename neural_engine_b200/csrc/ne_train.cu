@@ -63,6 +63,7 @@ struct TrainState {
   float* pool = nullptr;                 // masters + grads + m + v (fp32)
   size_t pool_floats = 0;
   void* act_pool = nullptr;              // saved activations + scratch
+  size_t act_bytes = 0;
   std::vector<Seg> segs;
   AdamSeg* d_segs = nullptr;             // device copy of the segment table
   float d_segs_wd = -2.f;                // weight decay the device table holds
@@ -128,6 +129,12 @@ void train_drop_step_graph(ne_ctx* ctx) {
 void free_train(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return;
   TrainState* t = ctx->train;
+  if (ctx->comm) {
+    // the peer mappings and chunk lists describe these pools
+    cudaStreamSynchronize(ctx->st);
+    if (ctx->comm->cs) cudaStreamSynchronize(ctx->comm->cs);
+    px_free(ctx);
+  }
   if (t->d_segs) cudaFree(t->d_segs);
   if (t->d_chunks) cudaFree(t->d_chunks);
   if (t->embed_scratch) cudaFree(t->embed_scratch);
@@ -396,6 +403,7 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
   uint8_t* base = nullptr;
   if ((s = dalloc(ctx, &base, bytes)) != NE_OK) return s;
   t->act_pool = base;
+  t->act_bytes = bytes;
   t->A.resize(L);
   for (size_t l = 0; l < L; ++l) {
     TrainActs& a = t->A[l];
@@ -487,25 +495,237 @@ static bool comm_active(const ne_ctx* ctx) {
   return ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce;
 }
 
-// ZeRO-1 (ne_comm_set_sharding): each matrix segment (and the embedding) whose
-// size splits into world equal parts of a multiple of 4 elements is owned in
-// parts -- rank r reduces, updates and keeps current the r-th part, and the
-// updated bf16 compute copies are all-gathered after the optimizer step; the
-// gains (and any segment that does not split) stay replicated.
+// ZeRO-1 (ne_comm_set_sharding): rank r owns part r of the training state.
+// Over peer memory (the default) every tensor is owned in parts with
+// boundaries at multiples of 64 elements (px_part), gains included.  Over NCCL
+// (NE_COMM_PX=0) a matrix segment (or the embedding) whose size splits into
+// world equal parts of a multiple of 4 elements is owned in parts and the
+// gains stay replicated.  Rank r reduces, updates and keeps current its parts;
+// the updated compute copies are all-gathered after the optimizer step.
 static bool shard_mode(const ne_ctx* ctx) {   // ownership (optimizer), whatever the reduction
   return ctx->comm && ctx->comm->world > 1 && ctx->comm->shard;
 }
 static bool shard_active(const ne_ctx* ctx) {   // the buckets reduce-scatter
   return comm_active(ctx) && ctx->comm->shard;
 }
-static bool seg_sharded(const ne_ctx* ctx, const Seg& sg) {
-  if (!shard_mode(ctx) || sg.w16 == nullptr) return false;
-  const long long W = ctx->comm->world;
-  return sg.n % W == 0 && (sg.n / W) % 4 == 0;
+static bool px_active(const ne_ctx* ctx) { return shard_active(ctx) && ctx->comm->px; }
+
+// The part [*off, *off + *len) of segment sg that `rank` owns; false (the
+// whole segment) when the segment is replicated.
+static bool seg_owned(const ne_ctx* ctx, const Seg& sg, int rank, long long* off,
+                      long long* len) {
+  if (shard_mode(ctx)) {
+    const int W = ctx->comm->world;
+    if (ctx->comm->px) {
+      px_part(sg.n, W, rank, off, len);
+      return true;
+    }
+    if (sg.w16 != nullptr && sg.n % W == 0 && (sg.n / W) % 4 == 0) {
+      *len = sg.n / W;
+      *off = *len * rank;
+      return true;
+    }
+  }
+  *off = 0;
+  *len = sg.n;
+  return false;
 }
-static long long shard_len(const ne_ctx* ctx, const Seg& sg) { return sg.n / ctx->comm->world; }
+static bool seg_sharded(const ne_ctx* ctx, const Seg& sg) {
+  long long o, n;
+  return seg_owned(ctx, sg, 0, &o, &n);
+}
+static long long shard_len(const ne_ctx* ctx, const Seg& sg) {
+  long long o, n;
+  seg_owned(ctx, sg, ctx->comm->rank, &o, &n);
+  return n;
+}
 static long long shard_off(const ne_ctx* ctx, const Seg& sg) {
-  return shard_len(ctx, sg) * ctx->comm->rank;
+  long long o, n;
+  seg_owned(ctx, sg, ctx->comm->rank, &o, &n);
+  return o;
+}
+
+// Segments [s0, s1) of exchange bucket b: 0 = tail (final norm + embedding),
+// 1 + l = layer l.
+static void bucket_segs(const TrainState* t, int b, int* s0, int* s1) {
+  const int tail0 = (int)t->segs.size() - 2;
+  if (b == 0) {
+    *s0 = tail0;
+    *s1 = (int)t->segs.size();
+    return;
+  }
+  const int l = b - 1;
+  *s0 = t->P[l].seg0;
+  *s1 = l + 1 < (int)t->P.size() ? t->P[l + 1].seg0 : tail0;
+}
+
+// Map the other ranks' pools and build the chunk lists of the peer-memory
+// exchange.  Collective (every rank, outside any stream capture): the IPC
+// handles travel in one NCCL all-gather.
+static ne_status px_setup(ne_ctx* ctx) {
+  TrainState* t = ctx->train;
+  Comm* c = ctx->comm;
+  PxState& x = c->pxs;
+  const int W = c->world, R = c->rank;
+  if (W > PX_MAX_WORLD)
+    return fail(ctx, NE_ERR_UNSUPPORTED, "peer-memory exchange: at most 8 ranks (NE_COMM_PX=0)");
+  const int L = ctx->cfg.n_layers;
+  ne_status s;
+  if ((s = dalloc(ctx, &x.flags, 256)) != NE_OK) return s;
+  NE_CUDA(cudaMemset(x.flags, 0, 256 * sizeof(uint32_t)));
+  // the (token id, dY row) gather buffer: [world][M] ids, then [world][M][D] rows
+  const int M = t->M, D = ctx->cfg.dim;
+  const size_t ids_bytes = ((size_t)W * M * 4 + 255) & ~(size_t)255;
+  const size_t need = ids_bytes + (size_t)W * M * D * 4;
+  if (c->gather_bytes < need) {
+    if (c->gather) NE_CUDA(cudaFree(c->gather));
+    c->gather = nullptr;
+    c->gather_bytes = 0;
+    uint8_t* g = nullptr;
+    if ((s = dalloc(ctx, &g, need)) != NE_OK) return s;
+    c->gather = g;
+    c->gather_bytes = need;
+  }
+  struct Rec {
+    cudaIpcMemHandle_t h[4];   // training pool, weight pool, activation pool, flags
+    long long pool_floats, act_bytes;
+    int M, L;
+  };
+  Rec mine{};
+  void* bases[4] = {t->pool, ctx->wpool, t->act_pool, x.flags};
+  for (int i = 0; i < 4; ++i) NE_CUDA(cudaIpcGetMemHandle(&mine.h[i], bases[i]));
+  mine.pool_floats = (long long)t->pool_floats;
+  mine.act_bytes = (long long)t->act_bytes;
+  mine.M = M;
+  mine.L = L;
+  Rec* d_rec = nullptr;
+  if ((s = dalloc(ctx, reinterpret_cast<uint8_t**>(&d_rec), sizeof(Rec) * (W + 1))) != NE_OK)
+    return s;
+  std::vector<Rec> all(W);
+  NE_CUDA(cudaMemcpy(d_rec + W, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
+  NE_CUDA(cudaDeviceSynchronize());   // the zeroed flags too, before any rank may read them
+  if ((s = comm_fence_in(ctx)) != NE_OK || (s = comm_allgather(ctx, d_rec + W, d_rec,
+                                                               sizeof(Rec))) != NE_OK ||
+      (s = comm_fence_out(ctx)) != NE_OK || (s = comm_sync(ctx)) != NE_OK) {
+    cudaFree(d_rec);
+    return s;
+  }
+  NE_CUDA(cudaMemcpy(all.data(), d_rec, sizeof(Rec) * W, cudaMemcpyDeviceToHost));
+  cudaFree(d_rec);
+  std::vector<const char*> wsrc(W), asrc(W);
+  for (int p = 0; p < W; ++p) {
+    const Rec& r = all[p];
+    if (r.pool_floats != mine.pool_floats || r.act_bytes != mine.act_bytes || r.M != M ||
+        r.L != L)
+      return fail(ctx, NE_ERR_INVALID, "peer-memory exchange: ranks differ in model or batch");
+    char* b[4];
+    if (p == R) {
+      for (int i = 0; i < 4; ++i) b[i] = static_cast<char*>(bases[i]);
+    } else {
+      for (int i = 0; i < 4; ++i) {
+        void* q = nullptr;
+        NE_CUDA(cudaIpcOpenMemHandle(&q, r.h[i], cudaIpcMemLazyEnablePeerAccess));
+        x.mapped.push_back(q);
+        b[i] = static_cast<char*>(q);
+      }
+    }
+    x.T.grad[p] = reinterpret_cast<float*>(b[0]) + (t->grad_pool - t->pool);
+    wsrc[p] = b[1];
+    asrc[p] = b[2];
+    x.T.flags[p] = reinterpret_cast<uint32_t*>(b[3]);
+  }
+  x.T.world = W;
+  x.T.rank = R;
+  x.T.limit_ns = (unsigned long long)c->timeout_ms * 1000000ull / 2;
+  // chunk lists
+  std::vector<PxChunk> ch;
+  constexpr int RS_CHUNK = 8192;        // floats
+  constexpr int CP_CHUNK = 64 << 10;    // bytes
+  x.rs_first.assign(L + 1, 0);
+  x.rs_count.assign(L + 1, 0);
+  for (int b = 0; b <= L; ++b) {
+    int s0, s1;
+    bucket_segs(t, b, &s0, &s1);
+    x.rs_first[b] = (int)ch.size();
+    for (int k = s0; k < s1; ++k) {
+      const Seg& sg = t->segs[k];
+      long long off, len;
+      seg_owned(ctx, sg, R, &off, &len);
+      const long long g0 = (sg.g - t->grad_pool) + off;
+      for (long long i = 0; i < len; i += RS_CHUNK)
+        ch.push_back({0, g0 + i, (int)std::min<long long>(RS_CHUNK, len - i), R});
+    }
+    x.rs_count[b] = (int)ch.size() - x.rs_first[b];
+  }
+  x.ag_first = (int)ch.size();
+  const char* wbase = static_cast<const char*>(ctx->wpool);
+  for (const Seg& sg : t->segs) {
+    for (int p = 0; p < W; ++p) {
+      if (p == R) continue;
+      long long off, len;
+      seg_owned(ctx, sg, p, &off, &len);
+      const long long o = sg.w16 ? reinterpret_cast<const char*>(sg.w16 + off) - wbase
+                                 : reinterpret_cast<const char*>(sg.w + off) - wbase;
+      const long long bytes = len * (sg.w16 ? 2 : 4);
+      for (long long i = 0; i < bytes; i += CP_CHUNK)
+        ch.push_back({o + i, o + i, (int)std::min<long long>(CP_CHUNK, bytes - i), p});
+    }
+  }
+  x.ag_count = (int)ch.size() - x.ag_first;
+  x.em_first = (int)ch.size();
+  const char* abase = static_cast<const char*>(t->act_pool);
+  const long long ids_off = reinterpret_cast<const char*>(t->ids) - abase;
+  const long long dy_off = reinterpret_cast<const char*>(t->dY) - abase;
+  for (int p = 0; p < W; ++p) {
+    ch.push_back({ids_off, (long long)p * M * 4, M * 4, p});
+    const long long rows = (long long)M * D * 4;
+    for (long long i = 0; i < rows; i += CP_CHUNK)
+      ch.push_back({dy_off + i, (long long)ids_bytes + (long long)p * rows + i,
+                    (int)std::min<long long>(CP_CHUNK, rows - i), p});
+  }
+  x.em_count = (int)ch.size() - x.em_first;
+  if ((s = dalloc(ctx, &x.d_chunks, ch.size())) != NE_OK) return s;
+  NE_CUDA(cudaMemcpy(x.d_chunks, ch.data(), ch.size() * sizeof(PxChunk), cudaMemcpyHostToDevice));
+  if ((s = dalloc(ctx, reinterpret_cast<uint8_t**>(&x.d_wsrc), sizeof(char*) * W)) != NE_OK ||
+      (s = dalloc(ctx, reinterpret_cast<uint8_t**>(&x.d_asrc), sizeof(char*) * W)) != NE_OK)
+    return s;
+  NE_CUDA(cudaMemcpy(x.d_wsrc, wsrc.data(), sizeof(char*) * W, cudaMemcpyHostToDevice));
+  NE_CUDA(cudaMemcpy(x.d_asrc, asrc.data(), sizeof(char*) * W, cudaMemcpyHostToDevice));
+  x.ready = true;
+  return NE_OK;
+}
+
+// The exchange is set up (it is at the first reduced micro-step; a call
+// before that sets it up here, outside any capture).
+static ne_status px_ready(ne_ctx* ctx) {
+  if (ctx->comm->aborted)
+    return fail(ctx, NE_ERR_STATE, "the exchange was aborted after a failed step");
+  return ctx->comm->pxs.ready ? NE_OK : px_setup(ctx);
+}
+
+// CTAs of the exchange kernels on the comm stream (they share the SMs with
+// the backward's GEMMs): NE_PX_CTAS, default 64.
+static int px_ctas() {
+  static const int n = [] {
+    const char* e = std::getenv("NE_PX_CTAS");
+    const int v = e ? std::atoi(e) : 0;
+    return v > 0 ? v : 64;
+  }();
+  return n;
+}
+
+// Publish bucket b's gradients (compute stream) and reduce this rank's part
+// of them over the ranks (comm stream).
+static ne_status px_bucket(ne_ctx* ctx, int b) {
+  if (ctx->comm->aborted)
+    return fail(ctx, NE_ERR_STATE, "the exchange was aborted after a failed step");
+  PxState& x = ctx->comm->pxs;
+  NE_CUDA(px_signal(x.flags, PX_READY0 + b, ctx->st));
+  ne_status s = comm_fence_in(ctx);
+  if (s != NE_OK) return s;
+  NE_CUDA(px_reduce(x.T, x.d_chunks + x.rs_first[b], x.rs_count[b], PX_READY0 + b, px_ctas(),
+                    ctx->d_status, ctx->comm->cs));
+  return NE_OK;
 }
 
 // One bucket (segments [s0, s1)): reduce-scatter the owned segments, all-reduce
@@ -550,6 +770,18 @@ static ne_status gather_owned(ne_ctx* ctx, int which) {
 static ne_status comm_after_lmhead(ne_ctx* ctx) {
   if (!comm_active(ctx)) return NE_OK;
   TrainState* t = ctx->train;
+  if (px_active(ctx)) {
+    if (!ctx->comm->pxs.ready) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      NE_CUDA(cudaStreamIsCapturing(ctx->st, &cs));
+      if (cs != cudaStreamCaptureStatusNone)
+        return fail(ctx, NE_ERR_STATE, "peer-memory exchange set up inside a capture");
+    }
+    ne_status s = px_ready(ctx);
+    if (s != NE_OK) return s;
+    NE_CUDA(px_epoch(ctx->comm->pxs.flags, ctx->st));
+    return px_bucket(ctx, 0);
+  }
   ne_status s = comm_fence_in(ctx);
   if (s != NE_OK) return s;
   if (shard_active(ctx)) return exchange_segments(ctx, (int)t->segs.size() - 2, (int)t->segs.size());
@@ -559,6 +791,7 @@ static ne_status comm_after_lmhead(ne_ctx* ctx) {
 static ne_status comm_after_layer(ne_ctx* ctx, int l) {
   if (!comm_active(ctx)) return NE_OK;
   TrainState* t = ctx->train;
+  if (px_active(ctx)) return px_bucket(ctx, 1 + l);
   ne_status s = comm_fence_in(ctx);
   if (s != NE_OK) return s;
   if (shard_active(ctx)) {
@@ -598,6 +831,21 @@ static ne_status comm_embed_bwd(ne_ctx* ctx) {
   (void)V;
   if (!comm_active(ctx)) return embed_scatter(ctx, t->ids, t->dY, M);
   Comm* c = ctx->comm;
+  if (px_active(ctx)) {
+    // after this rank's reduce-scatters (comm stream order) and its last
+    // layer's backward (fence): publish, then gather every rank's pairs
+    PxState& x = c->pxs;
+    const size_t ids_bytes = ((size_t)c->world * M * 4 + 255) & ~(size_t)255;
+    ne_status s;
+    if ((s = comm_fence_in(ctx)) != NE_OK) return s;
+    NE_CUDA(px_signal(x.flags, PX_EMBED, c->cs));
+    NE_CUDA(px_copy(x.T, x.d_asrc, static_cast<char*>(c->gather), x.d_chunks + x.em_first,
+                    x.em_count, PX_EMBED, px_ctas(), ctx->d_status, c->cs));
+    if ((s = comm_fence_out(ctx)) != NE_OK) return s;
+    return embed_scatter(ctx, reinterpret_cast<int32_t*>(c->gather),
+                         reinterpret_cast<float*>(static_cast<uint8_t*>(c->gather) + ids_bytes),
+                         c->world * M);
+  }
   const size_t ids_bytes = ((size_t)c->world * M * 4 + 255) & ~(size_t)255;
   const size_t need = ids_bytes + (size_t)c->world * M * D * 4;
   if (c->gather_bytes < need) {
@@ -1123,9 +1371,14 @@ static ne_status enqueue_norm(ne_ctx* ctx, float grad_scale, float grad_clip) {
                                 grad_scale, grad_clip, t->norm_out, ctx->st, sharded ? 1 : 0));
   if (!sharded) return NE_OK;
   ne_status s;
-  if ((s = comm_fence_in(ctx)) != NE_OK || (s = comm_allreduce(ctx, t->norm_out + 2, 1)) != NE_OK ||
-      (s = comm_fence_out(ctx)) != NE_OK)
+  if (ctx->comm->px) {
+    if ((s = px_ready(ctx)) != NE_OK) return s;
+    NE_CUDA(px_norm(ctx->comm->pxs.T, t->norm_out, ctx->d_status, ctx->st));
+  } else if ((s = comm_fence_in(ctx)) != NE_OK ||
+             (s = comm_allreduce(ctx, t->norm_out + 2, 1)) != NE_OK ||
+             (s = comm_fence_out(ctx)) != NE_OK) {
     return s;
+  }
   NE_LAUNCH(launch_norm_finish(t->norm_out, grad_scale, grad_clip, ctx->st));
   return NE_OK;
 }
@@ -1161,7 +1414,14 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
   if (shard_mode(ctx)) {
     // every rank needs the whole updated compute copy; the fp32 masters and
     // moments stay with their owners until ne_train_gather_state
-    if ((s = gather_owned(ctx, 4)) != NE_OK) return s;
+    if (ctx->comm->px) {
+      PxState& x = ctx->comm->pxs;
+      NE_CUDA(px_signal(x.flags, PX_W16, ctx->st));
+      NE_CUDA(px_copy(x.T, x.d_wsrc, static_cast<char*>(ctx->wpool), x.d_chunks + x.ag_first,
+                      x.ag_count, PX_W16, ctx->num_sms * 2, ctx->d_status, ctx->st));
+    } else if ((s = gather_owned(ctx, 4)) != NE_OK) {
+      return s;
+    }
     t->state_gathered = false;
   }
   if ((s = ne_train_zero_grads(ctx)) != NE_OK) return s;
@@ -1181,6 +1441,31 @@ NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which) {
   NE_CUDA(cudaSetDevice(ctx->device));
   if (!shard_mode(ctx)) return NE_OK;
   ne_status s;
+  if (ctx->comm->px) {
+    // not on the step's path: NCCL broadcasts of each rank's parts (the
+    // parts differ in length by a few elements, which rules out all-gather)
+    TrainState* t = ctx->train;
+    if ((s = comm_sync(ctx)) != NE_OK || (s = comm_fence_in(ctx)) != NE_OK ||
+        (s = comm_group(ctx, true)) != NE_OK)
+      return s;
+    for (int a = (which == 1 ? 3 : 0); a < (which == 1 ? 4 : 3) && s == NE_OK; ++a) {
+      for (const Seg& sg : t->segs) {
+        if (a == 0 && sg.w16 == nullptr) continue;   // the gains' masters are all-gathered each step
+        float* arr = a == 0 ? sg.w : a == 1 ? sg.m : a == 2 ? sg.v : sg.g;
+        for (int p = 0; p < ctx->comm->world && s == NE_OK; ++p) {
+          long long off, len;
+          seg_owned(ctx, sg, p, &off, &len);
+          if (len > 0) s = comm_broadcast(ctx, arr + off, (size_t)len * 4, p);
+        }
+      }
+    }
+    const ne_status e = comm_group(ctx, false);
+    if (s != NE_OK) return s;
+    if (e != NE_OK) return e;
+    if ((s = comm_fence_out(ctx)) != NE_OK) return s;
+    if (which == 0) t->state_gathered = true;
+    return ne_sync(ctx);
+  }
   if (which == 1) {
     if ((s = gather_owned(ctx, 3)) != NE_OK) return s;
   } else {
@@ -1189,6 +1474,13 @@ NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which) {
     ctx->train->state_gathered = true;
   }
   return ne_sync(ctx);
+}
+
+// The ZeRO-1 partition of the peer-memory exchange (host arithmetic only).
+NE_API ne_status ne_shard_range(long long n, int world, int rank, long long* off, long long* len) {
+  if (n < 0 || world < 1 || rank < 0 || rank >= world || !off || !len) return NE_ERR_INVALID;
+  px_part(n, world, rank, off, len);
+  return NE_OK;
 }
 
 // Learning-rate schedule of train.m:851-858: linear warmup, then cosine decay

@@ -36,7 +36,18 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
             "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
             "ne_comm_set_sharding", "ne_train_gather_state", "ne_train_fwd_bwd_timed",
-            "ne_train_value_ranges", "ne_comm_set_timeout")
+            "ne_train_value_ranges", "ne_comm_set_timeout", "ne_shard_range")
+
+def shard_range(n: int, world: int, rank: int, lib=None):
+    """(offset, length) of the part of an n-element tensor that `rank` owns
+    under ZeRO-1 over peer memory (ne_shard_range; host arithmetic)."""
+    lib = lib or load_library()
+    off, ln = C.c_longlong(0), C.c_longlong(0)
+    st = lib.ne_shard_range(int(n), int(world), int(rank), C.byref(off), C.byref(ln))
+    if st != 0:
+        raise NeError(st, "ne_shard_range")
+    return off.value, ln.value
+
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
                "gemm_w13", "swiglu", "gemm_w2", "gemm_lm_head", "embed_argmax")
@@ -154,6 +165,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_comm_init.argtypes = [P, P, I, I]
     lib.ne_comm_set_reduce.argtypes = [P, I]
     lib.ne_comm_set_timeout.argtypes = [P, I]
+    lib.ne_shard_range.argtypes = [C.c_longlong, I, I, C.POINTER(C.c_longlong),
+                                   C.POINTER(C.c_longlong)]
     lib.ne_comm_set_sharding.argtypes = [P, I]
     lib.ne_train_gather_state.argtypes = [P, I]
     lib.ne_grad_allreduce_async.argtypes = [P]

@@ -1,14 +1,18 @@
 """GPU, two or more devices: the in-library data-parallel gradient exchange
-(ne_comm_init + the bucketed NCCL all-reduce overlapped with the backward,
-plus the all-gathered input-embedding scatter).
+(ne_comm_init; per-layer buckets overlapped with the backward, plus the
+gathered input-embedding scatter), in three forms: the NCCL all-reduce with a
+replicated AdamW, ZeRO-1 over NVLink peer memory (the default sharded form:
+the library's own reduce-scatter / all-gather kernels with epoch flags), and
+ZeRO-1 over NCCL collectives (NE_COMM_PX=0).
 
-Two ranks each take half of a global batch; after one ne_train_fwd_bwd the
-gradient pool of every rank must equal (sum over ranks) the gradient of the
-mean loss over each half -- i.e. with grad_scale = 1/world, the gradient of
-the mean loss over the global batch computed on one device.  Tolerance:
-relative L2 <= 1e-4 per tensor (the dW reductions run over a different token
-split, so fp32 summation order differs).  Skipped with fewer than two GPUs:
-ranks that wait on one another are never run as processes sharing a GPU.
+world ranks each take an equal share of a global batch; after one
+ne_train_fwd_bwd the gradient pool of every rank must equal (sum over ranks)
+the gradient of the mean loss over each share -- i.e. with grad_scale =
+1/world, the gradient of the mean loss over the global batch computed on one
+device.  Tolerance: relative L2 <= 1e-4 per tensor (the dW reductions run over
+a different token split, so fp32 summation order differs).  World sizes above
+the GPU count are skipped: ranks that wait on one another are never run as
+processes sharing a GPU.
 """
 import numpy as np
 import pytest
@@ -42,12 +46,13 @@ def _rank(rank, world, uid, tok, q, mode):
     import sys
     import os
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ["NE_COMM_PX"] = "0" if mode == "zero1_nccl" else "1"
     try:
         torch.cuda.set_device(rank)
         B = tok.shape[0] // world
         e = _setup(rank, B, tok.shape[1] - 1)
         e.comm_init(uid, rank, world)
-        zero1 = mode == "zero1"
+        zero1 = mode in ("zero1", "zero1_nccl")
         if zero1:
             e.comm_set_sharding(True)
         loss = e.train_fwd_bwd(tok[rank * B:(rank + 1) * B])   # eager first micro-step
@@ -77,18 +82,19 @@ def _rel(a, b):
     return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
 
 
-@pytest.mark.parametrize("mode", ["allreduce", "zero1"])
-def test_bucketed_allreduce_equals_global_batch_gradient(mode):
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["allreduce", "zero1", "zero1_nccl"])
+def test_bucketed_allreduce_equals_global_batch_gradient(mode, world):
     """allreduce: every rank sums every bucket and takes the whole AdamW step;
-    zero1: buckets reduce-scatter, each rank updates its parts, the bf16
-    copies are all-gathered (ne_comm_set_sharding)."""
+    zero1 / zero1_nccl: buckets reduce-scatter, each rank updates its parts,
+    the bf16 copies are all-gathered (ne_comm_set_sharding), over peer memory
+    or over NCCL."""
     n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("needs two GPUs")
+    if n < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     import neural_engine_b200 as ne
     from oracle import model as om
-    world = 2
     cfg = _cfg()
     S = 32
     tok = om.prompt_tokens(cfg.vocab, S + 1, 8, batch=2 * world)
@@ -113,7 +119,7 @@ def test_bucketed_allreduce_equals_global_batch_gradient(mode):
     ref_norm = e.adamw_step(1, 1e-3)
     ref_w = e.get_masters()
     e.close()
-    (g0, g0b), (g1, g1b) = res[0][2], res[1][2]
+    (g0, g0b), (g1, g1b) = res[0][2], res[world - 1][2]
     # the captured replay reproduces the eager exchange on both ranks
     for L in range(cfg.n_layers):
         for k in ref["layers"][L]:
@@ -131,11 +137,15 @@ def test_bucketed_allreduce_equals_global_batch_gradient(mode):
     assert np.array_equal(g0["embed"], g1["embed"])
     assert _rel(np.asarray(g0["embed"]) / world, ref["embed"]) <= 1e-4
     assert _rel(np.asarray(g0["rms_final"]) / world, ref["rms_final"]) <= 1e-4
-    assert abs(res[0][3] - ref_norm) <= 1e-4 * ref_norm
+    for r in range(world):
+        assert abs(res[r][3] - ref_norm) <= 1e-4 * ref_norm, (r, res[r][3], ref_norm)
     # replicas stay identical (the embedding scatter is deterministic), and
     # match the single-device step up to sign flips of near-zero gradients
     # in Adam's first update
-    for L in range(cfg.n_layers):
-        assert np.array_equal(res[0][4]["layers"][L]["Wo"], res[1][4]["layers"][L]["Wo"])
-        assert _rel(res[1][4]["layers"][L]["Wo"], ref_w["layers"][L]["Wo"]) <= 1e-3
-    assert np.array_equal(res[0][4]["embed"], res[1][4]["embed"])
+    for r in range(1, world):
+        for L in range(cfg.n_layers):
+            for k in ("Wq", "Wo", "W1", "W2", "rms_att"):
+                assert np.array_equal(res[0][4]["layers"][L][k], res[r][4]["layers"][L][k]), \
+                    (r, L, k)
+            assert _rel(res[r][4]["layers"][L]["Wo"], ref_w["layers"][L]["Wo"]) <= 1e-3
+        assert np.array_equal(res[0][4]["embed"], res[r][4]["embed"])

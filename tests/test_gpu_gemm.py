@@ -324,3 +324,18 @@ def test_gemm_swiglu_transposed_epilogue(eng, F, N, K):
     assert torch.isfinite(got).all()
     err = (got - ref).abs().max().item()
     assert err <= 2 ** -8 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M,N,K", [(4000, 600, 8192), (1800, 1100, 16384), (520, 300, 65536)])
+def test_gemm_grouped_raster(eng, M, N, K):
+    """A panels beyond ~48 MB: the units run in raster groups of m-tiles
+    (ragged last group, ragged edge tiles; the first two shapes run on CTA
+    pairs, the third on single CTAs with its 128-row A panels of 16 MB)."""
+    a, b = _bf16((M, K), 21, 0.05), _bf16((N, K), 22, 0.05)
+    da, db = a.cuda(), b.cuda()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    eng.gemm_device(da.data_ptr(), K, M, db.data_ptr(), K, N, K, 1, out.data_ptr(), N)
+    eng.sync()
+    ref = _ref(a, b)
+    err = (out.cpu().double() - ref).abs().max().item()
+    assert err <= _tol(a, b, K), err
