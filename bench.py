@@ -435,6 +435,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     eng = ne.Engine(cfg, device=local)
     eng.set_weights(layers, rf, emb, qk)
     eng.train_alloc(B, S)
+    log(f"train {model} S={S}: allocated")
     stream = torch.cuda.ExternalStream(eng.stream_ptr)
     gen = torch.Generator(device="cuda").manual_seed((2000 if stories else 3000) + rank)
     tok = torch.randint(0, cfg.vocab, (B, S + 1), generator=gen, device="cuda", dtype=torch.int32)
@@ -456,6 +457,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     for _ in range(args.warmup):
         step()
     eng.sync()        # bounded by the exchange's deadline: a stuck exchange raises
+    log(f"train {model} S={S}: warm")
     barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -471,6 +473,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     clk = clocks.stop()
     t_ms = allmax(ev0.elapsed_time(ev1), world)
     ms_step = t_ms / args.steps
+    log(f"train {model} S={S}: {ms_step:.3f} ms/step")
     value = world * B * S * args.steps / (t_ms / 1000.0)
     peak, kind = tensor_peak()
     fpt = train_flops_per_token(S, cfg)
@@ -487,6 +490,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
     eng.sync()   # the last AdamW is asynchronous: the timed region ends when it has run
     te = allmax((time.perf_counter() - t0) / reps, world)
     eng.close()
+    log(f"train {model} S={S}: e2e done")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg.n_layers in (12, 28):
         v, dt, thr = cpu_train_sample(layers, rf, emb, qk, S=S, model=model,

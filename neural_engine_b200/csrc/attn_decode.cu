@@ -28,13 +28,6 @@
 //     takes a ticket on the pair's counter; the warp that takes the last
 //     ticket merges the pair's segments (log-sum-exp rescaling), writes the
 //     output and resets the counter -- no second kernel, no waiting.
-//   * Fused projection epilogue (qkv != nullptr): the kernel also does what
-//     the separate post-projection pass would (generate.py:153-162): it reads
-//     the QKV projection sums of its pair, applies the per-head QK RMSNorm and
-//     RoPE at the current position, forms q in registers, and the warp whose
-//     range ends the pair writes the new K/V row (fp16) to the cache and into
-//     its ring slot in place of the stale copy.  The warp that finishes a pair
-//     last clears the pair's projection sums for the next step's accumulation.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -84,13 +77,11 @@ __device__ __forceinline__ long long range_len(long long total, int W, int chp) 
 
 template <int HD, int GROUP>
 __global__ void __launch_bounds__(DaCfg<HD, GROUP>::WARPS * 32, 1)
-decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
-                   __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos, int P,
+decode_attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                   const __half* __restrict__ vc, int Tmax, const int* __restrict__ d_pos, int P,
                    int Hq, int Hkv, float qscale, float* __restrict__ part_o,
                    float* __restrict__ part_ml, int* __restrict__ pair_cnt,
-                   __nv_bfloat16* __restrict__ out, int* status, float* __restrict__ qkv,
-                   const float* __restrict__ qn, const float* __restrict__ kn, float qk_eps,
-                   const float2* __restrict__ rope_cs) {
+                   __nv_bfloat16* __restrict__ out, int* status) {
   using C = DaCfg<HD, GROUP>;
   constexpr int CHP = C::CHP, DPL = C::DPL, STAGES = C::STAGES, NW = C::WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -110,37 +101,6 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
   pdl_wait();   // q and the new K/V row come from the preceding kernel
 
   const int T = *d_pos + 1;
-  if (T < 1 || T > Tmax) {   // the new position must fit the cache
-    if (threadIdx.x == 0) atomicExch(status, DEV_ERR_BOUNDS);
-    return;
-  }
-  const int qkv_dim = (Hq + 2 * Hkv) * HD;
-  // RoPE of the new position, this lane's pairs (fused epilogue only)
-  float2 cs[DPL / 2];
-  if (qkv != nullptr) {
-#pragma unroll
-    for (int i = 0; i < DPL / 2; ++i)
-      cs[i] = rope_cs[(size_t)(T - 1) * (HD / 2) + lane * (DPL / 2) + i];
-  }
-  // per-head RMSNorm (optional gain) and interleaved-pair RoPE of one head's
-  // projection, this lane's dims (generate.py:97-110; the Qwen3 QK-norm)
-  auto norm_rope = [&](float (&v)[DPL], const float* gain) {
-    if (gain != nullptr) {
-      float ss = 0.f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) ss += v[d] * v[d];
-      ss = warp_sum(ss);
-      const float rms = sqrtf(ss / (float)HD + qk_eps);
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) v[d] = (v[d] / rms) * gain[lane * DPL + d];
-    }
-#pragma unroll
-    for (int i = 0; i < DPL / 2; ++i) {
-      const float v0 = v[2 * i], v1 = v[2 * i + 1];
-      v[2 * i] = v0 * cs[i].x - v1 * cs[i].y;
-      v[2 * i + 1] = v0 * cs[i].y + v1 * cs[i].x;
-    }
-  };
   const int W = gridDim.x * NW;
   const int w = blockIdx.x * NW + warp;
   const long long total = (long long)P * T;
@@ -183,25 +143,11 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
     const long long seg_end = ((long long)(pair + 1) * T < w_end) ? (long long)(pair + 1) * T : w_end;
     const int b = pair / Hkv, kvh = pair % Hkv;
     float qf[GROUP][DPL];
-    if (qkv != nullptr) {
-      // q of the group's heads straight from the projection sums
 #pragma unroll
-      for (int h = 0; h < GROUP; ++h) {
-        const float* qp = qkv + (size_t)b * qkv_dim + (kvh * GROUP + h) * HD + lane * DPL;
-        float v[DPL];
+    for (int h = 0; h < GROUP; ++h) {
+      const float* qp = q + ((size_t)b * Hq + kvh * GROUP + h) * HD + lane * DPL;
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) v[d] = qp[d];
-        norm_rope(v, qn);
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) qf[h][d] = v[d] * qscale;
-      }
-    } else {
-#pragma unroll
-      for (int h = 0; h < GROUP; ++h) {
-        const float* qp = q + ((size_t)b * Hq + kvh * GROUP + h) * HD + lane * DPL;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) qf[h][d] = qp[d] * qscale;
-      }
+      for (int d = 0; d < DPL; ++d) qf[h][d] = qp[d] * qscale;
     }
     float m[GROUP], l[GROUP], acc[GROUP][DPL];
 #pragma unroll
@@ -224,37 +170,6 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
       const int nvalid = (int)((seg_end - c_pos) < CHP ? (seg_end - c_pos) : CHP);
       const uint8_t* sK = ring + slot * 2 * C::CHUNK + lane * DPL * 2;
       const uint8_t* sV = sK + C::CHUNK;
-      if (qkv != nullptr && c_pos + nvalid == (long long)(pair + 1) * T) {
-        // this chunk ends the pair: its last row is the new position, whose K/V
-        // this warp forms, stores to the cache, and puts into the ring slot
-        const float* kp = qkv + (size_t)b * qkv_dim + (Hq + kvh) * HD + lane * DPL;
-        const float* vp = kp + (size_t)Hkv * HD;
-        float kv[DPL], vv[DPL];
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) {
-          kv[d] = kp[d];
-          vv[d] = vp[d];
-        }
-        norm_rope(kv, kn);
-        __half kh[DPL], vh[DPL];
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) {
-          kh[d] = __float2half_rn(kv[d]);
-          vh[d] = __float2half_rn(vv[d]);
-        }
-        const size_t row = ((size_t)pair * Tmax + (T - 1)) * HD + lane * DPL;
-        __half* sk = reinterpret_cast<__half*>(const_cast<uint8_t*>(sK) + (nvalid - 1) * C::ROW);
-        __half* sv = reinterpret_cast<__half*>(const_cast<uint8_t*>(sV) + (nvalid - 1) * C::ROW);
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) {
-          kc[row + d] = kh[d];
-          vc[row + d] = vh[d];
-          sk[d] = kh[d];
-          sv[d] = vh[d];
-        }
-        fence_proxy_async_smem();   // the slot is refilled by bulk copies later
-        __syncwarp();
-      }
       // partial dot products over this lane's dims: index p*GROUP + h
       float v[32];
 #pragma unroll
@@ -350,20 +265,6 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
     // segments of this pair: warps w0 .. w1 (the same cut as every warp makes)
     const int w0 = (int)(((long long)pair * T) / L);
     const int w1 = (int)(((long long)(pair + 1) * T - 1) / L);
-    // clears the pair's projection sums once no segment of it reads them
-    auto clear_pair = [&]() {
-      if (qkv == nullptr) return;
-      float* base = qkv + (size_t)b * qkv_dim;
-#pragma unroll
-      for (int h = 0; h < GROUP; ++h)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) base[(kvh * GROUP + h) * HD + lane * DPL + d] = 0.f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) {
-        base[(Hq + kvh) * HD + lane * DPL + d] = 0.f;
-        base[(Hq + Hkv + kvh) * HD + lane * DPL + d] = 0.f;
-      }
-    };
     if (w0 == w1) {
       // the whole pair is this segment: normalise and write the output
 #pragma unroll
@@ -373,7 +274,6 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
 #pragma unroll
         for (int d = 0; d < DPL; ++d) o[d] = __float2bfloat16_rn(acc[h][d] * inv);
       }
-      clear_pair();
       continue;
     }
     // ---- segment partial: slot (w, pair - first_pair)
@@ -420,7 +320,6 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
 #pragma unroll
       for (int d = 0; d < DPL; ++d) o[d] = __float2bfloat16_rn(O[d] * inv);
     }
-    clear_pair();
   }
   // Drain (bounded): copies issued but not consumed (only after an abort).
   for (int k = gc; k < issued; ++k) {
@@ -433,10 +332,9 @@ decode_attn_kernel(const float* __restrict__ q, __half* __restrict__ kc,
 }
 
 template <int HD, int G>
-cudaError_t launch_t(const float* q, __half* kc, __half* vc, int B, int Hq, int Hkv,
+cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, int Hq, int Hkv,
                      int Tmax, const int* d_pos, float qscale, float* part_o, float* part_ml,
-                     int* pair_cnt, __nv_bfloat16* out, int* status, cudaStream_t st,
-                     const DecodeQkv& f) {
+                     int* pair_cnt, __nv_bfloat16* out, int* status, cudaStream_t st) {
   using C = DaCfg<HD, G>;
   static bool attr = false;
   if (!attr) {
@@ -449,7 +347,7 @@ cudaError_t launch_t(const float* q, __half* kc, __half* vc, int B, int Hq, int 
   const int P = B * Hkv;
   return launch_k(decode_attn_kernel<HD, G>, dim3(grid), dim3(C::WARPS * 32), (size_t)C::SMEM,
                   st, q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale, part_o, part_ml, pair_cnt, out,
-                  status, f.qkv, f.qn, f.kn, f.qk_eps, f.rope_cs);
+                  status);
 }
 
 }  // namespace
@@ -462,25 +360,20 @@ size_t decode_attn_partial_slots(int B, int Hkv, int num_sms) {
   return (size_t)B * Hkv + 3 * W + 64;
 }
 
-cudaError_t launch_decode_attn(const float* q, __half* kc, __half* vc, int B, int Hq, int Hkv,
-                               int hd, int Tmax, const int* d_pos, float* part_o, float* part_ml,
-                               int* pair_cnt, __nv_bfloat16* out, int* status, cudaStream_t st,
-                               const DecodeQkv* fused) {
+cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
+                               int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
+                               float* part_ml, int* pair_cnt, __nv_bfloat16* out, int* status,
+                               cudaStream_t st) {
   const float qscale = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   const int group = Hq / Hkv;
-  const DecodeQkv f = fused ? *fused : DecodeQkv{};
   if (hd == 128 && group == 2)
-    return launch_t<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt,
-                            out, status, st, f);
+    return launch_t<128, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 128 && group == 1)
-    return launch_t<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt,
-                            out, status, st, f);
+    return launch_t<128, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 64 && group == 1)
-    return launch_t<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt,
-                           out, status, st, f);
+    return launch_t<64, 1>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   if (hd == 64 && group == 2)
-    return launch_t<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt,
-                           out, status, st, f);
+    return launch_t<64, 2>(q, kc, vc, B, Hq, Hkv, Tmax, d_pos, qscale, part_o, part_ml, pair_cnt, out, status, st);
   return cudaErrorInvalidValue;
 }
 

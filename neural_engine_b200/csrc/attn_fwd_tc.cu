@@ -13,7 +13,9 @@
 //   warp 1     MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers
 //              (128 x 128 fp32), and O += P_j V_j into the TMEM output
 //              accumulator (128 x 128 fp32); S_{j+1} is issued before waiting
-//              for P_j so the score MMAs overlap the softmax.
+//              for P_j so the score MMAs overlap the softmax, and P is double
+//              buffered so the softmax of tile j+1 overlaps the P.V product of
+//              tile j (it waits for that product only to rescale O).
 //   warps 2-9  softmax: two warps per TMEM lane quarter, thread = query row,
 //              each warp of the pair owning 64 of the tile's 128 key columns
 //              (and 64 of the 128 output columns); per tile: row max of the
@@ -53,9 +55,11 @@ constexpr uint32_t TA_V_BYTES = TA_BK * TA_HD * 2;      // 32 KB: 2 key blocks x
 constexpr uint32_t TA_P_BYTES = TA_BQ * TA_BK * 2;      // 32 KB: 2 atoms of 64 keys
 constexpr uint32_t TA_ATOM = 128 * 128;                 // 128 rows x 64 bf16
 constexpr uint32_t TA_MN_BOX = 64 * 64 * 2;             // one 64 (hd) x 64 (keys) V box
-// Q | K[2] | V[2] | P | barriers + row-max exchange (2 x 128 floats), plus 1 KB alignment slack
-constexpr int TA_SMEM = TA_Q_BYTES + 2 * TA_K_BYTES + 2 * TA_V_BYTES + TA_P_BYTES + 2048 + 1024;
-static_assert(1280 + 32 <= 2048, "barrier / exchange area");
+// Q | K[2] | V[2] | P[2] | barriers + row-max exchange (2 x 128 floats), plus 1 KB
+// alignment slack: 227 KB, the per-CTA maximum
+constexpr int TA_SMEM = TA_Q_BYTES + 2 * TA_K_BYTES + 2 * TA_V_BYTES + 2 * TA_P_BYTES + 2048 + 1024;
+static_assert(TA_SMEM <= 232448, "shared memory per CTA");
+static_assert(1312 + 32 <= 2048, "barrier / exchange area");
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -109,16 +113,16 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const uint32_t sQ = base;
   const uint32_t sK = sQ + TA_Q_BYTES;                    // [2]
   const uint32_t sV = sK + 2 * TA_K_BYTES;                // [2]
-  const uint32_t sP = sV + 2 * TA_V_BYTES;
-  const uint32_t bars = sP + TA_P_BYTES;
+  const uint32_t sP = sV + 2 * TA_V_BYTES;                // [2]
+  const uint32_t bars = sP + 2 * TA_P_BYTES;
   const uint32_t q_full = bars;
   const uint32_t kv_full = bars + 8;      // [2]
   const uint32_t kv_empty = bars + 24;    // [2]
   const uint32_t s_full = bars + 40;      // [2]
   const uint32_t s_free = bars + 56;      // [2]
-  const uint32_t p_full = bars + 72;
-  const uint32_t o_done = bars + 80;
+  const uint32_t p_full = bars + 72;      // [2]
   const uint32_t drain = bars + 88;
+  const uint32_t o_done = bars + 96;      // [2]
   uint8_t* const gbars = gbase + (bars - base);
   uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 128);
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 132);
@@ -142,8 +146,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(s_full + 8 * i, 1);
       mbar_init(s_free + 8 * i, TA_SOFTMAX);
     }
-    mbar_init(p_full, TA_SOFTMAX);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(p_full + 8 * i, TA_SOFTMAX);
+      mbar_init(o_done + 8 * i, 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -218,17 +224,18 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (ok && n_kt > 0) ok = issue_s(0);
       for (int j = 0; j < n_kt && ok; ++j) {
         if (j + 1 < n_kt && !(ok = issue_s(j + 1))) break;
-        if (!(ok = mbar_wait(p_full, j & 1, status, abort_flag))) break;
+        if (!(ok = mbar_wait(p_full + 8 * (j & 1), (j >> 1) & 1, status, abort_flag))) break;
         tc_fence_after();
         const uint32_t vbase = sV + (j & 1) * TA_V_BYTES;
+        const uint32_t pbase = sP + (j & 1) * TA_P_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TA_BK / 16; ++kk) {
-          const uint64_t ad = smem_desc_k_sw128(sP + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          const uint64_t ad = smem_desc_k_sw128(pbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
           const uint64_t bd =
               smem_desc_mn_sw128(vbase + (kk >> 2) * 2 * TA_MN_BOX, TA_MN_BOX) + 128 * (kk & 3);
           umma_f16(tmem + 256, ad, bd, IDESC_O, (j | kk) != 0);
         }
-        umma_commit(o_done);
+        umma_commit(o_done + 8 * (j & 1));
         umma_commit(kv_empty + 8 * (j & 1));
       }
       umma_commit(drain);
@@ -248,13 +255,14 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     float m = -1e30f, l = 0.f;
     bool ok = true;
     int* const xok = reinterpret_cast<int*>(gbars + 1280);         // [2][4] per-warp outcome
+    int* const xok2 = reinterpret_cast<int*>(gbars + 1312);        // [2][4] after the rescale wait
     for (int j = 0; j < n_kt; ++j) {
       const int st = j & 1;
-      // scores of tile j ready; the previous P.V product done (P is rewritten
-      // and O rescaled below).  Both warps of the pair reach the exchange
-      // barrier whatever the outcome, and leave together.
+      // scores of tile j ready, and the P buffer of this tile free (the P.V
+      // product of tile j - 2 done).  Both warps of the pair reach the exchange
+      // barriers whatever the outcome, and leave together.
       bool ready = true;
-      if (j > 0) ready = mbar_wait(o_done, (j - 1) & 1, status, abort_flag);
+      if (j >= 2) ready = mbar_wait(o_done + 8 * st, ((j >> 1) - 1) & 1, status, abort_flag);
       ready = mbar_wait(s_full + 8 * st, (j >> 1) & 1, status, abort_flag) && ready;
       ready = __all_sync(0xffffffffu, ready);
       tc_fence_after();
@@ -281,17 +289,27 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // the two warps of this lane quarter (64 threads) exchange their halves
       asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
       mx = fmaxf(mx, xmax[(half ^ 1) * 128 + row]);
-      const bool both = ready && xok[(half ^ 1) * 4 + quarter] != 0;
+      bool both = ready && xok[(half ^ 1) * 4 + quarter] != 0;
+      // Lazy rescaling: the running max m moves (and O, l are rescaled) only
+      // when the tile's max exceeds it by more than 2^8; otherwise p = exp2(s - m)
+      // stays below 256, well inside bf16 and fp32, and the TMEM round trip of
+      // O is skipped.  Both warps of the pair see the same m and mx, so both
+      // wait (or neither) for the previous P.V product before touching O.
+      const bool move = both && mx > m + 8.0f;
+      bool rs_ok = true;
+      if (move && j > 0)
+        rs_ok = mbar_wait(o_done + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, status, abort_flag);
+      rs_ok = __all_sync(0xffffffffu, rs_ok);
+      if (lane == 0) xok2[half * 4 + quarter] = rs_ok ? 1 : 0;
       asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");   // xmax / xok reusable
+      both = both && rs_ok && xok2[(half ^ 1) * 4 + quarter] != 0;
       if (!both) {
         ok = false;
         break;
       }
-      // Lazy rescaling: the running max m moves (and O, l are rescaled) only
-      // when the tile's max exceeds it by more than 2^8; otherwise p = exp2(s - m)
-      // stays below 256, well inside bf16 and fp32, and the TMEM round trip of
-      // O is skipped.  Both warps of the pair see the same m and mx.
-      const bool move = mx > m + 8.0f;
+      // the scores are in registers: the tensor cores may reuse this S buffer
+      tc_fence_before();
+      mbar_arrive(s_free + 8 * st);
       const float corr = move ? exp2f(m - mx) : 1.0f;
       if (move) m = mx;
       // pass 2: p = exp2(s - m) -> P (T, swizzled K-major rows), row sum
@@ -317,7 +335,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           }
         }
         // 32 keys = 4 chunks of 8 (16 bytes) in atom c / 64, chunk index (c % 64) / 8 + q
-        const uint32_t atom = sP + (c >> 6) * TA_ATOM + row * 128;
+        const uint32_t atom = sP + st * TA_P_BYTES + (c >> 6) * TA_ATOM + row * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int chunk = ((c & 63) >> 3) + q;
@@ -339,12 +357,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
       fence_async_smem();        // P visible to the tensor cores
       tc_fence_before();
-      mbar_arrive(s_free + 8 * st);
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + 8 * st);
     }
     // ---- output: O / l (bf16) and the row LSE (log2 domain)
     if (ok && n_kt > 0) {
-      const bool od = mbar_wait(o_done, (n_kt - 1) & 1, status, abort_flag);
+      const bool od =
+          mbar_wait(o_done + 8 * ((n_kt - 1) & 1), ((n_kt - 1) >> 1) & 1, status, abort_flag);
       // full row sum = both halves (same running max)
       xmax[half * 128 + row] = l;
       asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");

@@ -185,12 +185,6 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
   prof_mark(ctx, 9);
   const size_t kv_layer = ctx->layer_kv_elems();
   const bool swiglu_fused = decode_swiglu_fused(ctx, B);
-  // QK-norm, RoPE and the K/V append inside the decode attention
-  // (NE_DECODE_FUSED_QKV=0: the separate qkv_post pass)
-  static const bool fused_qkv = [] {
-    const char* e = std::getenv("NE_DECODE_FUSED_QKV");
-    return !(e && e[0] == '0');
-  }();
   // ctx->part holds the QKV and (unless fused) W1/W3 sums (zero between uses:
   // their consumers clear what they read); the Wo and W2 projections add
   // alpha * acc straight into the fp32 residual stream x.
@@ -201,29 +195,14 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
     prof_mark(ctx, 0);
     __half* kc = ctx->kcache + kv_layer * l;
     __half* vc = ctx->vcache + kv_layer * l;
-    if (fused_qkv) {
-      // the attention kernel normalises / rotates the projection sums itself
-      // and appends the new K/V row (no separate post-projection pass)
-      DecodeQkv f;
-      f.qkv = ctx->part;
-      f.qn = m.qk_norm ? w.q_norm : nullptr;
-      f.kn = m.qk_norm ? w.k_norm : nullptr;
-      f.qk_eps = m.qk_eps;
-      f.rope_cs = ctx->rope_cs;
-      prof_mark(ctx, 1);
-      NE_LAUNCH(launch_decode_attn(nullptr, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
-                                   ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->attn,
-                                   ctx->d_status, ctx->st, &f));
-    } else {
-      NE_LAUNCH(launch_qkv_post(ctx->part, 1, 0, B, 1, ctx->state, 0, Hq, Hkv, hd,
-                                m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
-                                m.qk_eps, ctx->rope_cs, ctx->q, 0, kc, vc, ctx->max_seq,
-                                ctx->d_status, ctx->st, 0, 1));
-      prof_mark(ctx, 1);
-      NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
-                                   ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->attn,
-                                   ctx->d_status, ctx->st));
-    }
+    NE_LAUNCH(launch_qkv_post(ctx->part, 1, 0, B, 1, ctx->state, 0, Hq, Hkv, hd,
+                              m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
+                              m.qk_eps, ctx->rope_cs, ctx->q, 0, kc, vc, ctx->max_seq,
+                              ctx->d_status, ctx->st, 0, 1));
+    prof_mark(ctx, 1);
+    NE_LAUNCH(launch_decode_attn(ctx->q, kc, vc, B, Hq, Hkv, hd, ctx->max_seq, ctx->state,
+                                 ctx->attn_po, ctx->attn_ml, ctx->attn_cnt, ctx->attn,
+                                 ctx->d_status, ctx->st));
     prof_mark(ctx, 2);
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->x, m.res_alpha)) != NE_OK)
       return s;

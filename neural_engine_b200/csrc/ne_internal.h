@@ -86,20 +86,10 @@ cudaError_t launch_argmax(const float* logits, int rows, int V, int32_t* next_to
 // Segment slots (each GROUP x (hd + 2) floats) the decode-attention partial
 // buffers must hold for batch B.
 size_t decode_attn_partial_slots(int B, int Hkv, int num_sms);
-// The QKV projection sums the decode attention post-processes itself (fused
-// epilogue): qkv [B][(Hq + 2 Hkv) hd] fp32 (cleared after use), optional QK
-// RMSNorm gains, RoPE table.
-struct DecodeQkv {
-  float* qkv = nullptr;
-  const float* qn = nullptr;
-  const float* kn = nullptr;
-  float qk_eps = 0.f;
-  const float2* rope_cs = nullptr;
-};
-cudaError_t launch_decode_attn(const float* q, __half* kc, __half* vc, int B, int Hq, int Hkv,
-                               int hd, int Tmax, const int* d_pos, float* part_o, float* part_ml,
-                               int* pair_cnt, __nv_bfloat16* out, int* status, cudaStream_t st,
-                               const DecodeQkv* fused = nullptr);
+cudaError_t launch_decode_attn(const float* q, const __half* kc, const __half* vc, int B, int Hq,
+                               int Hkv, int hd, int Tmax, const int* d_pos, float* part_o,
+                               float* part_ml, int* pair_cnt, __nv_bfloat16* out, int* status,
+                               cudaStream_t st);
 
 // ------------------------------------------------------------------ prefill attention
 // q: fp16 [B*S][Hq][hd] (row = b*S + s, position pos0 + s); cache fp16

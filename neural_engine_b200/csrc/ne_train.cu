@@ -106,6 +106,10 @@ struct TrainState {
   double* red = nullptr;                 // [2] sum of squares / loss sum
   int micro_steps = 0;                   // fwd_bwd calls since the last optimizer step
   std::vector<cudaEvent_t> phase_ev;     // ne_train_fwd_bwd_timed: one event per phase boundary
+  // page-locked staging of the host-buffer calls: the tokens of one batch,
+  // then the loss (the copies run from / into it, never from caller memory)
+  uint8_t* h_stage = nullptr;
+  size_t h_stage_tok = 0;                // bytes of the token part
   float* range_out = nullptr;            // ne_train_value_ranges: [4]
 };
 
@@ -146,6 +150,7 @@ void free_train(ne_ctx* ctx) {
   for (cudaEvent_t e : t->phase_ev)
     if (e) cudaEventDestroy(e);
   if (t->range_out) cudaFree(t->range_out);
+  if (t->h_stage) cudaFreeHost(t->h_stage);
   if (t->opt_ticket) cudaFree(t->opt_ticket);
   if (t->norm_out) cudaFree(t->norm_out);
   if (t->pool) cudaFree(t->pool);
@@ -432,6 +437,12 @@ NE_API ne_status ne_train_alloc(ne_ctx* ctx, int B, int S) {
     uint8_t* p = nullptr;
     if ((s = dalloc(ctx, &p, t->embed_scratch_bytes)) != NE_OK) return s;
     t->embed_scratch = p;
+  }
+  t->h_stage_tok = ((size_t)B * (S + 1) * 4 + 255) & ~(size_t)255;
+  if (cudaHostAlloc(reinterpret_cast<void**>(&t->h_stage), t->h_stage_tok + 256,
+                    cudaHostAllocDefault) != cudaSuccess) {
+    t->h_stage = nullptr;
+    return fail(ctx, NE_ERR_OOM, "cudaHostAlloc: token staging");
   }
   return ne_sync(ctx);
 }
@@ -1204,17 +1215,34 @@ NE_API ne_status ne_rmsnorm_bwd_add(ne_ctx* ctx, const float* d_dy, const float*
   return NE_OK;
 }
 
+// Host tokens -> the page-locked stage -> t->tok (ordered on the stream).
+static ne_status stage_tokens(ne_ctx* ctx, const int32_t* h_tokens) {
+  TrainState* t = ctx->train;
+  const size_t bytes = (size_t)t->B * (t->S + 1) * 4;
+  std::memcpy(t->h_stage, h_tokens, bytes);   // the stage is idle: every host call synchronises
+  NE_CUDA(cudaMemcpyAsync(t->tok, t->h_stage, bytes, cudaMemcpyHostToDevice, ctx->st));
+  return NE_OK;
+}
+
+// The loss (if asked for) through the stage, then the bounded synchronisation.
+static ne_status finish_host_call(ne_ctx* ctx, const float* d_loss, float* h_loss) {
+  TrainState* t = ctx->train;
+  float* staged = reinterpret_cast<float*>(t->h_stage + t->h_stage_tok);
+  if (d_loss) NE_CUDA(cudaMemcpyAsync(staged, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
+  const ne_status s = ne_sync(ctx);
+  if (s == NE_OK && d_loss) *h_loss = *staged;
+  return s;
+}
+
 NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss) {
   if (!ctx || !ctx->train || !h_tokens) return NE_ERR_STATE;
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
-  NE_CUDA(cudaMemcpyAsync(t->tok, h_tokens, (size_t)t->B * (t->S + 1) * 4, cudaMemcpyHostToDevice,
-                          ctx->st));
-  float* d_loss = reinterpret_cast<float*>(t->red + 2);
-  ne_status s = ne_train_fwd_bwd_device(ctx, t->tok, h_loss ? d_loss : nullptr);
+  ne_status s = stage_tokens(ctx, h_tokens);
   if (s != NE_OK) return s;
-  if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
-  return ne_sync(ctx);
+  float* d_loss = reinterpret_cast<float*>(t->red + 2);
+  if ((s = ne_train_fwd_bwd_device(ctx, t->tok, h_loss ? d_loss : nullptr)) != NE_OK) return s;
+  return finish_host_call(ctx, h_loss ? d_loss : nullptr, h_loss);
 }
 
 // One micro-step like ne_train_fwd_bwd, run without the captured graph and
@@ -1237,11 +1265,10 @@ NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, fl
     t->phase_ev.assign(nev, nullptr);
     for (cudaEvent_t& e : t->phase_ev) NE_CUDA(cudaEventCreate(&e));
   }
-  NE_CUDA(cudaMemcpyAsync(t->tok, h_tokens, (size_t)t->B * (t->S + 1) * 4, cudaMemcpyHostToDevice,
-                          ctx->st));
-  float* d_loss = reinterpret_cast<float*>(t->red + 2);
-  ne_status s = split_tokens(ctx, t->tok);
+  ne_status s = stage_tokens(ctx, h_tokens);
   if (s != NE_OK) return s;
+  float* d_loss = reinterpret_cast<float*>(t->red + 2);
+  if ((s = split_tokens(ctx, t->tok)) != NE_OK) return s;
   std::vector<int> phase;   // phase of the interval that ends at event k + 1
   size_t k = 0;
   auto mark = [&](int ph) -> ne_status {
@@ -1263,8 +1290,7 @@ NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, fl
   if ((s = ne_embed_bwd(ctx)) != NE_OK || (s = mark(6)) != NE_OK) return s;
   t->micro_steps++;
   t->steps_run++;
-  if (h_loss) NE_CUDA(cudaMemcpyAsync(h_loss, d_loss, 4, cudaMemcpyDeviceToHost, ctx->st));
-  if ((s = ne_sync(ctx)) != NE_OK) return s;
+  if ((s = finish_host_call(ctx, h_loss ? d_loss : nullptr, h_loss)) != NE_OK) return s;
   for (int i = 0; i < NE_TRAIN_PHASES; ++i) h_ms[i] = 0.f;
   for (size_t i = 0; i < phase.size(); ++i) {
     float ms = 0.f;
