@@ -293,9 +293,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // Lazy rescaling: the running max m moves (and O, l are rescaled) only
       // when the tile's max exceeds it by more than 2^8; otherwise p = exp2(s - m)
       // stays below 256, well inside bf16 and fp32, and the TMEM round trip of
-      // O is skipped.  Both warps of the pair see the same m and mx, so both
-      // wait (or neither) for the previous P.V product before touching O.
-      const bool move = both && mx > m + 8.0f;
+      // O is skipped.  The decision is per row, but tcgen05.ld / st are
+      // warp-collective, so a warp rescales its rows of O when any of them
+      // moves (corr = 1 for the others); both warps of the pair hold the same
+      // rows, m and mx, so both wait (or neither) for the previous P.V product.
+      const bool move_row = both && mx > m + 8.0f;
+      const bool move = __any_sync(0xffffffffu, move_row);
       bool rs_ok = true;
       if (move && j > 0)
         rs_ok = mbar_wait(o_done + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, status, abort_flag);
@@ -310,8 +313,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // the scores are in registers: the tensor cores may reuse this S buffer
       tc_fence_before();
       mbar_arrive(s_free + 8 * st);
-      const float corr = move ? exp2f(m - mx) : 1.0f;
-      if (move) m = mx;
+      const float corr = move_row ? exp2f(m - mx) : 1.0f;
+      if (move_row) m = mx;
       // pass 2: p = exp2(s - m) -> P (T, swizzled K-major rows), row sum
       float sum = 0.f;
 #pragma unroll

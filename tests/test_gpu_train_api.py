@@ -234,3 +234,37 @@ def test_sdpa_forward_matches_float64(hd, Hq, Hkv, B, S):
     ref_lse = torch.logsumexp(sc, -1) / np.log(2.0)
     assert (lse.cpu().double() - ref_lse).abs().max().item() <= 1e-3
     e.close()
+
+
+@pytest.mark.parametrize("S", [1024, 640])
+def test_sdpa_forward_rows_rescale_at_different_tiles(S):
+    """Scores that grow along the keys at a rate that alternates between
+    neighbouring query rows: odd rows' running maximum moves at every key tile
+    (their accumulated output is rescaled), even rows' never does after the
+    first, so the rows of one warp take different paths.  The output must
+    still match float64 (same tolerance as above)."""
+    import neural_engine_b200 as ne
+    hd, Hq, Hkv, B = 128, 2, 1, 1
+    cfg = ne.ModelConfig(1, 256, 256, Hq, Hkv, hd, 512)
+    e = ne.Engine(cfg)
+    g = torch.Generator().manual_seed(S)
+    u = torch.randn(hd, generator=g)
+    c = torch.where(torch.arange(S) % 2 == 1, torch.tensor(1.0), torch.tensor(0.05))
+    q = (c[:, None, None] * u[None, None, :]).expand(S, Hq, hd).reshape(S, Hq * hd)
+    q = q.to(torch.bfloat16)
+    t = torch.arange(S, dtype=torch.float32) / 128.0
+    k = (t[:, None] * u[None, :]).reshape(1, 1, S, hd).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, hd, generator=g).to(torch.bfloat16)
+    dq, dk, dv = q.cuda(), k.cuda(), v.cuda()
+    out = torch.zeros(B * S, Hq * hd, dtype=torch.bfloat16, device="cuda")
+    e.sdpa_fwd_device(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S, out.data_ptr(), 0)
+    e.sync()
+    qd = q.double().reshape(B, S, Hq, hd).permute(0, 2, 1, 3)
+    kd = k.double().repeat_interleave(Hq // Hkv, 1)
+    vd = v.double().repeat_interleave(Hq // Hkv, 1)
+    sc = qd @ kd.transpose(-1, -2) / hd ** 0.5
+    sc = sc.masked_fill(~torch.ones(S, S, dtype=torch.bool).tril(), float("-inf"))
+    ref = (torch.softmax(sc, -1) @ vd).permute(0, 2, 1, 3).reshape(B * S, Hq * hd)
+    got = out.cpu().double()
+    assert (got - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item() + 1e-3
+    e.close()
