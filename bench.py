@@ -510,7 +510,13 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
                        "batch_per_gpu": B, "seq_len": S,
                        "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
                        "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
-                       "parallelism": (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
+                       "parallelism": (f"dp{world} ZeRO-1 over NVLink peer memory (the "
+                                       "library's per-layer reduce-scatter kernels overlapped "
+                                       "with the backward, sharded AdamW, bf16 weight "
+                                       "all-gather; no NCCL on the step)"
+                                       if world > 1 and args.dp_mode == "zero1" and
+                                       os.environ.get("NE_COMM_PX", "1") != "0" else
+                                       f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
                                        "buckets overlapped with the backward, sharded AdamW, "
                                        "bf16 weight all-gather)"
                                        if world > 1 and args.dp_mode == "zero1" else

@@ -17,6 +17,7 @@ enum PxSlot : int {
   PX_NORM = 2,       // sum of squares published
   PX_W16 = 3,        // AdamW done: owned parts of the weights updated
   PX_NORM_PART = 4,  // two words
+  PX_ABORT = 6,      // set by this rank's first wait that ran out: its later waits give up at once
   PX_READY0 = 8      // + bucket: the bucket's gradients final (bucket 0 = tail, 1 + layer)
 };
 

@@ -1146,6 +1146,8 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
+  if (comm_active(ctx) && ctx->comm->aborted)   // also keeps a captured exchange from replaying
+    return fail(ctx, NE_ERR_STATE, "the exchange was aborted after a failed step");
   ne_status s = split_tokens(ctx, d_tokens);
   if (s != NE_OK) return s;
   // The first micro-step runs eagerly (kernel attributes and modules get

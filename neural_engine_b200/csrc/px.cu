@@ -41,13 +41,21 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 }
 
 // Thread 0: wait until flags[p][slot] >= the own epoch for every rank p.
-// Returns false (status set) when the wall-clock limit passes first.
+// Returns false (status set) when the wall-clock limit passes first, and from
+// then on at once: the first wait that ran out sets this rank's PX_ABORT
+// word, so the exchange kernels queued behind it do not each wait the limit.
 __device__ bool wait_peers(const PxTables& T, int slot, uint32_t epoch, int* status) {
+  volatile uint32_t* abort_word = T.flags[T.rank] + PX_ABORT;
+  if (*abort_word != 0u) {
+    atomicExch(status, DEV_ERR_TIMEOUT);
+    return false;
+  }
   const uint64_t t0 = globaltimer_ns();
   for (int p = 0; p < T.world; ++p) {
     const uint32_t* f = T.flags[p] + slot;
     while ((int)(ld_acquire_sys(f) - epoch) < 0) {
-      if (globaltimer_ns() - t0 > T.limit_ns) {
+      if (*abort_word != 0u || globaltimer_ns() - t0 > T.limit_ns) {
+        *abort_word = 1u;
         atomicExch(status, DEV_ERR_TIMEOUT);
         return false;
       }
