@@ -128,7 +128,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 132);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // longest-first order: CTAs are issued in linear block order, and the query
+  // tiles furthest down the causal triangle walk the most key tiles, so the
+  // linear index runs over every (sequence, head) of the last query tile first
+  const int nbh = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qt = gridDim.x - 1 - lin / nbh;
+  const int h = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
   const int kvh = h / (Hq / Hkv);
   const int q0 = qt * TA_BQ;
   const int n_keys = min(S, q0 + TA_BQ);                // causal: keys < q0 + 128
@@ -270,19 +276,30 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int kbase = j * TA_BK;
       // pass 1: this warp's 64 scores (kept in registers for pass 2), their
       // row max, then the max over both halves
+      // Tiles left of the diagonal tile hold only keys < q0 <= every row's
+      // position (and < S): no mask there (warp-uniform).  The maximum is taken
+      // over the raw scores and scaled once (qscale > 0, so exactly the maximum
+      // of the scaled scores).
+      const bool full = j < qt;
       uint32_t sr[2][32];
       float mx = m;
       if (ready) {
+        float mraw = -3.0e38f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           tmem_ld32(srow + c_lo + 32 * h, sr[h]);
+          if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = kbase + c_lo + 32 * h + i;
-            const float v = (key <= qpos && key < S) ? __uint_as_float(sr[h][i]) * qscale_log2 : -1e30f;
-            mx = fmaxf(mx, v);
+            for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(sr[h][i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int key = kbase + c_lo + 32 * h + i;
+              if (key <= qpos && key < S) mraw = fmaxf(mraw, __uint_as_float(sr[h][i]));
+            }
           }
         }
+        mx = fmaxf(mx, mraw > -3.0e38f ? mraw * qscale_log2 : -1e30f);
       }
       xmax[half * 128 + row] = mx;
       if (lane == 0) xok[half * 4 + quarter] = ready ? 1 : 0;
@@ -324,10 +341,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int key = kbase + c + i;
-          const float p0 = (key <= qpos && key < S)
-                               ? exp2f(__uint_as_float(sr[h][i]) * qscale_log2 - m) : 0.f;
-          const float p1 = (key + 1 <= qpos && key + 1 < S)
-                               ? exp2f(__uint_as_float(sr[h][i + 1]) * qscale_log2 - m) : 0.f;
+          float p0 = exp2f(fmaf(__uint_as_float(sr[h][i]), qscale_log2, -m));
+          float p1 = exp2f(fmaf(__uint_as_float(sr[h][i + 1]), qscale_log2, -m));
+          if (!full) {
+            if (!(key <= qpos && key < S)) p0 = 0.f;
+            if (!(key + 1 <= qpos && key + 1 < S)) p1 = 0.f;
+          }
           sum += p0 + p1;
           if constexpr (kF16) {
             const __half2 pk = __floats2half2_rn(p0, p1);
