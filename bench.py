@@ -63,6 +63,9 @@ def parse():
                     help="skip the prefill measurement (config 2)")
     ap.add_argument("--no-stories", action="store_true",
                     help="skip the Stories110M training measurement (config 3)")
+    ap.add_argument("--gemm-square", type=int, default=0,
+                    help="time one n x n x n bf16 product on the tcgen05 GEMM and exit "
+                         "(profiling aid; not a bench number)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="skip everything but the prefill measurement (profiling runs)")
     ap.add_argument("--prefill-seqs", default="256,2048",
@@ -660,6 +663,28 @@ def main():
         raise SystemExit("--profile-layers needs --train-only")
     layers, rf, emb, qk = host_weights(seed=0, cfg=profile_cfg(args) if args.profile_layers > 0
                                        else None)
+    if args.gemm_square > 0:
+        n = args.gemm_square
+        eng = ne.Engine(ne.ModelConfig(1, 128, 256, 2, 2, 64, 256), device=local)
+        g = torch.Generator(device="cuda").manual_seed(9)
+        a = (torch.randn(n, n, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        b = (torch.randn(n, n, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        c = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
+        stream = torch.cuda.ExternalStream(eng.stream_ptr)
+        ts = []
+        for i in range(8):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            eng.gemm_device(a.data_ptr(), n, n, b.data_ptr(), n, n, n, 2, c.data_ptr(), n)
+            e1.record(stream)
+            eng.sync()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        eng.close()
+        print(json.dumps({"gemm": f"{n}x{n}x{n} bf16 -> bf16", "ms": round(ms, 4),
+                          "tflops": round(2.0 * n ** 3 / (ms / 1000.0) / 1e12, 1)}), flush=True)
+        return
     if args.prefill_only:
         pf = run_prefill(args, rank, local, world, layers, rf, emb, qk)
         if rank == 0:

@@ -343,8 +343,17 @@ cudaError_t launch_t(const float* q, const __half* kc, const __half* vc, int B, 
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int grid = device_num_sms();
+  // Persistent grid of up to one CTA per SM, fewer when the cache is short:
+  // every warp should stream at least ~128 positions, so few sequences (B 1:
+  // 8 histories) are not cut into dozens of segments that one warp per history
+  // must then merge.  Sized by the cache capacity Tmax (the graph replays the
+  // launch for every position); the kernel cuts the current positions over
+  // however many warps it has.
   const int P = B * Hkv;
+  const long long want_warps = ((long long)P * Tmax + 127) / 128;
+  const long long want_ctas = (want_warps + C::WARPS - 1) / C::WARPS;
+  const int grid = (int)(want_ctas < device_num_sms() ? (want_ctas < 1 ? 1 : want_ctas)
+                                                      : device_num_sms());
   return launch_k(decode_attn_kernel<HD, G>, dim3(grid), dim3(C::WARPS * 32), (size_t)C::SMEM,
                   st, q, kc, vc, Tmax, d_pos, P, Hq, Hkv, qscale, part_o, part_ml, pair_cnt, out,
                   status);
