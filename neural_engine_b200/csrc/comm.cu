@@ -286,6 +286,9 @@ void px_free(ne_ctx* ctx) {
   for (void* p : x.mapped)
     if (p) cudaIpcCloseMemHandle(p);
   x.mapped.clear();
+  for (cudaEvent_t e : x.ag_ev)
+    if (e) cudaEventDestroy(e);
+  x.ag_ev.clear();
   for (void* p : {(void*)x.flags, (void*)x.d_wsrc, (void*)x.d_asrc, (void*)x.d_chunks})
     if (p) cudaFree(p);
   x = PxState();

@@ -20,7 +20,9 @@ struct PxState {
   const char** d_asrc = nullptr;       // [world] activation pool of each rank
   PxChunk* d_chunks = nullptr;         // every chunk list below, one allocation
   std::vector<int> rs_first, rs_count; // per bucket (0 = tail, 1 + layer)
-  int ag_first = 0, ag_count = 0;      // weight all-gather
+  int ag_first = 0, ag_count = 0;      // weight all-gather (every bucket)
+  std::vector<int> ag_bfirst, ag_bcount;   // the same per bucket (0 = tail, 1 + layer)
+  std::vector<cudaEvent_t> ag_ev;      // per bucket: its all-gather done (comm stream)
   int em_first = 0, em_count = 0;      // (token id, dY row) gather
 };
 

@@ -54,5 +54,6 @@ cudaError_t px_reduce(const PxTables& T, const PxChunk* chunks, int nchunks, int
 cudaError_t px_copy(const PxTables& T, const char* const* src, char* dst, const PxChunk* chunks,
                     int nchunks, int slot, int grid, int* status, cudaStream_t st);
 cudaError_t px_norm(const PxTables& T, float* norm_out, int* status, cudaStream_t st);
+cudaError_t px_wait(const PxTables& T, int slot, int* status, cudaStream_t st);
 
 }  // namespace ne

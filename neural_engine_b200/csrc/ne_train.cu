@@ -482,6 +482,10 @@ NE_API ne_status ne_train_set_masters(ne_ctx* ctx, int layer, const float* h_wq,
 // Refresh every bf16 compute copy from the fp32 masters.
 NE_API ne_status ne_train_sync_weights(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
+  if (ctx->comm && ctx->comm->cs) {   // after any weight all-gather still in flight
+    ne_status s = comm_fence_out(ctx);
+    if (s != NE_OK) return s;
+  }
   for (const Seg& sg : ctx->train->segs)
     if (sg.w16) NE_LAUNCH(launch_f32_to_bf16(sg.w, sg.w16, sg.n, ctx->st));
   return ne_sync(ctx);
@@ -668,21 +672,40 @@ static ne_status px_setup(ne_ctx* ctx) {
     }
     x.rs_count[b] = (int)ch.size() - x.rs_first[b];
   }
+  // weight all-gather, bucket by bucket in the order the next forward needs
+  // them: the tail (embedding, final norm), then layers 0 .. L-1
   x.ag_first = (int)ch.size();
+  x.ag_bfirst.assign(L + 1, 0);
+  x.ag_bcount.assign(L + 1, 0);
   const char* wbase = static_cast<const char*>(ctx->wpool);
-  for (const Seg& sg : t->segs) {
-    for (int p = 0; p < W; ++p) {
-      if (p == R) continue;
-      long long off, len;
-      seg_owned(ctx, sg, p, &off, &len);
-      const long long o = sg.w16 ? reinterpret_cast<const char*>(sg.w16 + off) - wbase
-                                 : reinterpret_cast<const char*>(sg.w + off) - wbase;
-      const long long bytes = len * (sg.w16 ? 2 : 4);
-      for (long long i = 0; i < bytes; i += CP_CHUNK)
-        ch.push_back({o + i, o + i, (int)std::min<long long>(CP_CHUNK, bytes - i), p});
+  for (int b = 0; b <= L; ++b) {
+    int s0, s1;
+    bucket_segs(t, b, &s0, &s1);
+    x.ag_bfirst[b] = (int)ch.size();
+    for (int k = s0; k < s1; ++k) {
+      const Seg& sg = t->segs[k];
+      for (int p = 0; p < W; ++p) {
+        if (p == R) continue;
+        long long off, len;
+        seg_owned(ctx, sg, p, &off, &len);
+        const long long o = sg.w16 ? reinterpret_cast<const char*>(sg.w16 + off) - wbase
+                                   : reinterpret_cast<const char*>(sg.w + off) - wbase;
+        const long long bytes = len * (sg.w16 ? 2 : 4);
+        for (long long i = 0; i < bytes; i += CP_CHUNK)
+          ch.push_back({o + i, o + i, (int)std::min<long long>(CP_CHUNK, bytes - i), p});
+      }
     }
+    x.ag_bcount[b] = (int)ch.size() - x.ag_bfirst[b];
   }
   x.ag_count = (int)ch.size() - x.ag_first;
+  x.ag_ev.assign(L + 1, nullptr);
+  for (cudaEvent_t& e : x.ag_ev) NE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  // captured micro-steps from before the exchange existed do not wait for its
+  // all-gathers: capture them again
+  for (cudaGraphExec_t& g : t->step_graphs) {
+    if (g) cudaGraphExecDestroy(g);
+    g = nullptr;
+  }
   x.em_first = (int)ch.size();
   const char* abase = static_cast<const char*>(t->act_pool);
   const long long ids_off = reinterpret_cast<const char*>(t->ids) - abase;
@@ -723,6 +746,20 @@ static int px_ctas() {
     return v > 0 ? v : 64;
   }();
   return n;
+}
+
+// The compute stream waits for bucket b's weight all-gather of the last
+// optimizer step (a no-op when there was none).  Inside a capture the wait is
+// an external-event node: each replay waits for the event's latest record.
+static ne_status px_weights_ready(ne_ctx* ctx, int b) {
+  if (!ctx->comm || !ctx->comm->shard || !ctx->comm->px || !ctx->comm->pxs.ready) return NE_OK;
+  const PxState& x = ctx->comm->pxs;
+  if (b < 0 || b >= (int)x.ag_ev.size()) return NE_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  NE_CUDA(cudaStreamIsCapturing(ctx->st, &cs));
+  NE_CUDA(cudaStreamWaitEvent(ctx->st, x.ag_ev[b],
+                              cs == cudaStreamCaptureStatusNone ? 0u : cudaEventWaitExternal));
+  return NE_OK;
 }
 
 // Publish bucket b's gradients (compute stream) and reduce this rank's part
@@ -925,6 +962,8 @@ static ne_status split_tokens(ne_ctx* ctx, const int32_t* d_tokens) {
 // embed + first norm of the split batch (t->ids)
 static ne_status embed_fwd_ids(ne_ctx* ctx) {
   NE_TRAIN_PRELUDE();
+  // the embedding / final norm (bucket 0) and layer 0's gains (bucket 1)
+  if ((s = px_weights_ready(ctx, 0)) != NE_OK || (s = px_weights_ready(ctx, 1)) != NE_OK) return s;
   NE_LAUNCH(launch_embed_rmsnorm(t->ids, t->embed_w, 1, V, D, ctx->L[0].rms_att, m.rms_eps,
                                  t->A[0].X, t->A[0].XN, M, ctx->d_status, st));
   // the attention residual of layer 0 accumulates onto a copy of x
@@ -947,6 +986,7 @@ NE_API ne_status ne_embed_fwd(ne_ctx* ctx, const int32_t* d_tokens) {
 NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
   NE_TRAIN_PRELUDE();
   NE_LAYER_CHECK(l);
+  if ((s = px_weights_ready(ctx, 1 + l)) != NE_OK) return s;
   const LayerW& w = ctx->L[l];
   TrainActs& a = t->A[l];
   if ((s = gemm(ctx, gc(a.XN, D, M, 0, w.wqkv, D, qkv, 0, D, EPI_F32, a.QKVR, qkv))) != NE_OK)
@@ -975,6 +1015,10 @@ NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
 NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int l) {
   NE_TRAIN_PRELUDE();
   NE_LAYER_CHECK(l);
+  // this layer's matrices, and the gain of the norm that follows (next layer / final)
+  if ((s = px_weights_ready(ctx, 1 + l)) != NE_OK ||
+      (s = px_weights_ready(ctx, l + 1 < m.n_layers ? 2 + l : 0)) != NE_OK)
+    return s;
   const LayerW& w = ctx->L[l];
   TrainActs& a = t->A[l];
   GemmCall c = gc(a.X2N, D, M, 0, w.w13, D, 2 * F, 0, D, EPI_SWIGLU, a.GATE, F);
@@ -1443,10 +1487,20 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
     // every rank needs the whole updated compute copy; the fp32 masters and
     // moments stay with their owners until ne_train_gather_state
     if (ctx->comm->px) {
+      // the other ranks' updated parts arrive on the comm stream, bucket by
+      // bucket, while the next micro-step's forward runs (each layer waits for
+      // its bucket's event); the gradients may be zeroed once every rank has
+      // published, i.e. finished reading them
       PxState& x = ctx->comm->pxs;
       NE_CUDA(px_signal(x.flags, PX_W16, ctx->st));
-      NE_CUDA(px_copy(x.T, x.d_wsrc, static_cast<char*>(ctx->wpool), x.d_chunks + x.ag_first,
-                      x.ag_count, PX_W16, ctx->num_sms * 2, ctx->d_status, ctx->st));
+      if ((s = comm_fence_in(ctx)) != NE_OK) return s;
+      for (int b = 0; b < (int)x.ag_ev.size(); ++b) {
+        NE_CUDA(px_copy(x.T, x.d_wsrc, static_cast<char*>(ctx->wpool),
+                        x.d_chunks + x.ag_bfirst[b], x.ag_bcount[b], PX_W16, px_ctas(),
+                        ctx->d_status, ctx->comm->cs));
+        NE_CUDA(cudaEventRecord(x.ag_ev[b], ctx->comm->cs));
+      }
+      NE_CUDA(px_wait(x.T, PX_W16, ctx->d_status, ctx->st));
     } else if ((s = gather_owned(ctx, 4)) != NE_OK) {
       return s;
     }

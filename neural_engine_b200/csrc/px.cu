@@ -143,6 +143,11 @@ __global__ void __launch_bounds__(256) px_copy_kernel(PxTables T, const char* co
   }
 }
 
+// Wait (one thread) until every rank published `slot` for the current epoch.
+__global__ void px_wait_kernel(PxTables T, int slot, int* status) {
+  wait_peers(T, slot, T.flags[T.rank][PX_EPOCH], status);
+}
+
 // Sharded gradient norm: publish this rank's sum of squares (norm_out[2]),
 // wait for every rank's, and leave their sum (in rank order) in norm_out[2].
 __global__ void px_norm_kernel(PxTables T, float* norm_out, int* status) {
@@ -184,6 +189,11 @@ cudaError_t px_copy(const PxTables& T, const char* const* src, char* dst, const 
   if (nchunks <= 0) return cudaSuccess;
   px_copy_kernel<<<grid < nchunks ? grid : nchunks, 256, 0, st>>>(T, src, dst, chunks, nchunks,
                                                                   slot, status);
+  return cudaGetLastError();
+}
+
+cudaError_t px_wait(const PxTables& T, int slot, int* status, cudaStream_t st) {
+  px_wait_kernel<<<1, 1, 0, st>>>(T, slot, status);
   return cudaGetLastError();
 }
 
