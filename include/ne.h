@@ -179,6 +179,23 @@ NE_API ne_status ne_gemm_device_ex(ne_ctx* ctx, const void* d_A, long long lda, 
                                    void* d_out, long long ld, float alpha, int bn, int splits,
                                    long long split_stride, int* h_splits);
 
+/* The dW product of the data-parallel training backward fused with its
+ * reduce-scatter: fp32 acc = A^T . B with A [K, M] and B [K, N] bf16 stored
+ * MN-major (lda >= M, ldb >= N), element (m, n) added, times alpha, into the
+ * copy of the rank that owns flat index i = m*ld + n:
+ *   h_dst[q][i] += alpha * acc   for h_bound[q] <= i < h_bound[q + 1].
+ * world 1..8; h_bound[0] = 0 <= h_bound[1] <= ... <= h_bound[world] = M*ld,
+ * every boundary a multiple of 64; ld a multiple of 64 and >= N; K a multiple
+ * of 64; the copies 16-byte aligned.  h_dst[q] for q != rank may be another
+ * GPU's memory (a CUDA IPC mapping over NVLink): those adds are system-scope
+ * vector reductions.  The adds are atomic, so their order (and the fp32 sum's
+ * rounding) is not fixed.  Replaces the dW cblas_sgemm + accumulation of
+ * train.m:555-597, 629-655 and 733-738 together with the gradient exchange. */
+NE_API ne_status ne_gemm_dw_owned(ne_ctx* ctx, const void* d_A, long long lda, int M,
+                                  const void* d_B, long long ldb, int N, int K, float alpha,
+                                  float* const* h_dst, const long long* h_bound, int world,
+                                  int rank, long long ld);
+
 /* The context's CUDA stream (a cudaStream_t), for events and interop. */
 NE_API void* ne_get_stream(const ne_ctx* ctx);
 

@@ -194,6 +194,21 @@ cudaError_t launch_epi(const GemmCall& c, const CUtensorMap& ta, const CUtensorM
       }
       break;
     }
+    case EPI_RESID_PEER: {
+      if constexpr (AMN == 1 && BMN == 1 && ch32) {   // the dW products of the training backward
+        const GemmPeerOut& po = *c.peer;
+        EpiResidPeer::Params p;
+        for (int r = 0; r < GEMM_PEER_MAX; ++r) p.dst[r] = r < po.world ? po.dst[r] : nullptr;
+        for (int r = 0; r <= GEMM_PEER_MAX; ++r) p.bound[r] = r <= po.world ? po.bound[r] : 0;
+        p.ld = c.ld;
+        p.abort = po.abort;
+        p.alpha = c.alpha;
+        p.world = po.world;
+        p.rank = po.rank;
+        return launch_t<BN, EpiResidPeer, FMT, AMN, BMN, CG>(ta, tb, tc, td, sh, p, grid, st);
+      }
+      break;
+    }
     case EPI_SWIGLU:
       if constexpr (kk && ch32) {
         // gate [M, N/2] bf16; optional h13 [M, N] bf16 (the raw projection)
@@ -335,6 +350,10 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   if (c.epi == EPI_F32_STATS && (!c.aux1 || (reinterpret_cast<uintptr_t>(c.aux1) & 7u) ||
                                  c.aux_ld < (c.N + 31) / 32))
     return cudaErrorInvalidValue;
+  if (c.epi == EPI_RESID_PEER &&
+      (!c.peer || c.peer->world < 1 || c.peer->world > GEMM_PEER_MAX || c.ld % 64 != 0 ||
+       c.peer->bound[c.peer->world] != (long long)c.M * c.ld))
+    return cudaErrorInvalidValue;
   const int num_sms = device_num_sms();
   int bn = pick_bn(c);
   if (c.b_mn && bn < 64) bn = 64;
@@ -342,7 +361,7 @@ cudaError_t gemm_run(const GemmCall& c, int* status, cudaStream_t st) {
   const int kb = c.K / GEMM_BK;
   if (kb % splits != 0) return cudaErrorInvalidValue;
   if (splits > 1 && c.epi != EPI_F32T && c.epi != EPI_F32 && c.epi != EPI_F32T_ADD &&
-      !(c.epi == EPI_RESID && c.atomic))
+      !(c.epi == EPI_RESID && c.atomic) && c.epi != EPI_RESID_PEER)
     return cudaErrorInvalidValue;
 
   const bool pair = gemm_pair_tiles(c) && bn == 256 && num_sms >= 2;

@@ -495,6 +495,74 @@ struct EpiBF16S {
   }
 };
 
+// fp32 accumulation into the owner of each element (the dW products of the
+// peer-memory ZeRO-1 exchange): element m*ld + n of the output goes to the rank
+// whose part holds it, local or over NVLink.  Staged (kStage 3): the warp's
+// 32 x 32 box is read back from shared memory four rows per instruction, so
+// each lane adds 16 contiguous bytes and a warp covers four 128-byte row
+// segments, as element-wise vector reductions (red.add: atomic at the
+// destination, so every rank and every split-K unit may add into the same
+// element; system scope for another GPU's memory).  Parts start at multiples
+// of 64 elements and ld is a multiple of 64, so a 32-column chunk of a row
+// has one owner.
+struct EpiResidPeer {
+  static constexpr int kStage = 3;
+  static constexpr int kCols = 32;
+  using Out = float;
+  struct Params {
+    float* dst[8];
+    long long bound[9];
+    long long ld;
+    const unsigned* abort;   // nonzero: the exchange gave up; no more adds into other ranks
+    float alpha;
+    int world, rank;
+  };
+  __device__ static int out_col(const Params&, int n0) { return n0; }
+  template <int CH>
+  __device__ static void stage(const Params& p, int, int, const float (&v)[CH], Out (&o)[kCols],
+                               int, int) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) o[j] = p.alpha * v[j];
+  }
+  // rows y .. y+31, columns n0 .. n0+31 from the box (stage_row layout: row r
+  // at r*128 bytes, its 16-byte chunk q at (q ^ (r & 7)) * 16)
+  __device__ static void flush(const Params& p, uint32_t box, int lane, int y, int n0, int M,
+                               int N) {
+    const int q = lane & 7;
+    const int n = n0 + 4 * q;
+    const bool stopped = p.abort && *reinterpret_cast<const volatile unsigned*>(p.abort) != 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3);
+      float4 w;
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(w.x), "=f"(w.y), "=f"(w.z), "=f"(w.w)
+                   : "r"(box + r * 128 + ((q ^ (r & 7)) << 4)));
+      const int m = y + r;
+      if (m >= M || n >= N) continue;
+      const long long e = (long long)m * p.ld + n;
+      int o = 0;
+      while (o + 1 < p.world && e >= p.bound[o + 1]) ++o;
+      if (stopped && o != p.rank) continue;
+      float* d = p.dst[o] + e;
+      if (n + 4 <= N) {
+        if (o != p.rank)
+          asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d),
+                       "f"(w.x), "f"(w.y), "f"(w.z), "f"(w.w) : "memory");
+        else
+          asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d),
+                       "f"(w.x), "f"(w.y), "f"(w.z), "f"(w.w) : "memory");
+      } else {
+        const float t[4] = {w.x, w.y, w.z, w.w};
+        for (int j = 0; j < 4 && n + j < N; ++j) {
+          if (o != p.rank) atomicAdd_system(d + j, t[j]);
+          else atomicAdd(d + j, t[j]);
+        }
+      }
+    }
+  }
+};
+
 // fp32 accumulation  out[m][n] += alpha * acc  through the TMA add (atomic per
 // element in L2, so split-K units may add into the same tile).
 struct EpiResidS {
@@ -638,7 +706,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   constexpr bool PAIR = CG == 2;
   constexpr int TILE_M = GEMM_BM * CG;          // rows of A per work unit (both CTAs)
   static_assert(!PAIR || !EpiTransposed<Epi>::value, "pair tiles: row-major epilogues only");
-  constexpr int STG = EpiStage<Epi>::value;   // 0: direct stores, 1: TMA store, 2: TMA add
+  // 0: direct stores, 1: TMA store, 2: TMA add, 3: the warp adds the box itself (Epi::flush)
+  constexpr int STG = EpiStage<Epi>::value;
   static_assert(!B_MN || BN % 64 == 0, "MN-major B needs whole 64-wide boxes");
   constexpr uint32_t MN_BOX = 64 * GEMM_BK * 2;   // one 64 (MN) x 64 (K) box
   constexpr int STAGES = C::STAGES;
@@ -684,7 +753,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if constexpr (STG != 0) tma_prefetch_desc(&tmC);
+    if constexpr (STG == 1 || STG == 2) tma_prefetch_desc(&tmC);
     if constexpr (EpiHasBox2<Epi>::value) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
@@ -962,25 +1031,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           } else {
             stage_row(sbuf, lane, o);
           }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            const int y = mt * TILE_M + row0 + quarter * 32;
-            if constexpr (EpiTransposed<Epi>::value) {
-              // output [N (batch), M (features)]: x = feature, y = batch row
-              if (y < sh.M && n0 < sh.N) tma_reduce_add_2d(&tmC, sbuf, y, n0);
-            } else {
-              if (y < sh.M && n0 < sh.N) {
-                const int x = Epi::out_col(ep, n0);
-                if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
-                else tma_reduce_add_2d(&tmC, sbuf, x, y);
-                if constexpr (EpiHasBox2<Epi>::value) {
-                  if (Epi::has_box2(ep))
-                    tma_store_2d(&tmD, sbuf + GEMM_STAGE_BOX2, Epi::out_col2(ep, n0), y);
+          if constexpr (STG == 3) {
+            __syncwarp();
+            Epi::flush(ep, sbuf, lane, mt * TILE_M + row0 + quarter * 32, n0, sh.M, sh.N);
+            __syncwarp();   // every lane has read the box before the next chunk's rows
+          } else {
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int y = mt * TILE_M + row0 + quarter * 32;
+              if constexpr (EpiTransposed<Epi>::value) {
+                // output [N (batch), M (features)]: x = feature, y = batch row
+                if (y < sh.M && n0 < sh.N) tma_reduce_add_2d(&tmC, sbuf, y, n0);
+              } else {
+                if (y < sh.M && n0 < sh.N) {
+                  const int x = Epi::out_col(ep, n0);
+                  if constexpr (STG == 1) tma_store_2d(&tmC, sbuf, x, y);
+                  else tma_reduce_add_2d(&tmC, sbuf, x, y);
+                  if constexpr (EpiHasBox2<Epi>::value) {
+                    if (Epi::has_box2(ep))
+                      tma_store_2d(&tmD, sbuf + GEMM_STAGE_BOX2, Epi::out_col2(ep, n0), y);
+                  }
                 }
               }
+              bulk_commit_group();
             }
-            bulk_commit_group();
           }
         }
       }

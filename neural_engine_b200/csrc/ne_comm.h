@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "../../include/ne.h"
+#include "ne_internal.h"
 #include "ne_px.h"
 
 namespace ne {
@@ -23,6 +24,16 @@ struct PxState {
   int ag_first = 0, ag_count = 0;      // weight all-gather (every bucket)
   std::vector<int> ag_bfirst, ag_bcount;   // the same per bucket (0 = tail, 1 + layer)
   std::vector<cudaEvent_t> ag_ev;      // per bucket: its all-gather done (comm stream)
+  // fused dW reduction: the layer matrices' dW products add straight into
+  // their owners' gradients (EPI_RESID_PEER); their reduce-scatter is skipped
+  bool fused = false;                  // set up for it (NE_PX_FUSED_DW, eligible shapes)
+  bool fused_now = false;              // the current micro-step uses it
+  bool owned_clean = false;            // owned fused parts zeroed and PX_ZEROED published
+  std::vector<GemmPeerOut> peer_out;   // per training segment (used where fused_seg)
+  std::vector<char> fused_seg;
+  std::vector<int> rsf_first, rsf_count;   // per bucket: reduce-scatter without the fused segments
+  int zf_first = 0, zf_count = 0;      // this rank's owned parts of the fused segments
+  int zr_first = 0, zr_count = 0;      // every other gradient float (zeroed after the all-gather)
   int em_first = 0, em_count = 0;      // (token id, dY row) gather
 };
 

@@ -20,6 +20,20 @@ enum GemmEpi : int {
   EPI_F32T_ADD = 8,    // swap-AB: out[n][m] += alpha * acc through the TMA add (split-K safe)
   EPI_ARGMAX_T = 9,    // swap-AB: atomicMax of (logit, ~m) keys into aux1 [N] (greedy LM head)
   EPI_SWIGLU_T = 10,   // swap-AB, K not split: bf16 out[n][m/2] = silu(h1)*h3 of a W1/W3 16-row-interleaved A
+  EPI_RESID_PEER = 11, // fp32 x[m][n] += alpha * acc added into the rank that owns element
+                       // m*ld + n (GemmCall::peer): the dW products of the peer-memory exchange
+};
+
+// Output of EPI_RESID_PEER: each rank's copy of the [M, ld] fp32 matrix (this
+// rank's: local) and the element boundaries of the ranks' parts (multiples of
+// 64, bound[world] = M * ld).
+constexpr int GEMM_PEER_MAX = 8;
+struct GemmPeerOut {
+  float* dst[GEMM_PEER_MAX];
+  long long bound[GEMM_PEER_MAX + 1];
+  const unsigned* abort = nullptr;   // this rank's abort word: set, no adds into other ranks
+  int world = 1;
+  int rank = 0;
 };
 
 struct GemmCall {
@@ -48,6 +62,7 @@ struct GemmCall {
   const void* aux3 = nullptr;   // EPI_ADD: input; EPI_SWIGLU_BWD: h13 [M, 2F]
   long long aux_ld = 0;         // EPI_SWIGLU_BWD: F
   int atomic = 0;               // EPI_RESID: accumulate with atomics (allows split-K)
+  const GemmPeerOut* peer = nullptr;   // EPI_RESID_PEER: where each element goes
 };
 
 // Returns the split-K factor gemm_run would use for `c` (resolving splits == 0).

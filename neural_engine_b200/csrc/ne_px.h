@@ -18,6 +18,8 @@ enum PxSlot : int {
   PX_W16 = 3,        // AdamW done: owned parts of the weights updated
   PX_NORM_PART = 4,  // two words
   PX_ABORT = 6,      // set by this rank's first wait that ran out: its later waits give up at once
+  PX_ZEROED = 7,     // this rank's owned dW parts are zero for exchanges >= this value: the
+                     // other ranks' fused dW products may add into them
   PX_READY0 = 8      // + bucket: the bucket's gradients final (bucket 0 = tail, 1 + layer)
 };
 
@@ -49,6 +51,10 @@ inline void px_part(long long n, int world, int rank, long long* off, long long*
 
 cudaError_t px_epoch(uint32_t* own_flags, cudaStream_t st);
 cudaError_t px_signal(uint32_t* own_flags, int slot, cudaStream_t st);
+// As px_signal, publishing the current epoch + 1 (PX_ZEROED: ready for the next exchange).
+cudaError_t px_signal_next(uint32_t* own_flags, int slot, cudaStream_t st);
+// Zero floats [dst_off, dst_off + len) of every chunk, relative to `base`.
+cudaError_t px_zero(float* base, const PxChunk* chunks, int nchunks, cudaStream_t st);
 cudaError_t px_reduce(const PxTables& T, const PxChunk* chunks, int nchunks, int slot, int grid,
                       int* status, cudaStream_t st);
 cudaError_t px_copy(const PxTables& T, const char* const* src, char* dst, const PxChunk* chunks,

@@ -98,9 +98,10 @@ struct TrainState {
   void* embed_scratch = nullptr;         // sort buffers of the embedding backward
   size_t embed_scratch_bytes = 0;
   // the micro-step after the token split, captured once as a CUDA graph
-  // captured micro-steps: [1] with the gradient exchange, [0] without
-  cudaGraphExec_t step_graphs[2] = {nullptr, nullptr};
-  const void* step_graph_rope[2] = {nullptr, nullptr};   // RoPE table each was captured with
+  // captured micro-steps: [0] without the gradient exchange, [1] with it,
+  // [2] with it and the dW products added into their owners (fused exchange)
+  cudaGraphExec_t step_graphs[3] = {nullptr, nullptr, nullptr};
+  const void* step_graph_rope[3] = {nullptr, nullptr, nullptr};   // RoPE table each was captured with
   long long steps_run = 0;                // micro-steps so far (the first runs eagerly)
   int32_t *ids = nullptr, *tgt = nullptr, *tok = nullptr;
   double* red = nullptr;                 // [2] sum of squares / loss sum
@@ -239,7 +240,7 @@ ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
   if (ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce && comm_reserved_sms() > 0)
     c.max_ctas = ctx->num_sms - comm_reserved_sms();
-  if (c.epi == EPI_RESID && c.a_mn && c.b_mn) {
+  if ((c.epi == EPI_RESID || c.epi == EPI_RESID_PEER) && c.a_mn && c.b_mn) {
     c.bn = 256;
     c.splits = dw_splits(c, ctx->num_sms);
     c.atomic = 1;
@@ -491,10 +492,54 @@ NE_API ne_status ne_train_sync_weights(ne_ctx* ctx) {
   return ne_sync(ctx);
 }
 
+NE_API ne_status ne_gemm_dw_owned(ne_ctx* ctx, const void* d_A, long long lda, int M,
+                                  const void* d_B, long long ldb, int N, int K, float alpha,
+                                  float* const* h_dst, const long long* h_bound, int world,
+                                  int rank, long long ld) {
+  if (!ctx || !d_A || !d_B || !h_dst || !h_bound || M <= 0 || N <= 0 || K <= 0 || world < 1 ||
+      world > GEMM_PEER_MAX || rank < 0 || rank >= world || lda < M || ldb < N)
+    return NE_ERR_INVALID;
+  if (K % 64 || ld % 64 || ld < N)
+    return fail(ctx, NE_ERR_UNSUPPORTED, "K and ld must be multiples of 64, ld >= N");
+  GemmPeerOut po;
+  po.world = world;
+  po.rank = rank;
+  for (int q = 0; q <= world; ++q) {
+    po.bound[q] = h_bound[q];
+    if (h_bound[q] % 64 || (q > 0 && h_bound[q] < h_bound[q - 1]))
+      return fail(ctx, NE_ERR_INVALID, "part boundaries: non-decreasing multiples of 64");
+  }
+  if (h_bound[0] != 0 || h_bound[world] != (long long)M * ld)
+    return fail(ctx, NE_ERR_INVALID, "part boundaries must span [0, M*ld]");
+  for (int q = 0; q < world; ++q) {
+    if (!h_dst[q] || (reinterpret_cast<uintptr_t>(h_dst[q]) & 15u))
+      return fail(ctx, NE_ERR_INVALID, "each copy: non-NULL and 16-byte aligned");
+    po.dst[q] = h_dst[q];
+  }
+  NE_CUDA(cudaSetDevice(ctx->device));
+  GemmCall c = gc(d_A, lda, M, 1, d_B, ldb, N, 1, K, EPI_RESID_PEER, h_dst[rank], ld, alpha);
+  c.peer = &po;
+  return gemm(ctx, c);
+}
+
 NE_API ne_status ne_train_zero_grads(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
   TrainState* t = ctx->train;
-  NE_CUDA(cudaMemsetAsync(t->grad_pool, 0, t->grad_floats * 4, ctx->st));
+  if (ctx->comm && ctx->comm->px && ctx->comm->pxs.ready && ctx->comm->pxs.fused) {
+    // fused dW exchange: this rank's owned parts of the layer matrices take
+    // the other ranks' dW products once it has published PX_ZEROED for their
+    // next exchange; after that only the rest may be cleared here
+    PxState& x = ctx->comm->pxs;
+    if (x.owned_clean) {
+      NE_CUDA(px_zero(t->grad_pool, x.d_chunks + x.zr_first, x.zr_count, ctx->st));
+    } else {
+      NE_CUDA(cudaMemsetAsync(t->grad_pool, 0, t->grad_floats * 4, ctx->st));
+      NE_CUDA(px_signal_next(x.flags, PX_ZEROED, ctx->st));
+      x.owned_clean = true;
+    }
+  } else {
+    NE_CUDA(cudaMemsetAsync(t->grad_pool, 0, t->grad_floats * 4, ctx->st));
+  }
   t->micro_steps = 0;
   return NE_OK;
 }
@@ -574,6 +619,20 @@ static void bucket_segs(const TrainState* t, int b, int* s0, int* s1) {
   *s1 = l + 1 < (int)t->P.size() ? t->P[l + 1].seg0 : tail0;
 }
 
+// Fused dW exchange over peer memory (NE_PX_FUSED_DW, default 1): the layer
+// matrices' dW products are added into their owners' parts by the GEMM
+// epilogue (fp32 red.add over NVLink) instead of being reduce-scattered
+// after each layer.  The sum's order then varies between runs (the adds
+// land in arrival order); NE_PX_FUSED_DW=0 keeps the rank-ordered,
+// reproducible reduction.
+static bool px_fused_dw() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_PX_FUSED_DW");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Map the other ranks' pools and build the chunk lists of the peer-memory
 // exchange.  Collective (every rank, outside any stream capture): the IPC
 // handles travel in one NCCL all-gather.
@@ -588,6 +647,12 @@ static ne_status px_setup(ne_ctx* ctx) {
   ne_status s;
   if ((s = dalloc(ctx, &x.flags, 256)) != NE_OK) return s;
   NE_CUDA(cudaMemset(x.flags, 0, 256 * sizeof(uint32_t)));
+  {
+    // the gradients are zero at the first exchange (the pool starts zeroed
+    // and every path that writes it runs a micro-step): open for epoch 1
+    const uint32_t one = 1u;
+    NE_CUDA(cudaMemcpy(x.flags + PX_ZEROED, &one, sizeof(one), cudaMemcpyHostToDevice));
+  }
   // the (token id, dY row) gather buffer: [world][M] ids, then [world][M][D] rows
   const int M = t->M, D = ctx->cfg.dim;
   const size_t ids_bytes = ((size_t)W * M * 4 + 255) & ~(size_t)255;
@@ -672,6 +737,53 @@ static ne_status px_setup(ne_ctx* ctx) {
     }
     x.rs_count[b] = (int)ch.size() - x.rs_first[b];
   }
+  // fused dW exchange: each layer matrix whose row length is a multiple of
+  // 64 takes its dW product straight into the owners' parts
+  // (EPI_RESID_PEER); its bucket then reduce-scatters only the gains
+  x.fused = px_fused_dw();
+  x.fused_seg.assign(t->segs.size(), 0);
+  x.peer_out.assign(t->segs.size(), GemmPeerOut{});
+  if (x.fused) {
+    const long long qd = (long long)ctx->cfg.n_heads * ctx->cfg.head_dim;
+    // row lengths of dWqkv [qkv, D], dWo [D, qd], dW13 [2F, D], dW2 [D, F]
+    const long long lds[4] = {D, qd, D, ctx->cfg.hidden};
+    for (int l = 0; l < L; ++l) {
+      for (int i = 0; i < 4; ++i) {
+        const int k = t->P[l].seg0 + i;
+        const Seg& sg = t->segs[k];
+        if (lds[i] % 64 != 0 || sg.n % lds[i] != 0) continue;
+        GemmPeerOut& po = x.peer_out[k];
+        po.world = W;
+        po.rank = R;
+        po.abort = x.flags + PX_ABORT;
+        for (int p = 0; p < W; ++p) {
+          po.dst[p] = x.T.grad[p] + (sg.g - t->grad_pool);
+          long long off, len;
+          px_part(sg.n, W, p, &off, &len);
+          po.bound[p] = off;
+        }
+        po.bound[W] = sg.n;
+        x.fused_seg[k] = 1;
+      }
+    }
+  }
+  x.rsf_first.assign(L + 1, 0);
+  x.rsf_count.assign(L + 1, 0);
+  for (int b = 0; b <= L; ++b) {
+    int s0, s1;
+    bucket_segs(t, b, &s0, &s1);
+    x.rsf_first[b] = (int)ch.size();
+    for (int k = s0; k < s1; ++k) {
+      if (x.fused_seg[k]) continue;
+      const Seg& sg = t->segs[k];
+      long long off, len;
+      seg_owned(ctx, sg, R, &off, &len);
+      const long long g0 = (sg.g - t->grad_pool) + off;
+      for (long long i = 0; i < len; i += RS_CHUNK)
+        ch.push_back({0, g0 + i, (int)std::min<long long>(RS_CHUNK, len - i), R});
+    }
+    x.rsf_count[b] = (int)ch.size() - x.rsf_first[b];
+  }
   // weight all-gather, bucket by bucket in the order the next forward needs
   // them: the tail (embedding, final norm), then layers 0 .. L-1
   x.ag_first = (int)ch.size();
@@ -718,6 +830,36 @@ static ne_status px_setup(ne_ctx* ctx) {
                     (int)std::min<long long>(CP_CHUNK, rows - i), p});
   }
   x.em_count = (int)ch.size() - x.em_first;
+  // zeroing lists: this rank's owned parts of the fused segments (cleared
+  // right after its optimizer step, before PX_ZEROED), and the complement in
+  // the gradient pool (cleared once every rank finished reading it)
+  {
+    constexpr long long Z_CHUNK = 1 << 16;   // floats
+    std::vector<std::pair<long long, long long>> own;   // [begin, end) float offsets
+    for (size_t k = 0; k < t->segs.size(); ++k) {
+      if (!x.fused_seg[k]) continue;
+      const Seg& sg = t->segs[k];
+      long long off, len;
+      seg_owned(ctx, sg, R, &off, &len);
+      if (len > 0) own.push_back({(sg.g - t->grad_pool) + off, (sg.g - t->grad_pool) + off + len});
+    }
+    std::sort(own.begin(), own.end());
+    auto push_range = [&](long long a, long long b) {
+      for (long long i = a; i < b; i += Z_CHUNK)
+        ch.push_back({0, i, (int)std::min<long long>(Z_CHUNK, b - i), R});
+    };
+    x.zf_first = (int)ch.size();
+    for (const auto& r : own) push_range(r.first, r.second);
+    x.zf_count = (int)ch.size() - x.zf_first;
+    x.zr_first = (int)ch.size();
+    long long at = 0;
+    for (const auto& r : own) {
+      push_range(at, r.first);
+      at = r.second;
+    }
+    push_range(at, (long long)t->grad_floats);
+    x.zr_count = (int)ch.size() - x.zr_first;
+  }
   if ((s = dalloc(ctx, &x.d_chunks, ch.size())) != NE_OK) return s;
   NE_CUDA(cudaMemcpy(x.d_chunks, ch.data(), ch.size() * sizeof(PxChunk), cudaMemcpyHostToDevice));
   if ((s = dalloc(ctx, reinterpret_cast<uint8_t**>(&x.d_wsrc), sizeof(char*) * W)) != NE_OK ||
@@ -771,9 +913,22 @@ static ne_status px_bucket(ne_ctx* ctx, int b) {
   NE_CUDA(px_signal(x.flags, PX_READY0 + b, ctx->st));
   ne_status s = comm_fence_in(ctx);
   if (s != NE_OK) return s;
-  NE_CUDA(px_reduce(x.T, x.d_chunks + x.rs_first[b], x.rs_count[b], PX_READY0 + b, px_ctas(),
-                    ctx->d_status, ctx->comm->cs));
+  const int first = x.fused_now ? x.rsf_first[b] : x.rs_first[b];
+  const int count = x.fused_now ? x.rsf_count[b] : x.rs_count[b];
+  NE_CUDA(px_reduce(x.T, x.d_chunks + first, count, PX_READY0 + b, px_ctas(), ctx->d_status,
+                    ctx->comm->cs));
   return NE_OK;
+}
+
+// Whether segment k's dW product goes straight to its owners in this
+// micro-step (the fused exchange), and the GEMM call that does it.
+static GemmCall dw_call(ne_ctx* ctx, GemmCall c, int k) {
+  if (!ctx->comm || !ctx->comm->px || !comm_active(ctx)) return c;
+  const PxState& x = ctx->comm->pxs;
+  if (!x.ready || !x.fused_now || k >= (int)x.fused_seg.size() || !x.fused_seg[k]) return c;
+  c.epi = EPI_RESID_PEER;
+  c.peer = &x.peer_out[k];
+  return c;
 }
 
 // One bucket (segments [s0, s1)): reduce-scatter the owned segments, all-reduce
@@ -827,7 +982,12 @@ static ne_status comm_after_lmhead(ne_ctx* ctx) {
     }
     ne_status s = px_ready(ctx);
     if (s != NE_OK) return s;
-    NE_CUDA(px_epoch(ctx->comm->pxs.flags, ctx->st));
+    PxState& x = ctx->comm->pxs;
+    NE_CUDA(px_epoch(x.flags, ctx->st));
+    // the first micro-step after the gradients were zeroed may add its dW
+    // products into the owners' parts, once every owner has cleared them
+    x.fused_now = x.fused && t->micro_steps == 0;
+    if (x.fused_now) NE_CUDA(px_wait(x.T, PX_ZEROED, ctx->d_status, ctx->st));
     return px_bucket(ctx, 0);
   }
   ne_status s = comm_fence_in(ctx);
@@ -1098,10 +1258,11 @@ NE_API ne_status ne_ffn_bwd(ne_ctx* ctx, int l) {
   c.aux3 = a.H13;
   c.aux_ld = F;
   if ((s = gemm(ctx, c)) != NE_OK) return s;
-  if ((s = gemm(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F, alpha))) != NE_OK)
+  if ((s = gemm(ctx, dw_call(ctx, gc(t->dY16, D, D, 1, a.GATE, F, F, 1, M, EPI_RESID, p.g2, F,
+                                      alpha), p.seg0 + 3))) != NE_OK)
     return s;
-  if ((s = gemm(ctx, gc(t->DH13, 2 * F, 2 * F, 1, a.X2N, D, D, 1, M, EPI_RESID, p.g13, D))) !=
-      NE_OK)
+  if ((s = gemm(ctx, dw_call(ctx, gc(t->DH13, 2 * F, 2 * F, 1, a.X2N, D, D, 1, M, EPI_RESID, p.g13,
+                                      D), p.seg0 + 2))) != NE_OK)
     return s;
   if ((s = gemm(ctx, gc(t->DH13, 2 * F, M, 0, w.w13, D, D, 1, 2 * F, EPI_F32, t->dXF, D))) !=
       NE_OK)
@@ -1126,8 +1287,8 @@ NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int l) {
   const TrainLayerP& p = t->P[l];
   GemmCall c = gc(t->dX216, D, M, 0, w.wo, qd, qd, 1, D, EPI_BF16, t->dO, qd, alpha);
   if ((s = gemm(ctx, c)) != NE_OK) return s;
-  if ((s = gemm(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd, alpha))) !=
-      NE_OK)
+  if ((s = gemm(ctx, dw_call(ctx, gc(t->dX216, D, D, 1, a.O, qd, qd, 1, M, EPI_RESID, p.go, qd,
+                                      alpha), p.seg0 + 1))) != NE_OK)
     return s;
   NE_LAUNCH(launch_attn_bwd(a.Q, a.K, a.V, a.O, t->dO, a.LSE, t->Dl, B, S, Hq, Hkv, hd, S, a.QKVR,
                             m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
@@ -1135,7 +1296,8 @@ NE_API ne_status ne_attn_bwd(ne_ctx* ctx, int l) {
   ctx->launches += 1;
   if ((s = gemm(ctx, gc(t->DQKV, qkv, M, 0, w.wqkv, D, D, 1, qkv, EPI_F32, t->dXF, D))) != NE_OK)
     return s;
-  if ((s = gemm(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D))) != NE_OK)
+  if ((s = gemm(ctx, dw_call(ctx, gc(t->DQKV, qkv, qkv, 1, a.XN, D, D, 1, M, EPI_RESID, p.gqkv, D),
+                             p.seg0))) != NE_OK)
     return s;
   NE_LAUNCH(launch_rmsnorm_bwd(t->dXF, a.X, w.rms_att, m.rms_eps, M, D, t->dX2, t->dY, t->dY16,
                                p.g_att, st));
@@ -1194,6 +1356,7 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
     return fail(ctx, NE_ERR_STATE, "the exchange was aborted after a failed step");
   ne_status s = split_tokens(ctx, d_tokens);
   if (s != NE_OK) return s;
+  if (ctx->comm) ctx->comm->pxs.owned_clean = false;   // the step writes the gradients
   // The first micro-step runs eagerly (kernel attributes and modules get
   // loaded outside any capture); later ones replay the captured graph.
   if (!use_step_graph(ctx) || t->steps_run == 0) {
@@ -1201,7 +1364,9 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   } else {
     // The graph always writes the loss to its own slot; copied out below.
     float* g_loss = reinterpret_cast<float*>(t->red + 3);
-    const int gi = comm_active(ctx) ? 1 : 0;
+    const bool fused = comm_active(ctx) && ctx->comm->px && ctx->comm->pxs.ready &&
+                       ctx->comm->pxs.fused && t->micro_steps == 0;
+    const int gi = !comm_active(ctx) ? 0 : fused ? 2 : 1;
     cudaGraphExec_t& sgraph = t->step_graphs[gi];
     if (sgraph && t->step_graph_rope[gi] != ctx->rope_cs) {
       NE_CUDA(cudaGraphExecDestroy(sgraph));
@@ -1315,6 +1480,7 @@ NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, fl
   if (s != NE_OK) return s;
   float* d_loss = reinterpret_cast<float*>(t->red + 2);
   if ((s = split_tokens(ctx, t->tok)) != NE_OK) return s;
+  if (ctx->comm) ctx->comm->pxs.owned_clean = false;
   std::vector<int> phase;   // phase of the interval that ends at event k + 1
   size_t k = 0;
   auto mark = [&](int ph) -> ne_status {
@@ -1492,6 +1658,13 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
       // its bucket's event); the gradients may be zeroed once every rank has
       // published, i.e. finished reading them
       PxState& x = ctx->comm->pxs;
+      if (x.fused) {
+        // only this rank reads its owned parts: clear them now and let the
+        // other ranks' next fused exchange add into them
+        NE_CUDA(px_zero(t->grad_pool, x.d_chunks + x.zf_first, x.zf_count, ctx->st));
+        NE_CUDA(px_signal_next(x.flags, PX_ZEROED, ctx->st));
+        x.owned_clean = true;
+      }
       NE_CUDA(px_signal(x.flags, PX_W16, ctx->st));
       if ((s = comm_fence_in(ctx)) != NE_OK) return s;
       for (int b = 0; b < (int)x.ag_ev.size(); ++b) {

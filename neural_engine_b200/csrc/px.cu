@@ -86,6 +86,23 @@ __global__ void px_signal_kernel(uint32_t* own, int slot) {
   st_release_sys(own + slot, own[PX_EPOCH]);
 }
 
+__global__ void px_signal_next_kernel(uint32_t* own, int slot) {
+  __threadfence_system();
+  st_release_sys(own + slot, own[PX_EPOCH] + 1u);
+}
+
+__global__ void __launch_bounds__(256) px_zero_kernel(float* base, const PxChunk* chunks,
+                                                      int nchunks) {
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const PxChunk ch = chunks[c];
+    float* d = base + ch.dst_off;
+    const int n4 = ch.len >> 2;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x)
+      reinterpret_cast<float4*>(d)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = (n4 << 2) + threadIdx.x; i < ch.len; i += blockDim.x) d[i] = 0.f;
+  }
+}
+
 // Reduce-scatter of one bucket: own[x] = sum over ranks p (in rank order) of
 // grad_p[x] for every x of the chunks (this rank's parts of the bucket's
 // tensors).  Chunk offsets are multiples of 4 floats; lengths too, except a
@@ -172,6 +189,17 @@ cudaError_t px_epoch(uint32_t* own_flags, cudaStream_t st) {
 
 cudaError_t px_signal(uint32_t* own_flags, int slot, cudaStream_t st) {
   px_signal_kernel<<<1, 1, 0, st>>>(own_flags, slot);
+  return cudaGetLastError();
+}
+
+cudaError_t px_signal_next(uint32_t* own_flags, int slot, cudaStream_t st) {
+  px_signal_next_kernel<<<1, 1, 0, st>>>(own_flags, slot);
+  return cudaGetLastError();
+}
+
+cudaError_t px_zero(float* base, const PxChunk* chunks, int nchunks, cudaStream_t st) {
+  if (nchunks <= 0) return cudaSuccess;
+  px_zero_kernel<<<nchunks < 592 ? nchunks : 592, 256, 0, st>>>(base, chunks, nchunks);
   return cudaGetLastError();
 }
 

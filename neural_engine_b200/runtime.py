@@ -36,7 +36,8 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_comm_unique_id", "ne_comm_init", "ne_comm_set_reduce", "ne_grad_allreduce_async",
             "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
             "ne_comm_set_sharding", "ne_train_gather_state", "ne_train_fwd_bwd_timed",
-            "ne_train_value_ranges", "ne_comm_set_timeout", "ne_shard_range")
+            "ne_train_value_ranges", "ne_comm_set_timeout", "ne_shard_range",
+            "ne_gemm_dw_owned")
 
 def shard_range(n: int, world: int, rank: int, lib=None):
     """(offset, length) of the part of an n-element tensor that `rank` owns
@@ -182,6 +183,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.ne_gemm_device.argtypes = [P, P, LL, I, P, LL, I, I, I, P, LL, F]
     lib.ne_gemm_device_ex.argtypes = [P, P, LL, I, P, LL, I, I, I, P, LL, F, I, I, LL,
                                       C.POINTER(C.c_int)]
+    lib.ne_gemm_dw_owned.argtypes = [P, P, LL, I, P, LL, I, I, F, C.POINTER(P),
+                                     C.POINTER(LL), I, I, LL]
     lib.ne_decode_kernels_per_step.argtypes = [P, I]
     lib.ne_get_stream.argtypes = [P]
     lib.ne_get_stream.restype = P
@@ -384,6 +387,16 @@ class Engine:
                                                ldb, N, K, epi, C.c_void_p(d_out), ld, alpha, bn,
                                                splits, split_stride, C.byref(used)))
         return used.value
+
+    def gemm_dw_owned(self, d_a: int, lda: int, M: int, d_b: int, ldb: int, N: int, K: int,
+                      alpha: float, dst: list, bounds: list, rank: int, ld: int):
+        """acc = A^T . B (both MN-major bf16), element m*ld + n added (x alpha) into
+        dst[q] for the q whose [bounds[q], bounds[q+1]) holds it."""
+        world = len(dst)
+        d = (C.c_void_p * world)(*[C.c_void_p(x) for x in dst])
+        b = (C.c_longlong * (world + 1))(*bounds)
+        self._check(self.lib.ne_gemm_dw_owned(self._ctx, C.c_void_p(d_a), lda, M, C.c_void_p(d_b),
+                                              ldb, N, K, alpha, d, b, world, rank, ld))
 
     def gemm(self, a: int, lda: int, M: int, b: int, ldb: int, N: int, K: int, epi: int, out: int,
              ld: int, alpha: float = 1.0, a_mn: int = 0, b_mn: int = 0, aux0: int = 0,

@@ -1,0 +1,146 @@
+"""GPU, two or more devices: the fused form of the peer-memory ZeRO-1 exchange,
+in which the layer matrices' dW GEMMs add their products straight into the
+owning ranks' gradient parts over NVLink (EPI_RESID_PEER, the default;
+NE_PX_FUSED_DW=0 keeps the rank-ordered reduce-scatter after each layer).
+
+Each rank runs the same schedule of optimizer steps, which moves the exchange
+through every transition of its zeroing protocol (an owner clears its parts
+and publishes PX_ZEROED before any other rank may add into them):
+  step 1  one micro-step (eager), AdamW
+  step 2  one micro-step (captured graph), AdamW
+  step 3  two micro-steps: reduction off, then on (the second is not the
+          first since zeroing, so it reduce-scatters), AdamW
+  step 4  one micro-step (fused again), gradients gathered, AdamW
+The fused run must match the rank-ordered run: per-micro-step losses within
+1e-5 relative, step 4's reduced gradients within 1e-5 relative L2 per tensor
+(only the fp32 summation order differs), the final masters within 1e-3
+relative L2 (Adam's first steps may flip the sign of near-zero updates), and
+every rank must hold the same gathered gradients and masters.  World sizes
+above the GPU count are skipped."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+SCHEDULE = [[True], [True], [False, True], [True]]   # reduction on/off per micro-step
+
+
+def _cfg():
+    from oracle import model as om
+    return om.ModelCfg(n_layers=2, dim=128, hidden=256, heads=4, kv_heads=2, head_dim=64,
+                       vocab=512, qk_norm=True, theta=1e6, eps=1e-6)
+
+
+def _rank(rank, world, uid, toks, q, fused):
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ["NE_COMM_PX"] = "1"
+    os.environ["NE_PX_FUSED_DW"] = "1" if fused else "0"
+    res = {"rank": rank}
+    try:
+        import neural_engine_b200 as ne
+        from oracle import model as om
+        torch.cuda.set_device(rank)
+        cfg = _cfg()
+        layers, rf, emb, qk = om.init_weights(cfg, seed=4, std=0.08, bf16=True)
+        layers, rf, qk = om.random_gains(cfg, layers, rf, qk)
+        B = toks[0].shape[0] // world
+        e = ne.Engine(cfg, device=rank)
+        e.set_weights(layers, rf, emb, qk)
+        e.train_alloc(B, toks[0].shape[1] - 1)
+        e.train_set_masters(layers, emb)
+        e.zero_grads()
+        e.comm_init(uid, rank, world)
+        e.comm_set_sharding(True)
+        losses = []
+        k = 0
+        for step, micro in enumerate(SCHEDULE):
+            for on in micro:
+                e.comm_set_reduce(on)
+                losses.append(e.train_fwd_bwd(toks[k][rank * B:(rank + 1) * B]))
+                k += 1
+            e.comm_set_reduce(True)
+            if step == len(SCHEDULE) - 1:
+                e.gather_state(grads=True)
+                res["grads"] = e.get_grads()
+            e.adamw_step(step + 1, 1e-3, grad_scale=1.0 / (world * len(micro)))
+        e.gather_state()
+        res["losses"] = losses
+        res["masters"] = e.get_masters()
+        e.close()
+    except Exception as ex:   # report instead of hanging the parent
+        res["error"] = repr(ex)
+    q.put(res)
+
+
+def _run(world, toks, fused):
+    import torch.multiprocessing as mp
+    import neural_engine_b200 as ne
+    uid = ne.Engine.comm_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, toks, q, fused))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        res[r["rank"]] = r
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert "error" not in res[r], (fused, r, res[r]["error"])
+    return res
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def _flat(tree, prefix=""):
+    if isinstance(tree, dict):
+        for k in tree:
+            yield from _flat(tree[k], f"{prefix}/{k}")
+    elif isinstance(tree, (list, tuple)) and tree and not np.isscalar(tree[0]):
+        for i, v in enumerate(tree):
+            yield from _flat(v, f"{prefix}/{i}")
+    else:
+        yield prefix, np.asarray(tree)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_dw_exchange_matches_rank_ordered(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from oracle import model as om
+    cfg = _cfg()
+    S = 32
+    n_micro = sum(len(m) for m in SCHEDULE)
+    toks = [om.prompt_tokens(cfg.vocab, S + 1, 11 + i, batch=2 * world) for i in range(n_micro)]
+    fused = _run(world, toks, True)
+    plain = _run(world, toks, False)
+    for r in range(world):
+        lf, lp = fused[r]["losses"], plain[r]["losses"]
+        assert len(lf) == n_micro
+        for a, b in zip(lf, lp):
+            assert abs(a - b) <= 1e-5 * abs(b), (r, lf, lp)
+    gf = dict(_flat(fused[0]["grads"]))
+    gp = dict(_flat(plain[0]["grads"]))
+    for name in gp:
+        assert _rel(gf[name], gp[name]) <= 1e-5, name
+    for r in range(1, world):
+        for name, v in _flat(fused[r]["grads"]):
+            assert np.array_equal(v, gf[name]), (r, name)
+    mf = dict(_flat(fused[0]["masters"]))
+    mp_ = dict(_flat(plain[0]["masters"]))
+    for name in mp_:
+        assert _rel(mf[name], mp_[name]) <= 1e-3, name
+    for r in range(1, world):
+        for name, v in _flat(fused[r]["masters"]):
+            assert np.array_equal(v, mf[name]), (r, name)

@@ -339,3 +339,36 @@ def test_gemm_grouped_raster(eng, M, N, K):
     ref = _ref(a, b)
     err = (out.cpu().double() - ref).abs().max().item()
     assert err <= _tol(a, b, K), err
+
+
+@pytest.mark.parametrize("M,N,K,ld,cuts", [(200, 208, 512, 256, (64 * 100, 64 * 401)),
+                                           (768, 512, 1024, 512, (0, 64 * 3000)),
+                                           (1024, 768, 2048, 768, (64 * 4000, 64 * 8000))])
+def test_gemm_dw_owned_parts(eng, M, N, K, ld, cuts):
+    """The fused dW exchange's epilogue on one GPU: three "ranks'" copies are
+    three local buffers (rank 1's is local, the others take the system-scope
+    reductions); each copy gains alpha * A^T B exactly on its own flat range
+    [bounds[q], bounds[q+1]) and keeps its other elements bit for bit.  Rows
+    beyond M and columns beyond N within ld are never touched."""
+    a, b = _bf16((K, M), 31), _bf16((K, N), 32, 0.1)      # MN-major operands
+    da, db = a.cuda(), b.cuda()
+    world, rank, alpha = 3, 1, 0.5
+    bounds = [0, cuts[0], cuts[1], M * ld]
+    init = [torch.randn(M, ld, generator=torch.Generator().manual_seed(40 + q)) for q in range(world)]
+    dst = [x.clone().cuda() for x in init]
+    eng.gemm_dw_owned(da.data_ptr(), M, M, db.data_ptr(), N, N, K, alpha,
+                      [x.data_ptr() for x in dst], bounds, rank, ld)
+    eng.sync()
+    ref = torch.zeros(M, ld, dtype=torch.float64)
+    ref[:, :N] = alpha * (a.double().T @ b.double())
+    tol = _tol(a, b, K) * alpha
+    for q in range(world):
+        got = dst[q].cpu().reshape(-1)
+        x0 = init[q].reshape(-1)
+        lo, hi = bounds[q], bounds[q + 1]
+        want = x0.double().clone()
+        want[lo:hi] += ref.reshape(-1)[lo:hi]
+        assert torch.equal(got[:lo], x0[:lo]) and torch.equal(got[hi:], x0[hi:]), q
+        if hi > lo:
+            err = (got[lo:hi].double() - want[lo:hi]).abs().max().item()
+            assert err <= tol + 1e-6, (q, err)
