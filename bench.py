@@ -421,6 +421,24 @@ def cpu_train_sample(layers, rf, emb, qk, S=256, reps=3, model="qwen3_06b"):
     return reps * S / dt, dt, threads
 
 
+def dp_label(world, mode):
+    """How the training step's gradients are exchanged at this world size."""
+    if world == 1:
+        return "dp1 (one GPU: no gradient exchange)"
+    if mode != "zero1":
+        return f"dp{world} (per-layer NCCL all-reduce buckets overlapped with the backward)"
+    if os.environ.get("NE_COMM_PX", "1") == "0":
+        return (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter buckets overlapped with the "
+                "backward, sharded AdamW, bf16 weight all-gather)")
+    if os.environ.get("NE_PX_FUSED_DW", "1") == "0":
+        return (f"dp{world} ZeRO-1 over NVLink peer memory (the library's per-layer "
+                "reduce-scatter kernels overlapped with the backward, sharded AdamW, bf16 "
+                "weight all-gather overlapped with the next forward; no NCCL on the step)")
+    return (f"dp{world} ZeRO-1 over NVLink peer memory (the dW GEMM epilogues add into the "
+            "owning ranks' gradients, the gains are reduce-scattered per layer, sharded AdamW, "
+            "bf16 weight all-gather overlapped with the next forward; no NCCL on the step)")
+
+
 def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwen3_06b",
               B=None, S=None):
     """Data-parallel training steps: BASELINE config 4 (Qwen3-0.6B, S 256, B 16
@@ -513,18 +531,7 @@ def run_train(args, rank, local, world, layers, rf, emb, qk, barrier, model="qwe
                        "batch_per_gpu": B, "seq_len": S,
                        "global_batch": B * world, "optimizer": "AdamW lr 3e-4 b 0.9/0.95 "
                        "eps 1e-8 wd 0.1 clip 1.0", "masters": "fp32",
-                       "parallelism": (f"dp{world} ZeRO-1 over NVLink peer memory (the "
-                                       "library's per-layer reduce-scatter kernels overlapped "
-                                       "with the backward, sharded AdamW, bf16 weight "
-                                       "all-gather; no NCCL on the step)"
-                                       if world > 1 and args.dp_mode == "zero1" and
-                                       os.environ.get("NE_COMM_PX", "1") != "0" else
-                                       f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter "
-                                       "buckets overlapped with the backward, sharded AdamW, "
-                                       "bf16 weight all-gather)"
-                                       if world > 1 and args.dp_mode == "zero1" else
-                                       f"dp{world} (per-layer NCCL all-reduce buckets "
-                                       "overlapped with the backward)")},
+                       "parallelism": dp_label(world, args.dp_mode)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_kind": kind,
                          "flops_per_token": fpt, "scope": "whole step"},

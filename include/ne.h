@@ -115,6 +115,31 @@ NE_API ne_status ne_load_ckpt_v4(ne_ctx* ctx, const char* path, ne_ckpt_info* in
  * readers ignore. */
 NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info);
 
+/* Host only (no context, no GPU): read and check a v4 checkpoint's header and
+ * size before anything is loaded.  NE_ERR_IO when the file cannot be opened;
+ * NE_ERR_FORMAT for a wrong magic or version, a header whose shapes are not a
+ * model (non-positive sizes, q_dim != n_heads * head_dim, n_heads not a
+ * multiple of kv_heads) and a file shorter than the body its header implies
+ * (a truncated checkpoint), the QKN1 block included when it is present.
+ * cfg (optional) receives n_layers, dim, hidden, n_heads, kv_heads, head_dim,
+ * vocab and qk_norm (the QKN1 block was present); its other fields are left
+ * as they were.  ne_load_ckpt_v4 runs the same checks, against the context's
+ * model, before it changes any weight or optimizer state. */
+NE_API ne_status ne_ckpt_probe(const char* path, ne_model_cfg* cfg, ne_ckpt_info* info);
+
+/* Host-side fault injection (tests of the callers' failure paths; no GPU
+ * fault is ever made).  The environment variable NE_FAULT_INJECT, read once,
+ * holds comma-separated items "<entry>:<n>[:<status>]": the n-th call (from 1)
+ * of the named entry point returns <status> (io, format, cuda, oom, timeout,
+ * state; default cuda) before it does any work, with ne_last_error saying
+ * "injected".  Entry points that take part: ne_ckpt_probe, ne_load_ckpt_v4,
+ * ne_save_ckpt_v4, ne_train_fwd_bwd, ne_train_fwd_bwd_device,
+ * ne_train_fwd_bwd_timed, ne_adamw_step, ne_prefill, ne_prefill_device,
+ * ne_decode_step, ne_generate, ne_comm_init and ne_shard_range.
+ * ne_fault_calls returns how many calls of `entry` were counted so far (0
+ * when no item names it). */
+NE_API int ne_fault_calls(const char* entry);
+
 /* ---- token loop (tools/generate.py:113-228) ------------------------------
  * Allocates the fp16 KV cache and the decode / prefill workspaces for up to
  * max_batch sequences of up to max_seq positions. */

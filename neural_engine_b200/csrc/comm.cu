@@ -30,6 +30,7 @@
 
 #include "ne_comm.h"
 #include "ne_ctx.h"
+#include "ne_fault.h"
 
 namespace ne {
 
@@ -313,6 +314,7 @@ NE_API ne_status ne_comm_unique_id(void* id_out) {
 
 NE_API ne_status ne_comm_init(ne_ctx* ctx, const void* id, int rank, int world) {
   if (!ctx || !id || world < 1 || rank < 0 || rank >= world) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_comm_init");
   NcclApi& api = nccl();
   if (!api.loaded) return fail(ctx, NE_ERR_UNSUPPORTED, api.error);
   NE_CUDA(cudaSetDevice(ctx->device));

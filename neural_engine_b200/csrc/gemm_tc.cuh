@@ -498,13 +498,12 @@ struct EpiBF16S {
 // fp32 accumulation into the owner of each element (the dW products of the
 // peer-memory ZeRO-1 exchange): element m*ld + n of the output goes to the rank
 // whose part holds it, local or over NVLink.  Staged (kStage 3): the warp's
-// 32 x 32 box is read back from shared memory four rows per instruction, so
-// each lane adds 16 contiguous bytes and a warp covers four 128-byte row
-// segments, as element-wise vector reductions (red.add: atomic at the
-// destination, so every rank and every split-K unit may add into the same
-// element; system scope for another GPU's memory).  Parts start at multiples
-// of 64 elements and ld is a multiple of 64, so a 32-column chunk of a row
-// has one owner.
+// 32 x 32 box is read back from shared memory one row per instruction, so a
+// warp's 32 adds cover one contiguous 128-byte row segment, as element-wise
+// fp32 reductions (red.add: atomic at the destination, so every rank and
+// every split-K unit may add into the same element; system scope for another
+// GPU's memory).  Parts start at multiples of 64 elements and ld is a
+// multiple of 64, so a 32-column chunk of a row has one owner.
 struct EpiResidPeer {
   static constexpr int kStage = 3;
   static constexpr int kCols = 32;
@@ -528,36 +527,28 @@ struct EpiResidPeer {
   // at r*128 bytes, its 16-byte chunk q at (q ^ (r & 7)) * 16)
   __device__ static void flush(const Params& p, uint32_t box, int lane, int y, int n0, int M,
                                int N) {
-    const int q = lane & 7;
-    const int n = n0 + 4 * q;
     const bool stopped = p.abort && *reinterpret_cast<const volatile unsigned*>(p.abort) != 0u;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = 4 * i + (lane >> 3);
-      float4 w;
-      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                   : "=f"(w.x), "=f"(w.y), "=f"(w.z), "=f"(w.w)
-                   : "r"(box + r * 128 + ((q ^ (r & 7)) << 4)));
-      const int m = y + r;
-      if (m >= M || n >= N) continue;
-      const long long e = (long long)m * p.ld + n;
-      int o = 0;
+    const bool col_ok = n0 + lane < N;
+    const uint32_t col = ((lane & 3) << 2);
+    // owner of row y's chunk, then advanced row by row (parts are contiguous)
+    long long e = (long long)y * p.ld + n0;
+    int o = 0;
+    while (o + 1 < p.world && e >= p.bound[o + 1]) ++o;
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r, e += p.ld) {
+      if (y + r >= M) break;
       while (o + 1 < p.world && e >= p.bound[o + 1]) ++o;
-      if (stopped && o != p.rank) continue;
-      float* d = p.dst[o] + e;
-      if (n + 4 <= N) {
-        if (o != p.rank)
-          asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d),
-                       "f"(w.x), "f"(w.y), "f"(w.z), "f"(w.w) : "memory");
-        else
-          asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d),
-                       "f"(w.x), "f"(w.y), "f"(w.z), "f"(w.w) : "memory");
+      float w;
+      asm volatile("ld.shared.f32 %0, [%1];"
+                   : "=f"(w)
+                   : "r"(box + r * 128 + ((((lane >> 2) ^ (r & 7)) << 4) | col)));
+      if (!col_ok) continue;
+      float* d = p.dst[o] + e + lane;
+      if (o != p.rank) {
+        if (!stopped)
+          asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(d), "f"(w) : "memory");
       } else {
-        const float t[4] = {w.x, w.y, w.z, w.w};
-        for (int j = 0; j < 4 && n + j < N; ++j) {
-          if (o != p.rank) atomicAdd_system(d + j, t[j]);
-          else atomicAdd(d + j, t[j]);
-        }
+        asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(d), "f"(w) : "memory");
       }
     }
   }

@@ -36,6 +36,7 @@
 #include "ne_ctx.h"
 #include "ne_device.cuh"
 #include "ne_internal.h"
+#include "ne_fault.h"
 
 using namespace ne;
 
@@ -648,6 +649,7 @@ NE_API ne_status ne_kv_reset(ne_ctx* ctx) {
 NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, int pos0,
                                    int32_t* d_next) {
   if (!ctx || !d_tokens || !d_next || B <= 0 || S <= 0 || pos0 < 0) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_prefill_device");
   if (!ready(ctx)) return fail(ctx, NE_ERR_STATE, "weights not set");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B > ctx->max_batch || pos0 + S > ctx->max_seq)
@@ -659,6 +661,7 @@ NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, 
 NE_API ne_status ne_prefill(ne_ctx* ctx, const int32_t* h_tokens, int B, int S, int pos0,
                             int32_t* h_next, float* h_logits) {
   if (!ctx || !h_tokens) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_prefill");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B <= 0 || S <= 0 || B > ctx->max_batch || pos0 < 0 || pos0 + S > ctx->max_seq)
     return fail(ctx, NE_ERR_INVALID, "batch or sequence exceeds the allocated KV cache");
@@ -820,6 +823,7 @@ NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B) {
 NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int pos, int32_t* h_next,
                                 float* h_logits) {
   if (!ctx || !h_tok) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_decode_step");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B <= 0 || B > ctx->max_batch || pos < 0 || pos >= ctx->max_seq)
     return fail(ctx, NE_ERR_INVALID, "batch or position exceeds the allocated KV cache");
@@ -840,6 +844,7 @@ NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int po
 NE_API ne_status ne_generate(ne_ctx* ctx, const int32_t* h_prompt, int B, int P, int n_new,
                              int32_t* h_out) {
   if (!ctx || !h_prompt || !h_out || B <= 0 || P <= 0 || n_new <= 0) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_generate");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B > ctx->max_batch || P + n_new - 1 > ctx->max_seq)
     return fail(ctx, NE_ERR_INVALID, "batch or sequence exceeds the allocated KV cache");

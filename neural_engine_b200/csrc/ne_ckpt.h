@@ -17,6 +17,10 @@ struct CkptHdr {
 static_assert(sizeof(CkptHdr) == 96, "v4 header must be 96 bytes");
 constexpr int kCkptMagic = 0x424C5A54;
 
+// Opens `path` and checks its header and size (ne_ckpt_probe's checks; with
+// `want`, also that the shapes are want's model).  Fills *hdr and *has_qk.
+ne_status ckpt_check(const char* path, const ne_model_cfg* want, CkptHdr* hdr, bool* has_qk);
+
 // With training state allocated, restores the fp32 masters, the gains and the
 // Adam moments exactly (and refreshes the bf16 compute copies); sets *handled
 // to false (and does nothing) when the context has no training state.

@@ -31,6 +31,7 @@
 #include "ne_comm.h"
 #include "ne_ctx.h"
 #include "ne_internal.h"
+#include "ne_fault.h"
 
 namespace ne {
 
@@ -1350,6 +1351,7 @@ static bool use_step_graph(const ne_ctx* ctx) {
 
 NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, float* d_loss) {
   if (!ctx || !ctx->train || !d_tokens) return NE_ERR_STATE;
+  NE_FAULT_POINT(ctx, "ne_train_fwd_bwd_device");
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
   if (comm_active(ctx) && ctx->comm->aborted)   // also keeps a captured exchange from replaying
@@ -1447,6 +1449,7 @@ static ne_status finish_host_call(ne_ctx* ctx, const float* d_loss, float* h_los
 
 NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss) {
   if (!ctx || !ctx->train || !h_tokens) return NE_ERR_STATE;
+  NE_FAULT_POINT(ctx, "ne_train_fwd_bwd");
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
   ne_status s = stage_tokens(ctx, h_tokens);
@@ -1466,6 +1469,7 @@ NE_API ne_status ne_train_fwd_bwd(ne_ctx* ctx, const int32_t* h_tokens, float* h
 NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, float* h_loss,
                                         float* h_ms) {
   if (!ctx || !ctx->train || !h_tokens || !h_ms) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_train_fwd_bwd_timed");
   TrainState* t = ctx->train;
   const int L = ctx->cfg.n_layers;
   NE_CUDA(cudaSetDevice(ctx->device));
@@ -1641,6 +1645,7 @@ NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm
 // the pre-clip norm, which makes this call wait for the step to finish.
 NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, float* h_grad_norm) {
   if (!ctx || !ctx->train || !cfg || t_step <= 0) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_adamw_step");
   TrainState* t = ctx->train;
   ne_status s = upload_segs(ctx, cfg->weight_decay);
   if (s != NE_OK) return s;
@@ -1734,6 +1739,8 @@ NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which) {
 // The ZeRO-1 partition of the peer-memory exchange (host arithmetic only).
 NE_API ne_status ne_shard_range(long long n, int world, int rank, long long* off, long long* len) {
   if (n < 0 || world < 1 || rank < 0 || rank >= world || !off || !len) return NE_ERR_INVALID;
+  ne_status fs;
+  if (fault_point("ne_shard_range", &fs)) return fs;
   px_part(n, world, rank, off, len);
   return NE_OK;
 }
@@ -1808,6 +1815,7 @@ ne_status xfer(ne_ctx* ctx, const TensorRef& r, int which, float* host, bool to_
 
 extern "C" NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info) {
   if (!ctx || !path) return NE_ERR_INVALID;
+  NE_FAULT_POINT(ctx, "ne_save_ckpt_v4");
   if (!ctx->train) return fail(ctx, NE_ERR_STATE, "ne_save_ckpt_v4 needs the training state");
   if (!ctx->train->state_gathered)
     return fail(ctx, NE_ERR_STATE, "sharded optimizer state: ne_train_gather_state on every rank first");

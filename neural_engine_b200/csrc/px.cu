@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256) px_zero_kernel(float* base, const PxChunk
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     const PxChunk ch = chunks[c];
     float* d = base + ch.dst_off;
-    const int n4 = ch.len >> 2;
+    const int n4 = (reinterpret_cast<uintptr_t>(d) & 15u) == 0 ? ch.len >> 2 : 0;
     for (int i = threadIdx.x; i < n4; i += blockDim.x)
       reinterpret_cast<float4*>(d)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = (n4 << 2) + threadIdx.x; i < ch.len; i += blockDim.x) d[i] = 0.f;

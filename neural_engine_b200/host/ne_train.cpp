@@ -276,6 +276,8 @@ struct TokenFile {
     n = bytes / (u32 ? 4 : 2);
     return true;
   }
+  // a file cut inside a token (its size not a whole number of tokens)
+  bool truncated() const { return bytes % (u32 ? 4 : 2) != 0; }
   uint32_t operator[](size_t i) const {
     return u32 ? static_cast<const uint32_t*>(base)[i] : static_cast<const uint16_t*>(base)[i];
   }
@@ -347,6 +349,7 @@ int main(int argc, char** argv) {
   }
   const int rank = env_int("RANK", 0), world = env_int("WORLD_SIZE", 1);
   const int device = a.device >= 0 ? a.device : env_int("LOCAL_RANK", 0);
+  ne_ctx* ctx = nullptr;
 
   // ---- host-only modes (no GPU)
   if (!a.dump_init.empty()) {
@@ -362,6 +365,11 @@ int main(int argc, char** argv) {
   if (!a.synthetic) {
     if (!tf.open_file(a.data, a.data_u32)) {
       std::printf("Cannot open %s\n", a.data.c_str());
+      return 1;
+    }
+    if (tf.truncated()) {
+      std::printf("Token file truncated: %zu bytes is not a whole number of %d-byte tokens\n",
+                  tf.bytes, a.data_u32 ? 4 : 2);
       return 1;
     }
     if (tf.n < (size_t)S + 2) {
@@ -388,15 +396,78 @@ int main(int argc, char** argv) {
     return 0;
   }
 
+  // ---- data-parallel rendezvous (host only, before any GPU work): rank 0
+  // publishes the NCCL id in a file, the others read it
+  unsigned char id[NE_COMM_ID_BYTES];
+  if (world > 1) {
+    const char* idf = std::getenv("NE_COMM_ID_FILE");
+    const std::string path = idf ? idf : "ne_comm_id.bin";
+    if (rank == 0) {
+      CHECK(ne_comm_unique_id(id));
+      const std::string tmp = path + ".tmp";
+      FILE* f = std::fopen(tmp.c_str(), "wb");
+      if (!f || std::fwrite(id, 1, sizeof(id), f) != sizeof(id) || std::fclose(f) != 0 ||
+          std::rename(tmp.c_str(), path.c_str()) != 0) {
+        std::fprintf(stderr, "cannot publish the NCCL id to %s\n", path.c_str());
+        return 1;
+      }
+    } else {
+      // a rank 0 that never starts (or died) ends this rank's wait at the
+      // communicator deadline (NE_COMM_TIMEOUT_MS, default 60 s)
+      const int limit_ms = env_int("NE_COMM_TIMEOUT_MS", 60000);
+      bool got = false;
+      const double t0 = now_ms();
+      while (!got) {
+        FILE* f = std::fopen(path.c_str(), "rb");
+        if (f) {
+          got = std::fread(id, 1, sizeof(id), f) == sizeof(id);
+          std::fclose(f);
+        }
+        if (got || now_ms() - t0 > limit_ms) break;
+        std::this_thread::sleep_for(std::chrono::milliseconds(50));
+      }
+      if (!got) {
+        std::fprintf(stderr, "rank %d: no NCCL id in %s after %d ms (rank 0 did not start)\n",
+                     rank, path.c_str(), limit_ms);
+        return 1;
+      }
+    }
+  }
+
+  // ---- the checkpoint to resume from, checked on the host before any GPU
+  // work: a corrupt or truncated file is reported instead of half-loaded
+  bool ckpt_usable = false;
+  if (a.resume) {
+    struct stat cst;
+    if (stat(mdl.ckpt.c_str(), &cst) == 0) {
+      ne_model_cfg hc = c;
+      const ne_status ps = ne_ckpt_probe(mdl.ckpt.c_str(), &hc, nullptr);
+      const bool same = hc.n_layers == c.n_layers && hc.dim == c.dim && hc.hidden == c.hidden &&
+                        hc.n_heads == c.n_heads && hc.kv_heads == c.kv_heads &&
+                        hc.head_dim == c.head_dim && hc.vocab == c.vocab;
+      if (ps != NE_OK || !same) {
+        std::printf("[RESUME FAILED] %s: %s\n", mdl.ckpt.c_str(),
+                    ps == NE_ERR_FORMAT ? "bad header or truncated file"
+                    : ps != NE_OK       ? ne_status_str(ps)
+                                        : "a different model");
+        if (!a.scratch) {
+          std::printf("  ERROR: unusable checkpoint; remove it or pass --scratch.\n");
+          return 1;
+        }
+      } else {
+        ckpt_usable = true;
+      }
+    }
+  }
+
   // ---- context and weights
-  ne_ctx* ctx = nullptr;
   CHECK(ne_init(&ctx, &c, device));
   int start_step = 0, adam_t = 0, total_steps = a.steps;
   float lr = a.lr, resume_loss = 0.f;
   double cum_train = 0, cum_wall = 0;
   int cum_steps = 0;
   bool resuming = false;
-  if (a.resume) {
+  if (a.resume && ckpt_usable) {
     ne_ckpt_info info{};
     if (ne_load_ckpt_v4(ctx, mdl.ckpt.c_str(), &info) == NE_OK) {
       CHECK(ne_train_alloc(ctx, B, S));
@@ -462,33 +533,6 @@ int main(int argc, char** argv) {
 
   // ---- data-parallel ranks
   if (world > 1) {
-    const char* idf = std::getenv("NE_COMM_ID_FILE");
-    const std::string path = idf ? idf : "ne_comm_id.bin";
-    unsigned char id[NE_COMM_ID_BYTES];
-    if (rank == 0) {
-      CHECK(ne_comm_unique_id(id));
-      const std::string tmp = path + ".tmp";
-      FILE* f = std::fopen(tmp.c_str(), "wb");
-      if (!f || std::fwrite(id, 1, sizeof(id), f) != sizeof(id) || std::fclose(f) != 0 ||
-          std::rename(tmp.c_str(), path.c_str()) != 0) {
-        std::fprintf(stderr, "cannot publish the NCCL id to %s\n", path.c_str());
-        return 1;
-      }
-    } else {
-      bool got = false;
-      for (int i = 0; i < 600 && !got; ++i) {   // at most 60 s
-        FILE* f = std::fopen(path.c_str(), "rb");
-        if (f) {
-          got = std::fread(id, 1, sizeof(id), f) == sizeof(id);
-          std::fclose(f);
-        }
-        if (!got) std::this_thread::sleep_for(std::chrono::milliseconds(100));
-      }
-      if (!got) {
-        std::fprintf(stderr, "rank %d: no NCCL id in %s\n", rank, path.c_str());
-        return 1;
-      }
-    }
     CHECK(ne_comm_init(ctx, id, rank, world));
     if (a.zero1) CHECK(ne_comm_set_sharding(ctx, 1));
   }

@@ -37,7 +37,7 @@ EXPORTED = ("ne_init", "ne_free", "ne_last_error", "ne_status_str", "ne_sync", "
             "ne_sdpa_fwd_device", "ne_train_set_vocab_map", "ne_stream_read",
             "ne_comm_set_sharding", "ne_train_gather_state", "ne_train_fwd_bwd_timed",
             "ne_train_value_ranges", "ne_comm_set_timeout", "ne_shard_range",
-            "ne_gemm_dw_owned")
+            "ne_gemm_dw_owned", "ne_ckpt_probe", "ne_fault_calls")
 
 def shard_range(n: int, world: int, rank: int, lib=None):
     """(offset, length) of the part of an n-element tensor that `rank` owns
@@ -48,6 +48,27 @@ def shard_range(n: int, world: int, rank: int, lib=None):
     if st != 0:
         raise NeError(st, "ne_shard_range")
     return off.value, ln.value
+
+
+def ckpt_probe(path: str, lib=None) -> tuple:
+    """Check a v4 checkpoint on the host (ne_ckpt_probe): returns (model shape
+    dict, header dict); raises NeError (io / format) for a missing, corrupt or
+    truncated file."""
+    lib = lib or load_library()
+    cfg, info = ModelCfgC(), CkptInfoC()
+    st = lib.ne_ckpt_probe(os.fsencode(path), C.byref(cfg), C.byref(info))
+    if st != 0:
+        raise NeError(st, f"ne_ckpt_probe {path}")
+    shape = {k: getattr(cfg, k) for k in ("n_layers", "dim", "hidden", "n_heads", "kv_heads",
+                                          "head_dim", "vocab", "qk_norm")}
+    hdr = {k: getattr(info, k) for k, _ in CkptInfoC._fields_}
+    return shape, hdr
+
+
+def fault_calls(entry: str, lib=None) -> int:
+    """Calls of `entry` counted by the NE_FAULT_INJECT hooks of this process."""
+    lib = lib or load_library()
+    return int(lib.ne_fault_calls(entry.encode()))
 
 
 PROF_GROUPS = ("gemm_qkv", "qkv_post", "decode_attention", "gemm_wo", "resid_rmsnorm",
@@ -185,6 +206,9 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
                                       C.POINTER(C.c_int)]
     lib.ne_gemm_dw_owned.argtypes = [P, P, LL, I, P, LL, I, I, F, C.POINTER(P),
                                      C.POINTER(LL), I, I, LL]
+    lib.ne_ckpt_probe.argtypes = [C.c_char_p, C.POINTER(ModelCfgC), C.POINTER(CkptInfoC)]
+    lib.ne_fault_calls.argtypes = [C.c_char_p]
+    lib.ne_fault_calls.restype = I
     lib.ne_decode_kernels_per_step.argtypes = [P, I]
     lib.ne_get_stream.argtypes = [P]
     lib.ne_get_stream.restype = P

@@ -63,3 +63,42 @@ def test_dp_allreduce_equals_global_batch_gradient():
     err, scale, tmax = q.get(timeout=5)
     assert err <= 1e-9 * max(scale, 1.0), (err, scale)
     assert tmax == 2.0
+
+
+def _leaver(rank, port, q):
+    """Rank 1 joins the coordination group and leaves between steps (nothing
+    in flight); rank 0's next max-over-ranks must end with an error, not wait."""
+    import sys
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    t0 = time.time()
+    try:
+        bench.allmax(1.0, 2)
+        q.put(("returned", time.time() - t0, ""))
+    except Exception as e:
+        q.put(("raised", time.time() - t0, repr(e)))
+    os._exit(0)
+
+
+def test_rank_that_leaves_ends_the_others_coordination():
+    """bench.py's coordination group (gloo, a short timeout): a rank that
+    exits between steps makes the next max-over-ranks raise on the others
+    within the timeout, so no bench rank waits for good."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_leaver, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    kind, took, msg = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=30)
+    assert kind == "raised", (kind, took, msg)
+    assert took < 60, took
