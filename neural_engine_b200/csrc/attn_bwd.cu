@@ -499,17 +499,20 @@ cudaError_t launch_bwd_t(const bf16* Q, const bf16* K, const bf16* V, const bf16
 
 }  // namespace
 
-cudaError_t launch_attn_dq_mma(const __nv_bfloat16* Q, const __nv_bfloat16* K,
-                               const __nv_bfloat16* V, const __nv_bfloat16* O,
-                               const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
-                               int Hq, int Hkv, int Tmax, const float* qkv_raw, const float* qn,
-                               float qk_eps, const float2* rope_cs, __nv_bfloat16* dqkv,
-                               float* dqn, cudaStream_t st) {
-  constexpr int HD = 128, LD = HD + 8;
+namespace {
+
+template <int HD>
+cudaError_t launch_dq_mma_hd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                             const __nv_bfloat16* V, const __nv_bfloat16* O,
+                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                             int Hq, int Hkv, int Tmax, const float* qkv_raw, const float* qn,
+                             float qk_eps, const float2* rope_cs, __nv_bfloat16* dqkv,
+                             float* dqn, cudaStream_t st) {
+  constexpr int LD = HD + 8;
   const float scale = 1.0f / sqrtf((float)HD);
   const float scale_log2 = scale * 1.4426950408889634f;
   const size_t smem2 = (size_t)(3 * QT_Q + 4 * QT_KEYS) * LD * sizeof(bf16) + QT_Q * sizeof(float);
-  static bool attr = false;
+  static bool attr = false;   // one flag per instantiation
   if (!attr) {
     cudaFuncSetAttribute(dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
     attr = true;
@@ -519,6 +522,23 @@ cudaError_t launch_attn_dq_mma(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                   QkBwd{qn, qk_eps, rope_cs}, dqkv, dqn);
 }
 
+}  // namespace
+
+cudaError_t launch_attn_dq_mma(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, const __nv_bfloat16* O,
+                               const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
+                               int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                               const float* qn, float qk_eps, const float2* rope_cs,
+                               __nv_bfloat16* dqkv, float* dqn, cudaStream_t st) {
+  if (hd == 128)
+    return launch_dq_mma_hd<128>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn,
+                                 qk_eps, rope_cs, dqkv, dqn, st);
+  if (hd == 64)
+    return launch_dq_mma_hd<64>(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn, qk_eps,
+                                rope_cs, dqkv, dqn, st);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const __nv_bfloat16* V, const __nv_bfloat16* O,
                             const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
@@ -526,7 +546,7 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
                             __nv_bfloat16* dqkv, float* dqn, float* dkn, int* status,
                             cudaStream_t st) {
-  // Kernel choice for head_dim 128 (NE_ATTN_BWD_TC): "0" the mma.sync pair,
+  // Kernel choice for head_dim 128 and 64 (NE_ATTN_BWD_TC): "0" the mma.sync pair,
   // "1" the tcgen05 pair, "dkdv" mma.sync dQ + tcgen05 dK/dV; unset: by
   // sequence length (TC_BOTH_MIN_S and longer take the tcgen05 pair).
   static const int mode = [] {
@@ -537,7 +557,7 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
     return 1;
   }();
   constexpr int TC_BOTH_MIN_S = 1024;   // measured: dQ on tcgen05 wins from ~1024 positions
-  if (hd == 128 && rope_cs != nullptr && mode != 0) {
+  if ((hd == 128 || hd == 64) && rope_cs != nullptr && mode != 0) {
     const bool tc_dq = mode == 1 || (mode == -1 && S >= TC_BOTH_MIN_S);
     return launch_attn_bwd_tc(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, hd, Tmax, qkv_raw, qn, kn,
                               qk_eps, rope_cs, dqkv, dqn, dkn, status, st, tc_dq);

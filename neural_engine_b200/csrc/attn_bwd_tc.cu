@@ -1,5 +1,5 @@
 // attn_bwd_tc.cu -- causal GQA attention backward on the tcgen05 tensor cores
-// (training step, head_dim 128, bf16 operands, fp32 accumulation in TMEM).
+// (training step, head_dim 128 or 64, bf16 operands, fp32 accumulation in TMEM).
 //
 // Same mathematics as attn_bwd.cu (the reference's sdpaBwd1 / sdpaBwd2,
 // ane-training/training/training_dynamic/mil_dynamic.h:583-707, then the GQA
@@ -21,7 +21,7 @@
 //                   the accumulators (no atomics).
 // Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
 // warps 2-9 element-wise work, two per TMEM lane quarter, each of the pair
-// owning 64 of the 128 columns.  Epilogues run the inverse RoPE and the
+// owning 64 of the 128 score columns (and HD / 2 of the head columns).  Epilogues run the inverse RoPE and the
 // QK-norm backward on each thread's row and write bf16 into the gradient of
 // the fused QKV projection; the norm gains' gradients are reduced per CTA in
 // shared memory and added with one atomic per column.  Every mbarrier wait is
@@ -44,22 +44,32 @@ namespace ne {
 namespace {
 
 using bf16 = __nv_bfloat16;
-constexpr int TB_HD = 128;
 constexpr int TB_THREADS = 320;
 constexpr int TB_EW = 256;                        // element-wise threads (warps 2..9)
 constexpr uint32_t TB_ATOM = 128 * 128;           // 128 rows x 64 bf16, 128-byte swizzle
-constexpr uint32_t TB_TILE = 2 * TB_ATOM;         // 128 rows x 128 bf16
+constexpr uint32_t TB_TILE = 2 * TB_ATOM;         // 128 rows x 128 bf16 (P, dS)
 constexpr uint32_t TB_HALF_ROWS = 64 * 128;       // 64 rows of one atom (MN-major K step)
-// gain-gradient staging: 128 rows x 129 floats (padded against bank conflicts)
-constexpr uint32_t TB_RED_BYTES = 128 * 129 * 4;
 // barrier area: 128 bytes of barriers / TMEM slot / abort flag, then the pair
 // exchange [2 quantities][2 halves][128 rows] floats
 constexpr int TB_BAR_AREA = 128 + 2 * 2 * 128 * 4;
-// dq: Q | dO | K | V | dS, then the barrier area (+1 KB alignment slack)
-constexpr int DQ_SMEM = 5 * TB_TILE + TB_BAR_AREA + 1024;
-// dkdv: K | V | Q | dO | P | dS | LSE, D (2 x 128 floats, 1 KB), barrier area
-constexpr int DKV_SMEM = 6 * TB_TILE + 1024 + TB_BAR_AREA + 1024;
-static_assert(TB_RED_BYTES <= 4 * TB_TILE, "staging fits in the operand tiles");
+
+// Sizes for head dim HD (64 or 128): the Q, dO, K and V tiles hold 128 rows
+// of HD / 64 atoms; each element-wise thread of a pair owns CW = HD / 2 head
+// columns of its row.
+template <int HD>
+struct TbCfg {
+  static_assert(HD == 64 || HD == 128, "head dim 64 or 128");
+  static constexpr int NA = HD / 64;
+  static constexpr int CW = HD / 2;
+  static constexpr uint32_t TILE = NA * TB_ATOM;
+  // gain-gradient staging: 128 rows x (HD + 1) floats (padded against bank conflicts)
+  static constexpr uint32_t RED_BYTES = 128 * (HD + 1) * 4;
+  static_assert(RED_BYTES <= 4 * TILE, "staging fits in the operand tiles");
+  // dq: Q | dO | K | V | dS, then the barrier area (+1 KB alignment slack)
+  static constexpr int DQ_SMEM = 4 * TILE + TB_TILE + TB_BAR_AREA + 1024;
+  // dkdv: K | V | Q | dO | P | dS | LSE, D (2 x 128 floats, 1 KB), barrier area
+  static constexpr int DKV_SMEM = 4 * TILE + 2 * TB_TILE + 1024 + TB_BAR_AREA + 1024;
+};
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -99,17 +109,19 @@ __device__ __forceinline__ void st_row32(uint32_t atom, int row, int c0, const u
   }
 }
 
-// S-type product: D[128 x 128] = A[128 x 128] . B[128 x 128]^T, both K-major tiles.
+// S-type product: D[128 x 128] = A[128 x HD] . B[128 x HD]^T, both K-major tiles.
+template <int HD>
 __device__ __forceinline__ void mma_kk(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc) {
 #pragma unroll
-  for (int kk = 0; kk < TB_HD / 16; ++kk) {
+  for (int kk = 0; kk < HD / 16; ++kk) {
     const uint64_t ad = smem_desc_k_sw128(a + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
     const uint64_t bd = smem_desc_k_sw128(b + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
     umma_f16(d, ad, bd, idesc, kk > 0);
   }
 }
-// Accumulating product: D[128 x 128] (+)= A[128 x 128 (K)] . B where B is a
-// K-major tile [K rows][128] read MN-major (the K dimension runs over its rows).
+// Accumulating product: D[128 x N] (+)= A[128 x 128 (K)] . B where B is a
+// K-major tile [K rows][N] read MN-major (the K dimension runs over its rows;
+// N = the idesc's width, 64-column chunks one atom apart).
 __device__ __forceinline__ void mma_kmn(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc,
                                         bool acc) {
 #pragma unroll
@@ -121,22 +133,25 @@ __device__ __forceinline__ void mma_kmn(uint32_t d, uint32_t a, uint32_t b, uint
 }
 
 // Inverse RoPE and QK-norm backward of one head row's gradient, this thread
-// holding 64 consecutive columns c_lo .. c_lo+63 (the pair's other thread the
-// other 64): d (in/out), x = raw pre-norm row (same columns), dg += d x rrms.
+// holding CW = HD / 2 consecutive columns c_lo .. c_lo+CW-1 (the pair's other
+// thread the other half): d (in/out), x = raw pre-norm row (same columns),
+// dg += d x rrms.
 // `xch` is the pair's exchange area [2][128] floats, `bar_id` its barrier.
 // Every thread of the pair calls this (ok or not) so the barriers match.
 struct RowBwd {
   const float* gain;      // QK-norm gain (nullptr: none)
   float eps;
-  const float2* rope_cs;  // [pos][64] (cos, sin)
+  const float2* rope_cs;  // [pos][HD / 2] (cos, sin)
 };
-__device__ __forceinline__ void row_bwd(float (&d)[64], const float* raw, int pos, bool ok,
+template <int HD>
+__device__ __forceinline__ void row_bwd(float (&d)[HD / 2], const float* raw, int pos, bool ok,
                                         int c_lo, const RowBwd& rb, float* xch, int half,
-                                        int row, int bar_id, float (&dg)[64]) {
+                                        int row, int bar_id, float (&dg)[HD / 2]) {
+  constexpr int CW = HD / 2;
   if (ok) {
-    const float2* cs = rb.rope_cs + (size_t)pos * (TB_HD / 2) + c_lo / 2;
+    const float2* cs = rb.rope_cs + (size_t)pos * (HD / 2) + c_lo / 2;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < CW / 2; ++i) {
       const float2 c = cs[i];
       const float d0 = d[2 * i], d1 = d[2 * i + 1];
       d[2 * i] = d0 * c.x + d1 * c.y;
@@ -144,15 +159,15 @@ __device__ __forceinline__ void row_bwd(float (&d)[64], const float* raw, int po
     }
   }
   if (rb.gain == nullptr) return;
-  float x[64];
+  float x[CW];
   float ss = 0.f, dot = 0.f;
 #pragma unroll
-  for (int i = 0; i < 64; i += 4) {
+  for (int i = 0; i < CW; i += 4) {
     const float4 xv = ok ? *reinterpret_cast<const float4*>(raw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     x[i] = xv.x; x[i + 1] = xv.y; x[i + 2] = xv.z; x[i + 3] = xv.w;
   }
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
+  for (int i = 0; i < CW; ++i) {
     ss += x[i] * x[i];
     dot += d[i] * rb.gain[c_lo + i] * x[i];
   }
@@ -162,33 +177,37 @@ __device__ __forceinline__ void row_bwd(float (&d)[64], const float* raw, int po
   ss += xch[(half ^ 1) * 128 + row];
   dot += xch[256 + (half ^ 1) * 128 + row];
   named_bar(bar_id, 64);   // the exchange area is reusable
-  const float rrms = 1.0f / sqrtf(ss / (float)TB_HD + rb.eps);
-  const float c = rrms * rrms * dot / (float)TB_HD;
+  const float rrms = 1.0f / sqrtf(ss / (float)HD + rb.eps);
+  const float c = rrms * rrms * dot / (float)HD;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
+  for (int i = 0; i < CW; ++i) {
     if (ok) dg[i] += d[i] * x[i] * rrms;
     d[i] = rrms * (rb.gain[c_lo + i] * d[i] - x[i] * c);
   }
 }
 
-// Sum the element-wise threads' gain-gradient rows (each thread: 64 columns
-// of one of 128 rows) over the rows and add them to dgain[128].  `red` is
-// free shared memory of TB_RED_BYTES; all 256 element-wise threads call it.
-__device__ __forceinline__ void gain_flush(const float (&dg)[64], float* red, int half, int row,
-                                           int t, float* dgain) {
+// Sum the element-wise threads' gain-gradient rows (each thread: HD / 2
+// columns of one of 128 rows) over the rows and add them to dgain[HD].  `red`
+// is free shared memory of TbCfg<HD>::RED_BYTES; all 256 element-wise threads
+// call it.
+template <int HD>
+__device__ __forceinline__ void gain_flush(const float (&dg)[HD / 2], float* red, int half,
+                                           int row, int t, float* dgain) {
+  constexpr int CW = HD / 2;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) red[row * 129 + half * 64 + i] = dg[i];
+  for (int i = 0; i < CW; ++i) red[row * (HD + 1) + half * CW + i] = dg[i];
   named_bar(5, TB_EW);
-  if (t < TB_HD) {
+  if (t < HD) {
     float s = 0.f;
-    for (int r = 0; r < 128; ++r) s += red[r * 129 + t];
+    for (int r = 0; r < 128; ++r) s += red[r * (HD + 1) + t];
     atomicAdd(dgain + t, s);
   }
 }
 
-__device__ __forceinline__ void store_row64_bf16(bf16* dst, const float (&d)[64]) {
+template <int N>
+__device__ __forceinline__ void store_row_bf16(bf16* dst, const float (&d)[N]) {
 #pragma unroll
-  for (int i = 0; i < 64; i += 8) {
+  for (int i = 0; i < N; i += 8) {
     uint4 pk;
     __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
@@ -205,6 +224,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* st
 }
 
 // ================================================================== dQ
+template <int HD>
 __global__ void __launch_bounds__(TB_THREADS, 1)
 dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -212,12 +232,14 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
              const float* __restrict__ LSE, float* __restrict__ Dl, int S, int Hq, int Hkv,
              int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
              RowBwd rb, bf16* __restrict__ dqkv, float* __restrict__ dqn, int* status) {
+  using C = TbCfg<HD>;
+  constexpr int CW = C::CW;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
-  const uint32_t sQ = base, sdO = sQ + TB_TILE, sK = sdO + TB_TILE, sV = sK + TB_TILE;
-  const uint32_t sdS = sV + TB_TILE;
+  const uint32_t sQ = base, sdO = sQ + C::TILE, sK = sdO + C::TILE, sV = sK + C::TILE;
+  const uint32_t sdS = sV + C::TILE;
   const uint32_t bars = sdS + TB_TILE;
   const uint32_t q_full = bars, kv_full = bars + 8, kv_empty = bars + 16, s_full = bars + 24;
   const uint32_t ds_full = bars + 32, dq_done = bars + 40, drain = bars + 48;
@@ -233,7 +255,7 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   const int n_keys = min(S, q0 + 128);
   const int n_kt = (n_keys + 127) / 128;
   constexpr uint32_t IDESC_S = umma_idesc_f16(128, 128, 1, 0, 0);
-  constexpr uint32_t IDESC_Q = umma_idesc_f16(128, TB_HD, 1, 0, 1);
+  constexpr uint32_t IDESC_Q = umma_idesc_f16(128, HD, 1, 0, 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -258,7 +280,7 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;   // S at +0, dP at +128, dQ at +256
+  const uint32_t tmem = *tmem_slot;   // S at +0, dP at +128, dQ at +256 (HD columns)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -266,16 +288,16 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
       const uint64_t pol = policy_evict_last();
       const int qrow = b * S + q0;
       const int kvrow = (b * Hkv + kvh) * Tmax;
-      mbar_arrive_expect_tx(q_full, 2 * TB_TILE);
-      for (int a = 0; a < 2; ++a) {
-        tma_load_2d(sQ + a * TB_ATOM, &tmQ, q_full, h * TB_HD + a * 64, qrow, pol);
-        tma_load_2d(sdO + a * TB_ATOM, &tmdO, q_full, h * TB_HD + a * 64, qrow, pol);
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE);
+      for (int a = 0; a < C::NA; ++a) {
+        tma_load_2d(sQ + a * TB_ATOM, &tmQ, q_full, h * HD + a * 64, qrow, pol);
+        tma_load_2d(sdO + a * TB_ATOM, &tmdO, q_full, h * HD + a * 64, qrow, pol);
       }
       int j = 0;
       for (; j < n_kt; ++j) {
         if (j > 0 && !mbar_wait(kv_empty, (j - 1) & 1, status, abort_flag)) break;
-        mbar_arrive_expect_tx(kv_full, 2 * TB_TILE);
-        for (int a = 0; a < 2; ++a) {
+        mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+        for (int a = 0; a < C::NA; ++a) {
           tma_load_2d(sK + a * TB_ATOM, &tmK, kv_full, a * 64, kvrow + j * 128, pol);
           tma_load_2d(sV + a * TB_ATOM, &tmV, kv_full, a * 64, kvrow + j * 128, pol);
         }
@@ -298,8 +320,8 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
       for (int j = 0; j < n_kt && ok; ++j) {
         if (!(ok = mbar_wait(kv_full, j & 1, status, abort_flag))) break;
         tc_fence_after();
-        mma_kk(tmem, sQ, sK, IDESC_S);           // S = Q K^T
-        mma_kk(tmem + 128, sdO, sV, IDESC_S);    // dP = dO V^T
+        mma_kk<HD>(tmem, sQ, sK, IDESC_S);           // S = Q K^T
+        mma_kk<HD>(tmem + 128, sdO, sV, IDESC_S);    // dP = dO V^T
         umma_commit(s_full);
         if (!(ok = mbar_wait(ds_full, j & 1, status, abort_flag))) break;
         tc_fence_after();
@@ -320,15 +342,16 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const int q = q0 + row;
     const bool qv = q < S;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int c_lo = half * 64;
+    const int c_lo = half * 64;    // this thread's score (key) columns
+    const int h_lo = half * CW;    // and head columns
     float* const pxch = xch;   // pairs own disjoint rows of the shared exchange area
     pdl_wait();   // O, dO and LSE come from earlier kernels
-    // D = rowsum(dO * O) over this thread's 64 columns, then the pair's sum
+    // D = rowsum(dO * O) over this thread's CW columns, then the pair's sum
     float dsum = 0.f;
     if (qv) {
-      const size_t off = ((size_t)(b * S + q) * Hq + h) * TB_HD + c_lo;
+      const size_t off = ((size_t)(b * S + q) * Hq + h) * HD + h_lo;
 #pragma unroll
-      for (int i = 0; i < 64; i += 8) {
+      for (int i = 0; i < CW; i += 8) {
         const uint4 ov = *reinterpret_cast<const uint4*>(O + off + i);
         const uint4 gv = *reinterpret_cast<const uint4*>(dO + off + i);
         const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
@@ -385,31 +408,32 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     }
     // ---- epilogue: dQ * scale through the RoPE / q-norm backward, bf16 out
     if (ok && n_kt > 0) ok = warp_wait(dq_done, (n_kt - 1) & 1, status, abort_flag);
-    float d[64];
+    float d[CW];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
     if (ok) {
       tc_fence_after();
-      for (int c = 0; c < 64; c += 32) {
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_off + 256 + c_lo + c, r);
+        tmem_ld32(tmem + lane_off + 256 + h_lo + c, r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
       }
     }
-    const int qkv_dim = (Hq + 2 * Hkv) * TB_HD;
+    const int qkv_dim = (Hq + 2 * Hkv) * HD;
     const size_t tok = (size_t)b * S + (qv ? q : 0);
     const bool rv = ok && qv;
-    float dg[64];
+    float dg[CW];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) dg[i] = 0.f;
-    row_bwd(d, qkv_raw + tok * qkv_dim + (size_t)h * TB_HD + c_lo, q, rv, c_lo, rb,
-            pxch, half, row, 1 + quarter, dg);
-    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + (size_t)h * TB_HD + c_lo, d);
+    for (int i = 0; i < CW; ++i) dg[i] = 0.f;
+    row_bwd<HD>(d, qkv_raw + tok * qkv_dim + (size_t)h * HD + h_lo, q, rv, h_lo, rb, pxch, half,
+                row, 1 + quarter, dg);
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + (size_t)h * HD + h_lo, d);
     if (rb.gain != nullptr) {
       // every MMA and load of this CTA has completed (dq_done of the last
       // tile, or nothing was issued): reuse the operand tiles as staging
-      gain_flush(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dqn);
+      gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dqn);
     }
   }
 
@@ -420,6 +444,7 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
 }
 
 // ================================================================== dK, dV
+template <int HD>
 __global__ void __launch_bounds__(TB_THREADS, 1)
 dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
                const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -427,13 +452,15 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                int Hkv, int Tmax, float scale_log2, float scale,
                const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
                float* __restrict__ dkn, int* status) {
+  using C = TbCfg<HD>;
+  constexpr int CW = C::CW;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
-  const uint32_t sK = base, sV = sK + TB_TILE, sQ = sV + TB_TILE, sdO = sQ + TB_TILE;
-  const uint32_t sP = sdO + TB_TILE, sdS = sP + TB_TILE;
-  float* const sL = reinterpret_cast<float*>(gbase + 6 * TB_TILE);   // [128]
+  const uint32_t sK = base, sV = sK + C::TILE, sQ = sV + C::TILE, sdO = sQ + C::TILE;
+  const uint32_t sP = sdO + C::TILE, sdS = sP + TB_TILE;
+  float* const sL = reinterpret_cast<float*>(gbase + 4 * C::TILE + 2 * TB_TILE);   // [128]
   float* const sD = sL + 128;                                        // [128]
   const uint32_t bars = sdS + TB_TILE + 1024;
   const uint32_t kv_full = bars, qd_full = bars + 8, qd_empty = bars + 16, s_full = bars + 24;
@@ -451,7 +478,7 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   const int n_qt = n_qt_all - kt;          // query tiles at or after this key tile
   const int n_it = G * n_qt;
   constexpr uint32_t IDESC_S = umma_idesc_f16(128, 128, 1, 0, 0);
-  constexpr uint32_t IDESC_O = umma_idesc_f16(128, TB_HD, 1, 0, 1);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, 1, 0, 1);
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -476,7 +503,7 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;   // S^T +0, dP^T +128, dV +256, dK +384
+  const uint32_t tmem = *tmem_slot;   // S^T +0, dP^T +128, dV +256, dK +384 (HD columns each)
 
   if (warp == 0) {
     // ------------------------------------------------ producer (whole warp)
@@ -484,8 +511,8 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint64_t pol = policy_evict_last();
     const int kvrow = (b * Hkv + kvh) * Tmax + k0;
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * TB_TILE);
-      for (int a = 0; a < 2; ++a) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+      for (int a = 0; a < C::NA; ++a) {
         tma_load_2d(sK + a * TB_ATOM, &tmK, kv_full, a * 64, kvrow, pol);
         tma_load_2d(sV + a * TB_ATOM, &tmV, kv_full, a * 64, kvrow, pol);
       }
@@ -502,11 +529,11 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         sD[r] = v ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
       }
       if (lane == 0) {
-        mbar_arrive_expect_tx(qd_full, 2 * TB_TILE);
+        mbar_arrive_expect_tx(qd_full, 2 * C::TILE);
         const int qrow = b * S + q0;
-        for (int a = 0; a < 2; ++a) {
-          tma_load_2d(sQ + a * TB_ATOM, &tmQ, qd_full, h * TB_HD + a * 64, qrow, pol);
-          tma_load_2d(sdO + a * TB_ATOM, &tmdO, qd_full, h * TB_HD + a * 64, qrow, pol);
+        for (int a = 0; a < C::NA; ++a) {
+          tma_load_2d(sQ + a * TB_ATOM, &tmQ, qd_full, h * HD + a * 64, qrow, pol);
+          tma_load_2d(sdO + a * TB_ATOM, &tmdO, qd_full, h * HD + a * 64, qrow, pol);
         }
       } else {
         mbar_arrive(qd_full);
@@ -528,8 +555,8 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       for (int it = 0; it < n_it && ok; ++it) {
         if (!(ok = mbar_wait(qd_full, it & 1, status, abort_flag))) break;
         tc_fence_after();
-        mma_kk(tmem, sK, sQ, IDESC_S);           // S^T = K Q^T
-        mma_kk(tmem + 128, sV, sdO, IDESC_S);    // dP^T = V dO^T
+        mma_kk<HD>(tmem, sK, sQ, IDESC_S);           // S^T = K Q^T
+        mma_kk<HD>(tmem + 128, sV, sdO, IDESC_S);    // dP^T = V dO^T
         umma_commit(s_full);
         if (!(ok = mbar_wait(ps_full, it & 1, status, abort_flag))) break;
         tc_fence_after();
@@ -597,43 +624,46 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     // ---- epilogue: dV unchanged, dK * scale through RoPE / k-norm backward
     if (ok && n_it > 0) ok = warp_wait(mm2_done, (n_it - 1) & 1, status, abort_flag);
-    const int qd = Hq * TB_HD, qkv_dim = (Hq + 2 * Hkv) * TB_HD;
+    const int qd = Hq * HD, qkv_dim = (Hq + 2 * Hkv) * HD;
     const size_t tok = (size_t)b * S + (kv ? key : 0);
-    const size_t kcol = (size_t)qd + (size_t)kvh * TB_HD, vcol = kcol + (size_t)Hkv * TB_HD;
+    const size_t kcol = (size_t)qd + (size_t)kvh * HD, vcol = kcol + (size_t)Hkv * HD;
     const bool rv = ok && kv;
-    float d[64];
+    const int h_lo = half * CW;   // this thread's head columns
+    float d[CW];
     if (ok) tc_fence_after();
     // dV
 #pragma unroll
-    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
     if (ok && n_it > 0) {
-      for (int c = 0; c < 64; c += 32) {
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_off + 256 + c_lo + c, r);
+        tmem_ld32(tmem + lane_off + 256 + h_lo + c, r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]);
       }
     }
-    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + vcol + c_lo, d);
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + vcol + h_lo, d);
     // dK
 #pragma unroll
-    for (int i = 0; i < 64; ++i) d[i] = 0.f;
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
     if (ok && n_it > 0) {
-      for (int c = 0; c < 64; c += 32) {
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_off + 384 + c_lo + c, r);
+        tmem_ld32(tmem + lane_off + 384 + h_lo + c, r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
       }
     }
-    float dg[64];
+    float dg[CW];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) dg[i] = 0.f;
-    row_bwd(d, qkv_raw + tok * qkv_dim + kcol + c_lo, key, rv, c_lo, rb, pxch, half, row,
-            1 + quarter, dg);
-    if (rv) store_row64_bf16(dqkv + tok * qkv_dim + kcol + c_lo, d);
+    for (int i = 0; i < CW; ++i) dg[i] = 0.f;
+    row_bwd<HD>(d, qkv_raw + tok * qkv_dim + kcol + h_lo, key, rv, h_lo, rb, pxch, half, row,
+                1 + quarter, dg);
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + kcol + h_lo, d);
     if (rb.gain != nullptr)
-      gain_flush(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dkn);
+      gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dkn);
   }
 
   tc_fence_before();
@@ -678,7 +708,47 @@ bool tmap_tile(CUtensorMap* tm, const void* ptr, long long rows, long long cols)
 
 }  // namespace
 
-bool attn_bwd_tc_supported(int hd) { return hd == TB_HD; }
+bool attn_bwd_tc_supported(int hd) { return hd == 128 || hd == 64; }
+
+namespace {
+
+template <int HD>
+cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
+                             const CUtensorMap& tv, const __nv_bfloat16* Q,
+                             const __nv_bfloat16* K, const __nv_bfloat16* V,
+                             const __nv_bfloat16* O, const __nv_bfloat16* dO, const float* LSE,
+                             float* Dl, int B, int S, int Hq, int Hkv, int Tmax,
+                             const float* qkv_raw, const float* qn, const float* kn, float qk_eps,
+                             const float2* rope_cs, __nv_bfloat16* dqkv, float* dqn, float* dkn,
+                             int* status, cudaStream_t st, bool tc_dq) {
+  using C = TbCfg<HD>;
+  static bool attr = false;   // one flag per instantiation
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(dq_tc_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::DQ_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(dkdv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::DKV_SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const float scale = 1.0f / sqrtf((float)HD);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int n_t = (S + 127) / 128;
+  // dQ first: it also publishes D, which dK / dV read
+  cudaError_t e =
+      tc_dq ? launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM,
+                       st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                       qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
+            : launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn,
+                                 qk_eps, rope_cs, dqkv, dqn, st);
+  if (e != cudaSuccess) return e;
+  return launch_k(dkdv_tc_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS), (size_t)C::DKV_SMEM,
+                  st, tq, tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                  qkv_raw, RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn, status);
+}
+
+}  // namespace
 
 cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, const __nv_bfloat16* O,
@@ -687,7 +757,8 @@ cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const float* qn, const float* kn, float qk_eps,
                                const float2* rope_cs, __nv_bfloat16* dqkv, float* dqn, float* dkn,
                                int* status, cudaStream_t st, bool tc_dq) {
-  if (hd != TB_HD || Hq % Hkv || S <= 0 || rope_cs == nullptr) return cudaErrorInvalidValue;
+  if ((hd != 128 && hd != 64) || Hq % Hkv || S <= 0 || rope_cs == nullptr)
+    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
        reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O) |
        reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dqkv) |
@@ -699,30 +770,13 @@ cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
       !tmap_tile(&tk, K, (long long)B * Hkv * Tmax, hd) ||
       !tmap_tile(&tv, V, (long long)B * Hkv * Tmax, hd))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         DQ_SMEM);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             DKV_SMEM);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  const float scale = 1.0f / sqrtf((float)hd);
-  const float scale_log2 = scale * 1.4426950408889634f;
-  const int n_t = (S + 127) / 128;
-  // dQ first: it also publishes D, which dK / dV read
-  cudaError_t e =
-      tc_dq ? launch_k(dq_tc_kernel, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)DQ_SMEM, st, tq,
-                       tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
-                       RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
-            : launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax, qkv_raw, qn, qk_eps,
-                                 rope_cs, dqkv, dqn, st);
-  if (e != cudaSuccess) return e;
-  return launch_k(dkdv_tc_kernel, dim3(n_t, Hkv, B), dim3(TB_THREADS), (size_t)DKV_SMEM, st, tq,
-                  tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
-                  RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn, status);
+  if (hd == 128)
+    return launch_bwd_tc_hd<128>(tq, tdo, tk, tv, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
+                                 qkv_raw, qn, kn, qk_eps, rope_cs, dqkv, dqn, dkn, status, st,
+                                 tc_dq);
+  return launch_bwd_tc_hd<64>(tq, tdo, tk, tv, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
+                              qkv_raw, qn, kn, qk_eps, rope_cs, dqkv, dqn, dkn, status, st,
+                              tc_dq);
 }
 
 }  // namespace ne

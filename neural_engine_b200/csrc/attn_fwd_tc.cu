@@ -1,5 +1,5 @@
 // attn_fwd_tc.cu -- causal GQA attention forward on the tcgen05 tensor cores
-// (training step, head_dim 128, bf16).
+// (training step and the token loop's prompt pass; head_dim 128 or 64).
 //
 // Math of the reference's sdpaFwd kernel (ane-training/training/
 // training_dynamic/mil_dynamic.h:184-198: softmax(Q K^T / sqrt(hd) + causal
@@ -44,21 +44,29 @@
 namespace ne {
 namespace {
 
-constexpr int TA_HD = 128;          // head dim (this kernel)
 constexpr int TA_BQ = 128;          // query rows per CTA (UMMA M)
 constexpr int TA_BK = 128;          // keys per tile (UMMA N of the score product)
 constexpr int TA_THREADS = 320;
 constexpr int TA_SOFTMAX = 256;     // softmax threads (warps 2..9)
-constexpr uint32_t TA_Q_BYTES = TA_BQ * TA_HD * 2;      // 32 KB: 2 atoms of 64 dims
-constexpr uint32_t TA_K_BYTES = TA_BK * TA_HD * 2;      // 32 KB
-constexpr uint32_t TA_V_BYTES = TA_BK * TA_HD * 2;      // 32 KB: 2 key blocks x 2 hd boxes
 constexpr uint32_t TA_P_BYTES = TA_BQ * TA_BK * 2;      // 32 KB: 2 atoms of 64 keys
-constexpr uint32_t TA_ATOM = 128 * 128;                 // 128 rows x 64 bf16
+constexpr uint32_t TA_ATOM = 128 * 128;                 // 128 rows x 64 16-bit elements
 constexpr uint32_t TA_MN_BOX = 64 * 64 * 2;             // one 64 (hd) x 64 (keys) V box
-// Q | K[2] | V[2] | P[2] | barriers + row-max exchange (2 x 128 floats), plus 1 KB
-// alignment slack: 227 KB, the per-CTA maximum
-constexpr int TA_SMEM = TA_Q_BYTES + 2 * TA_K_BYTES + 2 * TA_V_BYTES + 2 * TA_P_BYTES + 2048 + 1024;
-static_assert(TA_SMEM <= 232448, "shared memory per CTA");
+
+// Sizes for head dim HD (64 or 128): Q, K and V tiles hold HD / 64 atoms
+// (or boxes) per 128 rows.
+template <int HD>
+struct TaCfg {
+  static_assert(HD == 64 || HD == 128, "head dim 64 or 128");
+  static constexpr int NA = HD / 64;                          // 64-element column blocks
+  static constexpr uint32_t Q_BYTES = TA_BQ * HD * 2;
+  static constexpr uint32_t K_BYTES = TA_BK * HD * 2;
+  static constexpr uint32_t V_BYTES = TA_BK * HD * 2;         // 2 key blocks x NA hd boxes
+  static constexpr int OC = HD / 2;                           // output columns per softmax warp
+  // Q | K[2] | V[2] | P[2] | barriers + row-max exchange (2 x 128 floats), plus
+  // 1 KB alignment slack (227 KB, the per-CTA maximum, at HD 128)
+  static constexpr int SMEM = Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * TA_P_BYTES + 2048 + 1024;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
 static_assert(1312 + 32 <= 2048, "barrier / exchange area");
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -99,21 +107,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 
 // T = __nv_bfloat16 (training: Q, K, V and P bf16) or __half (the token
 // loop's prefill over the fp16 KV cache: Q, K, V and P fp16); the output is
-// bf16 either way.
-template <typename T>
+// bf16 either way.  HD = head dim (64: Stories110M, 128: Qwen3).
+template <typename T, int HD>
 __global__ void __launch_bounds__(TA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int S, int Hq, int Hkv, int Tmax,
                    float qscale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                    int* status) {
+  using C = TaCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
   const uint32_t sQ = base;
-  const uint32_t sK = sQ + TA_Q_BYTES;                    // [2]
-  const uint32_t sV = sK + 2 * TA_K_BYTES;                // [2]
-  const uint32_t sP = sV + 2 * TA_V_BYTES;                // [2]
+  const uint32_t sK = sQ + C::Q_BYTES;                    // [2]
+  const uint32_t sV = sK + 2 * C::K_BYTES;                // [2]
+  const uint32_t sP = sV + 2 * C::V_BYTES;                // [2]
   const uint32_t bars = sP + 2 * TA_P_BYTES;
   const uint32_t q_full = bars;
   const uint32_t kv_full = bars + 8;      // [2]
@@ -142,7 +151,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   constexpr bool kF16 = std::is_same<T, __half>::value;
   constexpr int FMT = kF16 ? 0 : 1;      // instruction-descriptor A/B format: 0 f16, 1 bf16
   constexpr uint32_t IDESC_S = umma_idesc_f16(TA_BQ, TA_BK, FMT, 0, 0);
-  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, TA_HD, FMT, 0, 1);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, HD, FMT, 0, 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -171,7 +180,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;          // S0 at +0, S1 at +128, O at +256
+  const uint32_t tmem = *tmem_slot;          // S0 at +0, S1 at +128, O at +256 (HD columns)
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -180,19 +189,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const uint64_t pol = policy_evict_last();
       const int qrow = b * S + q0;
       const int kvrow = (b * Hkv + kvh) * Tmax;
-      mbar_arrive_expect_tx(q_full, TA_Q_BYTES);
-      for (int a = 0; a < 2; ++a)
-        tma_load_2d(sQ + a * TA_ATOM, &tmQ, q_full, h * TA_HD + a * 64, qrow, pol);
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int a = 0; a < C::NA; ++a)
+        tma_load_2d(sQ + a * TA_ATOM, &tmQ, q_full, h * HD + a * 64, qrow, pol);
       for (int j = 0; j < n_kt; ++j) {
         const int st = j & 1;
         if (j >= 2 && !mbar_wait(kv_empty + 8 * st, ((j >> 1) - 1) & 1, status, abort_flag)) break;
-        mbar_arrive_expect_tx(kv_full + 8 * st, TA_K_BYTES + TA_V_BYTES);
+        mbar_arrive_expect_tx(kv_full + 8 * st, C::K_BYTES + C::V_BYTES);
         const int k0 = kvrow + j * TA_BK;
-        for (int a = 0; a < 2; ++a)
-          tma_load_2d(sK + st * TA_K_BYTES + a * TA_ATOM, &tmK, kv_full + 8 * st, a * 64, k0, pol);
+        for (int a = 0; a < C::NA; ++a)
+          tma_load_2d(sK + st * C::K_BYTES + a * TA_ATOM, &tmK, kv_full + 8 * st, a * 64, k0, pol);
         for (int kb = 0; kb < 2; ++kb)
-          for (int c = 0; c < 2; ++c)
-            tma_load_2d(sV + st * TA_V_BYTES + kb * 2 * TA_MN_BOX + c * TA_MN_BOX, &tmV,
+          for (int c = 0; c < C::NA; ++c)
+            tma_load_2d(sV + st * C::V_BYTES + kb * C::NA * TA_MN_BOX + c * TA_MN_BOX, &tmV,
                         kv_full + 8 * st, c * 64, k0 + kb * 64, pol);
       }
       // drain (bounded): every load issued has landed before the CTA exits
@@ -216,9 +225,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (j >= 2 && !mbar_wait(s_free + 8 * st, ((j >> 1) - 1) & 1, status, abort_flag))
           return false;
         tc_fence_after();
-        const uint32_t kbase = sK + st * TA_K_BYTES;
+        const uint32_t kbase = sK + st * C::K_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < TA_HD / 16; ++kk) {
+        for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t ad = smem_desc_k_sw128(sQ + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
           const uint64_t bd = smem_desc_k_sw128(kbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
           umma_f16(tmem + st * TA_BK, ad, bd, IDESC_S, kk > 0);
@@ -232,13 +241,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (j + 1 < n_kt && !(ok = issue_s(j + 1))) break;
         if (!(ok = mbar_wait(p_full + 8 * (j & 1), (j >> 1) & 1, status, abort_flag))) break;
         tc_fence_after();
-        const uint32_t vbase = sV + (j & 1) * TA_V_BYTES;
+        const uint32_t vbase = sV + (j & 1) * C::V_BYTES;
         const uint32_t pbase = sP + (j & 1) * TA_P_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TA_BK / 16; ++kk) {
           const uint64_t ad = smem_desc_k_sw128(pbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
           const uint64_t bd =
-              smem_desc_mn_sw128(vbase + (kk >> 2) * 2 * TA_MN_BOX, TA_MN_BOX) + 128 * (kk & 3);
+              smem_desc_mn_sw128(vbase + (kk >> 2) * C::NA * TA_MN_BOX, TA_MN_BOX) + 128 * (kk & 3);
           umma_f16(tmem + 256, ad, bd, IDESC_O, (j | kk) != 0);
         }
         umma_commit(o_done + 8 * (j & 1));
@@ -366,10 +375,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
       }
       l = l * corr + sum;   // this half's share of the row sum
-      // running output *= corr (the accumulator holds tiles < j); this warp's 64 columns
+      // running output *= corr (the accumulator holds tiles < j); this warp's
+      // HD / 2 columns
       if (j > 0 && move) {
         const uint32_t orow = tmem + lane_off + 256;
-        for (int c = c_lo; c < c_lo + 64; c += 32) {
+        for (int c = half * C::OC; c < half * C::OC + C::OC; c += 32) {
           uint32_t r[32];
           tmem_ld32(orow + c, r);
 #pragma unroll
@@ -394,8 +404,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         pdl_wait();
         const uint32_t orow = tmem + lane_off + 256;
         const float inv = 1.0f / lrow;
-        __nv_bfloat16* dst = out + ((size_t)b * S + qpos) * Hq * TA_HD + (size_t)h * TA_HD;
-        for (int c = c_lo; c < c_lo + 64; c += 32) {
+        __nv_bfloat16* dst = out + ((size_t)b * S + qpos) * Hq * HD + (size_t)h * HD;
+        for (int c = half * C::OC; c < half * C::OC + C::OC; c += 32) {
           uint32_t r[32];
           tmem_ld32(orow + c, r);
           if (qpos < S) {
@@ -461,10 +471,10 @@ bool tmap_16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, i
 
 namespace {
 
-template <typename T>
+template <typename T, int HD>
 cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, int Hkv, int hd,
                       int Tmax, __nv_bfloat16* out, float* lse, int* status, cudaStream_t st) {
-  if (hd != TA_HD || Hq % Hkv) return cudaErrorInvalidValue;
+  if (hd != HD || Hq % Hkv) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
        reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(out)) & 15)
     return cudaErrorInvalidValue;
@@ -477,14 +487,25 @@ cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, 
     return cudaErrorInvalidValue;
   static bool attr = false;   // one flag per instantiation
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<T, HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TaCfg<HD>::SMEM);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  return launch_k(attn_fwd_tc_kernel<T>, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B), dim3(TA_THREADS),
-                  (size_t)TA_SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax, qscale_log2, out, lse, status);
+  return launch_k(attn_fwd_tc_kernel<T, HD>, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B),
+                  dim3(TA_THREADS), (size_t)TaCfg<HD>::SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax,
+                  qscale_log2, out, lse, status);
+}
+
+template <typename T>
+cudaError_t launch_tc_hd(const T* Q, const T* K, const T* V, int B, int S, int Hq, int Hkv,
+                         int hd, int Tmax, __nv_bfloat16* out, float* lse, int* status,
+                         cudaStream_t st) {
+  if (hd == 128) return launch_tc<T, 128>(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, lse, status, st);
+  if (hd == 64) return launch_tc<T, 64>(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, lse, status, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -493,13 +514,13 @@ cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
                                int Tmax, __nv_bfloat16* out, float* lse, int* status,
                                cudaStream_t st) {
-  return launch_tc(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, lse, status, st);
+  return launch_tc_hd(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, lse, status, st);
 }
 
 cudaError_t launch_attn_fwd_tc_f16(const __half* Q, const __half* K, const __half* V, int B,
                                    int S, int Hq, int Hkv, int hd, int Tmax,
                                    __nv_bfloat16* out, int* status, cudaStream_t st) {
-  return launch_tc(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, nullptr, status, st);
+  return launch_tc_hd(Q, K, V, B, S, Hq, Hkv, hd, Tmax, out, nullptr, status, st);
 }
 
 }  // namespace ne

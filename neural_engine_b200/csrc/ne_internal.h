@@ -151,8 +151,8 @@ cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_cli
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
                                 float inv_bc2, const float* norm_out, cudaStream_t st);
-// Causal GQA attention forward on the tcgen05 tensor cores (head_dim 128,
-// bf16): Q [B*S][Hq*hd], K / V [B][Hkv][Tmax][hd]; out [B*S][Hq*hd] bf16 and
+// Causal GQA attention forward on the tcgen05 tensor cores (head_dim 128 or
+// 64, bf16): Q [B*S][Hq*hd], K / V [B][Hkv][Tmax][hd]; out [B*S][Hq*hd] bf16 and
 // the row log-sum-exp lse [B][Hq][S] (log2 domain).
 cudaError_t launch_attn_fwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, int B, int S, int Hq, int Hkv, int hd,
@@ -174,8 +174,8 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                             const float* qn, const float* kn, float qk_eps, const float2* rope_cs,
                             __nv_bfloat16* dqkv, float* dqn, float* dkn, int* status,
                             cudaStream_t st);
-// tcgen05 variant (head_dim 128), chosen by launch_attn_bwd; tc_dq = false
-// computes dQ (and D) with the mma.sync kernel and dK / dV with tcgen05.
+// tcgen05 variant (head_dim 128 or 64), chosen by launch_attn_bwd; tc_dq =
+// false computes dQ (and D) with the mma.sync kernel and dK / dV with tcgen05.
 cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, const __nv_bfloat16* O,
                                const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
@@ -183,11 +183,12 @@ cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const float* qn, const float* kn, float qk_eps,
                                const float2* rope_cs, __nv_bfloat16* dqkv, float* dqn, float* dkn,
                                int* status, cudaStream_t st, bool tc_dq);
-// mma.sync dQ kernel alone (also publishes D); head_dim 128.
+// mma.sync dQ kernel alone (also publishes D); head_dim 128 or 64.
 cudaError_t launch_attn_dq_mma(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, const __nv_bfloat16* O,
                                const __nv_bfloat16* dO, const float* LSE, float* Dl, int B, int S,
-                               int Hq, int Hkv, int Tmax, const float* qkv_raw, const float* qn,
+                               int Hq, int Hkv, int hd, int Tmax, const float* qkv_raw,
+                               const float* qn,
                                float qk_eps, const float2* rope_cs, __nv_bfloat16* dqkv,
                                float* dqn, cudaStream_t st);
 cudaError_t launch_rmsnorm_bwd(const float* dy, const float* x, const float* w, float eps, int M,

@@ -149,16 +149,18 @@ def test_training_reduces_loss():
     e.close()
 
 
-HD128 = [dict(head_dim=128, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=1e-6),
-         dict(head_dim=128, heads=4, kv_heads=4, qk_norm=False, theta=1e4, eps=1e-5)]
+TC_ATTN = [dict(head_dim=128, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=1e-6),
+           dict(head_dim=128, heads=4, kv_heads=4, qk_norm=False, theta=1e4, eps=1e-5),
+           dict(head_dim=64, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=1e-6),
+           dict(head_dim=64, heads=4, kv_heads=4, qk_norm=False, theta=1e4, eps=1e-5)]
 
 
-@pytest.mark.parametrize("kw", HD128)
+@pytest.mark.parametrize("kw", TC_ATTN)
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 256), (4, 80), (1, 1088)])
-def test_head_dim_128_attention_backward(kw, B, S):
-    """head_dim 128 takes the tcgen05 attention kernels (forward, dK / dV,
-    and dQ from 1024 positions on): several 128-row query / key tiles, a ragged
-    last tile, GQA groups of 2 and 1, with and without QK-norm."""
+def test_tensor_core_attention_backward(kw, B, S):
+    """head_dim 128 and 64 take the tcgen05 attention kernels (forward, dK /
+    dV, and dQ from 1024 positions on): several 128-row query / key tiles, a
+    ragged last tile, GQA groups of 2 and 1, with and without QK-norm."""
     cfg = _cfg(**kw)
     layers, rf, emb, qk = om.init_weights(cfg, seed=71, std=0.08, bf16=True)
     layers, rf, qk = om.random_gains(cfg, layers, rf, qk)

@@ -205,9 +205,10 @@ def test_rmsnorm_entry_points_match_float64():
 
 @pytest.mark.parametrize("hd,Hq,Hkv,B,S", [(128, 4, 2, 2, 256), (128, 2, 2, 1, 200),
                                            (128, 4, 2, 1, 384), (128, 2, 1, 3, 64),
-                                           (64, 4, 2, 2, 160)])
+                                           (64, 4, 2, 2, 160), (64, 12, 12, 2, 256),
+                                           (64, 2, 1, 1, 300), (64, 4, 2, 1, 1024)])
 def test_sdpa_forward_matches_float64(hd, Hq, Hkv, B, S):
-    """Causal GQA attention (tcgen05 kernel at head_dim 128) vs float64 softmax;
+    """Causal GQA attention (tcgen05 kernel at head_dim 128 and 64) vs float64 softmax;
     ragged and multi-tile sequence lengths; the row LSE (log2 domain) too.
     Tolerance: bf16 output, max-abs <= 2^-7 * max|O| + 1e-3; LSE <= 1e-3."""
     import neural_engine_b200 as ne
@@ -236,15 +237,16 @@ def test_sdpa_forward_matches_float64(hd, Hq, Hkv, B, S):
     e.close()
 
 
+@pytest.mark.parametrize("hd", [128, 64])
 @pytest.mark.parametrize("S", [1024, 640])
-def test_sdpa_forward_rows_rescale_at_different_tiles(S):
+def test_sdpa_forward_rows_rescale_at_different_tiles(S, hd):
     """Scores that grow along the keys at a rate that alternates between
     neighbouring query rows: odd rows' running maximum moves at every key tile
     (their accumulated output is rescaled), even rows' never does after the
     first, so the rows of one warp take different paths.  The output must
     still match float64 (same tolerance as above)."""
     import neural_engine_b200 as ne
-    hd, Hq, Hkv, B = 128, 2, 1, 1
+    Hq, Hkv, B = 2, 1, 1
     cfg = ne.ModelConfig(1, 256, 256, Hq, Hkv, hd, 512)
     e = ne.Engine(cfg)
     g = torch.Generator().manual_seed(S)
