@@ -81,6 +81,8 @@ def parse():
                          "ncu captures of the layer kernels; not a bench number")
     ap.add_argument("--profile-vocab", type=int, default=0,
                     help="with --profile-layers: vocabulary of the profiling model")
+    ap.add_argument("--train-model", choices=("qwen3_06b", "stories110m"), default="qwen3_06b",
+                    help="with --train-only: which training leg (config 4 or config 3)")
     ap.add_argument("--train-batch", type=int, default=16, help="training sequences per GPU")
     ap.add_argument("--train-seq", type=int, default=256)
     ap.add_argument("--train-seqs", default="256,1024",
@@ -700,7 +702,12 @@ def main():
             dist.destroy_process_group()
         return
     if args.train_only:
-        train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
+        if args.train_model == "stories110m":
+            s_w = host_weights(seed=0, cfg=ne.STORIES110M)
+            train = run_train(args, rank, local, world, *s_w, barrier, model="stories110m",
+                              B=32, S=256)
+        else:
+            train = run_train(args, rank, local, world, layers, rf, emb, qk, barrier)
         if rank == 0:
             print(json.dumps(dict(train, n_gpus=world, higher_is_better=True, vs_baseline=None,
                                   data="synthetic")), flush=True)

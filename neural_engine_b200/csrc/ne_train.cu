@@ -237,13 +237,24 @@ int comm_reserved_sms() {
   return r;
 }
 
+// Split-K of the fused dW products (NE_PX_FUSED_SPLITS): 1 (default) adds
+// each output element into its owner once; 0 lets the dW heuristic split K,
+// every split then sending its own partial sums over NVLink.
+int peer_dw_splits() {
+  static const int v = [] {
+    const char* e = std::getenv("NE_PX_FUSED_SPLITS");
+    return e && e[0] == '0' ? 0 : 1;
+  }();
+  return v;
+}
+
 ne_status gemm(ne_ctx* ctx, GemmCall c) {
   c.splits = 1;
   if (ctx->comm && ctx->comm->world > 1 && ctx->comm->reduce && comm_reserved_sms() > 0)
     c.max_ctas = ctx->num_sms - comm_reserved_sms();
   if ((c.epi == EPI_RESID || c.epi == EPI_RESID_PEER) && c.a_mn && c.b_mn) {
     c.bn = 256;
-    c.splits = dw_splits(c, ctx->num_sms);
+    c.splits = c.epi == EPI_RESID_PEER && peer_dw_splits() == 1 ? 1 : dw_splits(c, ctx->num_sms);
     c.atomic = 1;
   }
   cudaError_t e = gemm_run(c, ctx->d_status, ctx->st);
