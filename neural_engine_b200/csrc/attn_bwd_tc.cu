@@ -69,6 +69,9 @@ struct TbCfg {
   static constexpr int DQ_SMEM = 4 * TILE + TB_TILE + TB_BAR_AREA + 1024;
   // dkdv: K | V | Q | dO | P | dS | LSE, D (2 x 128 floats, 1 KB), barrier area
   static constexpr int DKV_SMEM = 4 * TILE + 2 * TB_TILE + 1024 + TB_BAR_AREA + 1024;
+  // dkdv_tp: K | V | Q[2] | dO[2] | LSE, D [2][2][128] floats (2 KB), barrier area
+  static constexpr int DKV_TP_SMEM = 6 * TILE + 2048 + TB_BAR_AREA + 1024;
+  static_assert(DKV_TP_SMEM <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -91,6 +94,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
       :
       : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (completion: tmem_wait_st).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void named_bar(int id, int threads) {
@@ -249,7 +266,13 @@ dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   float* const xch = reinterpret_cast<float*>(gbars + 128);   // [2][2][128], indexed by row
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // longest-first order: CTAs start in linear block order and the query
+  // tiles furthest down the causal triangle walk the most key tiles, so the
+  // linear index runs over every (sequence, head) of the last query tile first
+  const int nbh = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qt = gridDim.x - 1 - lin / nbh;
+  const int h = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
   const int kvh = h / (Hq / Hkv);
   const int q0 = qt * 128;
   const int n_keys = min(S, q0 + 128);
@@ -471,7 +494,13 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   float* const xch = reinterpret_cast<float*>(gbars + 128);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // longest-first order: the key tiles nearest the start see the most query
+  // tiles, so the linear block index runs over every (sequence, kv-head) of
+  // key tile 0 first
+  const int nbh = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int kt = lin / nbh;
+  const int kvh = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
   const int G = Hq / Hkv;
   const int k0 = kt * 128;
   const int n_qt_all = (S + 127) / 128;
@@ -522,22 +551,23 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       const int h = kvh * G + it / n_qt;
       const int q0 = (kt + it % n_qt) * 128;
       if (it > 0 && !warp_wait(qd_empty, (it - 1) & 1, status, abort_flag)) break;
+      // the tile copies first, then the row statistics (plain loads) while
+      // they are in flight; every lane arrives after its own stores
+      if (lane == 0) {
+        mbar_expect_tx(qd_full, 2 * C::TILE);
+        const int qrow = b * S + q0;
+        for (int a = 0; a < C::NA; ++a) {
+          tma_load_2d(sQ + a * TB_ATOM, &tmQ, qd_full, h * HD + a * 64, qrow, pol);
+          tma_load_2d(sdO + a * TB_ATOM, &tmdO, qd_full, h * HD + a * 64, qrow, pol);
+        }
+      }
       for (int r = lane; r < 128; r += 32) {
         const int qq = q0 + r;
         const bool v = qq < S;
         sL[r] = v ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
         sD[r] = v ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
       }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(qd_full, 2 * C::TILE);
-        const int qrow = b * S + q0;
-        for (int a = 0; a < C::NA; ++a) {
-          tma_load_2d(sQ + a * TB_ATOM, &tmQ, qd_full, h * HD + a * 64, qrow, pol);
-          tma_load_2d(sdO + a * TB_ATOM, &tmdO, qd_full, h * HD + a * 64, qrow, pol);
-        }
-      } else {
-        mbar_arrive(qd_full);
-      }
+      mbar_arrive(qd_full);
     }
     if (lane == 0) {   // drain (bounded)
       const uint64_t t0 = globaltimer_ns();
@@ -672,6 +702,311 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ================================================================== dK, dV (pipelined)
+// The same product as dkdv_tc_kernel with the query tile split into two
+// 64-query halves that run as independent streams, P^T and dS^T kept in
+// tensor memory, and Q / dO double-buffered:
+//   * TMEM: half h's S^T at columns [64h, 64h+64) and dP^T at [128+64h, ...);
+//     the element-wise warps of half h (the pair member owning those
+//     columns) overwrite them in place with bf16 P^T / dS^T (32 columns
+//     each), which the dV += P^T dO and dK += dS^T Q products read as their A
+//     operand straight from tensor memory; dV at 256, dK at 384.
+//   * The MMA thread issues half A's dV/dK products and the next tile's S^T /
+//     dP^T for half A while half B's warps are still in their element-wise
+//     pass, and the other way round, so the tensor cores and the element-wise
+//     warps overlap; the next Q / dO tile is loaded while the current one is
+//     in use.
+template <int HD>
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq,
+               int Hkv, int Tmax, float scale_log2, float scale,
+               const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
+               float* __restrict__ dkn, int* status) {
+  using C = TbCfg<HD>;
+  constexpr int CW = C::CW;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  // K | V | Q[2] | dO[2] | LSE, D [2 buffers][2][128] floats | barrier area
+  const uint32_t sK = base, sV = sK + C::TILE;
+  const uint32_t sQ0 = sV + C::TILE, sdO0 = sQ0 + 2 * C::TILE;
+  float* const sLD = reinterpret_cast<float*>(gbase + 6 * C::TILE);   // [2][2][128]
+  const uint32_t bars = base + 6 * C::TILE + 2048;
+  const uint32_t kv_full = bars;
+  const uint32_t qd_full = bars + 8;     // [2]
+  const uint32_t qd_empty = bars + 24;   // [2]
+  const uint32_t s_full = bars + 40;     // [2] per half
+  const uint32_t ps_full = bars + 56;    // [2] per half
+  const uint32_t acc_done = bars + 72, drain = bars + 80;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 96);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 100);
+  float* const xch = reinterpret_cast<float*>(gbars + 128);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // longest-first order (key tile 0 sees every query tile)
+  const int nbh = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int kt = lin / nbh;
+  const int kvh = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
+  const int G = Hq / Hkv;
+  const int k0 = kt * 128;
+  const int n_qt_all = (S + 127) / 128;
+  const int n_qt = n_qt_all - kt;          // query tiles at or after this key tile
+  const int n_it = G * n_qt;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(128, 64, 1, 0, 0);    // 128 keys x 64 queries
+  constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, 1, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(qd_full + 8 * i, 32);   // the producer warp's lanes (LSE / D) + the TMA bytes
+      mbar_init(qd_empty + 8 * i, 1);
+      mbar_init(s_full + 8 * i, 1);
+      mbar_init(ps_full + 8 * i, TB_EW / 2);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmdO);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer (whole warp)
+    pdl_wait();
+    const uint64_t pol = policy_evict_last();
+    const int kvrow = (b * Hkv + kvh) * Tmax + k0;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+      for (int a = 0; a < C::NA; ++a) {
+        tma_load_2d(sK + a * TB_ATOM, &tmK, kv_full, a * 64, kvrow, pol);
+        tma_load_2d(sV + a * TB_ATOM, &tmV, kv_full, a * 64, kvrow, pol);
+      }
+    }
+    int it = 0;
+    for (; it < n_it; ++it) {
+      const int buf = it & 1;
+      const int h = kvh * G + it / n_qt;
+      const int q0 = (kt + it % n_qt) * 128;
+      if (it >= 2 && !warp_wait(qd_empty + 8 * buf, ((it >> 1) - 1) & 1, status, abort_flag))
+        break;
+      if (lane == 0) {
+        mbar_expect_tx(qd_full + 8 * buf, 2 * C::TILE);
+        const int qrow = b * S + q0;
+        for (int a = 0; a < C::NA; ++a) {
+          tma_load_2d(sQ0 + buf * C::TILE + a * TB_ATOM, &tmQ, qd_full + 8 * buf, h * HD + a * 64,
+                      qrow, pol);
+          tma_load_2d(sdO0 + buf * C::TILE + a * TB_ATOM, &tmdO, qd_full + 8 * buf,
+                      h * HD + a * 64, qrow, pol);
+        }
+      }
+      float* const L = sLD + buf * 256;
+      for (int r = lane; r < 128; r += 32) {
+        const int qq = q0 + r;
+        const bool v = qq < S;
+        L[r] = v ? LSE[((size_t)b * Hq + h) * S + qq] : 0.f;
+        L[128 + r] = v ? Dl[((size_t)b * Hq + h) * S + qq] : 0.f;
+      }
+      mbar_arrive(qd_full + 8 * buf);
+    }
+    if (lane == 0) {   // drain (bounded): every load issued has landed
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(kv_full, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+      for (int j = (it > 2 ? it - 2 : 0); j < it; ++j) {
+        const uint64_t t1 = globaltimer_ns();
+        while (!mbar_try_wait(qd_full + 8 * (j & 1), (j >> 1) & 1))
+          if (globaltimer_ns() - t1 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      // half hh of iteration it: S^T = K Q_hh^T and dP^T = V dO_hh^T
+      auto mma1 = [&](int it, int hh) {
+        const int buf = it & 1;
+        const uint32_t q = sQ0 + buf * C::TILE + hh * TB_HALF_ROWS;
+        const uint32_t g = sdO0 + buf * C::TILE + hh * TB_HALF_ROWS;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t kd = smem_desc_k_sw128(sK + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          const uint64_t qdsc = smem_desc_k_sw128(q + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + 64 * hh, kd, qdsc, IDESC_S, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t vd = smem_desc_k_sw128(sV + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          const uint64_t gd = smem_desc_k_sw128(g + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + 128 + 64 * hh, vd, gd, IDESC_S, kk > 0);
+        }
+        umma_commit(s_full + 8 * hh);
+      };
+      // dV += P^T_hh dO_hh, dK += dS^T_hh Q_hh (A from tensor memory, K = 64 queries)
+      auto mma2 = [&](int it, int hh) {
+        const int buf = it & 1;
+        const uint32_t q = sQ0 + buf * C::TILE + hh * TB_HALF_ROWS;
+        const uint32_t g = sdO0 + buf * C::TILE + hh * TB_HALF_ROWS;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t gd = smem_desc_mn_sw128(g, TB_ATOM) + 128 * kk;
+          umma_f16_ts(tmem + 256, tmem + 64 * hh + 8 * kk, gd, IDESC_O,
+                      (it > 0 || hh > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t qdsc = smem_desc_mn_sw128(q, TB_ATOM) + 128 * kk;
+          umma_f16_ts(tmem + 384, tmem + 128 + 64 * hh + 8 * kk, qdsc, IDESC_O,
+                      (it > 0 || hh > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(kv_full, 0, status, abort_flag);
+      if (ok && n_it > 0 && (ok = mbar_wait(qd_full, 0, status, abort_flag))) {
+        tc_fence_after();
+        mma1(0, 0);
+        mma1(0, 1);
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!(ok = mbar_wait(ps_full + 8 * hh, it & 1, status, abort_flag))) break;
+          tc_fence_after();
+          mma2(it, hh);
+          if (hh == 1) umma_commit(qd_empty + 8 * (it & 1));   // both halves read Q / dO
+          if (it + 1 < n_it) {
+            if (hh == 0) {
+              const int nb = (it + 1) & 1;
+              if (!(ok = mbar_wait(qd_full + 8 * nb, ((it + 1) >> 1) & 1, status, abort_flag)))
+                break;
+              tc_fence_after();
+            }
+            mma1(it + 1, hh);
+          }
+        }
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ element-wise warps
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;        // query half of the tile this warp owns
+    const int row = quarter * 32 + lane;
+    const int key = k0 + row;
+    const bool kv = key < S;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float* const pxch = xch;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int buf = it & 1;
+      const int q0 = (kt + it % n_qt) * 128;
+      bool ready = warp_wait(s_full + 8 * half, it & 1, status, abort_flag);
+      ready = warp_wait(qd_full + 8 * buf, (it >> 1) & 1, status, abort_flag) && ready;
+      if (!ready) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* L = sLD + buf * 256 + 64 * half;
+      const float* Dv = L + 128;
+      const uint32_t srow = tmem + lane_off + 64 * half;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(srow + c, rs);
+        tmem_ld32(srow + 128 + c, rp);
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int ql = c + i + e;                   // query within this half
+            const int qq = q0 + 64 * half + ql;
+            const float p = (kv && key <= qq && qq < S)
+                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - L[ql]) : 0.f;
+            p2[e] = p;
+            d2[e] = p * (__uint_as_float(rp[i + e]) - Dv[ql]);
+          }
+          const __nv_bfloat162 pp = __floats2bfloat162_rn(p2[0], p2[1]);
+          const __nv_bfloat162 dd = __floats2bfloat162_rn(d2[0], d2[1]);
+          wp[i >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
+          wd[i >> 1] = *reinterpret_cast<const uint32_t*>(&dd);
+        }
+        // in place: the packed words of columns c..c+31 land in columns
+        // c/2 .. c/2+15, all of which this warp has already read
+        tmem_st16(srow + (c >> 1), wp);
+        tmem_st16(srow + 128 + (c >> 1), wd);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ps_full + 8 * half);
+    }
+    // ---- epilogue: dV unchanged, dK * scale through RoPE / k-norm backward
+    if (ok && n_it > 0) ok = warp_wait(acc_done, 0, status, abort_flag);
+    const int qd = Hq * HD, qkv_dim = (Hq + 2 * Hkv) * HD;
+    const size_t tok = (size_t)b * S + (kv ? key : 0);
+    const size_t kcol = (size_t)qd + (size_t)kvh * HD, vcol = kcol + (size_t)Hkv * HD;
+    const bool rv = ok && kv;
+    const int h_lo = half * CW;   // this thread's head columns
+    float d[CW];
+    if (ok) tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
+    if (ok && n_it > 0) {
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 256 + h_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]);
+      }
+    }
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + vcol + h_lo, d);
+#pragma unroll
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
+    if (ok && n_it > 0) {
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 384 + h_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
+      }
+    }
+    float dg[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) dg[i] = 0.f;
+    row_bwd<HD>(d, qkv_raw + tok * qkv_dim + kcol + h_lo, key, rv, h_lo, rb, pxch, half, row,
+                1 + quarter, dg);
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + kcol + h_lo, d);
+    if (rb.gain != nullptr)
+      gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dkn);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -712,6 +1047,16 @@ bool attn_bwd_tc_supported(int hd) { return hd == 128 || hd == 64; }
 
 namespace {
 
+// dK / dV kernel (NE_DKDV_TP): the pipelined one with P^T / dS^T in tensor
+// memory (default), or "0" the one with P^T / dS^T in shared memory.
+bool dkdv_pipelined() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_DKDV_TP");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int HD>
 cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
                              const CUtensorMap& tv, const __nv_bfloat16* Q,
@@ -730,6 +1075,9 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
     e = cudaFuncSetAttribute(dkdv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::DKV_SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(dkdv_tp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::DKV_TP_SMEM);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   const float scale = 1.0f / sqrtf((float)HD);
@@ -743,6 +1091,11 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
             : launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn,
                                  qk_eps, rope_cs, dqkv, dqn, st);
   if (e != cudaSuccess) return e;
+  if (dkdv_pipelined())
+    return launch_k(dkdv_tp_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS),
+                    (size_t)C::DKV_TP_SMEM, st, tq, tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv,
+                    Tmax, scale_log2, scale, qkv_raw, RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn,
+                    status);
   return launch_k(dkdv_tc_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS), (size_t)C::DKV_SMEM,
                   st, tq, tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
                   qkv_raw, RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn, status);
