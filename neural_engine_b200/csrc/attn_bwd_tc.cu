@@ -69,6 +69,8 @@ struct TbCfg {
   static constexpr int DQ_SMEM = 4 * TILE + TB_TILE + TB_BAR_AREA + 1024;
   // dkdv: K | V | Q | dO | P | dS | LSE, D (2 x 128 floats, 1 KB), barrier area
   static constexpr int DKV_SMEM = 4 * TILE + 2 * TB_TILE + 1024 + TB_BAR_AREA + 1024;
+  // dq_tp: Q | dO | K[2] | V[2] | barrier area
+  static constexpr int DQ_TP_SMEM = 6 * TILE + TB_BAR_AREA + 1024;
   // dkdv_tp: K | V | Q[2] | dO[2] | LSE, D [2][2][128] floats (2 KB), barrier area
   static constexpr int DKV_TP_SMEM = 6 * TILE + 2048 + TB_BAR_AREA + 1024;
   static_assert(DKV_TP_SMEM <= 232448, "shared memory per CTA");
@@ -702,6 +704,280 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ================================================================== dQ (pipelined)
+// dq_tc_kernel's product with the key tile split into two 64-key halves run
+// as independent streams (half h: S_h = Q K_h^T at TMEM columns [64h, 64h+64),
+// dP_h at [128+64h, ...); the element-wise warps owning those columns write
+// bf16 dS_h in place over S_h, and dQ += dS_h K_h reads it from tensor memory
+// as its A operand; dQ at 256), with K / V double-buffered so the next key
+// tile loads while the current one is in use.
+template <int HD>
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+             const bf16* __restrict__ O, const bf16* __restrict__ dO,
+             const float* __restrict__ LSE, float* __restrict__ Dl, int S, int Hq, int Hkv,
+             int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
+             RowBwd rb, bf16* __restrict__ dqkv, float* __restrict__ dqn, int* status) {
+  using C = TbCfg<HD>;
+  constexpr int CW = C::CW;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  // Q | dO | K[2] | V[2] | barrier area
+  const uint32_t sQ = base, sdO = sQ + C::TILE, sK0 = sdO + C::TILE, sV0 = sK0 + 2 * C::TILE;
+  const uint32_t bars = base + 6 * C::TILE;
+  const uint32_t q_full = bars;
+  const uint32_t kv_full = bars + 8;     // [2]
+  const uint32_t kv_empty = bars + 24;   // [2]
+  const uint32_t s_full = bars + 40;     // [2] per half
+  const uint32_t ds_full = bars + 56;    // [2] per half
+  const uint32_t acc_done = bars + 72, drain = bars + 80;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 96);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 100);
+  float* const xch = reinterpret_cast<float*>(gbars + 128);   // [2][2][128], indexed by row
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbh = gridDim.y * gridDim.z;   // longest-first (see dq_tc_kernel)
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qt = gridDim.x - 1 - lin / nbh;
+  const int h = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
+  const int kvh = h / (Hq / Hkv);
+  const int q0 = qt * 128;
+  const int n_keys = min(S, q0 + 128);
+  const int n_kt = (n_keys + 127) / 128;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(128, 64, 1, 0, 0);    // 128 queries x 64 keys
+  constexpr uint32_t IDESC_Q = umma_idesc_f16(128, HD, 1, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + 8 * i, 1);
+      mbar_init(kv_empty + 8 * i, 1);
+      mbar_init(s_full + 8 * i, 1);
+      mbar_init(ds_full + 8 * i, TB_EW / 2);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmdO);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = policy_evict_last();
+      const int qrow = b * S + q0;
+      const int kvrow = (b * Hkv + kvh) * Tmax;
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE);
+      for (int a = 0; a < C::NA; ++a) {
+        tma_load_2d(sQ + a * TB_ATOM, &tmQ, q_full, h * HD + a * 64, qrow, pol);
+        tma_load_2d(sdO + a * TB_ATOM, &tmdO, q_full, h * HD + a * 64, qrow, pol);
+      }
+      int j = 0;
+      for (; j < n_kt; ++j) {
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait(kv_empty + 8 * buf, ((j >> 1) - 1) & 1, status, abort_flag))
+          break;
+        mbar_arrive_expect_tx(kv_full + 8 * buf, 2 * C::TILE);
+        for (int a = 0; a < C::NA; ++a) {
+          tma_load_2d(sK0 + buf * C::TILE + a * TB_ATOM, &tmK, kv_full + 8 * buf, a * 64,
+                      kvrow + j * 128, pol);
+          tma_load_2d(sV0 + buf * C::TILE + a * TB_ATOM, &tmV, kv_full + 8 * buf, a * 64,
+                      kvrow + j * 128, pol);
+        }
+      }
+      // drain (bounded): the loads issued have landed before the CTA exits
+      {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+      for (int i = (j > 2 ? j - 2 : 0); i < j; ++i) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full + 8 * (i & 1), (i >> 1) & 1))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      // half hh of key tile j: S_hh = Q K_hh^T, dP_hh = dO V_hh^T
+      auto mma1 = [&](int j, int hh) {
+        const int buf = j & 1;
+        const uint32_t k = sK0 + buf * C::TILE + hh * TB_HALF_ROWS;
+        const uint32_t v = sV0 + buf * C::TILE + hh * TB_HALF_ROWS;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t qd = smem_desc_k_sw128(sQ + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          const uint64_t kd = smem_desc_k_sw128(k + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + 64 * hh, qd, kd, IDESC_S, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t gd = smem_desc_k_sw128(sdO + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          const uint64_t vd = smem_desc_k_sw128(v + (kk >> 2) * TB_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + 128 + 64 * hh, gd, vd, IDESC_S, kk > 0);
+        }
+        umma_commit(s_full + 8 * hh);
+      };
+      // dQ += dS_hh K_hh (A from tensor memory, K = 64 keys)
+      auto mma2 = [&](int j, int hh) {
+        const uint32_t k = sK0 + (j & 1) * C::TILE + hh * TB_HALF_ROWS;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t kd = smem_desc_mn_sw128(k, TB_ATOM) + 128 * kk;
+          umma_f16_ts(tmem + 256, tmem + 64 * hh + 8 * kk, kd, IDESC_Q,
+                      (j > 0 || hh > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, status, abort_flag);
+      if (ok && n_kt > 0 && (ok = mbar_wait(kv_full, 0, status, abort_flag))) {
+        tc_fence_after();
+        mma1(0, 0);
+        mma1(0, 1);
+      }
+      for (int j = 0; j < n_kt && ok; ++j) {
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!(ok = mbar_wait(ds_full + 8 * hh, j & 1, status, abort_flag))) break;
+          tc_fence_after();
+          mma2(j, hh);
+          if (hh == 1) umma_commit(kv_empty + 8 * (j & 1));
+          if (j + 1 < n_kt) {
+            if (hh == 0) {
+              if (!(ok = mbar_wait(kv_full + 8 * ((j + 1) & 1), ((j + 1) >> 1) & 1, status,
+                                   abort_flag)))
+                break;
+              tc_fence_after();
+            }
+            mma1(j + 1, hh);
+          }
+        }
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ element-wise warps
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;   // key half of each tile this warp owns
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const bool qv = q < S;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int h_lo = half * CW;         // head columns of the D sum and the epilogue
+    float* const pxch = xch;
+    pdl_wait();   // O, dO and LSE come from earlier kernels
+    float dsum = 0.f;
+    if (qv) {
+      const size_t off = ((size_t)(b * S + q) * Hq + h) * HD + h_lo;
+#pragma unroll
+      for (int i = 0; i < CW; i += 8) {
+        const uint4 ov = *reinterpret_cast<const uint4*>(O + off + i);
+        const uint4 gv = *reinterpret_cast<const uint4*>(dO + off + i);
+        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
+          dsum += of.x * gf.x + of.y * gf.y;
+        }
+      }
+    }
+    pxch[half * 128 + row] = dsum;
+    named_bar(1 + quarter, 64);
+    const float Drow = dsum + pxch[(half ^ 1) * 128 + row];
+    named_bar(1 + quarter, 64);
+    if (half == 0 && qv) Dl[((size_t)b * Hq + h) * S + q] = Drow;
+    const float Lrow = qv ? LSE[((size_t)b * Hq + h) * S + q] : 0.f;
+
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      if (!warp_wait(s_full + 8 * half, j & 1, status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t srow = tmem + lane_off + 64 * half;
+      const int kbase = j * 128 + 64 * half;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(srow + c, rs);
+        tmem_ld32(srow + 128 + c, rp);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float ds2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = kbase + c + i + e;
+            const float p = (qv && key <= q && key < S)
+                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - Lrow) : 0.f;
+            ds2[e] = p * (__uint_as_float(rp[i + e]) - Drow);
+          }
+          const __nv_bfloat162 pk = __floats2bfloat162_rn(ds2[0], ds2[1]);
+          w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+        }
+        tmem_st16(srow + (c >> 1), w);   // in place over scores this warp has read
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ds_full + 8 * half);
+    }
+    // ---- epilogue: dQ * scale through the RoPE / q-norm backward, bf16 out
+    if (ok && n_kt > 0) ok = warp_wait(acc_done, 0, status, abort_flag);
+    float d[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) d[i] = 0.f;
+    if (ok) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + 256 + h_lo + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]) * scale;
+      }
+    }
+    const int qkv_dim = (Hq + 2 * Hkv) * HD;
+    const size_t tok = (size_t)b * S + (qv ? q : 0);
+    const bool rv = ok && qv;
+    float dg[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) dg[i] = 0.f;
+    row_bwd<HD>(d, qkv_raw + tok * qkv_dim + (size_t)h * HD + h_lo, q, rv, h_lo, rb, pxch, half,
+                row, 1 + quarter, dg);
+    if (rv) store_row_bf16(dqkv + tok * qkv_dim + (size_t)h * HD + h_lo, d);
+    if (rb.gain != nullptr)
+      gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dqn);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // ================================================================== dK, dV (pipelined)
 // The same product as dkdv_tc_kernel with the query tile split into two
 // 64-query halves that run as independent streams, P^T and dS^T kept in
@@ -1056,6 +1332,15 @@ bool dkdv_pipelined() {
   }();
   return on;
 }
+// The tcgen05 dQ kernel (NE_DQ_TP): pipelined with dS in tensor memory
+// (default), or "0" the serial one with dS in shared memory.
+bool dq_pipelined() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_DQ_TP");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 template <int HD>
 cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
@@ -1078,6 +1363,9 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
     e = cudaFuncSetAttribute(dkdv_tp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::DKV_TP_SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(dq_tp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::DQ_TP_SMEM);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   const float scale = 1.0f / sqrtf((float)HD);
@@ -1085,11 +1373,15 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
   const int n_t = (S + 127) / 128;
   // dQ first: it also publishes D, which dK / dV read
   cudaError_t e =
-      tc_dq ? launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM,
-                       st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
-                       qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
-            : launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn,
-                                 qk_eps, rope_cs, dqkv, dqn, st);
+      !tc_dq ? launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn,
+                                  qk_eps, rope_cs, dqkv, dqn, st)
+      : dq_pipelined()
+          ? launch_k(dq_tp_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_TP_SMEM,
+                     st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                     qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
+          : launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM,
+                     st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                     qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status);
   if (e != cudaSuccess) return e;
   if (dkdv_pipelined())
     return launch_k(dkdv_tp_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS),

@@ -174,6 +174,43 @@ def test_tensor_core_attention_backward(kw, B, S):
     e.close()
 
 
+def _child_backward(kw, B, S, env, q):
+    import os
+    for k, v in env.items():
+        os.environ[k] = v
+    try:
+        cfg = _cfg(**kw)
+        layers, rf, emb, qk = om.init_weights(cfg, seed=71, std=0.08, bf16=True)
+        layers, rf, qk = om.random_gains(cfg, layers, rf, qk)
+        tok = om.prompt_tokens(cfg.vocab, S + 1, 72, batch=B)
+        e = _engine(cfg, layers, rf, emb, qk, B, S)
+        loss = e.train_fwd_bwd(tok)
+        ref_loss, g_ref = ot.loss_and_grads(cfg, layers, rf, emb, qk, tok)
+        assert abs(loss - ref_loss) <= LOSS_REL * ref_loss, (loss, ref_loss)
+        worst = _compare_grads(cfg, e.get_grads(), g_ref)
+        e.close()
+        q.put(("ok", worst))
+    except BaseException as ex:   # report to the parent
+        q.put(("fail", repr(ex)))
+
+
+@pytest.mark.parametrize("kw", [TC_ATTN[0], TC_ATTN[3]])
+@pytest.mark.parametrize("env", [{"NE_ATTN_BWD_TC": "1"},
+                                 {"NE_ATTN_BWD_TC": "1", "NE_DQ_TP": "0", "NE_DKDV_TP": "0"}])
+def test_tensor_core_dq_at_short_sequences(kw, env):
+    """The tcgen05 dQ kernels (pipelined, and with NE_DQ_TP=0 / NE_DKDV_TP=0 the
+    serial ones) at 256 positions, where the default takes the mma.sync dQ:
+    run in a fresh process so the switches are read there."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_child_backward, args=(kw, 2, 256, env, q))
+    p.start()
+    res = q.get(timeout=300)
+    p.join(timeout=60)
+    assert res[0] == "ok", res[1]
+
+
 @pytest.mark.parametrize("name", ["stories110m", "qwen3_06b"])
 def test_full_width_two_layers(name):
     """Full-width Stories110M / Qwen3-0.6B layers (2 of them, full vocabulary,
