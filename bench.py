@@ -432,7 +432,7 @@ def dp_label(world, mode):
     if os.environ.get("NE_COMM_PX", "1") == "0":
         return (f"dp{world} ZeRO-1 (per-layer NCCL reduce-scatter buckets overlapped with the "
                 "backward, sharded AdamW, bf16 weight all-gather)")
-    if os.environ.get("NE_PX_FUSED_DW", "1") == "0":
+    if os.environ.get("NE_PX_FUSED_DW", "0") != "1":
         return (f"dp{world} ZeRO-1 over NVLink peer memory (the library's per-layer "
                 "reduce-scatter kernels overlapped with the backward, sharded AdamW, bf16 "
                 "weight all-gather overlapped with the next forward; no NCCL on the step)")

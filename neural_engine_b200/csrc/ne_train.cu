@@ -631,16 +631,17 @@ static void bucket_segs(const TrainState* t, int b, int* s0, int* s1) {
   *s1 = l + 1 < (int)t->P.size() ? t->P[l + 1].seg0 : tail0;
 }
 
-// Fused dW exchange over peer memory (NE_PX_FUSED_DW, default 1): the layer
+// Fused dW exchange over peer memory (NE_PX_FUSED_DW=1): the layer
 // matrices' dW products are added into their owners' parts by the GEMM
 // epilogue (fp32 red.add over NVLink) instead of being reduce-scattered
 // after each layer.  The sum's order then varies between runs (the adds
-// land in arrival order); NE_PX_FUSED_DW=0 keeps the rank-ordered,
-// reproducible reduction.
+// land in arrival order).  Off by default: at 2 ranks the step measured
+// slower than the rank-ordered reduce-scatter kernels, which stay the
+// default (reproducible sums).
 static bool px_fused_dw() {
   static const bool on = [] {
     const char* e = std::getenv("NE_PX_FUSED_DW");
-    return !(e && e[0] == '0');
+    return e && e[0] == '1';
   }();
   return on;
 }

@@ -1,7 +1,7 @@
 """GPU, two or more devices: the fused form of the peer-memory ZeRO-1 exchange,
 in which the layer matrices' dW GEMMs add their products straight into the
-owning ranks' gradient parts over NVLink (EPI_RESID_PEER, the default;
-NE_PX_FUSED_DW=0 keeps the rank-ordered reduce-scatter after each layer).
+owning ranks' gradient parts over NVLink (EPI_RESID_PEER, NE_PX_FUSED_DW=1;
+the default keeps the rank-ordered reduce-scatter after each layer).
 
 Each rank runs the same schedule of optimizer steps, which moves the exchange
 through every transition of its zeroing protocol (an owner clears its parts
