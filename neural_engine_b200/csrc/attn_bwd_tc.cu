@@ -162,16 +162,19 @@ struct RowBwd {
   float eps;
   const float2* rope_cs;  // [pos][HD / 2] (cos, sin)
 };
+// cs_smem (optional): this row's (cos, sin) pairs staged by rope_stage,
+// pair i at cs_smem[i ^ swz]; otherwise they are read from the table.
 template <int HD>
 __device__ __forceinline__ void row_bwd(float (&d)[HD / 2], const float* raw, int pos, bool ok,
                                         int c_lo, const RowBwd& rb, float* xch, int half,
-                                        int row, int bar_id, float (&dg)[HD / 2]) {
+                                        int row, int bar_id, float (&dg)[HD / 2],
+                                        const float2* cs_smem = nullptr, int swz = 0) {
   constexpr int CW = HD / 2;
   if (ok) {
     const float2* cs = rb.rope_cs + (size_t)pos * (HD / 2) + c_lo / 2;
 #pragma unroll
     for (int i = 0; i < CW / 2; ++i) {
-      const float2 c = cs[i];
+      const float2 c = cs_smem ? cs_smem[i ^ swz] : cs[i];
       const float d0 = d[2 * i], d1 = d[2 * i + 1];
       d[2 * i] = d0 * c.x + d1 * c.y;
       d[2 * i + 1] = d1 * c.x - d0 * c.y;
@@ -704,6 +707,44 @@ dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// The RoPE (cos, sin) pairs of this warp's 32 rows (positions pos0 .. pos0+31,
+// lane r = row r), HD / 4 pairs from pair c_lo / 2 on, into stg[32][HD / 4]:
+// each row read by the whole warp in one coalesced pass, pair i of row r
+// stored at i ^ (r & 15), so the row-per-thread reads that follow hit
+// distinct banks.  Positions at or past S are not read (zeros).
+template <int HD>
+__device__ __forceinline__ void rope_stage(float2* stg, const float2* table, int pos0, int S,
+                                           int c_lo, int lane) {
+  constexpr int NP = HD / 4;
+#pragma unroll 4
+  for (int r = 0; r < 32; ++r) {
+    const int pos = pos0 + r;
+    if (lane < NP)
+      stg[r * NP + (lane ^ (r & 15))] =
+          pos < S ? table[(size_t)pos * (HD / 2) + c_lo / 2 + lane] : make_float2(0.f, 0.f);
+  }
+  __syncwarp();
+}
+
+// This thread's HD / 2 values of row `row` as bf16 into a tile of 128 rows x
+// HD in 128-byte-swizzled atoms of 64 columns (the layout a SWIZZLE_128B
+// tensor store reads), columns h_lo .. h_lo + HD / 2 - 1.
+template <int HD>
+__device__ __forceinline__ void stage_row_bf16(uint32_t tile, int row, int h_lo,
+                                               const float (&d)[HD / 2]) {
+#pragma unroll
+  for (int c = 0; c < HD / 2; c += 32) {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const __nv_bfloat162 pk = __floats2bfloat162_rn(d[c + i], d[c + i + 1]);
+      w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+    }
+    const int col = h_lo + c;
+    st_row32(tile + (col >> 6) * TB_ATOM, row, col & 63, w);
+  }
+}
+
 // ================================================================== dQ (pipelined)
 // dq_tc_kernel's product with the key tile split into two 64-key halves run
 // as independent streams (half h: S_h = Q K_h^T at TMEM columns [64h, 64h+64),
@@ -715,6 +756,7 @@ template <int HD>
 __global__ void __launch_bounds__(TB_THREADS, 1)
 dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+             const __grid_constant__ CUtensorMap tmO,
              const bf16* __restrict__ O, const bf16* __restrict__ dO,
              const float* __restrict__ LSE, float* __restrict__ Dl, int S, int Hq, int Hkv,
              int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
@@ -919,6 +961,7 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
       tc_fence_after();
       const uint32_t srow = tmem + lane_off + 64 * half;
       const int kbase = j * 128 + 64 * half;
+      const bool nomask = qv && j < qt;   // key tiles before the diagonal: keys < q0 <= q
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
         uint32_t rs[32], rp[32];
@@ -930,9 +973,11 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
           float ds2[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = kbase + c + i + e;
-            const float p = (qv && key <= q && key < S)
-                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - Lrow) : 0.f;
+            float p = ex2_fast(fmaf(__uint_as_float(rs[i + e]), scale_log2, -Lrow));
+            if (!nomask) {
+              const int key = kbase + c + i + e;
+              if (!(qv && key <= q && key < S)) p = 0.f;
+            }
             ds2[e] = p * (__uint_as_float(rp[i + e]) - Drow);
           }
           const __nv_bfloat162 pk = __floats2bfloat162_rn(ds2[0], ds2[1]);
@@ -962,12 +1007,25 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const int qkv_dim = (Hq + 2 * Hkv) * HD;
     const size_t tok = (size_t)b * S + (qv ? q : 0);
     const bool rv = ok && qv;
+    // every MMA has completed: the operand tiles are free.  RoPE rows of this
+    // warp's 32 queries in the Q / dO tiles, the dQ tile in the last V tile
+    float2* const rstg = reinterpret_cast<float2*>(gbase) + (warp - 2) * 32 * (HD / 4);
+    const uint32_t st_q = sV0 + C::TILE;
+    rope_stage<HD>(rstg, rb.rope_cs, q0 + quarter * 32, S, h_lo, lane);
     float dg[CW];
 #pragma unroll
     for (int i = 0; i < CW; ++i) dg[i] = 0.f;
     row_bwd<HD>(d, qkv_raw + tok * qkv_dim + (size_t)h * HD + h_lo, q, rv, h_lo, rb, pxch, half,
-                row, 1 + quarter, dg);
-    if (rv) store_row_bf16(dqkv + tok * qkv_dim + (size_t)h * HD + h_lo, d);
+                row, 1 + quarter, dg, rstg + lane * (HD / 4), lane & 15);
+    stage_row_bf16<HD>(st_q, row, h_lo, d);
+    fence_async_smem();
+    named_bar(6, TB_EW);   // the tile staged; the RoPE rows read
+    if (warp == 2 && lane == 0 && ok) {
+      // one tensor store per 64 columns (rows at or past S are clipped)
+      for (int a = 0; a < C::NA; ++a) tma_store_3d(&tmO, st_q + a * TB_ATOM, h * HD + a * 64, q0, b);
+      bulk_commit_group();
+      bulk_wait_all();
+    }
     if (rb.gain != nullptr)
       gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dqn);
   }
@@ -996,6 +1054,7 @@ template <int HD>
 __global__ void __launch_bounds__(TB_THREADS, 1)
 dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
                const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const __grid_constant__ CUtensorMap tmO,
                const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq,
                int Hkv, int Tmax, float scale_log2, float scale,
                const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
@@ -1203,6 +1262,9 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       const float* L = sLD + buf * 256 + 64 * half;
       const float* Dv = L + 128;
       const uint32_t srow = tmem + lane_off + 64 * half;
+      // queries of an off-diagonal, complete tile all follow every key of
+      // this tile: no causal or length mask there
+      const bool nomask = kv && (it % n_qt) != 0 && q0 + 128 <= S;
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
         uint32_t rs[32], rp[32];
@@ -1210,21 +1272,28 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_ld32(srow + 128 + c, rp);
         uint32_t wp[16], wd[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float p2[2], d2[2];
+        for (int i = 0; i < 32; i += 4) {
+          const float4 lv = *reinterpret_cast<const float4*>(L + c + i);
+          const float4 dv = *reinterpret_cast<const float4*>(Dv + c + i);
+          const float la[4] = {lv.x, lv.y, lv.z, lv.w}, da[4] = {dv.x, dv.y, dv.z, dv.w};
+          float p4[4], d4[4];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int ql = c + i + e;                   // query within this half
-            const int qq = q0 + 64 * half + ql;
-            const float p = (kv && key <= qq && qq < S)
-                                ? exp2f(__uint_as_float(rs[i + e]) * scale_log2 - L[ql]) : 0.f;
-            p2[e] = p;
-            d2[e] = p * (__uint_as_float(rp[i + e]) - Dv[ql]);
+          for (int e = 0; e < 4; ++e) {
+            float p = ex2_fast(fmaf(__uint_as_float(rs[i + e]), scale_log2, -la[e]));
+            if (!nomask) {
+              const int qq = q0 + 64 * half + c + i + e;
+              if (!(kv && key <= qq && qq < S)) p = 0.f;
+            }
+            p4[e] = p;
+            d4[e] = p * (__uint_as_float(rp[i + e]) - da[e]);
           }
-          const __nv_bfloat162 pp = __floats2bfloat162_rn(p2[0], p2[1]);
-          const __nv_bfloat162 dd = __floats2bfloat162_rn(d2[0], d2[1]);
-          wp[i >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
-          wd[i >> 1] = *reinterpret_cast<const uint32_t*>(&dd);
+#pragma unroll
+          for (int e = 0; e < 4; e += 2) {
+            const __nv_bfloat162 pp = __floats2bfloat162_rn(p4[e], p4[e + 1]);
+            const __nv_bfloat162 dd = __floats2bfloat162_rn(d4[e], d4[e + 1]);
+            wp[(i + e) >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
+            wd[(i + e) >> 1] = *reinterpret_cast<const uint32_t*>(&dd);
+          }
         }
         // in place: the packed words of columns c..c+31 land in columns
         // c/2 .. c/2+15, all of which this warp has already read
@@ -1242,6 +1311,11 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const size_t kcol = (size_t)qd + (size_t)kvh * HD, vcol = kcol + (size_t)Hkv * HD;
     const bool rv = ok && kv;
     const int h_lo = half * CW;   // this thread's head columns
+    // every MMA has completed: the operand tiles are free.  RoPE rows of this
+    // warp's 32 keys in the K / V tiles, the dV and dK tiles in the dO tiles
+    float2* const rstg = reinterpret_cast<float2*>(gbase) + (warp - 2) * 32 * (HD / 4);
+    const uint32_t st_v = sdO0, st_k = sdO0 + C::TILE;
+    rope_stage<HD>(rstg, rb.rope_cs, k0 + quarter * 32, S, h_lo, lane);
     float d[CW];
     if (ok) tc_fence_after();
 #pragma unroll
@@ -1255,7 +1329,7 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         for (int i = 0; i < 32; ++i) d[c + i] = __uint_as_float(r[i]);
       }
     }
-    if (rv) store_row_bf16(dqkv + tok * qkv_dim + vcol + h_lo, d);
+    stage_row_bf16<HD>(st_v, row, h_lo, d);
 #pragma unroll
     for (int i = 0; i < CW; ++i) d[i] = 0.f;
     if (ok && n_it > 0) {
@@ -1271,8 +1345,19 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
     for (int i = 0; i < CW; ++i) dg[i] = 0.f;
     row_bwd<HD>(d, qkv_raw + tok * qkv_dim + kcol + h_lo, key, rv, h_lo, rb, pxch, half, row,
-                1 + quarter, dg);
-    if (rv) store_row_bf16(dqkv + tok * qkv_dim + kcol + h_lo, d);
+                1 + quarter, dg, rstg + lane * (HD / 4), lane & 15);
+    stage_row_bf16<HD>(st_k, row, h_lo, d);
+    fence_async_smem();
+    named_bar(6, TB_EW);   // both tiles staged; the RoPE rows read
+    if (warp == 2 && lane == 0 && ok) {
+      // one tensor store per 64 columns of each (rows at or past S are clipped)
+      for (int a = 0; a < C::NA; ++a) {
+        tma_store_3d(&tmO, st_v + a * TB_ATOM, (int)vcol + a * 64, k0, b);
+        tma_store_3d(&tmO, st_k + a * TB_ATOM, (int)kcol + a * 64, k0, b);
+      }
+      bulk_commit_group();
+      bulk_wait_all();
+    }
     if (rb.gain != nullptr)
       gain_flush<HD>(dg, reinterpret_cast<float*>(gbase), half, row, threadIdx.x - 64, dkn);
   }
@@ -1317,6 +1402,22 @@ bool tmap_tile(CUtensorMap* tm, const void* ptr, long long rows, long long cols)
          CUDA_SUCCESS;
 }
 
+// bf16 [B][S][cols] (row-major, cols contiguous) as a 3D map with
+// 128-byte-swizzled boxes of 64 columns x 128 rows x 1 sequence: tensor
+// stores of a 128-row tile stop at the sequence's end.
+bool tmap_rows3d(CUtensorMap* tm, const void* ptr, long long B, long long S, long long cols) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)(S * cols * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool attn_bwd_tc_supported(int hd) { return hd == 128 || hd == 64; }
@@ -1344,7 +1445,7 @@ bool dq_pipelined() {
 
 template <int HD>
 cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
-                             const CUtensorMap& tv, const __nv_bfloat16* Q,
+                             const CUtensorMap& tv, const CUtensorMap& to, const __nv_bfloat16* Q,
                              const __nv_bfloat16* K, const __nv_bfloat16* V,
                              const __nv_bfloat16* O, const __nv_bfloat16* dO, const float* LSE,
                              float* Dl, int B, int S, int Hq, int Hkv, int Tmax,
@@ -1377,7 +1478,7 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
                                   qk_eps, rope_cs, dqkv, dqn, st)
       : dq_pipelined()
           ? launch_k(dq_tp_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_TP_SMEM,
-                     st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                     st, tq, tdo, tk, tv, to, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
                      qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
           : launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM,
                      st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
@@ -1385,7 +1486,7 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
   if (e != cudaSuccess) return e;
   if (dkdv_pipelined())
     return launch_k(dkdv_tp_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS),
-                    (size_t)C::DKV_TP_SMEM, st, tq, tdo, tk, tv, LSE, (const float*)Dl, S, Hq, Hkv,
+                    (size_t)C::DKV_TP_SMEM, st, tq, tdo, tk, tv, to, LSE, (const float*)Dl, S, Hq, Hkv,
                     Tmax, scale_log2, scale, qkv_raw, RowBwd{kn, qk_eps, rope_cs}, dqkv, dkn,
                     status);
   return launch_k(dkdv_tc_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS), (size_t)C::DKV_SMEM,
@@ -1409,17 +1510,18 @@ cudaError_t launch_attn_bwd_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
        reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dqkv) |
        reinterpret_cast<uintptr_t>(qkv_raw)) & 15)
     return cudaErrorInvalidValue;
-  CUtensorMap tq, tdo, tk, tv;
+  CUtensorMap tq, tdo, tk, tv, to;
   if (!tmap_tile(&tq, Q, (long long)B * S, (long long)Hq * hd) ||
       !tmap_tile(&tdo, dO, (long long)B * S, (long long)Hq * hd) ||
       !tmap_tile(&tk, K, (long long)B * Hkv * Tmax, hd) ||
-      !tmap_tile(&tv, V, (long long)B * Hkv * Tmax, hd))
+      !tmap_tile(&tv, V, (long long)B * Hkv * Tmax, hd) ||
+      !tmap_rows3d(&to, dqkv, B, S, (long long)(Hq + 2 * Hkv) * hd))
     return cudaErrorInvalidValue;
   if (hd == 128)
-    return launch_bwd_tc_hd<128>(tq, tdo, tk, tv, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
+    return launch_bwd_tc_hd<128>(tq, tdo, tk, tv, to, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
                                  qkv_raw, qn, kn, qk_eps, rope_cs, dqkv, dqn, dkn, status, st,
                                  tc_dq);
-  return launch_bwd_tc_hd<64>(tq, tdo, tk, tv, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
+  return launch_bwd_tc_hd<64>(tq, tdo, tk, tv, to, Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, Tmax,
                               qkv_raw, qn, kn, qk_eps, rope_cs, dqkv, dqn, dkn, status, st,
                               tc_dq);
 }

@@ -111,7 +111,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 template <typename T, int HD>
 __global__ void __launch_bounds__(TA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, int S, int Hq, int Hkv, int Tmax,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                   int S, int Hq, int Hkv, int Tmax,
                    float qscale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                    int* status) {
   using C = TaCfg<HD>;
@@ -298,8 +299,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int h = 0; h < 2; ++h) {
           tmem_ld32(srow + c_lo + 32 * h, sr[h]);
           if (full) {
+            // four independent chains (the compiler keeps fmaxf's order)
+            float m4[4] = {mraw, -3.0e38f, -3.0e38f, -3.0e38f};
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(sr[h][i]));
+            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(sr[h][i]));
+            mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -342,7 +346,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const float corr = move_row ? exp2f(m - mx) : 1.0f;
       if (move_row) m = mx;
       // pass 2: p = exp2(s - m) -> P (T, swizzled K-major rows), row sum
-      float sum = 0.f;
+      float sum = 0.f, sum2 = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = c_lo + 32 * h;
@@ -350,13 +354,14 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int key = kbase + c + i;
-          float p0 = exp2f(fmaf(__uint_as_float(sr[h][i]), qscale_log2, -m));
-          float p1 = exp2f(fmaf(__uint_as_float(sr[h][i + 1]), qscale_log2, -m));
+          float p0 = ex2_fast(fmaf(__uint_as_float(sr[h][i]), qscale_log2, -m));
+          float p1 = ex2_fast(fmaf(__uint_as_float(sr[h][i + 1]), qscale_log2, -m));
           if (!full) {
             if (!(key <= qpos && key < S)) p0 = 0.f;
             if (!(key + 1 <= qpos && key + 1 < S)) p1 = 0.f;
           }
-          sum += p0 + p1;
+          sum += p0;
+          sum2 += p1;
           if constexpr (kF16) {
             const __half2 pk = __floats2half2_rn(p0, p1);
             w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
@@ -374,7 +379,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                        w[4 * q + 3]);
         }
       }
-      l = l * corr + sum;   // this half's share of the row sum
+      l = l * corr + (sum + sum2);   // this half's share of the row sum
       // running output *= corr (the accumulator holds tiles < j); this warp's
       // HD / 2 columns
       if (j > 0 && move) {
@@ -391,7 +396,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tc_fence_before();
       mbar_arrive(p_full + 8 * st);
     }
-    // ---- output: O / l (bf16) and the row LSE (log2 domain)
+    // ---- output: O / l (bf16) and the row LSE (log2 domain).  Every MMA has
+    // completed once the last P.V product is done, so the first K buffer
+    // holds the bf16 output tile (swizzled atoms) for one tensor store per 64
+    // columns; rows at or past S are clipped by the store.
+    bool staged = false;
     if (ok && n_kt > 0) {
       const bool od =
           mbar_wait(o_done + 8 * ((n_kt - 1) & 1), ((n_kt - 1) >> 1) & 1, status, abort_flag);
@@ -404,24 +413,39 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         pdl_wait();
         const uint32_t orow = tmem + lane_off + 256;
         const float inv = 1.0f / lrow;
-        __nv_bfloat16* dst = out + ((size_t)b * S + qpos) * Hq * HD + (size_t)h * HD;
         for (int c = half * C::OC; c < half * C::OC + C::OC; c += 32) {
           uint32_t r[32];
           tmem_ld32(orow + c, r);
-          if (qpos < S) {
+          uint32_t w[16];
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 pk;
-              __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&pk);
+          for (int i = 0; i < 32; i += 2) {
+            const __nv_bfloat162 pk = __floats2bfloat162_rn(__uint_as_float(r[i]) * inv,
+                                                            __uint_as_float(r[i + 1]) * inv);
+            w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          }
+          const uint32_t atom = sK + (c >> 6) * TA_ATOM + row * 128;
 #pragma unroll
-              for (int t = 0; t < 4; ++t)
-                hv[t] = __floats2bfloat162_rn(__uint_as_float(r[i + 2 * t]) * inv,
-                                              __uint_as_float(r[i + 2 * t + 1]) * inv);
-              *reinterpret_cast<uint4*>(dst + c + i) = pk;
-            }
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = ((c & 63) >> 3) + q;
+            st_shared_v4(atom + ((chunk ^ (row & 7)) << 4), w[4 * q], w[4 * q + 1],
+                         w[4 * q + 2], w[4 * q + 3]);
           }
         }
+        staged = true;
         if (half == 0 && qpos < S && lse) lse[((size_t)b * Hq + h) * S + qpos] = m + log2f(lrow);
+      }
+    }
+    // every softmax warp reaches this barrier, whatever happened before
+    if (lane == 0) xok[half * 4 + quarter] = staged ? 1 : 0;
+    fence_async_smem();
+    asm volatile("bar.sync 5, %0;" ::"r"(TA_SOFTMAX) : "memory");
+    if (warp == 2 && lane == 0) {
+      bool all = true;
+      for (int i = 0; i < 8; ++i) all = all && xok[i] != 0;
+      if (all) {
+        for (int a = 0; a < C::NA; ++a) tma_store_3d(&tmO, sK + a * TA_ATOM, h * HD + a * 64, q0, b);
+        bulk_commit_group();
+        bulk_wait_all();
       }
     }
   }
@@ -467,6 +491,21 @@ bool tmap_16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, i
          CUDA_SUCCESS;
 }
 
+// bf16 [B][S][cols] as a 3D map with 128-byte-swizzled boxes of 64 columns
+// x 128 rows x 1 sequence (tensor stores of a 128-row tile stop at S).
+bool tmap_rows3d(CUtensorMap* tm, const void* ptr, long long B, long long S, long long cols) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)(S * cols * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 }  // namespace
 
 namespace {
@@ -480,10 +519,11 @@ cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, 
     return cudaErrorInvalidValue;
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!tmap_16(&tq, Q, (long long)B * S, (long long)Hq * hd, TA_BQ, dt) ||
       !tmap_16(&tk, K, (long long)B * Hkv * Tmax, hd, TA_BK, dt) ||
-      !tmap_16(&tv, V, (long long)B * Hkv * Tmax, hd, 64, dt))
+      !tmap_16(&tv, V, (long long)B * Hkv * Tmax, hd, 64, dt) ||
+      !tmap_rows3d(&to, out, B, S, (long long)Hq * hd))
     return cudaErrorInvalidValue;
   static bool attr = false;   // one flag per instantiation
   if (!attr) {
@@ -495,7 +535,7 @@ cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, 
   }
   const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   return launch_k(attn_fwd_tc_kernel<T, HD>, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B),
-                  dim3(TA_THREADS), (size_t)TaCfg<HD>::SMEM, st, tq, tk, tv, S, Hq, Hkv, Tmax,
+                  dim3(TA_THREADS), (size_t)TaCfg<HD>::SMEM, st, tq, tk, tv, to, S, Hq, Hkv, Tmax,
                   qscale_log2, out, lse, status);
 }
 

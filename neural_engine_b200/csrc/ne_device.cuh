@@ -39,6 +39,15 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// 2^x by the MUFU's approximate base-2 exponential (PTX ex2.approx.ftz.f32:
+// relative error about 2^-22, results below 2^-126 flushed to zero), one
+// instruction; the attention softmax's probabilities go to 16-bit storage.
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Raise the barrier's expected transaction bytes without an arrival (the
 // arrivals come separately, e.g. after the arriving threads' own stores).
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
@@ -114,6 +123,14 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int32_t c0,
+                                             int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
 }
 __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, uint32_t src, int32_t c0,
                                                   int32_t c1) {
