@@ -716,12 +716,15 @@ template <int HD>
 __device__ __forceinline__ void rope_stage(float2* stg, const float2* table, int pos0, int S,
                                            int c_lo, int lane) {
   constexpr int NP = HD / 4;
-#pragma unroll 4
-  for (int r = 0; r < 32; ++r) {
-    const int pos = pos0 + r;
-    if (lane < NP)
-      stg[r * NP + (lane ^ (r & 15))] =
-          pos < S ? table[(size_t)pos * (HD / 2) + c_lo / 2 + lane] : make_float2(0.f, 0.f);
+  if (lane < NP) {
+    float2 v[32];   // every row's load in flight before the first store
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const int pos = pos0 + r;
+      v[r] = pos < S ? table[(size_t)pos * (HD / 2) + c_lo / 2 + lane] : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r) stg[r * NP + (lane ^ (r & 15))] = v[r];
   }
   __syncwarp();
 }

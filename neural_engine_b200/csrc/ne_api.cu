@@ -295,7 +295,7 @@ ne_status enqueue_prefill(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, in
     const char* e = getenv("NE_PREFILL_TC");
     return !(e && e[0] == '0');
   }();
-  const bool tc_attn = tc_on && pos0 == 0 && (hd == 128 || hd == 64);
+  const bool tc_attn = tc_on && pos0 == 0 && (hd == 128 || (hd == 64 && attn_tc64()));
   const int seqs_per_chunk = std::max(1, ctx->pf_rows / S);
   for (int b0 = 0; b0 < B; b0 += seqs_per_chunk) {
     const int nb = std::min(seqs_per_chunk, B - b0);

@@ -1,5 +1,6 @@
 // ne_internal.h -- declarations shared by the library's translation units.
 #pragma once
+#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -151,6 +152,17 @@ cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_cli
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
                                 float inv_bc2, const float* norm_out, cudaStream_t st);
+// Whether head dim 64 takes the tcgen05 attention kernels (NE_ATTN_TC64=1);
+// by default it keeps the mma.sync ones, measured faster at that width (the
+// element-wise work per 128 x 128 tile is the same as at 128, the products
+// half as long).
+inline bool attn_tc64() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_ATTN_TC64");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
 // Causal GQA attention forward on the tcgen05 tensor cores (head_dim 128 or
 // 64, bf16): Q [B*S][Hq*hd], K / V [B][Hkv][Tmax][hd]; out [B*S][Hq*hd] bf16 and
 // the row log-sum-exp lse [B][Hq][S] (log2 domain).

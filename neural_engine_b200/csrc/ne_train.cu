@@ -1167,7 +1167,7 @@ NE_API ne_status ne_attn_fwd(ne_ctx* ctx, int l) {
   NE_LAUNCH(launch_qkv_post(a.QKVR, 1, 0, M, S, nullptr, 0, Hq, Hkv, hd,
                             m.qk_norm ? w.q_norm : nullptr, m.qk_norm ? w.k_norm : nullptr,
                             m.qk_eps, ctx->rope_cs, a.Q, 2, a.K, a.V, S, ctx->d_status, st, 1));
-  if ((hd == 128 || hd == 64) && attn_tc_enabled())
+  if ((hd == 128 || (hd == 64 && attn_tc64())) && attn_tc_enabled())
     NE_LAUNCH(launch_attn_fwd_tc(a.Q, a.K, a.V, B, S, Hq, Hkv, hd, S, a.O, a.LSE, ctx->d_status, st));
   else
     NE_LAUNCH(launch_prefill_attn_bf16(a.Q, a.K, a.V, B, S, 0, Hq, Hkv, hd, S, a.O, st, a.LSE));
@@ -2078,7 +2078,7 @@ extern "C" NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, con
   const auto* k = static_cast<const __nv_bfloat16*>(d_k);
   const auto* v = static_cast<const __nv_bfloat16*>(d_v);
   auto* o = static_cast<__nv_bfloat16*>(d_out);
-  if ((m.head_dim == 128 || m.head_dim == 64) && attn_tc_enabled())
+  if ((m.head_dim == 128 || (m.head_dim == 64 && attn_tc64())) && attn_tc_enabled())
     NE_LAUNCH(launch_attn_fwd_tc(q, k, v, B, S, m.n_heads, m.kv_heads, m.head_dim, S, o, d_lse,
                                  ctx->d_status, ctx->st));
   else

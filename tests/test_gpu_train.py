@@ -158,9 +158,10 @@ TC_ATTN = [dict(head_dim=128, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=
 @pytest.mark.parametrize("kw", TC_ATTN)
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 256), (4, 80), (1, 1088)])
 def test_tensor_core_attention_backward(kw, B, S):
-    """head_dim 128 and 64 take the tcgen05 attention kernels (forward, dK /
-    dV, and dQ from 1024 positions on): several 128-row query / key tiles, a
-    ragged last tile, GQA groups of 2 and 1, with and without QK-norm."""
+    """Head dim 128 takes the tcgen05 attention kernels (forward, dK / dV, and
+    dQ from 1024 positions on), head dim 64 the mma.sync ones by default:
+    several 128-row query / key tiles, a ragged last tile, GQA groups of 2 and
+    1, with and without QK-norm."""
     cfg = _cfg(**kw)
     layers, rf, emb, qk = om.init_weights(cfg, seed=71, std=0.08, bf16=True)
     layers, rf, qk = om.random_gains(cfg, layers, rf, qk)
@@ -194,21 +195,34 @@ def _child_backward(kw, B, S, env, q):
         q.put(("fail", repr(ex)))
 
 
-@pytest.mark.parametrize("kw", [TC_ATTN[0], TC_ATTN[3]])
-@pytest.mark.parametrize("env", [{"NE_ATTN_BWD_TC": "1"},
-                                 {"NE_ATTN_BWD_TC": "1", "NE_DQ_TP": "0", "NE_DKDV_TP": "0"}])
-def test_tensor_core_dq_at_short_sequences(kw, env):
-    """The tcgen05 dQ kernels (pipelined, and with NE_DQ_TP=0 / NE_DKDV_TP=0 the
-    serial ones) at 256 positions, where the default takes the mma.sync dQ:
-    run in a fresh process so the switches are read there."""
+def _in_child(kw, B, S, env):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    p = ctx.Process(target=_child_backward, args=(kw, 2, 256, env, q))
+    p = ctx.Process(target=_child_backward, args=(kw, B, S, env, q))
     p.start()
     res = q.get(timeout=300)
     p.join(timeout=60)
     assert res[0] == "ok", res[1]
+
+
+@pytest.mark.parametrize("kw", [TC_ATTN[0], TC_ATTN[3]])
+@pytest.mark.parametrize("env", [{"NE_ATTN_BWD_TC": "1", "NE_ATTN_TC64": "1"},
+                                 {"NE_ATTN_BWD_TC": "1", "NE_ATTN_TC64": "1", "NE_DQ_TP": "0",
+                                  "NE_DKDV_TP": "0"}])
+def test_tensor_core_dq_at_short_sequences(kw, env):
+    """The tcgen05 dQ kernels (pipelined, and with NE_DQ_TP=0 / NE_DKDV_TP=0 the
+    serial ones) at 256 positions, where the default takes the mma.sync dQ:
+    run in a fresh process so the switches are read there."""
+    _in_child(kw, 2, 256, env)
+
+
+@pytest.mark.parametrize("kw", [TC_ATTN[2], TC_ATTN[3]])
+@pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
+def test_head_dim_64_tensor_core_attention(kw, B, S):
+    """Head dim 64 on the tcgen05 forward, dQ and dK/dV kernels
+    (NE_ATTN_TC64=1; the default keeps the mma.sync ones there)."""
+    _in_child(kw, B, S, {"NE_ATTN_TC64": "1"})
 
 
 @pytest.mark.parametrize("name", ["stories110m", "qwen3_06b"])

@@ -208,7 +208,8 @@ def test_rmsnorm_entry_points_match_float64():
                                            (64, 4, 2, 2, 160), (64, 12, 12, 2, 256),
                                            (64, 2, 1, 1, 300), (64, 4, 2, 1, 1024)])
 def test_sdpa_forward_matches_float64(hd, Hq, Hkv, B, S):
-    """Causal GQA attention (tcgen05 kernel at head_dim 128 and 64) vs float64 softmax;
+    """Causal GQA attention (tcgen05 kernel at head_dim 128, the mma.sync one at
+    64 unless NE_ATTN_TC64=1) vs float64 softmax;
     ragged and multi-tile sequence lengths; the row LSE (log2 domain) too.
     Tolerance: bf16 output, max-abs <= 2^-7 * max|O| + 1e-3; LSE <= 1e-3."""
     import neural_engine_b200 as ne
