@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -102,6 +103,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (completion: tmem_wait_st).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
@@ -456,6 +471,333 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ------------------------------------------------------------------ two query tiles
+// A second form for GQA groups of even size: one CTA owns the same 128 query
+// rows of two q-heads that share a kv-head (tiles A and B), so every K / V
+// tile it loads serves both.  Each element-wise thread owns a whole score row
+// (no exchange between warps), P overwrites its scores in tensor memory as
+// bf16 / fp16 (the A operand of O += P V read from TMEM), and the MMA thread
+// alternates between the tiles: while tile A's warps run the softmax of key
+// tile j, the tensor cores run tile B's products, and the other way round.
+//   TMEM: S_A [0, 128), S_B [128, 256), O_A at 256, O_B at 256 + HD.
+//   warps 2-5: tile A (one per TMEM lane quarter), warps 6-9: tile B.
+template <int HD>
+struct Ta2Cfg {
+  static constexpr int NA = HD / 64;
+  static constexpr uint32_t Q_BYTES = 128 * HD * 2;         // one query tile
+  static constexpr uint32_t K_BYTES = 128 * HD * 2;
+  static constexpr uint32_t KV_BYTES = 2 * K_BYTES;         // K then V of one stage
+  static constexpr int NS = HD == 128 ? 2 : 3;              // K / V stages
+  static constexpr int SMEM = 2 * Q_BYTES + NS * KV_BYTES + 1024 + 1024;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(TA_THREADS, 1)
+attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    int S, int Hq, int Hkv, int Tmax, float qscale_log2, float* __restrict__ lse,
+                    int* status) {
+  using C = Ta2Cfg<HD>;
+  constexpr int NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base;                                 // [2] tiles A, B
+  const uint32_t sKV = sQ + 2 * C::Q_BYTES;                 // [NS] stages: K | V
+  const uint32_t bars = sKV + NS * C::KV_BYTES;
+  const uint32_t q_full = bars;
+  const uint32_t kv_full = bars + 8;      // [NS]
+  const uint32_t kv_empty = bars + 32;    // [NS]
+  const uint32_t s_full = bars + 56;      // [2] per tile
+  const uint32_t p_full = bars + 72;      // [2] per tile
+  const uint32_t o_last = bars + 88;      // [2] per tile: its last P.V product done
+  const uint32_t drain = bars + 104;
+  uint8_t* const gbars = gbase + (bars - base);
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(gbars + 112);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(gbars + 116);
+  int* const xok = reinterpret_cast<int*>(gbars + 128);     // [8] per softmax warp
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // longest-first order over (query tile, head pair, sequence)
+  const int nbh = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qt = gridDim.x - 1 - lin / nbh;
+  const int hp = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
+  const int hA = 2 * hp;
+  const int kvh = hA / (Hq / Hkv);                          // shared by hA and hA + 1
+  const int q0 = qt * TA_BQ;
+  const int n_keys = min(S, q0 + TA_BQ);
+  const int n_kt = (n_keys + TA_BK - 1) / TA_BK;
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  constexpr int FMT = kF16 ? 0 : 1;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(TA_BQ, TA_BK, FMT, 0, 0);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(TA_BQ, HD, FMT, 0, 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(kv_full + 8 * i, 1);
+      mbar_init(kv_empty + 8 * i, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + 8 * t, 1);
+      mbar_init(p_full + 8 * t, 128);
+      mbar_init(o_last + 8 * t, 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = policy_evict_last();
+      const int qrow = b * S + q0;
+      const int kvrow = (b * Hkv + kvh) * Tmax;
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int a = 0; a < C::NA; ++a)
+          tma_load_2d(sQ + t * C::Q_BYTES + a * TA_ATOM, &tmQ, q_full, (hA + t) * HD + a * 64,
+                      qrow, pol);
+      int j = 0;
+      for (; j < n_kt; ++j) {
+        const int st = j % NS;
+        if (j >= NS && !mbar_wait(kv_empty + 8 * st, ((j / NS) - 1) & 1, status, abort_flag))
+          break;
+        mbar_arrive_expect_tx(kv_full + 8 * st, C::KV_BYTES);
+        const uint32_t sk = sKV + st * C::KV_BYTES, sv = sk + C::K_BYTES;
+        const int k0 = kvrow + j * TA_BK;
+        for (int a = 0; a < C::NA; ++a)
+          tma_load_2d(sk + a * TA_ATOM, &tmK, kv_full + 8 * st, a * 64, k0, pol);
+        for (int kb = 0; kb < 2; ++kb)
+          for (int c = 0; c < C::NA; ++c)
+            tma_load_2d(sv + kb * C::NA * TA_MN_BOX + c * TA_MN_BOX, &tmV, kv_full + 8 * st,
+                        c * 64, k0 + kb * 64, pol);
+      }
+      // drain (bounded): every load issued has landed before the CTA exits
+      {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+      for (int i = (j > NS ? j - NS : 0); i < j; ++i) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full + 8 * (i % NS), (i / NS) & 1))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      auto issue_s = [&](int t, int j) {   // S_t = Q_t K_j^T
+        const uint32_t kbase = sKV + (j % NS) * C::KV_BYTES;
+        const uint32_t qbase = sQ + t * C::Q_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad = smem_desc_k_sw128(qbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          const uint64_t bd = smem_desc_k_sw128(kbase + (kk >> 2) * TA_ATOM) + 2 * (kk & 3);
+          umma_f16(tmem + 128 * t, ad, bd, IDESC_S, kk > 0);
+        }
+        umma_commit(s_full + 8 * t);
+      };
+      auto issue_pv = [&](int t, int j) {   // O_t += P_t V_j (P_t from TMEM)
+        const uint32_t vbase = sKV + (j % NS) * C::KV_BYTES + C::K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TA_BK / 16; ++kk) {
+          const uint64_t bd =
+              smem_desc_mn_sw128(vbase + (kk >> 2) * C::NA * TA_MN_BOX, TA_MN_BOX) + 128 * (kk & 3);
+          umma_f16_ts(tmem + 256 + HD * t, tmem + 128 * t + 8 * kk, bd, IDESC_O, (j | kk) != 0);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, status, abort_flag) && mbar_wait(kv_full, 0, status, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; j < n_kt && ok; ++j) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!(ok = mbar_wait(p_full + 8 * t, j & 1, status, abort_flag))) break;
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == 1) umma_commit(kv_empty + 8 * (j % NS));   // K_j / V_j read by both tiles
+          if (j + 1 < n_kt) {
+            if (t == 0) {
+              const int nst = (j + 1) % NS;
+              if (!(ok = mbar_wait(kv_full + 8 * nst, ((j + 1) / NS) & 1, status, abort_flag)))
+                break;
+              tc_fence_after();
+            }
+            issue_s(t, j + 1);
+          } else {
+            umma_commit(o_last + 8 * t);
+          }
+        }
+      }
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > 100000000ull) break;
+    }
+  } else {
+    // ------------------------------------------------ softmax / output (warps 2..9)
+    const int t = (warp - 2) >> 2;                 // tile A or B
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;           // query row within the tile = TMEM lane
+    const int qpos = q0 + row;
+    const int h = hA + t;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t srow = tmem + lane_off + 128 * t;
+    const uint32_t orow = tmem + lane_off + 256 + HD * t;
+    float m = -1e30f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      const bool ready =
+          __all_sync(0xffffffffu, mbar_wait(s_full + 8 * t, j & 1, status, abort_flag));
+      if (!ready) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool full = j < qt;                   // left of the diagonal: no mask
+      const int kbase = j * TA_BK;
+      // pass 1: the row maximum of the raw scores (scaled once; qscale > 0)
+      float m4[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(srow + 32 * c, r);
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(r[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = kbase + 32 * c + i;
+            if (key <= qpos && key < S) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(r[i]));
+          }
+        }
+      }
+      const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      const float mx = fmaxf(m, mraw > -3.0e38f ? mraw * qscale_log2 : -1e30f);
+      // lazy rescale (see attn_fwd_tc_kernel), decided per warp: O_t's last
+      // product is complete (S_t of this tile was issued after it)
+      const bool move_row = mx > m + 8.0f;
+      const bool move = __any_sync(0xffffffffu, move_row);
+      const float corr = move_row ? ex2_fast(m - mx) : 1.0f;
+      if (move_row) m = mx;
+      if (move && j > 0) {
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(orow + c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+          tmem_st32(orow + c, r);
+        }
+      }
+      // pass 2: p = exp2(s - m), 16-bit, over the scores in place (chunk c's
+      // packed words go to columns 16c .. 16c+15, all read already)
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(srow + 32 * c, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float p0 = ex2_fast(fmaf(__uint_as_float(r[i]), qscale_log2, -m));
+          float p1 = ex2_fast(fmaf(__uint_as_float(r[i + 1]), qscale_log2, -m));
+          if (!full) {
+            const int key = kbase + 32 * c + i;
+            if (!(key <= qpos && key < S)) p0 = 0.f;
+            if (!(key + 1 <= qpos && key + 1 < S)) p1 = 0.f;
+          }
+          sum0 += p0;
+          sum1 += p1;
+          if constexpr (kF16) {
+            const __half2 pk = __floats2half2_rn(p0, p1);
+            w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          } else {
+            const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
+            w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+          }
+        }
+        tmem_st16(srow + 16 * c, w);
+      }
+      l = l * corr + (sum0 + sum1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full + 8 * t);
+    }
+    // ---- output: O / l into this tile's (now free) Q buffer, one tensor
+    // store per 64 columns (rows at or past S are clipped); the row LSE
+    bool staged = false;
+    if (ok && __all_sync(0xffffffffu, mbar_wait(o_last + 8 * t, 0, status, abort_flag))) {
+      tc_fence_after();
+      pdl_wait();
+      const float inv = 1.0f / l;
+      const uint32_t stile = sQ + t * C::Q_BYTES;
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(orow + c, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const __nv_bfloat162 pk = __floats2bfloat162_rn(__uint_as_float(r[i]) * inv,
+                                                          __uint_as_float(r[i + 1]) * inv);
+          w[i >> 1] = *reinterpret_cast<const uint32_t*>(&pk);
+        }
+        const uint32_t atom = stile + (c >> 6) * TA_ATOM + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((c & 63) >> 3) + q;
+          st_shared_v4(atom + ((chunk ^ (row & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2],
+                       w[4 * q + 3]);
+        }
+      }
+      staged = true;
+      if (qpos < S && lse) lse[((size_t)b * Hq + h) * S + qpos] = m + log2f(l);
+    }
+    if (lane == 0) xok[warp - 2] = staged ? 1 : 0;
+    fence_async_smem();
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this tile's four warps
+    if (warp == 2 + 4 * t && lane == 0) {
+      bool all = true;
+      for (int i = 0; i < 4; ++i) all = all && xok[4 * t + i] != 0;
+      if (all) {
+        for (int a = 0; a < C::NA; ++a)
+          tma_store_3d(&tmO, sQ + t * C::Q_BYTES + a * TA_ATOM, h * HD + a * 64, q0, b);
+        bulk_commit_group();
+        bulk_wait_all();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -510,6 +852,16 @@ bool tmap_rows3d(CUtensorMap* tm, const void* ptr, long long B, long long S, lon
 
 namespace {
 
+// GQA groups of even size take the two-tile kernel (NE_ATTN_FWD2=0: the
+// one-tile kernel for every group size).
+bool fwd_two_tiles() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_ATTN_FWD2");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T, int HD>
 cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, int Hkv, int hd,
                       int Tmax, __nv_bfloat16* out, float* lse, int* status, cudaStream_t st) {
@@ -531,9 +883,16 @@ cudaError_t launch_tc(const T* Q, const T* K, const T* V, int B, int S, int Hq, 
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          TaCfg<HD>::SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_fwd_tc2_kernel<T, HD>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Ta2Cfg<HD>::SMEM);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   const float qscale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  if ((Hq / Hkv) % 2 == 0 && fwd_two_tiles())
+    return launch_k(attn_fwd_tc2_kernel<T, HD>, dim3((S + TA_BQ - 1) / TA_BQ, Hq / 2, B),
+                    dim3(TA_THREADS), (size_t)Ta2Cfg<HD>::SMEM, st, tq, tk, tv, to, S, Hq, Hkv,
+                    Tmax, qscale_log2, lse, status);
   return launch_k(attn_fwd_tc_kernel<T, HD>, dim3((S + TA_BQ - 1) / TA_BQ, Hq, B),
                   dim3(TA_THREADS), (size_t)TaCfg<HD>::SMEM, st, tq, tk, tv, to, S, Hq, Hkv, Tmax,
                   qscale_log2, out, lse, status);

@@ -217,6 +217,13 @@ def test_tensor_core_dq_at_short_sequences(kw, env):
     _in_child(kw, 2, 256, env)
 
 
+@pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
+def test_one_tile_forward_kernel_for_even_groups(B, S):
+    """GQA groups of 2 take the two-tile forward by default; NE_ATTN_FWD2=0
+    runs the one-tile kernel for them too."""
+    _in_child(TC_ATTN[0], B, S, {"NE_ATTN_FWD2": "0"})
+
+
 @pytest.mark.parametrize("kw", [TC_ATTN[2], TC_ATTN[3]])
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
 def test_head_dim_64_tensor_core_attention(kw, B, S):
