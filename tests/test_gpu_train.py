@@ -217,6 +217,52 @@ def test_tensor_core_dq_at_short_sequences(kw, env):
     _in_child(kw, 2, 256, env)
 
 
+def _child_steps(kw, B, S, env, n_steps, q):
+    import os
+    for k, v in env.items():
+        os.environ[k] = v
+    try:
+        cfg = _cfg(**kw)
+        layers, rf, emb, qk = om.init_weights(cfg, seed=81, std=0.08, bf16=True)
+        e = _engine(cfg, layers, rf, emb, qk, B, S)
+        losses = []
+        for i in range(n_steps):
+            tok = om.prompt_tokens(cfg.vocab, S + 1, 90 + i, batch=B)
+            losses.append(e.train_fwd_bwd(tok))
+            e.adamw_step(i + 1, 1e-3, return_norm=False)
+        tok = om.prompt_tokens(cfg.vocab, S + 1, 99, batch=B)
+        losses.append(e.train_fwd_bwd(tok))
+        q.put(("ok", losses, e.get_masters(), e.get_grads()))
+        e.close()
+    except BaseException as ex:
+        q.put(("fail", repr(ex), None, None))
+
+
+def test_overlapped_optimizer_step_is_exact():
+    """NE_ADAM_OVERLAP=1: AdamW runs bucket by bucket on its own stream beside
+    the next micro-step's forward (eager, then graph-replayed micro-steps).  The
+    arithmetic is the same, so the losses, masters and the next gradients must
+    equal the serial run's bit for bit."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = []
+    for env in ({}, {"NE_ADAM_OVERLAP": "1"}):
+        q = ctx.Queue()
+        p = ctx.Process(target=_child_steps, args=(TC_ATTN[0], 2, 128, env, 4, q))
+        p.start()
+        out.append(q.get(timeout=300))
+        p.join(timeout=60)
+    for r in out:
+        assert r[0] == "ok", r[1]
+    assert out[0][1] == out[1][1], (out[0][1], out[1][1])
+    for part in (2, 3):
+        a, b = out[0][part], out[1][part]
+        for L in range(len(a["layers"])):
+            for k in a["layers"][L]:
+                assert np.array_equal(a["layers"][L][k], b["layers"][L][k]), (part, L, k)
+        assert np.array_equal(a["embed"], b["embed"]), part
+
+
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
 def test_one_tile_forward_kernel_for_even_groups(B, S):
     """GQA groups of 2 take the two-tile forward by default; NE_ATTN_FWD2=0
