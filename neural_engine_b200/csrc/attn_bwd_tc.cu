@@ -35,6 +35,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "ne_device.cuh"
 #include "ne_internal.h"
@@ -932,26 +933,44 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const int h_lo = half * CW;         // head columns of the D sum and the epilogue
     float* const pxch = xch;
     pdl_wait();   // O, dO and LSE come from earlier kernels
-    float dsum = 0.f;
-    if (qv) {
-      const size_t off = ((size_t)(b * S + q) * Hq + h) * HD + h_lo;
+    {
+      // D = rowsum(dO * O): each warp of the pair takes 16 of the quarter's
+      // 32 rows, a whole row per pass (every lane HD / 32 contiguous columns,
+      // so the loads are coalesced), all 32 loads in flight before the sums
+      constexpr int EPL = HD / 32;
+      using V = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
+      const int r0 = quarter * 32 + half * 16;
+      V ov[16], gv[16];
 #pragma unroll
-      for (int i = 0; i < CW; i += 8) {
-        const uint4 ov = *reinterpret_cast<const uint4*>(O + off + i);
-        const uint4 gv = *reinterpret_cast<const uint4*>(dO + off + i);
-        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
-        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
-          dsum += of.x * gf.x + of.y * gf.y;
+      for (int k = 0; k < 16; ++k) {
+        const int qq = q0 + r0 + k;
+        if (qq < S) {
+          const size_t off = ((size_t)(b * S + qq) * Hq + h) * HD + lane * EPL;
+          ov[k] = *reinterpret_cast<const V*>(O + off);
+          gv[k] = *reinterpret_cast<const V*>(dO + off);
+        } else {
+          ov[k] = V{};
+          gv[k] = V{};
         }
       }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[k]);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[k]);
+        float d = 0.f;
+#pragma unroll
+        for (int t = 0; t < EPL / 2; ++t) {
+          const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
+          d += of.x * gf.x + of.y * gf.y;
+        }
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
+        if (lane == 0) pxch[r0 + k] = d;
+      }
     }
-    pxch[half * 128 + row] = dsum;
     named_bar(1 + quarter, 64);
-    const float Drow = dsum + pxch[(half ^ 1) * 128 + row];
-    named_bar(1 + quarter, 64);
+    const float Drow = pxch[row];
+    named_bar(1 + quarter, 64);   // the exchange area is reusable
     if (half == 0 && qv) Dl[((size_t)b * Hq + h) * S + q] = Drow;
     const float Lrow = qv ? LSE[((size_t)b * Hq + h) * S + q] : 0.f;
 

@@ -122,21 +122,8 @@ __global__ void resid_rmsnorm_kernel(float* __restrict__ x, const float* __restr
 template <int V4>
 __global__ void __launch_bounds__(256)
 rmsnorm_rows_kernel(const float* __restrict__ x, int rows, const float* __restrict__ g,
-                    float eps, __nv_bfloat16* __restrict__ xn, float* __restrict__ copy,
-                    const char* __restrict__ pf, unsigned long long pf_bytes) {
+                    float eps, __nv_bfloat16* __restrict__ xn, float* __restrict__ copy) {
   pdl_trigger();
-  if (pf != nullptr) {
-    // this thread's share of the range, in 16-byte multiples
-    const unsigned long long nt = (unsigned long long)gridDim.x * blockDim.x;
-    const unsigned long long t = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const unsigned long long per = ((pf_bytes + nt - 1) / nt + 15) & ~15ull;
-    const unsigned long long off = t * per;
-    if (off < pf_bytes) {
-      const unsigned long long n = pf_bytes - off < per ? pf_bytes - off : per;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf + off), "r"((unsigned)n)
-                   : "memory");
-    }
-  }
   pdl_wait();
   constexpr int D = V4 * 128;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -388,25 +375,20 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
 
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
-                                 int rows, cudaStream_t st, float* copy, const void* pf,
-                                 size_t pf_bytes) {
-  // the prefetch range: 16-byte aligned start, whole 16-byte units
-  const char* pfc = static_cast<const char*>(pf);
-  if (pfc && ((reinterpret_cast<uintptr_t>(pfc) & 15) || pf_bytes < 16)) pfc = nullptr;
-  const unsigned long long pfn = pfc ? (unsigned long long)(pf_bytes & ~(size_t)15) : 0ull;
+                                 int rows, cudaStream_t st, float* copy) {
   if (nsplit == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(copy) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(g) & 15) == 0 && (reinterpret_cast<uintptr_t>(xn) & 7) == 0) {
     const dim3 grid((rows + 7) / 8);
     switch (D) {
       case 512: return launch_k(rmsnorm_rows_kernel<4>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
-                          copy, pfc, pfn);
+                          copy);
       case 768: return launch_k(rmsnorm_rows_kernel<6>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
-                          copy, pfc, pfn);
+                          copy);
       case 1024: return launch_k(rmsnorm_rows_kernel<8>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
-                          copy, pfc, pfn);
+                          copy);
       case 2048: return launch_k(rmsnorm_rows_kernel<16>, grid, dim3(256), 0, st, x, rows, g, eps, xn,
-                          copy, pfc, pfn);
+                          copy);
       default: break;
     }
   }

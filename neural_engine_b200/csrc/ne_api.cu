@@ -83,16 +83,6 @@ ne_status gemm_decode(ne_ctx* ctx, const __nv_bfloat16* W, int n_out, int K,
 // (EPI_SWIGLU_T) when its tiles fill the SMs without splitting K (B > 128 on
 // 148 SMs): no fp32 h1/h3 sums in HBM and no separate SwiGLU kernel.
 // NE_DECODE_SWIGLU=0 keeps the split projection + swiglu_split pair.
-// Decode step (NE_DECODE_PREFETCH=1): the norm kernels ask L2 for the weights
-// of the products that follow them.
-static bool decode_prefetch() {
-  static const bool on = [] {
-    const char* e = std::getenv("NE_DECODE_PREFETCH");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 bool decode_swiglu_fused(ne_ctx* ctx, int rows) {
   static const bool on = [] {
     const char* e = std::getenv("NE_DECODE_SWIGLU");
@@ -218,11 +208,8 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
     if ((s = gemm_decode(ctx, w.wo, D, q_dim, ctx->attn, q_dim, B, ctx->x, m.res_alpha)) != NE_OK)
       return s;
     prof_mark(ctx, 3);
-    // (NE_DECODE_PREFETCH) the FFN weights, W1/W3 then W2 (contiguous), asked
-    // into L2 while the norm waits for the Wo product
     NE_LAUNCH(launch_resid_rmsnorm(ctx->x, nullptr, 0, 0, 1.f, D, w.rms_ffn, m.rms_eps, ctx->xn, B,
-                                   ctx->st, nullptr, decode_prefetch() ? w.w13 : nullptr,
-                                   (size_t)3 * F * D * 2));
+                                   ctx->st));
     prof_mark(ctx, 4);
     if (swiglu_fused) {
       if ((s = gemm_decode_swiglu(ctx, w.w13, ctx->xn, D, B, ctx->gate)) != NE_OK) return s;
@@ -237,9 +224,8 @@ ne_status enqueue_decode_step(ne_ctx* ctx, int B, int32_t* d_out_tokens, bool ke
     if ((s = gemm_decode(ctx, w.w2, D, F, ctx->gate, F, B, ctx->x, m.res_alpha)) != NE_OK) return s;
     prof_mark(ctx, 7);
     const float* next_g = (l + 1 < m.n_layers) ? ctx->L[l + 1].rms_att : ctx->rms_final;
-    const void* next_w = decode_prefetch() && l + 1 < m.n_layers ? ctx->L[l + 1].wqkv : nullptr;
     NE_LAUNCH(launch_resid_rmsnorm(ctx->x, nullptr, 0, 0, 1.f, D, next_g, m.rms_eps, ctx->xn, B,
-                                   ctx->st, nullptr, next_w, (size_t)qkv_dim * D * 2));
+                                   ctx->st));
     prof_mark(ctx, 4);
   }
   if (keep_logits) {

@@ -81,13 +81,9 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tok, const void* table, int tabl
                                  int* status, cudaStream_t st);
 // x[r] += alpha * sum of nsplit slabs (nsplit may be 0); xn = rmsnorm(x) (bf16);
 // copy (optional) receives the resulting x, e.g. to seed the next residual sum.
-// pf / pf_bytes (optional, norm-only form): a read-only range (the weights of
-// the products that follow) the kernel asks L2 to fetch, before it waits for
-// its predecessor.
 cudaError_t launch_resid_rmsnorm(float* x, const float* P, int nsplit, long long split_stride,
                                  float alpha, int D, const float* g, float eps, __nv_bfloat16* xn,
-                                 int rows, cudaStream_t st, float* copy = nullptr,
-                                 const void* pf = nullptr, size_t pf_bytes = 0);
+                                 int rows, cudaStream_t st, float* copy = nullptr);
 // q_type: 0 = fp32 q, 1 = fp16 q (with fp16 K/V); kv_bf16: q, K and V all bf16
 // (training path).
 cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride, int rows,
