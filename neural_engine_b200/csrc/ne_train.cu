@@ -184,6 +184,9 @@ void train_opt_fence(ne_ctx* ctx) {
   TrainState* t = ctx->train;
   if (t->opt_st && t->opt_pending) {
     cudaStreamWaitEvent(ctx->st, t->opt_done, 0);
+    // host readers and writers of the state use synchronous copies (the
+    // legacy stream, which does not order against the library's streams)
+    cudaEventSynchronize(t->opt_done);
     t->opt_pending = false;
   }
 }
@@ -1491,6 +1494,7 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   }
   t->micro_steps++;
   t->steps_run++;
+  t->opt_pending = false;   // the step's backward waited for any overlapped optimizer step
   return NE_OK;
 }
 
