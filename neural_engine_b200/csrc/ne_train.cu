@@ -670,7 +670,7 @@ static void bucket_segs(const TrainState* t, int b, int* s0, int* s1) {
 // after each layer.  The sum's order then varies between runs (the adds
 // land in arrival order).  Off by default: at 2 ranks the step measured
 // slower than the rank-ordered reduce-scatter kernels, which stay the
-// default (reproducible sums).
+// default.
 static bool px_fused_dw() {
   static const bool on = [] {
     const char* e = std::getenv("NE_PX_FUSED_DW");

@@ -238,15 +238,19 @@ def _child_steps(kw, B, S, env, n_steps, q):
         q.put(("fail", repr(ex), None, None))
 
 
-def test_overlapped_optimizer_step_is_exact():
+def test_overlapped_optimizer_step_matches_serial():
     """NE_ADAM_OVERLAP=1: AdamW runs bucket by bucket on its own stream beside
     the next micro-step's forward (eager, then graph-replayed micro-steps).  The
-    arithmetic is the same, so the losses, masters and the next gradients must
-    equal the serial run's bit for bit."""
+    arithmetic is the same, but the split-K dW products add their partial sums
+    in arrival order, so two serial runs already differ in the last bits after
+    a few steps.  The overlapped run must stay as close to a serial run as a
+    second serial run does (within 4x, plus 1e-5): a forward that read a bucket
+    before its update, or a backward that accumulated into gradients not yet
+    cleared, moves it far outside that."""
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     out = []
-    for env in ({}, {"NE_ADAM_OVERLAP": "1"}):
+    for env in ({}, {}, {"NE_ADAM_OVERLAP": "1"}):
         q = ctx.Queue()
         p = ctx.Process(target=_child_steps, args=(TC_ATTN[0], 2, 128, env, 4, q))
         p.start()
@@ -254,13 +258,20 @@ def test_overlapped_optimizer_step_is_exact():
         p.join(timeout=60)
     for r in out:
         assert r[0] == "ok", r[1]
-    assert out[0][1] == out[1][1], (out[0][1], out[1][1])
-    for part in (2, 3):
-        a, b = out[0][part], out[1][part]
-        for L in range(len(a["layers"])):
-            for k in a["layers"][L]:
-                assert np.array_equal(a["layers"][L][k], b["layers"][L][k]), (part, L, k)
-        assert np.array_equal(a["embed"], b["embed"]), part
+    ref, again, ov = out
+
+    def near(name, x_ref, x_again, x_ov):
+        d_again = _rel(x_again, x_ref)
+        d_ov = _rel(x_ov, x_ref)
+        assert d_ov <= 4 * d_again + 1e-5, (name, d_ov, d_again)
+
+    near("losses", ref[1], again[1], ov[1])
+    for part, what in ((2, "masters"), (3, "gradients")):
+        for L in range(len(ref[part]["layers"])):
+            for k in ref[part]["layers"][L]:
+                near((what, L, k), ref[part]["layers"][L][k], again[part]["layers"][L][k],
+                     ov[part]["layers"][L][k])
+        near((what, "embed"), ref[part]["embed"], again[part]["embed"], ov[part]["embed"])
 
 
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
