@@ -329,7 +329,7 @@ __global__ void norm_finish_kernel(float* norm_out, float grad_scale, float grad
 __global__ void __launch_bounds__(256)
 adamw_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict__ chunks,
                     float lr, float b1, float b2, float eps, float inv_bc1, float inv_bc2,
-                    const float* __restrict__ norm_out, int zero_grads) {
+                    const float* __restrict__ norm_out) {
   pdl_trigger();
   pdl_wait();
   const OptChunk c = chunks[blockIdx.x];
@@ -351,7 +351,6 @@ adamw_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict
     for (int i = threadIdx.x; i < (n >> 2); i += 256) {
       float4 wv = w4[i], mv = m4[i], vv = v4[i];
       const float4 gv = g4[i];
-      if (zero_grads) const_cast<float4*>(g4)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       a.step(wv.x, gv.x, mv.x, vv.x);
       a.step(wv.y, gv.y, mv.y, vv.y);
       a.step(wv.z, gv.z, mv.z, vv.z);
@@ -372,7 +371,6 @@ adamw_chunks_kernel(const AdamSeg* __restrict__ segs, const OptChunk* __restrict
   for (int i = i0 + threadIdx.x; i < n; i += 256) {
     float wi = w[i], mi = m[i], vi = v[i];
     a.step(wi, g[i], mi, vi);
-    if (zero_grads) const_cast<float*>(g)[i] = 0.f;
     w[i] = wi;
     m[i] = mi;
     v[i] = vi;
@@ -475,10 +473,9 @@ cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_cli
 
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
-                                float inv_bc2, const float* norm_out, cudaStream_t st,
-                                int zero_grads) {
+                                float inv_bc2, const float* norm_out, cudaStream_t st) {
   return launch_k(adamw_chunks_kernel, dim3(nchunks), dim3(256), 0, st, segs, chunks, lr, b1, b2,
-                  eps, inv_bc1, inv_bc2, norm_out, zero_grads);
+                  eps, inv_bc1, inv_bc2, norm_out);
 }
 
 // ------------------------------------------------------------ value ranges

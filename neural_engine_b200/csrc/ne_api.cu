@@ -483,7 +483,6 @@ NE_API void ne_free(ne_ctx* ctx) {
 
 NE_API ne_status ne_sync(ne_ctx* ctx) {
   if (!ctx) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   if (ctx->comm && ctx->comm->world > 1) {
     // bounded: a gradient exchange that cannot finish aborts the communicator
     ne_status s = comm_sync(ctx);
@@ -510,7 +509,6 @@ NE_API ne_status ne_set_layer_weights(ne_ctx* ctx, int layer, const float* wq, c
                                       const float* rms_ffn, const float* q_norm,
                                       const float* k_norm) {
   if (!ctx) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   const ne_model_cfg& m = ctx->cfg;
   if (layer < 0 || layer >= m.n_layers || !wq || !wk || !wv || !wo || !w1 || !w2 || !w3 ||
       !rms_att || !rms_ffn)
@@ -551,7 +549,6 @@ NE_API ne_status ne_set_layer_weights(ne_ctx* ctx, int layer, const float* wq, c
 
 NE_API ne_status ne_set_global_weights(ne_ctx* ctx, const float* rms_final, const float* embed) {
   if (!ctx || !rms_final || !embed) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   const ne_model_cfg& m = ctx->cfg;
   NE_CUDA(cudaSetDevice(ctx->device));
   NE_CUDA(cudaMemcpy(ctx->rms_final, rms_final, (size_t)m.dim * 4, cudaMemcpyHostToDevice));
@@ -652,7 +649,6 @@ NE_API ne_status ne_kv_reset(ne_ctx* ctx) {
 NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, int S, int pos0,
                                    int32_t* d_next) {
   if (!ctx || !d_tokens || !d_next || B <= 0 || S <= 0 || pos0 < 0) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_FAULT_POINT(ctx, "ne_prefill_device");
   if (!ready(ctx)) return fail(ctx, NE_ERR_STATE, "weights not set");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
@@ -665,7 +661,6 @@ NE_API ne_status ne_prefill_device(ne_ctx* ctx, const int32_t* d_tokens, int B, 
 NE_API ne_status ne_prefill(ne_ctx* ctx, const int32_t* h_tokens, int B, int S, int pos0,
                             int32_t* h_next, float* h_logits) {
   if (!ctx || !h_tokens) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_FAULT_POINT(ctx, "ne_prefill");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B <= 0 || S <= 0 || B > ctx->max_batch || pos0 < 0 || pos0 + S > ctx->max_seq)
@@ -691,7 +686,6 @@ ne_status decode_loop(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0, int n_
 
 NE_API ne_status ne_decode_loop_device(ne_ctx* ctx, const int32_t* d_tok, int B, int pos0,
                                        int n_steps, int32_t* d_out) {
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   return decode_loop(ctx, d_tok, B, pos0, n_steps, d_out, false);
 }
 
@@ -770,7 +764,6 @@ NE_API ne_status ne_profile_decode_step(ne_ctx* ctx, int B, int pos, float* h_ms
   if (!ctx || !h_ms || B <= 0) return NE_ERR_INVALID;
   if (!ready(ctx)) return fail(ctx, NE_ERR_STATE, "weights not set");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   if (B > ctx->max_batch || pos < 0 || pos >= ctx->max_seq)
     return fail(ctx, NE_ERR_INVALID, "batch or position exceeds the allocated KV cache");
   NE_CUDA(cudaSetDevice(ctx->device));
@@ -830,7 +823,6 @@ NE_API int ne_decode_kernels_per_step(const ne_ctx* ctx, int B) {
 NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int pos, int32_t* h_next,
                                 float* h_logits) {
   if (!ctx || !h_tok) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_FAULT_POINT(ctx, "ne_decode_step");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B <= 0 || B > ctx->max_batch || pos < 0 || pos >= ctx->max_seq)
@@ -852,7 +844,6 @@ NE_API ne_status ne_decode_step(ne_ctx* ctx, const int32_t* h_tok, int B, int po
 NE_API ne_status ne_generate(ne_ctx* ctx, const int32_t* h_prompt, int B, int P, int n_new,
                              int32_t* h_out) {
   if (!ctx || !h_prompt || !h_out || B <= 0 || P <= 0 || n_new <= 0) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_FAULT_POINT(ctx, "ne_generate");
   if (!ctx->kcache) return fail(ctx, NE_ERR_STATE, "ne_kv_alloc not called");
   if (B > ctx->max_batch || P + n_new - 1 > ctx->max_seq)

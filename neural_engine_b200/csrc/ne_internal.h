@@ -6,8 +6,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-struct ne_ctx;
-
 namespace ne {
 
 // ------------------------------------------------------------------ GEMM
@@ -151,14 +149,9 @@ cudaError_t launch_sumsq_chunks(const AdamSeg* segs, const OptChunk* chunks, int
                                 float grad_clip, float* norm_out, cudaStream_t st,
                                 int partial_only = 0);
 cudaError_t launch_norm_finish(float* norm_out, float grad_scale, float grad_clip, cudaStream_t st);
-// zero_grads: each chunk's gradients are cleared after they are read.
 cudaError_t launch_adamw_chunks(const AdamSeg* segs, const OptChunk* chunks, int nchunks,
                                 float lr, float b1, float b2, float eps, float inv_bc1,
-                                float inv_bc2, const float* norm_out, cudaStream_t st,
-                                int zero_grads = 0);
-// The training state's overlapped optimizer step (if one is pending) is
-// complete before the work enqueued next on the context's stream.
-void train_opt_fence(ne_ctx* ctx);
+                                float inv_bc2, const float* norm_out, cudaStream_t st);
 // Whether head dim 64 takes the tcgen05 attention kernels (NE_ATTN_TC64=1);
 // by default it keeps the mma.sync ones, measured faster at that width (the
 // element-wise work per 128 x 128 tile is the same as at 128, the products

@@ -113,16 +113,6 @@ struct TrainState {
   uint8_t* h_stage = nullptr;
   size_t h_stage_tok = 0;                // bytes of the token part
   float* range_out = nullptr;            // ne_train_value_ranges: [4]
-  // the optimizer step overlapped with the next micro-step's forward
-  // (NE_ADAM_OVERLAP, replicated optimizer state): the norm on the compute
-  // stream, then AdamW bucket by bucket on opt_st, each forward layer waiting
-  // for its bucket's event, the backward for all of them
-  cudaStream_t opt_st = nullptr;
-  std::vector<cudaEvent_t> opt_ev;       // per bucket (0 = tail, 1 + layer)
-  cudaEvent_t opt_norm_ev = nullptr, opt_done = nullptr;
-  bool opt_pending = false;              // opt_done not yet waited by the compute stream
-  std::vector<int> seg_chunk0;           // first optimizer chunk of each segment (+ the end)
-  bool in_forward = false;               // the forward part of a micro-step is being enqueued
 };
 
 // Drops the captured training step (it may hold NCCL calls of a communicator
@@ -159,14 +149,6 @@ void free_train(ne_ctx* ctx) {
   for (void* p : {(void*)t->d_c2f, (void*)t->d_f2c, (void*)t->Ec, (void*)t->dEc})
     if (p) cudaFree(p);
   if (t->opt_partial) cudaFree(t->opt_partial);
-  if (t->opt_st) {
-    cudaStreamSynchronize(t->opt_st);
-    cudaStreamDestroy(t->opt_st);
-  }
-  for (cudaEvent_t e : t->opt_ev)
-    if (e) cudaEventDestroy(e);
-  if (t->opt_norm_ev) cudaEventDestroy(t->opt_norm_ev);
-  if (t->opt_done) cudaEventDestroy(t->opt_done);
   for (cudaEvent_t e : t->phase_ev)
     if (e) cudaEventDestroy(e);
   if (t->range_out) cudaFree(t->range_out);
@@ -177,18 +159,6 @@ void free_train(ne_ctx* ctx) {
   if (t->act_pool) cudaFree(t->act_pool);
   delete t;
   ctx->train = nullptr;
-}
-
-void train_opt_fence(ne_ctx* ctx) {
-  if (!ctx || !ctx->train) return;
-  TrainState* t = ctx->train;
-  if (t->opt_st && t->opt_pending) {
-    cudaStreamWaitEvent(ctx->st, t->opt_done, 0);
-    // host readers and writers of the state use synchronous copies (the
-    // legacy stream, which does not order against the library's streams)
-    cudaEventSynchronize(t->opt_done);
-    t->opt_pending = false;
-  }
 }
 
 }  // namespace ne
@@ -496,7 +466,6 @@ NE_API ne_status ne_train_set_masters(ne_ctx* ctx, int layer, const float* h_wq,
                                       const float* h_wv, const float* h_wo, const float* h_w1,
                                       const float* h_w2, const float* h_w3) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   const ne_model_cfg& m = ctx->cfg;
   TrainState* t = ctx->train;
   if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
@@ -526,7 +495,6 @@ NE_API ne_status ne_train_set_masters(ne_ctx* ctx, int layer, const float* h_wq,
 // Refresh every bf16 compute copy from the fp32 masters.
 NE_API ne_status ne_train_sync_weights(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   if (ctx->comm && ctx->comm->cs) {   // after any weight all-gather still in flight
     ne_status s = comm_fence_out(ctx);
     if (s != NE_OK) return s;
@@ -568,7 +536,6 @@ NE_API ne_status ne_gemm_dw_owned(ne_ctx* ctx, const void* d_A, long long lda, i
 
 NE_API ne_status ne_train_zero_grads(ne_ctx* ctx) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   TrainState* t = ctx->train;
   if (ctx->comm && ctx->comm->px && ctx->comm->pxs.ready && ctx->comm->pxs.fused) {
     // fused dW exchange: this rank's owned parts of the layer matrices take
@@ -936,56 +903,10 @@ static int px_ctas() {
   return n;
 }
 
-// The compute stream waits for event e (inside a capture as an external-event
-// node: each replay waits for the event's latest record).
-static ne_status stream_wait(ne_ctx* ctx, cudaEvent_t e) {
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  NE_CUDA(cudaStreamIsCapturing(ctx->st, &cs));
-  NE_CUDA(cudaStreamWaitEvent(ctx->st, e, cs == cudaStreamCaptureStatusNone ? 0u : cudaEventWaitExternal));
-  return NE_OK;
-}
-
-// Optimizer step overlapped with the next micro-step's forward
-// (NE_ADAM_OVERLAP=1, replicated optimizer state only): the gradient norm on
-// the compute stream, then AdamW bucket by bucket (tail, layer 0, 1, ...) on a
-// low-priority stream, each clearing its gradients as it reads them; the
-// forward waits for each bucket's event before the layer that reads it, the
-// backward for the whole step.
-static bool opt_overlap(const ne_ctx* ctx) {
-  static const bool on = [] {
-    const char* e = std::getenv("NE_ADAM_OVERLAP");
-    return e && e[0] == '1';
-  }();
-  return on && !shard_mode(ctx);
-}
-
-static ne_status opt_setup(ne_ctx* ctx) {
-  TrainState* t = ctx->train;
-  if (t->opt_st) return NE_OK;
-  int least = 0, greatest = 0;
-  NE_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
-  NE_CUDA(cudaStreamCreateWithPriority(&t->opt_st, cudaStreamNonBlocking, least));
-  t->opt_ev.assign(ctx->cfg.n_layers + 1, nullptr);
-  for (cudaEvent_t& e : t->opt_ev) NE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-  NE_CUDA(cudaEventCreateWithFlags(&t->opt_norm_ev, cudaEventDisableTiming));
-  NE_CUDA(cudaEventCreateWithFlags(&t->opt_done, cudaEventDisableTiming));
-  // micro-steps captured before this do not wait for the buckets: capture again
-  for (cudaGraphExec_t& g : t->step_graphs) {
-    if (g) cudaGraphExecDestroy(g);
-    g = nullptr;
-  }
-  return NE_OK;
-}
-
 // The compute stream waits for bucket b's weight all-gather of the last
 // optimizer step (a no-op when there was none).  Inside a capture the wait is
 // an external-event node: each replay waits for the event's latest record.
 static ne_status px_weights_ready(ne_ctx* ctx, int b) {
-  TrainState* t = ctx->train;
-  if (t && t->opt_st && b >= 0 && b < (int)t->opt_ev.size()) {   // the bucket's AdamW
-    ne_status s = stream_wait(ctx, t->opt_ev[b]);
-    if (s != NE_OK) return s;
-  }
   if (!ctx->comm || !ctx->comm->shard || !ctx->comm->px || !ctx->comm->pxs.ready) return NE_OK;
   const PxState& x = ctx->comm->pxs;
   if (b < 0 || b >= (int)x.ag_ev.size()) return NE_OK;
@@ -1294,10 +1215,6 @@ NE_API ne_status ne_ffn_fwd(ne_ctx* ctx, int l) {
 // d_loss (device, optional) receives the batch's mean loss.
 NE_API ne_status ne_lmhead_ce_fwd_bwd(ne_ctx* ctx, float* d_loss) {
   NE_TRAIN_PRELUDE();
-  if (t->opt_st) {   // the backward writes gradients the overlapped AdamW clears
-    if ((s = stream_wait(ctx, t->opt_done)) != NE_OK) return s;
-    t->opt_pending = false;
-  }
   const float ce_scale = 1.0f / (float)M;
   // classifier rows: the whole tied embedding, or its compacted rows
   const bool cmp = t->CV > 0;
@@ -1494,7 +1411,6 @@ NE_API ne_status ne_train_fwd_bwd_device(ne_ctx* ctx, const int32_t* d_tokens, f
   }
   t->micro_steps++;
   t->steps_run++;
-  t->opt_pending = false;   // the step's backward waited for any overlapped optimizer step
   return NE_OK;
 }
 
@@ -1618,7 +1534,6 @@ NE_API ne_status ne_train_fwd_bwd_timed(ne_ctx* ctx, const int32_t* h_tokens, fl
 // output: h_out = {x_min, x_max, dy_min, dy_max} (train.m:771-776).
 NE_API ne_status ne_train_value_ranges(ne_ctx* ctx, float* h_out) {
   if (!ctx || !ctx->train || !h_out) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   TrainState* t = ctx->train;
   NE_CUDA(cudaSetDevice(ctx->device));
   if (!t->range_out) {
@@ -1637,7 +1552,6 @@ NE_API ne_status ne_train_value_ranges(ne_ctx* ctx, float* h_out) {
 // comm stream, ordered after and before the compute stream's work.
 NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx) {
   if (!ctx || !ctx->train || !ctx->comm) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   if (ctx->comm->world == 1) return NE_OK;
   NE_CUDA(cudaSetDevice(ctx->device));
   ne_status s;
@@ -1648,7 +1562,6 @@ NE_API ne_status ne_grad_allreduce_async(ne_ctx* ctx) {
 
 NE_API ne_status ne_train_grad_pool(ne_ctx* ctx, float** d_grads, size_t* n_floats) {
   if (!ctx || !ctx->train || !d_grads || !n_floats) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   *d_grads = ctx->train->grad_pool;
   *n_floats = ctx->train->grad_floats;
   return NE_OK;
@@ -1664,9 +1577,7 @@ static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
     const bool sharded = shard_mode(ctx);
     const bool count_replicated = !sharded || ctx->comm->rank == 0;
     std::vector<OptChunk> hc;
-    t->seg_chunk0.assign(t->segs.size() + 1, 0);
     for (size_t k = 0; k < t->segs.size(); ++k) {
-      t->seg_chunk0[k] = (int)hc.size();
       const Seg& sg = t->segs[k];
       const bool own = seg_sharded(ctx, sg);
       const long long b0 = own ? shard_off(ctx, sg) : 0;
@@ -1679,7 +1590,6 @@ static ne_status upload_segs(ne_ctx* ctx, float weight_decay) {
         hc.push_back({(int)k, vec, off, (int)std::min<long long>(OPT_CHUNK, b1 - off), norm});
     }
     t->nchunks = (int)hc.size();
-    t->seg_chunk0[t->segs.size()] = t->nchunks;
     ne_status s;
     if ((s = dalloc(ctx, &t->d_chunks, hc.size())) != NE_OK ||
         (s = dalloc(ctx, &t->opt_partial, hc.size())) != NE_OK ||
@@ -1729,7 +1639,6 @@ static ne_status enqueue_norm(ne_ctx* ctx, float grad_scale, float grad_clip) {
 
 NE_API ne_status ne_train_grad_norm(ne_ctx* ctx, float grad_scale, float* h_norm) {
   if (!ctx || !ctx->train || !h_norm) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   TrainState* t = ctx->train;
   ne_status s = upload_segs(ctx, t->d_segs ? t->d_segs_wd : 0.f);
   if (s != NE_OK) return s;
@@ -1750,37 +1659,11 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
   if (!ctx || !ctx->train || !cfg || t_step <= 0) return NE_ERR_INVALID;
   NE_FAULT_POINT(ctx, "ne_adamw_step");
   TrainState* t = ctx->train;
-  train_opt_fence(ctx);
   ne_status s = upload_segs(ctx, cfg->weight_decay);
   if (s != NE_OK) return s;
   const float bc1 = 1.0f - std::pow(cfg->beta1, (float)t_step);
   const float bc2 = 1.0f - std::pow(cfg->beta2, (float)t_step);
   if ((s = enqueue_norm(ctx, cfg->grad_scale, cfg->grad_clip)) != NE_OK) return s;
-  if (opt_overlap(ctx)) {
-    if ((s = opt_setup(ctx)) != NE_OK) return s;
-    NE_CUDA(cudaEventRecord(t->opt_norm_ev, ctx->st));
-    NE_CUDA(cudaStreamWaitEvent(t->opt_st, t->opt_norm_ev, 0));
-    const int L = ctx->cfg.n_layers;
-    for (int b = 0; b <= L; ++b) {   // in the order the next forward reads them
-      int s0, s1;
-      bucket_segs(t, b, &s0, &s1);
-      const int c0 = t->seg_chunk0[s0], c1 = t->seg_chunk0[s1];
-      if (c1 > c0)
-        NE_LAUNCH(launch_adamw_chunks(t->d_segs, t->d_chunks + c0, c1 - c0, cfg->lr, cfg->beta1,
-                                      cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, t->norm_out,
-                                      t->opt_st, 1));
-      NE_CUDA(cudaEventRecord(t->opt_ev[b], t->opt_st));
-    }
-    NE_CUDA(cudaEventRecord(t->opt_done, t->opt_st));
-    t->opt_pending = true;
-    t->micro_steps = 0;   // the gradients are cleared by the update itself
-    if (h_grad_norm) {
-      NE_CUDA(cudaMemcpyAsync(h_grad_norm, t->norm_out, sizeof(float), cudaMemcpyDeviceToHost,
-                              ctx->st));
-      return ne_sync(ctx);
-    }
-    return NE_OK;
-  }
   NE_LAUNCH(launch_adamw_chunks(t->d_segs, t->d_chunks, t->nchunks, cfg->lr, cfg->beta1,
                                 cfg->beta2, cfg->eps, 1.0f / bc1, 1.0f / bc2, t->norm_out, ctx->st));
   if (shard_mode(ctx)) {
@@ -1827,7 +1710,6 @@ NE_API ne_status ne_adamw_step(ne_ctx* ctx, const ne_adam_cfg* cfg, int t_step, 
 // state getters see whole tensors.  Collective: every rank calls it.
 NE_API ne_status ne_train_gather_state(ne_ctx* ctx, int which) {
   if (!ctx || !ctx->train || which < 0 || which > 1) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_CUDA(cudaSetDevice(ctx->device));
   if (!shard_mode(ctx)) return NE_OK;
   ne_status s;
@@ -1945,7 +1827,6 @@ ne_status xfer(ne_ctx* ctx, const TensorRef& r, int which, float* host, bool to_
 
 extern "C" NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const ne_ckpt_info* info) {
   if (!ctx || !path) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   NE_FAULT_POINT(ctx, "ne_save_ckpt_v4");
   if (!ctx->train) return fail(ctx, NE_ERR_STATE, "ne_save_ckpt_v4 needs the training state");
   if (!ctx->train->state_gathered)
@@ -2039,7 +1920,6 @@ extern "C" NE_API ne_status ne_save_ckpt_v4(ne_ctx* ctx, const char* path, const
 namespace ne {
 
 ne_status train_ckpt_load(ne_ctx* ctx, const char* path, ne_ckpt_info* info, bool* handled) {
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   *handled = false;
   if (!ctx->train) return NE_OK;
   *handled = true;
@@ -2151,7 +2031,6 @@ extern "C" NE_API ne_status ne_train_get_layer(ne_ctx* ctx, int layer, int which
                                                float* h_rms_att, float* h_rms_ffn,
                                                float* h_q_norm, float* h_k_norm) {
   if (!ctx || !ctx->train || which < 0 || which > 3) return NE_ERR_INVALID;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   TrainState* t = ctx->train;
   const ne_model_cfg& m = ctx->cfg;
   if (layer < -1 || layer >= m.n_layers) return NE_ERR_INVALID;
@@ -2216,7 +2095,6 @@ extern "C" NE_API ne_status ne_sdpa_fwd_device(ne_ctx* ctx, const void* d_q, con
 // embedding gradient.  CV = 0 (or NULL) restores the full vocabulary.
 extern "C" NE_API ne_status ne_train_set_vocab_map(ne_ctx* ctx, const int32_t* h_c2f, int CV) {
   if (!ctx || !ctx->train) return NE_ERR_STATE;
-  train_opt_fence(ctx);   // an overlapped optimizer step is complete
   TrainState* t = ctx->train;
   const ne_model_cfg& m = ctx->cfg;
   NE_CUDA(cudaSetDevice(ctx->device));

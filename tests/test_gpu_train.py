@@ -217,63 +217,6 @@ def test_tensor_core_dq_at_short_sequences(kw, env):
     _in_child(kw, 2, 256, env)
 
 
-def _child_steps(kw, B, S, env, n_steps, q):
-    import os
-    for k, v in env.items():
-        os.environ[k] = v
-    try:
-        cfg = _cfg(**kw)
-        layers, rf, emb, qk = om.init_weights(cfg, seed=81, std=0.08, bf16=True)
-        e = _engine(cfg, layers, rf, emb, qk, B, S)
-        losses = []
-        for i in range(n_steps):
-            tok = om.prompt_tokens(cfg.vocab, S + 1, 90 + i, batch=B)
-            losses.append(e.train_fwd_bwd(tok))
-            e.adamw_step(i + 1, 1e-3, return_norm=False)
-        tok = om.prompt_tokens(cfg.vocab, S + 1, 99, batch=B)
-        losses.append(e.train_fwd_bwd(tok))
-        q.put(("ok", losses, e.get_masters(), e.get_grads()))
-        e.close()
-    except BaseException as ex:
-        q.put(("fail", repr(ex), None, None))
-
-
-def test_overlapped_optimizer_step_matches_serial():
-    """NE_ADAM_OVERLAP=1: AdamW runs bucket by bucket on its own stream beside
-    the next micro-step's forward (eager, then graph-replayed micro-steps).  The
-    arithmetic is the same, but the split-K dW products add their partial sums
-    in arrival order, so two serial runs already differ in the last bits after
-    a few steps.  The overlapped run must stay as close to a serial run as a
-    second serial run does (within 4x, plus 1e-5): a forward that read a bucket
-    before its update, or a backward that accumulated into gradients not yet
-    cleared, moves it far outside that."""
-    import multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    out = []
-    for env in ({}, {}, {"NE_ADAM_OVERLAP": "1"}):
-        q = ctx.Queue()
-        p = ctx.Process(target=_child_steps, args=(TC_ATTN[0], 2, 128, env, 4, q))
-        p.start()
-        out.append(q.get(timeout=300))
-        p.join(timeout=60)
-    for r in out:
-        assert r[0] == "ok", r[1]
-    ref, again, ov = out
-
-    def near(name, x_ref, x_again, x_ov):
-        d_again = _rel(x_again, x_ref)
-        d_ov = _rel(x_ov, x_ref)
-        assert d_ov <= 4 * d_again + 1e-5, (name, d_ov, d_again)
-
-    near("losses", ref[1], again[1], ov[1])
-    for part, what in ((2, "masters"), (3, "gradients")):
-        for L in range(len(ref[part]["layers"])):
-            for k in ref[part]["layers"][L]:
-                near((what, L, k), ref[part]["layers"][L][k], again[part]["layers"][L][k],
-                     ov[part]["layers"][L][k])
-        near((what, "embed"), ref[part]["embed"], again[part]["embed"], ov[part]["embed"])
-
-
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 1088)])
 def test_one_tile_forward_kernel_for_even_groups(B, S):
     """GQA groups of 2 take the two-tile forward by default; NE_ATTN_FWD2=0
