@@ -106,9 +106,12 @@ __global__ void __launch_bounds__(256) px_zero_kernel(float* base, const PxChunk
 // Reduce-scatter of one bucket: own[x] = sum over ranks p (in rank order) of
 // grad_p[x] for every x of the chunks (this rank's parts of the bucket's
 // tensors).  Chunk offsets are multiples of 4 floats; lengths too, except a
-// tensor's last chunk.
+// tensor's last chunk.  WM bounds the world size at compile time; each thread
+// keeps U = 8 / WM float4 positions (U x W loads over NVLink) in flight.
+template <int WM>
 __global__ void __launch_bounds__(256) px_reduce_kernel(PxTables T, const PxChunk* chunks,
                                                         int nchunks, int slot, int* status) {
+  constexpr int U = 8 / WM;
   if (!cta_wait_peers(T, slot, status)) return;
   const int W = T.world;
   float* own = T.grad[T.rank];
@@ -116,21 +119,30 @@ __global__ void __launch_bounds__(256) px_reduce_kernel(PxTables T, const PxChun
     const PxChunk ch = chunks[c];
     const long long base = ch.dst_off;   // float offset from the gradient base
     const int n4 = ch.len >> 2;
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 v[PX_MAX_WORLD];
+    for (int i0 = threadIdx.x; i0 < n4; i0 += blockDim.x * U) {
+      float4 v[U][WM];
 #pragma unroll
-      for (int p = 0; p < PX_MAX_WORLD; ++p)
-        if (p < W) v[p] = reinterpret_cast<const float4*>(T.grad[p] + base)[i];
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * blockDim.x;
 #pragma unroll
-      for (int p = 0; p < PX_MAX_WORLD; ++p)
-        if (p < W) {
-          acc.x += v[p].x;
-          acc.y += v[p].y;
-          acc.z += v[p].z;
-          acc.w += v[p].w;
-        }
-      reinterpret_cast<float4*>(own + base)[i] = acc;
+        for (int p = 0; p < WM; ++p)
+          if (p < W && i < n4) v[u][p] = reinterpret_cast<const float4*>(T.grad[p] + base)[i];
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i >= n4) break;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < WM; ++p)
+          if (p < W) {
+            acc.x += v[u][p].x;
+            acc.y += v[u][p].y;
+            acc.z += v[u][p].z;
+            acc.w += v[u][p].w;
+          }
+        reinterpret_cast<float4*>(own + base)[i] = acc;
+      }
     }
     for (int i = (n4 << 2) + threadIdx.x; i < ch.len; i += blockDim.x) {
       float acc = 0.f;
@@ -154,8 +166,20 @@ __global__ void __launch_bounds__(256) px_copy_kernel(PxTables T, const char* co
     const uintptr_t ends = reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d);
     const bool vec = (ends & 15u) == 0;
     const int n16 = vec ? ch.len >> 4 : 0;
-    for (int i = threadIdx.x; i < n16; i += blockDim.x)
-      reinterpret_cast<uint4*>(d)[i] = reinterpret_cast<const uint4*>(s)[i];
+    constexpr int U = 4;   // 16-byte loads in flight per thread
+    for (int i0 = threadIdx.x; i0 < n16; i0 += blockDim.x * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < n16) v[u] = reinterpret_cast<const uint4*>(s)[i];
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < n16) reinterpret_cast<uint4*>(d)[i] = v[u];
+      }
+    }
     for (int i = (n16 << 4) + threadIdx.x; i < ch.len; i += blockDim.x) d[i] = s[i];
   }
 }
@@ -207,8 +231,10 @@ cudaError_t px_reduce(const PxTables& T, const PxChunk* chunks, int nchunks, int
                       int* status, cudaStream_t st) {
   if (nchunks <= 0) return cudaSuccess;
   if (T.world > PX_MAX_WORLD) return cudaErrorInvalidValue;
-  px_reduce_kernel<<<grid < nchunks ? grid : nchunks, 256, 0, st>>>(T, chunks, nchunks, slot,
-                                                                    status);
+  const int g = grid < nchunks ? grid : nchunks;
+  if (T.world <= 2) px_reduce_kernel<2><<<g, 256, 0, st>>>(T, chunks, nchunks, slot, status);
+  else if (T.world <= 4) px_reduce_kernel<4><<<g, 256, 0, st>>>(T, chunks, nchunks, slot, status);
+  else px_reduce_kernel<8><<<g, 256, 0, st>>>(T, chunks, nchunks, slot, status);
   return cudaGetLastError();
 }
 
