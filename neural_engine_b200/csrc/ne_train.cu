@@ -893,12 +893,14 @@ static ne_status px_ready(ne_ctx* ctx) {
 }
 
 // CTAs of the exchange kernels on the comm stream (they share the SMs with
-// the backward's GEMMs): NE_PX_CTAS, default 64.
+// the backward's GEMMs): NE_PX_CTAS, default 128.  Their NVLink bandwidth
+// grows with the loads in flight, so fewer CTAs cost more than the SMs they
+// free (2 ranks, Qwen3 S 256: 16 CTAs 40.2, 32 30.4, 64 26.8, 128 26.4 ms).
 static int px_ctas() {
   static const int n = [] {
     const char* e = std::getenv("NE_PX_CTAS");
     const int v = e ? std::atoi(e) : 0;
-    return v > 0 ? v : 64;
+    return v > 0 ? v : 128;
   }();
   return n;
 }

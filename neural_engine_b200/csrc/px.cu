@@ -107,11 +107,11 @@ __global__ void __launch_bounds__(256) px_zero_kernel(float* base, const PxChunk
 // grad_p[x] for every x of the chunks (this rank's parts of the bucket's
 // tensors).  Chunk offsets are multiples of 4 floats; lengths too, except a
 // tensor's last chunk.  WM bounds the world size at compile time; each thread
-// keeps U = 8 / WM float4 positions (U x W loads over NVLink) in flight.
+// keeps U = 16 / WM float4 positions (U x W loads over NVLink) in flight.
 template <int WM>
 __global__ void __launch_bounds__(256) px_reduce_kernel(PxTables T, const PxChunk* chunks,
                                                         int nchunks, int slot, int* status) {
-  constexpr int U = 8 / WM;
+  constexpr int U = 16 / WM;
   if (!cta_wait_peers(T, slot, status)) return;
   const int W = T.world;
   float* own = T.grad[T.rank];
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(256) px_copy_kernel(PxTables T, const char* co
     const uintptr_t ends = reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d);
     const bool vec = (ends & 15u) == 0;
     const int n16 = vec ? ch.len >> 4 : 0;
-    constexpr int U = 4;   // 16-byte loads in flight per thread
+    constexpr int U = 8;   // 16-byte loads in flight per thread
     for (int i0 = threadIdx.x; i0 < n16; i0 += blockDim.x * U) {
       uint4 v[U];
 #pragma unroll
