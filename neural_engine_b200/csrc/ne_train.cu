@@ -893,14 +893,15 @@ static ne_status px_ready(ne_ctx* ctx) {
 }
 
 // CTAs of the exchange kernels on the comm stream (they share the SMs with
-// the backward's GEMMs): NE_PX_CTAS, default 128.  Their NVLink bandwidth
+// the backward's GEMMs): NE_PX_CTAS, default 256.  Their NVLink bandwidth
 // grows with the loads in flight, so fewer CTAs cost more than the SMs they
-// free (2 ranks, Qwen3 S 256: 16 CTAs 40.2, 32 30.4, 64 26.8, 128 26.4 ms).
+// free (2 ranks, Qwen3 S 256, 16 loads per thread: 64 CTAs 26.8, 128 25.7,
+// 256 25.4 ms per step).
 static int px_ctas() {
   static const int n = [] {
     const char* e = std::getenv("NE_PX_CTAS");
     const int v = e ? std::atoi(e) : 0;
-    return v > 0 ? v : 128;
+    return v > 0 ? v : 256;
   }();
   return n;
 }
