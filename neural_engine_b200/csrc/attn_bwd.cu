@@ -556,7 +556,9 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
     if (e[0] == 'd') return 2;
     return 1;
   }();
-  constexpr int TC_BOTH_MIN_S = 1024;   // measured: dQ on tcgen05 wins from ~1024 positions
+  // measured (Qwen3 S 256 step, the pipelined dQ with its D pre-pass): 24.52 ms
+  // with the tcgen05 dQ against 24.69 ms with the mma.sync one
+  constexpr int TC_BOTH_MIN_S = 256;
   if ((hd == 128 || (hd == 64 && attn_tc64())) && rope_cs != nullptr && mode != 0) {
     const bool tc_dq = mode == 1 || (mode == -1 && S >= TC_BOTH_MIN_S);
     return launch_attn_bwd_tc(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, hd, Tmax, qkv_raw, qn, kn,

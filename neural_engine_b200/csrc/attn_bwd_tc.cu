@@ -749,20 +749,74 @@ __device__ __forceinline__ void stage_row_bf16(uint32_t tile, int row, int h_lo,
   }
 }
 
+// ================================================================== D = rowsum(dO * O)
+// One pass over the attention output and its gradient before the pipelined
+// dQ / dK-dV kernels: D[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
+// (the softmax backward's row term, FlashAttention-2's preprocessing step).
+// Rows (token, head) are HD contiguous bf16 in both tensors; a warp takes 8
+// consecutive rows, every lane HD / 32 contiguous columns of each, all 16
+// loads in flight before the sums.  HBM-bound: 4 * HD bytes read per row.
+constexpr int RD_ROWS_PER_WARP = 8;
+constexpr int RD_THREADS = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(RD_THREADS)
+attn_rowdot_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, float* __restrict__ Dl,
+                   int rows, int S, int Hq) {
+  constexpr int EPL = HD / 32;
+  using V = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
+  pdl_trigger();
+  pdl_wait();   // dO comes from the preceding product
+  const int lane = threadIdx.x & 31;
+  const int r0 = (blockIdx.x * (RD_THREADS / 32) + (threadIdx.x >> 5)) * RD_ROWS_PER_WARP;
+  V ov[RD_ROWS_PER_WARP], gv[RD_ROWS_PER_WARP];
+#pragma unroll
+  for (int k = 0; k < RD_ROWS_PER_WARP; ++k) {
+    if (r0 + k < rows) {
+      const size_t off = (size_t)(r0 + k) * HD + lane * EPL;
+      ov[k] = *reinterpret_cast<const V*>(O + off);
+      gv[k] = *reinterpret_cast<const V*>(dO + off);
+    } else {
+      ov[k] = V{};
+      gv[k] = V{};
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < RD_ROWS_PER_WARP; ++k) {
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[k]);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[k]);
+    float d = 0.f;
+#pragma unroll
+    for (int t = 0; t < EPL / 2; ++t) {
+      const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
+      d += of.x * gf.x + of.y * gf.y;
+    }
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
+    const int r = r0 + k;
+    if (lane == k && r < rows) {
+      // row r = (b * S + q) * Hq + h  ->  D[(b * Hq + h) * S + q]
+      const int h = r % Hq, bq = r / Hq;
+      const int q = bq % S, b = bq / S;
+      Dl[((size_t)b * Hq + h) * S + q] = d;
+    }
+  }
+}
+
 // ================================================================== dQ (pipelined)
 // dq_tc_kernel's product with the key tile split into two 64-key halves run
 // as independent streams (half h: S_h = Q K_h^T at TMEM columns [64h, 64h+64),
 // dP_h at [128+64h, ...); the element-wise warps owning those columns write
 // bf16 dS_h in place over S_h, and dQ += dS_h K_h reads it from tensor memory
 // as its A operand; dQ at 256), with K / V double-buffered so the next key
-// tile loads while the current one is in use.
+// tile loads while the current one is in use.  D comes from attn_rowdot_kernel
+// (computing it here held every element-wise warp ~8 us before its first tile).
 template <int HD>
 __global__ void __launch_bounds__(TB_THREADS, 1)
 dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
              const __grid_constant__ CUtensorMap tmO,
-             const bf16* __restrict__ O, const bf16* __restrict__ dO,
-             const float* __restrict__ LSE, float* __restrict__ Dl, int S, int Hq, int Hkv,
+             const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq, int Hkv,
              int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
              RowBwd rb, bf16* __restrict__ dqkv, float* __restrict__ dqn, int* status) {
   using C = TbCfg<HD>;
@@ -930,48 +984,10 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const int q = q0 + row;
     const bool qv = q < S;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int h_lo = half * CW;         // head columns of the D sum and the epilogue
+    const int h_lo = half * CW;         // head columns of the epilogue
     float* const pxch = xch;
-    pdl_wait();   // O, dO and LSE come from earlier kernels
-    {
-      // D = rowsum(dO * O): each warp of the pair takes 16 of the quarter's
-      // 32 rows, a whole row per pass (every lane HD / 32 contiguous columns,
-      // so the loads are coalesced), all 32 loads in flight before the sums
-      constexpr int EPL = HD / 32;
-      using V = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
-      const int r0 = quarter * 32 + half * 16;
-      V ov[16], gv[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int qq = q0 + r0 + k;
-        if (qq < S) {
-          const size_t off = ((size_t)(b * S + qq) * Hq + h) * HD + lane * EPL;
-          ov[k] = *reinterpret_cast<const V*>(O + off);
-          gv[k] = *reinterpret_cast<const V*>(dO + off);
-        } else {
-          ov[k] = V{};
-          gv[k] = V{};
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[k]);
-        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[k]);
-        float d = 0.f;
-#pragma unroll
-        for (int t = 0; t < EPL / 2; ++t) {
-          const float2 of = __bfloat1622float2(o2[t]), gf = __bfloat1622float2(g2[t]);
-          d += of.x * gf.x + of.y * gf.y;
-        }
-#pragma unroll
-        for (int sh = 16; sh > 0; sh >>= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
-        if (lane == 0) pxch[r0 + k] = d;
-      }
-    }
-    named_bar(1 + quarter, 64);
-    const float Drow = pxch[row];
-    named_bar(1 + quarter, 64);   // the exchange area is reusable
-    if (half == 0 && qv) Dl[((size_t)b * Hq + h) * S + q] = Drow;
+    pdl_wait();   // D (attn_rowdot_kernel) and LSE come from earlier kernels
+    const float Drow = qv ? Dl[((size_t)b * Hq + h) * S + q] : 0.f;
     const float Lrow = qv ? LSE[((size_t)b * Hq + h) * S + q] : 0.f;
 
     bool ok = true;
@@ -1494,17 +1510,26 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
   const float scale = 1.0f / sqrtf((float)HD);
   const float scale_log2 = scale * 1.4426950408889634f;
   const int n_t = (S + 127) / 128;
-  // dQ first: it also publishes D, which dK / dV read
-  cudaError_t e =
-      !tc_dq ? launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn,
-                                  qk_eps, rope_cs, dqkv, dqn, st)
-      : dq_pipelined()
-          ? launch_k(dq_tp_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_TP_SMEM,
-                     st, tq, tdo, tk, tv, to, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
-                     qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status)
-          : launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM,
-                     st, tq, tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
-                     qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status);
+  // dQ first: the mma.sync and serial tcgen05 kernels also publish D, which
+  // dK / dV read; the pipelined one reads D from its own pre-pass
+  cudaError_t e;
+  if (!tc_dq) {
+    e = launch_attn_dq_mma(Q, K, V, O, dO, LSE, Dl, B, S, Hq, Hkv, HD, Tmax, qkv_raw, qn, qk_eps,
+                           rope_cs, dqkv, dqn, st);
+  } else if (dq_pipelined()) {
+    const int rows = B * S * Hq;
+    const int per_block = RD_ROWS_PER_WARP * (RD_THREADS / 32);
+    e = launch_k(attn_rowdot_kernel<HD>, dim3((rows + per_block - 1) / per_block),
+                 dim3(RD_THREADS), 0, st, O, dO, Dl, rows, S, Hq);
+    if (e != cudaSuccess) return e;
+    e = launch_k(dq_tp_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_TP_SMEM, st,
+                 tq, tdo, tk, tv, to, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                 qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status);
+  } else {
+    e = launch_k(dq_tc_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_SMEM, st, tq,
+                 tdo, tk, tv, O, dO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                 RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status);
+  }
   if (e != cudaSuccess) return e;
   if (dkdv_pipelined())
     return launch_k(dkdv_tp_kernel<HD>, dim3(n_t, Hkv, B), dim3(TB_THREADS),
