@@ -74,6 +74,7 @@ struct TbCfg {
   static constexpr int DQ_TP_SMEM = 6 * TILE + TB_BAR_AREA + 1024;
   // dkdv_tp: K | V | Q[2] | dO[2] | LSE, D [2][2][128] floats (2 KB), barrier area
   static constexpr int DKV_TP_SMEM = 6 * TILE + 2048 + TB_BAR_AREA + 1024;
+  static constexpr int BWD_TP_SMEM = DQ_TP_SMEM > DKV_TP_SMEM ? DQ_TP_SMEM : DKV_TP_SMEM;
   static_assert(DKV_TP_SMEM <= 232448, "shared memory per CTA");
 };
 
@@ -811,14 +812,16 @@ attn_rowdot_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, floa
 // as its A operand; dQ at 256), with K / V double-buffered so the next key
 // tile loads while the current one is in use.  D comes from attn_rowdot_kernel
 // (computing it here held every element-wise warp ~8 us before its first tile).
+// Work unit `lin` of B x Hq x (query tiles) units, longest first; the tensor
+// maps are the kernel's own parameters (passed by reference, so TMA reads them
+// from parameter space).
 template <int HD>
-__global__ void __launch_bounds__(TB_THREADS, 1)
-dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
-             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-             const __grid_constant__ CUtensorMap tmO,
-             const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq, int Hkv,
-             int Tmax, float scale_log2, float scale, const float* __restrict__ qkv_raw,
-             RowBwd rb, bf16* __restrict__ dqkv, float* __restrict__ dqn, int* status) {
+__device__ __forceinline__ void
+dq_tp_body(const CUtensorMap& tmQ, const CUtensorMap& tmdO, const CUtensorMap& tmK,
+           const CUtensorMap& tmV, const CUtensorMap& tmO, const float* __restrict__ LSE,
+           const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+           float scale, const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
+           float* __restrict__ dqn, int* status, int lin, int B) {
   using C = TbCfg<HD>;
   constexpr int CW = C::CW;
   extern __shared__ uint8_t smem_raw[];
@@ -840,10 +843,9 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   float* const xch = reinterpret_cast<float*>(gbars + 128);   // [2][2][128], indexed by row
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nbh = gridDim.y * gridDim.z;   // longest-first (see dq_tc_kernel)
-  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  const int qt = gridDim.x - 1 - lin / nbh;
-  const int h = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
+  const int nbh = Hq * B;   // longest-first (see dq_tc_kernel)
+  const int qt = (S + 127) / 128 - 1 - lin / nbh;
+  const int h = (lin % nbh) % Hq, b = (lin % nbh) / Hq;
   const int kvh = h / (Hq / Hkv);
   const int q0 = qt * 128;
   const int n_keys = min(S, q0 + 128);
@@ -1088,15 +1090,14 @@ dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
 //     pass, and the other way round, so the tensor cores and the element-wise
 //     warps overlap; the next Q / dO tile is loaded while the current one is
 //     in use.
+// Work unit `lin` of B x Hkv x (key tiles) units, longest (key tile 0) first.
 template <int HD>
-__global__ void __launch_bounds__(TB_THREADS, 1)
-dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
-               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-               const __grid_constant__ CUtensorMap tmO,
-               const float* __restrict__ LSE, const float* __restrict__ Dl, int S, int Hq,
-               int Hkv, int Tmax, float scale_log2, float scale,
-               const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
-               float* __restrict__ dkn, int* status) {
+__device__ __forceinline__ void
+dkdv_tp_body(const CUtensorMap& tmQ, const CUtensorMap& tmdO, const CUtensorMap& tmK,
+             const CUtensorMap& tmV, const CUtensorMap& tmO, const float* __restrict__ LSE,
+             const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+             float scale, const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
+             float* __restrict__ dkn, int* status, int lin, int B) {
   using C = TbCfg<HD>;
   constexpr int CW = C::CW;
   extern __shared__ uint8_t smem_raw[];
@@ -1121,10 +1122,9 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // longest-first order (key tile 0 sees every query tile)
-  const int nbh = gridDim.y * gridDim.z;
-  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nbh = Hkv * B;
   const int kt = lin / nbh;
-  const int kvh = (lin % nbh) % gridDim.y, b = (lin % nbh) / gridDim.y;
+  const int kvh = (lin % nbh) % Hkv, b = (lin % nbh) / Hkv;
   const int G = Hq / Hkv;
   const int k0 = kt * 128;
   const int n_qt_all = (S + 127) / 128;
@@ -1406,6 +1406,54 @@ dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+template <int HD>
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dq_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+             const __grid_constant__ CUtensorMap tmO, const float* __restrict__ LSE,
+             const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+             float scale, const float* __restrict__ qkv_raw, RowBwd rb, bf16* __restrict__ dqkv,
+             float* __restrict__ dqn, int* status) {
+  dq_tp_body<HD>(tmQ, tmdO, tmK, tmV, tmO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale, qkv_raw,
+                 rb, dqkv, dqn, status,
+                 blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), gridDim.z);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(TB_THREADS, 1)
+dkdv_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const __grid_constant__ CUtensorMap tmO, const float* __restrict__ LSE,
+               const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+               float scale, const float* __restrict__ qkv_raw, RowBwd rb,
+               bf16* __restrict__ dqkv, float* __restrict__ dkn, int* status) {
+  dkdv_tp_body<HD>(tmQ, tmdO, tmK, tmV, tmO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                   qkv_raw, rb, dqkv, dkn, status,
+                   blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), gridDim.z);
+}
+
+// dK/dV and dQ in one launch (both read D from the pre-pass and nothing the
+// other writes): CTAs [0, n_kv) take the dK/dV units, the rest the dQ units,
+// so the longest units (dK/dV of key tile 0) start first and the two kernels'
+// partial last waves share the SMs instead of following one another.
+template <int HD>
+__global__ void __launch_bounds__(TB_THREADS, 1)
+bwd_tp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              const __grid_constant__ CUtensorMap tmO, const float* __restrict__ LSE,
+              const float* __restrict__ Dl, int S, int Hq, int Hkv, int Tmax, float scale_log2,
+              float scale, const float* __restrict__ qkv_raw, RowBwd rbq, RowBwd rbk,
+              bf16* __restrict__ dqkv, float* __restrict__ dqn, float* __restrict__ dkn,
+              int* status, int B) {
+  const int n_kv = ((S + 127) / 128) * Hkv * B;
+  if ((int)blockIdx.x < n_kv)
+    dkdv_tp_body<HD>(tmQ, tmdO, tmK, tmV, tmO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                     qkv_raw, rbk, dqkv, dkn, status, (int)blockIdx.x, B);
+  else
+    dq_tp_body<HD>(tmQ, tmdO, tmK, tmV, tmO, LSE, Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
+                   qkv_raw, rbq, dqkv, dqn, status, (int)blockIdx.x - n_kv, B);
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -1481,6 +1529,16 @@ bool dq_pipelined() {
   return on;
 }
 
+// The pipelined dQ and dK/dV kernels in one launch (NE_ATTN_BWD_MERGE, "0"
+// keeps two launches).
+bool bwd_merged() {
+  static const bool on = [] {
+    const char* e = std::getenv("NE_ATTN_BWD_MERGE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int HD>
 cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
                              const CUtensorMap& tv, const CUtensorMap& to, const __nv_bfloat16* Q,
@@ -1505,6 +1563,9 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
     e = cudaFuncSetAttribute(dq_tp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::DQ_TP_SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_tp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::BWD_TP_SMEM);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   const float scale = 1.0f / sqrtf((float)HD);
@@ -1522,6 +1583,11 @@ cudaError_t launch_bwd_tc_hd(const CUtensorMap& tq, const CUtensorMap& tdo, cons
     e = launch_k(attn_rowdot_kernel<HD>, dim3((rows + per_block - 1) / per_block),
                  dim3(RD_THREADS), 0, st, O, dO, Dl, rows, S, Hq);
     if (e != cudaSuccess) return e;
+    if (dkdv_pipelined() && bwd_merged())
+      return launch_k(bwd_tp_kernel<HD>, dim3(n_t * (Hkv + Hq) * B), dim3(TB_THREADS),
+                      (size_t)C::BWD_TP_SMEM, st, tq, tdo, tk, tv, to, LSE, (const float*)Dl, S,
+                      Hq, Hkv, Tmax, scale_log2, scale, qkv_raw, RowBwd{qn, qk_eps, rope_cs},
+                      RowBwd{kn, qk_eps, rope_cs}, dqkv, dqn, dkn, status, B);
     e = launch_k(dq_tp_kernel<HD>, dim3(n_t, Hq, B), dim3(TB_THREADS), (size_t)C::DQ_TP_SMEM, st,
                  tq, tdo, tk, tv, to, LSE, (const float*)Dl, S, Hq, Hkv, Tmax, scale_log2, scale,
                  qkv_raw, RowBwd{qn, qk_eps, rope_cs}, dqkv, dqn, status);

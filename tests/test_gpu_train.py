@@ -208,12 +208,15 @@ def _in_child(kw, B, S, env):
 
 @pytest.mark.parametrize("kw", [TC_ATTN[0], TC_ATTN[3]])
 @pytest.mark.parametrize("env", [{"NE_ATTN_BWD_TC": "1", "NE_ATTN_TC64": "1"},
+                                 {"NE_ATTN_BWD_TC": "1", "NE_ATTN_TC64": "1",
+                                  "NE_ATTN_BWD_MERGE": "0"},
                                  {"NE_ATTN_BWD_TC": "1", "NE_ATTN_TC64": "1", "NE_DQ_TP": "0",
                                   "NE_DKDV_TP": "0"}])
 def test_tensor_core_dq_at_short_sequences(kw, env):
-    """The tcgen05 dQ kernels (pipelined, and with NE_DQ_TP=0 / NE_DKDV_TP=0 the
-    serial ones) at 256 positions, where the default takes the mma.sync dQ:
-    run in a fresh process so the switches are read there."""
+    """The tcgen05 dQ kernels at 256 positions: pipelined (dQ and dK/dV in one
+    launch, or with NE_ATTN_BWD_MERGE=0 in two) and, with NE_DQ_TP=0 /
+    NE_DKDV_TP=0, the serial ones; run in a fresh process so the switches are
+    read there."""
     _in_child(kw, 2, 256, env)
 
 
