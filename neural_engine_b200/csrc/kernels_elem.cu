@@ -404,6 +404,9 @@ cudaError_t launch_qkv_post(const float* qkv, int nsplit, long long split_stride
                             void* q_out, int q_type, void* kc, void* vc, int Tmax, int* status,
                             cudaStream_t st, int kv_bf16, int zero_src) {
   const int nh = Hq + 2 * Hkv;
+  // four heads per warp where they divide the row (measured, Qwen3: one head
+  // per warp cost 1 ms more per S 256 training step and 0.05 ms per B 256
+  // decode step; eight per warp no better for training, 0.05 ms worse for decode)
   const bool by4 = nh % 4 == 0;
   const int warps = rows * (by4 ? nh / 4 : nh);
   const int threads = 256;
