@@ -556,8 +556,8 @@ cudaError_t launch_attn_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
     if (e[0] == 'd') return 2;
     return 1;
   }();
-  // measured (Qwen3 S 256 step, the pipelined dQ with its D pre-pass): 24.52 ms
-  // with the tcgen05 dQ against 24.69 ms with the mma.sync one
+  // from 256 positions (two 128-key tiles) the pipelined tcgen05 dQ with its D
+  // pre-pass, merged with dK/dV, measured at least as fast as the mma.sync dQ
   constexpr int TC_BOTH_MIN_S = 256;
   if ((hd == 128 || (hd == 64 && attn_tc64())) && rope_cs != nullptr && mode != 0) {
     const bool tc_dq = mode == 1 || (mode == -1 && S >= TC_BOTH_MIN_S);

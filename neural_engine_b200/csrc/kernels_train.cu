@@ -44,8 +44,8 @@ __device__ __forceinline__ float block_sum256(float v, float* red) {
 // One warp per row (no block barriers in the row reductions); 8 warps per
 // block walk RB_ROWS rows each and reduce their dw partials once per block.
 // All of a row's loads (x, dy, the residual) are issued before its reductions.
-// Measured (Qwen3 S 256 step, one box): 2 rows per warp 24.03 ms, 1 row
-// 24.34 ms, 4 rows 24.53 ms.
+// Measured (Qwen3 S 256 step, one box, in this order): 2 rows per warp
+// 24.03 ms, 1 row 24.34 ms, 4 rows 24.53 ms (within the drift of later runs).
 constexpr int RB_ROWS = 2;
 template <int PER>
 __global__ void __launch_bounds__(256)
