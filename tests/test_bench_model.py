@@ -5,7 +5,9 @@ they are pinned here against the closed forms of the measurement definitions:
 Qwen3-0.6B 596,042,752 parameters (440.4 M in the layers, 155.58 M in the tied
 embedding), Stories110M 109,529,856; decode bytes per step = bf16 weights once
 + B x (K/V of T positions + the new K/V row); training = 3 x the forward's
-FLOPs (2 x params + causal attention 2*L*Hq*hd*(S+1) per token).
+FLOPs (2 x params + causal attention 2*L*Hq*hd*(S+1) per token).  Also the
+host-side records of the line: the clock record (median SM clock, throttle
+reasons) and the label of the gradient exchange.
 """
 import importlib.util
 import os
@@ -56,3 +58,39 @@ def test_training_and_prefill_flops(bench):
     for S in (256, 2048):
         assert bench.prefill_flops(16, S) == 16 * S * (2 * mats + attn * (S + 1)) + \
             16 * 2 * 151936 * 1024
+
+
+def test_clock_record_reads_reasons_and_median(bench):
+    """The clocks object of the bench line: median SM clock under load, the max
+    clock, and which throttle reasons were active at any sample (the rejection
+    rule reads hw_slowdown / hw_thermal_slowdown / sw_thermal_slowdown)."""
+    cs = bench.ClockSampler(0)
+    head = ["0"]
+    cs.rows = [
+        head + ["1965", "1965", "700.0", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+        head + ["1912", "1965", "990.1", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+        head + ["1927", "1965", "995.0", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+        head + ["[N/A]", "1965", "0", "0x0"],          # unreadable sample: skipped
+        ["garbage"],
+    ]
+    rec = cs.stop()
+    assert rec == {"sm_mhz": 1927.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                   "samples": 3}
+    cs.rows = [head + ["1500", "1965", "900", "0x8", "Active", "Not Active", "Active", "Not Active"]]
+    assert cs.stop()["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    cs.rows = []
+    assert cs.stop() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+
+def test_dp_label_names_the_exchange(bench, monkeypatch):
+    monkeypatch.delenv("NE_COMM_PX", raising=False)
+    monkeypatch.delenv("NE_PX_FUSED_DW", raising=False)
+    assert bench.dp_label(1, "zero1").startswith("dp1 ")
+    assert "peer memory" in bench.dp_label(4, "zero1") and "reduce-scatter kernels" in \
+        bench.dp_label(4, "zero1")
+    assert "all-reduce" in bench.dp_label(2, "allreduce")
+    monkeypatch.setenv("NE_PX_FUSED_DW", "1")
+    assert "dW GEMM epilogues" in bench.dp_label(8, "zero1")
+    monkeypatch.setenv("NE_COMM_PX", "0")
+    assert "NCCL reduce-scatter" in bench.dp_label(8, "zero1")
+    assert bench.allmax(3.5, 1) == 3.5
