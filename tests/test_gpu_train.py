@@ -159,7 +159,7 @@ TC_ATTN = [dict(head_dim=128, heads=4, kv_heads=2, qk_norm=True, theta=1e6, eps=
 @pytest.mark.parametrize("B,S", [(2, 224), (1, 256), (4, 80), (1, 1088)])
 def test_tensor_core_attention_backward(kw, B, S):
     """Head dim 128 takes the tcgen05 attention kernels (forward, dK / dV, and
-    dQ from 1024 positions on), head dim 64 the mma.sync ones by default:
+    dQ from 256 positions on), head dim 64 the mma.sync ones by default:
     several 128-row query / key tiles, a ragged last tile, GQA groups of 2 and
     1, with and without QK-norm."""
     cfg = _cfg(**kw)
