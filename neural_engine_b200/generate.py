@@ -83,6 +83,28 @@ def _softmax(x):
     return e / np.sum(e)
 
 
+def sample_probs(lg, top_p: float, vocab: int):
+    """The sampling distribution of generate.py:203-213 from tempered logits
+    ``lg`` (logits / temperature): softmax, then, for top_p < 1, the smallest
+    set of most probable tokens whose cumulative probability reaches top_p,
+    renormalised in float32."""
+    probs = _softmax(lg)
+    if top_p < 1.0:
+        sorted_idx = np.argsort(-probs)
+        cum = np.cumsum(probs[sorted_idx])
+        cutoff = np.searchsorted(cum, top_p) + 1
+        mask = np.zeros(vocab, dtype=np.float32)
+        mask[sorted_idx[:cutoff]] = probs[sorted_idx[:cutoff]]
+        mask /= mask.sum()
+        probs = mask
+    return probs
+
+
+def sample_token(logits, temperature: float, top_p: float, vocab: int) -> int:
+    """One sampled token (generate.py:202-215) drawn with numpy's global RNG."""
+    return int(np.random.choice(vocab, p=sample_probs(logits / temperature, top_p, vocab)))
+
+
 def generate(info, layers, rms_final, embed, tokenizer, prompt_tokens, max_tokens, temperature,
              top_p, engine: Engine | None = None):
     """Autoregressive generation with KV cache (generate.py:113-228)."""
@@ -108,17 +130,7 @@ def generate(info, layers, rms_final, embed, tokenizer, prompt_tokens, max_token
         if greedy:
             tok = int(nxt[0])                                         # generate.py:200
         else:
-            lg = logits[0] / temperature                              # :202
-            probs = _softmax(lg)
-            if top_p < 1.0:                                           # :206-213
-                sorted_idx = np.argsort(-probs)
-                cum = np.cumsum(probs[sorted_idx])
-                cutoff = np.searchsorted(cum, top_p) + 1
-                mask = np.zeros(cfg.vocab, dtype=np.float32)
-                mask[sorted_idx[:cutoff]] = probs[sorted_idx[:cutoff]]
-                mask /= mask.sum()
-                probs = mask
-            tok = int(np.random.choice(cfg.vocab, p=probs))           # :215
+            tok = sample_token(logits[0], temperature, top_p, cfg.vocab)  # :202-215
         generated.append(tok)
         print(tokenizer.decode([tok]), end="", flush=True)            # :220-221
         if tok == tokenizer.eos_token_id or i == max_tokens - 1:      # :224

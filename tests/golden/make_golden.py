@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference tree is mounted:
 
-    python tests/golden/make_golden.py --ref <reference root>
+    python tests/golden/make_golden.py --ref <reference root> [--only name,...]
 
 What it does
   * ``ref_*`` fixtures: runs the reference's OWN numpy token loop --
@@ -15,6 +15,12 @@ What it does
     NOT used: it reads the GQA header fields from the wrong slots
     (generate.py:28 vs config.h:89); the info dict is built from the correct
     header instead.
+  * ``ref_tiny_gqa_topp`` / ``ref_tiny_gqa_temp``: the same generate() on the
+    sampling branch (temperature 0.8 with top-p 0.9; temperature 1.3 without
+    top-p) after ``np.random.seed``; records the tempered logits of every
+    draw (the vocabulary-sized input of the module's ``softmax``, wrapped),
+    the distribution passed to ``np.random.choice`` (through the ``np``
+    proxy) and the sampled tokens.
   * ``qwen3_c1``: the Qwen3-0.6B decode configuration (QK-norm, theta 1e6,
     eps 1e-6 -- outside what generate.py can express) from the oracle's
     parameterised restatement, which the ``ref_*`` fixtures pin to
@@ -65,6 +71,28 @@ class _ArgmaxRecorder:
     def argmax(self, a, *args, **kw):
         self.seen.append(np.array(a, dtype=np.float32, copy=True))
         return np.argmax(a, *args, **kw)
+
+
+class _SampleRecorder:
+    """Forwards to numpy; records the probabilities passed to
+    ``np.random.choice`` (the reference's sampling draw, generate.py:215)."""
+
+    def __init__(self):
+        self.probs = []
+        rec = self
+
+        class _Random:
+            def __getattr__(self, name):
+                return getattr(np.random, name)
+
+            def choice(self, a, *args, p=None, **kw):
+                rec.probs.append(np.array(p, copy=True))
+                return np.random.choice(a, *args, p=p, **kw)
+
+        self.random = _Random()
+
+    def __getattr__(self, name):
+        return getattr(np, name)
 
 
 class _StubTokenizer:
@@ -147,6 +175,50 @@ def make_ref_case(mod, name, cfg, wseed, pseed, n_prompt, n_tokens, gains=False,
     print(f"{name}: {n_tokens} tokens in {dt:.1f}s; tokens[:8]={toks[:8]}")
 
 
+def make_sampled_case(mod, name, cfg, wseed, pseed, n_prompt, n_tokens, temperature, top_p,
+                      seed, gains=False, std=0.02):
+    """The reference's own sampling branch (generate.py:201-215): generate()
+    with temperature / top-p after ``np.random.seed(seed)``.  Records the
+    tempered logits each draw was made from (the vocabulary-sized input of
+    the module's ``softmax``), the distribution passed to np.random.choice
+    and the sampled tokens."""
+    layers, rms_final, embed, qk = om.init_weights(cfg, seed=wseed, std=std)
+    if gains:
+        layers, rms_final, qk = om.random_gains(cfg, layers, rms_final, qk)
+    prompt = om.prompt_tokens(cfg.vocab, n_prompt, pseed)
+    info = {"dim": cfg.dim, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
+            "hd": cfg.head_dim, "q_dim": cfg.q_dim, "kv_dim": cfg.kv_dim,
+            "gqa_ratio": cfg.heads // cfg.kv_heads, "hidden": cfg.hidden,
+            "n_layers": cfg.n_layers, "vocab": cfg.vocab}
+    tempered = []
+    orig_softmax = mod.softmax
+
+    def softmax_rec(x):
+        if np.shape(x) == (cfg.vocab,):
+            tempered.append(np.array(x, copy=True))
+        return orig_softmax(x)
+
+    rec = _SampleRecorder()
+    saved_np = mod.np
+    mod.np, mod.softmax = rec, softmax_rec
+    try:
+        np.random.seed(seed)
+        with contextlib.redirect_stdout(io.StringIO()):
+            toks = mod.generate(info, layers, rms_final, embed, _StubTokenizer(),
+                                [int(t) for t in prompt], n_tokens, temperature, top_p)
+    finally:
+        mod.np, mod.softmax = saved_np, orig_softmax
+    assert len(tempered) == len(rec.probs) == len(toks) == n_tokens
+    np.savez(os.path.join(HERE, f"{name}.npz"),
+             cfg=np.array([cfg.n_layers, cfg.dim, cfg.hidden, cfg.heads, cfg.kv_heads,
+                           cfg.head_dim, cfg.vocab]),
+             wseed=wseed, pseed=pseed, gains=int(gains), std=std, prompt=prompt,
+             temperature=temperature, top_p=top_p, seed=seed, tokens=np.array(toks, np.int32),
+             tempered=np.stack(tempered), probs=np.stack(rec.probs),
+             checksum=weights_checksum(layers, rms_final, embed, qk))
+    print(f"{name}: T {temperature} top-p {top_p}: tokens[:8]={toks[:8]}")
+
+
 def make_qwen3_case(name, n_prompt, n_tokens, full_logit_steps=(0,)):
     cfg = om.QWEN3_06B
     layers, rms_final, embed, qk = om.init_weights(cfg, seed=0, bf16=True)
@@ -170,20 +242,37 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="reference repository root")
     ap.add_argument("--skip-qwen3", action="store_true")
+    ap.add_argument("--only", default="", help="comma-separated fixture names to write")
     args = ap.parse_args()
     mod = load_reference_generate(args.ref)
-    # tiny GQA model with non-unit gains: exercises every branch quickly
-    make_ref_case(mod, "ref_tiny_gqa", om.tiny(), 3, 4, 8, 24, gains=True,
-                  full_logit_steps=tuple(range(24)), std=0.25)
-    # tiny MHA model (Stories-like head layout)
-    make_ref_case(mod, "ref_tiny_mha", om.tiny(heads=4, kv_heads=4), 5, 6, 6, 16,
-                  full_logit_steps=tuple(range(16)), std=0.25)
-    # Stories110M, seed-0 weights, 16-token prompt (seed 1), 64 tokens
-    make_ref_case(mod, "ref_stories110m_c0", om.STORIES110M, 0, 1, 16, 64,
-                  full_logit_steps=(0, 63))
+    cases = [
+        # tiny GQA model with non-unit gains: exercises every branch quickly
+        ("ref_tiny_gqa", lambda: make_ref_case(mod, "ref_tiny_gqa", om.tiny(), 3, 4, 8, 24,
+                                               gains=True, full_logit_steps=tuple(range(24)),
+                                               std=0.25)),
+        # tiny MHA model (Stories-like head layout)
+        ("ref_tiny_mha", lambda: make_ref_case(mod, "ref_tiny_mha", om.tiny(heads=4, kv_heads=4),
+                                               5, 6, 6, 16, full_logit_steps=tuple(range(16)),
+                                               std=0.25)),
+        # the sampling branch: top-p masking, then plain temperature sampling
+        ("ref_tiny_gqa_topp", lambda: make_sampled_case(mod, "ref_tiny_gqa_topp", om.tiny(), 3, 4,
+                                                        8, 24, 0.8, 0.9, 1234, gains=True,
+                                                        std=0.25)),
+        ("ref_tiny_gqa_temp", lambda: make_sampled_case(mod, "ref_tiny_gqa_temp", om.tiny(), 3, 4,
+                                                        8, 24, 1.3, 1.0, 77, gains=True,
+                                                        std=0.25)),
+        # Stories110M, seed-0 weights, 16-token prompt (seed 1), 64 tokens
+        ("ref_stories110m_c0", lambda: make_ref_case(mod, "ref_stories110m_c0", om.STORIES110M,
+                                                     0, 1, 16, 64, full_logit_steps=(0, 63))),
+    ]
     if not args.skip_qwen3:
         # BASELINE config 1 (B = 1): 512-token prompt, first 32 greedy steps
-        make_qwen3_case("qwen3_c1", 512, 32, full_logit_steps=(0, 31))
+        cases.append(("qwen3_c1", lambda: make_qwen3_case("qwen3_c1", 512, 32,
+                                                          full_logit_steps=(0, 31))))
+    only = set(filter(None, args.only.split(",")))
+    for name, make in cases:
+        if not only or name in only:
+            make()
 
 
 if __name__ == "__main__":
