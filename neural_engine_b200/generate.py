@@ -9,14 +9,18 @@ Mirrors ane-training/training/training_dynamic/tools/generate.py:
     as generate.py:113-228.  The forward pass runs in the CUDA kernels;
     greedy decoding (temperature < 1e-6) stays entirely on the device, and
     sampling pulls the step's logits to the host and applies generate.py's
-    temperature / top-p rule (generate.py:201-215) with numpy's global RNG.
+    temperature / top-p rule (generate.py:201-215) with numpy's global RNG;
+  * ``main()``: the command line of generate.py:231-274
+    (``python -m neural_engine_b200.generate ckpt.bin -m <tokenizer> -p ...``).
 Extra ``info`` keys select the Qwen3 numerics the reference cannot express:
 ``eps``, ``theta``, ``qk_norm`` (with ``q_norm`` / ``k_norm`` gains lists),
 ``qk_eps``, ``res_alpha``.
 """
 from __future__ import annotations
 
+import argparse
 import struct
+import sys
 
 import numpy as np
 
@@ -142,3 +146,72 @@ def generate(info, layers, rms_final, embed, tokenizer, prompt_tokens, max_token
         pos += 1
     print()
     return generated
+
+
+class _IdTokenizer:
+    """Stand-in tokenizer for ``--prompt-ids``: prints token ids, no EOS."""
+    eos_token_id = None
+
+    @staticmethod
+    def decode(ids):
+        return "".join(f"{int(i)} " for i in ids)
+
+
+def main(argv=None):
+    """Command line of generate.py:231-274 (same arguments and output), on
+    libne.so.  ``--prompt-ids`` (comma-separated token ids) stands in for a
+    text prompt where no tokenizer is at hand; ``--model`` is then not needed."""
+    parser = argparse.ArgumentParser(description="Generate text from a v4 checkpoint (libne.so)")
+    parser.add_argument("checkpoint", help="Path to the v4 checkpoint (.bin)")
+    parser.add_argument("--model", "-m", default=None,
+                        help="HF model ID for tokenizer (e.g. Qwen/Qwen3-0.6B)")
+    parser.add_argument("--prompt", "-p", default="Once upon a time",
+                        help="Text prompt (default: 'Once upon a time')")
+    parser.add_argument("--prompt-ids", default=None,
+                        help="comma-separated prompt token ids instead of --prompt")
+    parser.add_argument("--tokens", "-n", type=int, default=100,
+                        help="Max tokens to generate (default: 100)")
+    parser.add_argument("--temp", "-t", type=float, default=0.8,
+                        help="Sampling temperature (default: 0.8, 0=greedy)")
+    parser.add_argument("--top-p", type=float, default=0.9,
+                        help="Top-p nucleus sampling (default: 0.9)")
+    parser.add_argument("--seed", type=int, default=None,
+                        help="Random seed for reproducibility")
+    args = parser.parse_args(argv)
+    if args.prompt_ids is None and args.model is None:
+        parser.error("--model is required for a text prompt (or give --prompt-ids)")
+
+    if args.seed is not None:
+        np.random.seed(args.seed)
+
+    info, layers, rms_final, embed = read_checkpoint(args.checkpoint)
+    if args.prompt_ids is not None:
+        tokenizer = _IdTokenizer()
+        prompt_tokens = [int(t) for t in args.prompt_ids.split(",") if t.strip()]
+        shown = args.prompt_ids
+    else:
+        try:
+            from transformers import AutoTokenizer
+        except ImportError:
+            print("Install dependencies: pip install transformers")
+            sys.exit(1)
+        print(f"Loading tokenizer: {args.model}")
+        tokenizer = AutoTokenizer.from_pretrained(args.model, trust_remote_code=True)
+        prompt_tokens = tokenizer.encode(args.prompt)
+        shown = args.prompt
+    if not prompt_tokens or min(prompt_tokens) < 0 or max(prompt_tokens) >= info["vocab"]:
+        parser.error(f"prompt token ids must lie in [0, {info['vocab']})")
+    print(f"Prompt ({len(prompt_tokens)} tokens): {shown}")
+    print(f"Generating {args.tokens} tokens (temp={args.temp}, top_p={args.top_p})...")
+    print("---")
+
+    generated = generate(info, layers, rms_final, embed, tokenizer, prompt_tokens, args.tokens,
+                         args.temp, args.top_p)
+
+    print("---")
+    print(f"Generated {len(generated)} tokens")
+    return generated
+
+
+if __name__ == "__main__":
+    main()
