@@ -1767,7 +1767,10 @@ NE_API float ne_lr_schedule(int step, float max_lr, int warmup_steps, int total_
   if (step < warmup_steps) return max_lr * ((float)(step + 1)) / warmup_steps;
   const float decay_ratio = (float)(step - warmup_steps) / (float)(total_steps - warmup_steps);
   const float min_lr = max_lr * min_lr_frac;
-  return min_lr + 0.5f * (1.0f + cosf(3.14159265358979323846f * decay_ratio)) * (max_lr - min_lr);
+  // cosf of a double product, as train.m:857 writes cosf(M_PI * decay_ratio)
+  return min_lr +
+         0.5f * (1.0f + cosf((float)(3.14159265358979323846 * (double)decay_ratio))) *
+             (max_lr - min_lr);
 }
 
 }  // extern "C"

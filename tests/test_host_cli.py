@@ -101,3 +101,25 @@ def test_uint32_token_file_reads_ids_beyond_uint16(tmp_path):
                           "--print-windows", "10"], check=True, capture_output=True, text=True,
                          timeout=60).stdout.split()
     assert [int(x) for x in out] == hd.sample_windows(len(data), 256, 10, seed=42)
+
+
+def test_lr_schedule_follows_train_m():
+    """ne_lr_schedule (a host function of libne.so, no GPU) against train.m:851-858
+    restated in float32 (numpy's float32 cos stands in for libm's cosf: one ulp)."""
+    from neural_engine_b200 import runtime
+    from oracle import train as ot
+    lib = runtime.load_library()
+    f32 = np.float32
+    for max_lr, warmup, total, frac in [(3e-4, 100, 1000, 0.1), (1e-3, 0, 50, 0.0),
+                                         (2e-4, 10, 11, 0.5)]:
+        for step in range(total):
+            got = lib.ne_lr_schedule(step, max_lr, warmup, total, frac)
+            mx, mn = f32(max_lr), f32(max_lr) * f32(frac)
+            if step < warmup:
+                want = mx * f32(step + 1) / f32(warmup)
+            else:
+                ratio = f32(step - warmup) / f32(total - warmup)
+                arg = f32(np.pi * np.float64(ratio))           # cosf(M_PI * decay_ratio)
+                want = mn + f32(0.5) * (f32(1.0) + np.cos(arg)) * (mx - mn)
+            assert abs(got - float(want)) <= 2.5e-7 * max_lr, (step, got, want)
+            assert abs(got - ot.lr_schedule(step, max_lr, warmup, total, frac)) <= 1e-6 * max_lr
