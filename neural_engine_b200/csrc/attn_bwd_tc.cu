@@ -19,6 +19,14 @@
 //                   dS^T (bf16) into shared memory, dV += P^T dO and
 //                   dK += dS^T Q in TMEM, so the group's dK / dV are summed in
 //                   the accumulators (no atomics).
+//   attn_rowdot_kernel  D = rowsum(dO * O) for the pipelined kernels.
+//   dq_tp / dkdv_tp     the same products pipelined: the tile split into two
+//                   64-wide halves run as independent streams, P / dS kept in
+//                   TMEM in place over the scores as the A operand of the
+//                   accumulating products, the streamed operand double-
+//                   buffered (the defaults; bodies shared by dq_tp_kernel,
+//                   dkdv_tp_kernel and bwd_tp_kernel, which runs both in one
+//                   launch, dK/dV units first).
 // Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
 // warps 2-9 element-wise work, two per TMEM lane quarter, each of the pair
 // owning 64 of the 128 score columns (and HD / 2 of the head columns).  Epilogues run the inverse RoPE and the
