@@ -34,7 +34,7 @@ class FakeTokenizer:
 
 @pytest.fixture()
 def tok(monkeypatch):
-    import transformers
+    transformers = pytest.importorskip("transformers")
     holder = {}
 
     def from_pretrained(name, trust_remote_code=False):
